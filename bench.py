@@ -1,0 +1,396 @@
+#!/usr/bin/env python3
+"""Benchmark driver (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload vgg16|lif]
+
+Workloads
+  vgg16 (default) -- VGG16-SNN T=4 inference, batch 64 per GPU, 32x32x3 input,
+                     BN folded, LIF tau=2 / v_th=1 / hard reset, 2x2 max-pool,
+                     classifier 512-4096-4096-10 with the logits averaged over T.
+                     Metric: images/s over all ranks (weak scaling: batch 64 per
+                     GPU; one NCCL all-gather of the [64, 10] logits per step).
+  lif             -- multi-step LIF sweep point T=32, N=2^27 float32 with
+                     fp32 spikes + packed spikes + final v.  Metric: HBM GB/s
+                     (algorithmic bytes 4TN + 4TN + TN/8 + 4N per step).
+
+Timing: W warm-up steps, then K steps bracketed by barrier + synchronize and
+CUDA events on the launching stream; the slowest rank's time is reported.
+Inputs are larger than L2 for 'lif'; for 'vgg16' a 256 MB buffer is written
+between steps to flush L2.  --impl reference times the reference's CPU
+algorithm (this repository's oracle restatement of it) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "triton-pass-analysis_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.samples = []
+        self.proc = None
+        self.gpu = gpu_index
+        self.window = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = self.samples
+        if self.window:
+            inside = [r for r in rows if self.window[0] - 0.05 <= r[0] <= self.window[1] + 0.25]
+            rows = inside or rows
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for _, line in rows:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        if args.impl == "reference":
+            return rank, world, local, None
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return rank, world, local, dist
+    if args.impl != "reference":
+        torch.cuda.set_device(0)
+    return 0, 1, 0, None
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(dist, value):
+    if dist is None:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(dist, value):
+    if dist is None:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------------------
+class LifWorkload:
+    name = "lif"
+
+    def __init__(self, T=32, N=1 << 27):
+        self.T, self.N = T, N
+        self.bytes_per_step = 4 * T * N + 4 * T * N + T * N // 8 + 4 * N
+        self.metric = "LIF kernel HBM GB/s (T=32, N=2^27, fp32 spikes + packed + final v)"
+        self.unit = "GB/s"
+        self.dtype = "f32"
+
+    def config(self):
+        return {"workload": "lif_sweep_T32_N2^27", "T": self.T, "N": self.N,
+                "outputs": "fp32 spikes + packed spikes + final v",
+                "l2": "inputs larger than L2 (16 GiB per step)"}
+
+    def setup(self, rank, world):
+        from snn_compiler.kernels import neurons as K
+        self.K = K
+        T, N = self.T, self.N
+        g = torch.Generator(device="cuda").manual_seed(rank)
+        self.x = (torch.randn(T, N, device="cuda", generator=g) + 0.5)
+        self.sp = torch.empty(T, N, device="cuda")
+        self.pk = torch.empty(T, (N + 31) // 32, device="cuda", dtype=torch.int32)
+        self.vo = torch.empty(N, device="cuda")
+        from snn_compiler import _lib
+        self._lib = _lib
+        self.L = _lib.lib()
+        self.launches_per_step = 1
+
+    def _launch(self, x, sp, pk, vo, stream):
+        st = self.L.snnb_neuron_multistep(
+            self._lib.ptr(x), 0, self.T, self.N, None, None, 1, 1, 0, 0.5, 0.5, None, 1, 0.0,
+            0, 1.0, None, None, self._lib.ptr(sp), 0, self._lib.ptr(pk), None,
+            self._lib.ptr(vo), stream)
+        self._lib.check(st, "snnb_neuron_multistep")
+
+    def step(self):
+        s = torch.cuda.current_stream().cuda_stream
+        import ctypes
+        self._launch(self.x, self.sp, self.pk, self.vo, ctypes.c_void_p(s))
+
+    def kernel_events(self, steps):
+        """Per-launch durations of the dominant kernel (here: the only one)."""
+        return None
+
+    def units_per_step(self):
+        return self.bytes_per_step / 1e9
+
+    # --- end to end through the public API with host buffers
+    def e2e_setup(self):
+        T, N = self.T, min(self.N, 1 << 24)
+        self.eN = N
+        self.hx = torch.randn(T, N).add_(0.5).pin_memory()
+        self.hpk = torch.empty(T, (N + 31) // 32, dtype=torch.int32).pin_memory()
+        self.hv = torch.empty(N).pin_memory()
+        self.e2e_bytes = 4 * T * N + 4 * T * N + T * N // 8 + 4 * N
+        self.h2d = 4 * T * N
+        self.d2h = 4 * T * ((N + 31) // 32) + 4 * N
+
+    def e2e_step(self):
+        xd = self.hx.to("cuda", non_blocking=True)
+        r = self.K.neuron_multistep(xd, decay_factor=0.5, input_scale=0.5, packed=True,
+                                    v_out=True)
+        self.hpk.copy_(r["packed"], non_blocking=True)
+        self.hv.copy_(r["v"], non_blocking=True)
+
+    def e2e_units(self):
+        return self.e2e_bytes / 1e9
+
+    def roofline(self, kernel_ms, peaks):
+        achieved = self.bytes_per_step / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"], "kernel": "neuron_vec8_kernel<float,float>",
+                "algorithmic_bytes_per_launch": self.bytes_per_step}
+
+    # --- CPU (oracle) path
+    def cpu_sample(self):
+        T, N = self.T, 1 << 22
+        x = (torch.randn(T, N, generator=torch.Generator().manual_seed(0)) + 0.5).numpy()
+        return {"T": T, "N": N, "x": x, "bytes": 4 * T * N + 4 * T * N + T * N // 8 + 4 * N}
+
+    def cpu_run(self, s, threads):
+        from oracle import neurons as ON, bitops as OB
+        o = ON.lif_multistep(s["x"], df=np.float32(0.5), sc=np.float32(0.5), want_v=True,
+                             nthreads=threads)
+        OB.pack_rows(o["spikes"])
+        return s["bytes"] / 1e9
+
+
+# ----------------------------------------------------------------------------------------
+def time_cpu(workload, threads, reps=3):
+    s = workload.cpu_sample()
+    workload.cpu_run(s, threads)          # warm-up
+    ts = []
+    units = 0
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        units = workload.cpu_run(s, threads)
+        ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    return units / med, s, med
+
+
+def run_reference(args, workload):
+    """CPU arm: the reference's algorithm (oracle restatement) on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from oracle import neurons as ON
+    cores = min(threads, ON.max_threads()) if workload.name == "lif" else threads
+    vals = []
+    s = workload.cpu_sample()
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        u = workload.cpu_run(s, threads)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            vals.append((u, dt))
+    tot_u = sum(u for u, _ in vals)
+    tot_t = sum(t for _, t in vals)
+    v = tot_u / tot_t
+    sample = {k: v_ for k, v_ in s.items() if isinstance(v_, (int, float, str))}
+    line = {"metric": workload.metric, "value": round(v, 3), "unit": workload.unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * tot_t / len(vals), 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": workload.dtype,
+            "data": "synthetic", "config": workload.config(), "impl": "reference",
+            "cpu_baseline": {"value": round(v, 3), "unit": workload.unit, "cores": cores,
+                             "kind": "port", "sample": json.dumps(sample)},
+            "e2e": {"value": round(v, 3), "unit": workload.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, workload):
+    rank, world, local, dist = dist_setup(args)
+    peaks = load_peaks()
+    workload.setup(rank, world)
+    flush = None
+    if getattr(workload, "flush_l2", False):
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(args.warmup):
+        workload.step()
+        if flush is not None:
+            flush.fill_(1)
+    barrier(dist)
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_wall0 = time.time()
+    for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(1)
+        ev[i][0].record(stream)
+        workload.step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    t_wall1 = time.time()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    my_ms = sum(step_ms)
+    total_ms = max_over_ranks(dist, my_ms)
+    kern = workload.kernel_events(args.steps)
+    kernel_ms = statistics.mean(kern) if kern else statistics.mean(step_ms)
+    kernel_ms = max_over_ranks(dist, kernel_ms)
+    if sampler:
+        sampler.mark(t_wall0, t_wall1)
+    clocks = sampler.stop() if sampler else None
+    units = sum_over_ranks(dist, workload.units_per_step() * args.steps)
+    value = units / (total_ms * 1e-3)
+
+    # end to end through the public API, host buffers, copies inside the timed region
+    workload.e2e_setup()
+    for _ in range(max(1, args.warmup)):
+        workload.e2e_step()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 10))
+    e0.record(stream)
+    for _ in range(e_steps):
+        workload.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    e_units = sum_over_ranks(dist, workload.e2e_units() * e_steps)
+    e2e = {"value": round(e_units / (e_ms * 1e-3), 3), "unit": workload.unit,
+           "h2d_bytes_per_step": int(workload.h2d), "d2h_bytes_per_step": int(workload.d2h)}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            threads = os.cpu_count() or 1
+            torch.set_num_threads(threads)
+            v, s, med = time_cpu(workload, threads)
+            sample = {k: v_ for k, v_ in s.items() if isinstance(v_, (int, float, str))}
+            cpu = {"value": round(v, 3), "unit": workload.unit, "cores": threads,
+                   "kind": "port", "sample": json.dumps(sample) + f" median {med:.3f}s"}
+        line = {"metric": workload.metric, "value": round(value, 3), "unit": workload.unit,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": workload.dtype,
+                "data": "synthetic", "config": workload.config(),
+                "roofline": workload.roofline(kernel_ms, peaks),
+                "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": int(workload.launches_per_step * args.steps),
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="lif", choices=["lif"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    wl = {"lif": LifWorkload}[args.workload]()
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,98 @@
+/*
+ * snnb200.h -- C ABI of libsnnb200.so, the sm_100a (B200) kernels behind the
+ * snn_compiler.kernels / snn_compiler.nn API.
+ *
+ * Every entry point
+ *   - takes plain device pointers, element counts and a CUDA stream
+ *     (snnb_stream_t is a cudaStream_t; NULL means the legacy default stream),
+ *   - launches asynchronously on that stream and never synchronises it,
+ *   - allocates nothing: the caller owns every input, output and workspace,
+ *   - returns an int status (SNNB_OK or a negative SNNB_ERR_*), never aborts and
+ *     never throws across the boundary.
+ * Shapes follow the reference's flattening: a multi-step tensor [T, B, ...] is
+ * [T, N] with N = numel of one step, in memory order.
+ */
+#ifndef SNNB200_H
+#define SNNB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* snnb_stream_t;
+
+/* status codes */
+#define SNNB_OK                 0
+#define SNNB_ERR_ARG           -1   /* bad pointer / size / alignment / combination */
+#define SNNB_ERR_UNSUPPORTED   -2   /* valid request this build does not implement */
+#define SNNB_ERR_CUDA          -3   /* a CUDA runtime call or launch failed */
+#define SNNB_ERR_TIMEOUT       -4   /* a bounded device-side wait gave up */
+#define SNNB_ERR_DEVICE        -5   /* a device-side check recorded an error */
+
+/* element types */
+#define SNNB_F32   0
+#define SNNB_F16   1
+#define SNNB_BF16  2
+#define SNNB_U8    3
+
+/* threshold modes, snn_compiler/kernels/neurons.py:66-68 */
+#define SNNB_THR_SCALAR       0
+#define SNNB_THR_PER_CHANNEL  1
+#define SNNB_THR_PER_NEURON   2
+
+/* ABI revision of this header; bumped on any signature change. */
+int snnb_abi_version(void);
+
+/* Human-readable text of a status code (static storage). */
+const char* snnb_status_string(int status);
+
+/* Text of the last CUDA error seen by this library on the calling thread. */
+const char* snnb_last_cuda_error(void);
+
+/*
+ * K2 -- multi-step IF / LIF / PLIF neuron over x [T, N].
+ *
+ * Replaces the Triton kernels and Python entry points
+ *   if_lif                      snn_compiler/kernels/neurons.py:311-376 (_if_lif_kernel :85-138)
+ *   fused_bias_if_lif           snn_compiler/kernels/fused.py:117-226   (_bias_if_lif_kernel :50-114)
+ *   fused_bias_if_lif_rate      snn_compiler/kernels/fused.py:303-382   (kernel :242-300)
+ *   fused_bias_if_lif_stateful  snn_compiler/kernels/fused.py:444-507   (kernel :398-441)
+ * in one launch.  Per element n and step t, every operation rounded to float32
+ * in this order (no FMA contraction):
+ *   in = x[t,n] (+ bias[c]) (+ residual[t,n]);  v = decay*v + input_scale*in;
+ *   s = v >= thr;  soft: v -= s*thr;  hard: v = s ? v_reset : v
+ * with c = n % C (channel_last) or (n / HW) % C.
+ *
+ * x, residual   : [T, N] of x_dtype (F32 / F16 / BF16); residual may be NULL.
+ * bias          : [C] float32 or NULL.
+ * plif_w        : NULL, or a device float32 scalar w; then input_scale = k and
+ *                 decay = 1 - k with k = sigmoid(w) (evaluated in double and
+ *                 rounded to float32), overriding the two float arguments.
+ * thr           : [C] (per channel) or [N] (per neuron) float32 for those modes.
+ * v_init        : [N] float32 initial potential, or NULL for zeros.
+ * outputs (any subset, NULL = not written):
+ *   spikes        [T, N] of spikes_dtype (F32 / F16 / BF16 / U8), values 0 or 1
+ *   spikes_packed [T, ceil(N/32)] uint32: bit i of word w of step t = s[t, 32w+i]
+ *   count         [N] float32 = sum over t of s  (rate-coded output)
+ *   v_out         [N] float32 potential after the last step
+ * Vectorised 16-byte loads are used when N is a multiple of 8 and every
+ * pointer is 16-byte aligned; otherwise a scalar path runs.
+ */
+int snnb_neuron_multistep(
+    const void* x, int x_dtype, int64_t T, int64_t N,
+    const float* bias, const void* residual, int64_t C, int64_t HW, int channel_last,
+    float decay, float input_scale, const float* plif_w,
+    int hard_reset, float v_reset,
+    int thr_mode, float thr_scalar, const float* thr,
+    const float* v_init,
+    void* spikes, int spikes_dtype,
+    uint32_t* spikes_packed, float* count, float* v_out,
+    snnb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNNB200_H */

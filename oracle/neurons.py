@@ -5,7 +5,8 @@ Python side of oracle/lif.c.  Parameter derivation follows the reference:
   LIF: df = 1 - 1/tau (or decay), sc = 1/tau if decay_input else 1.0
                                                       snn_compiler/kernels/neurons.py:352-354, :473-475
   PLIF (SpikingJelly ParametricLIFNode, no snn_compiler counterpart):
-       k = sigmoid(w) in float32, df = 1 - k, sc = k
+       k = sigmoid(w) evaluated in double and rounded to float32, df = 1 - k
+       (float32 subtraction), sc = k
 All arrays are flat in MEMORY order: x is [T, N] where N = numel of one step.
 """
 from __future__ import annotations
@@ -64,8 +65,8 @@ def neuron_params(neuron="if", *, tau=2.0, decay=None, decay_input=True, plif_w=
         sc = (1.0 / tau) if decay_input else 1.0
         return f32(df), f32(sc)
     if neuron == "plif":
-        w = np.float32(0.0 if plif_w is None else plif_w)
-        k = np.float32(1.0) / (np.float32(1.0) + np.exp(-w, dtype=np.float32))
+        w = np.float64(np.float32(0.0 if plif_w is None else plif_w))
+        k = np.float32(1.0 / (1.0 + np.exp(-w)))
         return np.float32(np.float32(1.0) - k), np.float32(k)
     raise ValueError(f"unknown neuron: {neuron!r}")
 

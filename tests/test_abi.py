@@ -1,0 +1,63 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol that
+include/snnb200.h declares, and rejects bad arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "snnb200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(snnb_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from snn_compiler import _lib
+    L = _lib.lib()
+    names = declared_functions()
+    assert "snnb_neuron_multistep" in names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert L.snnb_abi_version() >= 1
+
+
+def test_every_declared_entry_has_a_python_signature():
+    from snn_compiler import _lib
+    helpers = {"snnb_abi_version", "snnb_status_string", "snnb_last_cuda_error"}
+    for n in declared_functions():
+        if n not in helpers:
+            assert n in _lib.SIGNATURES, n
+
+
+def test_status_strings():
+    from snn_compiler import _lib
+    L = _lib.lib()
+    assert L.snnb_status_string(0) == b"ok"
+    assert L.snnb_status_string(-1) == b"invalid argument"
+    assert L.snnb_status_string(-4) == b"device wait timed out"
+
+
+def test_neuron_rejects_bad_arguments_without_a_device():
+    from snn_compiler import _lib
+    L = _lib.lib()
+    f = L.snnb_neuron_multistep
+    base = dict(x=None, xd=0, T=4, N=16, bias=None, res=None, C=1, HW=1, cl=0, df=0.5, sc=0.5,
+                w=None, hard=1, vr=0.0, mode=0, ts=1.0, thr=None, vinit=None, sp=None, sd=0,
+                pk=None, cnt=None, vo=None, st=None)
+
+    def call(**kw):
+        a = {**base, **kw}
+        return f(*a.values())
+    assert call(T=-1) == -1                      # negative T
+    assert call(N=-5) == -1                      # negative N
+    assert call(xd=7) == -1                      # unknown x dtype
+    assert call(mode=1) == -1                    # per-channel threshold without a pointer
+    assert call(mode=9) == -1                    # unknown threshold mode
+    assert call(x=None) == -1                    # T > 0 with no input
+    assert call(N=0) == 0                        # empty input is a no-op

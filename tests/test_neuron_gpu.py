@@ -1,0 +1,192 @@
+"""K2 parity: the sm_100a multi-step neuron vs the CPU oracle and the reference's
+golden vectors (bit-exact spikes, counts and potentials)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import neurons as ON
+from oracle import params as OP
+from test_oracle_golden import LIF, N_CASES, lif_case
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _nk():
+    from snn_compiler import kernels as K
+    return K
+
+
+def _to_dev(x_np, dtype, layout):
+    x = torch.from_numpy(x_np).to(getattr(torch, dtype))
+    if layout == "NHWC":
+        T_, B_, C_, H_, W_ = x.shape
+        x = x.reshape(T_ * B_, C_, H_, W_).contiguous(memory_format=torch.channels_last)
+        return x.to(DEV).view(T_, B_, C_, H_, W_)
+    return x.to(DEV)
+
+
+@pytest.mark.parametrize("i", range(N_CASES))
+def test_if_lif_matches_reference_golden(i):
+    x, y, m = lif_case(i)
+    K = _nk()
+    xd = _to_dev(x, m["dtype"], m["layout"])
+    thr = m["thr"]
+    thr = float(thr) if np.ndim(thr) == 0 else torch.from_numpy(np.asarray(thr, np.float32)).to(DEV)
+    decay = None if np.isnan(m["decay"]) else float(m["decay"])
+    out = K.if_lif(xd, neuron=m["neuron"], tau=float(m["tau"]), decay=decay,
+                   decay_input=bool(m["di"]), soft_reset=bool(m["soft"]), v_threshold=thr,
+                   v_reset=float(m["v_reset"]), layout=m["layout"])
+    assert out.dtype == xd.dtype and out.stride() == xd.stride()
+    got = out.float().cpu().numpy().astype(np.uint8)
+    assert np.array_equal(got, y), (m, int((got != y).sum()))
+
+
+def test_rate_coded_matches_reference_golden():
+    K = _nk()
+    for r in range(int(LIF["n_rate"])):
+        k = f"r{r:03d}"
+        neuron, decay, soft = [str(s) for s in LIF[k + "_meta"]]
+        x = torch.from_numpy(LIF[k + "_x"]).to(DEV)
+        cnt = K.fused_bias_if_lif_rate(x, None, neuron=neuron, tau=2.0,
+                                       decay=None if decay == "None" else float(decay),
+                                       soft_reset=soft == "True", v_threshold=1.0)
+        assert np.array_equal(cnt.cpu().numpy(), LIF[k + "_count"]), k
+
+
+CASES = [
+    # (T, N, C, dtype, bias, residual, thr_mode, hard)
+    (4, 1 << 16, 16, "float32", False, False, "scalar", True),
+    (4, 1 << 16, 64, "bfloat16", True, False, "per_c", True),
+    (8, 12345, 5, "float32", True, True, "per_n", False),
+    (3, 33, 3, "float16", False, True, "scalar", False),
+    (1, 7, 7, "float32", True, False, "per_c", True),
+    (33, 4096, 16, "float32", True, True, "per_c", False),
+    (5, 1000, 8, "float32", False, False, "per_n", True),
+    (0, 4096, 16, "float32", True, False, "scalar", True),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_all_outputs_against_oracle(case):
+    """Every output mode at once (spikes, packed bits, count, final v) with v_init,
+    on a 3-D [T, N/C, C] tensor (channel = last axis): vector path when N % 8 == 0,
+    scalar path otherwise."""
+    T, N, C, dt, has_b, has_r, mode, hard = case
+    K = _nk()
+    g = OP.gen(1000 + N + T)
+    x = (torch.randn(T, N, generator=g) + 0.5).to(getattr(torch, dt))
+    bias = torch.randn(C, generator=g) * 0.3 if has_b else None
+    res = (torch.randn(T, N, generator=g) * 0.5).to(x.dtype) if has_r else None
+    if mode == "scalar":
+        thr = 0.9
+    elif mode == "per_c":
+        thr = torch.rand(C, generator=g) * 0.5 + 0.5
+    else:
+        thr = torch.rand(N, generator=g) + 0.5
+    v_init = torch.randn(N, generator=g) * 0.3
+    shape = (T, N // C, C)
+    r = K.neuron_multistep(
+        x.to(DEV).view(shape), decay_factor=0.75, input_scale=0.3, soft_reset=not hard,
+        v_reset=-0.2, v_threshold=thr if isinstance(thr, float) else thr.to(DEV),
+        bias=None if bias is None else bias.to(DEV),
+        residual=None if res is None else res.to(DEV).view(shape),
+        v_init=v_init.to(DEV), packed=True, count=True, v_out=True)
+    o = ON.lif_multistep(x.float().numpy().reshape(T, N), df=np.float32(0.75),
+                         sc=np.float32(0.3), hard_reset=hard, v_reset=-0.2,
+                         thr=thr if isinstance(thr, float) else thr.numpy(),
+                         bias=None if bias is None else bias.numpy(),
+                         residual=None if res is None else res.float().numpy(),
+                         C=C, HW=1, channel_last=True, v_init=v_init.numpy(),
+                         want_count=True, want_v=True)
+    assert r["spikes"].dtype == x.dtype
+    assert np.array_equal(r["spikes"].float().cpu().numpy().reshape(T, N), o["spikes"])
+    assert np.array_equal(r["count"].cpu().numpy().reshape(-1), o["count"])
+    assert np.array_equal(r["v"].cpu().numpy().reshape(-1), o["v"])
+    from oracle import bitops as OB
+    pk = r["packed"].cpu().numpy().view(np.uint32)
+    assert np.array_equal(pk, OB.pack_rows(o["spikes"]).reshape(T, -1))
+
+
+def test_nhwc_bias_per_channel_matches_oracle():
+    K = _nk()
+    g = OP.gen(77)
+    T, B, C, H, W = 4, 3, 24, 5, 7
+    x = torch.randn(T, B, C, H, W, generator=g) + 0.4
+    bias = torch.randn(C, generator=g) * 0.2
+    thr = torch.rand(C, generator=g) * 0.5 + 0.6
+    xd = x.reshape(T * B, C, H, W).contiguous(memory_format=torch.channels_last).to(DEV)
+    xd = xd.view(T, B, C, H, W)
+    out = K.fused_bias_if_lif(xd, bias.to(DEV), neuron="lif", tau=2.0, v_threshold=thr.to(DEV),
+                              layout="NHWC")
+    mem = x.permute(0, 1, 3, 4, 2).reshape(T, -1).numpy()
+    o = ON.lif_multistep(mem, df=np.float32(0.5), sc=np.float32(0.5), thr=thr.numpy(),
+                         bias=bias.numpy(), C=C, HW=H * W, channel_last=True)
+    got = out.permute(0, 1, 3, 4, 2).reshape(T, -1).cpu().numpy()
+    assert np.array_equal(got, o["spikes"])
+
+
+def test_stateful_chunked_equals_full_on_device():
+    """snn_compiler/tests/test_largeT_and_rate.py:106-132 on the device."""
+    from snn_compiler.nn import StatefulLIFNode, LIFNode
+    g = OP.gen(5)
+    T = 32
+    x = torch.randn(T, 2, 16, 14, 14, generator=g).to(DEV)
+    for soft in (True, False):
+        ref = LIFNode(tau=2.0, soft_reset=soft)(x)
+        for chunk in (4, 8, 16, 32):
+            mod = StatefulLIFNode(tau=2.0, soft_reset=soft)
+            v = None
+            parts = []
+            for i in range(0, T, chunk):
+                s, v = mod(x[i:i + chunk].contiguous(), v_init=v, return_v=True)
+                parts.append(s)
+            assert torch.equal(torch.cat(parts), ref)
+
+
+def test_plif_matches_lif_at_w0_and_oracle_elsewhere():
+    from snn_compiler.nn import PLIFNode, LIFNode
+    g = OP.gen(9)
+    x = (torch.randn(8, 4, 1000, generator=g) + 0.5).to(DEV)
+    p = PLIFNode(init_tau=2.0).to(DEV)
+    assert torch.equal(p(x), LIFNode(tau=2.0)(x))
+    for w in (-1.3, 0.7):
+        with torch.no_grad():
+            p.w.fill_(w)
+        df, sc = ON.neuron_params("plif", plif_w=w)
+        o = ON.lif_multistep(x.cpu().reshape(8, -1).numpy(), df=df, sc=sc)
+        got = p(x).cpu().reshape(8, -1).numpy()
+        assert np.array_equal(got, o["spikes"])
+
+
+def test_large_lif_sweep_shape_sampled_against_oracle():
+    """Config-1 shape T=8, N=2^24: bit-exact on a random sample of 2^18 neurons,
+    plus internal consistency of packed bits, counts and spikes everywhere."""
+    K = _nk()
+    T, N = 8, 1 << 24
+    x = OP.lif_input(0, T=T, N=N)
+    xd = x.to(DEV)
+    r = K.neuron_multistep(xd.view(T, 1, N), decay_factor=0.5, input_scale=0.5,
+                           packed=True, count=True, v_out=True)
+    idx = torch.randperm(N, generator=OP.gen(1))[: 1 << 18].sort().values
+    o = ON.lif_multistep(x[:, idx].numpy(), df=np.float32(0.5), sc=np.float32(0.5),
+                         want_count=True, want_v=True)
+    sp = r["spikes"].view(T, N)
+    assert np.array_equal(sp[:, idx.to(DEV)].cpu().numpy(), o["spikes"])
+    assert np.array_equal(r["v"].view(N)[idx.to(DEV)].cpu().numpy(), o["v"])
+    assert torch.equal(sp.sum(0), r["count"].view(N))
+    bits = ((r["packed"].view(torch.int32).unsqueeze(-1) >> torch.arange(32, device=DEV)) & 1)
+    assert torch.equal(bits.reshape(T, -1)[:, :N].float(), sp)
+
+
+def test_bad_arguments_raise_like_reference():
+    K = _nk()
+    x = torch.randn(4, 2, 8, device=DEV)
+    with pytest.raises(ValueError):
+        K.if_lif(x, neuron="cuba")
+    with pytest.raises(ValueError):
+        K.if_lif(x, v_threshold=torch.ones(5, device=DEV))
+    with pytest.raises(AssertionError):
+        K.if_lif(x.cpu())
+    with pytest.raises(AssertionError):
+        K.if_lif(x.transpose(1, 2))

@@ -1,0 +1,44 @@
+// Shared helpers for the sm_100a kernels of libsnnb200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "snnb200.h"
+
+namespace snnb {
+
+// Records the text of a CUDA error for snnb_last_cuda_error() and maps it to a status.
+int record_cuda_error(cudaError_t e);
+
+// Status of the most recent launch on this thread (cudaGetLastError, which also clears it).
+inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SNNB_OK : record_cuda_error(e);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T spike_value(bool s);
+template <> __device__ __forceinline__ float spike_value<float>(bool s) { return s ? 1.0f : 0.0f; }
+template <> __device__ __forceinline__ __half spike_value<__half>(bool s) {
+    return __ushort_as_half(s ? (unsigned short)0x3C00 : (unsigned short)0);
+}
+template <> __device__ __forceinline__ __nv_bfloat16 spike_value<__nv_bfloat16>(bool s) {
+    return __ushort_as_bfloat16(s ? (unsigned short)0x3F80 : (unsigned short)0);
+}
+template <> __device__ __forceinline__ uint8_t spike_value<uint8_t>(bool s) { return s ? 1 : 0; }
+
+// Membrane charge with every product and the sum rounded separately to float32
+// (no FMA contraction), matching the reference's eager torch-CPU loop.
+__device__ __forceinline__ float charge(float v, float df, float sc, float in) {
+    return __fadd_rn(__fmul_rn(df, v), __fmul_rn(sc, in));
+}
+
+}  // namespace snnb
