@@ -91,6 +91,36 @@ int snnb_neuron_multistep(
     uint32_t* spikes_packed, float* count, float* v_out,
     snnb_stream_t stream);
 
+/*
+ * K4 -- bit packing of {0,1} or {-1,+1} rows into 32-bit words.
+ *
+ * Replaces _pack_N_kernel / _pack_N (snn_compiler/kernels/attention.py:195-242) and
+ * the torch bit-pack bitpack_N (snn_compiler/explore/attention/phase6b_bitpack.py:35-46):
+ * element k of row r goes to bit (k % 32) of word out[r * ldw + k / 32] (LSB first);
+ * words from ceil(K/32) to ldw-1 are written as zero.
+ * x        : [rows, K] of SNNB_F32 / F16 / BF16 / U8, row-major.
+ * positive : 0 -> bit = (x != 0)  ({0,1} spikes);  1 -> bit = (x > 0)  ({-1,+1} signs).
+ * ldw      : words per packed row, >= ceil(K/32) (use a multiple of 4 for snnb_bgemm).
+ */
+int snnb_bitpack(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ldw,
+                 int positive, uint32_t* out, snnb_stream_t stream);
+
+/*
+ * K4 -- binary GEMM over packed rows with AND / XOR + popcount.
+ *
+ * Replaces _ktv_popcount_kernel (snn_compiler/kernels/attention.py:217-233) and
+ * spike_ktv_popcount (attention.py:245-258), generalised:
+ *   mode 0: C[m,n] = sum_k A[m,k] B[n,k]                 A, B in {0,1}
+ *   mode 1: C[m,n] = sum_k A[m,k] (2 Bbit[n,k] - 1)      A in {0,1}, B in {-1,+1}
+ *   mode 2: C[m,n] = sum_k (2 Abit - 1)(2 Bbit - 1)      A, B in {-1,+1} (XNOR form)
+ * A [M, ldw], B [N, ldw] packed as by snnb_bitpack (16-byte aligned, ldw % 4 == 0,
+ * zero padding words); C [M, N] int32 row-major, exact.
+ * splits: number of k-range splits (0 = choose to fill the GPU); with more than
+ * one split C is zeroed with cudaMemsetAsync and partial sums are added atomically.
+ */
+int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int64_t N,
+               int64_t K, int64_t ldw, int mode, int splits, snnb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
