@@ -121,6 +121,64 @@ int snnb_bitpack(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld
 int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int64_t N,
                int64_t K, int64_t ldw, int mode, int splits, snnb_stream_t stream);
 
+/*
+ * K1 -- fused conv3x3 (stride 1, pad 1) + folded-BN bias + multi-step LIF (+ 2x2 max-pool)
+ * on the tcgen05 tensor cores (bf16 x bf16 -> f32 in TMEM, operands fed by TMA).
+ *
+ * Replaces, per layer, F.conv2d + _bias_if_lif_kernel + nn.MaxPool2d of
+ *   FusedConvBNNeuron.forward   snn_compiler/nn/modules.py:347-357 (_conv_bn :324-345)
+ *   fused_bias_if_lif           snn_compiler/kernels/fused.py:117-226
+ *   VGGSNN pool                 snn_compiler/zoo/vgg.py:56, :100-104 (pool='max')
+ * x    : bf16 spikes / activations NHWC [T*B, H, W, Cin] (frame t*B + b), Cin % 64 == 0
+ * w    : bf16 folded weights [Cout, 3, 3, Cin] (K-major), Cout % 32 == 0
+ * bias : f32 [Cout] folded bias b' (added inside the neuron, fused.py:106-108)
+ * out  : bf16 spikes NHWC [T*B, Ho, Wo, Cout], Ho = H/2 and Wo = W/2 when pool != 0
+ * The neuron is v = decay*v + input_scale*(conv + b'); s = v >= v_threshold; reset.
+ * Pixel blocks of 128 rows: W must divide 128 or be a multiple of 128, likewise H for
+ * the rows per block; pooling needs even H and W.
+ */
+int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin,
+                     const void* w, const float* bias, int64_t Cout,
+                     float decay, float input_scale, float v_threshold, float v_reset,
+                     int hard_reset, int pool, void* out, snnb_stream_t stream);
+
+/*
+ * K1, linear variant: spikes [T*B, K] bf16 @ w [N, K] bf16 + bias -> multi-step LIF ->
+ * bf16 spikes [T*B, N].  Replaces FusedLinearNeuron.forward
+ * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 64 == 0.
+ */
+int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                    const float* bias, int64_t N, float decay, float input_scale,
+                    float v_threshold, float v_reset, int hard_reset, void* out,
+                    snnb_stream_t stream);
+
+/*
+ * K1, classifier head: out[b, n] = mean over t of (x[t*B+b] @ w[n]^T + bias[n]), f32.
+ * Replaces the last nn.Linear of VGGSNN (snn_compiler/zoo/vgg.py:84, :111-114) and the
+ * caller's mean over T (examples/vgg16_snn/vgg16_test.py:243).  K % 64 == 0, N <= 64.
+ */
+int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                     const float* bias, int64_t N, float* out, snnb_stream_t stream);
+
+/*
+ * First (real-valued input) layer of a spiking CNN: float32 direct conv3x3 (pad 1)
+ * + bias + multi-step LIF (+ 2x2 max-pool) -> bf16 spikes NHWC [T*B, Ho, Wo, Cout].
+ * Replaces the first FusedConvBNNeuron of VGGSNN, whose input is the float image
+ * (snn_compiler/zoo/vgg.py:88-94).  x: f32 NCHW [Ti, B, Cin, H, W]; Ti = T, or Ti = 1
+ * when the same image drives every step (direct encoding: the conv runs once).
+ * w: f32 [Cout, Cin, 3, 3]; Cout % 8 == 0.
+ */
+int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_t B, int64_t Cin,
+                        int64_t H, int64_t W, const float* w, const float* bias, int64_t Cout,
+                        float decay, float input_scale, float v_threshold, float v_reset,
+                        int hard_reset, int pool, void* out, snnb_stream_t stream);
+
+/*
+ * Reads and clears the device status word that kernels with bounded waits write
+ * (SNNB_ERR_TIMEOUT after a wait gave up).  Synchronises `stream`.
+ */
+int snnb_read_device_status(snnb_stream_t stream, int* status_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,162 @@
+"""K1 parity: the fused tcgen05 conv3x3 / linear + bias + multi-step LIF (+ max-pool)
+kernels vs the CPU oracle (torch-CPU float32 conv of the same bf16 weights + the
+oracle neuron).
+
+The products are exact in both (spikes x bf16 weights); only the float32 summation
+order differs, so the criterion is BASELINE's: spikes may differ only at neurons
+whose first disagreement sits where the oracle's charged potential is within 1e-4
+of the threshold, and on at most 0.1% of all spikes; pooled outputs must equal the
+2x2 OR of the kernel's own unpooled spikes exactly.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import params as OP
+from oracle import vgg as OV
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+THR = 1.0
+
+
+def _C():
+    from snn_compiler.kernels import conv
+    return conv
+
+
+def flip_check(gpu, ref, vpre, thr=THR, window=1e-4, max_frac=1e-3):
+    """gpu, ref, vpre: [T, ...] float tensors.  Every neuron's first mismatching step
+    must have |vpre - thr| < window; total mismatch fraction <= max_frac."""
+    T = gpu.shape[0]
+    g = gpu.reshape(T, -1)
+    r = ref.reshape(T, -1)
+    v = vpre.reshape(T, -1)
+    mism = g != r
+    frac = mism.float().mean().item()
+    assert frac <= max_frac, f"spike mismatch fraction {frac:.2e}"
+    if mism.any():
+        first = torch.argmax(mism.int(), dim=0)
+        cols = mism.any(0).nonzero().squeeze(1)
+        vt = v[first[cols], cols]
+        assert ((vt - thr).abs() < window).all(), (vt - thr).abs().max()
+    return frac
+
+
+def _layer_case(T, B, Cin, Cout, H, p, seed, pool):
+    g = OP.gen(seed)
+    x = (torch.rand(T, B, Cin, H, H, generator=g) < p).float()
+    w = (torch.randn(Cout, Cin, 3, 3, generator=g) * (2.0 / (9 * Cin)) ** 0.5)
+    w = w.to(torch.bfloat16).float()
+    b = torch.rand(Cout, generator=g) * 0.9 + 0.3
+    return x, w, b
+
+
+GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x32 input
+    (4, 1, 64, 64, 32),
+    (4, 2, 64, 128, 16),
+    (4, 2, 128, 256, 8),
+    (4, 8, 256, 512, 4),
+    (4, 32, 512, 512, 2),
+    (3, 2, 64, 64, 8),
+    (6, 4, 192, 96, 8),
+]
+
+
+@pytest.mark.parametrize("geom", GEOMS)
+def test_conv3x3_lif_against_oracle(geom):
+    T, B, Cin, Cout, H = geom
+    C = _C()
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.15, hash(geom) & 0xffff, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    wd = C.weight_khwc(w).to(DEV)
+    bd = b.to(DEV)
+    y = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, pool=False)
+    yp = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, pool=True) if H % 2 == 0 else None
+    assert C.device_status() == 0
+    s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True)
+    got = y.float().cpu().permute(0, 1, 4, 2, 3)                        # -> [T,B,C,H,W]
+    assert got.sum() > 0, "degenerate case: no spikes"
+    flip_check(got, s, vpre)
+    if yp is not None:
+        own = F.max_pool2d(got.reshape(T * B, Cout, H, H), 2, 2).reshape(T, B, Cout, H // 2, H // 2)
+        assert torch.equal(yp.float().cpu().permute(0, 1, 4, 2, 3), own)
+
+
+def test_conv3x3_soft_reset_and_if_neuron():
+    C = _C()
+    T, B, Cin, Cout, H = 4, 2, 64, 64, 8
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.3, 11, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    for neuron, soft in (("if", True), ("lif", True), ("if", False)):
+        y = C.conv3x3_lif(xd, C.weight_khwc(w).to(DEV), b.to(DEV), neuron=neuron, tau=2.0,
+                          soft_reset=soft, v_threshold=0.8, v_reset=-0.1)
+        from oracle import neurons as ON
+        yc = F.conv2d(x.reshape(T * B, Cin, H, H), w, None, padding=1).reshape(T, B, Cout, H, H)
+        df, sc = ON.neuron_params(neuron, tau=2.0)
+        o = ON.lif_multistep(yc.reshape(T, -1).numpy(), df=df, sc=sc, hard_reset=not soft,
+                             v_reset=-0.1, thr=0.8, bias=b.numpy(), C=Cout, HW=H * H,
+                             want_vpre=True)
+        got = y.float().cpu().permute(0, 1, 4, 2, 3)
+        flip_check(got, torch.from_numpy(o["spikes"]).reshape(got.shape),
+                   torch.from_numpy(o["vpre"]).reshape(got.shape), thr=0.8)
+
+
+@pytest.mark.parametrize("TBKN", [(4, 64, 512, 4096), (4, 8, 4096, 256), (2, 130, 128, 96)])
+def test_linear_lif_against_oracle(TBKN):
+    T, B, K, N = TBKN
+    C = _C()
+    g = OP.gen(K + N)
+    x = (torch.rand(T, B, K, generator=g) < 0.2).float()
+    w = (torch.randn(N, K, generator=g) * (2.0 / K) ** 0.5).to(torch.bfloat16).float()
+    b = torch.rand(N, generator=g) * 0.9 + 0.3
+    y = C.linear_lif(x.to(torch.bfloat16).to(DEV), w.to(torch.bfloat16).to(DEV), b.to(DEV),
+                     tau=2.0, v_threshold=THR)
+    yc = F.linear(x.reshape(T * B, K), w).reshape(T, B, N)
+    s, vpre = OV.lif_seq(yc, b, want_vpre=True)
+    got = y.float().cpu()
+    assert got.sum() > 0
+    flip_check(got, s, vpre)
+
+
+@pytest.mark.parametrize("TBKN", [(4, 64, 4096, 10), (4, 8, 512, 64), (3, 5, 128, 16)])
+def test_linear_mean_against_oracle(TBKN):
+    T, B, K, N = TBKN
+    C = _C()
+    g = OP.gen(3 * K + N)
+    x = (torch.rand(T, B, K, generator=g) < 0.2).float()
+    w = (torch.randn(N, K, generator=g) * (2.0 / K) ** 0.5).to(torch.bfloat16).float()
+    b = torch.randn(N, generator=g) * 0.1
+    y = C.linear_mean(x.to(torch.bfloat16).to(DEV), w.to(torch.bfloat16).to(DEV), b.to(DEV))
+    ref = (F.linear(x.reshape(T * B, K), w) + b).reshape(T, B, N).mean(0)
+    assert torch.allclose(y.cpu(), ref, rtol=1e-5, atol=1e-5), (y.cpu() - ref).abs().max()
+
+
+@pytest.mark.parametrize("static", [True, False])
+@pytest.mark.parametrize("pool", [False, True])
+def test_first_conv_lif_against_oracle(static, pool):
+    C = _C()
+    T, B, Cin, Cout, H = 4, 3, 3, 64, 32
+    g = OP.gen(21)
+    img = torch.rand(1 if static else T, B, Cin, H, H, generator=g)
+    w = torch.randn(Cout, Cin, 3, 3, generator=g) * (2.0 / 27) ** 0.5
+    b = torch.rand(Cout, generator=g) * 0.6 + 0.3
+    y = C.first_conv_lif(img.to(DEV), w.to(DEV), b.to(DEV), T=T, tau=2.0, v_threshold=THR,
+                         pool=pool)
+    x = img.expand(T, B, Cin, H, H) if static else img
+    s, p, vpre = OV.conv_bn_lif_pool(x.contiguous(), w, b, pool=pool, want_vpre=True)
+    got = y.float().cpu().permute(0, 1, 4, 2, 3)
+    if not pool:
+        flip_check(got, s, vpre)
+    else:
+        mism = (got != p).float().mean().item()
+        assert mism <= 1e-3
+
+
+def test_bad_geometry_is_rejected():
+    C = _C()
+    x = torch.zeros(4, 1, 8, 8, 48, device=DEV, dtype=torch.bfloat16)     # Cin % 64 != 0
+    w = torch.zeros(64, 3, 3, 48, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        C.conv3x3_lif(x, w, torch.zeros(64, device=DEV))

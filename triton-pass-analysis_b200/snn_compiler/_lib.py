@@ -30,6 +30,12 @@ SIGNATURES = {
                               P, P, I32, P, P, P, P],
     "snnb_bitpack": [P, I32, I64, I64, I64, I32, P, P],
     "snnb_bgemm": [P, P, P, I64, I64, I64, I64, I32, I32, P],
+    "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P, P],
+    "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, P],
+    "snnb_linear_mean": [P, I64, I64, I64, P, P, I64, P, P],
+    "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
+                            P],
+    "snnb_read_device_status": [P, P],
 }
 
 _lib = None

@@ -1,0 +1,181 @@
+"""Fused conv / linear + bias + multi-step LIF (+ max-pool) entry points (K1).
+
+Low-level entries work on channels-last frames, the layout the kernels stream:
+  conv3x3_lif(x [T, B, H, W, Cin] bf16, w [Cout, 3, 3, Cin] bf16, bias f32) -> spikes
+  linear_lif(x [T, B, K] bf16, w [N, K] bf16, bias)                        -> spikes
+  linear_mean(x [T, B, K] bf16, w [N, K] bf16, bias)                       -> f32 [B, N]
+  first_conv_lif(img f32 [Ti, B, Cin, H, W], w f32 [Cout, Cin, 3, 3], bias) -> spikes
+The reference-API entries conv_neuron / linear_neuron / conv_bn_neuron
+(snn_compiler/kernels/fused.py:513-611) sit on top of them.
+
+Each call is one launch of libsnnb200.so; the conv runs on tcgen05 tensor cores
+(bf16 operands, f32 accumulation in TMEM) with the neuron in the epilogue.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from .fused import fold_conv_bn
+from .neurons import neuron_coeffs
+
+
+def _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset):
+    if not isinstance(v_threshold, (int, float)):
+        raise NotImplementedError("the fused conv / linear kernels take a scalar v_threshold")
+    df, sc = neuron_coeffs(neuron, tau, decay, decay_input)
+    return float(df), float(sc), float(v_threshold), float(v_reset), 0 if soft_reset else 1
+
+
+def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
+                tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
+                v_threshold=1.0, v_reset: float = 0.0, pool: bool = False,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1:3] == (3, 3)
+    T, B, H, W, Cin = x.shape
+    Cout = w.shape[0]
+    assert w.shape[3] == Cin, (tuple(w.shape), Cin)
+    assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == Cout
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    Ho, Wo = (H // 2, W // 2) if pool else (H, W)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_conv3x3_lif(_lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias),
+                                     Cout, df, sc, thr, vr, hard, int(bool(pool)), _lib.ptr(out),
+                                     _lib.stream_of(x))
+    _lib.check(st, "snnb_conv3x3_lif")
+    return out
+
+
+def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
+               tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
+               v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None):
+    """x [T, B, K] bf16 @ w[N, K]^T + bias -> LIF -> spikes [T, B, N] bf16."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
+    T, B, K = x.shape
+    N = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.numel() == N
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    if out is None:
+        out = torch.empty(T, B, N, device=x.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_linear_lif(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N, df, sc,
+                                    thr, vr, hard, _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_linear_lif")
+    return out
+
+
+def linear_mean(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """mean over T of (x[t] @ w^T + bias): x [T, B, K] bf16 -> f32 [B, N] (N <= 64)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
+    T, B, K = x.shape
+    N = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.numel() == N
+    if out is None:
+        out = torch.empty(B, N, device=x.device, dtype=torch.float32)
+    st = _lib.lib().snnb_linear_mean(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N,
+                                     _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_linear_mean")
+    return out
+
+
+def first_conv_lif(img: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, T: int,
+                   neuron: str = "lif", tau: float = 2.0, decay=None, decay_input: bool = True,
+                   soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                   pool: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Real-valued input layer: img f32 [Ti, B, Cin, H, W] (Ti = T, or 1 for direct
+    encoding) with f32 weights [Cout, Cin, 3, 3] -> spikes [T, B, Ho, Wo, Cout] bf16."""
+    assert img.is_cuda and img.dtype == torch.float32 and img.is_contiguous() and img.ndim == 5
+    assert w.dtype == torch.float32 and w.is_contiguous() and w.shape[2:] == (3, 3)
+    Ti, B, Cin, H, W = img.shape
+    Cout = w.shape[0]
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    Ho, Wo = (H // 2, W // 2) if pool else (H, W)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout, device=img.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_first_conv_lif(_lib.ptr(img), Ti, T, B, Cin, H, W, _lib.ptr(w),
+                                        _lib.ptr(bias), Cout, df, sc, thr, vr, hard,
+                                        int(bool(pool)), _lib.ptr(out), _lib.stream_of(img))
+    _lib.check(st, "snnb_first_conv_lif")
+    return out
+
+
+def device_status(stream_tensor: torch.Tensor | None = None) -> int:
+    """Read and clear the device status word (SNNB_ERR_TIMEOUT after a bounded wait gave up)."""
+    import ctypes
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    v = ctypes.c_int(0)
+    _lib.check(_lib.lib().snnb_read_device_status(s, ctypes.byref(v)), "snnb_read_device_status")
+    return v.value
+
+
+# ---- reference-API entries ----------------------------------------------------------------
+def weight_khwc(w: torch.Tensor) -> torch.Tensor:
+    """torch conv weight [Cout, Cin, 3, 3] -> the kernels' K-major [Cout, 3, 3, Cin] bf16."""
+    return w.detach().permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)
+
+
+def _to_frames(x_seq: torch.Tensor) -> torch.Tensor:
+    """[T, B, C, H, W] (NCHW or channels-last view) -> contiguous [T, B, H, W, C] bf16."""
+    return x_seq.permute(0, 1, 3, 4, 2).to(torch.bfloat16).contiguous()
+
+
+def _from_frames(y: torch.Tensor, dtype, layout: str) -> torch.Tensor:
+    """[T, B, H, W, C] -> [T, B, C, H, W] view (channels-last storage) or contiguous."""
+    v = y.permute(0, 1, 4, 2, 3)
+    if layout == "NHWC":
+        return v.to(dtype)
+    return v.contiguous().to(dtype)
+
+
+def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=1,
+                neuron: str = "if", tau: float = 2.0, decay=None, decay_input: bool = True,
+                soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                layout: str = "NCHW"):
+    """conv + bias + neuron (reference fused.py:513-551).  The fused kernel covers the
+    spiking-CNN case: 3x3, stride 1, padding 1, dilation 1, groups 1, Cin % 64 == 0."""
+    if tuple(weight.shape[2:]) != (3, 3) or _pair(stride) != (1, 1) or _pair(padding) != (1, 1) \
+            or _pair(dilation) != (1, 1) or groups != 1:
+        raise NotImplementedError("fused conv kernel: 3x3, stride 1, padding 1, groups 1 only")
+    x = _to_frames(x_seq)
+    Cout = weight.shape[0]
+    b = bias.detach().float().contiguous() if bias is not None else \
+        torch.zeros(Cout, device=x.device)
+    y = conv3x3_lif(x, weight_khwc(weight), b, neuron=neuron, tau=tau, decay=decay,
+                    decay_input=decay_input, soft_reset=soft_reset, v_threshold=v_threshold,
+                    v_reset=v_reset)
+    return _from_frames(y, x_seq.dtype, layout)
+
+
+def linear_neuron(x_seq, weight, bias, *, neuron: str = "if", tau: float = 2.0, decay=None,
+                  decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
+                  v_reset: float = 0.0):
+    """linear + bias + neuron (reference fused.py:554-579); in_features % 64 == 0."""
+    T, B = x_seq.shape[:2]
+    x = x_seq.reshape(T, B, -1).to(torch.bfloat16).contiguous()
+    N = weight.shape[0]
+    b = bias.detach().float().contiguous() if bias is not None else \
+        torch.zeros(N, device=x.device)
+    y = linear_lif(x, weight.detach().to(torch.bfloat16).contiguous(), b, neuron=neuron,
+                   tau=tau, decay=decay, decay_input=decay_input, soft_reset=soft_reset,
+                   v_threshold=v_threshold, v_reset=v_reset)
+    return y.to(x_seq.dtype)
+
+
+def conv_bn_neuron(x_seq, conv_w, conv_b, bn_w, bn_b, bn_mean, bn_var, bn_eps, *, stride=1,
+                   padding=0, dilation=1, groups=1, **neuron_kwargs):
+    """conv + BN (folded on the host) + neuron (reference fused.py:602-611)."""
+    new_w, new_b = fold_conv_bn(conv_w, conv_b, bn_w, bn_b, bn_mean, bn_var, bn_eps)
+    return conv_neuron(x_seq, new_w, new_b, stride=stride, padding=padding, dilation=dilation,
+                       groups=groups, **neuron_kwargs)
+
+
+def _pair(v):
+    return tuple(v) if isinstance(v, (tuple, list)) else (v, v)
