@@ -171,7 +171,8 @@ class LifWorkload:
                 "outputs": "fp32 spikes + packed spikes + final v",
                 "l2": "inputs larger than L2 (16 GiB per step)"}
 
-    def setup(self, rank, world):
+    def setup(self, rank, world, dist=None):
+        self.world = world
         from snn_compiler.kernels import neurons as K
         self.K = K
         T, N = self.T, self.N
@@ -246,6 +247,139 @@ class LifWorkload:
         return s["bytes"] / 1e9
 
 
+
+class VggWorkload:
+    """VGG16-SNN T=4 inference, batch 64 per GPU (config 0 at the benchmark batch)."""
+    name = "vgg16"
+    flush_l2 = True
+
+    def __init__(self, B=64, T=4):
+        self.B, self.T = B, T
+        self.metric = "VGG16-SNN T=4 inference images/s (batch 64 per GPU, 32x32x3, 10 classes)"
+        self.unit = "images/s"
+        self.dtype = "bf16"
+
+    def config(self):
+        return {"workload": "vgg16_snn_T4_b64_per_gpu", "model": "VGG16-SNN",
+                "layers": "13 conv3x3 + BN(folded) + LIF + 5 maxpool; fc 512-4096-4096-10",
+                "T": self.T, "batch_per_gpu": self.B, "global_batch": self.B * self.world,
+                "input": "32x32x3 U(0,1), direct encoding", "classes": 10,
+                "lif": "tau=2, v_th=1, hard reset 0, decay_input",
+                "weights": "Kaiming-normal seeded, BN folded, bf16 (layer 1 f32)",
+                "parallelism": f"dp{self.world}",
+                "collective": "NCCL all_gather of [64,10] f32 logits per step" if self.world > 1
+                else "none",
+                "l2": "256 MB buffer written before every timed step",
+                "launch": "CUDA graphs (3 segments, dominant layer timed alone)"}
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.zoo.vgg import SpikingVGG, random_vgg_params
+        self.world, self.dist = world, dist
+        P = random_vgg_params(1)
+        self.eng = SpikingVGG(P, T=self.T, device="cuda")
+        g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+        self.img = torch.rand(1, self.B, 3, 32, 32, device="cuda", generator=g)
+        steps, out = self.eng.plan(self.img)
+        for _ in range(3):
+            for _, _, fn in steps:
+                fn()
+        torch.cuda.synchronize()
+        # per-launch profile (eager, events) to find the dominant kernel
+        reps = 10
+        times = [[] for _ in steps]
+        for _ in range(reps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(steps) + 1)]
+            evs[0].record()
+            for i, (_, _, fn) in enumerate(steps):
+                fn()
+                evs[i + 1].record()
+            torch.cuda.synchronize()
+            for i in range(len(steps)):
+                times[i].append(evs[i].elapsed_time(evs[i + 1]))
+        self.layer_ms = [statistics.median(t) for t in times]
+        self.layer_names = [s[0] for s in steps]
+        self.layer_flops = [s[1] for s in steps]
+        dom = max(range(1, len(steps)), key=lambda i: self.layer_ms[i])
+        self.dom = dom
+        self.launches_per_step = len(steps)
+        self.out = self.eng.capture(self.img, split_at=dom)
+        self.dom_graph = 1
+        self.gathered = torch.empty(world * self.B, 10, device="cuda") if world > 1 else None
+        self._dom_events = []
+        self.flops_img = self.eng.flops_per_image()
+
+    def _between(self, i):
+        if i == self.dom_graph:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._pending = e
+        elif i == self.dom_graph + 1:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._dom_events.append((self._pending, e))
+
+    def step(self):
+        self.eng.replay(between=self._between)
+        if self.gathered is not None:
+            self.dist.all_gather_into_tensor(self.gathered, self.out)
+
+    def kernel_events(self, steps):
+        ev = self._dom_events[-steps:]
+        return [a.elapsed_time(b) for a, b in ev]
+
+    def units_per_step(self):
+        return self.B
+
+    def e2e_setup(self):
+        self.h_img = torch.rand(1, self.B, 3, 32, 32).pin_memory()
+        n_out = (self.world * self.B if self.world > 1 else self.B) * 10
+        self.h_out = torch.empty(n_out).pin_memory()
+        self.h2d = self.h_img.numel() * 4
+        self.d2h = n_out * 4
+
+    def e2e_step(self):
+        self.img.copy_(self.h_img, non_blocking=True)
+        self.eng.replay()
+        res = self.out
+        if self.gathered is not None:
+            self.dist.all_gather_into_tensor(self.gathered, self.out)
+            res = self.gathered
+        self.h_out.copy_(res.view(-1), non_blocking=True)
+
+    def e2e_units(self):
+        return self.B
+
+    def roofline(self, kernel_ms, peaks):
+        flops = self.layer_flops[self.dom]
+        achieved = flops / (kernel_ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"]
+        traffic = None
+        tp = os.path.join(REPO, "profiles", "dram_traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get(self.layer_names[self.dom])
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
+                "kernel": f"conv_lif_kernel ({self.layer_names[self.dom]})",
+                "algorithmic_flops_per_launch": flops,
+                "kernel_ms": round(kernel_ms, 5),
+                "per_layer_ms_eager": {n: round(t, 4) for n, t in
+                                       zip(self.layer_names, self.layer_ms)},
+                "model_tflops_per_s": None}
+
+    def cpu_sample(self):
+        from oracle import params as OP
+        P = OP.vgg16_params(1)
+        B = 16
+        x = OP.vgg16_input(0, T=self.T, B=B)
+        return {"B": B, "T": self.T, "P": P, "x": x, "what": "oracle VGG16 forward, torch-CPU f32 conv + C LIF"}
+
+    def cpu_run(self, s, threads):
+        from oracle import vgg as OV
+        torch.set_num_threads(threads)
+        OV.vgg16_forward(s["x"], s["P"], weights="fp32")
+        return s["B"]
+
 # ----------------------------------------------------------------------------------------
 def time_cpu(workload, threads, reps=3):
     s = workload.cpu_sample()
@@ -296,7 +430,7 @@ def run_reference(args, workload):
 def run_ours(args, workload):
     rank, world, local, dist = dist_setup(args)
     peaks = load_peaks()
-    workload.setup(rank, world)
+    workload.setup(rank, world, dist)
     flush = None
     if getattr(workload, "flush_l2", False):
         flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -332,6 +466,9 @@ def run_ours(args, workload):
     clocks = sampler.stop() if sampler else None
     units = sum_over_ranks(dist, workload.units_per_step() * args.steps)
     value = units / (total_ms * 1e-3)
+    roof = workload.roofline(kernel_ms, peaks)
+    if getattr(workload, "flops_img", None):
+        roof["model_tflops_per_s"] = round(value * workload.flops_img / 1e12 / world, 2)
 
     # end to end through the public API, host buffers, copies inside the timed region
     workload.e2e_setup()
@@ -364,7 +501,7 @@ def run_ours(args, workload):
                 "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": workload.dtype,
                 "data": "synthetic", "config": workload.config(),
-                "roofline": workload.roofline(kernel_ms, peaks),
+                "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(workload.launches_per_step * args.steps),
                 "clocks": clocks}
@@ -380,12 +517,13 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="lif", choices=["lif"])
+    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    wl = {"lif": LifWorkload}[args.workload]()
+    wl = {"lif": LifWorkload, "vgg16": VggWorkload}[args.workload]()
+    wl.world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, wl)
     else:

@@ -161,6 +161,14 @@ int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, const void*
                      const float* bias, int64_t N, float* out, snnb_stream_t stream);
 
 /*
+ * K1, classifier head without the mean: out[t*B + b, n] = x[t*B+b] @ w[n]^T + bias[n], f32
+ * [T*B, N] -- the per-step logits VGGSNN.forward returns (snn_compiler/zoo/vgg.py:111-115).
+ * K % 64 == 0, N <= 64.
+ */
+int snnb_linear_out(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                    const float* bias, int64_t N, float* out, snnb_stream_t stream);
+
+/*
  * First (real-valued input) layer of a spiking CNN: float32 direct conv3x3 (pad 1)
  * + bias + multi-step LIF (+ 2x2 max-pool) -> bf16 spikes NHWC [T*B, Ho, Wo, Cout].
  * Replaces the first FusedConvBNNeuron of VGGSNN, whose input is the float image

@@ -46,7 +46,8 @@ struct ConvParams {
     int taps;                     // 9 (3x3 conv) or 1 (linear / 1x1)
     int cin_blocks;               // Cin / 64
     int pool;
-    int mode;                     // 0: LIF spikes bf16;  1: mean over T of (acc + bias), f32
+    int mode;                     // 0: LIF spikes bf16;  1: mean over T of (acc + bias), f32;
+                                  // 2: per-step (acc + bias), f32 [T*B, Cout]
     float df, sc, thr, v_reset;
     int hard;
     const float* bias;
@@ -242,7 +243,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             v[c * 32 + j] = vv;
                             mask |= (s ? 1u : 0u) << j;
                         } else {
-                            v[c * 32 + j] = __fadd_rn(v[c * 32 + j], in);
+                            v[c * 32 + j] = p.mode == 1 ? __fadd_rn(v[c * 32 + j], in) : in;
                         }
                     }
                     smask[c * 128 + m] = mask;
@@ -254,11 +255,23 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 #pragma unroll
                 for (int j = 0; j < BN && j < 16; ++j) {
                     const float in = __fadd_rn(r[j], sbias[j]);
-                    v[j] = __fadd_rn(v[j], in);   // BN < 32 only in mean mode
+                    v[j] = p.mode == 1 ? __fadd_rn(v[j], in) : in;   // BN < 32: head modes only
                 }
             }
             tc::tc_fence_before();
             tc::mbar_arrive(acce_bar(a));
+            if (p.mode == 2) {
+                if (row_valid) {
+                    float* outf = static_cast<float*>(p.out);
+                    const int64_t row = (int64_t)t * p.B + gimg;
+#pragma unroll
+                    for (int j = 0; j < BN; ++j) {
+                        const int c = n0 + j;
+                        if (c < p.Cout) outf[row * p.Cout + c] = v[j];
+                    }
+                }
+                continue;
+            }
             if (p.mode != 0) continue;
             tc::named_bar_sync(1, 128);
             // ---- store the spikes of step t
@@ -483,7 +496,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (pool && ((H % 2) || (W % 2) || (bw % 2) || (bh % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
     int BN;
-    if (mode == 1) {
+    if (mode != 0) {
         BN = Cout <= 16 ? 16 : (Cout <= 32 ? 32 : 64);
     } else {
         if (Cout % 32) return SNNB_ERR_UNSUPPORTED;
@@ -558,6 +571,13 @@ extern "C" int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, 
     if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 64) return SNNB_ERR_ARG;
     return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, 0.f, 0.f, 0.f, 0.f, 0,
                         0, 1, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int snnb_linear_out(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                               const float* bias, int64_t N, float* out, snnb_stream_t stream) {
+    if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 64) return SNNB_ERR_ARG;
+    return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, 0.f, 0.f, 0.f, 0.f, 0,
+                        0, 2, out, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_t B, int64_t Cin,

@@ -33,6 +33,7 @@ SIGNATURES = {
     "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P, P],
     "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, P],
     "snnb_linear_mean": [P, I64, I64, I64, P, P, I64, P, P],
+    "snnb_linear_out": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
                             P],
     "snnb_read_device_status": [P, P],

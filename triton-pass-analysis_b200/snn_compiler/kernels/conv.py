@@ -85,6 +85,22 @@ def linear_mean(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
     return out
 
 
+def linear_out(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-step logits x[t] @ w^T + bias: x [T, B, K] bf16 -> f32 [T, B, N] (N <= 64)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
+    T, B, K = x.shape
+    N = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.numel() == N
+    if out is None:
+        out = torch.empty(T, B, N, device=x.device, dtype=torch.float32)
+    st = _lib.lib().snnb_linear_out(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N,
+                                    _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_linear_out")
+    return out
+
+
 def first_conv_lif(img: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, T: int,
                    neuron: str = "lif", tau: float = 2.0, decay=None, decay_input: bool = True,
                    soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,

@@ -1,0 +1,298 @@
+"""VGG-SNN on the fused sm_100a kernels (reference snn_compiler/zoo/vgg.py).
+
+``VGGSNN`` keeps the reference's module structure (Conv2d -> BatchNorm2d -> LIF per
+cfg entry, 2x2 pool at 'P', classifier Linear+LIF, Linear+LIF, Linear; vgg.py:43-115)
+so reference weights load unchanged; ``fc_in`` lets a 32x32 input feed the
+classifier (the reference hard-codes 224-pixel inputs at vgg.py:74).  Its forward
+runs ``SpikingVGG``, the inference engine:
+
+  layer 1   snnb_first_conv_lif   float32 conv of the real-valued image + bias + LIF
+  layers 2+ snnb_conv3x3_lif      tcgen05 conv + folded-BN bias + LIF (+ max-pool)
+  fc1, fc2  snnb_linear_lif       tcgen05 GEMM + bias + LIF
+  fc3       snnb_linear_mean / snnb_linear_out   logits (averaged over T, or per step)
+
+Activations stay on the device as bf16 channels-last spikes [T, B, H, W, C]; BN is
+folded once at construction (fold_conv_bn, fused.py:585-599); a whole forward can be
+captured into CUDA graphs (``capture``) so one replay issues every launch.  Only
+max-pooling is fused (pool='max'); spikes are {0,1}, so max-pool is an OR.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from ..kernels import conv as KC
+from ..kernels.fused import fold_conv_bn
+from ..nn.modules import LIFNode, IFNode
+
+VGG16_CFG = [64, 64, "P", 128, 128, "P", 256, 256, 256, "P",
+             512, 512, 512, "P", 512, 512, 512, "P"]
+VGG11_CFG = [64, "P", 128, "P", 256, 256, "P", 512, 512, "P", 512, 512, "P"]
+VGG13_CFG = [64, 64, "P", 128, 128, "P", 256, 256, "P", 512, 512, "P", 512, 512, "P"]
+VGG19_CFG = [64, 64, "P", 128, 128, "P", 256, 256, 256, 256, "P",
+             512, 512, 512, 512, "P", 512, 512, 512, 512, "P"]
+
+
+def random_vgg_params(seed: int = 1, *, cfg=VGG16_CFG, num_classes: int = 10, in_ch: int = 3,
+                      fc_hidden: int = 4096, fc_in: int | None = None):
+    """Seeded synthetic weights with the benchmark's draws, generated on the host:
+    conv / linear weights Kaiming-normal (fan_in, gain sqrt 2), biases U(+-1/sqrt(fan_in)),
+    BN gamma U(0.8, 1.2), beta N(0, 0.1), running mean N(0, 0.1), var U(0.5, 1.5), eps 1e-5."""
+    g = torch.Generator().manual_seed(int(seed))
+    convs = []
+    ch = in_ch
+    for v in cfg:
+        if v == "P":
+            convs[-1]["pool"] = True
+            continue
+        fan_in = ch * 9
+        convs.append({
+            "w": torch.randn(v, ch, 3, 3, generator=g) * math.sqrt(2.0 / fan_in),
+            "b": (torch.rand(v, generator=g) * 2 - 1) / math.sqrt(fan_in),
+            "gamma": torch.rand(v, generator=g) * 0.4 + 0.8,
+            "beta": torch.randn(v, generator=g) * 0.1,
+            "mean": torch.randn(v, generator=g) * 0.1,
+            "var": torch.rand(v, generator=g) + 0.5,
+            "eps": 1e-5, "pool": False,
+        })
+        ch = v
+    fc_in = ch if fc_in is None else fc_in
+    fcs = []
+    for fin, fout in ((fc_in, fc_hidden), (fc_hidden, fc_hidden), (fc_hidden, num_classes)):
+        fcs.append({"w": torch.randn(fout, fin, generator=g) * math.sqrt(2.0 / fin),
+                    "b": (torch.rand(fout, generator=g) * 2 - 1) / math.sqrt(fin)})
+    return {"convs": convs, "fcs": fcs, "num_classes": num_classes}
+
+
+class SpikingVGG:
+    """Inference engine: folded bf16 weights resident on one device, fused launches."""
+
+    def __init__(self, P, *, T: int = 4, tau: float = 2.0, decay_input: bool = True,
+                 v_threshold: float = 1.0, v_reset: float = 0.0, soft_reset: bool = False,
+                 neuron: str = "lif", device="cuda"):
+        self.T = T
+        self.lif = dict(neuron=neuron, tau=tau, decay_input=decay_input, soft_reset=soft_reset,
+                        v_threshold=v_threshold, v_reset=v_reset)
+        dev = torch.device(device)
+        self.device = dev
+        self.layers = []
+        for i, c in enumerate(P["convs"]):
+            w, b = fold_conv_bn(c["w"].float(), None if c.get("b") is None else c["b"].float(),
+                                c["gamma"].float(), c["beta"].float(), c["mean"].float(),
+                                c["var"].float(), c["eps"])
+            if i == 0:
+                wd = w.contiguous().to(dev)                       # f32 [Cout, Cin, 3, 3]
+            else:
+                wd = KC.weight_khwc(w).to(dev)                    # bf16 [Cout, 3, 3, Cin]
+            self.layers.append({"w": wd, "b": b.float().contiguous().to(dev),
+                                "pool": bool(c["pool"]), "cout": w.shape[0],
+                                "cin": w.shape[1]})
+        self.fcs = [{"w": f["w"].to(torch.bfloat16).contiguous().to(dev),
+                     "b": f["b"].float().contiguous().to(dev)} for f in P["fcs"]]
+        self.num_classes = P["fcs"][-1]["w"].shape[0]
+        self._bufs = {}
+        self.graphs = None
+
+    # ---- per-layer launch plan -----------------------------------------------------------
+    def plan(self, img: torch.Tensor, *, per_step_logits: bool = False):
+        """List of (name, flops, callable) for one forward over img [Ti, B, 3, H, W] f32.
+        Buffers are allocated once per (B, H, W) and reused."""
+        Ti, B, Cin, H, W = img.shape
+        T = self.T
+        key = (B, H, W, per_step_logits)
+        if key not in self._bufs:
+            bufs = []
+            h, w = H, W
+            for L in self.layers:
+                ho, wo = (h // 2, w // 2) if L["pool"] else (h, w)
+                bufs.append(torch.empty(T, B, ho, wo, L["cout"], device=self.device,
+                                        dtype=torch.bfloat16))
+                h, w = ho, wo
+            feat = h * w * self.layers[-1]["cout"]
+            assert feat == self.fcs[0]["w"].shape[1], (feat, tuple(self.fcs[0]["w"].shape))
+            fbufs = [torch.empty(T, B, f["w"].shape[0], device=self.device, dtype=torch.bfloat16)
+                     for f in self.fcs[:-1]]
+            out = torch.empty((T, B, self.num_classes) if per_step_logits else (B, self.num_classes),
+                              device=self.device, dtype=torch.float32)
+            self._bufs[key] = (bufs, fbufs, out)
+        bufs, fbufs, out = self._bufs[key]
+        steps = []
+        h, w = H, W
+        x_prev = None
+        for i, L in enumerate(self.layers):
+            flops = 2 * T * B * h * w * L["cout"] * L["cin"] * 9
+            if i == 0:
+                fn = (lambda L=L, o=bufs[0]: KC.first_conv_lif(img, L["w"], L["b"], T=T,
+                                                             pool=L["pool"], out=o, **self.lif))
+            else:
+                fn = (lambda L=L, x=x_prev, o=bufs[i]: KC.conv3x3_lif(x, L["w"], L["b"],
+                                                                    pool=L["pool"], out=o,
+                                                                    **self.lif))
+            steps.append((f"conv{i + 1}_{L['cin']}x{L['cout']}@{h}", flops, fn))
+            x_prev = bufs[i]
+            if L["pool"]:
+                h, w = h // 2, w // 2
+        hcur = x_prev.view(T, B, -1)
+        for j, f in enumerate(self.fcs[:-1]):
+            K, N = f["w"].shape[1], f["w"].shape[0]
+            steps.append((f"fc{j + 1}_{K}x{N}", 2 * T * B * K * N,
+                          (lambda f=f, x=hcur, o=fbufs[j]: KC.linear_lif(x, f["w"], f["b"], out=o,
+                                                                        **self.lif))))
+            hcur = fbufs[j]
+        f = self.fcs[-1]
+        K, N = f["w"].shape[1], f["w"].shape[0]
+        head = KC.linear_out if per_step_logits else KC.linear_mean
+        steps.append((f"fc{len(self.fcs)}_{K}x{N}", 2 * T * B * K * N,
+                      (lambda f=f, x=hcur: head(x, f["w"], f["b"], out=out))))
+        return steps, out
+
+    def forward(self, img: torch.Tensor, *, per_step_logits: bool = False) -> torch.Tensor:
+        """img [B, 3, H, W] (direct encoding: the same image at every step) or
+        [Ti, B, 3, H, W] f32 -> logits averaged over T [B, classes] (or [T, B, classes])."""
+        if img.ndim == 4:
+            img = img.unsqueeze(0)
+        img = img.to(self.device, torch.float32).contiguous()
+        steps, out = self.plan(img, per_step_logits=per_step_logits)
+        for _, _, fn in steps:
+            fn()
+        return out
+
+    __call__ = forward
+
+    def flops_per_image(self, H: int = 32, W: int = 32) -> int:
+        """Dense algorithmic FLOPs of one image (every conv at every step)."""
+        img = torch.empty(1, 1, 3, H, W)
+        total = 0
+        h, w = H, W
+        for L in self.layers:
+            total += 2 * self.T * h * w * L["cout"] * L["cin"] * 9
+            if L["pool"]:
+                h, w = h // 2, w // 2
+        for f in self.fcs:
+            total += 2 * self.T * f["w"].shape[0] * f["w"].shape[1]
+        del img
+        return total
+
+    # ---- CUDA graphs ----------------------------------------------------------------------
+    def capture(self, img: torch.Tensor, *, split_at: int | None = None):
+        """Capture the forward over the static input buffer ``img`` into CUDA graphs.
+        With split_at=i the launches are split into three graphs [0, i), [i], (i, end) so
+        that the i-th launch can be timed alone between replays.  Returns the output."""
+        if img.ndim == 4:
+            img = img.unsqueeze(0)
+        steps, out = self.plan(img)
+        for _, _, fn in steps:            # warm up (sets kernel attributes, caches maps)
+            fn()
+        torch.cuda.synchronize()
+        groups = [list(range(len(steps)))] if split_at is None else \
+            [list(range(split_at)), [split_at], list(range(split_at + 1, len(steps)))]
+        self.graphs = []
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        for grp in groups:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.graph_pool):
+                for k in grp:
+                    steps[k][2]()
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+        self.graph_out = out
+        return out
+
+    def replay(self, between=None):
+        """Replay the captured graphs; ``between(i)`` runs before graph i (events)."""
+        for i, g in enumerate(self.graphs):
+            if between is not None:
+                between(i)
+            g.replay()
+        if between is not None:
+            between(len(self.graphs))
+        return self.graph_out
+
+
+class VGGSNN(nn.Module):
+    """Reference-structured VGG-SNN (snn_compiler/zoo/vgg.py:43-115) whose forward runs
+    the fused engine.  forward(x_seq [T, B, 3, H, W]) -> logits [T, B, classes]."""
+
+    def __init__(self, cfg, num_classes=1000, *, in_ch=3, fc_hidden=4096, with_bn=True,
+                 neuron="lif", tau=2.0, decay_input=True, soft_reset=False, v_threshold=1.0,
+                 v_reset=0.0, layout="NCHW", pool="max", fc_in=None, input_size=224):
+        super().__init__()
+        if pool != "max":
+            raise NotImplementedError("the fused kernels implement pool='max' (OR of spikes)")
+        if not with_bn:
+            raise NotImplementedError("VGGSNN here expects BN layers (folded at fuse time)")
+        feats = []
+        ch = in_ch
+        for v in cfg:
+            if v == "P":
+                feats.append(nn.MaxPool2d(2, 2))
+            else:
+                feats.append(nn.Conv2d(ch, v, 3, padding=1, bias=True))
+                feats.append(nn.BatchNorm2d(v))
+                feats.append(LIFNode(tau=tau, decay_input=decay_input, soft_reset=soft_reset,
+                                     v_threshold=v_threshold, v_reset=v_reset, layout=layout)
+                             if neuron == "lif" else
+                             IFNode(soft_reset=soft_reset, v_threshold=v_threshold,
+                                    v_reset=v_reset, layout=layout))
+                ch = v
+        self.features = nn.Sequential(*feats)
+        n_pool = sum(1 for x in cfg if x == "P")
+        self.fc_in_dim = fc_in if fc_in is not None else ch * (input_size // 2 ** n_pool) ** 2
+        self.classifier = nn.Sequential(
+            nn.Linear(self.fc_in_dim, fc_hidden), nn.Identity(),
+            nn.Linear(fc_hidden, fc_hidden), nn.Identity(),
+            nn.Linear(fc_hidden, num_classes))
+        self.cfg = list(cfg)
+        self.neuron_kw = dict(tau=tau, decay_input=decay_input, soft_reset=soft_reset,
+                              v_threshold=v_threshold, v_reset=v_reset, neuron=neuron)
+        self._engine = None
+
+    def params_dict(self):
+        convs, it = [], iter(self.features)
+        for m in self.features:
+            if isinstance(m, nn.Conv2d):
+                convs.append({"w": m.weight.detach(), "b": None if m.bias is None else m.bias.detach(),
+                              "pool": False})
+            elif isinstance(m, nn.BatchNorm2d):
+                convs[-1].update(gamma=m.weight.detach(), beta=m.bias.detach(),
+                                 mean=m.running_mean.detach(), var=m.running_var.detach(),
+                                 eps=m.eps)
+            elif isinstance(m, nn.MaxPool2d):
+                convs[-1]["pool"] = True
+        del it
+        lins = [m for m in self.classifier if isinstance(m, nn.Linear)]
+        fcs = [{"w": l.weight.detach(), "b": l.bias.detach()} for l in lins]
+        return {"convs": convs, "fcs": fcs}
+
+    def fuse(self, T: int = 4):
+        dev = next(self.parameters()).device
+        self._engine = SpikingVGG(self.params_dict(), T=T, device=dev, **self.neuron_kw)
+        return self._engine
+
+    def forward(self, x_seq):
+        T = x_seq.shape[0]
+        if self._engine is None or self._engine.T != T:
+            self.fuse(T)
+        return self._engine.forward(x_seq.float().contiguous(), per_step_logits=True)
+
+
+def _build(cfg, *, fused=True, init_bn=True, **kw):
+    m = VGGSNN(cfg, **kw)
+    if init_bn:
+        g = torch.Generator().manual_seed(0)
+        for mod in m.modules():
+            if isinstance(mod, nn.BatchNorm2d):
+                with torch.no_grad():
+                    mod.running_mean.copy_(torch.randn(mod.running_mean.shape, generator=g) * 0.1)
+                    mod.running_var.copy_(torch.rand(mod.running_var.shape, generator=g) + 0.5)
+                    mod.weight.copy_(torch.rand(mod.weight.shape, generator=g) + 0.5)
+                    mod.bias.copy_(torch.randn(mod.bias.shape, generator=g) * 0.1)
+    return m.eval()
+
+
+def vgg11_snn(**kw): return _build(VGG11_CFG, **kw)
+def vgg13_snn(**kw): return _build(VGG13_CFG, **kw)
+def vgg16_snn(**kw): return _build(VGG16_CFG, **kw)
+def vgg19_snn(**kw): return _build(VGG19_CFG, **kw)
