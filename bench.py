@@ -252,6 +252,8 @@ class VggWorkload:
     """VGG16-SNN T=4 inference, batch 64 per GPU (config 0 at the benchmark batch)."""
     name = "vgg16"
     flush_l2 = True
+    load_choices = None
+    save_choices = None
 
     def __init__(self, B=64, T=4):
         self.B, self.T = B, T
@@ -277,6 +279,9 @@ class VggWorkload:
         self.world, self.dist = world, dist
         P = random_vgg_params(1)
         self.eng = SpikingVGG(P, T=self.T, device="cuda")
+        if self.load_choices:
+            table = json.load(open(self.load_choices))
+            self.eng.choice = {tuple(json.loads(k)): tuple(v) for k, v in table.items()}
         g = torch.Generator(device="cuda").manual_seed(1000 + rank)
         self.img = torch.rand(1, self.B, 3, 32, 32, device="cuda", generator=g)
         steps, out = self.eng.plan(self.img)
@@ -284,23 +289,16 @@ class VggWorkload:
             for _, _, fn in steps:
                 fn()
         torch.cuda.synchronize()
-        # per-launch profile (eager, events) to find the dominant kernel
-        reps = 10
-        times = [[] for _ in steps]
-        for _ in range(reps):
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(steps) + 1)]
-            evs[0].record()
-            for i, (_, _, fn) in enumerate(steps):
-                fn()
-                evs[i + 1].record()
-            torch.cuda.synchronize()
-            for i in range(len(steps)):
-                times[i].append(evs[i].elapsed_time(evs[i + 1]))
-        self.layer_ms = [statistics.median(t) for t in times]
-        self.layer_names = [s[0] for s in steps]
-        self.layer_flops = [s[1] for s in steps]
+        # per-launch device time (each layer from its own CUDA graph) -> dominant kernel
+        prof = self.eng.profile_layers(self.img)
+        self.layer_names = [n for n, _, _ in prof]
+        self.layer_flops = [f for _, f, _ in prof]
+        self.layer_ms = [m for _, _, m in prof]
         dom = max(range(1, len(steps)), key=lambda i: self.layer_ms[i])
         self.dom = dom
+        if self.save_choices and rank == 0:
+            json.dump({json.dumps(list(k)): list(v) for k, v in self.eng.choice.items()},
+                      open(self.save_choices, "w"))
         self.launches_per_step = len(steps)
         self.out = self.eng.capture(self.img, split_at=dom)
         self.dom_graph = 1
@@ -363,8 +361,9 @@ class VggWorkload:
                 "kernel": f"conv_lif_kernel ({self.layer_names[self.dom]})",
                 "algorithmic_flops_per_launch": flops,
                 "kernel_ms": round(kernel_ms, 5),
-                "per_layer_ms_eager": {n: round(t, 4) for n, t in
-                                       zip(self.layer_names, self.layer_ms)},
+                "per_layer_device_ms": {n: round(t, 4) for n, t in
+                                        zip(self.layer_names, self.layer_ms)},
+                "choices": {str(k): v for k, v in self.eng.choice.items()},
                 "model_tflops_per_s": None}
 
     def cpu_sample(self):
@@ -379,6 +378,92 @@ class VggWorkload:
         torch.set_num_threads(threads)
         OV.vgg16_forward(s["x"], s["P"], weights="fp32")
         return s["B"]
+
+
+class ConvLayerWorkload:
+    """One fused conv3x3 + BN(folded) + LIF + 2x2 max-pool layer (config 2)."""
+    name = "conv"
+    flush_l2 = True
+
+    def __init__(self, cin=512, cout=512, H=56, B=64, T=4, p=0.15, fixed=None):
+        self.cin, self.cout, self.H, self.B, self.T, self.p = cin, cout, H, B, T, p
+        self.fixed = fixed
+        self.flops = 2 * T * B * H * H * cout * cin * 9
+        self.metric = f"fused conv3x3+BN+LIF+maxpool TFLOP/s (Cin={cin}, Cout={cout}, H=W={H}, B={B}, T={T})"
+        self.unit = "TFLOP/s"
+        self.dtype = "bf16"
+
+    def config(self):
+        return {"workload": f"conv_layer_{self.cin}x{self.cout}@{self.H}", "T": self.T,
+                "B": self.B, "Cin": self.cin, "Cout": self.cout, "H": self.H, "W": self.H,
+                "spike_p": self.p, "pool": "max 2x2", "l2": "256 MB buffer written before every step"}
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.kernels import conv as KC
+        self.KC = KC
+        self.world = world
+        g = torch.Generator(device="cuda").manual_seed(7 + rank)
+        T, B, H, C = self.T, self.B, self.H, self.cin
+        self.x = (torch.rand(T, B, H, H, C, device="cuda", generator=g) < self.p).to(torch.bfloat16)
+        w = torch.randn(self.cout, 3, 3, C, device="cuda", generator=g) * (2.0 / (9 * C)) ** 0.5
+        self.w = w.to(torch.bfloat16).contiguous()
+        self.b = torch.rand(self.cout, device="cuda", generator=g) * 0.9 + 0.3
+        self.out = torch.empty(T, B, H // 2, H // 2, self.cout, device="cuda", dtype=torch.bfloat16)
+        self.ws = None
+        # pick the fastest (variant, block_n) the way the VGG engine does
+        run = lambda v, bn, sp: KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out,
+                                               variant=v, block_n=bn, splits=sp)
+        self.choice = self.fixed if self.fixed else KC.pick_fastest(run, self.cout, T, 9 * C // 64)
+        nws = KC.split_workspace_bytes(T, B, H, H, self.cout, self.choice[2])
+        self.ws = torch.empty(nws // 4, device="cuda") if nws else None
+        self.launches_per_step = 1
+
+    def step(self):
+        v, bn, sp = self.choice
+        self.KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out, variant=v, block_n=bn,
+                            splits=sp, workspace=self.ws)
+
+    def kernel_events(self, steps):
+        return None
+
+    def units_per_step(self):
+        return self.flops / 1e12
+
+    def e2e_setup(self):
+        self.hx = self.x.cpu().pin_memory()
+        self.hout = torch.empty(self.out.shape, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.hx.numel() * 2
+        self.d2h = self.hout.numel() * 2
+
+    def e2e_step(self):
+        self.x.copy_(self.hx, non_blocking=True)
+        self.step()
+        self.hout.copy_(self.out, non_blocking=True)
+
+    def e2e_units(self):
+        return self.flops / 1e12
+
+    def roofline(self, kernel_ms, peaks):
+        achieved = self.flops / (kernel_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
+                "kernel": f"conv_lif (variant, block_n, splits = {self.choice})",
+                "algorithmic_flops_per_launch": self.flops, "traffic": None}
+
+    def cpu_sample(self):
+        from oracle import params as OP
+        B, H, C = 1, self.H, self.cin
+        x = OP.spikes(0, (self.T, B, C, H, H), self.p)
+        w = torch.randn(self.cout, C, 3, 3, generator=OP.gen(1)) * (2.0 / (9 * C)) ** 0.5
+        b = torch.rand(self.cout, generator=OP.gen(2)) * 0.9 + 0.3
+        return {"B": B, "x": x, "w": w, "b": b, "what": "oracle conv+LIF+pool, torch-CPU f32"}
+
+    def cpu_run(self, s, threads):
+        from oracle import vgg as OV
+        torch.set_num_threads(threads)
+        OV.conv_bn_lif_pool(s["x"], s["w"], s["b"], pool=True)
+        return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
 
 # ----------------------------------------------------------------------------------------
 def time_cpu(workload, threads, reps=3):
@@ -517,12 +602,28 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif"])
+    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif", "conv"])
+    ap.add_argument("--layer", default="512,512,56", help="conv workload: Cin,Cout,H")
+    ap.add_argument("--batch", type=int, default=64, help="conv workload batch")
+    ap.add_argument("--choice", default=None,
+                    help="conv workload: fixed 'variant,block_n' instead of timing the candidates")
+    ap.add_argument("--save-choices", default=None, help="vgg16: write the tuned kernel table")
+    ap.add_argument("--load-choices", default=None,
+                    help="vgg16: use a tuned kernel table instead of timing (e.g. under ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    wl = {"lif": LifWorkload, "vgg16": VggWorkload}[args.workload]()
+    if args.workload == "conv":
+        cin, cout, hh = (int(v) for v in args.layer.split(","))
+        fixed = tuple(int(v) for v in args.choice.split(",")) if args.choice else None
+        if fixed and len(fixed) == 2:
+            fixed = fixed + (1,)
+        wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed)
+    else:
+        wl = {"lif": LifWorkload, "vgg16": VggWorkload}[args.workload]()
+        if args.workload == "vgg16":
+            wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
     wl.world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, wl)

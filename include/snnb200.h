@@ -7,6 +7,7 @@
  *     (snnb_stream_t is a cudaStream_t; NULL means the legacy default stream),
  *   - launches asynchronously on that stream and never synchronises it,
  *   - allocates nothing: the caller owns every input, output and workspace,
+ *     and passes workspace explicitly where a kernel needs scratch memory,
  *   - returns an int status (SNNB_OK or a negative SNNB_ERR_*), never aborts and
  *     never throws across the boundary.
  * Shapes follow the reference's flattening: a multi-step tensor [T, B, ...] is
@@ -134,36 +135,54 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  * bias : f32 [Cout] folded bias b' (added inside the neuron, fused.py:106-108)
  * out  : bf16 spikes NHWC [T*B, Ho, Wo, Cout], Ho = H/2 and Wo = W/2 when pool != 0
  * The neuron is v = decay*v + input_scale*(conv + b'); s = v >= v_threshold; reset.
- * Pixel blocks of 128 rows: W must divide 128 or be a multiple of 128, likewise H for
- * the rows per block; pooling needs even H and W.
+ * variant : 0 = choose; 1 = the CTA walks the T steps of a 128-pixel block with two
+ *           TMEM accumulators; 2 = T folded into the 128 accumulator rows (128/T pixels
+ *           per CTA, T in {2, 4, 8}) for layers too small to fill the GPU otherwise.
+ * block_n : output channels per CTA, 0 = choose, or 32 / 64 / 128 (dividing Cout), or 256
+ *           with variant 2.
+ * splits  : 1, or k-range splits for small layers (variant 2): each split's float32
+ *           partial sums go to `workspace` (caller-owned, >= snnb_split_workspace_bytes,
+ *           16-byte aligned) and a second kernel adds them in a fixed order, adds the bias
+ *           and runs the neuron (+ pool).  workspace may be NULL when splits == 1.
+ * Pixel blocks: W must divide the block's pixel count or be a multiple of it, likewise
+ * H for the rows per block; pooling needs even H and W.
  */
 int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin,
                      const void* w, const float* bias, int64_t Cout,
                      float decay, float input_scale, float v_threshold, float v_reset,
-                     int hard_reset, int pool, void* out, snnb_stream_t stream);
+                     int hard_reset, int pool, int variant, int block_n, int splits,
+                     void* workspace, int64_t workspace_bytes, void* out,
+                     snnb_stream_t stream);
 
 /*
  * K1, linear variant: spikes [T*B, K] bf16 @ w [N, K] bf16 + bias -> multi-step LIF ->
  * bf16 spikes [T*B, N].  Replaces FusedLinearNeuron.forward
- * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 64 == 0.
+ * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 64 == 0,
+ * N % 32 == 0; variant / block_n as for snnb_conv3x3_lif.
  */
 int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                     const float* bias, int64_t N, float decay, float input_scale,
-                    float v_threshold, float v_reset, int hard_reset, void* out,
+                    float v_threshold, float v_reset, int hard_reset, int variant, int block_n,
+                    int splits, void* workspace, int64_t workspace_bytes, void* out,
                     snnb_stream_t stream);
 
+/* Workspace bytes snnb_conv3x3_lif / snnb_linear_lif (H = W = 1) need for `splits`. */
+int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cout,
+                                   int splits);
+
 /*
- * K1, classifier head: out[b, n] = mean over t of (x[t*B+b] @ w[n]^T + bias[n]), f32.
+ * Classifier head: out[b, n] = mean over t of (x[t*B+b] @ w[n]^T + bias[n]), f32.
  * Replaces the last nn.Linear of VGGSNN (snn_compiler/zoo/vgg.py:84, :111-114) and the
- * caller's mean over T (examples/vgg16_snn/vgg16_test.py:243).  K % 64 == 0, N <= 64.
+ * caller's mean over T (examples/vgg16_snn/vgg16_test.py:243).  K % 8 == 0, N <= 64;
+ * a few dot products per sample, computed on the CUDA cores.
  */
 int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                      const float* bias, int64_t N, float* out, snnb_stream_t stream);
 
 /*
- * K1, classifier head without the mean: out[t*B + b, n] = x[t*B+b] @ w[n]^T + bias[n], f32
+ * Classifier head without the mean: out[t*B + b, n] = x[t*B+b] @ w[n]^T + bias[n], f32
  * [T*B, N] -- the per-step logits VGGSNN.forward returns (snn_compiler/zoo/vgg.py:111-115).
- * K % 64 == 0, N <= 64.
+ * K % 8 == 0, N <= 64.
  */
 int snnb_linear_out(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                     const float* bias, int64_t N, float* out, snnb_stream_t stream);

@@ -8,6 +8,8 @@ whose first disagreement sits where the oracle's charged potential is within 1e-
 of the threshold, and on at most 0.1% of all spikes; pooled outputs must equal the
 2x2 OR of the kernel's own unpooled spikes exactly.
 """
+import itertools
+
 import numpy as np
 import pytest
 import torch
@@ -61,19 +63,35 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
     (4, 32, 512, 512, 2),
     (3, 2, 64, 64, 8),
     (6, 4, 192, 96, 8),
+    (4, 2, 64, 64, 56),     # config-2 spatial size: partial pixel blocks at the edges
+    (4, 3, 64, 64, 14),
+    (2, 5, 64, 128, 7),     # odd size: no pooling
 ]
 
 
+VARIANTS = [(0, 0, 1), (1, 32, 1), (1, 128, 1), (2, 32, 1), (2, 64, 1), (2, 128, 1), (2, 256, 1),
+            (2, 128, 3), (2, 256, 4)]
+
+
+@pytest.mark.parametrize("vb", VARIANTS)
 @pytest.mark.parametrize("geom", GEOMS)
-def test_conv3x3_lif_against_oracle(geom):
+def test_conv3x3_lif_against_oracle(geom, vb):
+    """Both kernel variants (T sequential in the CTA / T folded into M) and several
+    channel-block widths on every VGG16 pixel-block geometry."""
     T, B, Cin, Cout, H = geom
+    variant, block_n, splits = vb
+    if block_n and Cout % block_n:
+        pytest.skip("block_n must divide Cout")
+    if variant == 2 and T not in (2, 4, 8):
+        pytest.skip("T folding needs T in {2, 4, 8}")
     C = _C()
-    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.15, hash(geom) & 0xffff, False)
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.15, sum(geom) * 31 + Cout, False)
     xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
     wd = C.weight_khwc(w).to(DEV)
     bd = b.to(DEV)
-    y = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, pool=False)
-    yp = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, pool=True) if H % 2 == 0 else None
+    kw = dict(tau=2.0, v_threshold=THR, variant=variant, block_n=block_n, splits=splits)
+    y = C.conv3x3_lif(xd, wd, bd, pool=False, **kw)
+    yp = C.conv3x3_lif(xd, wd, bd, pool=True, **kw) if H % 2 == 0 else None
     assert C.device_status() == 0
     s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True)
     got = y.float().cpu().permute(0, 1, 4, 2, 3)                        # -> [T,B,C,H,W]
@@ -89,9 +107,10 @@ def test_conv3x3_soft_reset_and_if_neuron():
     T, B, Cin, Cout, H = 4, 2, 64, 64, 8
     x, w, b = _layer_case(T, B, Cin, Cout, H, 0.3, 11, False)
     xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
-    for neuron, soft in (("if", True), ("lif", True), ("if", False)):
+    for (neuron, soft), variant in itertools.product((("if", True), ("lif", True), ("if", False)),
+                                                     (1, 2)):
         y = C.conv3x3_lif(xd, C.weight_khwc(w).to(DEV), b.to(DEV), neuron=neuron, tau=2.0,
-                          soft_reset=soft, v_threshold=0.8, v_reset=-0.1)
+                          soft_reset=soft, v_threshold=0.8, v_reset=-0.1, variant=variant)
         from oracle import neurons as ON
         yc = F.conv2d(x.reshape(T * B, Cin, H, H), w, None, padding=1).reshape(T, B, Cout, H, H)
         df, sc = ON.neuron_params(neuron, tau=2.0)
@@ -103,16 +122,20 @@ def test_conv3x3_soft_reset_and_if_neuron():
                    torch.from_numpy(o["vpre"]).reshape(got.shape), thr=0.8)
 
 
+@pytest.mark.parametrize("vb", [(0, 0, 1), (1, 64, 1), (2, 32, 1), (2, 128, 1), (2, 128, 2)])
 @pytest.mark.parametrize("TBKN", [(4, 64, 512, 4096), (4, 8, 4096, 256), (2, 130, 128, 96)])
-def test_linear_lif_against_oracle(TBKN):
+def test_linear_lif_against_oracle(TBKN, vb):
     T, B, K, N = TBKN
+    variant, block_n, splits = vb
+    if block_n and N % block_n:
+        pytest.skip("block_n must divide N")
     C = _C()
     g = OP.gen(K + N)
     x = (torch.rand(T, B, K, generator=g) < 0.2).float()
     w = (torch.randn(N, K, generator=g) * (2.0 / K) ** 0.5).to(torch.bfloat16).float()
     b = torch.rand(N, generator=g) * 0.9 + 0.3
     y = C.linear_lif(x.to(torch.bfloat16).to(DEV), w.to(torch.bfloat16).to(DEV), b.to(DEV),
-                     tau=2.0, v_threshold=THR)
+                     tau=2.0, v_threshold=THR, variant=variant, block_n=block_n, splits=splits)
     yc = F.linear(x.reshape(T * B, K), w).reshape(T, B, N)
     s, vpre = OV.lif_seq(yc, b, want_vpre=True)
     got = y.float().cpu()

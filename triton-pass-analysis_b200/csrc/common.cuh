@@ -41,4 +41,16 @@ __device__ __forceinline__ float charge(float v, float df, float sc, float in) {
     return __fadd_rn(__fmul_rn(df, v), __fmul_rn(sc, in));
 }
 
+// 8 spike bits -> 8 bf16 values (0.0 / 1.0) packed in 16 bytes, bit i -> element i.
+__device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = ((bits8 >> (2 * i)) & 1u) ? 0x3F80u : 0u;
+        const uint32_t hi = ((bits8 >> (2 * i + 1)) & 1u) ? 0x3F800000u : 0u;
+        w[i] = lo | hi;
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 }  // namespace snnb

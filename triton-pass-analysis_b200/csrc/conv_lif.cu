@@ -41,28 +41,86 @@ constexpr int A_TILE_BYTES = 128 * 128;          // 128 rows x 64 bf16
 
 struct ConvParams {
     int T, B, H, W, Cin, Cout;
-    int bw, bh, bn;               // pixel block: bn images x bh rows x bw columns (product 128)
-    int tiles_w, tiles_h, n_tiles_n;
+    int bw, bh, bn;               // pixel block: bn images x bh rows x bw columns
+    int tiles_w, tiles_h, n_tiles_n, num_tiles;
     int taps;                     // 9 (3x3 conv) or 1 (linear / 1x1)
     int cin_blocks;               // Cin / 64
     int pool;
-    int mode;                     // 0: LIF spikes bf16;  1: mean over T of (acc + bias), f32;
-                                  // 2: per-step (acc + bias), f32 [T*B, Cout]
     float df, sc, thr, v_reset;
     int hard;
     const float* bias;
-    void* out;
+    __nv_bfloat16* out;
     int* status;
+    int splits;                   // k-range splits (T-folded kernel); 1 = none
+    float* partial;               // split-K: f32 partial sums [splits][T][B*H*W][Cout]
 };
 
+struct Tile {
+    int w0, h0, img0, n0;
+};
+
+__device__ __forceinline__ Tile decode_tile(int tile, const ConvParams& p, int BN) {
+    const int nt = tile % p.n_tiles_n;
+    const int mt = tile / p.n_tiles_n;
+    const int tw = mt % p.tiles_w;
+    const int th = (mt / p.tiles_w) % p.tiles_h;
+    const int tn = mt / (p.tiles_w * p.tiles_h);
+    return Tile{tw * p.bw, th * p.bh, tn * p.bn, nt * BN};
+}
+
+// Spike bits of one (step, 32-channel slice) of the pixel block -> bf16 NHWC, pooled
+// (OR of each 2x2 window) or not; 64 bytes per (pixel, slice), 16-byte stores.
+// mask(pix) returns the 32-bit spike word of block pixel pix.
+template <typename MaskFn>
+__device__ __forceinline__ void store_spikes(const ConvParams& p, const Tile& tl, int t, int c,
+                                             int pix_item, MaskFn mask) {
+    if (p.pool) {
+        const int pw = p.bw / 2, ph = p.bh / 2;
+        const int xw = pix_item % pw, xh = (pix_item / pw) % ph, xn = pix_item / (pw * ph);
+        const int m00 = 2 * xw + p.bw * (2 * xh + p.bh * xn);
+        const uint32_t bits = mask(m00) | mask(m00 + 1) | mask(m00 + p.bw) | mask(m00 + p.bw + 1);
+        const int Ho = p.H / 2, Wo = p.W / 2;
+        const int ow = tl.w0 / 2 + xw, oh = tl.h0 / 2 + xh, on = tl.img0 + xn;
+        if (ow >= Wo || oh >= Ho || on >= p.B) return;
+        const int64_t base = ((((int64_t)t * p.B + on) * Ho + oh) * Wo + ow) * p.Cout + tl.n0 + c * 32;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + base);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
+    } else {
+        const int xw = pix_item % p.bw, xh = (pix_item / p.bw) % p.bh, xn = pix_item / (p.bw * p.bh);
+        const int ow = tl.w0 + xw, oh = tl.h0 + xh, on = tl.img0 + xn;
+        if (ow >= p.W || oh >= p.H || on >= p.B) return;
+        const uint32_t bits = mask(pix_item);
+        const int64_t base = ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) * p.Cout + tl.n0 + c * 32;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + base);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
+    }
+}
+
+// Producer drain after an abort: wait (bounded) for the copies still in flight.
+__device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int stage, uint32_t phase,
+                                           int issued) {
+    for (int k = 0; k < stages && k < issued; ++k) {
+        if (--stage < 0) { stage = stages - 1; phase ^= 1u; }
+        const long long t0 = clock64();
+        while (!tc::mbar_try_wait(bar0 + 8u * stage, phase) &&
+               clock64() - t0 < tc::WAIT_LIMIT_CYCLES) {
+        }
+    }
+}
+
+// ---- variant 1: T sequential inside the CTA ---------------------------------------------
+// Persistent: CTA c handles tiles c, c + gridDim.x, ...  Every (tile, step) is one
+// accumulation into one of two TMEM accumulators used alternately, so the epilogue of
+// step i (LIF + stores) overlaps the MMAs of step i + 1 -- across tile boundaries too.
 template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_TILE = BN * 128;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * A_TILE_BYTES;
     static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;          // (BN/32) x 128 u32
-    static constexpr int BIAS_OFF = MASK_OFF + (BN / 32 > 0 ? BN / 32 : 1) * 128 * 4;
-    static constexpr int BAR_OFF = BIAS_OFF + BN * 4;
+    static constexpr int BAR_OFF = MASK_OFF + (BN / 32) * 128 * 4;
     static constexpr int NBARS = 2 * STAGES + 4;
     static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
     static constexpr int ABORT_OFF = TMEM_OFF + 4;
@@ -70,32 +128,18 @@ struct Smem {
     static constexpr int DYN = TOTAL + 1024;     // slack for 1024-byte alignment
 };
 
-__device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
-    uint4 r;
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t lo = ((bits8 >> (2 * i)) & 1u) ? 0x3F80u : 0u;
-        const uint32_t hi = ((bits8 >> (2 * i + 1)) & 1u) ? 0x3F800000u : 0u;
-        w[i] = lo | hi;
-    }
-    r.x = w[0]; r.y = w[1]; r.z = w[2]; r.w = w[3];
-    return r;
-}
-
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const ConvParams p) {
     using S = Smem<BN, STAGES>;
+    constexpr int NCH = BN / 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = tc::smem_u32(smem);
     uint32_t* smask = reinterpret_cast<uint32_t*>(smem + S::MASK_OFF);
-    float* sbias = reinterpret_cast<float*>(smem + S::BIAS_OFF);
     const uint32_t bar0 = sbase + S::BAR_OFF;
-    // barrier addresses
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
@@ -104,15 +148,9 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nt = blockIdx.x % p.n_tiles_n;
-    const int mt = blockIdx.x / p.n_tiles_n;
-    const int tw = mt % p.tiles_w;
-    const int th = (mt / p.tiles_w) % p.tiles_h;
-    const int tn = mt / (p.tiles_w * p.tiles_h);
-    const int w0 = tw * p.bw, h0 = th * p.bh, img0 = tn * p.bn, n0 = nt * BN;
     const int KB = p.taps * p.cin_blocks;
     constexpr uint32_t STAGE_TX = A_TILE_BYTES + S::B_TILE;
-    constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -128,10 +166,6 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         tc::prefetch_tmap(&tmA);
         tc::prefetch_tmap(&tmB);
     }
-    for (int i = threadIdx.x; i < BN; i += THREADS) {
-        const int c = n0 + i;
-        sbias[i] = (p.bias && c < p.Cout) ? p.bias[c] : 0.0f;
-    }
     if (warp == 1) {
         tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
         tc::tmem_relinquish();
@@ -144,40 +178,33 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            int stage = 0;
+            int stage = 0, issued = 0;
             uint32_t phase = 0;
-            int issued = 0;
             bool ok = true;
-            for (int t = 0; t < p.T && ok; ++t) {
-                const int f0 = t * p.B + img0;
-                for (int kb = 0; kb < KB; ++kb) {
-                    if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    const int tap = kb / p.cin_blocks;
-                    const int cb = kb - tap * p.cin_blocks;
-                    const int r = p.taps == 9 ? tap / 3 : 1;
-                    const int s = p.taps == 9 ? tap % 3 : 1;
-                    tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-                    tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, full_bar(stage),
-                                    cb * 64, w0 + s - 1, h0 + r - 1, f0);
-                    tc::tma_load_2d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
-                                    tap * p.Cin + cb * 64, n0);
-                    ++issued;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-                }
-            }
-            if (!ok) {
-                // drain: wait (bounded) for the copies still in flight in every ring slot
-                for (int k = 0; k < STAGES && k < issued; ++k) {
-                    if (--stage < 0) { stage = STAGES - 1; phase ^= 1u; }
-                    const long long t0 = clock64();
-                    while (!tc::mbar_try_wait(full_bar(stage), phase) &&
-                           clock64() - t0 < tc::WAIT_LIMIT_CYCLES) {
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const Tile tl = decode_tile(tile, p, BN);
+                for (int t = 0; t < p.T && ok; ++t) {
+                    const int f0 = t * p.B + tl.img0;
+                    for (int kb = 0; kb < KB; ++kb) {
+                        if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        const int tap = kb / p.cin_blocks;
+                        const int cb = kb - tap * p.cin_blocks;
+                        const int r = p.taps == 9 ? tap / 3 : 1;
+                        const int s = p.taps == 9 ? tap % 3 : 1;
+                        tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
+                        tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
+                                        full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
+                        tc::tma_load_2d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
+                                        tap * p.Cin + cb * 64, tl.n0);
+                        ++issued;
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
                 }
             }
+            if (!ok) drain_ring(bar0, STAGES, stage, phase, issued);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
@@ -185,145 +212,84 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
             int stage = 0;
             uint32_t phase = 0;
+            uint32_t it = 0;
             bool ok = true;
-            for (int t = 0; t < p.T && ok; ++t) {
-                const int a = t & 1;
-                if (!tc::mbar_wait(acce_bar(a), ((t >> 1) & 1) ^ 1u, abort_flag, p.status)) break;
-                tc::tc_fence_after();
-                const uint32_t dcol = tmem + a * BN;
-                for (int kb = 0; kb < KB; ++kb) {
-                    if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                for (int t = 0; t < p.T && ok; ++t, ++it) {
+                    const int a = it & 1;
+                    if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
-                    const uint32_t sa = sbase + S::A_OFF + stage * A_TILE_BYTES;
-                    const uint32_t sb = sbase + S::B_OFF + stage * S::B_TILE;
-                    const uint64_t da = tc::sdesc_k_sw128(sa);
-                    const uint64_t db = tc::sdesc_k_sw128(sb);
+                    const uint32_t dcol = tmem + a * BN;
+                    for (int kb = 0; kb < KB; ++kb) {
+                        if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::tc_fence_after();
+                        const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
+                        const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)   // 4 x K=16 inside the 128-byte swizzle atom
-                        tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
-                    tc::umma_commit(empty_bar(stage));
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        for (int k = 0; k < 4; ++k)   // 4 x K=16 inside the 128-byte swizzle atom
+                            tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
+                        tc::umma_commit(empty_bar(stage));
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    }
+                    if (ok) tc::umma_commit(accf_bar(a));
                 }
-                if (ok) tc::umma_commit(accf_bar(a));
             }
         }
     } else {
         // ------------------------------------------------------------- epilogue
         const int q = warp & 3;                  // TMEM lane quadrant of this warp
-        const int m = 32 * q + lane;             // pixel row of the tile
+        const int m = 32 * q + lane;             // pixel row of the block
         const int et = threadIdx.x - 64;         // 0..127
-        const int mw = m % p.bw, mh = (m / p.bw) % p.bh, mn = m / (p.bw * p.bh);
-        const int gw = w0 + mw, gh = h0 + mh, gimg = img0 + mn;
-        const bool row_valid = gw < p.W && gh < p.H && gimg < p.B;
-        float v[BN];
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+            const Tile tl = decode_tile(tile, p, BN);
+            const float* bias = p.bias + tl.n0;
+            float v[BN];
 #pragma unroll
-        for (int j = 0; j < BN; ++j) v[j] = 0.0f;
-        for (int t = 0; t < p.T; ++t) {
-            const int a = t & 1;
-            if (!tc::mbar_wait(accf_bar(a), (t >> 1) & 1, abort_flag, p.status)) break;
-            tc::tc_fence_after();
-            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
-            if (BN >= 32) {
+            for (int j = 0; j < BN; ++j) v[j] = 0.0f;
+            for (int t = 0; t < p.T; ++t, ++it) {
+                const int a = it & 1;
+                if (!tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = 0; c < NCH; ++c) {
                     float r[32];
                     tc::tmem_ld32(tbase + c * 32, r);
                     tc::tmem_wait_ld();
                     uint32_t mask = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const float in = __fadd_rn(r[j], sbias[c * 32 + j]);
-                        if (p.mode == 0) {
-                            float vv = charge(v[c * 32 + j], p.df, p.sc, in);
-                            const bool s = vv >= p.thr;
-                            vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
-                            v[c * 32 + j] = vv;
-                            mask |= (s ? 1u : 0u) << j;
-                        } else {
-                            v[c * 32 + j] = p.mode == 1 ? __fadd_rn(v[c * 32 + j], in) : in;
-                        }
+                        const float in = __fadd_rn(r[j], __ldg(bias + c * 32 + j));
+                        float vv = charge(v[c * 32 + j], p.df, p.sc, in);
+                        const bool s = vv >= p.thr;
+                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                        v[c * 32 + j] = vv;
+                        mask |= (s ? 1u : 0u) << j;
                     }
                     smask[c * 128 + m] = mask;
                 }
-            } else {
-                float r[16];
-                tc::tmem_ld16(tbase, r);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < BN && j < 16; ++j) {
-                    const float in = __fadd_rn(r[j], sbias[j]);
-                    v[j] = p.mode == 1 ? __fadd_rn(v[j], in) : in;   // BN < 32: head modes only
+                tc::tc_fence_before();
+                tc::mbar_arrive(acce_bar(a));
+                tc::named_bar_sync(1, 128);
+                const int npix = p.pool ? 32 : 128;
+                for (int item = et; item < npix * NCH; item += 128) {
+                    const int pix = item / NCH, c = item - pix * NCH;
+                    store_spikes(p, tl, t, c, pix, [&](int mm) { return smask[c * 128 + mm]; });
                 }
-            }
-            tc::tc_fence_before();
-            tc::mbar_arrive(acce_bar(a));
-            if (p.mode == 2) {
-                if (row_valid) {
-                    float* outf = static_cast<float*>(p.out);
-                    const int64_t row = (int64_t)t * p.B + gimg;
-#pragma unroll
-                    for (int j = 0; j < BN; ++j) {
-                        const int c = n0 + j;
-                        if (c < p.Cout) outf[row * p.Cout + c] = v[j];
-                    }
-                }
-                continue;
-            }
-            if (p.mode != 0) continue;
-            tc::named_bar_sync(1, 128);
-            // ---- store the spikes of step t
-            const int nchunks = BN / 32;
-            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-            if (p.pool) {
-                const int pw = p.bw / 2, ph = p.bh / 2;
-                const int npix = pw * ph * p.bn;
-                const int Ho = p.H / 2, Wo = p.W / 2;
-                for (int item = et; item < npix * nchunks; item += 128) {
-                    const int pix = item / nchunks, c = item - pix * nchunks;
-                    const int xw = pix % pw, xh = (pix / pw) % ph, xn = pix / (pw * ph);
-                    const int m00 = 2 * xw + p.bw * (2 * xh + p.bh * xn);
-                    const uint32_t bits = smask[c * 128 + m00] | smask[c * 128 + m00 + 1] |
-                                          smask[c * 128 + m00 + p.bw] |
-                                          smask[c * 128 + m00 + p.bw + 1];
-                    const int ow = w0 / 2 + xw, oh = h0 / 2 + xh, on = img0 + xn;
-                    if (ow >= Wo || oh >= Ho || on >= p.B) continue;
-                    const int64_t base =
-                        ((((int64_t)t * p.B + on) * Ho + oh) * Wo + ow) * p.Cout + n0 + c * 32;
-                    uint4* dst = reinterpret_cast<uint4*>(out + base);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
-                }
-            } else {
-                for (int item = et; item < 128 * nchunks; item += 128) {
-                    const int pix = item / nchunks, c = item - pix * nchunks;
-                    const int xw = pix % p.bw, xh = (pix / p.bw) % p.bh, xn = pix / (p.bw * p.bh);
-                    const int ow = w0 + xw, oh = h0 + xh, on = img0 + xn;
-                    if (ow >= p.W || oh >= p.H || on >= p.B) continue;
-                    const uint32_t bits = smask[c * 128 + pix];
-                    const int64_t base =
-                        ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) * p.Cout + n0 + c * 32;
-                    uint4* dst = reinterpret_cast<uint4*>(out + base);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
-                }
-            }
-            tc::named_bar_sync(1, 128);
-        }
-        if (p.mode == 1 && row_valid) {
-            // mean over T of (acc + bias): f32 [B, Cout] (linear layers: pixel = image)
-            float* out = static_cast<float*>(p.out);
-            const float inv = 1.0f / (float)p.T;
-            const int64_t row = (int64_t)gimg;
-#pragma unroll
-            for (int j = 0; j < BN; ++j) {
-                const int c = n0 + j;
-                if (c < p.Cout) out[row * p.Cout + c] = __fmul_rn(v[j], inv);
+                tc::named_bar_sync(1, 128);
             }
         }
-        (void)row_valid;
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -333,110 +299,403 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
 }
 
-// ---- first layer: real-valued image, Cin = 3, fp32 SIMT ------------------------------
-// Direct 3x3 conv in float32 (the image is not exact in bf16) + bias + multi-step LIF.
-// x: f32 NCHW [Ti, B, Cin, H, W] with Ti = T, or Ti = 1 for direct encoding (the same
-// image at every step: the conv is computed once).  w: f32 [Cout, Cin, 3, 3] (torch
-// layout).  out: bf16 NHWC spikes [T*B, Ho, Wo, Cout] (pooled if requested).
-// Thread = one output pixel x 8 output channels; the LIF state lives in registers.
-__global__ void __launch_bounds__(256) first_conv_lif_kernel(
-    const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W,
-    const float* __restrict__ w, const float* __restrict__ bias, int Cout,
-    float df, float sc, float thr, float v_reset, int hard, int pool,
-    __nv_bfloat16* __restrict__ out) {
-    const int groups = Cout / 8;
-    const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
+// ---- variant 2: T folded into M -----------------------------------------------------------
+// For layers whose pixel count is too small to fill the GPU with 128-pixel blocks: the
+// 128 accumulator rows of a tile are TS steps x P = 128/TS pixels (row t*P + p), so the
+// grid is TS times larger and each tile runs the K loop once.  One 5-D TMA box per k-slab
+// (channels, w, h, image, step) lands the TS per-step pixel blocks in consecutive rows of
+// the A tile.  The epilogue stages each 32-column slice of the accumulator through shared
+// memory (row stride 33 words, conflict-free) so that a thread owns (pixel, columns) and
+// runs the T recurrence of those neurons itself; spike bits are OR-ed into per-(step,
+// slice, pixel) words, then stored.  Persistent, with two TMEM accumulators alternating
+// between consecutive work items of a CTA.
+//
+// Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
+// accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
+// then runs in reduce_lif_kernel, which adds the splits in a fixed order.
+template <int BN, int STAGES, int TS>
+struct SmemTM {
+    static constexpr int P = 128 / TS;
+    static constexpr int NCH = BN / 32;
+    static constexpr int B_TILE = BN * 128;
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = STAGES * A_TILE_BYTES;
+    static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 128 x 33 f32
+    static constexpr int MASK_OFF = Y_OFF + 128 * 33 * 4;               // TS x NCH x P u32
+    static constexpr int BAR_OFF = (MASK_OFF + TS * NCH * P * 4 + 7) & ~7;
+    static constexpr int NBARS = 2 * STAGES + 4;
+    static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
+    static constexpr int ABORT_OFF = TMEM_OFF + 4;
+    static constexpr int TOTAL = ABORT_OFF + 4;
+    static constexpr int DYN = TOTAL + 1024;
+};
+
+template <int BN, int STAGES, int TS>
+__global__ void __launch_bounds__(THREADS, 1)
+conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const ConvParams p) {
+    using S = SmemTM<BN, STAGES, TS>;
+    constexpr int P = S::P, NCH = S::NCH;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = tc::smem_u32(smem);
+    float* ybuf = reinterpret_cast<float*>(smem + S::Y_OFF);
+    uint32_t* smask = reinterpret_cast<uint32_t*>(smem + S::MASK_OFF);
+    const uint32_t bar0 = sbase + S::BAR_OFF;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KB = p.taps * p.cin_blocks;
+    const int splits = p.splits;
+    const int num_items = p.num_tiles * splits;
+    constexpr uint32_t STAGE_TX = A_TILE_BYTES + S::B_TILE;
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    auto krange = [&](int s, int& k0, int& k1) {
+        k0 = (int)((int64_t)KB * s / splits);
+        k1 = (int)((int64_t)KB * (s + 1) / splits);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(full_bar(s), 1);
+            tc::mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            tc::mbar_init(accf_bar(a), 1);
+            tc::mbar_init(acce_bar(a), 128);
+        }
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmA);
+        tc::prefetch_tmap(&tmB);
+    }
+    for (int i = threadIdx.x; i < TS * NCH * P; i += THREADS) smask[i] = 0u;
+    if (warp == 1) {
+        tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0, issued = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+                const Tile tl = decode_tile(item / splits, p, BN);
+                int k0, k1;
+                krange(item % splits, k0, k1);
+                for (int kb = k0; kb < k1; ++kb) {
+                    if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tap = kb / p.cin_blocks;
+                    const int cb = kb - tap * p.cin_blocks;
+                    const int r = p.taps == 9 ? tap / 3 : 1;
+                    const int s = p.taps == 9 ? tap % 3 : 1;
+                    tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
+                    tc::tma_load_5d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, full_bar(stage),
+                                    cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, tl.img0, 0);
+                    tc::tma_load_2d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
+                                    tap * p.Cin + cb * 64, tl.n0);
+                    ++issued;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) drain_ring(bar0, STAGES, stage, phase, issued);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+            int stage = 0;
+            uint32_t phase = 0, it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
+                int k0, k1;
+                krange(item % splits, k0, k1);
+                const int a = it & 1;
+                if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) break;
+                tc::tc_fence_after();
+                const uint32_t dcol = tmem + a * BN;
+                for (int kb = k0; kb < k1; ++kb) {
+                    if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
+                    const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
+                    tc::umma_commit(empty_bar(stage));
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc::umma_commit(accf_bar(a));
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const int row = 32 * q + lane;
+        const int et = threadIdx.x - 64;
+        const int pp = et % P, g = et / P;              // pixel, column group (TS groups)
+        constexpr int NCOL = 32 / TS;
+        const int64_t npix_total = (int64_t)p.B * p.H * p.W;
+        uint32_t it = 0;
+        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
+            const Tile tl = decode_tile(item / splits, p, BN);
+            const int a = it & 1;
+            if (!tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status)) break;
+            tc::tc_fence_after();
+            if (p.partial) {
+                // ---- split-K: raw float32 partial sums of this split
+                const int split = item % splits;
+                const int t = row / P, px = row % P;
+                const int xw = px % p.bw, xh = (px / p.bw) % p.bh, xn = px / (p.bw * p.bh);
+                const int ow = tl.w0 + xw, oh = tl.h0 + xh, on = tl.img0 + xn;
+                const bool valid = ow < p.W && oh < p.H && on < p.B;
+                const int64_t gpix = ((int64_t)on * p.H + oh) * p.W + ow;
+                float* dst = p.partial + (((int64_t)split * p.T + t) * npix_total + gpix) * p.Cout + tl.n0;
+#pragma unroll 1
+                for (int c = 0; c < NCH; ++c) {
+                    float r[32];
+                    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32, r);
+                    tc::tmem_wait_ld();
+                    if (valid) {
+                        float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            d4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                    }
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(acce_bar(a));
+                continue;
+            }
+#pragma unroll 1
+            for (int c = 0; c < NCH; ++c) {
+                float r[32];
+                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32, r);
+                tc::tmem_wait_ld();
+                if (c == NCH - 1) {           // accumulator fully read: hand it back
+                    tc::tc_fence_before();
+                    tc::mbar_arrive(acce_bar(a));
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ybuf[row * 33 + j] = r[j];
+                tc::named_bar_sync(1, 128);
+                uint32_t bits[TS];
+#pragma unroll
+                for (int t = 0; t < TS; ++t) bits[t] = 0u;
+#pragma unroll
+                for (int jj = 0; jj < NCOL; ++jj) {
+                    const int col = g * NCOL + jj;
+                    const float bb = __ldg(p.bias + tl.n0 + c * 32 + col);
+                    float v = 0.0f;
+#pragma unroll
+                    for (int t = 0; t < TS; ++t) {
+                        const float in = __fadd_rn(ybuf[(t * P + pp) * 33 + col], bb);
+                        float vv = charge(v, p.df, p.sc, in);
+                        const bool s = vv >= p.thr;
+                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                        v = vv;
+                        bits[t] |= (s ? 1u : 0u) << col;
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < TS; ++t)
+                    if (bits[t]) atomicOr(&smask[(t * NCH + c) * P + pp], bits[t]);
+                tc::named_bar_sync(1, 128);
+            }
+            // ---- stores
+            const int npix = p.pool ? P / 4 : P;
+            for (int w_item = et; w_item < TS * npix * NCH; w_item += 128) {
+                const int c = w_item % NCH;
+                const int rest = w_item / NCH;
+                const int pix = rest % npix, t = rest / npix;
+                store_spikes(p, tl, t, c, pix,
+                             [&](int mm) { return smask[(t * NCH + c) * P + mm]; });
+            }
+            tc::named_bar_sync(1, 128);
+            for (int i = et; i < TS * NCH * P; i += 128) smask[i] = 0u;
+            tc::named_bar_sync(1, 128);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ---- split-K reduction + bias + multi-step LIF (+ 2x2 max-pool) -------------------------
+// partial [S][T][B*H*W][C] f32 -> spikes bf16 [T][B][Ho][Wo][C].  Thread = one output
+// pixel (a 2x2 window when pooling) x 8 channels; the splits are added in order
+// s = 0..S-1, then the bias, then the neuron runs over t with v in registers.
+template <bool POOL>
+__global__ void __launch_bounds__(256) reduce_lif_kernel(const float* __restrict__ partial, int S,
+                                                         int T, int B, int H, int W, int C,
+                                                         const float* __restrict__ bias, float df,
+                                                         float sc, float thr, float v_reset,
+                                                         int hard, __nv_bfloat16* __restrict__ out) {
+    constexpr int NP = POOL ? 4 : 1;
+    const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
+    const int groups = C / 8;
     const int64_t total = (int64_t)B * Ho * Wo * groups;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= total) return;
     const int g = (int)(gid % groups);
     int64_t r = gid / groups;
-    const int ow = (int)(r % Wo); r /= Wo;
+    const int ow = (int)(r % Wo);
+    r /= Wo;
     const int oh = (int)(r % Ho);
     const int b = (int)(r / Ho);
-    const int npix = pool ? 4 : 1;
-    float v[4][8];
+    const int64_t npix = (int64_t)B * H * W;
+    float bb[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 8; ++j) bb[j] = __ldg(bias + g * 8 + j);
+    float v[NP][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
-    float y[4][8];
+    for (int q = 0; q < NP; ++q)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q][j] = 0.0f;
     for (int t = 0; t < T; ++t) {
-        const int ti = Ti == 1 ? 0 : t;
-        if (ti == t || t == 0) {
-            for (int pi = 0; pi < npix; ++pi) {
-                const int h = pool ? 2 * oh + (pi >> 1) : oh;
-                const int ww = pool ? 2 * ow + (pi & 1) : ow;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int co = g * 8 + j;
-                    float acc = 0.0f;
-                    for (int ci = 0; ci < Cin; ++ci) {
-                        const float* xc = x + (((int64_t)ti * B + b) * Cin + ci) * H * W;
-                        const float* wc = w + ((int64_t)co * Cin + ci) * 9;
-#pragma unroll
-                        for (int kh = 0; kh < 3; ++kh) {
-                            const int ih = h + kh - 1;
-                            if (ih < 0 || ih >= H) continue;
-#pragma unroll
-                            for (int kw = 0; kw < 3; ++kw) {
-                                const int iw = ww + kw - 1;
-                                if (iw < 0 || iw >= W) continue;
-                                acc = __fmaf_rn(__ldg(xc + ih * W + iw), __ldg(wc + kh * 3 + kw), acc);
-                            }
-                        }
-                    }
-                    y[pi][j] = acc;
-                }
-            }
-        }
         uint32_t bits = 0;
-        for (int pi = 0; pi < npix; ++pi) {
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+            const int h = POOL ? 2 * oh + (q >> 1) : oh;
+            const int w = POOL ? 2 * ow + (q & 1) : ow;
+            const int64_t pix = ((int64_t)b * H + h) * W + w;
+            float acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+            for (int s = 0; s < S; ++s) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    partial + (((int64_t)s * T + t) * npix + pix) * C + g * 8);
+                const float4 x0 = __ldcs(src), x1 = __ldcs(src + 1);
+                acc[0] = __fadd_rn(acc[0], x0.x); acc[1] = __fadd_rn(acc[1], x0.y);
+                acc[2] = __fadd_rn(acc[2], x0.z); acc[3] = __fadd_rn(acc[3], x0.w);
+                acc[4] = __fadd_rn(acc[4], x1.x); acc[5] = __fadd_rn(acc[5], x1.y);
+                acc[6] = __fadd_rn(acc[6], x1.z); acc[7] = __fadd_rn(acc[7], x1.w);
+            }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float in = __fadd_rn(y[pi][j], __ldg(bias + g * 8 + j));
-                float vv = charge(v[pi][j], df, sc, in);
-                const bool s = vv >= thr;
-                vv = hard ? (s ? v_reset : vv) : (s ? __fsub_rn(vv, thr) : vv);
-                v[pi][j] = vv;
-                bits |= (s ? 1u : 0u) << j;
+                const float in = __fadd_rn(acc[j], bb[j]);
+                float vv = charge(v[q][j], df, sc, in);
+                const bool sp = vv >= thr;
+                vv = hard ? (sp ? v_reset : vv) : (sp ? __fsub_rn(vv, thr) : vv);
+                v[q][j] = vv;
+                bits |= (sp ? 1u : 0u) << j;
             }
         }
-        const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * Cout + g * 8;
+        const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 8;
         *reinterpret_cast<uint4*>(out + o) = spikes_to_bf16x8(bits & 0xffu);
     }
 }
 
-template <int BN, int STAGES>
-int launch_conv(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p, int grid,
-                cudaStream_t s) {
-    using S = Smem<BN, STAGES>;
-    cudaError_t e = cudaFuncSetAttribute(conv_lif_kernel<BN, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::DYN);
+int sm_count() {
+    static int n[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+            v = 148;
+        n[dev] = v;
+    }
+    return n[dev];
+}
+
+template <typename K>
+int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const ConvParams& p, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return record_cuda_error(e);
-    conv_lif_kernel<BN, STAGES><<<grid, THREADS, S::DYN, s>>>(ta, tb, p);
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, THREADS, smem);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (occ < 1) return SNNB_ERR_UNSUPPORTED;
+    const int64_t cap = (int64_t)sm_count() * occ;
+    const int grid = (int)(p.num_tiles < cap ? p.num_tiles : cap);
+    kernel<<<grid, THREADS, smem, s>>>(ta, tb, p);
     return launch_status();
 }
 
-// Pixel block of 128 rows for an H x W image batch: full rows when W <= 128, pairs
-// of rows / columns kept even for pooling.
-bool choose_block(int H, int W, int& bw, int& bh, int& bn) {
-    if (W >= 128) {
-        if (W % 128) return false;
-        bw = 128; bh = 1; bn = 1;
+// Ring depths fill the ~227 KB of shared memory: at these tile sizes one k-slab of MMAs
+// (0.1-0.4 us) is far shorter than a TMA round trip, so depth is what keeps the tensor
+// pipe fed.
+template <int BN, int STAGES>
+int launch_conv(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
+    return launch_persistent(conv_lif_kernel<BN, STAGES>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
+}
+
+template <int BN, int STAGES, int TS>
+int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+                   cudaStream_t s) {
+    return launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS>, SmemTM<BN, STAGES, TS>::DYN, ta,
+                             tb, p, s);
+}
+
+template <int TS>
+int launch_tm_bn(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+                 cudaStream_t s) {
+    switch (BN) {
+        case 256: return launch_conv_tm<256, 4, TS>(ta, tb, p, s);
+        case 128: return launch_conv_tm<128, 6, TS>(ta, tb, p, s);
+        case 64: return launch_conv_tm<64, 8, TS>(ta, tb, p, s);
+        default: return launch_conv_tm<32, 9, TS>(ta, tb, p, s);
+    }
+}
+
+// Pixel block of P rows (P = 128, or 128 / T when T is folded into M) for an H x W
+// image batch: bw columns x bh rows x bn images with bw * bh * bn == P.  Exact tilings
+// are preferred; otherwise power-of-two block sides leave partial blocks at the right /
+// bottom / last-image edges, whose out-of-range rows the TMA zero-fills and the
+// epilogue never stores.  With pooling bw and bh are even so that every 2x2 window
+// lies inside one block.
+static int pow2_floor(int v) {
+    int r = 1;
+    while (r * 2 <= v) r *= 2;
+    return r;
+}
+
+bool choose_block(int H, int W, int P, bool pool, int& bw, int& bh, int& bn) {
+    if (W >= P && W % P == 0 && !pool) {
+        bw = P; bh = 1; bn = 1;
         return true;
     }
-    if (128 % W) return false;
-    bw = W;
-    const int rows = 128 / W;
-    if (H >= rows) {
-        if (H % rows) return false;
-        bh = rows; bn = 1;
+    if (W >= P / 2 && pool) {
+        bw = P / 2; bh = 2; bn = 1;
+    } else if (W < P && P % W == 0) {
+        bw = W;
     } else {
-        if (rows % H) return false;
-        bh = H; bn = rows / H;
+        bw = pow2_floor(W < P ? W : P);
+        if (pool && bw < 2) return false;
     }
-    return true;
+    const int rows = P / bw;
+    if (pool && bw == P / 2) {
+        bh = 2; bn = 1;
+    } else if (H >= rows) {
+        bh = rows; bn = 1;
+    } else if (rows % H == 0) {
+        bh = H; bn = rows / H;
+    } else {
+        bh = pow2_floor(H);
+        bn = rows / bh;
+    }
+    if (bw * bh * bn != P) return false;
+    return !pool || ((bw % 2 == 0) && (bh % 2 == 0));
 }
 
 }  // namespace
@@ -484,33 +743,82 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 namespace {
 
 // Shared host path of the conv / linear entries.
+// variant: 0 = choose, 1 = T sequential inside the CTA (128-pixel blocks),
+//          2 = T folded into M (128/T-pixel blocks, T in {2, 4, 8}).
+// block_n: 0 = choose, else 32 / 64 / 128 (/ 256 with variant 2) output channels per CTA.
+// splits : > 1 splits the K range (variant 2 only): partial sums go to `workspace`
+//          ([splits][T][B*H*W][Cout] f32, caller-owned) and reduce_lif_kernel finishes.
 int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                  const float* bias, int Cout, int taps, float df, float sc, float thr,
-                 float v_reset, int hard, int pool, int mode, void* out, cudaStream_t s) {
-    if (!x || !w || !out) return SNNB_ERR_ARG;
+                 float v_reset, int hard, int pool, int variant, int block_n, int splits,
+                 void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s) {
+    if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
-    if (Cin % 64 != 0) return SNNB_ERR_UNSUPPORTED;
+    if (Cin % 64 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
-    int bw, bh, bn;
-    if (!choose_block(H, W, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
-    if (pool && ((H % 2) || (W % 2) || (bw % 2) || (bh % 2))) return SNNB_ERR_UNSUPPORTED;
+    if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    int BN;
-    if (mode != 0) {
-        BN = Cout <= 16 ? 16 : (Cout <= 32 ? 32 : 64);
-    } else {
-        if (Cout % 32) return SNNB_ERR_UNSUPPORTED;
-        BN = (Cout % 128 == 0) ? 128 : (Cout % 64 == 0 ? 64 : 32);
+    if (variant < 0 || variant > 2) return SNNB_ERR_ARG;
+    if (block_n != 0 && block_n != 32 && block_n != 64 && block_n != 128 && block_n != 256)
+        return SNNB_ERR_ARG;
+    if (block_n && Cout % block_n) return SNNB_ERR_ARG;
+    if (splits < 1) splits = 1;
+    const int KB = taps * (Cin / 64);
+    if (splits > KB) return SNNB_ERR_ARG;
+    const bool tm_ok = (T == 2 || T == 4 || T == 8);
+    if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;
+    if (splits > 1 && (variant == 1 || !tm_ok)) return SNNB_ERR_UNSUPPORTED;
+    if (splits > 1) variant = 2;
+    const int bn_max = (Cout % 128 == 0) ? 128 : (Cout % 64 == 0 ? 64 : 32);
+    int bw, bh, bn;
+    if (variant == 0) {
+        // sequential kernel unless its grid leaves SMs idle and folding T is possible
+        variant = 1;
+        if (tm_ok && choose_block(H, W, 128, pool, bw, bh, bn)) {
+            const int64_t seq_grid = ((int64_t)((W + bw - 1) / bw) * ((H + bh - 1) / bh) *
+                                      ((B + bn - 1) / bn)) * (Cout / (block_n ? block_n : bn_max));
+            if (seq_grid < 2 * 148) variant = 2;
+        } else if (tm_ok) {
+            variant = 2;
+        }
+    }
+    if (variant == 1 && block_n == 256) return SNNB_ERR_UNSUPPORTED;   // v[] would not fit
+    const int P = variant == 2 ? 128 / T : 128;
+    if (!choose_block(H, W, P, pool, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
+    const int64_t mtiles = (int64_t)((W + bw - 1) / bw) * ((H + bh - 1) / bh) * ((B + bn - 1) / bn);
+    int BN = block_n;
+    if (!BN) {
+        BN = bn_max;
+        // narrower channel blocks until the grid covers the SMs
+        while (BN > 32 && mtiles * (Cout / BN) * splits < 148) BN /= 2;
+    }
+    if (splits > 1) {
+        const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
+        if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
     }
     int* status = device_status_ptr();
     if (!status) return SNNB_ERR_CUDA;
-    // activation map: dims (Cin, W, H, T*B), box (64, bw, bh, bn)
     CUtensorMap ta, tb;
-    const uint64_t adims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)T * B};
-    const uint64_t astr[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
-    const uint32_t abox[4] = {64, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn};
-    int rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, adims, astr, abox,
+    int rc;
+    if (variant == 2) {
+        // activation map: dims (Cin, W, H, B, T), box (64, bw, bh, bn, T): one box = the
+        // pixel block at every step, rows ordered (t, pixel)
+        const uint64_t adims[5] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B,
+                                   (uint64_t)T};
+        const uint64_t astr[4] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2,
+                                  (uint64_t)H * W * Cin * 2, (uint64_t)B * H * W * Cin * 2};
+        const uint32_t abox[5] = {64, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn, (uint32_t)T};
+        rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, x, adims, astr, abox,
                          CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+        // activation map: dims (Cin, W, H, T*B), box (64, bw, bh, bn)
+        const uint64_t adims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)T * B};
+        const uint64_t astr[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2,
+                                  (uint64_t)H * W * Cin * 2};
+        const uint32_t abox[4] = {64, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn};
+        rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, adims, astr, abox,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     if (rc != SNNB_OK) return rc;
     // weight map: dims (taps*Cin, Cout), box (64, BN)
     const uint64_t bdims[2] = {(uint64_t)taps * Cin, (uint64_t)Cout};
@@ -523,18 +831,37 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.T = T; p.B = B; p.H = H; p.W = W; p.Cin = Cin; p.Cout = Cout;
     p.bw = bw; p.bh = bh; p.bn = bn;
     p.tiles_w = (W + bw - 1) / bw; p.tiles_h = (H + bh - 1) / bh;
-    const int tiles_n = (B + bn - 1) / bn;
-    p.n_tiles_n = (Cout + BN - 1) / BN;
-    p.taps = taps; p.cin_blocks = Cin / 64; p.pool = pool; p.mode = mode;
+    p.n_tiles_n = Cout / BN;
+    p.taps = taps; p.cin_blocks = Cin / 64; p.pool = pool;
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
-    p.bias = bias; p.out = out; p.status = status;
-    const int64_t grid = (int64_t)p.tiles_w * p.tiles_h * tiles_n * p.n_tiles_n;
-    if (grid > 0x7fffffff) return SNNB_ERR_ARG;
+    p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
+    p.splits = splits;
+    p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+    const int64_t ntiles = mtiles * p.n_tiles_n;
+    if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
+    p.num_tiles = (int)ntiles;
+    if (variant == 2) {
+        switch (T) {
+            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s); break;
+            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s); break;
+            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s); break;
+        }
+        if (rc != SNNB_OK || splits == 1) return rc;
+        const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
+        const int64_t threads = (int64_t)B * Ho * Wo * (Cout / 8);
+        const int64_t blocks = (threads + 255) / 256;
+        if (pool)
+            reduce_lif_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(
+                p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset, p.hard, p.out);
+        else
+            reduce_lif_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(
+                p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset, p.hard, p.out);
+        return launch_status();
+    }
     switch (BN) {
-        case 128: return launch_conv<128, 4>(ta, tb, p, (int)grid, s);
-        case 64: return launch_conv<64, 6>(ta, tb, p, (int)grid, s);
-        case 32: return launch_conv<32, 6>(ta, tb, p, (int)grid, s);
-        default: return launch_conv<16, 6>(ta, tb, p, (int)grid, s);
+        case 128: return launch_conv<128, 6>(ta, tb, p, s);
+        case 64: return launch_conv<64, 8>(ta, tb, p, s);
+        default: return launch_conv<32, 10>(ta, tb, p, s);
     }
 }
 
@@ -546,58 +873,33 @@ using namespace snnb;
 extern "C" int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
                                 int64_t Cin, const void* w, const float* bias, int64_t Cout,
                                 float decay, float input_scale, float v_threshold, float v_reset,
-                                int hard_reset, int pool, void* out, snnb_stream_t stream) {
+                                int hard_reset, int pool, int variant, int block_n, int splits,
+                                void* workspace, int64_t workspace_bytes, void* out,
+                                snnb_stream_t stream) {
     if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
         Cin > 0x7fffffff || Cout > 0x7fffffff)
         return SNNB_ERR_ARG;
     return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout, 9, decay,
-                        input_scale, v_threshold, v_reset, hard_reset, pool, 0, out,
-                        static_cast<cudaStream_t>(stream));
+                        input_scale, v_threshold, v_reset, hard_reset, pool, variant, block_n,
+                        splits, workspace, workspace_bytes, out, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                                const float* bias, int64_t N, float decay, float input_scale,
-                               float v_threshold, float v_reset, int hard_reset, void* out,
-                               snnb_stream_t stream) {
+                               float v_threshold, float v_reset, int hard_reset, int variant,
+                               int block_n, int splits, void* workspace, int64_t workspace_bytes,
+                               void* out, snnb_stream_t stream) {
     if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 0x7fffffff) return SNNB_ERR_ARG;
     // a linear layer is a 1x1 "conv" over B images of 1 x 1 pixels
     return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, decay, input_scale,
-                        v_threshold, v_reset, hard_reset, 0, 0, out,
-                        static_cast<cudaStream_t>(stream));
+                        v_threshold, v_reset, hard_reset, 0, variant, block_n, splits, workspace,
+                        workspace_bytes, out, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
-                                const float* bias, int64_t N, float* out, snnb_stream_t stream) {
-    if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 64) return SNNB_ERR_ARG;
-    return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, 0.f, 0.f, 0.f, 0.f, 0,
-                        0, 1, out, static_cast<cudaStream_t>(stream));
-}
-
-extern "C" int snnb_linear_out(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
-                               const float* bias, int64_t N, float* out, snnb_stream_t stream) {
-    if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 64) return SNNB_ERR_ARG;
-    return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, 0.f, 0.f, 0.f, 0.f, 0,
-                        0, 2, out, static_cast<cudaStream_t>(stream));
-}
-
-extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_t B, int64_t Cin,
-                                   int64_t H, int64_t W, const float* w, const float* bias,
-                                   int64_t Cout, float decay, float input_scale,
-                                   float v_threshold, float v_reset, int hard_reset, int pool,
-                                   void* out, snnb_stream_t stream) {
-    if (!x || !w || !bias || !out) return SNNB_ERR_ARG;
-    if (T <= 0 || B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return SNNB_ERR_ARG;
-    if (Ti != 1 && Ti != T) return SNNB_ERR_ARG;
-    if (Cout % 8 || !aligned16(out)) return SNNB_ERR_ARG;
-    if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
-    if (T * B * Cin * H * W > ((int64_t)1 << 40)) return SNNB_ERR_ARG;
-    const int Ho = pool ? (int)H / 2 : (int)H, Wo = pool ? (int)W / 2 : (int)W;
-    const int64_t total = B * Ho * Wo * (Cout / 8);
-    const int64_t blocks = (total + 255) / 256;
-    first_conv_lif_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        x, (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay,
-        input_scale, v_threshold, v_reset, hard_reset, pool, static_cast<__nv_bfloat16*>(out));
-    return launch_status();
+extern "C" int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W,
+                                              int64_t Cout, int splits) {
+    if (splits <= 1) return 0;
+    return (int64_t)splits * T * B * H * W * Cout * 4;
 }
 
 extern "C" int snnb_read_device_status(snnb_stream_t stream, int* status_out) {

@@ -30,8 +30,9 @@ SIGNATURES = {
                               P, P, I32, P, P, P, P],
     "snnb_bitpack": [P, I32, I64, I64, I64, I32, P, P],
     "snnb_bgemm": [P, P, P, I64, I64, I64, I64, I32, I32, P],
-    "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P, P],
-    "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, P],
+    "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32,
+                         I32, P, I64, P, P],
+    "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32, P, I64, P, P],
     "snnb_linear_mean": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_linear_out": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
@@ -58,6 +59,8 @@ def lib():
         L.snnb_status_string.restype = ctypes.c_char_p
         L.snnb_status_string.argtypes = [ctypes.c_int]
         L.snnb_last_cuda_error.restype = ctypes.c_char_p
+        L.snnb_split_workspace_bytes.restype = ctypes.c_int64
+        L.snnb_split_workspace_bytes.argtypes = [I64, I64, I64, I64, I64, I32]
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)
             fn.argtypes = args

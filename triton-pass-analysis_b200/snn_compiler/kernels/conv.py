@@ -30,8 +30,11 @@ def _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset)
 def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
                 tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
                 v_threshold=1.0, v_reset: float = 0.0, pool: bool = False,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool)."""
+                out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
+                splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool).
+    variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M; block_n: 0 or 32/64/128/256;
+    splits > 1: split-K with float32 partials in `workspace` (allocated here if None)."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1:3] == (3, 3)
     T, B, H, W, Cin = x.shape
@@ -43,16 +46,20 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     Ho, Wo = (H // 2, W // 2) if pool else (H, W)
     if out is None:
         out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
+    ws, ws_bytes = _workspace(workspace, splits, T, B, H, W, Cout, x.device)
     st = _lib.lib().snnb_conv3x3_lif(_lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias),
-                                     Cout, df, sc, thr, vr, hard, int(bool(pool)), _lib.ptr(out),
-                                     _lib.stream_of(x))
+                                     Cout, df, sc, thr, vr, hard, int(bool(pool)), int(variant),
+                                     int(block_n), int(splits), _lib.ptr(ws), ws_bytes,
+                                     _lib.ptr(out), _lib.stream_of(x))
     _lib.check(st, "snnb_conv3x3_lif")
     return out
 
 
 def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
                tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
-               v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None):
+               v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,
+               variant: int = 0, block_n: int = 0, splits: int = 1,
+               workspace: torch.Tensor | None = None):
     """x [T, B, K] bf16 @ w[N, K]^T + bias -> LIF -> spikes [T, B, N] bf16."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
@@ -63,10 +70,26 @@ def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: 
                                       v_reset)
     if out is None:
         out = torch.empty(T, B, N, device=x.device, dtype=torch.bfloat16)
+    ws, ws_bytes = _workspace(workspace, splits, T, B, 1, 1, N, x.device)
     st = _lib.lib().snnb_linear_lif(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N, df, sc,
-                                    thr, vr, hard, _lib.ptr(out), _lib.stream_of(x))
+                                    thr, vr, hard, int(variant), int(block_n), int(splits),
+                                    _lib.ptr(ws), ws_bytes, _lib.ptr(out), _lib.stream_of(x))
     _lib.check(st, "snnb_linear_lif")
     return out
+
+
+def split_workspace_bytes(T, B, H, W, Cout, splits) -> int:
+    return int(_lib.lib().snnb_split_workspace_bytes(T, B, H, W, Cout, int(splits)))
+
+
+def _workspace(ws, splits, T, B, H, W, Cout, device):
+    need = split_workspace_bytes(T, B, H, W, Cout, splits)
+    if need == 0:
+        return None, 0
+    if ws is None:
+        ws = torch.empty(need // 4, device=device, dtype=torch.float32)
+    assert ws.is_cuda and ws.is_contiguous() and ws.numel() * ws.element_size() >= need
+    return ws, ws.numel() * ws.element_size()
 
 
 def linear_mean(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
@@ -121,6 +144,54 @@ def first_conv_lif(img: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, T:
                                         int(bool(pool)), _lib.ptr(out), _lib.stream_of(img))
     _lib.check(st, "snnb_first_conv_lif")
     return out
+
+
+def time_graph(fn, reps: int = 10) -> float:
+    """Device milliseconds per call of fn (a launcher on the current stream): reps calls
+    are captured into one CUDA graph and the replay is timed with events, so host-side
+    launch overhead does not enter the figure."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms
+
+
+def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8):
+    """(variant, block_n, splits) configurations a layer admits."""
+    out = []
+    for v in ((1, 2) if T in (2, 4, 8) else (1,)):
+        for bn in ((32, 64, 128) if v == 1 else (32, 64, 128, 256)):
+            if cout % bn:
+                continue
+            out.append((v, bn, 1))
+            if v == 2 and bn >= 128:
+                s = 2
+                while s <= max_splits and s <= kslabs // 2:
+                    out.append((v, bn, s))
+                    s *= 2
+    return out
+
+
+def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10):
+    """Time launch(variant, block_n, splits) for every configuration the layer admits
+    (on its real operands, device time via time_graph) and return the fastest."""
+    best, best_ms = (0, 0, 1), float("inf")
+    for cfg in candidates(cout, T, kslabs):
+        ms = time_graph(lambda: launch(*cfg), reps)
+        if ms < best_ms:
+            best, best_ms = cfg, ms
+    return best
 
 
 def device_status(stream_tensor: torch.Tensor | None = None) -> int:

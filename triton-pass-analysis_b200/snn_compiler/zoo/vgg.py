@@ -71,8 +71,10 @@ class SpikingVGG:
 
     def __init__(self, P, *, T: int = 4, tau: float = 2.0, decay_input: bool = True,
                  v_threshold: float = 1.0, v_reset: float = 0.0, soft_reset: bool = False,
-                 neuron: str = "lif", device="cuda"):
+                 neuron: str = "lif", device="cuda", autotune: bool = True):
         self.T = T
+        self.autotune = autotune
+        self.choice = {}          # (layer, B, H, W) -> (variant, block_n) picked by timing
         self.lif = dict(neuron=neuron, tau=tau, decay_input=decay_input, soft_reset=soft_reset,
                         v_threshold=v_threshold, v_reset=v_reset)
         dev = torch.device(device)
@@ -93,6 +95,7 @@ class SpikingVGG:
                      "b": f["b"].float().contiguous().to(dev)} for f in P["fcs"]]
         self.num_classes = P["fcs"][-1]["w"].shape[0]
         self._bufs = {}
+        self._workspace = None
         self.graphs = None
 
     # ---- per-layer launch plan -----------------------------------------------------------
@@ -127,9 +130,12 @@ class SpikingVGG:
                 fn = (lambda L=L, o=bufs[0]: KC.first_conv_lif(img, L["w"], L["b"], T=T,
                                                              pool=L["pool"], out=o, **self.lif))
             else:
-                fn = (lambda L=L, x=x_prev, o=bufs[i]: KC.conv3x3_lif(x, L["w"], L["b"],
-                                                                    pool=L["pool"], out=o,
-                                                                    **self.lif))
+                fn = self._tuned(("conv", i, B, h, w), L["cout"], 9 * L["cin"] // 64,
+                                 lambda v, bn, sp, L=L, x=x_prev, o=bufs[i], hh=h, ww=w:
+                                 KC.conv3x3_lif(x, L["w"], L["b"], pool=L["pool"], out=o,
+                                                variant=v, block_n=bn, splits=sp,
+                                                workspace=self._ws(T, B, hh, ww, L["cout"], sp),
+                                                **self.lif))
             steps.append((f"conv{i + 1}_{L['cin']}x{L['cout']}@{h}", flops, fn))
             x_prev = bufs[i]
             if L["pool"]:
@@ -138,8 +144,12 @@ class SpikingVGG:
         for j, f in enumerate(self.fcs[:-1]):
             K, N = f["w"].shape[1], f["w"].shape[0]
             steps.append((f"fc{j + 1}_{K}x{N}", 2 * T * B * K * N,
-                          (lambda f=f, x=hcur, o=fbufs[j]: KC.linear_lif(x, f["w"], f["b"], out=o,
-                                                                        **self.lif))))
+                          self._tuned(("fc", j, B, 1, 1), N, K // 64,
+                                      lambda v, bn, sp, f=f, x=hcur, o=fbufs[j], NN=N:
+                                      KC.linear_lif(x, f["w"], f["b"], out=o, variant=v,
+                                                    block_n=bn, splits=sp,
+                                                    workspace=self._ws(T, B, 1, 1, NN, sp),
+                                                    **self.lif))))
             hcur = fbufs[j]
         f = self.fcs[-1]
         K, N = f["w"].shape[1], f["w"].shape[0]
@@ -147,6 +157,26 @@ class SpikingVGG:
         steps.append((f"fc{len(self.fcs)}_{K}x{N}", 2 * T * B * K * N,
                       (lambda f=f, x=hcur: head(x, f["w"], f["b"], out=out))))
         return steps, out
+
+    def _ws(self, T, B, H, W, Cout, splits):
+        """Split-K workspace, one buffer shared by every layer of the engine (layers run one
+        after another on one stream), grown to the largest request."""
+        need = KC.split_workspace_bytes(T, B, H, W, Cout, splits)
+        if need == 0:
+            return None
+        if self._workspace is None or self._workspace.numel() * 4 < need:
+            self._workspace = torch.empty(need // 4, device=self.device, dtype=torch.float32)
+        return self._workspace
+
+    def _tuned(self, key, cout, kslabs, launch):
+        """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
+        call times every (variant, block_n, splits) the layer admits and keeps the fastest."""
+        def run():
+            if key not in self.choice:
+                self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs) \
+                    if self.autotune else (0, 0, 1)
+            return launch(*self.choice[key])
+        return run
 
     def forward(self, img: torch.Tensor, *, per_step_logits: bool = False) -> torch.Tensor:
         """img [B, 3, H, W] (direct encoding: the same image at every step) or
@@ -160,6 +190,16 @@ class SpikingVGG:
         return out
 
     __call__ = forward
+
+    def profile_layers(self, img: torch.Tensor, reps: int = 10):
+        """[(name, flops, device ms per launch)] for one forward plan, each launch timed
+        alone from a CUDA graph of `reps` repetitions (no host overhead in the figure)."""
+        if img.ndim == 4:
+            img = img.unsqueeze(0)
+        steps, _ = self.plan(img)
+        for _, _, fn in steps:
+            fn()
+        return [(name, flops, KC.time_graph(fn, reps)) for name, flops, fn in steps]
 
     def flops_per_image(self, H: int = 32, W: int = 32) -> int:
         """Dense algorithmic FLOPs of one image (every conv at every step)."""
