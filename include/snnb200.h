@@ -140,7 +140,7 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *           per CTA, T in {2, 4, 8}) for layers too small to fill the GPU otherwise.
  * block_n : output channels per CTA, 0 = choose, or 32 / 64 / 128 (dividing Cout), or 256
  *           with variant 2.
- * splits  : 1, or k-range splits for small layers (variant 2): each split's float32
+ * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32
  *           partial sums go to `workspace` (caller-owned, >= snnb_split_workspace_bytes,
  *           16-byte aligned) and a second kernel adds them in a fixed order, adds the bias
  *           and runs the neuron (+ pool).  workspace may be NULL when splits == 1.

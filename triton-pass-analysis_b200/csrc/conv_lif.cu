@@ -312,7 +312,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 //
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
-// then runs in reduce_lif_kernel, which adds the splits in a fixed order.
+// then runs after splitsum_kernel, which adds the splits in a fixed order.
 template <int BN, int STAGES, int TS>
 struct SmemTM {
     static constexpr int P = 128 / TS;
@@ -540,15 +540,50 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 }
 
 // ---- split-K reduction + bias + multi-step LIF (+ 2x2 max-pool) -------------------------
-// partial [S][T][B*H*W][C] f32 -> spikes bf16 [T][B][Ho][Wo][C].  Thread = one output
-// pixel (a 2x2 window when pooling) x 8 channels; the splits are added in order
-// s = 0..S-1, then the bias, then the neuron runs over t with v in registers.
+// Two passes over partial [S][T][B*H*W][C] f32, both fully parallel:
+//  1. splitsum_kernel: thread = (step, pixel, 8 channels); issues its S loads at once,
+//     adds them in the order s = 0..S-1, adds the bias, and writes y in place of split 0;
+//  2. lif_pool_kernel: thread = (output pixel, 8 channels); loads y of its pixels for
+//     every step, runs the neuron over t with v in registers, ORs 2x2 windows when
+//     pooling, and stores bf16 spikes [T][B][Ho][Wo][C].
+template <int S>
+__global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ partial, int64_t rows,
+                                                       int C, const float* __restrict__ bias) {
+    const int groups = C / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= rows * groups) return;
+    const int g = (int)(gid % groups);
+    const int64_t row = gid / groups;                 // t * npix + pixel
+    const int64_t stride = rows * C;                  // one split
+    float4 v[S][2];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const float4* src = reinterpret_cast<const float4*>(partial + s * stride + row * C + g * 8);
+        v[s][0] = __ldcs(src);
+        v[s][1] = __ldcs(src + 1);
+    }
+    float acc[8];
+    acc[0] = v[0][0].x; acc[1] = v[0][0].y; acc[2] = v[0][0].z; acc[3] = v[0][0].w;
+    acc[4] = v[0][1].x; acc[5] = v[0][1].y; acc[6] = v[0][1].z; acc[7] = v[0][1].w;
+#pragma unroll
+    for (int s = 1; s < S; ++s) {
+        acc[0] = __fadd_rn(acc[0], v[s][0].x); acc[1] = __fadd_rn(acc[1], v[s][0].y);
+        acc[2] = __fadd_rn(acc[2], v[s][0].z); acc[3] = __fadd_rn(acc[3], v[s][0].w);
+        acc[4] = __fadd_rn(acc[4], v[s][1].x); acc[5] = __fadd_rn(acc[5], v[s][1].y);
+        acc[6] = __fadd_rn(acc[6], v[s][1].z); acc[7] = __fadd_rn(acc[7], v[s][1].w);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __ldg(bias + g * 8 + j));
+    float4* dst = reinterpret_cast<float4*>(partial + row * C + g * 8);
+    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
 template <bool POOL>
-__global__ void __launch_bounds__(256) reduce_lif_kernel(const float* __restrict__ partial, int S,
-                                                         int T, int B, int H, int W, int C,
-                                                         const float* __restrict__ bias, float df,
-                                                         float sc, float thr, float v_reset,
-                                                         int hard, __nv_bfloat16* __restrict__ out) {
+__global__ void __launch_bounds__(256) lif_pool_kernel(const float* __restrict__ y, int T, int B,
+                                                       int H, int W, int C, float df, float sc,
+                                                       float thr, float v_reset, int hard,
+                                                       __nv_bfloat16* __restrict__ out) {
     constexpr int NP = POOL ? 4 : 1;
     const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
     const int groups = C / 8;
@@ -562,37 +597,41 @@ __global__ void __launch_bounds__(256) reduce_lif_kernel(const float* __restrict
     const int oh = (int)(r % Ho);
     const int b = (int)(r / Ho);
     const int64_t npix = (int64_t)B * H * W;
-    float bb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) bb[j] = __ldg(bias + g * 8 + j);
     float v[NP][8];
 #pragma unroll
     for (int q = 0; q < NP; ++q)
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[q][j] = 0.0f;
-    for (int t = 0; t < T; ++t) {
-        uint32_t bits = 0;
+    // loads of the next step are issued before the current step's neuron update
+    float4 nxt[NP][2];
+    auto load_step = [&](int t, float4 (&dst)[NP][2]) {
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
             const int h = POOL ? 2 * oh + (q >> 1) : oh;
             const int w = POOL ? 2 * ow + (q & 1) : ow;
-            const int64_t pix = ((int64_t)b * H + h) * W + w;
-            float acc[8];
+            const float4* src = reinterpret_cast<const float4*>(
+                y + ((int64_t)t * npix + ((int64_t)b * H + h) * W + w) * C + g * 8);
+            dst[q][0] = __ldcs(src);
+            dst[q][1] = __ldcs(src + 1);
+        }
+    };
+    if (T > 0) load_step(0, nxt);
+    for (int t = 0; t < T; ++t) {
+        float4 in[NP][2];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-            for (int s = 0; s < S; ++s) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    partial + (((int64_t)s * T + t) * npix + pix) * C + g * 8);
-                const float4 x0 = __ldcs(src), x1 = __ldcs(src + 1);
-                acc[0] = __fadd_rn(acc[0], x0.x); acc[1] = __fadd_rn(acc[1], x0.y);
-                acc[2] = __fadd_rn(acc[2], x0.z); acc[3] = __fadd_rn(acc[3], x0.w);
-                acc[4] = __fadd_rn(acc[4], x1.x); acc[5] = __fadd_rn(acc[5], x1.y);
-                acc[6] = __fadd_rn(acc[6], x1.z); acc[7] = __fadd_rn(acc[7], x1.w);
-            }
+        for (int q = 0; q < NP; ++q) {
+            in[q][0] = nxt[q][0];
+            in[q][1] = nxt[q][1];
+        }
+        if (t + 1 < T) load_step(t + 1, nxt);
+        uint32_t bits = 0;
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+            const float x[8] = {in[q][0].x, in[q][0].y, in[q][0].z, in[q][0].w,
+                                in[q][1].x, in[q][1].y, in[q][1].z, in[q][1].w};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float in = __fadd_rn(acc[j], bb[j]);
-                float vv = charge(v[q][j], df, sc, in);
+                float vv = charge(v[q][j], df, sc, x[j]);
                 const bool sp = vv >= thr;
                 vv = hard ? (sp ? v_reset : vv) : (sp ? __fsub_rn(vv, thr) : vv);
                 v[q][j] = vv;
@@ -602,6 +641,22 @@ __global__ void __launch_bounds__(256) reduce_lif_kernel(const float* __restrict
         const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 8;
         *reinterpret_cast<uint4*>(out + o) = spikes_to_bf16x8(bits & 0xffu);
     }
+}
+
+int launch_splitsum(float* partial, int S, int64_t rows, int C, const float* bias, cudaStream_t s) {
+    const int64_t threads = rows * (C / 8);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    switch (S) {
+        case 2: splitsum_kernel<2><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 3: splitsum_kernel<3><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 4: splitsum_kernel<4><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 5: splitsum_kernel<5><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 6: splitsum_kernel<6><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 7: splitsum_kernel<7><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        case 8: splitsum_kernel<8><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
+        default: return SNNB_ERR_UNSUPPORTED;
+    }
+    return launch_status();
 }
 
 int sm_count() {
@@ -627,7 +682,8 @@ int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorM
     if (e != cudaSuccess) return record_cuda_error(e);
     if (occ < 1) return SNNB_ERR_UNSUPPORTED;
     const int64_t cap = (int64_t)sm_count() * occ;
-    const int grid = (int)(p.num_tiles < cap ? p.num_tiles : cap);
+    const int64_t items = (int64_t)p.num_tiles * (p.splits > 1 ? p.splits : 1);
+    const int grid = (int)(items < cap ? items : cap);
     kernel<<<grid, THREADS, smem, s>>>(ta, tb, p);
     return launch_status();
 }
@@ -763,6 +819,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         return SNNB_ERR_ARG;
     if (block_n && Cout % block_n) return SNNB_ERR_ARG;
     if (splits < 1) splits = 1;
+    if (splits > 8) return SNNB_ERR_UNSUPPORTED;
     const int KB = taps * (Cin / 64);
     if (splits > KB) return SNNB_ERR_ARG;
     const bool tm_ok = (T == 2 || T == 4 || T == 8);
@@ -847,15 +904,17 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
             default: rc = launch_tm_bn<8>(BN, ta, tb, p, s); break;
         }
         if (rc != SNNB_OK || splits == 1) return rc;
+        rc = launch_splitsum(p.partial, splits, (int64_t)T * B * H * W, Cout, bias, s);
+        if (rc != SNNB_OK) return rc;
         const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
         const int64_t threads = (int64_t)B * Ho * Wo * (Cout / 8);
         const int64_t blocks = (threads + 255) / 256;
         if (pool)
-            reduce_lif_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(
-                p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset, p.hard, p.out);
+            lif_pool_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(
+                p.partial, T, B, H, W, Cout, df, sc, thr, v_reset, p.hard, p.out);
         else
-            reduce_lif_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(
-                p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset, p.hard, p.out);
+            lif_pool_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(
+                p.partial, T, B, H, W, Cout, df, sc, thr, v_reset, p.hard, p.out);
         return launch_status();
     }
     switch (BN) {
