@@ -171,6 +171,28 @@ int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W, i
                                    int splits);
 
 /*
+ * snnb_conv3x3_lif for callers that cannot allocate (no counterpart in the reference):
+ * the same fused conv + bias + LIF (+ pool), with the split-K partial sums kept in a fixed
+ * scratch array inside the library (16 MiB, held on every GPU that loads the library until
+ * the process exits) instead of a caller workspace.  Meant for plugin or runtime hosts that
+ * offer no scratch buffer and forbid cudaMalloc / cudaFree (which may also synchronise the
+ * device) once they are running.  The call itself allocates nothing.
+ *   - Requests whose partial sums exceed 16 MiB (snnb_split_workspace_bytes) return
+ *     SNNB_ERR_ARG.
+ *   - The first call on a device looks up the array's device address with that device
+ *     current; make that first call before any stream capture.
+ *   - Every call on a device shares the one array, and its contents persist between calls
+ *     (nothing in it needs to start at zero).  Calls whose kernels overlap on the GPU --
+ *     different streams, or concurrent host threads -- race on it: serialise them.
+ * Arguments as snnb_conv3x3_lif, with variant chosen (split-K when splits > 1).
+ */
+int snnb_conv3x3_lif_static_scratch(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                                    int64_t Cin, const void* w, const float* bias, int64_t Cout,
+                                    float decay, float input_scale, float v_threshold,
+                                    float v_reset, int hard_reset, int pool, int block_n,
+                                    int splits, void* out, snnb_stream_t stream);
+
+/*
  * Classifier head: out[b, n] = mean over t of (x[t*B+b] @ w[n]^T + bias[n]), f32.
  * Replaces the last nn.Linear of VGGSNN (snn_compiler/zoo/vgg.py:84, :111-114) and the
  * caller's mean over T (examples/vgg16_snn/vgg16_test.py:243).  K % 8 == 0, N <= 64;

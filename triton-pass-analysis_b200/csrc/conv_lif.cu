@@ -28,6 +28,8 @@
 //           NHWC stored with 16-byte writes.  Only spikes reach HBM.
 // Every mbarrier wait is bounded; on timeout the CTA records SNNB_ERR_TIMEOUT, drains
 // its in-flight copies, frees its TMEM and returns.
+#include <mutex>
+
 #include "tc_common.cuh"
 
 namespace snnb {
@@ -974,4 +976,58 @@ extern "C" int snnb_read_device_status(snnb_stream_t stream, int* status_out) {
     if (e != cudaSuccess) return record_cuda_error(e);
     *status_out = h;
     return SNNB_OK;
+}
+
+// ---- split-K conv without any allocation ------------------------------------------------
+// Some callers cannot hand this library a workspace: a plugin interface whose enqueue call
+// offers no scratch buffer, a runtime whose device memory is fixed at start-up and that
+// forbids cudaMalloc afterwards, or code that must not risk the implicit device
+// synchronisation cudaMalloc / cudaFree can cause.  For them the split-K path of
+// snnb_conv3x3_lif can use the fixed scratch array below instead of a caller buffer.
+//
+// The array lives in the library image: every GPU that loads libsnnb200.so holds these
+// SNNB_STATIC_SCRATCH_BYTES until the process exits.  Host code must not use the symbol
+// itself as a device address (on the host it only names a stand-in); the address is looked
+// up once per device with cudaGetSymbolAddress and handed to the kernels.
+#define SNNB_STATIC_SCRATCH_BYTES (16ll << 20)
+static __device__ __align__(256) float g_static_scratch[SNNB_STATIC_SCRATCH_BYTES / 4];
+
+namespace {
+std::mutex g_static_scratch_lock;
+void* g_static_scratch_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int snnb_conv3x3_lif_static_scratch(
+    const void* x, int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin, const void* w,
+    const float* bias, int64_t Cout, float decay, float input_scale, float v_threshold,
+    float v_reset, int hard_reset, int pool, int block_n, int splits, void* out,
+    snnb_stream_t stream) {
+    if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
+        Cin > 0x7fffffff || Cout > 0x7fffffff || T <= 0 || B <= 0 || H <= 0 || W <= 0 ||
+        Cout <= 0 || splits < 1 || splits > 8)
+        return SNNB_ERR_ARG;
+    const int64_t need = snnb_split_workspace_bytes(T, B, H, W, Cout, splits);
+    if (need > SNNB_STATIC_SCRATCH_BYTES) return SNNB_ERR_ARG;   // exceeds the fixed scratch
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (dev < 0 || dev >= 64) return SNNB_ERR_UNSUPPORTED;
+    void* scratch = nullptr;
+    {
+        // first call on this device: resolve the array's device address (device current)
+        std::lock_guard<std::mutex> guard(g_static_scratch_lock);
+        if (!g_static_scratch_ptr[dev]) {
+            void* ptr = nullptr;
+            e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+            if (e != cudaSuccess) return record_cuda_error(e);
+            g_static_scratch_ptr[dev] = ptr;
+        }
+        scratch = g_static_scratch_ptr[dev];
+    }
+    // Every element of the partial sums that is read was first written by this call, so
+    // nothing in the scratch has to start at zero.
+    return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout, 9,
+                        decay, input_scale, v_threshold, v_reset, hard_reset, pool,
+                        splits > 1 ? 2 : 0, block_n, splits, scratch, need > 0 ? need : 0, out,
+                        static_cast<cudaStream_t>(stream));
 }

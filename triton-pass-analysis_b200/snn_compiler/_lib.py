@@ -38,6 +38,8 @@ SIGNATURES = {
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
                             P],
     "snnb_read_device_status": [P, P],
+    "snnb_conv3x3_lif_static_scratch": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32,
+                                        I32, I32, I32, P, P],
 }
 
 _lib = None
