@@ -465,6 +465,98 @@ class ConvLayerWorkload:
         OV.conv_bn_lif_pool(s["x"], s["w"], s["b"], pool=True)
         return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
 
+
+class AttnWorkload:
+    """Spiking self-attention block (config 3): x [T=4, B=32, N=196, D=384] spikes, 12 heads."""
+    name = "attention"
+    flush_l2 = True
+
+    def __init__(self, B=32, T=4, N=196, D=384, H=12):
+        self.B, self.T, self.N, self.D, self.H = B, T, N, D, H
+        M = T * B * N
+        d = D // H
+        self.flops = 2 * M * D * 3 * D + 2 * M * D * D + T * B * H * 4 * N * d * d
+        self.metric = ("spiking self-attention block TFLOP/s (T=4, B=32, N=196, D=384, 12 heads; "
+                       "Q/K/V Linear+BN+LIF, (QK^T)V*0.125 + LIF, proj Linear+BN+LIF)")
+        self.unit = "TFLOP/s"
+        self.dtype = "bf16"
+
+    def config(self):
+        return {"workload": "spike_attention_block_T4_B32_N196_D384", "T": self.T,
+                "batch_per_gpu": self.B, "tokens": self.N, "dim": self.D, "heads": self.H,
+                "input": "Bernoulli(0.15) spikes", "weights": "N(0, 0.02) seeded, BN folded, bf16",
+                "l2": "256 MB buffer written before every step"}
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.kernels import conv as KC
+        from snn_compiler.nn.attention import SpikeAttentionBlock, random_attention_params
+        self.world = world
+        self.blk = SpikeAttentionBlock(random_attention_params(1, D=self.D), heads=self.H,
+                                       scale=0.125, qkv_vth=1.0, attn_vth=0.5, out_vth=1.0)
+        g = torch.Generator(device="cuda").manual_seed(11 + rank)
+        self.x = (torch.rand(self.T, self.B, self.N, self.D, device="cuda", generator=g)
+                  < 0.15).to(torch.bfloat16)
+        stages = self.blk.stages(self.x)
+        self.stage_names = [s[0] for s in stages]
+        self.stage_flops = [s[1] for s in stages]
+        self.stage_ms = [KC.time_graph(s[2]) for s in stages]
+        self.dom = max(range(len(stages)), key=lambda i: self.stage_ms[i])
+        self.launches_per_step = 3
+        self._fns = [s[2] for s in stages]
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            for fn in self._fns:
+                fn()
+
+    def step(self):
+        self.graph.replay()
+
+    def kernel_events(self, steps):
+        return None
+
+    def units_per_step(self):
+        return self.flops / 1e12
+
+    def e2e_setup(self):
+        self.hx = self.x.cpu().pin_memory()
+        T, B, N, D = self.x.shape
+        self.hy = torch.empty(T, B * N, D, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.hx.numel() * 2
+        self.d2h = self.hy.numel() * 2
+
+    def e2e_step(self):
+        self.x.copy_(self.hx, non_blocking=True)
+        y = self.blk.forward(self.x)
+        self.hy.copy_(y.view(self.hy.shape), non_blocking=True)
+
+    def e2e_units(self):
+        return self.flops / 1e12
+
+    def roofline(self, kernel_ms, peaks):
+        # dominant launch timed alone from its own graph
+        ms = self.stage_ms[self.dom]
+        achieved = self.stage_flops[self.dom] / (ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
+                "kernel": self.stage_names[self.dom], "traffic": None,
+                "per_stage_device_ms": {n: round(m, 4) for n, m in
+                                        zip(self.stage_names, self.stage_ms)},
+                "block_ms": round(kernel_ms, 4)}
+
+    def cpu_sample(self):
+        from oracle import params as OP
+        B = 2
+        return {"B": B, "x": OP.spikes(0, (self.T, B, self.N, self.D), 0.15),
+                "P": OP.attention_params(1, D=self.D, heads=self.H),
+                "what": "oracle SSA block, torch-CPU f32 linears + C LIF"}
+
+    def cpu_run(self, s, threads):
+        from oracle import attention as OA
+        torch.set_num_threads(threads)
+        OA.ssa_forward(s["x"], s["P"], heads=self.H, qkv_vth=1.0, attn_vth=0.5, out_vth=1.0)
+        return self.flops * s["B"] / self.B / 1e12
+
 # ----------------------------------------------------------------------------------------
 def time_cpu(workload, threads, reps=3):
     s = workload.cpu_sample()
@@ -602,7 +694,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif", "conv"])
+    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif", "conv", "attention"])
     ap.add_argument("--layer", default="512,512,56", help="conv workload: Cin,Cout,H")
     ap.add_argument("--batch", type=int, default=64, help="conv workload batch")
     ap.add_argument("--choice", default=None,
@@ -621,7 +713,7 @@ def main():
             fixed = fixed + (1,)
         wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed)
     else:
-        wl = {"lif": LifWorkload, "vgg16": VggWorkload}[args.workload]()
+        wl = {"lif": LifWorkload, "vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
         if args.workload == "vgg16":
             wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
     wl.world = int(os.environ.get("WORLD_SIZE", "1"))

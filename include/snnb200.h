@@ -130,7 +130,8 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *   FusedConvBNNeuron.forward   snn_compiler/nn/modules.py:347-357 (_conv_bn :324-345)
  *   fused_bias_if_lif           snn_compiler/kernels/fused.py:117-226
  *   VGGSNN pool                 snn_compiler/zoo/vgg.py:56, :100-104 (pool='max')
- * x    : bf16 spikes / activations NHWC [T*B, H, W, Cin] (frame t*B + b), Cin % 64 == 0
+ * x    : bf16 spikes / activations NHWC [T*B, H, W, Cin] (frame t*B + b), Cin % 8 == 0
+ *        (channels are consumed in 64-wide slabs; a partial last slab reads zeros)
  * w    : bf16 folded weights [Cout, 3, 3, Cin] (K-major), Cout % 32 == 0
  * bias : f32 [Cout] folded bias b' (added inside the neuron, fused.py:106-108)
  * out  : bf16 spikes NHWC [T*B, Ho, Wo, Cout], Ho = H/2 and Wo = W/2 when pool != 0
@@ -157,7 +158,7 @@ int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W, 
 /*
  * K1, linear variant: spikes [T*B, K] bf16 @ w [N, K] bf16 + bias -> multi-step LIF ->
  * bf16 spikes [T*B, N].  Replaces FusedLinearNeuron.forward
- * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 64 == 0,
+ * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 8 == 0,
  * N % 32 == 0; variant / block_n as for snnb_conv3x3_lif.
  */
 int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
@@ -221,6 +222,36 @@ int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_t B, int64_
                         int64_t H, int64_t W, const float* w, const float* bias, int64_t Cout,
                         float decay, float input_scale, float v_threshold, float v_reset,
                         int hard_reset, int pool, void* out, snnb_stream_t stream);
+
+/*
+ * Linear layer with a float32 result and no neuron: out[t*B+b, n] = x[t*B+b] @ w[n]^T +
+ * bias[n] for spike (or any bf16) rows x [T*B, K] and bf16 w [N, K]; out f32 [T*B, N].
+ * Replaces the projection Conv1d 1x1 (+ folded BN) that ends the spiking self-attention
+ * block (snn_compiler/nn/attention.py:154-160).  T in {2, 4, 8}, K % 8 == 0, N % 32 == 0.
+ */
+int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                    const float* bias, int64_t N, float* out, snnb_stream_t stream);
+
+/*
+ * K3 -- spiking self-attention core: kv = K^T V (bit-packed AND + popcount), then
+ * a = Q kv and a multi-step neuron on a * scale, v kept across t in registers.
+ * Replaces spike_ktv / spike_ktv_popcount (snn_compiler/kernels/attention.py:177-258),
+ * spike_av_lif (attention.py:107-137) and their use in FusedSpikeAttention.forward
+ * (snn_compiler/nn/attention.py:149-150).  q, k, v: bf16 {0,1} with element (t, b, h, n, i)
+ * at base + t*st + b*sb + h*sh + n*sn + i (a fused [T, B, N, 3D] projection output or
+ * separate [T, B, H, N, d] tensors).  d <= 32, N <= 256, N*d <= 8192 (d % 4 == 0) or
+ * N*d <= 2048.
+ * kv_in  : optional f32 [T, B, H, d, d]; when given, K and V are not read.
+ * kv_out : optional f32 [T, B, H, d, d] (K^T V as float).
+ * out    : bf16 spikes at out + t*ot + b*ob + h*oh + n*on + j, or NULL (kv only).
+ * Neuron: v = decay*v + input_scale*(a*scale); s = v >= v_threshold; reset.
+ */
+int snnb_spike_attention_core(const void* q, const void* k, const void* v, int64_t st,
+                              int64_t sb, int64_t sh, int64_t sn, const float* kv_in,
+                              float* kv_out, void* out, int64_t ot, int64_t ob, int64_t oh,
+                              int64_t on, int64_t T, int64_t B, int64_t H, int64_t N, int64_t d,
+                              float decay, float input_scale, float scale, float v_threshold,
+                              float v_reset, int hard_reset, snnb_stream_t stream);
 
 /*
  * Reads and clears the device status word that kernels with bounded waits write

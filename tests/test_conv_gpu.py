@@ -66,6 +66,8 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
     (4, 2, 64, 64, 56),     # config-2 spatial size: partial pixel blocks at the edges
     (4, 3, 64, 64, 14),
     (2, 5, 64, 128, 7),     # odd size: no pooling
+    (4, 2, 48, 64, 8),      # partial 64-channel slab (zero-filled by the TMA)
+    (4, 4, 96, 64, 4),
 ]
 
 
@@ -179,7 +181,7 @@ def test_first_conv_lif_against_oracle(static, pool):
 
 def test_bad_geometry_is_rejected():
     C = _C()
-    x = torch.zeros(4, 1, 8, 8, 48, device=DEV, dtype=torch.bfloat16)     # Cin % 64 != 0
-    w = torch.zeros(64, 3, 3, 48, device=DEV, dtype=torch.bfloat16)
+    x = torch.zeros(4, 1, 8, 8, 20, device=DEV, dtype=torch.bfloat16)     # Cin % 8 != 0
+    w = torch.zeros(64, 3, 3, 20, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError):
         C.conv3x3_lif(x, w, torch.zeros(64, device=DEV))

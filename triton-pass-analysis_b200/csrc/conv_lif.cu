@@ -199,8 +199,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
                         tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
                                         full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
-                        tc::tma_load_2d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
-                                        tap * p.Cin + cb * 64, tl.n0);
+                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
+                                        cb * 64, tap, tl.n0);
                         ++issued;
                         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
@@ -408,8 +408,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
                     tc::tma_load_5d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, full_bar(stage),
                                     cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, tl.img0, 0);
-                    tc::tma_load_2d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
-                                    tap * p.Cin + cb * 64, tl.n0);
+                    tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
+                                    cb * 64, tap, tl.n0);
                     ++issued;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -649,6 +649,7 @@ int launch_splitsum(float* partial, int S, int64_t rows, int C, const float* bia
     const int64_t threads = rows * (C / 8);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     switch (S) {
+        case 1: splitsum_kernel<1><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
         case 2: splitsum_kernel<2><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
         case 3: splitsum_kernel<3><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
         case 4: splitsum_kernel<4><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
@@ -812,7 +813,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s) {
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
-    if (Cin % 64 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
+    if (Cin % 8 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
     if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
@@ -822,7 +823,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (block_n && Cout % block_n) return SNNB_ERR_ARG;
     if (splits < 1) splits = 1;
     if (splits > 8) return SNNB_ERR_UNSUPPORTED;
-    const int KB = taps * (Cin / 64);
+    const int KB = taps * ((Cin + 63) / 64);
     if (splits > KB) return SNNB_ERR_ARG;
     const bool tm_ok = (T == 2 || T == 4 || T == 8);
     if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;
@@ -879,11 +880,11 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                          CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc != SNNB_OK) return rc;
-    // weight map: dims (taps*Cin, Cout), box (64, BN)
-    const uint64_t bdims[2] = {(uint64_t)taps * Cin, (uint64_t)Cout};
-    const uint64_t bstr[1] = {(uint64_t)taps * Cin * 2};
-    const uint32_t bbox[2] = {64, (uint32_t)BN};
-    rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, bdims, bstr, bbox,
+    // weight map: dims (Cin, taps, Cout), box (64, 1, BN): channels past Cin read as zero
+    const uint64_t bdims[3] = {(uint64_t)Cin, (uint64_t)taps, (uint64_t)Cout};
+    const uint64_t bstr[2] = {(uint64_t)Cin * 2, (uint64_t)taps * Cin * 2};
+    const uint32_t bbox[3] = {64, 1, (uint32_t)BN};
+    rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
     ConvParams p;
@@ -891,7 +892,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.bw = bw; p.bh = bh; p.bn = bn;
     p.tiles_w = (W + bw - 1) / bw; p.tiles_h = (H + bh - 1) / bh;
     p.n_tiles_n = Cout / BN;
-    p.taps = taps; p.cin_blocks = Cin / 64; p.pool = pool;
+    p.taps = taps; p.cin_blocks = (Cin + 63) / 64; p.pool = pool;
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.splits = splits;
@@ -955,6 +956,60 @@ extern "C" int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, c
     return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)K, w, bias, (int)N, 1, decay, input_scale,
                         v_threshold, v_reset, hard_reset, 0, variant, block_n, splits, workspace,
                         workspace_bytes, out, static_cast<cudaStream_t>(stream));
+}
+
+// Linear layer with a float32 result (no neuron): out[t*B + b, n] = x[t*B + b] @ w[n]^T + bias[n].
+// Runs the T-folded tensor-core kernel with its raw-accumulator epilogue (one split, the
+// output buffer as the partial-sum array), then adds the bias in place.
+extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                               const float* bias, int64_t N, float* out, snnb_stream_t stream) {
+    if (!x || !w || !bias || !out) return SNNB_ERR_ARG;
+    if (T <= 0 || B <= 0 || K <= 0 || N <= 0) return SNNB_ERR_ARG;
+    if (T > 0x7fffffff || B > 0x7fffffff || K > 0x7fffffff || N > 0x7fffffff) return SNNB_ERR_ARG;
+    if (!(T == 2 || T == 4 || T == 8)) return SNNB_ERR_UNSUPPORTED;
+    if (K % 8 || N % 32) return SNNB_ERR_UNSUPPORTED;
+    if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
+    int* status = device_status_ptr();
+    if (!status) return SNNB_ERR_CUDA;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int iT = (int)T, iB = (int)B, iK = (int)K, iN = (int)N;
+    int bw, bh, bn;
+    if (!choose_block(1, 1, 128 / iT, false, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
+    const int64_t mtiles = (iB + bn - 1) / bn;
+    int BN = (iN % 128 == 0) ? 128 : (iN % 64 == 0 ? 64 : 32);
+    while (BN > 32 && mtiles * (iN / BN) < 148) BN /= 2;
+    CUtensorMap ta, tb;
+    const uint64_t adims[5] = {(uint64_t)K, 1, 1, (uint64_t)B, (uint64_t)T};
+    const uint64_t astr[4] = {(uint64_t)K * 2, (uint64_t)K * 2, (uint64_t)K * 2,
+                              (uint64_t)B * K * 2};
+    const uint32_t abox[5] = {64, 1, 1, (uint32_t)bn, (uint32_t)T};
+    int rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, x, adims, astr, abox,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SNNB_OK) return rc;
+    const uint64_t bdims[3] = {(uint64_t)K, 1, (uint64_t)N};
+    const uint64_t bstr[2] = {(uint64_t)K * 2, (uint64_t)K * 2};
+    const uint32_t bbox[3] = {64, 1, (uint32_t)BN};
+    rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SNNB_OK) return rc;
+    ConvParams p;
+    p.T = iT; p.B = iB; p.H = 1; p.W = 1; p.Cin = iK; p.Cout = iN;
+    p.bw = bw; p.bh = bh; p.bn = bn;
+    p.tiles_w = 1; p.tiles_h = 1;
+    p.n_tiles_n = iN / BN;
+    p.taps = 1; p.cin_blocks = (iK + 63) / 64; p.pool = 0;
+    p.df = 0.f; p.sc = 0.f; p.thr = 0.f; p.v_reset = 0.f; p.hard = 1;
+    p.bias = bias; p.out = nullptr; p.status = status;
+    p.splits = 1;
+    p.partial = out;
+    p.num_tiles = (int)(mtiles * p.n_tiles_n);
+    switch (iT) {
+        case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s); break;
+        case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s); break;
+        default: rc = launch_tm_bn<8>(BN, ta, tb, p, s); break;
+    }
+    if (rc != SNNB_OK) return rc;
+    return launch_splitsum(out, 1, (int64_t)T * B, iN, bias, s);
 }
 
 extern "C" int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W,

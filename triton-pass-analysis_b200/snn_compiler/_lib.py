@@ -38,6 +38,9 @@ SIGNATURES = {
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
                             P],
     "snnb_read_device_status": [P, P],
+    "snnb_linear_f32": [P, I64, I64, I64, P, P, I64, P, P],
+    "snnb_spike_attention_core": [P, P, P, I64, I64, I64, I64, P, P, P, I64, I64, I64, I64,
+                                  I64, I64, I64, I64, I64, F, F, F, F, F, I32, P],
     "snnb_conv3x3_lif_static_scratch": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32,
                                         I32, I32, I32, P, P],
 }

@@ -92,6 +92,22 @@ def _workspace(ws, splits, T, B, H, W, Cout, device):
     return ws, ws.numel() * ws.element_size()
 
 
+def linear_f32(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, B, K] bf16 @ w[N, K]^T + bias -> float32 [T, B, N] (no neuron); T in {2,4,8}."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
+    T, B, K = x.shape
+    N = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.numel() == N
+    if out is None:
+        out = torch.empty(T, B, N, device=x.device, dtype=torch.float32)
+    st = _lib.lib().snnb_linear_f32(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N,
+                                    _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_linear_f32")
+    return out
+
+
 def linear_mean(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
     """mean over T of (x[t] @ w^T + bias): x [T, B, K] bf16 -> f32 [B, N] (N <= 64)."""

@@ -1,6 +1,9 @@
 """nn.Module API (reference snn_compiler/nn/__init__.py)."""
 from .modules import (IFNode, LIFNode, PLIFNode, FusedAddNeuron, RateCodedIFNode,
                       RateCodedLIFNode, StatefulLIFNode)
+from .attention import (FusedSpikeAttention, SpikeAttentionBlock, is_spiking_self_attention,
+                        is_ms_attention, is_spiking_attention)
 
 __all__ = ["IFNode", "LIFNode", "PLIFNode", "FusedAddNeuron", "RateCodedIFNode",
-           "RateCodedLIFNode", "StatefulLIFNode"]
+           "RateCodedLIFNode", "StatefulLIFNode", "FusedSpikeAttention", "SpikeAttentionBlock",
+           "is_spiking_self_attention", "is_ms_attention", "is_spiking_attention"]
