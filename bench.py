@@ -162,14 +162,14 @@ class LifWorkload:
     def __init__(self, T=32, N=1 << 27):
         self.T, self.N = T, N
         self.bytes_per_step = 4 * T * N + 4 * T * N + T * N // 8 + 4 * N
-        self.metric = "LIF kernel HBM GB/s (T=32, N=2^27, fp32 spikes + packed + final v)"
+        self.metric = f"LIF kernel HBM GB/s (T={T}, N={N}, fp32 spikes + packed + final v)"
         self.unit = "GB/s"
         self.dtype = "f32"
 
     def config(self):
-        return {"workload": "lif_sweep_T32_N2^27", "T": self.T, "N": self.N,
+        return {"workload": f"lif_sweep_T{self.T}_N{self.N}", "T": self.T, "N": self.N,
                 "outputs": "fp32 spikes + packed spikes + final v",
-                "l2": "inputs larger than L2 (16 GiB per step)"}
+                "l2": f"inputs larger than L2 ({4 * self.T * self.N / 2**30:.2f} GiB per step)"}
 
     def setup(self, rank, world, dist=None):
         self.world = world
@@ -557,6 +557,89 @@ class AttnWorkload:
         OA.ssa_forward(s["x"], s["P"], heads=self.H, qkv_vth=1.0, attn_vth=0.5, out_vth=1.0)
         return self.flops * s["B"] / self.B / 1e12
 
+
+class BgemmWorkload:
+    """Bit-packed {0,1} x {-1,+1} GEMM (config 4): A Bernoulli(0.2) [M, K], B +-1 [K, N]."""
+    name = "bgemm"
+    flush_l2 = True
+
+    def __init__(self, M=16384, K=8192, N=8192):
+        self.M, self.K, self.N = M, K, N
+        w = (K + 31) // 32
+        self.bytes = 4 * w * (M + N) + 4 * M * N          # packed A + packed B + int32 C
+        self.word_ops = M * N * w
+        self.metric = f"binary GEMM (AND+popcount) GB/s, M={M} K={K} N={N}"
+        self.unit = "GB/s"
+        self.dtype = "u32"
+
+    def config(self):
+        return {"workload": f"bgemm_{self.M}x{self.K}x{self.N}", "M": self.M, "K": self.K,
+                "N": self.N, "A": "Bernoulli(0.2) {0,1}", "B": "+-1 p=0.5",
+                "bytes_per_step": self.bytes, "word_ops_per_step": self.word_ops,
+                "l2": "256 MB buffer written before every step"}
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.kernels import binary as KB
+        self.KB = KB
+        self.world = world
+        g = torch.Generator(device="cuda").manual_seed(3 + rank)
+        A = (torch.rand(self.M, self.K, device="cuda", generator=g) < 0.2).to(torch.uint8)
+        Bt = (torch.rand(self.N, self.K, device="cuda", generator=g) < 0.5).to(torch.uint8)
+        self.Ap, self.Bp = KB.bitpack(A), KB.bitpack(Bt)
+        self.C = torch.empty(self.M, self.N, device="cuda", dtype=torch.int32)
+        del A, Bt
+        self.launches_per_step = 1
+
+    def step(self):
+        self.KB.bgemm(self.Ap, self.Bp, self.K, mode=1, out=self.C)
+
+    def kernel_events(self, steps):
+        return None
+
+    def units_per_step(self):
+        return self.bytes / 1e9
+
+    def e2e_setup(self):
+        self.hA, self.hB = self.Ap.cpu().pin_memory(), self.Bp.cpu().pin_memory()
+        self.hC = torch.empty(self.C.shape, dtype=torch.int32).pin_memory()
+        self.h2d = (self.hA.numel() + self.hB.numel()) * 4
+        self.d2h = self.hC.numel() * 4
+
+    def e2e_step(self):
+        self.Ap.copy_(self.hA, non_blocking=True)
+        self.Bp.copy_(self.hB, non_blocking=True)
+        self.step()
+        self.hC.copy_(self.C, non_blocking=True)
+
+    def e2e_units(self):
+        return self.bytes / 1e9
+
+    def roofline(self, kernel_ms, peaks):
+        # the AND+popcount contraction is bound by the integer popcount pipe, not HBM:
+        # report the HBM fraction as asked, and the word-op rate next to it
+        achieved = self.bytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"], "kernel": "bgemm_kernel<1>", "traffic": None,
+                "popc_word_ops_per_s": round(self.word_ops / (kernel_ms * 1e-3), 1),
+                "note": "compute-bound on the popcount pipe; the HBM fraction is not the limit"}
+
+    def cpu_sample(self):
+        from oracle import params as OP
+        M = 64
+        A, Bb = OP.binary_gemm_operands(4, M, self.K, self.N)
+        return {"M": M, "A": A.numpy().astype("int8"), "B": (Bb.numpy().astype("int8") * 2 - 1),
+                "what": "oracle unpacked integer matmul (numpy, int64 accumulate) on 64 rows"}
+
+    def cpu_run(self, s, threads):
+        import numpy as np
+        torch.set_num_threads(threads)
+        a = torch.from_numpy(s["A"].astype(np.float32))
+        b = torch.from_numpy(s["B"].astype(np.float32))
+        torch.matmul(a, b)                   # exact: |sums| < 2^24
+        w = (self.K + 31) // 32
+        return (4 * w * (s["M"] + self.N) + 4 * s["M"] * self.N) / 1e9
+
 # ----------------------------------------------------------------------------------------
 def time_cpu(workload, threads, reps=3):
     s = workload.cpu_sample()
@@ -694,7 +777,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="vgg16", choices=["vgg16", "lif", "conv", "attention"])
+    ap.add_argument("--workload", default="vgg16",
+                    choices=["vgg16", "lif", "conv", "attention", "bgemm"])
+    ap.add_argument("--lif-shape", default="32,134217728", help="lif workload: T,N")
+    ap.add_argument("--gemm-shape", default="16384,8192,8192", help="bgemm workload: M,K,N")
     ap.add_argument("--layer", default="512,512,56", help="conv workload: Cin,Cout,H")
     ap.add_argument("--batch", type=int, default=64, help="conv workload batch")
     ap.add_argument("--choice", default=None,
@@ -713,7 +799,14 @@ def main():
             fixed = fixed + (1,)
         wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed)
     else:
-        wl = {"lif": LifWorkload, "vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
+        if args.workload == "lif":
+            lt, ln = (int(v) for v in args.lif_shape.split(","))
+            wl = LifWorkload(T=lt, N=ln)
+        elif args.workload == "bgemm":
+            gm, gk, gn = (int(v) for v in args.gemm_shape.split(","))
+            wl = BgemmWorkload(gm, gk, gn)
+        else:
+            wl = {"vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
         if args.workload == "vgg16":
             wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
     wl.world = int(os.environ.get("WORLD_SIZE", "1"))
