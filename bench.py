@@ -299,7 +299,7 @@ class VggWorkload:
         if self.save_choices and rank == 0:
             json.dump({json.dumps(list(k)): list(v) for k, v in self.eng.choice.items()},
                       open(self.save_choices, "w"))
-        self.launches_per_step = len(steps)
+        self.launches_per_step = self.eng.kernel_launches(self.B)
         self.out = self.eng.capture(self.img, split_at=dom)
         self.dom_graph = 1
         self.gathered = torch.empty(world * self.B, 10, device="cuda") if world > 1 else None

@@ -33,3 +33,31 @@ def test_vggsnn_module_structure_and_params():
     P = m.params_dict()
     assert len(P["convs"]) == 13 and sum(c["pool"] for c in P["convs"]) == 5
     assert [tuple(f["w"].shape) for f in P["fcs"]] == [(4096, 512), (4096, 4096), (10, 4096)]
+
+
+def test_fused_modules_construct_like_reference():
+    """FusedConv(BN)(Add)Neuron / FusedLinearNeuron keep the reference's constructor
+    arguments and parameter layout (snn_compiler/nn/modules.py:160-443); construction
+    needs no GPU."""
+    import torch.nn as nn
+    from oracle import vgg as OV
+    from snn_compiler.nn import (FusedConvBNAddNeuron, FusedConvBNNeuron, FusedConvNeuron,
+                                 FusedLinearNeuron)
+    conv, bn = nn.Conv2d(8, 16, 3, padding=1), nn.BatchNorm2d(16).eval()
+    with torch.no_grad():
+        bn.running_mean.uniform_(-0.1, 0.1)
+        bn.running_var.uniform_(0.5, 1.5)
+    m = FusedConvBNNeuron(conv, bn, neuron="lif", tau=2.0, v_threshold=0.7)
+    w, b = OV.fold_conv_bn(conv.weight.detach(), conv.bias.detach(), bn.weight.detach(),
+                           bn.bias.detach(), bn.running_mean, bn.running_var, bn.eps)
+    assert torch.equal(m.weight.detach(), w) and torch.equal(m.bias.detach(), b)
+    assert m.v_threshold == 0.7 and m.fold_bn and m.layout == "NCHW"
+    u = FusedConvBNNeuron(conv, bn, fold_bn=False)
+    assert u.bias is None and torch.equal(u.bn_var, bn.running_var)
+    assert set(dict(u.named_parameters())) == {"weight", "conv_bias"}
+    a = FusedConvBNAddNeuron(conv, bn, v_threshold=torch.ones(16))
+    assert a.v_threshold.shape == (16,)
+    c = FusedConvNeuron(8, 16, 3, stride=2, padding=1, bias=False)
+    assert c.bias is None and c.stride == (2, 2)
+    lin = FusedLinearNeuron(32, 64)
+    assert lin.weight.shape == (64, 32) and lin.bias.shape == (64,)

@@ -242,25 +242,43 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
                 neuron: str = "if", tau: float = 2.0, decay=None, decay_input: bool = True,
                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
                 layout: str = "NCHW"):
-    """conv + bias + neuron (reference fused.py:513-551).  The fused kernel covers the
-    spiking-CNN case: 3x3, stride 1, padding 1, dilation 1, groups 1, Cin % 64 == 0."""
-    if tuple(weight.shape[2:]) != (3, 3) or _pair(stride) != (1, 1) or _pair(padding) != (1, 1) \
-            or _pair(dilation) != (1, 1) or groups != 1:
-        raise NotImplementedError("fused conv kernel: 3x3, stride 1, padding 1, groups 1 only")
-    x = _to_frames(x_seq)
-    Cout = weight.shape[0]
+    """conv + bias + neuron (reference fused.py:513-551) for x_seq [T, B, Cin, H, W].
+    3x3 / stride 1 / padding 1 convs with a scalar threshold run one fused launch: the
+    tcgen05 kernel when Cin % 8 == 0 and Cout % 32 == 0 (bf16 operands), the float32
+    CUDA-core kernel for a float32 input with Cin % 8 != 0 (the image layer).  Any other
+    geometry keeps the reference's two steps: torch's conv, then the fused neuron kernel."""
+    from .fused import fused_bias_if_lif
+    Cin, Cout = weight.shape[1], weight.shape[0]
+    kw = dict(neuron=neuron, tau=tau, decay=decay, decay_input=decay_input,
+              soft_reset=soft_reset, v_threshold=v_threshold, v_reset=v_reset)
     b = bias.detach().float().contiguous() if bias is not None else \
-        torch.zeros(Cout, device=x.device)
-    y = conv3x3_lif(x, weight_khwc(weight), b, neuron=neuron, tau=tau, decay=decay,
-                    decay_input=decay_input, soft_reset=soft_reset, v_threshold=v_threshold,
-                    v_reset=v_reset)
-    return _from_frames(y, x_seq.dtype, layout)
+        torch.zeros(Cout, device=x_seq.device)
+    if tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1) and \
+            _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1 and \
+            isinstance(v_threshold, (int, float)):
+        if Cin % 8 == 0 and Cout % 32 == 0:
+            y = conv3x3_lif(_to_frames(x_seq), weight_khwc(weight), b, **kw)
+            return _from_frames(y, x_seq.dtype, layout)
+        if x_seq.dtype == torch.float32 and Cout % 8 == 0:
+            y = first_conv_lif(x_seq.contiguous(), weight.detach().float().contiguous(), b,
+                               T=x_seq.shape[0], **kw)
+            return _from_frames(y, x_seq.dtype, layout)
+    T, B = x_seq.shape[:2]
+    x4 = x_seq.reshape(T * B, *x_seq.shape[2:])
+    x4 = x4.contiguous(memory_format=torch.channels_last) if layout == "NHWC" else x4.contiguous()
+    y = torch.nn.functional.conv2d(x4, weight.to(x4.dtype), None, stride, padding, dilation,
+                                   groups)
+    if layout == "NHWC":
+        y = y.contiguous(memory_format=torch.channels_last)
+    return fused_bias_if_lif(y.view(T, B, *y.shape[1:]), None if bias is None else b,
+                             layout=layout, **kw)
 
 
 def linear_neuron(x_seq, weight, bias, *, neuron: str = "if", tau: float = 2.0, decay=None,
                   decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
                   v_reset: float = 0.0):
-    """linear + bias + neuron (reference fused.py:554-579); in_features % 64 == 0."""
+    """linear + bias + neuron (reference fused.py:554-579); one fused launch (bf16
+    operands, float32 accumulation); in_features % 8 == 0, out_features % 32 == 0."""
     T, B = x_seq.shape[:2]
     x = x_seq.reshape(T, B, -1).to(torch.bfloat16).contiguous()
     N = weight.shape[0]

@@ -104,3 +104,6 @@ def fold_conv_bn(conv_w, conv_b, bn_w, bn_b, bn_mean, bn_var, bn_eps):
         conv_b = torch.zeros_like(bn_w)
     new_b = (conv_b - bn_mean) * inv_std + bn_b
     return new_w, new_b
+
+
+from .conv import conv_bn_neuron, conv_neuron, linear_neuron  # noqa: E402  (conv imports fold_conv_bn)

@@ -1,9 +1,12 @@
 """nn.Module API (reference snn_compiler/nn/__init__.py)."""
 from .modules import (IFNode, LIFNode, PLIFNode, FusedAddNeuron, RateCodedIFNode,
                       RateCodedLIFNode, StatefulLIFNode)
+from .fused_layers import (FusedConvNeuron, FusedLinearNeuron, FusedConvBNNeuron,
+                           FusedConvBNAddNeuron)
 from .attention import (FusedSpikeAttention, SpikeAttentionBlock, is_spiking_self_attention,
                         is_ms_attention, is_spiking_attention)
 
-__all__ = ["IFNode", "LIFNode", "PLIFNode", "FusedAddNeuron", "RateCodedIFNode",
+__all__ = ["IFNode", "LIFNode", "PLIFNode", "FusedAddNeuron", "FusedConvNeuron",
+           "FusedLinearNeuron", "FusedConvBNNeuron", "FusedConvBNAddNeuron", "RateCodedIFNode",
            "RateCodedLIFNode", "StatefulLIFNode", "FusedSpikeAttention", "SpikeAttentionBlock",
            "is_spiking_self_attention", "is_ms_attention", "is_spiking_attention"]

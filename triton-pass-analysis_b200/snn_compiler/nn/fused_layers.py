@@ -1,0 +1,244 @@
+"""Conv / linear + neuron modules, same constructors and forward signatures as the reference.
+
+Mirrors snn_compiler/nn/modules.py of the reference:
+  FusedConvNeuron        :160-217   conv (+ bias) + IF/LIF
+  FusedLinearNeuron      :220-255   linear (+ bias) + IF/LIF
+  FusedConvBNNeuron      :258-357   conv + BN (folded at construction, or kept separate) + IF/LIF
+  FusedConvBNAddNeuron   :360-443   conv + BN + residual add + IF/LIF
+x_seq is [T, B, C, H, W] (logical NCHW; channels-last storage when layout="NHWC") or
+[T, B, features]; the result has the same layout.
+
+Routing (every launch is libsnnb200.so):
+  - 3x3 / stride 1 / padding 1 convs on spike-like input (Cin % 8 == 0, Cout % 32 == 0):
+    one launch of the fused tcgen05 conv + bias + neuron kernel (bf16 operands, float32
+    accumulation -- the reference's bf16 mode);
+  - the same geometry on a float32 input with Cin % 8 != 0 (the image-input first layer):
+    the float32 CUDA-core conv + neuron kernel;
+  - linears with in_features % 8 == 0 and out_features % 32 == 0: the fused linear kernel;
+  - fold_bn=False, the residual form and any other conv geometry keep the reference's own
+    two-step structure: torch's conv (+ eval BN) followed by the fused neuron kernel
+    (snnb_neuron_multistep), exactly as modules.py:324-357 / :415-443 do.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..kernels import conv as KC
+from ..kernels.fused import fold_conv_bn, fused_bias_if_lif
+
+
+def _pair(v):
+    return tuple(v) if isinstance(v, (tuple, list)) else (v, v)
+
+
+def _store_threshold(mod, v_threshold):
+    if isinstance(v_threshold, torch.Tensor):
+        mod.register_buffer("v_threshold", v_threshold.float().contiguous())
+    else:
+        mod.v_threshold = float(v_threshold)
+
+
+class _NeuronArgs:
+    def _set_neuron(self, neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset):
+        self.neuron = neuron
+        self.tau = tau
+        self.decay = decay
+        self.decay_input = decay_input
+        self.soft_reset = soft_reset
+        self.v_reset = v_reset
+        _store_threshold(self, v_threshold)
+
+    def _neuron_kw(self):
+        return dict(neuron=self.neuron, tau=self.tau, decay=self.decay,
+                    decay_input=self.decay_input, soft_reset=self.soft_reset,
+                    v_threshold=self.v_threshold, v_reset=self.v_reset)
+
+
+def _fused_conv_ok(weight, stride, padding, dilation, groups, v_threshold):
+    return (tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1)
+            and _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1
+            and isinstance(v_threshold, (int, float)))
+
+
+def _conv_lif(x_seq, weight, bias, layout, kw, cache):
+    """Fused conv + bias + neuron for a 3x3 / s1 / p1 conv.  `cache` holds the kernel-layout
+    weights so they are converted once per module, not per call."""
+    T, B, Cin = x_seq.shape[:3]
+    Cout = weight.shape[0]
+    b = bias.detach().float().contiguous() if bias is not None else \
+        torch.zeros(Cout, device=x_seq.device)
+    if Cin % 8 == 0 and Cout % 32 == 0:
+        key = ("khwc", weight.data_ptr(), weight._version)
+        if cache.get("key") != key:
+            cache.clear()
+            cache["key"], cache["w"] = key, KC.weight_khwc(weight)
+        y = KC.conv3x3_lif(KC._to_frames(x_seq), cache["w"], b, **kw)
+        return KC._from_frames(y, x_seq.dtype, layout)
+    if x_seq.dtype == torch.float32 and Cout % 8 == 0:
+        w = weight.detach().float().contiguous()
+        y = KC.first_conv_lif(x_seq.contiguous(), w, b, T=T, **kw)
+        return KC._from_frames(y, x_seq.dtype, layout)
+    return None
+
+
+def _torch_conv(x_seq, weight, bias, stride, padding, dilation, groups, layout):
+    """torch conv on [T*B, C, H, W] frames -> y_seq [T, B, Cout, Ho, Wo] (the reference's
+    conv step, modules.py:199-206)."""
+    T, B = x_seq.shape[:2]
+    x4 = x_seq.reshape(T * B, *x_seq.shape[2:])
+    w = weight
+    if layout == "NHWC":
+        x4 = x4.contiguous(memory_format=torch.channels_last)
+        w = weight.to(memory_format=torch.channels_last)
+    else:
+        x4 = x4.contiguous()
+    y = F.conv2d(x4, w.to(x4.dtype), bias=bias, stride=stride, padding=padding,
+                 dilation=dilation, groups=groups)
+    if layout == "NHWC":
+        y = y.contiguous(memory_format=torch.channels_last)
+    return y.view(T, B, *y.shape[1:])
+
+
+class FusedConvNeuron(nn.Module, _NeuronArgs):
+    """Conv2d + (optional) bias + IF/LIF (reference modules.py:160-217)."""
+
+    def __init__(self, in_ch, out_ch, kernel_size, *, stride=1, padding=0, dilation=1,
+                 groups=1, bias: bool = True, neuron: str = "if", tau: float = 2.0,
+                 decay: float | None = None, decay_input: bool = True,
+                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                 layout: str = "NCHW"):
+        super().__init__()
+        conv = nn.Conv2d(in_ch, out_ch, kernel_size, stride=stride, padding=padding,
+                         dilation=dilation, groups=groups, bias=bias)
+        self.weight = nn.Parameter(conv.weight.detach().clone())
+        self.bias = nn.Parameter(conv.bias.detach().clone()) if bias else None
+        self.stride, self.padding = conv.stride, conv.padding
+        self.dilation, self.groups = conv.dilation, conv.groups
+        self.layout = layout
+        self._set_neuron(neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset)
+        self._cache = {}
+
+    def forward(self, x_seq):
+        if _fused_conv_ok(self.weight, self.stride, self.padding, self.dilation, self.groups,
+                          self.v_threshold):
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+                          self._cache)
+            if y is not None:
+                return y
+        y = _torch_conv(x_seq, self.weight, None, self.stride, self.padding, self.dilation,
+                        self.groups, self.layout)
+        b = None if self.bias is None else self.bias.detach().float().contiguous()
+        return fused_bias_if_lif(y, b, layout=self.layout, **self._neuron_kw())
+
+
+class FusedLinearNeuron(nn.Module, _NeuronArgs):
+    """Linear + (optional) bias + IF/LIF (reference modules.py:220-255)."""
+
+    def __init__(self, in_features, out_features, *, bias: bool = True, neuron: str = "if",
+                 tau: float = 2.0, decay: float | None = None, decay_input: bool = True,
+                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0):
+        super().__init__()
+        lin = nn.Linear(in_features, out_features, bias=bias)
+        self.weight = nn.Parameter(lin.weight.detach().clone())
+        self.bias = nn.Parameter(lin.bias.detach().clone()) if bias else None
+        self._set_neuron(neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset)
+
+    def forward(self, x_seq):
+        K, N = self.weight.shape[1], self.weight.shape[0]
+        if K % 8 == 0 and N % 32 == 0 and isinstance(self.v_threshold, (int, float)):
+            return KC.linear_neuron(x_seq, self.weight, self.bias, **self._neuron_kw())
+        T, B = x_seq.shape[:2]
+        y = F.linear(x_seq.reshape(T * B, -1), self.weight.to(x_seq.dtype)).view(T, B, N)
+        b = None if self.bias is None else self.bias.detach().float().contiguous()
+        return fused_bias_if_lif(y, b, layout="NCHW", **self._neuron_kw())
+
+
+class _ConvBNBase(nn.Module, _NeuronArgs):
+    def __init__(self, conv: nn.Conv2d, bn: nn.BatchNorm2d, fold_bn, neuron, tau, decay,
+                 decay_input, soft_reset, v_threshold, v_reset, layout):
+        super().__init__()
+        assert bn.running_mean is not None
+        self.fold_bn = fold_bn
+        if fold_bn:
+            new_w, new_b = fold_conv_bn(conv.weight.detach(),
+                                        conv.bias.detach() if conv.bias is not None else None,
+                                        bn.weight.detach(), bn.bias.detach(),
+                                        bn.running_mean.detach(), bn.running_var.detach(),
+                                        bn.eps)
+            self.weight = nn.Parameter(new_w)
+            self.bias = nn.Parameter(new_b)
+        else:
+            self.weight = nn.Parameter(conv.weight.detach().clone())
+            self.register_parameter(
+                "conv_bias",
+                nn.Parameter(conv.bias.detach().clone()) if conv.bias is not None else None)
+            self.register_buffer("bn_weight", bn.weight.detach().clone())
+            self.register_buffer("bn_bias", bn.bias.detach().clone())
+            self.register_buffer("bn_mean", bn.running_mean.detach().clone())
+            self.register_buffer("bn_var", bn.running_var.detach().clone())
+            self.bn_eps = bn.eps
+            self.bias = None
+        self.stride, self.padding = conv.stride, conv.padding
+        self.dilation, self.groups = conv.dilation, conv.groups
+        self.layout = layout
+        self._set_neuron(neuron, tau, decay, decay_input, soft_reset, v_threshold, v_reset)
+        self._cache = {}
+
+    def _conv_bn(self, x_seq):
+        """(y_seq, neuron bias) through torch's conv (+ eval BN) -- modules.py:324-345."""
+        if self.fold_bn:
+            y = _torch_conv(x_seq, self.weight, None, self.stride, self.padding, self.dilation,
+                            self.groups, self.layout)
+            return y, self.bias.detach().float().contiguous()
+        y = _torch_conv(x_seq, self.weight, self.conv_bias, self.stride, self.padding,
+                        self.dilation, self.groups, self.layout)
+        T, B = y.shape[:2]
+        y4 = F.batch_norm(y.reshape(T * B, *y.shape[2:]), self.bn_mean, self.bn_var,
+                          self.bn_weight, self.bn_bias, training=False, eps=self.bn_eps)
+        if self.layout == "NHWC":
+            y4 = y4.contiguous(memory_format=torch.channels_last)
+        return y4.view(T, B, *y4.shape[1:]), None
+
+
+class FusedConvBNNeuron(_ConvBNBase):
+    """Conv2d + BN + IF/LIF (reference modules.py:258-357).  fold_bn=True folds BN into
+    the conv at construction and runs the fused kernel; fold_bn=False keeps conv and BN as
+    separate ops (bit-identical pre-activation to the unfused network) and fuses only the
+    neuron."""
+
+    def __init__(self, conv: nn.Conv2d, bn: nn.BatchNorm2d, *, fold_bn: bool = True,
+                 neuron: str = "if", tau: float = 2.0, decay: float | None = None,
+                 decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
+                 v_reset: float = 0.0, layout: str = "NCHW"):
+        super().__init__(conv, bn, fold_bn, neuron, tau, decay, decay_input, soft_reset,
+                         v_threshold, v_reset, layout)
+
+    def forward(self, x_seq):
+        if self.fold_bn and _fused_conv_ok(self.weight, self.stride, self.padding,
+                                           self.dilation, self.groups, self.v_threshold):
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+                          self._cache)
+            if y is not None:
+                return y
+        y, b = self._conv_bn(x_seq)
+        return fused_bias_if_lif(y, b, layout=self.layout, **self._neuron_kw())
+
+
+class FusedConvBNAddNeuron(_ConvBNBase):
+    """Conv2d + BN + residual add + IF/LIF (reference modules.py:360-443):
+    spike = neuron(conv_bn(x) + bias + residual), the residual consumed inside the
+    neuron kernel's t loop."""
+
+    def __init__(self, conv: nn.Conv2d, bn: nn.BatchNorm2d, *, fold_bn: bool = True,
+                 neuron: str = "if", tau: float = 2.0, decay: float | None = None,
+                 decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
+                 v_reset: float = 0.0, layout: str = "NCHW"):
+        super().__init__(conv, bn, fold_bn, neuron, tau, decay, decay_input, soft_reset,
+                         v_threshold, v_reset, layout)
+
+    def forward(self, x_seq, residual_seq):
+        y, b = self._conv_bn(x_seq)
+        return fused_bias_if_lif(y, b, residual=residual_seq, layout=self.layout,
+                                 **self._neuron_kw())
