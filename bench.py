@@ -413,7 +413,8 @@ class ConvLayerWorkload:
         # pick the fastest (variant, block_n) the way the VGG engine does
         run = lambda v, bn, sp: KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out,
                                                variant=v, block_n=bn, splits=sp)
-        self.choice = self.fixed if self.fixed else KC.pick_fastest(run, self.cout, T, 9 * C // 64)
+        self.choice = self.fixed if self.fixed else KC.pick_fastest(
+            run, self.cout, T, 9 * C // 64, band=KC.band_block_ns(H, C, self.cout))
         nws = KC.split_workspace_bytes(T, B, H, H, self.cout, self.choice[2])
         self.ws = torch.empty(nws // 4, device="cuda") if nws else None
         self.launches_per_step = 1

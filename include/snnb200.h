@@ -138,9 +138,13 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  * The neuron is v = decay*v + input_scale*(conv + b'); s = v >= v_threshold; reset.
  * variant : 0 = choose; 1 = the CTA walks the T steps of a 128-pixel block with two
  *           TMEM accumulators; 2 = T folded into the 128 accumulator rows (128/T pixels
- *           per CTA, T in {2, 4, 8}) for layers too small to fill the GPU otherwise.
+ *           per CTA, T in {2, 4, 8}) for layers too small to fill the GPU otherwise;
+ *           3 = as 1 on bands of 128/W whole image rows (W in {8, 16, 32, 64}), each
+ *           64-channel slab loaded once per column tap with its halo rows and reused by
+ *           the three row taps, the channel block's weights resident in shared memory
+ *           (9 * ceil(Cin/64) * block_n <= 864; SNNB_ERR_UNSUPPORTED otherwise).
  * block_n : output channels per CTA, 0 = choose, or 32 / 64 / 128 (dividing Cout), or 256
- *           with variant 2.
+ *           with variant 2; 32 / 64 with variant 3.
  * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32
  *           partial sums go to `workspace` (caller-owned, >= snnb_split_workspace_bytes,
  *           16-byte aligned) and a second kernel adds them in a fixed order, adds the bias

@@ -72,7 +72,7 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
 
 
 VARIANTS = [(0, 0, 1), (1, 32, 1), (1, 128, 1), (2, 32, 1), (2, 64, 1), (2, 128, 1), (2, 256, 1),
-            (2, 128, 3), (2, 256, 4)]
+            (2, 128, 3), (2, 256, 4), (3, 32, 1), (3, 64, 1)]
 
 
 @pytest.mark.parametrize("vb", VARIANTS)
@@ -87,6 +87,12 @@ def test_conv3x3_lif_against_oracle(geom, vb):
     if variant == 2 and T not in (2, 4, 8):
         pytest.skip("T folding needs T in {2, 4, 8}")
     C = _C()
+    if variant == 3 and block_n not in C.band_block_ns(H, Cin, Cout):
+        x = torch.zeros(T, B, H, H, Cin, device=DEV, dtype=torch.bfloat16)
+        with pytest.raises(RuntimeError):
+            C.conv3x3_lif(x, torch.zeros(Cout, 3, 3, Cin, device=DEV, dtype=torch.bfloat16),
+                          torch.zeros(Cout, device=DEV), variant=3, block_n=block_n)
+        return
     x, w, b = _layer_case(T, B, Cin, Cout, H, 0.15, sum(geom) * 31 + Cout, False)
     xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
     wd = C.weight_khwc(w).to(DEV)

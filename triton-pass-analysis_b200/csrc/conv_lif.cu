@@ -55,6 +55,8 @@ struct ConvParams {
     int* status;
     int splits;                   // k-range splits (T-folded kernel); 1 = none
     float* partial;               // split-K: f32 partial sums [splits][T][B*H*W][Cout]
+    int mtiles;                   // pixel tiles per channel block (band kernel)
+    int ring, a_bytes, w_bytes;   // band kernel: A ring depth, bytes per A stage, weight bytes
 };
 
 struct Tile {
@@ -258,7 +260,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             for (int j = 0; j < BN; ++j) v[j] = 0.0f;
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
-                if (!tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status)) {
+                const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
+                if (tc::named_bar_any(1, 128, !got)) {
                     ok = false;
                     break;
                 }
@@ -457,7 +460,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
             const Tile tl = decode_tile(item / splits, p, BN);
             const int a = it & 1;
-            if (!tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status)) break;
+            const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
+            if (tc::named_bar_any(1, 128, !got)) break;
             tc::tc_fence_after();
             if (p.partial) {
                 // ---- split-K: raw float32 partial sums of this split
@@ -531,6 +535,262 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::named_bar_sync(1, 128);
             for (int i = et; i < TS * NCH * P; i += 128) smask[i] = 0u;
             tc::named_bar_sync(1, 128);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ---- variant 3: row bands, halo reuse, resident weights ------------------------------------
+// For 3x3 layers whose width W divides 128 (W in 8..64): a tile is a band of bh = 128 / W
+// whole rows of one image, walked over t as in variant 1 (two TMEM accumulators, v in the
+// epilogue's registers).  Per (step, 64-channel slab) the producer loads the band plus one
+// halo row above and below three times, shifted by one column each (dx = 0, 1, 2; columns
+// outside the image read zeros).  The 128-row A operand of tap (dy, dx) is copy dx from
+// row dy*W on -- an offset of dy*W*128 bytes, a multiple of the 1024-byte swizzle atom --
+// so one load serves the three taps of a column: 3 loads of (bh+2)*W rows per slab
+// instead of 9 loads of 128 rows.  The weights of the CTA's channel block (9 taps x Cin x
+// BN, <= 108 KB) stay in shared memory; tiles are ordered channel-block-major so a CTA
+// reloads them only when its next tile belongs to another block.  Weight slab (cb, dx)
+// holds taps dy = 0..2 as [dy][BN rows][64 channels].
+constexpr int BAND_MAX_STAGES = 8;
+
+template <int BN>
+struct SmemBand {
+    static constexpr int MASK_BYTES = (BN / 32) * 128 * 4;
+    static constexpr int NBARS = 2 * BAND_MAX_STAGES + 6;
+    // layout (runtime sizes): weights [w_bytes] | A ring [ring x a_bytes] | masks | barriers |
+    // TMEM slot | abort flag
+    static int dyn_bytes(int w_bytes, int ring, int a_bytes) {
+        return w_bytes + ring * a_bytes + MASK_BYTES + NBARS * 8 + 8 + 1024;
+    }
+};
+
+__device__ __forceinline__ Tile decode_band(int tile, const ConvParams& p, int BN) {
+    const int nb = tile / p.mtiles;
+    const int mt = tile - nb * p.mtiles;
+    const int img = mt / p.tiles_h;
+    const int band = mt - img * p.tiles_h;
+    return Tile{0, band * p.bh, img, nb * BN};
+}
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const ConvParams p) {
+    using S = SmemBand<BN>;
+    constexpr int NCH = BN / 32;
+    constexpr uint32_t TAP_BYTES = BN * 128;
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = tc::smem_u32(smem);
+    const int nst = p.ring;
+    const uint32_t a_off = (uint32_t)p.w_bytes;
+    const uint32_t a_bytes = (uint32_t)p.a_bytes;
+    const uint32_t mask_off = a_off + (uint32_t)nst * a_bytes;
+    uint32_t* smask = reinterpret_cast<uint32_t*>(smem + mask_off);
+    const uint32_t bar_off = mask_off + S::MASK_BYTES;
+    const uint32_t bar0 = sbase + bar_off;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (BAND_MAX_STAGES + s); };
+    auto accf_bar = [&](int a) { return bar0 + 8u * (2 * BAND_MAX_STAGES + a); };
+    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * BAND_MAX_STAGES + 2 + a); };
+    const uint32_t wfull_bar = bar0 + 8u * (2 * BAND_MAX_STAGES + 4);
+    const uint32_t wempty_bar = bar0 + 8u * (2 * BAND_MAX_STAGES + 5);
+    const uint32_t tmem_off = bar_off + S::NBARS * 8;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + tmem_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + tmem_off + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int CB = p.cin_blocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < nst; ++s) {
+            tc::mbar_init(full_bar(s), 1);
+            tc::mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            tc::mbar_init(accf_bar(a), 1);
+            tc::mbar_init(acce_bar(a), 128);
+        }
+        tc::mbar_init(wfull_bar, 1);
+        tc::mbar_init(wempty_bar, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmA);
+        tc::prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(sbase + tmem_off, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int stage = 0, issued = 0, cur_nb = -1;
+            uint32_t phase = 0, wloads = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const Tile tl = decode_band(tile, p, BN);
+                const int nb = tile / p.mtiles;
+                if (nb != cur_nb) {
+                    // the previous block's weights are free once every MMA reading them is done
+                    if (wloads > 0 &&
+                        !tc::mbar_wait(wempty_bar, (wloads - 1) & 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_expect_tx(wfull_bar, (uint32_t)p.w_bytes);
+                    for (int cb = 0; cb < CB; ++cb)
+                        for (int dx = 0; dx < 3; ++dx)
+                            for (int dy = 0; dy < 3; ++dy)
+                                tc::tma_load_3d(
+                                    sbase + (uint32_t)((cb * 3 + dx) * 3 + dy) * TAP_BYTES, &tmB,
+                                    wfull_bar, cb * 64, dy * 3 + dx, tl.n0);
+                    ++wloads;
+                    cur_nb = nb;
+                }
+                for (int t = 0; t < p.T && ok; ++t) {
+                    const int f = t * p.B + tl.img0;
+                    for (int cb = 0; cb < CB && ok; ++cb) {
+                        for (int dx = 0; dx < 3; ++dx) {
+                            if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
+                                ok = false;
+                                break;
+                            }
+                            tc::mbar_expect_tx(full_bar(stage), a_bytes);
+                            tc::tma_load_4d(sbase + a_off + (uint32_t)stage * a_bytes, &tmA,
+                                            full_bar(stage), cb * 64, dx - 1, tl.h0 - 1, f);
+                            ++issued;
+                            if (++stage == nst) { stage = 0; phase ^= 1u; }
+                        }
+                    }
+                }
+            }
+            if (!ok) {
+                drain_ring(bar0, nst, stage, phase, issued);
+                if (wloads > 0) {
+                    const long long t0 = clock64();
+                    while (!tc::mbar_try_wait(wfull_bar, (wloads - 1) & 1u) &&
+                           clock64() - t0 < tc::WAIT_LIMIT_CYCLES) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+            const uint32_t row_step = (uint32_t)p.W * 128u;     // one image row of the band copy
+            int stage = 0, cur_nb = -1;
+            uint32_t phase = 0, it = 0, wl = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const int nb = tile / p.mtiles;
+                if (nb != cur_nb) {
+                    if (wl > 0) tc::umma_commit(wempty_bar);
+                    if (!tc::mbar_wait(wfull_bar, wl & 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    ++wl;
+                    cur_nb = nb;
+                }
+                for (int t = 0; t < p.T && ok; ++t, ++it) {
+                    const int a = it & 1;
+                    if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t dcol = tmem + a * BN;
+                    for (int cb = 0; cb < CB && ok; ++cb) {
+                        for (int dx = 0; dx < 3; ++dx) {
+                            if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
+                                ok = false;
+                                break;
+                            }
+                            tc::tc_fence_after();
+                            const uint32_t abase = sbase + a_off + (uint32_t)stage * a_bytes;
+                            const uint32_t wbase = sbase + (uint32_t)((cb * 3 + dx) * 3) * TAP_BYTES;
+#pragma unroll
+                            for (int dy = 0; dy < 3; ++dy) {
+                                const uint64_t da = tc::sdesc_k_sw128(abase + dy * row_step);
+                                const uint64_t db = tc::sdesc_k_sw128(wbase + dy * TAP_BYTES);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
+                                                  (cb | dx | dy | k) != 0);
+                            }
+                            tc::umma_commit(empty_bar(stage));
+                            if (++stage == nst) { stage = 0; phase ^= 1u; }
+                        }
+                    }
+                    if (ok) tc::umma_commit(accf_bar(a));
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int m = 32 * q + lane;
+        const int et = threadIdx.x - 64;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+            const Tile tl = decode_band(tile, p, BN);
+            const float* bias = p.bias + tl.n0;
+            float v[BN];
+#pragma unroll
+            for (int j = 0; j < BN; ++j) v[j] = 0.0f;
+            for (int t = 0; t < p.T; ++t, ++it) {
+                const int a = it & 1;
+                const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
+                if (tc::named_bar_any(1, 128, !got)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    float r[32];
+                    tc::tmem_ld32(tbase + c * 32, r);
+                    tc::tmem_wait_ld();
+                    uint32_t mask = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float in = __fadd_rn(r[j], __ldg(bias + c * 32 + j));
+                        float vv = charge(v[c * 32 + j], p.df, p.sc, in);
+                        const bool s = vv >= p.thr;
+                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                        v[c * 32 + j] = vv;
+                        mask |= (s ? 1u : 0u) << j;
+                    }
+                    smask[c * 128 + m] = mask;
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(acce_bar(a));
+                tc::named_bar_sync(1, 128);
+                const int npix = p.pool ? 32 : 128;
+                for (int item = et; item < npix * NCH; item += 128) {
+                    const int pix = item / NCH, c = item - pix * NCH;
+                    store_spikes(p, tl, t, c, pix, [&](int mm) { return smask[c * 128 + mm]; });
+                }
+                tc::named_bar_sync(1, 128);
+            }
         }
     }
     tc::tc_fence_before();
@@ -801,9 +1061,86 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 
 namespace {
 
+// ---- variant 3 host path -----------------------------------------------------------------
+constexpr int BAND_W_MAX = 108 * 1024;          // resident weights per CTA
+
+int smem_optin() {
+    static int v[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 227 * 1024;
+    if (!v[dev]) {
+        int x = 0;
+        if (cudaDeviceGetAttribute(&x, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            x <= 0)
+            x = 227 * 1024;
+        v[dev] = x;
+    }
+    return v[dev];
+}
+
+// Channel-block width for the band kernel, or 0 if the layer does not qualify.
+int band_block_n(int W, int Cin, int Cout, int block_n) {
+    if (!(W == 8 || W == 16 || W == 32 || W == 64)) return 0;
+    const int CB = (Cin + 63) / 64;
+    auto fits = [&](int bn) { return Cout % bn == 0 && 9 * CB * bn * 128 <= BAND_W_MAX; };
+    if (block_n) return (block_n == 32 || block_n == 64) && fits(block_n) ? block_n : 0;
+    if (fits(64)) return 64;
+    return fits(32) ? 32 : 0;
+}
+
+int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
+                   const float* bias, int Cout, int BN, float df, float sc, float thr,
+                   float v_reset, int hard, int pool, void* out, int* status, cudaStream_t s) {
+    const int bh = 128 / W;
+    if (pool && (bh % 2)) return SNNB_ERR_UNSUPPORTED;
+    const int CB = (Cin + 63) / 64;
+    const int a_bytes = (bh + 2) * W * 128;
+    const int w_bytes = 9 * CB * BN * 128;
+    const int fixed = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, 0, a_bytes)
+                               : SmemBand<32>::dyn_bytes(w_bytes, 0, a_bytes);
+    int ring = (smem_optin() - fixed) / a_bytes;
+    if (ring > BAND_MAX_STAGES) ring = BAND_MAX_STAGES;
+    if (ring < 2) return SNNB_ERR_UNSUPPORTED;
+    // activation map: dims (Cin, W, H, T*B), box (64, W, bh + 2, 1): the band and its halo
+    CUtensorMap ta, tb;
+    const uint64_t adims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)T * B};
+    const uint64_t astr[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
+    const uint32_t abox[4] = {64, (uint32_t)W, (uint32_t)(bh + 2), 1};
+    int rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, adims, astr, abox,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SNNB_OK) return rc;
+    // weight map: dims (Cin, 9 taps, Cout), box (64, 1, BN): one tap's slab of the block
+    const uint64_t bdims[3] = {(uint64_t)Cin, 9, (uint64_t)Cout};
+    const uint64_t bstr[2] = {(uint64_t)Cin * 2, (uint64_t)9 * Cin * 2};
+    const uint32_t bbox[3] = {64, 1, (uint32_t)BN};
+    rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SNNB_OK) return rc;
+    ConvParams p;
+    p.T = T; p.B = B; p.H = H; p.W = W; p.Cin = Cin; p.Cout = Cout;
+    p.bw = W; p.bh = bh; p.bn = 1;
+    p.tiles_w = 1; p.tiles_h = (H + bh - 1) / bh;
+    p.n_tiles_n = Cout / BN;
+    p.mtiles = B * p.tiles_h;
+    const int64_t ntiles = (int64_t)p.mtiles * p.n_tiles_n;
+    if (ntiles > 0x7fffffff) return SNNB_ERR_ARG;
+    p.num_tiles = (int)ntiles;
+    p.taps = 9; p.cin_blocks = CB; p.pool = pool;
+    p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
+    p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
+    p.splits = 1; p.partial = nullptr;
+    p.ring = ring; p.a_bytes = a_bytes; p.w_bytes = w_bytes;
+    if (BN == 64)
+        return launch_persistent(conv_lif_band_kernel<64>,
+                                 SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes), ta, tb, p, s);
+    return launch_persistent(conv_lif_band_kernel<32>,
+                             SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes), ta, tb, p, s);
+}
+
 // Shared host path of the conv / linear entries.
 // variant: 0 = choose, 1 = T sequential inside the CTA (128-pixel blocks),
-//          2 = T folded into M (128/T-pixel blocks, T in {2, 4, 8}).
+//          2 = T folded into M (128/T-pixel blocks, T in {2, 4, 8}),
+//          3 = row bands with halo reuse and resident weights (W in {8, 16, 32, 64}).
 // block_n: 0 = choose, else 32 / 64 / 128 (/ 256 with variant 2) output channels per CTA.
 // splits : > 1 splits the K range (variant 2 only): partial sums go to `workspace`
 //          ([splits][T][B*H*W][Cout] f32, caller-owned) and reduce_lif_kernel finishes.
@@ -817,7 +1154,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
     if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    if (variant < 0 || variant > 2) return SNNB_ERR_ARG;
+    if (variant < 0 || variant > 3) return SNNB_ERR_ARG;
     if (block_n != 0 && block_n != 32 && block_n != 64 && block_n != 128 && block_n != 256)
         return SNNB_ERR_ARG;
     if (block_n && Cout % block_n) return SNNB_ERR_ARG;
@@ -825,6 +1162,15 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (splits > 8) return SNNB_ERR_UNSUPPORTED;
     const int KB = taps * ((Cin + 63) / 64);
     if (splits > KB) return SNNB_ERR_ARG;
+    if (variant == 3) {
+        if (taps != 9 || splits > 1) return SNNB_ERR_UNSUPPORTED;
+        const int BN3 = band_block_n(W, Cin, Cout, block_n);
+        if (!BN3) return SNNB_ERR_UNSUPPORTED;
+        int* st = device_status_ptr();
+        if (!st) return SNNB_ERR_CUDA;
+        return run_band_layer(x, T, B, H, W, Cin, w, bias, Cout, BN3, df, sc, thr, v_reset, hard,
+                              pool, out, st, s);
+    }
     const bool tm_ok = (T == 2 || T == 4 || T == 8);
     if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;
     if (splits > 1 && (variant == 1 || !tm_ok)) return SNNB_ERR_UNSUPPORTED;

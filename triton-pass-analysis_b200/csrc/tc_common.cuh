@@ -198,6 +198,22 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier with an OR reduction: every one of `threads` threads passes its predicate
+// and all of them get true if any passed true.  Used after bounded waits so that the
+// threads of a role agree on aborting and none is left waiting at a later barrier.
+__device__ __forceinline__ bool named_bar_any(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 }  // namespace tc
 
 // Host: device pointer of this library's status word on the current device

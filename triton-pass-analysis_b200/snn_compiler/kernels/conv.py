@@ -33,7 +33,8 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
                 out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
                 splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool).
-    variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M; block_n: 0 or 32/64/128/256;
+    variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M, 3 row bands with halo reuse
+    and resident weights (band_block_ns); block_n: 0 or 32/64/128/256;
     splits > 1: split-K with float32 partials in `workspace` (allocated here if None)."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1:3] == (3, 3)
@@ -183,8 +184,19 @@ def time_graph(fn, reps: int = 10) -> float:
     return ms
 
 
-def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8):
-    """(variant, block_n, splits) configurations a layer admits."""
+def band_block_ns(W: int, cin: int, cout: int):
+    """Channel-block widths the band kernel (variant 3) accepts for a 3x3 layer: W in
+    {8, 16, 32, 64} and the block's weights (9 * ceil(Cin/64) * block_n rows of 128 bytes)
+    within 108 KB of shared memory."""
+    if W not in (8, 16, 32, 64):
+        return ()
+    cb = (cin + 63) // 64
+    return tuple(bn for bn in (32, 64) if cout % bn == 0 and 9 * cb * bn <= 864)
+
+
+def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=()):
+    """(variant, block_n, splits) configurations a layer admits; `band` lists the
+    block widths of variant 3 the layer qualifies for (band_block_ns)."""
     out = []
     for v in ((1, 2) if T in (2, 4, 8) else (1,)):
         for bn in ((32, 64, 128) if v == 1 else (32, 64, 128, 256)):
@@ -196,14 +208,15 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8):
                 while s <= max_splits and s <= kslabs // 2:
                     out.append((v, bn, s))
                     s *= 2
+    out.extend((3, bn, 1) for bn in band)
     return out
 
 
-def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10):
+def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=()):
     """Time launch(variant, block_n, splits) for every configuration the layer admits
     (on its real operands, device time via time_graph) and return the fastest."""
     best, best_ms = (0, 0, 1), float("inf")
-    for cfg in candidates(cout, T, kslabs):
+    for cfg in candidates(cout, T, kslabs, band=band):
         ms = time_graph(lambda: launch(*cfg), reps)
         if ms < best_ms:
             best, best_ms = cfg, ms

@@ -135,7 +135,8 @@ class SpikingVGG:
                                  KC.conv3x3_lif(x, L["w"], L["b"], pool=L["pool"], out=o,
                                                 variant=v, block_n=bn, splits=sp,
                                                 workspace=self._ws(T, B, hh, ww, L["cout"], sp),
-                                                **self.lif))
+                                                **self.lif),
+                                 band=KC.band_block_ns(w, L["cin"], L["cout"]))
             steps.append((f"conv{i + 1}_{L['cin']}x{L['cout']}@{h}", flops, fn))
             x_prev = bufs[i]
             if L["pool"]:
@@ -168,12 +169,12 @@ class SpikingVGG:
             self._workspace = torch.empty(need // 4, device=self.device, dtype=torch.float32)
         return self._workspace
 
-    def _tuned(self, key, cout, kslabs, launch):
+    def _tuned(self, key, cout, kslabs, launch, band=()):
         """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
         call times every (variant, block_n, splits) the layer admits and keeps the fastest."""
         def run():
             if key not in self.choice:
-                self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs) \
+                self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs, band=band) \
                     if self.autotune else (0, 0, 1)
             return launch(*self.choice[key])
         return run
