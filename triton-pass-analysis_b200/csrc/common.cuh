@@ -41,6 +41,15 @@ __device__ __forceinline__ float charge(float v, float df, float sc, float in) {
     return __fadd_rn(__fmul_rn(df, v), __fmul_rn(sc, in));
 }
 
+// Reset after the threshold test.  A compile-time HARD keeps the per-neuron code free of
+// branches (a run-time choice here was compiled to a branch per neuron and made the LIF
+// epilogues ~3x slower).
+template <bool HARD>
+__device__ __forceinline__ float reset_v(float v, bool s, float thr, float v_reset) {
+    if (HARD) return s ? v_reset : v;
+    return s ? __fsub_rn(v, thr) : v;
+}
+
 // 8 spike bits -> 8 bf16 values (0.0 / 1.0) packed in 16 bytes, bit i -> element i.
 __device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
     uint32_t w[4];

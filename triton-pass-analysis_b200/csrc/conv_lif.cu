@@ -102,37 +102,99 @@ __device__ __forceinline__ void store_spikes(const ConvParams& p, const Tile& tl
     }
 }
 
-// Producer drain after an abort: wait (bounded) for the copies still in flight.
-__device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int stage, uint32_t phase,
-                                           int issued) {
-    for (int k = 0; k < stages && k < issued; ++k) {
+// Producer drain after a failed wait: wait (bounded, whole warp) for the copies still in
+// flight -- the last min(stages, issued) stages before ring position (stage, phase).
+__device__ __forceinline__ void drain_ring_warp(uint32_t bar0, int stages, int stage,
+                                                uint32_t phase, uint32_t issued) {
+    for (uint32_t k = 0; k < (uint32_t)stages && k < issued; ++k) {
         if (--stage < 0) { stage = stages - 1; phase ^= 1u; }
-        const long long t0 = clock64();
-        while (!tc::mbar_try_wait(bar0 + 8u * stage, phase) &&
-               clock64() - t0 < tc::WAIT_LIMIT_CYCLES) {
-        }
+        tc::mbar_wait_warp(bar0 + 8u * stage, phase, 0);
     }
+}
+
+// Spikes of one (step, pixel) of a pixel block, stored by the thread that owns the pixel
+// (TMEM lane m; the block is bn images x bh rows x bw columns, row-major): unpooled, its BN
+// channels as 16-byte stores; pooled, the 2x2 OR formed with shuffles (column pairs are
+// adjacent lanes, row pairs lanes bw apart when bw < 32) or through shared memory (row pair
+// in another warp), stored by the window's top-left thread.  Every epilogue thread calls it
+// (shuffles, barrier); `sm` is this step's half of the double-buffered exchange area.
+template <int NCH>
+__device__ __forceinline__ void store_pixel(const ConvParams& p, const Tile& tl, int t, int m,
+                                            uint32_t (&mk)[NCH], uint32_t* sm) {
+    const int x = m % p.bw, y = (m / p.bw) % p.bh, n = m / (p.bw * p.bh);
+    const int ow = tl.w0 + x, oh = tl.h0 + y, on = tl.img0 + n;
+    const bool inside = ow < p.W && oh < p.H && on < p.B;
+    const int64_t frame = (int64_t)t * p.B + on;
+    if (!p.pool) {
+        if (inside) {
+            uint4* dst = reinterpret_cast<uint4*>(p.out + ((frame * p.H + oh) * p.W + ow) * p.Cout + tl.n0);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+        }
+        return;
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], 1);
+    if (p.bw < 32) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], p.bw);
+    } else {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) sm[c * 128 + m] = mk[c];
+        tc::named_bar_sync(1, 128);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) mk[c] |= sm[c * 128 + (m ^ p.bw)];
+    }
+    if (((x | y) & 1) == 0 && inside) {
+        const int Ho = p.H / 2, Wo = p.W / 2;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + ((frame * Ho + oh / 2) * Wo + ow / 2) * p.Cout + tl.n0);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+    }
+}
+
+// LIF over one 32-column slice of a thread's accumulator row: v = decay*v + scale*(acc + b),
+// threshold, reset; returns the spike bits.
+template <bool HARD>
+__device__ __forceinline__ uint32_t lif_slice(const float (&r)[32], const float* bias, float* v,
+                                              const ConvParams& p) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float in = __fadd_rn(r[j], bias[j]);
+        float vv = charge(v[j], p.df, p.sc, in);
+        const bool s = vv >= p.thr;
+        v[j] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
+        mask |= (s ? 1u : 0u) << j;
+    }
+    return mask;
 }
 
 // ---- variant 1: T sequential inside the CTA ---------------------------------------------
 // Persistent: CTA c handles tiles c, c + gridDim.x, ...  Every (tile, step) is one
 // accumulation into one of two TMEM accumulators used alternately, so the epilogue of
 // step i (LIF + stores) overlaps the MMAs of step i + 1 -- across tile boundaries too.
+// Producer and MMA roles are whole warps that wait together (mbar_wait_warp) and issue
+// from one elected lane; a failed wait follows the protocol of the band kernel below.
 template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_TILE = BN * 128;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * A_TILE_BYTES;
-    static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;          // (BN/32) x 128 u32
-    static constexpr int BAR_OFF = MASK_OFF + (BN / 32) * 128 * 4;
-    static constexpr int NBARS = 2 * STAGES + 4;
+    static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;          // 2 x (BN/32) x 128 u32
+    static constexpr int BAR_OFF = MASK_OFF + 2 * (BN / 32) * 128 * 4;
+    static constexpr int NBARS = 2 * STAGES + 5;
     static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
     static constexpr int ABORT_OFF = TMEM_OFF + 4;
     static constexpr int TOTAL = ABORT_OFF + 4;
     static constexpr int DYN = TOTAL + 1024;     // slack for 1024-byte alignment
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool HARD>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const ConvParams p) {
@@ -148,6 +210,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
 
@@ -165,6 +228,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc::mbar_init(accf_bar(a), 1);
             tc::mbar_init(acce_bar(a), 128);
         }
+        tc::mbar_init(done_bar, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmA);
@@ -181,19 +245,15 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
-        if (lane == 0) {
-            int stage = 0, issued = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const Tile tl = decode_tile(tile, p, BN);
-                for (int t = 0; t < p.T && ok; ++t) {
-                    const int f0 = t * p.B + tl.img0;
-                    for (int kb = 0; kb < KB; ++kb) {
-                        if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
-                            ok = false;
-                            break;
-                        }
+        int stage = 0, istage = 0;
+        uint32_t phase = 0, iphase = 0, issued = 0, failed = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const Tile tl = decode_tile(tile, p, BN);
+            for (int t = 0; t < p.T; ++t) {
+                const int f0 = t * p.B + tl.img0;
+                for (int kb = 0; kb < KB; ++kb) {
+                    failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                    if (!failed && tc::elect_one()) {
                         const int tap = kb / p.cin_blocks;
                         const int cb = kb - tap * p.cin_blocks;
                         const int r = p.taps == 9 ? tap / 3 : 1;
@@ -203,98 +263,89 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                         full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
                                         cb * 64, tap, tl.n0);
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    if (!failed) {
                         ++issued;
-                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        istage = stage;
+                        iphase = phase;
                     }
                 }
             }
-            if (!ok) drain_ring(bar0, STAGES, stage, phase, issued);
+        }
+        if (failed) {
+            drain_ring_warp(bar0, STAGES, istage, iphase, issued);
+            if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t it = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                for (int t = 0; t < p.T && ok; ++t, ++it) {
-                    const int a = it & 1;
-                    if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
+        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+        int stage = 0;
+        uint32_t phase = 0, it = 0, failed = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            for (int t = 0; t < p.T; ++t, ++it) {
+                const int a = it & 1;
+                failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
+                tc::tc_fence_after();
+                const uint32_t dcol = tmem + a * BN;
+                for (int kb = 0; kb < KB; ++kb) {
+                    failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
                     tc::tc_fence_after();
-                    const uint32_t dcol = tmem + a * BN;
-                    for (int kb = 0; kb < KB; ++kb) {
-                        if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
-                            ok = false;
-                            break;
-                        }
-                        tc::tc_fence_after();
+                    if (tc::elect_one()) {
                         const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                         const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)   // 4 x K=16 inside the 128-byte swizzle atom
                             tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
                         tc::umma_commit(empty_bar(stage));
-                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
-                    if (ok) tc::umma_commit(accf_bar(a));
+                    __syncwarp();
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
+                if (tc::elect_one()) tc::umma_commit(accf_bar(a));
+                __syncwarp();
             }
         }
+        if (tc::elect_one()) tc::umma_commit(done_bar);
+        __syncwarp();
+        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         // ------------------------------------------------------------- epilogue
         const int q = warp & 3;                  // TMEM lane quadrant of this warp
         const int m = 32 * q + lane;             // pixel row of the block
-        const int et = threadIdx.x - 64;         // 0..127
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        uint32_t it = 0, failed = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_tile(tile, p, BN);
-            const float* bias = p.bias + tl.n0;
+            const float4* bias4 = reinterpret_cast<const float4*>(p.bias + tl.n0);
             float v[BN];
 #pragma unroll
             for (int j = 0; j < BN; ++j) v[j] = 0.0f;
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
-                const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
-                if (tc::named_bar_any(1, 128, !got)) {
-                    ok = false;
-                    break;
-                }
+                failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
                 tc::tc_fence_after();
                 const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
+                uint32_t mk[NCH];
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
-                    float r[32];
+                    float r[32], bb[32];
                     tc::tmem_ld32(tbase + c * 32, r);
-                    tc::tmem_wait_ld();
-                    uint32_t mask = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float in = __fadd_rn(r[j], __ldg(bias + c * 32 + j));
-                        float vv = charge(v[c * 32 + j], p.df, p.sc, in);
-                        const bool s = vv >= p.thr;
-                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
-                        v[c * 32 + j] = vv;
-                        mask |= (s ? 1u : 0u) << j;
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 b4 = __ldg(bias4 + c * 8 + j);
+                        bb[4 * j] = b4.x; bb[4 * j + 1] = b4.y; bb[4 * j + 2] = b4.z; bb[4 * j + 3] = b4.w;
                     }
-                    smask[c * 128 + m] = mask;
+                    tc::tmem_wait_ld();
+                    mk[c] = lif_slice<HARD>(r, bb, v + c * 32, p);
                 }
                 tc::tc_fence_before();
                 tc::mbar_arrive(acce_bar(a));
-                tc::named_bar_sync(1, 128);
-                const int npix = p.pool ? 32 : 128;
-                for (int item = et; item < npix * NCH; item += 128) {
-                    const int pix = item / NCH, c = item - pix * NCH;
-                    store_spikes(p, tl, t, c, pix, [&](int mm) { return smask[c * 128 + mm]; });
-                }
-                tc::named_bar_sync(1, 128);
+                store_pixel<NCH>(p, tl, t, m, mk, smask + (it & 1) * (NCH * 128));
             }
         }
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -328,14 +379,14 @@ struct SmemTM {
     static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 128 x 33 f32
     static constexpr int MASK_OFF = Y_OFF + 128 * 33 * 4;               // TS x NCH x P u32
     static constexpr int BAR_OFF = (MASK_OFF + TS * NCH * P * 4 + 7) & ~7;
-    static constexpr int NBARS = 2 * STAGES + 4;
+    static constexpr int NBARS = 2 * STAGES + 5;
     static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
     static constexpr int ABORT_OFF = TMEM_OFF + 4;
     static constexpr int TOTAL = ABORT_OFF + 4;
     static constexpr int DYN = TOTAL + 1024;
 };
 
-template <int BN, int STAGES, int TS>
+template <int BN, int STAGES, int TS, bool HARD>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
@@ -352,6 +403,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
 
@@ -375,6 +427,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::mbar_init(accf_bar(a), 1);
             tc::mbar_init(acce_bar(a), 128);
         }
+        tc::mbar_init(done_bar, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmA);
@@ -391,19 +444,16 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {
-            int stage = 0, issued = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-                const Tile tl = decode_tile(item / splits, p, BN);
-                int k0, k1;
-                krange(item % splits, k0, k1);
-                for (int kb = k0; kb < k1; ++kb) {
-                    if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
+        // ------------------------------------------------------------- TMA producer
+        int stage = 0, istage = 0;
+        uint32_t phase = 0, iphase = 0, issued = 0, failed = 0;
+        for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+            const Tile tl = decode_tile(item / splits, p, BN);
+            int k0, k1;
+            krange(item % splits, k0, k1);
+            for (int kb = k0; kb < k1; ++kb) {
+                failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                if (!failed && tc::elect_one()) {
                     const int tap = kb / p.cin_blocks;
                     const int cb = kb - tap * p.cin_blocks;
                     const int r = p.taps == 9 ? tap / 3 : 1;
@@ -413,42 +463,53 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                     cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, tl.img0, 0);
                     tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
                                     cb * 64, tap, tl.n0);
+                }
+                __syncwarp();
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                if (!failed) {
                     ++issued;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    istage = stage;
+                    iphase = phase;
                 }
             }
-            if (!ok) drain_ring(bar0, STAGES, stage, phase, issued);
+        }
+        if (failed) {
+            drain_ring_warp(bar0, STAGES, istage, iphase, issued);
+            if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
-            int stage = 0;
-            uint32_t phase = 0, it = 0;
-            bool ok = true;
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
-                int k0, k1;
-                krange(item % splits, k0, k1);
-                const int a = it & 1;
-                if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) break;
+        // ------------------------------------------------------------- MMA issuer
+        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+        int stage = 0;
+        uint32_t phase = 0, it = 0, failed = 0;
+        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
+            int k0, k1;
+            krange(item % splits, k0, k1);
+            const int a = it & 1;
+            failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
+            tc::tc_fence_after();
+            const uint32_t dcol = tmem + a * BN;
+            for (int kb = k0; kb < k1; ++kb) {
+                failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
                 tc::tc_fence_after();
-                const uint32_t dcol = tmem + a * BN;
-                for (int kb = k0; kb < k1; ++kb) {
-                    if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::tc_fence_after();
+                if (tc::elect_one()) {
                     const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                     const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
                         tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
                     tc::umma_commit(empty_bar(stage));
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
-                if (ok) tc::umma_commit(accf_bar(a));
+                __syncwarp();
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
+            if (tc::elect_one()) tc::umma_commit(accf_bar(a));
+            __syncwarp();
         }
+        if (tc::elect_one()) tc::umma_commit(done_bar);
+        __syncwarp();
+        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         const int q = warp & 3;
         const int row = 32 * q + lane;
@@ -456,12 +517,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const int pp = et % P, g = et / P;              // pixel, column group (TS groups)
         constexpr int NCOL = 32 / TS;
         const int64_t npix_total = (int64_t)p.B * p.H * p.W;
-        uint32_t it = 0;
+        uint32_t it = 0, failed = 0;
         for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
             const Tile tl = decode_tile(item / splits, p, BN);
             const int a = it & 1;
-            const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
-            if (tc::named_bar_any(1, 128, !got)) break;
+            failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
             if (p.partial) {
                 // ---- split-K: raw float32 partial sums of this split
@@ -513,7 +573,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         const float in = __fadd_rn(ybuf[(t * P + pp) * 33 + col], bb);
                         float vv = charge(v, p.df, p.sc, in);
                         const bool s = vv >= p.thr;
-                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                        vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
                         v = vv;
                         bits[t] |= (s ? 1u : 0u) << col;
                     }
@@ -536,6 +596,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             for (int i = et; i < TS * NCH * P; i += 128) smask[i] = 0u;
             tc::named_bar_sync(1, 128);
         }
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -561,12 +622,12 @@ constexpr int BAND_MAX_STAGES = 8;
 
 template <int BN>
 struct SmemBand {
-    static constexpr int MASK_BYTES = (BN / 32) * 128 * 4;
-    static constexpr int NBARS = 2 * BAND_MAX_STAGES + 6;
+    static constexpr int MASK_BYTES = 2 * (BN / 32) * 128 * 4;     // double-buffered pool exchange
+    static constexpr int NBARS = 2 * BAND_MAX_STAGES + 7;
     // layout (runtime sizes): weights [w_bytes] | A ring [ring x a_bytes] | masks | barriers |
     // TMEM slot | abort flag
     static int dyn_bytes(int w_bytes, int ring, int a_bytes) {
-        return w_bytes + ring * a_bytes + MASK_BYTES + NBARS * 8 + 8 + 1024;
+        return w_bytes + ring * 3 * a_bytes + MASK_BYTES + NBARS * 8 + 8 + 1024;
     }
 };
 
@@ -578,7 +639,7 @@ __device__ __forceinline__ Tile decode_band(int tile, const ConvParams& p, int B
     return Tile{0, band * p.bh, img, nb * BN};
 }
 
-template <int BN>
+template <int BN, bool HARD>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const ConvParams p) {
@@ -592,8 +653,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     const uint32_t sbase = tc::smem_u32(smem);
     const int nst = p.ring;
     const uint32_t a_off = (uint32_t)p.w_bytes;
-    const uint32_t a_bytes = (uint32_t)p.a_bytes;
-    const uint32_t mask_off = a_off + (uint32_t)nst * a_bytes;
+    const uint32_t a_bytes = (uint32_t)p.a_bytes;        // one column-shifted copy
+    const uint32_t st_bytes = 3 * a_bytes;               // a stage: the three copies of a slab
+    const uint32_t mask_off = a_off + (uint32_t)nst * st_bytes;
     uint32_t* smask = reinterpret_cast<uint32_t*>(smem + mask_off);
     const uint32_t bar_off = mask_off + S::MASK_BYTES;
     const uint32_t bar0 = sbase + bar_off;
@@ -603,6 +665,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * BAND_MAX_STAGES + 2 + a); };
     const uint32_t wfull_bar = bar0 + 8u * (2 * BAND_MAX_STAGES + 4);
     const uint32_t wempty_bar = bar0 + 8u * (2 * BAND_MAX_STAGES + 5);
+    const uint32_t done_bar = bar0 + 8u * (2 * BAND_MAX_STAGES + 6);
     const uint32_t tmem_off = bar_off + S::NBARS * 8;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + tmem_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + tmem_off + 4);
@@ -621,6 +684,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         tc::mbar_init(wfull_bar, 1);
         tc::mbar_init(wempty_bar, 1);
+        tc::mbar_init(done_bar, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmA);
@@ -635,22 +699,21 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Failure protocol: every role walks the whole schedule; a bounded wait that gives up
+    // sets the role's `failed`, after which its waits return at once (no branch on the wait
+    // results inside the loops -- see mbar_wait_warp).  The producer stops issuing copies,
+    // drains the ones in flight, and the CTA records SNNB_ERR_TIMEOUT at the end.
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
-        if (lane == 0) {
-            int stage = 0, issued = 0, cur_nb = -1;
-            uint32_t phase = 0, wloads = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const Tile tl = decode_band(tile, p, BN);
-                const int nb = tile / p.mtiles;
-                if (nb != cur_nb) {
-                    // the previous block's weights are free once every MMA reading them is done
-                    if (wloads > 0 &&
-                        !tc::mbar_wait(wempty_bar, (wloads - 1) & 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
+        int stage = 0, cur_nb = -1, istage = 0;
+        uint32_t phase = 0, wloads = 0, failed = 0, issued = 0, iphase = 0, wissued = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const Tile tl = decode_band(tile, p, BN);
+            const int nb = tile / p.mtiles;
+            if (nb != cur_nb) {
+                // the previous block's weights are free once every MMA reading them is done
+                if (wloads > 0) failed |= 1u - tc::mbar_wait_warp(wempty_bar, (wloads - 1) & 1u, failed);
+                if (!failed && tc::elect_one()) {
                     tc::mbar_expect_tx(wfull_bar, (uint32_t)p.w_bytes);
                     for (int cb = 0; cb < CB; ++cb)
                         for (int dx = 0; dx < 3; ++dx)
@@ -658,72 +721,78 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                                 tc::tma_load_3d(
                                     sbase + (uint32_t)((cb * 3 + dx) * 3 + dy) * TAP_BYTES, &tmB,
                                     wfull_bar, cb * 64, dy * 3 + dx, tl.n0);
-                    ++wloads;
-                    cur_nb = nb;
                 }
-                for (int t = 0; t < p.T && ok; ++t) {
-                    const int f = t * p.B + tl.img0;
-                    for (int cb = 0; cb < CB && ok; ++cb) {
-                        for (int dx = 0; dx < 3; ++dx) {
-                            if (!tc::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.status)) {
-                                ok = false;
-                                break;
-                            }
-                            tc::mbar_expect_tx(full_bar(stage), a_bytes);
-                            tc::tma_load_4d(sbase + a_off + (uint32_t)stage * a_bytes, &tmA,
-                                            full_bar(stage), cb * 64, dx - 1, tl.h0 - 1, f);
-                            ++issued;
-                            if (++stage == nst) { stage = 0; phase ^= 1u; }
-                        }
-                    }
-                }
+                __syncwarp();
+                wissued += failed ? 0u : 1u;
+                ++wloads;
+                cur_nb = nb;
             }
-            if (!ok) {
-                drain_ring(bar0, nst, stage, phase, issued);
-                if (wloads > 0) {
-                    const long long t0 = clock64();
-                    while (!tc::mbar_try_wait(wfull_bar, (wloads - 1) & 1u) &&
-                           clock64() - t0 < tc::WAIT_LIMIT_CYCLES) {
+            for (int t = 0; t < p.T; ++t) {
+                const int f = t * p.B + tl.img0;
+                for (int cb = 0; cb < CB; ++cb) {
+                    failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                    if (!failed && tc::elect_one()) {
+                        tc::mbar_expect_tx(full_bar(stage), st_bytes);
+                        const uint32_t dst = sbase + a_off + (uint32_t)stage * st_bytes;
+                        for (int dx = 0; dx < 3; ++dx)
+                            tc::tma_load_4d(dst + dx * a_bytes, &tmA, full_bar(stage), cb * 64,
+                                            dx - 1, tl.h0 - 1, f);
+                    }
+                    __syncwarp();
+                    if (++stage == nst) { stage = 0; phase ^= 1u; }
+                    if (!failed) {            // ring position after the last issued stage
+                        ++issued;
+                        istage = stage;
+                        iphase = phase;
                     }
                 }
             }
         }
+        if (failed) {
+            // wait (bounded) for the copies still in flight: the last min(nst, issued) stages
+            // issued and the last weight load
+            int st = istage;
+            uint32_t ph = iphase;
+            for (uint32_t k = 0; k < (uint32_t)nst && k < issued; ++k) {
+                if (--st < 0) { st = nst - 1; ph ^= 1u; }
+                tc::mbar_wait_warp(full_bar(st), ph, 0);
+            }
+            if (wissued > 0) tc::mbar_wait_warp(wfull_bar, (wissued - 1) & 1u, 0);
+            if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
+        }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
-            const uint32_t row_step = (uint32_t)p.W * 128u;     // one image row of the band copy
-            int stage = 0, cur_nb = -1;
-            uint32_t phase = 0, it = 0, wl = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const int nb = tile / p.mtiles;
-                if (nb != cur_nb) {
-                    if (wl > 0) tc::umma_commit(wempty_bar);
-                    if (!tc::mbar_wait(wfull_bar, wl & 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::tc_fence_after();
-                    ++wl;
-                    cur_nb = nb;
+        // The whole warp walks the schedule and waits; one elected lane issues.
+        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+        const uint32_t row_step = (uint32_t)p.W * 128u;         // one image row of the band copy
+        int stage = 0, cur_nb = -1;
+        uint32_t phase = 0, it = 0, wl = 0, failed = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const int nb = tile / p.mtiles;
+            if (nb != cur_nb) {
+                if (wl > 0) {
+                    if (tc::elect_one()) tc::umma_commit(wempty_bar);
+                    __syncwarp();
                 }
-                for (int t = 0; t < p.T && ok; ++t, ++it) {
-                    const int a = it & 1;
-                    if (!tc::mbar_wait(acce_bar(a), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
+                failed |= 1u - tc::mbar_wait_warp(wfull_bar, wl & 1u, failed);
+                tc::tc_fence_after();
+                ++wl;
+                cur_nb = nb;
+            }
+            for (int t = 0; t < p.T; ++t, ++it) {
+                const int a = it & 1;
+                failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
+                tc::tc_fence_after();
+                const uint32_t dcol = tmem + a * BN;
+                for (int cb = 0; cb < CB; ++cb) {
+                    // one wait per slab (36 MMAs): each wait costs the issuer ~100 cycles
+                    failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
                     tc::tc_fence_after();
-                    const uint32_t dcol = tmem + a * BN;
-                    for (int cb = 0; cb < CB && ok; ++cb) {
+                    const uint32_t sb = sbase + a_off + (uint32_t)stage * st_bytes;
+                    if (tc::elect_one()) {
+#pragma unroll
                         for (int dx = 0; dx < 3; ++dx) {
-                            if (!tc::mbar_wait(full_bar(stage), phase, abort_flag, p.status)) {
-                                ok = false;
-                                break;
-                            }
-                            tc::tc_fence_after();
-                            const uint32_t abase = sbase + a_off + (uint32_t)stage * a_bytes;
+                            const uint32_t abase = sb + dx * a_bytes;
                             const uint32_t wbase = sbase + (uint32_t)((cb * 3 + dx) * 3) * TAP_BYTES;
 #pragma unroll
                             for (int dy = 0; dy < 3; ++dy) {
@@ -734,36 +803,52 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                                     tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
                                                   (cb | dx | dy | k) != 0);
                             }
-                            tc::umma_commit(empty_bar(stage));
-                            if (++stage == nst) { stage = 0; phase ^= 1u; }
                         }
+                        tc::umma_commit(empty_bar(stage));
                     }
-                    if (ok) tc::umma_commit(accf_bar(a));
+                    __syncwarp();
+                    if (++stage == nst) { stage = 0; phase ^= 1u; }
                 }
+                if (tc::elect_one()) tc::umma_commit(accf_bar(a));
+                __syncwarp();
             }
         }
+        // every MMA issued must be complete before the CTA frees its TMEM
+        if (tc::elect_one()) tc::umma_commit(done_bar);
+        __syncwarp();
+        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         // ------------------------------------------------------------- epilogue
+        // Thread = TMEM lane = band pixel m (row y = m / W, column x = m % W).  The bias of
+        // the channel block stays in registers for the tile, v across t; shared memory is
+        // touched only to pool across warps (W >= 32), because while the tensor pipe streams
+        // operands every shared-memory / L1 round trip of the epilogue waits ~1000 cycles.
         const int q = warp & 3;
         const int m = 32 * q + lane;
-        const int et = threadIdx.x - 64;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int W = p.W;
+        const int x = m % W, y = m / W;
+        const int Ho = p.pool ? p.H / 2 : p.H, Wo = p.pool ? W / 2 : W;
+        uint32_t it = 0, failed = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_band(tile, p, BN);
-            const float* bias = p.bias + tl.n0;
+            float bias[BN];
+            const float4* bias4 = reinterpret_cast<const float4*>(p.bias + tl.n0);
+#pragma unroll
+            for (int j = 0; j < BN / 4; ++j) {
+                const float4 b4 = __ldg(bias4 + j);
+                bias[4 * j] = b4.x; bias[4 * j + 1] = b4.y; bias[4 * j + 2] = b4.z; bias[4 * j + 3] = b4.w;
+            }
             float v[BN];
 #pragma unroll
             for (int j = 0; j < BN; ++j) v[j] = 0.0f;
+            const int hy = tl.h0 + y;                         // image row of this pixel
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
-                const bool got = tc::mbar_wait(accf_bar(a), (it >> 1) & 1u, abort_flag, p.status);
-                if (tc::named_bar_any(1, 128, !got)) {
-                    ok = false;
-                    break;
-                }
+                failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
                 tc::tc_fence_after();
                 const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
+                uint32_t mk[NCH];
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
                     float r[32];
@@ -772,26 +857,57 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t mask = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const float in = __fadd_rn(r[j], __ldg(bias + c * 32 + j));
+                        const float in = __fadd_rn(r[j], bias[c * 32 + j]);
                         float vv = charge(v[c * 32 + j], p.df, p.sc, in);
                         const bool s = vv >= p.thr;
-                        vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                        vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
                         v[c * 32 + j] = vv;
                         mask |= (s ? 1u : 0u) << j;
                     }
-                    smask[c * 128 + m] = mask;
+                    mk[c] = mask;
                 }
                 tc::tc_fence_before();
                 tc::mbar_arrive(acce_bar(a));
-                tc::named_bar_sync(1, 128);
-                const int npix = p.pool ? 32 : 128;
-                for (int item = et; item < npix * NCH; item += 128) {
-                    const int pix = item / NCH, c = item - pix * NCH;
-                    store_spikes(p, tl, t, c, pix, [&](int mm) { return smask[c * 128 + mm]; });
+                const int64_t frame = (int64_t)t * p.B + tl.img0;
+                if (!p.pool) {
+                    if (hy < p.H) {
+                        uint4* dst = reinterpret_cast<uint4*>(
+                            p.out + ((frame * Ho + hy) * Wo + x) * p.Cout + tl.n0);
+#pragma unroll
+                        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+                    }
+                } else {
+                    // 2x2 max-pool = OR: column pairs are adjacent lanes; row pairs are lanes
+                    // W apart (W < 32) or the same lane of another warp (W >= 32)
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], 1);
+                    if (W < 32) {
+#pragma unroll
+                        for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], W);
+                    } else {
+                        uint32_t* sm = smask + (it & 1) * (NCH * 128);
+#pragma unroll
+                        for (int c = 0; c < NCH; ++c) sm[c * 128 + m] = mk[c];
+                        tc::named_bar_sync(1, 128);
+#pragma unroll
+                        for (int c = 0; c < NCH; ++c) mk[c] |= sm[c * 128 + (m ^ W)];
+                    }
+                    if (((x | y) & 1) == 0 && hy < p.H) {
+                        uint4* dst = reinterpret_cast<uint4*>(
+                            p.out + ((frame * Ho + hy / 2) * Wo + x / 2) * p.Cout + tl.n0);
+#pragma unroll
+                        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+                    }
                 }
-                tc::named_bar_sync(1, 128);
             }
         }
+        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -956,14 +1072,16 @@ int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorM
 // pipe fed.
 template <int BN, int STAGES>
 int launch_conv(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
-    return launch_persistent(conv_lif_kernel<BN, STAGES>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
+    return p.hard ? launch_persistent(conv_lif_kernel<BN, STAGES, true>, Smem<BN, STAGES>::DYN, ta, tb, p, s)
+                  : launch_persistent(conv_lif_kernel<BN, STAGES, false>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
 }
 
 template <int BN, int STAGES, int TS>
 int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
                    cudaStream_t s) {
-    return launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS>, SmemTM<BN, STAGES, TS>::DYN, ta,
-                             tb, p, s);
+    constexpr int dyn = SmemTM<BN, STAGES, TS>::DYN;
+    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true>, dyn, ta, tb, p, s)
+                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false>, dyn, ta, tb, p, s);
 }
 
 template <int TS>
@@ -1098,7 +1216,7 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     const int w_bytes = 9 * CB * BN * 128;
     const int fixed = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, 0, a_bytes)
                                : SmemBand<32>::dyn_bytes(w_bytes, 0, a_bytes);
-    int ring = (smem_optin() - fixed) / a_bytes;
+    int ring = (smem_optin() - fixed) / (3 * a_bytes);
     if (ring > BAND_MAX_STAGES) ring = BAND_MAX_STAGES;
     if (ring < 2) return SNNB_ERR_UNSUPPORTED;
     // activation map: dims (Cin, W, H, T*B), box (64, W, bh + 2, 1): the band and its halo
@@ -1130,11 +1248,13 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.splits = 1; p.partial = nullptr;
     p.ring = ring; p.a_bytes = a_bytes; p.w_bytes = w_bytes;
+    const int dyn = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes)
+                             : SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes);
     if (BN == 64)
-        return launch_persistent(conv_lif_band_kernel<64>,
-                                 SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes), ta, tb, p, s);
-    return launch_persistent(conv_lif_band_kernel<32>,
-                             SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes), ta, tb, p, s);
+        return hard ? launch_persistent(conv_lif_band_kernel<64, true>, dyn, ta, tb, p, s)
+                    : launch_persistent(conv_lif_band_kernel<64, false>, dyn, ta, tb, p, s);
+    return hard ? launch_persistent(conv_lif_band_kernel<32, true>, dyn, ta, tb, p, s)
+                : launch_persistent(conv_lif_band_kernel<32, false>, dyn, ta, tb, p, s);
 }
 
 // Shared host path of the conv / linear entries.

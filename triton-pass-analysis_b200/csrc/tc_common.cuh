@@ -64,6 +64,54 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// One lane of a converged warp (elect.sync): the lane that issues a TMA copy, an MMA or a
+// commit for the whole warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// Bounded wait of a whole converged warp, as one asm block: the lanes spin on try_wait and
+// agree through votes, so every lane leaves together and compiled code never branches on a
+// per-lane value (a branch there costs the MMA issuer its warp-uniform registers: each
+// tcgen05.mma issued after it took ~4x longer).  Returns 1 when the phase completed, 0 after
+// WAIT_LIMIT_CYCLES or at once when skip != 0 (an earlier wait of this warp failed).
+__device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity, uint32_t skip) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "@q bra WFAIL_%=;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "vote.sync.all.pred p, p, 0xffffffff;\n\t"
+        "@p bra WOK_%=;\n\t"
+        "mov.u64 t0, %%clock64;\n\t"
+        "WLOOP_%=:\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "vote.sync.all.pred p, p, 0xffffffff;\n\t"
+        "@p bra WOK_%=;\n\t"
+        "mov.u64 t1, %%clock64;\n\t"
+        "sub.u64 t1, t1, t0;\n\t"
+        "setp.lt.u64 q, t1, %4;\n\t"
+        "vote.sync.any.pred q, q, 0xffffffff;\n\t"
+        "@q bra WLOOP_%=;\n\t"
+        "WFAIL_%=:\n\t"
+        "mov.u32 %0, 0;\n\t"
+        "bra.uni WEND_%=;\n\t"
+        "WOK_%=:\n\t"
+        "mov.u32 %0, 1;\n\t"
+        "WEND_%=:\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "memory");
+    return ok;
+}
+
 // ---- TMA (tiled, no multicast) ------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, uint32_t bar,
                                             int c0, int c1) {
