@@ -76,6 +76,7 @@ __device__ __forceinline__ uint32_t row_mask(const __nv_bfloat16* row, int d, bo
 constexpr int JG = 4;                    // features per work item in the Q kv stage
 constexpr int MAX_ITEMS = 8;             // work items per thread: N * d / JG <= 2048
 
+template <bool HARD>
 __global__ void __launch_bounds__(THREADS) attention_core_kernel(const AttnParams p) {
     __shared__ uint32_t kbits[MAX_D][MAX_W];
     __shared__ uint32_t vbits[MAX_D][MAX_W];
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(THREADS) attention_core_kernel(const AttnParam
                     const float in = __fmul_rn(a[j], p.scale);
                     float vv = charge(vm[k][j], p.df, p.sc, in);
                     const bool s = vv >= p.thr;
-                    vv = p.hard ? (s ? p.v_reset : vv) : (s ? __fsub_rn(vv, p.thr) : vv);
+                    vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
                     vm[k][j] = vv;
                     bits |= (s ? 1u : 0u) << j;
                 }
@@ -224,6 +225,9 @@ extern "C" int snnb_spike_attention_core(
     p.T = (int)T; p.B = (int)B; p.H = (int)H; p.N = (int)N; p.d = (int)d;
     p.df = decay; p.sc = input_scale; p.scale = scale; p.thr = v_threshold; p.v_reset = v_reset;
     p.hard = hard_reset ? 1 : 0; p.do_av = do_av;
-    attention_core_kernel<<<(unsigned)(B * H), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    if (p.hard)
+        attention_core_kernel<true><<<(unsigned)(B * H), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    else
+        attention_core_kernel<false><<<(unsigned)(B * H), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
     return launch_status();
 }

@@ -368,7 +368,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 //
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
-// then runs after splitsum_kernel, which adds the splits in a fixed order.
+// then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
 template <int BN, int STAGES, int TS>
 struct SmemTM {
     static constexpr int P = 128 / TS;
@@ -918,12 +918,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
 }
 
 // ---- split-K reduction + bias + multi-step LIF (+ 2x2 max-pool) -------------------------
-// Two passes over partial [S][T][B*H*W][C] f32, both fully parallel:
-//  1. splitsum_kernel: thread = (step, pixel, 8 channels); issues its S loads at once,
-//     adds them in the order s = 0..S-1, adds the bias, and writes y in place of split 0;
-//  2. lif_pool_kernel: thread = (output pixel, 8 channels); loads y of its pixels for
-//     every step, runs the neuron over t with v in registers, ORs 2x2 windows when
-//     pooling, and stores bf16 spikes [T][B][Ho][Wo][C].
+// splitsum_kernel<S>: thread = (step, pixel, 8 channels); adds the S partial sums in the
+// order s = 0..S-1 and the bias, in place of split 0 (S = 1: the bias add of the
+// float32-output linear).  splitsum_lif_kernel (below) finishes split-K conv layers.
 template <int S>
 __global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ partial, int64_t rows,
                                                        int C, const float* __restrict__ bias) {
@@ -957,11 +954,15 @@ __global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ parti
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-template <bool POOL>
-__global__ void __launch_bounds__(256) lif_pool_kernel(const float* __restrict__ y, int T, int B,
-                                                       int H, int W, int C, float df, float sc,
-                                                       float thr, float v_reset, int hard,
-                                                       __nv_bfloat16* __restrict__ out) {
+// Split-K finish in one pass: thread = (output pixel, 8 channels).  Per step it loads the S
+// partial sums of each of its (pooled: four) pixels at once, adds them in the order
+// s = 0..S-1, adds the bias, runs the neuron with v in registers, ORs 2x2 windows when
+// pooling and stores bf16 spikes [T][B][Ho][Wo][C].
+template <int S, bool POOL, bool HARD>
+__global__ void __launch_bounds__(256) splitsum_lif_kernel(
+    const float* __restrict__ partial, int T, int B, int H, int W, int C,
+    const float* __restrict__ bias, float df, float sc, float thr, float v_reset,
+    __nv_bfloat16* __restrict__ out) {
     constexpr int NP = POOL ? 4 : 1;
     const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
     const int groups = C / 8;
@@ -975,44 +976,47 @@ __global__ void __launch_bounds__(256) lif_pool_kernel(const float* __restrict__
     const int oh = (int)(r % Ho);
     const int b = (int)(r / Ho);
     const int64_t npix = (int64_t)B * H * W;
+    const int64_t split_stride = (int64_t)T * npix * C;
+    float bb[8];
+    {
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + g * 8));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + g * 8) + 1);
+        bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
+        bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+    }
     float v[NP][8];
 #pragma unroll
     for (int q = 0; q < NP; ++q)
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[q][j] = 0.0f;
-    // loads of the next step are issued before the current step's neuron update
-    float4 nxt[NP][2];
-    auto load_step = [&](int t, float4 (&dst)[NP][2]) {
+    for (int t = 0; t < T; ++t) {
+        uint32_t bits = 0;
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
             const int h = POOL ? 2 * oh + (q >> 1) : oh;
             const int w = POOL ? 2 * ow + (q & 1) : ow;
             const float4* src = reinterpret_cast<const float4*>(
-                y + ((int64_t)t * npix + ((int64_t)b * H + h) * W + w) * C + g * 8);
-            dst[q][0] = __ldcs(src);
-            dst[q][1] = __ldcs(src + 1);
-        }
-    };
-    if (T > 0) load_step(0, nxt);
-    for (int t = 0; t < T; ++t) {
-        float4 in[NP][2];
+                partial + ((int64_t)t * npix + ((int64_t)b * H + h) * W + w) * C + g * 8);
+            float4 in[S][2];
 #pragma unroll
-        for (int q = 0; q < NP; ++q) {
-            in[q][0] = nxt[q][0];
-            in[q][1] = nxt[q][1];
-        }
-        if (t + 1 < T) load_step(t + 1, nxt);
-        uint32_t bits = 0;
+            for (int k = 0; k < S; ++k) {          // all S loads in flight at once
+                in[k][0] = __ldcs(src + k * (split_stride / 4));
+                in[k][1] = __ldcs(src + k * (split_stride / 4) + 1);
+            }
+            float y[8] = {in[0][0].x, in[0][0].y, in[0][0].z, in[0][0].w,
+                          in[0][1].x, in[0][1].y, in[0][1].z, in[0][1].w};
 #pragma unroll
-        for (int q = 0; q < NP; ++q) {
-            const float x[8] = {in[q][0].x, in[q][0].y, in[q][0].z, in[q][0].w,
-                                in[q][1].x, in[q][1].y, in[q][1].z, in[q][1].w};
+            for (int k = 1; k < S; ++k) {
+                y[0] = __fadd_rn(y[0], in[k][0].x); y[1] = __fadd_rn(y[1], in[k][0].y);
+                y[2] = __fadd_rn(y[2], in[k][0].z); y[3] = __fadd_rn(y[3], in[k][0].w);
+                y[4] = __fadd_rn(y[4], in[k][1].x); y[5] = __fadd_rn(y[5], in[k][1].y);
+                y[6] = __fadd_rn(y[6], in[k][1].z); y[7] = __fadd_rn(y[7], in[k][1].w);
+            }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float vv = charge(v[q][j], df, sc, x[j]);
+                float vv = charge(v[q][j], df, sc, __fadd_rn(y[j], bb[j]));
                 const bool sp = vv >= thr;
-                vv = hard ? (sp ? v_reset : vv) : (sp ? __fsub_rn(vv, thr) : vv);
-                v[q][j] = vv;
+                v[q][j] = reset_v<HARD>(vv, sp, thr, v_reset);
                 bits |= (sp ? 1u : 0u) << j;
             }
         }
@@ -1021,20 +1025,43 @@ __global__ void __launch_bounds__(256) lif_pool_kernel(const float* __restrict__
     }
 }
 
+template <int S>
+int launch_splitsum_lif_s(const float* partial, int T, int B, int H, int W, int C,
+                          const float* bias, float df, float sc, float thr, float v_reset,
+                          int hard, int pool, __nv_bfloat16* out, cudaStream_t s) {
+    const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
+    const int64_t threads = (int64_t)B * Ho * Wo * (C / 8);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    if (pool) {
+        if (hard) splitsum_lif_kernel<S, true, true><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        else splitsum_lif_kernel<S, true, false><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+    } else {
+        if (hard) splitsum_lif_kernel<S, false, true><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        else splitsum_lif_kernel<S, false, false><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+    }
+    return launch_status();
+}
+
+int launch_splitsum_lif(const float* partial, int S, int T, int B, int H, int W, int C,
+                        const float* bias, float df, float sc, float thr, float v_reset, int hard,
+                        int pool, __nv_bfloat16* out, cudaStream_t s) {
+    switch (S) {
+        case 2: return launch_splitsum_lif_s<2>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 3: return launch_splitsum_lif_s<3>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 4: return launch_splitsum_lif_s<4>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 5: return launch_splitsum_lif_s<5>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 6: return launch_splitsum_lif_s<6>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 7: return launch_splitsum_lif_s<7>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 8: return launch_splitsum_lif_s<8>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        default: return SNNB_ERR_UNSUPPORTED;
+    }
+}
+
 int launch_splitsum(float* partial, int S, int64_t rows, int C, const float* bias, cudaStream_t s) {
     const int64_t threads = rows * (C / 8);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
-    switch (S) {
-        case 1: splitsum_kernel<1><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 2: splitsum_kernel<2><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 3: splitsum_kernel<3><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 4: splitsum_kernel<4><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 5: splitsum_kernel<5><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 6: splitsum_kernel<6><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 7: splitsum_kernel<7><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        case 8: splitsum_kernel<8><<<blocks, 256, 0, s>>>(partial, rows, C, bias); break;
-        default: return SNNB_ERR_UNSUPPORTED;
-    }
+    if (S != 1) return SNNB_ERR_UNSUPPORTED;
+    splitsum_kernel<1><<<blocks, 256, 0, s>>>(partial, rows, C, bias);
     return launch_status();
 }
 
@@ -1263,7 +1290,7 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
 //          3 = row bands with halo reuse and resident weights (W in {8, 16, 32, 64}).
 // block_n: 0 = choose, else 32 / 64 / 128 (/ 256 with variant 2) output channels per CTA.
 // splits : > 1 splits the K range (variant 2 only): partial sums go to `workspace`
-//          ([splits][T][B*H*W][Cout] f32, caller-owned) and reduce_lif_kernel finishes.
+//          ([splits][T][B*H*W][Cout] f32, caller-owned) and splitsum_lif_kernel finishes.
 int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                  const float* bias, int Cout, int taps, float df, float sc, float thr,
                  float v_reset, int hard, int pool, int variant, int block_n, int splits,
@@ -1373,18 +1400,8 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
             default: rc = launch_tm_bn<8>(BN, ta, tb, p, s); break;
         }
         if (rc != SNNB_OK || splits == 1) return rc;
-        rc = launch_splitsum(p.partial, splits, (int64_t)T * B * H * W, Cout, bias, s);
-        if (rc != SNNB_OK) return rc;
-        const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
-        const int64_t threads = (int64_t)B * Ho * Wo * (Cout / 8);
-        const int64_t blocks = (threads + 255) / 256;
-        if (pool)
-            lif_pool_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(
-                p.partial, T, B, H, W, Cout, df, sc, thr, v_reset, p.hard, p.out);
-        else
-            lif_pool_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(
-                p.partial, T, B, H, W, Cout, df, sc, thr, v_reset, p.hard, p.out);
-        return launch_status();
+        return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
+                                   p.hard, pool, p.out, s);
     }
     switch (BN) {
         case 128: return launch_conv<128, 6>(ta, tb, p, s);

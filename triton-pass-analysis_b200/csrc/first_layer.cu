@@ -16,11 +16,11 @@ namespace {
 
 constexpr int THREADS = 128;
 
-template <bool POOL, int CG>
+template <bool POOL, int CG, bool HARD>
 __global__ void __launch_bounds__(THREADS) first_conv_lif_kernel(
     const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W,
     const float* __restrict__ w, const float* __restrict__ bias, int Cout,
-    float df, float sc, float thr, float v_reset, int hard, __nv_bfloat16* __restrict__ out) {
+    float df, float sc, float thr, float v_reset, __nv_bfloat16* __restrict__ out) {
     extern __shared__ float sw[];                    // [Cin*9][Cout]
     const int K = Cin * 9;
     for (int i = threadIdx.x; i < K * Cout; i += THREADS) {
@@ -85,8 +85,7 @@ __global__ void __launch_bounds__(THREADS) first_conv_lif_kernel(
                 const float in = __fadd_rn(y[q][j], bb[j]);
                 float vv = charge(v[q][j], df, sc, in);
                 const bool s = vv >= thr;
-                vv = hard ? (s ? v_reset : vv) : (s ? __fsub_rn(vv, thr) : vv);
-                v[q][j] = vv;
+                v[q][j] = reset_v<HARD>(vv, s, thr, v_reset);
                 bits[j / 32] |= (s ? 1u : 0u) << (j % 32);
             }
         }
@@ -122,28 +121,21 @@ extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_
     if (blocks > 0x7fffffffll) return SNNB_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     auto* o = static_cast<__nv_bfloat16*>(out);
-    cudaError_t e;
-    if (pool) {
-        e = cudaFuncSetAttribute(first_conv_lif_kernel<true, 16>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto run = [&](auto kernel) -> int {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return record_cuda_error(e);
-        first_conv_lif_kernel<true, 16><<<(unsigned)blocks, THREADS, smem, s>>>(
+        kernel<<<(unsigned)blocks, THREADS, smem, s>>>(
             x, (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay,
-            input_scale, v_threshold, v_reset, hard_reset, o);
-    } else if (CG == 64) {
-        e = cudaFuncSetAttribute(first_conv_lif_kernel<false, 64>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        first_conv_lif_kernel<false, 64><<<(unsigned)blocks, THREADS, smem, s>>>(
-            x, (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay,
-            input_scale, v_threshold, v_reset, hard_reset, o);
-    } else {
-        e = cudaFuncSetAttribute(first_conv_lif_kernel<false, 16>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        first_conv_lif_kernel<false, 16><<<(unsigned)blocks, THREADS, smem, s>>>(
-            x, (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay,
-            input_scale, v_threshold, v_reset, hard_reset, o);
-    }
-    return launch_status();
+            input_scale, v_threshold, v_reset, o);
+        return launch_status();
+    };
+    if (pool)
+        return hard_reset ? run(first_conv_lif_kernel<true, 16, true>)
+                          : run(first_conv_lif_kernel<true, 16, false>);
+    if (CG == 64)
+        return hard_reset ? run(first_conv_lif_kernel<false, 64, true>)
+                          : run(first_conv_lif_kernel<false, 64, false>);
+    return hard_reset ? run(first_conv_lif_kernel<false, 16, true>)
+                      : run(first_conv_lif_kernel<false, 16, false>);
 }

@@ -4,10 +4,7 @@
 // Replaces the last nn.Linear of VGGSNN (snn_compiler/zoo/vgg.py:84, run at :111-114)
 // and the caller's mean over T (examples/vgg16_snn/vgg16_test.py:243).  With N <= 64
 // outputs the product is a few dot products per sample -- far too narrow for a
-// tensor-core tile -- so it runs on the CUDA cores: one CTA per sample and one warp
-// per output, 16-byte loads of the bf16 spike row and of the weight row, warp-shuffle
-// reductions.  Per step
-// y_t = dot + b (float32); mean = (((y_0 + y_1) + y_2) + ...) * (1/T).
+// tensor-core tile -- so it runs on the CUDA cores.
 #include "common.cuh"
 
 namespace snnb {
@@ -23,41 +20,89 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 q, float (&o)[8]) {
     }
 }
 
-// One CTA per sample, one warp per output (N <= 32 warps): for every step the warp
-// takes the dot product of the sample's spike row with its weight row (16-byte loads,
-// each lane a strided slice of K), reduces it with shuffles, and lane 0 keeps the
-// running per-step sum.  No block-wide synchronisation.
-__global__ void linear_head_kernel(
+// One CTA of 256 threads per sample.  A pass covers up to TC steps x NC outputs: every
+// thread takes a strided set of 8-element K slices, loads the TC spike slices and NC weight
+// slices at once (16-byte loads), and keeps TC x NC independent float32 partial sums; the
+// partials are reduced with shuffles within warps and through shared memory across the
+// 8 warps.  Per step y_t = dot + b; mean = (((y_0 + y_1) + y_2) + ...) * (1/T).
+constexpr int HEAD_THREADS = 256;
+constexpr int TC = 4, NC = 8;
+
+__global__ void __launch_bounds__(HEAD_THREADS) linear_head_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int B, int K, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ bias, int N, int per_step, float* __restrict__ out) {
+    __shared__ float red[HEAD_THREADS / 32][TC * NC];
+    __shared__ float mean_acc[64];
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K8 = K / 8;
-    for (int n = warp; n < N; n += blockDim.x >> 5) {
-        const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)n * K);
-        const float bn = __ldg(bias + n);
-        float mean_acc = 0.0f;
-        for (int t = 0; t < T; ++t) {
-            const uint4* xr = reinterpret_cast<const uint4*>(x + ((int64_t)t * B + b) * K);
-            float acc = 0.0f;
-            for (int k8 = lane; k8 < K8; k8 += 32) {
-                float xv[8], wv[8];
-                bf16x8_to_f32(__ldg(xr + k8), xv);
-                bf16x8_to_f32(__ldg(wr + k8), wv);
+    if (threadIdx.x < 64) mean_acc[threadIdx.x] = 0.0f;
+    for (int t0 = 0; t0 < T; t0 += TC) {
+        for (int n0 = 0; n0 < N; n0 += NC) {
+            float acc[TC][NC];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc = __fmaf_rn(xv[i], wv[i], acc);
+            for (int i = 0; i < TC; ++i)
+#pragma unroll
+                for (int j = 0; j < NC; ++j) acc[i][j] = 0.0f;
+            for (int k8 = threadIdx.x; k8 < K8; k8 += HEAD_THREADS) {
+                uint4 xq[TC], wq[NC];
+#pragma unroll
+                for (int i = 0; i < TC; ++i)
+                    xq[i] = t0 + i < T ? __ldg(reinterpret_cast<const uint4*>(
+                                             x + ((int64_t)(t0 + i) * B + b) * K) + k8)
+                                       : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int j = 0; j < NC; ++j)
+                    wq[j] = n0 + j < N ? __ldg(reinterpret_cast<const uint4*>(
+                                             w + (int64_t)(n0 + j) * K) + k8)
+                                       : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int i = 0; i < TC; ++i) {
+                    float xv[8];
+                    bf16x8_to_f32(xq[i], xv);
+#pragma unroll
+                    for (int j = 0; j < NC; ++j) {
+                        float wv[8];
+                        bf16x8_to_f32(wq[j], wv);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[i][j] = __fmaf_rn(xv[e], wv[e], acc[i][j]);
+                    }
+                }
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            const float y = __fadd_rn(acc, bn);
-            if (per_step) {
-                if (lane == 0) out[((int64_t)t * B + b) * N + n] = y;
-            } else {
-                mean_acc = __fadd_rn(mean_acc, y);
+            for (int i = 0; i < TC; ++i)
+#pragma unroll
+                for (int j = 0; j < NC; ++j) {
+                    float a = acc[i][j];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                    if (lane == 0) red[warp][i * NC + j] = a;
+                }
+            __syncthreads();
+            if (threadIdx.x < TC * NC) {
+                const int i = threadIdx.x / NC, j = threadIdx.x % NC;
+                const int t = t0 + i, n = n0 + j;
+                if (t < T && n < N) {
+                    float d = red[0][threadIdx.x];
+#pragma unroll
+                    for (int k = 1; k < HEAD_THREADS / 32; ++k) d += red[k][threadIdx.x];
+                    const float y = __fadd_rn(d, __ldg(bias + n));
+                    if (per_step) out[((int64_t)t * B + b) * N + n] = y;
+                    else red[0][threadIdx.x] = y;
+                }
             }
+            __syncthreads();
+            if (!per_step && threadIdx.x < NC && n0 + threadIdx.x < N) {
+                // steps in order, so the running sum matches (((y_0 + y_1) + y_2) + ...)
+                float m = mean_acc[n0 + threadIdx.x];
+                for (int i = 0; i < TC && t0 + i < T; ++i) m = __fadd_rn(m, red[0][i * NC + threadIdx.x]);
+                mean_acc[n0 + threadIdx.x] = m;
+            }
+            __syncthreads();
         }
-        if (!per_step && lane == 0) out[(int64_t)b * N + n] = __fmul_rn(mean_acc, 1.0f / (float)T);
     }
+    if (!per_step && threadIdx.x < N)
+        out[(int64_t)b * N + threadIdx.x] = __fmul_rn(mean_acc[threadIdx.x], 1.0f / (float)T);
 }
 
 int run_head(const void* x, int64_t T, int64_t B, int64_t K, const void* w, const float* bias,
@@ -66,8 +111,7 @@ int run_head(const void* x, int64_t T, int64_t B, int64_t K, const void* w, cons
     if (T <= 0 || B <= 0 || K <= 0 || N <= 0 || N > 64) return SNNB_ERR_ARG;
     if (K % 8 || !aligned16(x) || !aligned16(w)) return SNNB_ERR_ARG;
     if (B > 0x7fffffff || T > 0x7fffffff || K > 0x7fffffff) return SNNB_ERR_ARG;
-    const int threads = 32 * (int)(N < 32 ? N : 32);
-    linear_head_kernel<<<(unsigned)B, threads, 0, s>>>(
+    linear_head_kernel<<<(unsigned)B, HEAD_THREADS, 0, s>>>(
         static_cast<const __nv_bfloat16*>(x), (int)T, (int)B, (int)K,
         static_cast<const __nv_bfloat16*>(w), bias, (int)N, per_step, out);
     return launch_status();
