@@ -78,6 +78,8 @@ constexpr int MAX_ITEMS = 8;             // work items per thread: N * d / JG <=
 
 template <bool HARD>
 __global__ void __launch_bounds__(THREADS) attention_core_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ uint32_t kbits[MAX_D][MAX_W];
     __shared__ uint32_t vbits[MAX_D][MAX_W];
     __shared__ __align__(16) float kv[MAX_D][MAX_D];
@@ -225,9 +227,7 @@ extern "C" int snnb_spike_attention_core(
     p.T = (int)T; p.B = (int)B; p.H = (int)H; p.N = (int)N; p.d = (int)d;
     p.df = decay; p.sc = input_scale; p.scale = scale; p.thr = v_threshold; p.v_reset = v_reset;
     p.hard = hard_reset ? 1 : 0; p.do_av = do_av;
-    if (p.hard)
-        attention_core_kernel<true><<<(unsigned)(B * H), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    else
-        attention_core_kernel<false><<<(unsigned)(B * H), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    return launch_status();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return p.hard ? launch_k(attention_core_kernel<true>, dim3((unsigned)(B * H)), dim3(THREADS), 0, s, p)
+                  : launch_k(attention_core_kernel<false>, dim3((unsigned)(B * H)), dim3(THREADS), 0, s, p);
 }

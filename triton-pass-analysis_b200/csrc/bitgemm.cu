@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(THREADS) bgemm_kernel(const uint32_t* __restri
                                                         int32_t* __restrict__ C, int64_t M,
                                                         int64_t N, int64_t ldw, int64_t kbits,
                                                         int64_t w_per_split, int atomic) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) uint32_t sm[];
     uint32_t* rowpop = sm + STAGES * STAGE_WORDS;
     const int tid = threadIdx.x;
@@ -181,6 +183,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) bitpack_kernel(const T* __restrict__ x, int64_t rows,
                                                       int64_t K, int64_t ldw, int positive,
                                                       uint32_t* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = rows * ldw;
     if (gid >= total) return;
@@ -222,17 +226,12 @@ extern "C" int snnb_bitpack(const void* x, int x_dtype, int64_t rows, int64_t K,
     if (blocks > 0x7fffffffll) return SNNB_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (x_dtype) {
-        case SNNB_F32: bitpack_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(
-            static_cast<const float*>(x), rows, K, ldw, positive, out); break;
-        case SNNB_F16: bitpack_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(
-            static_cast<const __half*>(x), rows, K, ldw, positive, out); break;
-        case SNNB_BF16: bitpack_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(x), rows, K, ldw, positive, out); break;
-        case SNNB_U8: bitpack_kernel<uint8_t><<<(unsigned)blocks, 256, 0, s>>>(
-            static_cast<const uint8_t*>(x), rows, K, ldw, positive, out); break;
+        case SNNB_F32: return launch_k(bitpack_kernel<float>, dim3((unsigned)blocks), dim3(256), 0, s, static_cast<const float*>(x), rows, K, ldw, positive, out);
+        case SNNB_F16: return launch_k(bitpack_kernel<__half>, dim3((unsigned)blocks), dim3(256), 0, s, static_cast<const __half*>(x), rows, K, ldw, positive, out);
+        case SNNB_BF16: return launch_k(bitpack_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), rows, K, ldw, positive, out);
+        case SNNB_U8: return launch_k(bitpack_kernel<uint8_t>, dim3((unsigned)blocks), dim3(256), 0, s, static_cast<const uint8_t*>(x), rows, K, ldw, positive, out);
         default: return SNNB_ERR_ARG;
     }
-    return launch_status();
 }
 
 extern "C" int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int64_t N,
@@ -264,16 +263,13 @@ extern "C" int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int6
     switch (mode) {
         case 0:
             cudaFuncSetAttribute(bgemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-            bgemm_kernel<0><<<grid, THREADS, SMEM_BYTES, s>>>(A, B, C, M, N, ldw, K, wps, atomic);
-            break;
+            return launch_k(bgemm_kernel<0>, grid, dim3(THREADS), SMEM_BYTES, s, A, B, C, M, N, ldw, K, wps, atomic);
         case 1:
             cudaFuncSetAttribute(bgemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-            bgemm_kernel<1><<<grid, THREADS, SMEM_BYTES, s>>>(A, B, C, M, N, ldw, K, wps, atomic);
-            break;
+            return launch_k(bgemm_kernel<1>, grid, dim3(THREADS), SMEM_BYTES, s, A, B, C, M, N, ldw, K, wps, atomic);
         default:
             cudaFuncSetAttribute(bgemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-            bgemm_kernel<2><<<grid, THREADS, SMEM_BYTES, s>>>(A, B, C, M, N, ldw, K, wps, atomic);
-            break;
+            return launch_k(bgemm_kernel<2>, grid, dim3(THREADS), SMEM_BYTES, s, A, B, C, M, N, ldw, K, wps, atomic);
     }
     return launch_status();
 }

@@ -242,6 +242,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
@@ -386,8 +388,11 @@ struct SmemTM {
     static constexpr int DYN = TOTAL + 1024;
 };
 
-template <int BN, int STAGES, int TS, bool HARD>
-__global__ void __launch_bounds__(THREADS, 1)
+// NP producer warps (warp 0 and warps 6 ..) take the k-slab stages round-robin: each TMA
+// issue occupies its thread for ~250 cycles whatever the box size, so one issuing thread
+// cannot keep up with 4 MMAs per stage.
+template <int BN, int STAGES, int TS, bool HARD, int NP>
+__global__ void __launch_bounds__(THREADS + 32 * (NP - 1), 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
     using S = SmemTM<BN, STAGES, TS>;
@@ -433,7 +438,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         tc::prefetch_tmap(&tmA);
         tc::prefetch_tmap(&tmB);
     }
-    for (int i = threadIdx.x; i < TS * NCH * P; i += THREADS) smask[i] = 0u;
+    for (int i = threadIdx.x; i < TS * NCH * P; i += blockDim.x) smask[i] = 0u;
     if (warp == 1) {
         tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
         tc::tmem_relinquish();
@@ -442,16 +447,23 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
-    if (warp == 0) {
-        // ------------------------------------------------------------- TMA producer
-        int stage = 0, istage = 0;
-        uint32_t phase = 0, iphase = 0, issued = 0, failed = 0;
+    if (warp == 0 || warp >= 6) {
+        // ------------------------------------------------------------- TMA producers
+        // producer pi issues the stages g with g % NP == pi (g counts k-slabs over the
+        // whole schedule, as the MMA warp does)
+        const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
+        uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
         for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
             const Tile tl = decode_tile(item / splits, p, BN);
             int k0, k1;
             krange(item % splits, k0, k1);
-            for (int kb = k0; kb < k1; ++kb) {
+            for (int kb = k0; kb < k1; ++kb, ++g) {
+                if (g % NP != pi) continue;
+                const int stage = (int)(g % STAGES);
+                const uint32_t phase = (g / STAGES) & 1u;
                 failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
                 if (!failed && tc::elect_one()) {
                     const int tap = kb / p.cin_blocks;
@@ -465,16 +477,17 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                     cb * 64, tap, tl.n0);
                 }
                 __syncwarp();
-                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 if (!failed) {
                     ++issued;
-                    istage = stage;
-                    iphase = phase;
+                    last_g = g;
                 }
             }
         }
         if (failed) {
-            drain_ring_warp(bar0, STAGES, istage, iphase, issued);
+            // wait (bounded) for this producer's copies still in flight
+            uint32_t gg = last_g;
+            for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP)
+                tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
             if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else if (warp == 1) {
@@ -490,9 +503,10 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::tc_fence_after();
             const uint32_t dcol = tmem + a * BN;
             for (int kb = k0; kb < k1; ++kb) {
-                failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
-                tc::tc_fence_after();
+                // only the issuing lane waits for the stage; the others meet it at __syncwarp
                 if (tc::elect_one()) {
+                    failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
+                    tc::tc_fence_after();
                     const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                     const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
@@ -505,6 +519,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
             if (tc::elect_one()) tc::umma_commit(accf_bar(a));
             __syncwarp();
+            // lane 0 (the elected lane) owns the failure flag of the stage waits; the warp-wide
+            // waits need the same skip value in every lane
+            failed = __shfl_sync(0xffffffffu, failed, 0);
         }
         if (tc::elect_one()) tc::umma_commit(done_bar);
         __syncwarp();
@@ -698,6 +715,8 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     // Failure protocol: every role walks the whole schedule; a bounded wait that gives up
     // sets the role's `failed`, after which its waits return at once (no branch on the wait
@@ -924,6 +943,8 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
 template <int S>
 __global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ partial, int64_t rows,
                                                        int C, const float* __restrict__ bias) {
+    pdl_wait();
+    pdl_trigger();
     const int groups = C / 8;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= rows * groups) return;
@@ -963,6 +984,8 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     const float* __restrict__ partial, int T, int B, int H, int W, int C,
     const float* __restrict__ bias, float df, float sc, float thr, float v_reset,
     __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NP = POOL ? 4 : 1;
     const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
     const int groups = C / 8;
@@ -1033,11 +1056,11 @@ int launch_splitsum_lif_s(const float* partial, int T, int B, int H, int W, int 
     const int64_t threads = (int64_t)B * Ho * Wo * (C / 8);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     if (pool) {
-        if (hard) splitsum_lif_kernel<S, true, true><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
-        else splitsum_lif_kernel<S, true, false><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        if (hard) return launch_k(splitsum_lif_kernel<S, true, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        else return launch_k(splitsum_lif_kernel<S, true, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
     } else {
-        if (hard) splitsum_lif_kernel<S, false, true><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
-        else splitsum_lif_kernel<S, false, false><<<blocks, 256, 0, s>>>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        if (hard) return launch_k(splitsum_lif_kernel<S, false, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        else return launch_k(splitsum_lif_kernel<S, false, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
     }
     return launch_status();
 }
@@ -1061,8 +1084,7 @@ int launch_splitsum(float* partial, int S, int64_t rows, int C, const float* bia
     const int64_t threads = rows * (C / 8);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     if (S != 1) return SNNB_ERR_UNSUPPORTED;
-    splitsum_kernel<1><<<blocks, 256, 0, s>>>(partial, rows, C, bias);
-    return launch_status();
+    return launch_k(splitsum_kernel<1>, dim3(blocks), dim3(256), 0, s, partial, rows, C, bias);
 }
 
 int sm_count() {
@@ -1080,18 +1102,17 @@ int sm_count() {
 
 template <typename K>
 int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorMap& tb,
-                      const ConvParams& p, cudaStream_t s) {
+                      const ConvParams& p, cudaStream_t s, int threads = THREADS) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return record_cuda_error(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, THREADS, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
     if (e != cudaSuccess) return record_cuda_error(e);
     if (occ < 1) return SNNB_ERR_UNSUPPORTED;
     const int64_t cap = (int64_t)sm_count() * occ;
     const int64_t items = (int64_t)p.num_tiles * (p.splits > 1 ? p.splits : 1);
     const int grid = (int)(items < cap ? items : cap);
-    kernel<<<grid, THREADS, smem, s>>>(ta, tb, p);
-    return launch_status();
+    return launch_k(kernel, dim3(grid), dim3(threads), smem, s, ta, tb, p);
 }
 
 // Ring depths fill the ~227 KB of shared memory: at these tile sizes one k-slab of MMAs
@@ -1107,8 +1128,10 @@ template <int BN, int STAGES, int TS>
 int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
                    cudaStream_t s) {
     constexpr int dyn = SmemTM<BN, STAGES, TS>::DYN;
-    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true>, dyn, ta, tb, p, s)
-                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false>, dyn, ta, tb, p, s);
+    constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
+    constexpr int threads = THREADS + 32 * (NP - 1);
+    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP>, dyn, ta, tb, p, s, threads);
 }
 
 template <int TS>

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(THREADS) first_conv_lif_kernel(
     const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W,
     const float* __restrict__ w, const float* __restrict__ bias, int Cout,
     float df, float sc, float thr, float v_reset, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float sw[];                    // [Cin*9][Cout]
     const int K = Cin * 9;
     for (int i = threadIdx.x; i < K * Cout; i += THREADS) {
@@ -96,6 +98,200 @@ __global__ void __launch_bounds__(THREADS) first_conv_lif_kernel(
     }
 }
 
+// Band form for the common case (no pooling, 128 % W == 0, Cout % 16 == 0, Cout <= 128):
+// a CTA owns a band of R = 128 / W whole rows of one image; its input patch (R + 2 rows with
+// the zero halo, all Cin channels) and the weights ([tap][cout]) are staged in shared
+// memory, and thread = (pixel, 16 output channels) -- the 16-channel group is warp-uniform,
+// so weight reads are broadcasts.  Few registers per thread keep many warps resident to
+// hide the staging and store latency.
+constexpr int BAND_CG = 16;
+
+template <bool HARD>
+__global__ void __launch_bounds__(1024) first_conv_band_kernel(
+    const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W,
+    const float* __restrict__ w, const float* __restrict__ bias, int Cout,
+    float df, float sc, float thr, float v_reset, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float smf[];
+    const int K = Cin * 9;
+    const int R = 128 / W;
+    const int PW = W + 2, PH = R + 2;
+    float* sw = smf;                                  // [K][Cout]
+    float* sb = smf + K * Cout;                       // [Cout]
+    float* sx = sb + Cout;                            // [Cin][PH][PW]
+    const int nb = (H + R - 1) / R;
+    const int b = blockIdx.x / nb, h0 = (blockIdx.x % nb) * R;
+    for (int i = threadIdx.x; i < K * Cout; i += blockDim.x) {
+        const int co = i % Cout, k = i / Cout;       // k = ci*9 + kh*3 + kw (torch order)
+        sw[i] = __ldg(w + (int64_t)co * K + k);
+    }
+    for (int i = threadIdx.x; i < Cout; i += blockDim.x) sb[i] = __ldg(bias + i);
+    const int p = threadIdx.x & 127, g = threadIdx.x >> 7;
+    const int py = p / W, px = p % W;
+    const int c0 = g * BAND_CG;
+    const bool live = h0 + py < H;
+    float v[BAND_CG], y[BAND_CG];
+#pragma unroll
+    for (int j = 0; j < BAND_CG; ++j) v[j] = 0.0f;
+    for (int t = 0; t < T; ++t) {
+        if (t == 0 || Ti != 1) {
+            const int ti = Ti == 1 ? 0 : t;
+            if (t > 0) __syncthreads();               // previous step done with sx
+            for (int i = threadIdx.x; i < Cin * PH * PW; i += blockDim.x) {
+                const int ci = i / (PH * PW), rem = i % (PH * PW);
+                const int ih = h0 + rem / PW - 1, iw = rem % PW - 1;
+                sx[i] = (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                            ? __ldg(x + (((int64_t)ti * B + b) * Cin + ci) * H * W + ih * W + iw)
+                            : 0.0f;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < BAND_CG; ++j) y[j] = 0.0f;
+            for (int ci = 0; ci < Cin; ++ci) {
+#pragma unroll
+                for (int kh = 0; kh < 3; ++kh) {
+#pragma unroll
+                    for (int kw = 0; kw < 3; ++kw) {
+                        const float xv = sx[(ci * PH + py + kh) * PW + px + kw];
+                        const float4* wk = reinterpret_cast<const float4*>(
+                            sw + (ci * 9 + kh * 3 + kw) * Cout + c0);
+#pragma unroll
+                        for (int q = 0; q < BAND_CG / 4; ++q) {
+                            const float4 w4 = wk[q];
+                            y[4 * q] = __fmaf_rn(xv, w4.x, y[4 * q]);
+                            y[4 * q + 1] = __fmaf_rn(xv, w4.y, y[4 * q + 1]);
+                            y[4 * q + 2] = __fmaf_rn(xv, w4.z, y[4 * q + 2]);
+                            y[4 * q + 3] = __fmaf_rn(xv, w4.w, y[4 * q + 3]);
+                        }
+                    }
+                }
+            }
+        }
+        uint32_t bits = 0;
+#pragma unroll
+        for (int j = 0; j < BAND_CG; ++j) {
+            const float in = __fadd_rn(y[j], sb[c0 + j]);
+            float vv = charge(v[j], df, sc, in);
+            const bool s = vv >= thr;
+            v[j] = reset_v<HARD>(vv, s, thr, v_reset);
+            bits |= (s ? 1u : 0u) << j;
+        }
+        if (live) {
+            uint4* dst = reinterpret_cast<uint4*>(
+                out + ((((int64_t)t * B + b) * H + h0 + py) * W + px) * Cout + c0);
+            dst[0] = spikes_to_bf16x8(bits & 0xffu);
+            dst[1] = spikes_to_bf16x8(bits >> 8);
+        }
+    }
+}
+
+// Quad form (no pooling, W % 4 == 0, Cout % 16 == 0): thread = 4 horizontally adjacent
+// pixels x 16 output channels, so each weight read from shared memory feeds 4 pixels and
+// each 6-value input row segment feeds 3 taps x 4 pixels (shared-memory instructions per
+// FMA drop ~3x against one pixel per thread, which was load/store-unit bound).  With direct
+// encoding the input current conv + b is computed once and reused at every step.
+constexpr int QUAD_THREADS = 128;
+
+template <bool HARD>
+__global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
+    const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W, int R,
+    const float* __restrict__ w, const float* __restrict__ bias, int Cout,
+    float df, float sc, float thr, float v_reset, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float smf[];
+    const int K = Cin * 9;
+    const int PW = W + 2, PH = R + 2;
+    float* sw = smf;                                  // [K][Cout]
+    float* sb = smf + K * Cout;                       // [Cout]
+    float* sx = sb + Cout;                            // [Cin][PH][PW]
+    const int nb = (H + R - 1) / R;
+    const int b = blockIdx.x / nb, h0 = (blockIdx.x % nb) * R;
+    for (int i = threadIdx.x; i < K * Cout; i += QUAD_THREADS) {
+        const int co = i % Cout, k = i / Cout;       // k = ci*9 + kh*3 + kw (torch order)
+        sw[i] = __ldg(w + (int64_t)co * K + k);
+    }
+    for (int i = threadIdx.x; i < Cout; i += QUAD_THREADS) sb[i] = __ldg(bias + i);
+    const int quads = R * (W / 4);
+    const int qd = threadIdx.x % quads, g = threadIdx.x / quads;
+    const int py = qd / (W / 4), px0 = 4 * (qd % (W / 4));
+    const int c0 = g * 16;
+    const bool live = g * 16 < Cout && h0 + py < H;
+    float in[4][16], v[4][16];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[p][j] = 0.0f;
+    for (int t = 0; t < T; ++t) {
+        if (t == 0 || Ti != 1) {
+            const int ti = Ti == 1 ? 0 : t;
+            if (t > 0) __syncthreads();               // previous step done with sx
+            for (int i = threadIdx.x; i < Cin * PH * PW; i += QUAD_THREADS) {
+                const int ci = i / (PH * PW), rem = i % (PH * PW);
+                const int ih = h0 + rem / PW - 1, iw = rem % PW - 1;
+                sx[i] = (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                            ? __ldg(x + (((int64_t)ti * B + b) * Cin + ci) * H * W + ih * W + iw)
+                            : 0.0f;
+            }
+            __syncthreads();
+            if (live) {
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) in[p][j] = 0.0f;
+                for (int ci = 0; ci < Cin; ++ci) {
+#pragma unroll
+                    for (int kh = 0; kh < 3; ++kh) {
+                        const float* row = sx + (ci * PH + py + kh) * PW + px0;
+                        float xr[6];
+#pragma unroll
+                        for (int e = 0; e < 6; ++e) xr[e] = row[e];
+#pragma unroll
+                        for (int kw = 0; kw < 3; ++kw) {
+                            const float4* wk = reinterpret_cast<const float4*>(
+                                sw + (ci * 9 + kh * 3 + kw) * Cout + c0);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float4 w4 = wk[q];
+#pragma unroll
+                                for (int p = 0; p < 4; ++p) {
+                                    const float xv = xr[p + kw];
+                                    in[p][4 * q] = __fmaf_rn(xv, w4.x, in[p][4 * q]);
+                                    in[p][4 * q + 1] = __fmaf_rn(xv, w4.y, in[p][4 * q + 1]);
+                                    in[p][4 * q + 2] = __fmaf_rn(xv, w4.z, in[p][4 * q + 2]);
+                                    in[p][4 * q + 3] = __fmaf_rn(xv, w4.w, in[p][4 * q + 3]);
+                                }
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) in[p][j] = __fadd_rn(in[p][j], sb[c0 + j]);
+            }
+        }
+        if (live) {
+            uint4* dst = reinterpret_cast<uint4*>(
+                out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0) * Cout + c0);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                uint32_t bits = 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float vv = charge(v[p][j], df, sc, in[p][j]);
+                    const bool s = vv >= thr;
+                    v[p][j] = reset_v<HARD>(vv, s, thr, v_reset);
+                    bits |= (s ? 1u : 0u) << j;
+                }
+                dst[p * (Cout / 8)] = spikes_to_bf16x8(bits & 0xffu);
+                dst[p * (Cout / 8) + 1] = spikes_to_bf16x8(bits >> 8);
+            }
+        }
+    }
+}
+
 }  // namespace
 }  // namespace snnb
 
@@ -121,14 +317,51 @@ extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_
     if (blocks > 0x7fffffffll) return SNNB_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     auto* o = static_cast<__nv_bfloat16*>(out);
+    if (!pool && W % 4 == 0 && W <= 4 * QUAD_THREADS && Cout % 16 == 0 && Cin <= 16) {
+        // rows per CTA so that R x (W/4) quads x (Cout/16) groups fill the CTA
+        const int per_row = (int)(W / 4) * (int)(Cout / 16);
+        const int R = per_row <= QUAD_THREADS ? QUAD_THREADS / per_row : 0;
+        const int64_t nblk = B * ((H + (R ? R : 1) - 1) / (R ? R : 1));
+        const int64_t qsmem = (9 * Cin * Cout + Cout + Cin * (R + 2) * (W + 2)) * 4;
+        if (R >= 1 && nblk <= 0x7fffffffll && qsmem <= 64 * 1024) {
+            auto quad = [&](auto kernel) -> int {
+                cudaError_t e = cudaFuncSetAttribute(
+                    kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem);
+                if (e != cudaSuccess) return record_cuda_error(e);
+                return launch_k(kernel, dim3((unsigned)nblk), dim3(QUAD_THREADS), qsmem, s, x,
+                                (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, R, w, bias,
+                                (int)Cout, decay, input_scale, v_threshold, v_reset, o);
+            };
+            return hard_reset ? quad(first_conv_quad_kernel<true>)
+                              : quad(first_conv_quad_kernel<false>);
+        }
+    }
+    if (!pool && W >= 8 && W <= 128 && 128 % W == 0 && Cout % BAND_CG == 0 && Cout <= 128 &&
+        Cin <= 16) {
+        const int R = 128 / (int)W;
+        const int64_t nblk = B * ((H + R - 1) / R);
+        const int64_t bsmem = (9 * Cin * Cout + Cout + Cin * (R + 2) * (W + 2)) * 4;
+        if (nblk <= 0x7fffffffll && bsmem <= 200 * 1024) {
+            const int threads = 128 * (int)(Cout / BAND_CG);
+            auto band = [&](auto kernel) -> int {
+                cudaError_t e = cudaFuncSetAttribute(
+                    kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem);
+                if (e != cudaSuccess) return record_cuda_error(e);
+                return launch_k(kernel, dim3((unsigned)nblk), dim3(threads), bsmem, s, x, (int)Ti,
+                                (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout,
+                                decay, input_scale, v_threshold, v_reset, o);
+            };
+            return hard_reset ? band(first_conv_band_kernel<true>)
+                              : band(first_conv_band_kernel<false>);
+        }
+    }
     auto run = [&](auto kernel) -> int {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return record_cuda_error(e);
-        kernel<<<(unsigned)blocks, THREADS, smem, s>>>(
-            x, (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay,
-            input_scale, v_threshold, v_reset, o);
-        return launch_status();
+        return launch_k(kernel, dim3((unsigned)blocks), dim3(THREADS), smem, s, x, (int)Ti, (int)T,
+                        (int)B, (int)Cin, (int)H, (int)W, w, bias, (int)Cout, decay, input_scale,
+                        v_threshold, v_reset, o);
     };
     if (pool)
         return hard_reset ? run(first_conv_lif_kernel<true, 16, true>)

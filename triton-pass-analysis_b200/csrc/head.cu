@@ -31,6 +31,8 @@ constexpr int TC = 4, NC = 8;
 __global__ void __launch_bounds__(HEAD_THREADS) linear_head_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int B, int K, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ bias, int N, int per_step, float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[HEAD_THREADS / 32][TC * NC];
     __shared__ float mean_acc[64];
     const int b = blockIdx.x;
@@ -111,10 +113,9 @@ int run_head(const void* x, int64_t T, int64_t B, int64_t K, const void* w, cons
     if (T <= 0 || B <= 0 || K <= 0 || N <= 0 || N > 64) return SNNB_ERR_ARG;
     if (K % 8 || !aligned16(x) || !aligned16(w)) return SNNB_ERR_ARG;
     if (B > 0x7fffffff || T > 0x7fffffff || K > 0x7fffffff) return SNNB_ERR_ARG;
-    linear_head_kernel<<<(unsigned)B, HEAD_THREADS, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), (int)T, (int)B, (int)K,
-        static_cast<const __nv_bfloat16*>(w), bias, (int)N, per_step, out);
-    return launch_status();
+    return launch_k(linear_head_kernel, dim3((unsigned)B), dim3(HEAD_THREADS), 0, s,
+                    static_cast<const __nv_bfloat16*>(x), (int)T, (int)B, (int)K,
+                    static_cast<const __nv_bfloat16*>(w), bias, (int)N, per_step, out);
 }
 
 }  // namespace

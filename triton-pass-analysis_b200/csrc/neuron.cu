@@ -120,6 +120,8 @@ constexpr int THREADS = 256;
 
 template <typename TX, typename TS>
 __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t g = (int64_t)blockIdx.x * THREADS + threadIdx.x;
     const int64_t n0 = g * VEC;
     const bool active = n0 < p.N;          // N % VEC == 0: a vector is all in or all out
@@ -208,6 +210,8 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
 // covers 32 consecutive neurons, so one ballot is one packed word.
 template <typename TX, typename TS>
 __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n = (int64_t)blockIdx.x * THREADS + threadIdx.x;
     const bool active = n < p.N;
     const int lane = threadIdx.x & 31;
@@ -253,12 +257,10 @@ int launch_typed(const NeuronParams& p, bool vec, cudaStream_t s) {
     if (vec) {
         const int64_t threads = (p.N + VEC - 1) / VEC;
         const int64_t blocks = (threads + THREADS - 1) / THREADS;
-        neuron_vec8_kernel<TX, TS><<<(unsigned)blocks, THREADS, 0, s>>>(p);
-    } else {
-        const int64_t blocks = (p.N + THREADS - 1) / THREADS;
-        neuron_scalar_kernel<TX, TS><<<(unsigned)blocks, THREADS, 0, s>>>(p);
+        return launch_k(neuron_vec8_kernel<TX, TS>, dim3((unsigned)blocks), dim3(THREADS), 0, s, p);
     }
-    return launch_status();
+    const int64_t blocks = (p.N + THREADS - 1) / THREADS;
+    return launch_k(neuron_scalar_kernel<TX, TS>, dim3((unsigned)blocks), dim3(THREADS), 0, s, p);
 }
 
 template <typename TX>

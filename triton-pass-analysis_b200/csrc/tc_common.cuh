@@ -112,6 +112,37 @@ __device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity
     return ok;
 }
 
+// The same bounded wait for one thread (the elected lane of the MMA warp: only it touches
+// the stage it waits for).  No votes, so it adds nothing to the issue path when the phase
+// has already completed.
+__device__ __forceinline__ uint32_t mbar_wait_lane(uint32_t bar, uint32_t parity, uint32_t skip) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "@q bra LFAIL_%=;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "@p bra LOK_%=;\n\t"
+        "mov.u64 t0, %%clock64;\n\t"
+        "LLOOP_%=:\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "@p bra LOK_%=;\n\t"
+        "mov.u64 t1, %%clock64;\n\t"
+        "sub.u64 t1, t1, t0;\n\t"
+        "setp.lt.u64 q, t1, %4;\n\t"
+        "@q bra LLOOP_%=;\n\t"
+        "LFAIL_%=:\n\t"
+        "mov.u32 %0, 0;\n\t"
+        "bra.uni LEND_%=;\n\t"
+        "LOK_%=:\n\t"
+        "mov.u32 %0, 1;\n\t"
+        "LEND_%=:\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "memory");
+    return ok;
+}
+
 // ---- TMA (tiled, no multicast) ------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, uint32_t bar,
                                             int c0, int c1) {
