@@ -54,64 +54,105 @@ def load_peaks():
 # ----------------------------------------------------------------------------------------
 # clocks sampled during the timed region
 class ClockSampler:
+    """SM clock and clock-event reasons sampled every ~1 ms through NVML (read only) while
+    the timed region runs; falls back to nvidia-smi polling when NVML is unavailable."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.samples = []
-        self.proc = None
+        self.samples = []          # (time, sm_mhz, max_mhz, set of reason names)
         self.gpu = gpu_index
         self.window = None
+        self.proc = None
+        self.stop_flag = False
+        self.nvml = None
 
     def start(self):
         try:
+            import pynvml
+            pynvml.nvmlInit()
+            # the NVML device of this process's CUDA device, by PCI address (NVML indexes all
+            # GPUs of the node, whatever CUDA_VISIBLE_DEVICES selects)
+            prop = torch.cuda.get_device_properties(torch.cuda.current_device())
+            try:
+                bus = "%08x:%02x:%02x.0" % (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nvml, self.h = pynvml, h
+            self.bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
+                 "-lms", "100", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
+    def _poll_nvml(self):
+        p = self.nvml
+        while not self.stop_flag:
+            try:
+                sm = p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)
+                mx = p.nvmlDeviceGetMaxClockInfo(self.h, p.NVML_CLOCK_SM)
+                rb = p.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                rs = {n for n, b in self.bits.items() if rb & b}
+                self.samples.append((time.time(), float(sm), float(mx), rs))
+            except Exception:
+                pass
+            time.sleep(0.001)
+
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.samples.append((time.time(), line.strip()))
+            parts = [q.strip() for q in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rs = {n for n, v in zip(self.NAMES, parts[5:9]) if v.lower().startswith("active")}
+                self.samples.append((time.time(), float(parts[1]), float(parts[2]), rs))
+            except ValueError:
+                continue
 
     def mark(self, t0, t1):
         self.window = (t0, t1)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = self.samples
-        if self.window:
-            inside = [r for r in rows if self.window[0] - 0.05 <= r[0] <= self.window[1] + 0.25]
-            rows = inside or rows
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for _, line in rows:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
+        self.stop_flag = True
+        if self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.nvml is None and self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no NVML / nvidia-smi"],
+                    "samples": 0}
+        rows = list(self.samples)
+        if self.window and rows:
+            inside = [r for r in rows if self.window[0] <= r[0] <= self.window[1]]
+            if not inside:      # window shorter than the polling period: nearest samples
+                rows = sorted(rows, key=lambda r: min(abs(r[0] - self.window[0]),
+                                                      abs(r[0] - self.window[1])))[:2]
+            else:
+                rows = inside
+        sm = [r[1] for r in rows]
+        reasons = sorted(set().union(*[r[3] for r in rows])) if rows else []
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "sm_max_mhz": max(r[2] for r in rows) if rows else None, "reasons": reasons,
+                "samples": len(rows), "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------------------
@@ -254,6 +295,7 @@ class VggWorkload:
     flush_l2 = True
     load_choices = None
     save_choices = None
+    eager = False
 
     def __init__(self, B=64, T=4):
         self.B, self.T = B, T
@@ -272,7 +314,8 @@ class VggWorkload:
                 "collective": "NCCL all_gather of [64,10] f32 logits per step" if self.world > 1
                 else "none",
                 "l2": "256 MB buffer written before every timed step",
-                "launch": "CUDA graphs (3 segments, dominant layer timed alone)"}
+                "launch": "eager launches" if self.eager else
+                          "CUDA graphs (3 segments, dominant layer timed alone)"}
 
     def setup(self, rank, world, dist=None):
         from snn_compiler.zoo.vgg import SpikingVGG, random_vgg_params
@@ -300,11 +343,29 @@ class VggWorkload:
             json.dump({json.dumps(list(k)): list(v) for k, v in self.eng.choice.items()},
                       open(self.save_choices, "w"))
         self.launches_per_step = self.eng.kernel_launches(self.B)
-        self.out = self.eng.capture(self.img, split_at=dom)
+        if self.eager:
+            # launches issued one by one (for profilers that replay single kernels); same work
+            self.steps_eager, self.out = steps, out
+        else:
+            self.out = self.eng.capture(self.img, split_at=dom)
         self.dom_graph = 1
         self.gathered = torch.empty(world * self.B, 10, device="cuda") if world > 1 else None
         self._dom_events = []
         self.flops_img = self.eng.flops_per_image()
+
+    def _kernel_label(self, i):
+        """Name of the kernel that runs plan step i (the autotuned variant)."""
+        name = self.layer_names[i]
+        if i == 0:
+            return f"first_conv_lif ({name})"
+        keys = [k for k in self.eng.choice if k[2] == self.B]
+        key = sorted(keys, key=lambda k: (k[0] != "conv", k[1]))[i - 1] if i - 1 < len(keys) else None
+        if key is None:
+            return f"linear_head_kernel ({name})"
+        v = self.eng.choice[key]
+        kern = {1: "conv_lif_kernel", 2: "conv_lif_tm_kernel", 3: "conv_lif_band_kernel"}.get(
+            v[0], "conv_lif (auto)")
+        return f"{kern}<block_n={v[1]}, splits={v[2]}> ({name})"
 
     def _between(self, i):
         if i == self.dom_graph:
@@ -316,8 +377,21 @@ class VggWorkload:
             e.record()
             self._dom_events.append((self._pending, e))
 
+    def _forward(self, between=None):
+        if not self.eager:
+            return self.eng.replay(between=between)
+        groups = [range(self.dom), [self.dom], range(self.dom + 1, len(self.steps_eager))]
+        for i, grp in enumerate(groups):
+            if between is not None:
+                between(i)
+            for k in grp:
+                self.steps_eager[k][2]()
+        if between is not None:
+            between(len(groups))
+        return self.out
+
     def step(self):
-        self.eng.replay(between=self._between)
+        self._forward(between=self._between)
         if self.gathered is not None:
             self.dist.all_gather_into_tensor(self.gathered, self.out)
 
@@ -337,7 +411,7 @@ class VggWorkload:
 
     def e2e_step(self):
         self.img.copy_(self.h_img, non_blocking=True)
-        self.eng.replay()
+        self._forward()
         res = self.out
         if self.gathered is not None:
             self.dist.all_gather_into_tensor(self.gathered, self.out)
@@ -358,7 +432,7 @@ class VggWorkload:
         return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
-                "kernel": f"conv_lif_kernel ({self.layer_names[self.dom]})",
+                "kernel": self._kernel_label(self.dom),
                 "algorithmic_flops_per_launch": flops,
                 "kernel_ms": round(kernel_ms, 5),
                 "per_layer_device_ms": {n: round(t, 4) for n, t in
@@ -790,6 +864,9 @@ def main():
     ap.add_argument("--load-choices", default=None,
                     help="vgg16: use a tuned kernel table instead of timing (e.g. under ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--eager", action="store_true",
+                    help="vgg16: launch the forward kernel by kernel instead of replaying CUDA "
+                         "graphs (for kernel-replaying profilers; the same work)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -810,6 +887,7 @@ def main():
             wl = {"vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
         if args.workload == "vgg16":
             wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
+            wl.eager = args.eager
     wl.world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, wl)

@@ -1,5 +1,6 @@
 // Status helpers of the C ABI (snnb200.h).
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -7,6 +8,14 @@
 namespace snnb {
 namespace {
 thread_local char g_last_error[256] = "";
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("SNNB_NO_PDL");
+        return !(v && v[0] && v[0] != '0');
+    }();
+    return on;
 }
 
 int record_cuda_error(cudaError_t e) {

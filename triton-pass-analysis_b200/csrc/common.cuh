@@ -32,6 +32,10 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// SNNB_NO_PDL=1 in the environment launches without the attribute (plain stream order),
+// e.g. under a profiler that replays kernels one by one.
+bool pdl_enabled();
+
 template <typename... KArgs, typename... Args>
 inline int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                     Args&&... args) {
@@ -44,7 +48,7 @@ inline int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
     return e == cudaSuccess ? launch_status() : record_cuda_error(e);
 }

@@ -292,21 +292,34 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tc::tc_fence_after();
                 const uint32_t dcol = tmem + a * BN;
                 for (int kb = 0; kb < KB; ++kb) {
-                    failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
-                    tc::tc_fence_after();
+                    int nstage = stage + 1;
+                    uint32_t nphase = phase;
+                    if (nstage == STAGES) { nstage = 0; nphase ^= 1u; }
+                    // the issuing lane alone waits, for the next stage before committing this
+                    // one (a wait queued behind a commit returns only once the pipe drained)
                     if (tc::elect_one()) {
+                        if (kb == 0) {
+                            failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
+                            tc::tc_fence_after();
+                        }
                         const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                         const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)   // 4 x K=16 inside the 128-byte swizzle atom
                             tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
+                        if (kb + 1 < KB) {
+                            failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
+                            tc::tc_fence_after();
+                        }
                         tc::umma_commit(empty_bar(stage));
                     }
                     __syncwarp();
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    stage = nstage;
+                    phase = nphase;
                 }
                 if (tc::elect_one()) tc::umma_commit(accf_bar(a));
                 __syncwarp();
+                failed = __shfl_sync(0xffffffffu, failed, 0);
             }
         }
         if (tc::elect_one()) tc::umma_commit(done_bar);
@@ -503,19 +516,31 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::tc_fence_after();
             const uint32_t dcol = tmem + a * BN;
             for (int kb = k0; kb < k1; ++kb) {
-                // only the issuing lane waits for the stage; the others meet it at __syncwarp
+                int nstage = stage + 1;
+                uint32_t nphase = phase;
+                if (nstage == STAGES) { nstage = 0; nphase ^= 1u; }
+                // only the issuing lane waits for stages (the others meet it at __syncwarp),
+                // and it waits for the next stage before committing this one: a wait queued
+                // behind a commit would not return until the tensor pipe had drained
                 if (tc::elect_one()) {
-                    failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
-                    tc::tc_fence_after();
+                    if (kb == k0) {
+                        failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
+                        tc::tc_fence_after();
+                    }
                     const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                     const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
                         tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
+                    if (kb + 1 < k1) {
+                        failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
+                        tc::tc_fence_after();
+                    }
                     tc::umma_commit(empty_bar(stage));
                 }
                 __syncwarp();
-                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                stage = nstage;
+                phase = nphase;
             }
             if (tc::elect_one()) tc::umma_commit(accf_bar(a));
             __syncwarp();
@@ -804,11 +829,16 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 tc::tc_fence_after();
                 const uint32_t dcol = tmem + a * BN;
                 for (int cb = 0; cb < CB; ++cb) {
-                    // one wait per slab (36 MMAs): each wait costs the issuer ~100 cycles
-                    failed |= 1u - tc::mbar_wait_warp(full_bar(stage), phase, failed);
-                    tc::tc_fence_after();
+                    int nstage = stage + 1;
+                    uint32_t nphase = phase;
+                    if (nstage == nst) { nstage = 0; nphase ^= 1u; }
                     const uint32_t sb = sbase + a_off + (uint32_t)stage * st_bytes;
+                    // the issuing lane alone waits, for the next slab before committing this one
                     if (tc::elect_one()) {
+                        if (cb == 0) {
+                            failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
+                            tc::tc_fence_after();
+                        }
 #pragma unroll
                         for (int dx = 0; dx < 3; ++dx) {
                             const uint32_t abase = sb + dx * a_bytes;
@@ -823,13 +853,19 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                                                   (cb | dx | dy | k) != 0);
                             }
                         }
+                        if (cb + 1 < CB) {
+                            failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
+                            tc::tc_fence_after();
+                        }
                         tc::umma_commit(empty_bar(stage));
                     }
                     __syncwarp();
-                    if (++stage == nst) { stage = 0; phase ^= 1u; }
+                    stage = nstage;
+                    phase = nphase;
                 }
                 if (tc::elect_one()) tc::umma_commit(accf_bar(a));
                 __syncwarp();
+                failed = __shfl_sync(0xffffffffu, failed, 0);
             }
         }
         // every MMA issued must be complete before the CTA frees its TMEM

@@ -181,9 +181,9 @@ class SpikingVGG:
 
     def kernel_launches(self, B: int) -> int:
         """Kernel launches of one forward at batch B after its layers were tuned: one per
-        layer, plus the split reduction and the neuron launch of every split-K layer."""
+        layer, plus the split-K finish (sum + bias + neuron) of every split-K layer."""
         n = len(self.layers) + len(self.fcs)
-        return n + sum(2 for k, c in self.choice.items() if k[2] == B and c[2] > 1)
+        return n + sum(1 for k, c in self.choice.items() if k[2] == B and c[2] > 1)
 
     def forward(self, img: torch.Tensor, *, per_step_logits: bool = False) -> torch.Tensor:
         """img [B, 3, H, W] (direct encoding: the same image at every step) or
