@@ -68,6 +68,7 @@ class ClockSampler:
         self.proc = None
         self.stop_flag = False
         self.nvml = None
+        self.error = None
 
     def start(self):
         try:
@@ -102,17 +103,23 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _poll_nvml(self):
+    def _sample_nvml(self):
         p = self.nvml
-        while not self.stop_flag:
+        try:
+            sm = p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)
+            mx = p.nvmlDeviceGetMaxClockInfo(self.h, p.NVML_CLOCK_SM)
             try:
-                sm = p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)
-                mx = p.nvmlDeviceGetMaxClockInfo(self.h, p.NVML_CLOCK_SM)
                 rb = p.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                rs = {n for n, b in self.bits.items() if rb & b}
-                self.samples.append((time.time(), float(sm), float(mx), rs))
             except Exception:
-                pass
+                rb = p.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+            rs = {n for n, b in self.bits.items() if rb & b}
+            self.samples.append((time.time(), float(sm), float(mx), rs))
+        except Exception as e:          # keep the first error for the report
+            self.error = self.error or f"{type(e).__name__}: {e}"
+
+    def _poll_nvml(self):
+        while not self.stop_flag:
+            self._sample_nvml()
             time.sleep(0.001)
 
     def _read_smi(self):
@@ -131,6 +138,10 @@ class ClockSampler:
 
     def stop(self):
         self.stop_flag = True
+        if self.nvml is not None:
+            self.thread.join(timeout=1.0)
+            if not self.samples:           # timed region shorter than one poll: sample now
+                self._sample_nvml()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -150,9 +161,12 @@ class ClockSampler:
                 rows = inside
         sm = [r[1] for r in rows]
         reasons = sorted(set().union(*[r[3] for r in rows])) if rows else []
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(r[2] for r in rows) if rows else None, "reasons": reasons,
-                "samples": len(rows), "source": "nvml" if self.nvml else "nvidia-smi"}
+        out = {"sm_mhz": statistics.median(sm) if sm else None,
+               "sm_max_mhz": max(r[2] for r in rows) if rows else None, "reasons": reasons,
+               "samples": len(rows), "source": "nvml" if self.nvml else "nvidia-smi"}
+        if not rows and self.error:
+            out["error"] = self.error
+        return out
 
 
 # ----------------------------------------------------------------------------------------
@@ -315,7 +329,7 @@ class VggWorkload:
                 else "none",
                 "l2": "256 MB buffer written before every timed step",
                 "launch": "eager launches" if self.eager else
-                          "CUDA graphs (3 segments, dominant layer timed alone)"}
+                          "one CUDA graph per forward (timing events around the dominant launch)"}
 
     def setup(self, rank, world, dist=None):
         from snn_compiler.zoo.vgg import SpikingVGG, random_vgg_params
@@ -347,7 +361,8 @@ class VggWorkload:
             # launches issued one by one (for profilers that replay single kernels); same work
             self.steps_eager, self.out = steps, out
         else:
-            self.out = self.eng.capture(self.img, split_at=dom)
+            # one graph per forward, with a timing-event pair around the dominant launch
+            self.out = self.eng.capture(self.img, mark=dom)
         self.dom_graph = 1
         self.gathered = torch.empty(world * self.B, 10, device="cuda") if world > 1 else None
         self._dom_events = []
@@ -379,7 +394,7 @@ class VggWorkload:
 
     def _forward(self, between=None):
         if not self.eager:
-            return self.eng.replay(between=between)
+            return self.eng.replay()
         groups = [range(self.dom), [self.dom], range(self.dom + 1, len(self.steps_eager))]
         for i, grp in enumerate(groups):
             if between is not None:
@@ -396,8 +411,21 @@ class VggWorkload:
             self.dist.all_gather_into_tensor(self.gathered, self.out)
 
     def kernel_events(self, steps):
-        ev = self._dom_events[-steps:]
-        return [a.elapsed_time(b) for a, b in ev]
+        if self.eager:
+            ev = self._dom_events[-steps:]
+            return [a.elapsed_time(b) for a, b in ev]
+        # the dominant launch inside the one-graph forward: replays after the timed region,
+        # each on a flushed L2 as in the timed steps, reading the in-graph event pair
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        out = []
+        for _ in range(min(steps, 20)):
+            flush.fill_(1)
+            self.eng.replay()
+            torch.cuda.synchronize()
+            a, b = self.eng.mark_events
+            out.append(a.elapsed_time(b))
+        del flush
+        return out
 
     def units_per_step(self):
         return self.B
@@ -849,7 +877,7 @@ def run_ours(args, workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="vgg16",

@@ -223,10 +223,13 @@ class SpikingVGG:
         return total
 
     # ---- CUDA graphs ----------------------------------------------------------------------
-    def capture(self, img: torch.Tensor, *, split_at: int | None = None):
+    def capture(self, img: torch.Tensor, *, split_at: int | None = None,
+                mark: int | None = None):
         """Capture the forward over the static input buffer ``img`` into CUDA graphs.
         With split_at=i the launches are split into three graphs [0, i), [i], (i, end) so
-        that the i-th launch can be timed alone between replays.  Returns the output."""
+        that the i-th launch can be timed alone between replays.  With mark=i the forward is
+        one graph holding a pair of timing events around launch i (``self.mark_events``;
+        read them after a replay has completed).  Returns the output."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
         steps, out = self.plan(img)
@@ -237,11 +240,19 @@ class SpikingVGG:
             [list(range(split_at)), [split_at], list(range(split_at + 1, len(steps)))]
         self.graphs = []
         self.graph_pool = torch.cuda.graph_pool_handle()
+        self.mark_events = None
+        if mark is not None:
+            self.mark_events = (torch.cuda.Event(enable_timing=True, external=True),
+                                torch.cuda.Event(enable_timing=True, external=True))
         for grp in groups:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=self.graph_pool):
                 for k in grp:
+                    if k == mark:
+                        self.mark_events[0].record()
                     steps[k][2]()
+                    if k == mark:
+                        self.mark_events[1].record()
             self.graphs.append(g)
         torch.cuda.synchronize()
         self.graph_out = out
