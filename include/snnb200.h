@@ -142,7 +142,8 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *           3 = as 1 on bands of 128/W whole image rows (W in {8, 16, 32, 64}), each
  *           64-channel slab loaded once per column tap with its halo rows and reused by
  *           the three row taps, the channel block's weights resident in shared memory
- *           (9 * ceil(Cin/64) * block_n <= 864; SNNB_ERR_UNSUPPORTED otherwise).
+ *           (9 * ceil(Cin/64) * block_n <= 864; SNNB_ERR_UNSUPPORTED otherwise);
+ *           4 = as 2 with two 128-row tiles per CTA sharing every weight stage (block_n <= 128).
  * block_n : output channels per CTA, 0 = choose, or 32 / 64 / 128 (dividing Cout), or 256
  *           with variant 2; 32 / 64 with variant 3.
  * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32

@@ -384,17 +384,17 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
 // then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
-template <int BN, int STAGES, int TS>
+template <int BN, int STAGES, int TS, int MH>
 struct SmemTM {
     static constexpr int P = 128 / TS;
     static constexpr int NCH = BN / 32;
     static constexpr int B_TILE = BN * 128;
     static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = STAGES * A_TILE_BYTES;
+    static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
     static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 128 x 33 f32
     static constexpr int MASK_OFF = Y_OFF + 128 * 33 * 4;               // TS x NCH x P u32
     static constexpr int BAR_OFF = (MASK_OFF + TS * NCH * P * 4 + 7) & ~7;
-    static constexpr int NBARS = 2 * STAGES + 5;
+    static constexpr int NBARS = 2 * STAGES + 4 * MH + 1;
     static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
     static constexpr int ABORT_OFF = TMEM_OFF + 4;
     static constexpr int TOTAL = ABORT_OFF + 4;
@@ -404,11 +404,15 @@ struct SmemTM {
 // NP producer warps (warp 0 and warps 6 ..) take the k-slab stages round-robin: each TMA
 // issue occupies its thread for ~250 cycles whatever the box size, so one issuing thread
 // cannot keep up with 4 MMAs per stage.
-template <int BN, int STAGES, int TS, bool HARD, int NP>
+// MH M-tiles per work item (MH = 2: two 128-row tiles of the same channel block share each
+// weight stage, so every weight byte brought into shared memory feeds twice the MMAs --
+// these layers are bound by the L2 -> shared-memory stream of ~55 B/cycle per SM).  Each
+// tile has its own pair of TMEM accumulators (slot = (item & 1) * MH + h).
+template <int BN, int STAGES, int TS, bool HARD, int NP, int MH>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1), 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
-    using S = SmemTM<BN, STAGES, TS>;
+    using S = SmemTM<BN, STAGES, TS, MH>;
     constexpr int P = S::P, NCH = S::NCH;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -420,8 +424,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
-    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-    const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
+    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 * MH + a); };
+    const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4 * MH);
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
 
@@ -429,8 +433,18 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const int KB = p.taps * p.cin_blocks;
     const int splits = p.splits;
     const int num_items = p.num_tiles * splits;
-    constexpr uint32_t STAGE_TX = A_TILE_BYTES + S::B_TILE;
-    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    constexpr uint32_t STAGE_TX = MH * A_TILE_BYTES + S::B_TILE;
+    constexpr uint32_t TMEM_COLS = 2 * MH * BN < 32 ? 32 : 2 * MH * BN;
+    static_assert(2 * MH * BN <= 512, "accumulators exceed TMEM");
+    // M-tile h of a work item; false when the item's last tile lies past the layer (odd
+    // tile count) -- its box reads zeros and the epilogue stores nothing
+    auto half_tile = [&](int item, int h, Tile& tl) {
+        const int tile2 = item / splits;
+        const int nt = tile2 % p.n_tiles_n;
+        const int mt = (tile2 / p.n_tiles_n) * MH + h;
+        tl = decode_tile(mt * p.n_tiles_n + nt, p, BN);
+        return mt < p.mtiles;
+    };
     auto krange = [&](int s, int& k0, int& k1) {
         k0 = (int)((int64_t)KB * s / splits);
         k1 = (int)((int64_t)KB * (s + 1) / splits);
@@ -441,7 +455,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::mbar_init(full_bar(s), 1);
             tc::mbar_init(empty_bar(s), 1);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < 2 * MH; ++a) {
             tc::mbar_init(accf_bar(a), 1);
             tc::mbar_init(acce_bar(a), 128);
         }
@@ -470,7 +484,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
         uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
         for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-            const Tile tl = decode_tile(item / splits, p, BN);
+            Tile tl[MH];
+#pragma unroll
+            for (int h = 0; h < MH; ++h) half_tile(item, h, tl[h]);
             int k0, k1;
             krange(item % splits, k0, k1);
             for (int kb = k0; kb < k1; ++kb, ++g) {
@@ -484,10 +500,13 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const int r = p.taps == 9 ? tap / 3 : 1;
                     const int s = p.taps == 9 ? tap % 3 : 1;
                     tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-                    tc::tma_load_5d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, full_bar(stage),
-                                    cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, tl.img0, 0);
+#pragma unroll
+                    for (int h = 0; h < MH; ++h)
+                        tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES, &tmA,
+                                        full_bar(stage), cb * 64, tl[h].w0 + s - 1,
+                                        tl[h].h0 + r - 1, tl[h].img0, 0);
                     tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
-                                    cb * 64, tap, tl.n0);
+                                    cb * 64, tap, tl[0].n0);
                 }
                 __syncwarp();
                 if (!failed) {
@@ -511,10 +530,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
             int k0, k1;
             krange(item % splits, k0, k1);
-            const int a = it & 1;
-            failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
+            const int a0 = (it & 1) * MH;            // this item's first accumulator slot
+#pragma unroll
+            for (int h = 0; h < MH; ++h)
+                failed |= 1u - tc::mbar_wait_warp(acce_bar(a0 + h), ((it >> 1) & 1u) ^ 1u, failed);
             tc::tc_fence_after();
-            const uint32_t dcol = tmem + a * BN;
             for (int kb = k0; kb < k1; ++kb) {
                 int nstage = stage + 1;
                 uint32_t nphase = phase;
@@ -527,11 +547,16 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
                         tc::tc_fence_after();
                     }
-                    const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF + stage * A_TILE_BYTES);
                     const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
+                    for (int h = 0; h < MH; ++h) {
+                        const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF +
+                                                              (stage * MH + h) * A_TILE_BYTES);
+                        const uint32_t dcol = tmem + (a0 + h) * BN;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
+                    }
                     if (kb + 1 < k1) {
                         failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
                         tc::tc_fence_after();
@@ -542,7 +567,10 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 stage = nstage;
                 phase = nphase;
             }
-            if (tc::elect_one()) tc::umma_commit(accf_bar(a));
+            if (tc::elect_one()) {
+#pragma unroll
+                for (int h = 0; h < MH; ++h) tc::umma_commit(accf_bar(a0 + h));
+            }
             __syncwarp();
             // lane 0 (the elected lane) owns the failure flag of the stage waits; the warp-wide
             // waits need the same skip value in every lane
@@ -561,8 +589,10 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const int64_t npix_total = (int64_t)p.B * p.H * p.W;
         uint32_t it = 0, failed = 0;
         for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
-            const Tile tl = decode_tile(item / splits, p, BN);
-            const int a = it & 1;
+          for (int h = 0; h < MH; ++h) {
+            Tile tl;
+            half_tile(item, h, tl);
+            const int a = (int)(it & 1) * MH + h;
             failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
             if (p.partial) {
@@ -637,6 +667,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc::named_bar_sync(1, 128);
             for (int i = et; i < TS * NCH * P; i += 128) smask[i] = 0u;
             tc::named_bar_sync(1, 128);
+          }
         }
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     }
@@ -1160,19 +1191,27 @@ int launch_conv(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& 
                   : launch_persistent(conv_lif_kernel<BN, STAGES, false>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
 }
 
-template <int BN, int STAGES, int TS>
+template <int BN, int STAGES, int TS, int MH = 1>
 int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
                    cudaStream_t s) {
-    constexpr int dyn = SmemTM<BN, STAGES, TS>::DYN;
+    constexpr int dyn = SmemTM<BN, STAGES, TS, MH>::DYN;
     constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
     constexpr int threads = THREADS + 32 * (NP - 1);
-    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP>, dyn, ta, tb, p, s, threads)
-                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP>, dyn, ta, tb, p, s, threads);
+    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH>, dyn, ta, tb, p, s, threads);
 }
 
 template <int TS>
 int launch_tm_bn(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
-                 cudaStream_t s) {
+                 cudaStream_t s, int mh = 1) {
+    if (mh == 2) {
+        switch (BN) {
+            case 128: return launch_conv_tm<128, 4, TS, 2>(ta, tb, p, s);
+            case 64: return launch_conv_tm<64, 5, TS, 2>(ta, tb, p, s);
+            case 32: return launch_conv_tm<32, 5, TS, 2>(ta, tb, p, s);
+            default: return SNNB_ERR_UNSUPPORTED;
+        }
+    }
     switch (BN) {
         case 256: return launch_conv_tm<256, 4, TS>(ta, tb, p, s);
         case 128: return launch_conv_tm<128, 6, TS>(ta, tb, p, s);
@@ -1360,7 +1399,13 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
     if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    if (variant < 0 || variant > 3) return SNNB_ERR_ARG;
+    if (variant < 0 || variant > 4) return SNNB_ERR_ARG;
+    // variant 4: T folded into M with two M-tiles per CTA sharing each weight stage
+    const int mh = variant == 4 ? 2 : 1;
+    if (variant == 4) {
+        if (block_n == 256) return SNNB_ERR_UNSUPPORTED;      // 2 x 2 x 256 TMEM columns
+        variant = 2;
+    }
     if (block_n != 0 && block_n != 32 && block_n != 64 && block_n != 128 && block_n != 256)
         return SNNB_ERR_ARG;
     if (block_n && Cout % block_n) return SNNB_ERR_ARG;
@@ -1381,6 +1426,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;
     if (splits > 1 && (variant == 1 || !tm_ok)) return SNNB_ERR_UNSUPPORTED;
     if (splits > 1) variant = 2;
+    if (mh == 2 && variant != 2) return SNNB_ERR_UNSUPPORTED;
     const int bn_max = (Cout % 128 == 0) ? 128 : (Cout % 64 == 0 ? 64 : 32);
     int bw, bh, bn;
     if (variant == 0) {
@@ -1402,7 +1448,8 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (!BN) {
         BN = bn_max;
         // narrower channel blocks until the grid covers the SMs
-        while (BN > 32 && mtiles * (Cout / BN) * splits < 148) BN /= 2;
+        if (mh == 2 && BN > 128) BN = 128;
+        while (BN > 32 && ((mtiles + mh - 1) / mh) * (Cout / BN) * splits < 148) BN /= 2;
     }
     if (splits > 1) {
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
@@ -1449,14 +1496,15 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.splits = splits;
     p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
-    const int64_t ntiles = mtiles * p.n_tiles_n;
+    const int64_t ntiles = ((mtiles + mh - 1) / mh) * p.n_tiles_n;
+    p.mtiles = (int)mtiles;
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
     p.num_tiles = (int)ntiles;
     if (variant == 2) {
         switch (T) {
-            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s); break;
-            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s); break;
-            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s); break;
+            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh); break;
+            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh); break;
+            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh); break;
         }
         if (rc != SNNB_OK || splits == 1) return rc;
         return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
@@ -1544,6 +1592,7 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     p.bias = bias; p.out = nullptr; p.status = status;
     p.splits = 1;
     p.partial = out;
+    p.mtiles = (int)mtiles;
     p.num_tiles = (int)(mtiles * p.n_tiles_n);
     switch (iT) {
         case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s); break;
