@@ -1042,10 +1042,11 @@ __global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ parti
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// Split-K finish in one pass: thread = (output pixel, 8 channels).  Per step it loads the S
-// partial sums of each of its (pooled: four) pixels at once, adds them in the order
-// s = 0..S-1, adds the bias, runs the neuron with v in registers, ORs 2x2 windows when
-// pooling and stores bf16 spikes [T][B][Ho][Wo][C].
+// Split-K finish in one pass: thread = (pixel, 8 channels).  Per step it loads the S
+// partial sums of its pixel at once, adds them in the order s = 0..S-1, adds the bias, runs
+// the neuron with v in registers and stores bf16 spikes [T][B][Ho][Wo][C].  With pooling the
+// four pixels of a 2x2 window are four adjacent lanes that OR their spike bits by shuffles;
+// the first of them stores the pooled spikes.
 template <int S, bool POOL, bool HARD>
 __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     const float* __restrict__ partial, int T, int B, int H, int W, int C,
@@ -1056,35 +1057,35 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     constexpr int NP = POOL ? 4 : 1;
     const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
     const int groups = C / 8;
-    const int64_t total = (int64_t)B * Ho * Wo * groups;
+    const int64_t total = (int64_t)B * Ho * Wo * groups * NP;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= total) return;
-    const int g = (int)(gid % groups);
-    int64_t r = gid / groups;
+    // out-of-range lanes stay (no early exit) so the window shuffles see full warps; total
+    // is a multiple of 4, so a window's four lanes are all in range or all out
+    const bool valid = gid < total;
+    const int q = POOL ? (int)(gid & 3) : 0;
+    int64_t r = POOL ? (gid >> 2) : gid;
+    const int g = (int)(r % groups);
+    r /= groups;
     const int ow = (int)(r % Wo);
     r /= Wo;
     const int oh = (int)(r % Ho);
     const int b = (int)(r / Ho);
+    const int h = POOL ? 2 * oh + (q >> 1) : oh;
+    const int w = POOL ? 2 * ow + (q & 1) : ow;
     const int64_t npix = (int64_t)B * H * W;
     const int64_t split_stride = (int64_t)T * npix * C;
-    float bb[8];
-    {
+    float bb[8], v[8];
+    if (valid) {
         const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + g * 8));
         const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + g * 8) + 1);
         bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
         bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
     }
-    float v[NP][8];
 #pragma unroll
-    for (int q = 0; q < NP; ++q)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[q][j] = 0.0f;
+    for (int j = 0; j < 8; ++j) v[j] = 0.0f;
     for (int t = 0; t < T; ++t) {
         uint32_t bits = 0;
-#pragma unroll
-        for (int q = 0; q < NP; ++q) {
-            const int h = POOL ? 2 * oh + (q >> 1) : oh;
-            const int w = POOL ? 2 * ow + (q & 1) : ow;
+        if (valid) {
             const float4* src = reinterpret_cast<const float4*>(
                 partial + ((int64_t)t * npix + ((int64_t)b * H + h) * W + w) * C + g * 8);
             float4 in[S][2];
@@ -1104,14 +1105,20 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float vv = charge(v[q][j], df, sc, __fadd_rn(y[j], bb[j]));
+                float vv = charge(v[j], df, sc, __fadd_rn(y[j], bb[j]));
                 const bool sp = vv >= thr;
-                v[q][j] = reset_v<HARD>(vv, sp, thr, v_reset);
+                v[j] = reset_v<HARD>(vv, sp, thr, v_reset);
                 bits |= (sp ? 1u : 0u) << j;
             }
         }
-        const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 8;
-        *reinterpret_cast<uint4*>(out + o) = spikes_to_bf16x8(bits & 0xffu);
+        if (POOL) {
+            bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+            bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+        }
+        if (valid && q == 0) {
+            const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 8;
+            *reinterpret_cast<uint4*>(out + o) = spikes_to_bf16x8(bits & 0xffu);
+        }
     }
 }
 
@@ -1120,7 +1127,7 @@ int launch_splitsum_lif_s(const float* partial, int T, int B, int H, int W, int 
                           const float* bias, float df, float sc, float thr, float v_reset,
                           int hard, int pool, __nv_bfloat16* out, cudaStream_t s) {
     const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
-    const int64_t threads = (int64_t)B * Ho * Wo * (C / 8);
+    const int64_t threads = (int64_t)B * Ho * Wo * (C / 8) * (pool ? 4 : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     if (pool) {
         if (hard) return launch_k(splitsum_lif_kernel<S, true, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);

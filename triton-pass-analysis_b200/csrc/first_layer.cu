@@ -189,11 +189,14 @@ __global__ void __launch_bounds__(1024) first_conv_band_kernel(
 // Quad form (no pooling, W % 4 == 0, Cout % 16 == 0): thread = 4 horizontally adjacent
 // pixels x 16 output channels, so each weight read from shared memory feeds 4 pixels and
 // each 6-value input row segment feeds 3 taps x 4 pixels (shared-memory instructions per
-// FMA drop ~3x against one pixel per thread, which was load/store-unit bound).  With direct
-// encoding the input current conv + b is computed once and reused at every step.
+// FMA drop ~3x against one pixel per thread, which was load/store-unit bound).  Channel
+// pairs go through the packed float32x2 FMA / add / mul of sm_100 (each component rounded
+// as the scalar __fmaf_rn / __fadd_rn / __fmul_rn), halving the arithmetic instructions.
+// With direct encoding the scaled input current sc * (conv + b) is computed once and
+// reused at every step.
 constexpr int QUAD_THREADS = 128;
 
-template <bool HARD>
+template <bool HARD, bool DIRECT>
 __global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
     const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W, int R,
     const float* __restrict__ w, const float* __restrict__ bias, int Cout,
@@ -205,7 +208,9 @@ __global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
     const int PW = W + 2, PH = R + 2;
     float* sw = smf;                                  // [K][Cout]
     float* sb = smf + K * Cout;                       // [Cout]
-    float* sx = sb + Cout;                            // [Cin][PH][PW]
+    // [Cin][PH][PW] pixels, each stored twice (x, x) so that one 8-byte load gives the
+    // broadcast operand of a packed FMA
+    float2* sx = reinterpret_cast<float2*>(sb + Cout);
     const int nb = (H + R - 1) / R;
     const int b = blockIdx.x / nb, h0 = (blockIdx.x % nb) * R;
     for (int i = threadIdx.x; i < K * Cout; i += QUAD_THREADS) {
@@ -218,77 +223,89 @@ __global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
     const int py = qd / (W / 4), px0 = 4 * (qd % (W / 4));
     const int c0 = g * 16;
     const bool live = g * 16 < Cout && h0 + py < H;
-    float in[4][16], v[4][16];
+    const float2 df2 = make_float2(df, df), sc2 = make_float2(sc, sc);
+    float2 u[4][8];                                   // sc * (conv + b), channel pairs
+    float2 v[4][8];
+    // stage frame ti of the input and compute u = sc * (conv + b) for this thread's pixels
+    auto conv = [&](int ti) {
+        for (int i = threadIdx.x; i < Cin * PH * PW; i += QUAD_THREADS) {
+            const int ci = i / (PH * PW), rem = i % (PH * PW);
+            const int ih = h0 + rem / PW - 1, iw = rem % PW - 1;
+            const float xv = (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                        ? __ldg(x + (((int64_t)ti * B + b) * Cin + ci) * H * W + ih * W + iw)
+                        : 0.0f;
+            sx[i] = make_float2(xv, xv);
+        }
+        __syncthreads();
+        if (!live) return;
 #pragma unroll
-    for (int p = 0; p < 4; ++p)
+        for (int p = 0; p < 4; ++p)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[p][j] = 0.0f;
-    for (int t = 0; t < T; ++t) {
-        if (t == 0 || Ti != 1) {
-            const int ti = Ti == 1 ? 0 : t;
-            if (t > 0) __syncthreads();               // previous step done with sx
-            for (int i = threadIdx.x; i < Cin * PH * PW; i += QUAD_THREADS) {
-                const int ci = i / (PH * PW), rem = i % (PH * PW);
-                const int ih = h0 + rem / PW - 1, iw = rem % PW - 1;
-                sx[i] = (ih >= 0 && ih < H && iw >= 0 && iw < W)
-                            ? __ldg(x + (((int64_t)ti * B + b) * Cin + ci) * H * W + ih * W + iw)
-                            : 0.0f;
-            }
-            __syncthreads();
-            if (live) {
+            for (int j = 0; j < 8; ++j) u[p][j] = make_float2(0.0f, 0.0f);
+        for (int ci = 0; ci < Cin; ++ci) {
 #pragma unroll
-                for (int p = 0; p < 4; ++p)
+            for (int kh = 0; kh < 3; ++kh) {
+                const float2* row = sx + (ci * PH + py + kh) * PW + px0;
+                float2 xr[6];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) in[p][j] = 0.0f;
-                for (int ci = 0; ci < Cin; ++ci) {
+                for (int e = 0; e < 6; ++e) xr[e] = row[e];
 #pragma unroll
-                    for (int kh = 0; kh < 3; ++kh) {
-                        const float* row = sx + (ci * PH + py + kh) * PW + px0;
-                        float xr[6];
+                for (int kw = 0; kw < 3; ++kw) {
+                    const float4* wk =
+                        reinterpret_cast<const float4*>(sw + (ci * 9 + kh * 3 + kw) * Cout + c0);
 #pragma unroll
-                        for (int e = 0; e < 6; ++e) xr[e] = row[e];
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 w4 = wk[q];
+                        const float2 wlo = make_float2(w4.x, w4.y);
+                        const float2 whi = make_float2(w4.z, w4.w);
 #pragma unroll
-                        for (int kw = 0; kw < 3; ++kw) {
-                            const float4* wk = reinterpret_cast<const float4*>(
-                                sw + (ci * 9 + kh * 3 + kw) * Cout + c0);
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const float4 w4 = wk[q];
-#pragma unroll
-                                for (int p = 0; p < 4; ++p) {
-                                    const float xv = xr[p + kw];
-                                    in[p][4 * q] = __fmaf_rn(xv, w4.x, in[p][4 * q]);
-                                    in[p][4 * q + 1] = __fmaf_rn(xv, w4.y, in[p][4 * q + 1]);
-                                    in[p][4 * q + 2] = __fmaf_rn(xv, w4.z, in[p][4 * q + 2]);
-                                    in[p][4 * q + 3] = __fmaf_rn(xv, w4.w, in[p][4 * q + 3]);
-                                }
-                            }
+                        for (int p = 0; p < 4; ++p) {
+                            u[p][2 * q] = __ffma2_rn(xr[p + kw], wlo, u[p][2 * q]);
+                            u[p][2 * q + 1] = __ffma2_rn(xr[p + kw], whi, u[p][2 * q + 1]);
                         }
                     }
                 }
-#pragma unroll
-                for (int p = 0; p < 4; ++p)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) in[p][j] = __fadd_rn(in[p][j], sb[c0 + j]);
             }
         }
-        if (live) {
-            uint4* dst = reinterpret_cast<uint4*>(
-                out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0) * Cout + c0);
+        const float2* b2 = reinterpret_cast<const float2*>(sb + c0);
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                uint32_t bits = 0;
+        for (int p = 0; p < 4; ++p)
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    float vv = charge(v[p][j], df, sc, in[p][j]);
-                    const bool s = vv >= thr;
-                    v[p][j] = reset_v<HARD>(vv, s, thr, v_reset);
-                    bits |= (s ? 1u : 0u) << j;
-                }
-                dst[p * (Cout / 8)] = spikes_to_bf16x8(bits & 0xffu);
-                dst[p * (Cout / 8) + 1] = spikes_to_bf16x8(bits >> 8);
+            for (int j = 0; j < 8; ++j) u[p][j] = __fmul2_rn(sc2, __fadd2_rn(u[p][j], b2[j]));
+    };
+    // one LIF step of this thread's 64 neurons and the spike stores of frame t
+    auto lif = [&](int t) {
+        if (!live) return;
+        uint4* dst = reinterpret_cast<uint4*>(
+            out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0) * Cout + c0);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            uint32_t bits = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                // v = df * v + sc * in, each product and the sum rounded separately
+                const float2 vv = __fadd2_rn(__fmul2_rn(df2, v[p][j]), u[p][j]);
+                const bool s0 = vv.x >= thr, s1 = vv.y >= thr;
+                v[p][j] = make_float2(reset_v<HARD>(vv.x, s0, thr, v_reset),
+                                      reset_v<HARD>(vv.y, s1, thr, v_reset));
+                bits |= (s0 ? 1u : 0u) << (2 * j);
+                bits |= (s1 ? 1u : 0u) << (2 * j + 1);
             }
+            dst[p * (Cout / 8)] = spikes_to_bf16x8(bits & 0xffu);
+            dst[p * (Cout / 8) + 1] = spikes_to_bf16x8(bits >> 8);
         }
+    };
+    if (DIRECT) conv(0);                              // one input frame for every step
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[p][j] = make_float2(0.0f, 0.0f);
+    for (int t = 0; t < T; ++t) {
+        if (!DIRECT) {
+            if (t > 0) __syncthreads();               // previous step done with sx
+            conv(t);
+        }
+        lif(t);
     }
 }
 
@@ -322,7 +339,7 @@ extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_
         const int per_row = (int)(W / 4) * (int)(Cout / 16);
         const int R = per_row <= QUAD_THREADS ? QUAD_THREADS / per_row : 0;
         const int64_t nblk = B * ((H + (R ? R : 1) - 1) / (R ? R : 1));
-        const int64_t qsmem = (9 * Cin * Cout + Cout + Cin * (R + 2) * (W + 2)) * 4;
+        const int64_t qsmem = (9 * Cin * Cout + Cout + 2 * Cin * (R + 2) * (W + 2)) * 4;
         if (R >= 1 && nblk <= 0x7fffffffll && qsmem <= 64 * 1024) {
             auto quad = [&](auto kernel) -> int {
                 cudaError_t e = cudaFuncSetAttribute(
@@ -332,8 +349,11 @@ extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_
                                 (int)Ti, (int)T, (int)B, (int)Cin, (int)H, (int)W, R, w, bias,
                                 (int)Cout, decay, input_scale, v_threshold, v_reset, o);
             };
-            return hard_reset ? quad(first_conv_quad_kernel<true>)
-                              : quad(first_conv_quad_kernel<false>);
+            if (Ti == 1)
+                return hard_reset ? quad(first_conv_quad_kernel<true, true>)
+                                  : quad(first_conv_quad_kernel<false, true>);
+            return hard_reset ? quad(first_conv_quad_kernel<true, false>)
+                              : quad(first_conv_quad_kernel<false, false>);
         }
     }
     if (!pool && W >= 8 && W <= 128 && 128 % W == 0 && Cout % BAND_CG == 0 && Cout <= 128 &&
