@@ -92,6 +92,32 @@ int snnb_neuron_multistep(
     uint32_t* spikes_packed, float* count, float* v_out,
     snnb_stream_t stream);
 
+/* two-state / nonlinear neuron models of snnb_neuron_cuba_eif */
+#define SNNB_MODEL_CUBA  0
+#define SNNB_MODEL_EIF   1
+
+/*
+ * K2, second form -- multi-step CubaLIF or exponential IF over x [T, N] -> spikes of
+ * x's dtype.
+ *
+ * Replaces the Triton kernels and Python entry points
+ *   cuba_lif   snn_compiler/kernels/neurons.py:379-418 (_cuba_lif_kernel :143-194)
+ *   eif        snn_compiler/kernels/neurons.py:421-457 (_eif_kernel :200-261)
+ * following their eager restatements naive_cuba_lif / naive_eif (:505-557): per element n
+ * and step t, each operation rounded to float32 in this order (no FMA contraction):
+ *   CUBA:  i = a*i + input_scale*x;  v = b*v + i
+ *   EIF :  e = exp(min((v - v_rh) / delta_T, 16));  v = (a*v + delta_T*e) + input_scale*x
+ *   s = v >= thr;  soft: v -= s*thr;  hard: v = s ? v_reset : v
+ * (a = alpha, b = beta for CUBA; a = decay for EIF; i and v start at 0).  exp is CUDA's
+ * expf, which may differ from a CPU exp in the last bit.  thr modes and the channel index
+ * (c = n % C when channel_last, else (n / HW) % C) as for snnb_neuron_multistep.
+ */
+int snnb_neuron_cuba_eif(
+    const void* x, int x_dtype, int64_t T, int64_t N, int64_t C, int64_t HW, int channel_last,
+    int model, float a, float b, float input_scale, float delta_T, float v_rh,
+    int hard_reset, float v_reset, int thr_mode, float thr_scalar, const float* thr,
+    void* spikes, snnb_stream_t stream);
+
 /*
  * K4 -- bit packing of {0,1} or {-1,+1} rows into 32-bit words.
  *
@@ -143,9 +169,12 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *           64-channel slab loaded once per column tap with its halo rows and reused by
  *           the three row taps, the channel block's weights resident in shared memory
  *           (9 * ceil(Cin/64) * block_n <= 864; SNNB_ERR_UNSUPPORTED otherwise);
- *           4 = as 2 with two 128-row tiles per CTA sharing every weight stage (block_n <= 128).
- * block_n : output channels per CTA, 0 = choose, or 32 / 64 / 128 (dividing Cout), or 256
- *           with variant 2; 32 / 64 with variant 3.
+ *           4 = as 2 with two 128-row tiles per CTA sharing every weight stage (block_n <= 128);
+ *           5 = as 2 on CTA pairs (clusters of 2, M = 256 tcgen05 MMAs with cta_group::2):
+ *           each CTA stages its own 128-row tile and half of the block_n weight rows
+ *           (block_n 64 / 128 / 256).
+ * block_n : output channels per CTA (per CTA pair for variant 5), 0 = choose, or 32 / 64 /
+ *           128 (dividing Cout), or 256 with variants 2 and 5; 32 / 64 with variant 3.
  * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32
  *           partial sums go to `workspace` (caller-owned, >= snnb_split_workspace_bytes,
  *           16-byte aligned) and a second kernel adds them in a fixed order, adds the bias

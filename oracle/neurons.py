@@ -170,3 +170,120 @@ def naive_if_lif(x_seq, *, neuron="if", tau=2.0, decay=None, decay_input=True,
     if nhwc:
         s = s.permute(0, 1, 4, 2, 3)
     return s.to(x_seq.dtype)
+
+
+# ---- CubaLIF / EIF ------------------------------------------------------------------------
+# Restatement of the reference's eager naive_cuba_lif / naive_eif
+# (snn_compiler/kernels/neurons.py:505-534 and :537-557) in numpy float32: every product,
+# sum, difference and quotient is one IEEE float32 operation, evaluated in the reference's
+# order.  exp is numpy's float32 exp, which may differ from torch's or CUDA's in the last
+# bit; the tests allow spike flips only where the charged potential is that close to the
+# threshold.
+
+def _thr_per_neuron(thr, T, N, C, HW, channel_last):
+    if isinstance(thr, (int, float, np.floating)):
+        return np.full((N,), np.float32(thr), np.float32)
+    a = np.ascontiguousarray(thr, dtype=np.float32).reshape(-1)
+    if a.size == C and C != N:
+        n = np.arange(N, dtype=np.int64)
+        c = n % C if channel_last else (n // HW) % C
+        return a[c]
+    if a.size == N:
+        return a
+    raise ValueError(f"threshold of size {a.size} matches neither C={C} nor N={N}")
+
+
+def cuba_lif_multistep(x, *, alpha, beta, input_scale=1.0, hard_reset=True, v_reset=0.0,
+                       thr=1.0, C=1, HW=1, channel_last=False, want_vpre=False):
+    """x [T, N] float32 (memory order) -> {'spikes' [T, N] f32, 'vpre' [T, N] f32}:
+    i = alpha*i + input_scale*x; v = beta*v + i; s = v >= thr; reset."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, N = x.shape
+    a, b, sc = np.float32(alpha), np.float32(beta), np.float32(input_scale)
+    th = _thr_per_neuron(thr, T, N, C, HW, channel_last)
+    vr = np.float32(v_reset)
+    i = np.zeros((N,), np.float32)
+    v = np.zeros((N,), np.float32)
+    spikes = np.empty((T, N), np.float32)
+    vpre = np.empty((T, N), np.float32) if want_vpre else None
+    for t in range(T):
+        i = a * i + sc * x[t]
+        v = b * v + i
+        s = v >= th
+        spikes[t] = s
+        if want_vpre:
+            vpre[t] = v
+        v = np.where(s, vr, v) if hard_reset else np.where(s, v - th, v)
+    out = {"spikes": spikes}
+    if want_vpre:
+        out["vpre"] = vpre
+    return out
+
+
+def eif_multistep(x, *, decay, delta_T=1.0, v_rh=0.5, input_scale=1.0, hard_reset=True,
+                  v_reset=0.0, thr=1.0, C=1, HW=1, channel_last=False, want_vpre=False):
+    """x [T, N] float32 -> {'spikes', 'vpre'}:
+    v = (decay*v + delta_T*exp(min((v - v_rh)/delta_T, 16))) + input_scale*x."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, N = x.shape
+    df, dT, rh, sc = (np.float32(decay), np.float32(delta_T), np.float32(v_rh),
+                      np.float32(input_scale))
+    th = _thr_per_neuron(thr, T, N, C, HW, channel_last)
+    vr = np.float32(v_reset)
+    v = np.zeros((N,), np.float32)
+    spikes = np.empty((T, N), np.float32)
+    vpre = np.empty((T, N), np.float32) if want_vpre else None
+    with np.errstate(over="ignore"):
+        for t in range(T):
+            e = np.exp(np.minimum((v - rh) / dT, np.float32(16.0)))
+            v = (df * v + dT * e) + sc * x[t]
+            s = v >= th
+            spikes[t] = s
+            if want_vpre:
+                vpre[t] = v
+            v = np.where(s, vr, v) if hard_reset else np.where(s, v - th, v)
+    out = {"spikes": spikes}
+    if want_vpre:
+        out["vpre"] = vpre
+    return out
+
+
+def cuba_eif_params(model, **kw):
+    """(a, b) of the reference's derivation: CubaLIF alpha = exp(-dt/tau_syn),
+    beta = exp(-dt/tau_mem) (neurons.py:511-512); EIF decay = 1 - 1/tau (:541)."""
+    import math
+    if model == "cuba":
+        dt = kw.get("dt", 1.0)
+        a = math.exp(-dt / kw.get("tau_syn", 2.0)) if kw.get("decay_syn") is None \
+            else float(kw["decay_syn"])
+        b = math.exp(-dt / kw.get("tau_mem", 4.0)) if kw.get("decay_mem") is None \
+            else float(kw["decay_mem"])
+        return a, b
+    tau = kw.get("tau", 2.0)
+    return ((1.0 - 1.0 / tau) if kw.get("decay") is None else float(kw["decay"])), 0.0
+
+
+def naive_cuba_eif(model, x_seq, *, want_vpre=False, layout="NCHW", **kw):
+    """Oracle counterpart of naive_cuba_lif / naive_eif (neurons.py:505-557) on a torch CPU
+    tensor [T, B, ...] in memory order; kw are the reference's keyword arguments.
+    Returns the oracle dict ('spikes' / 'vpre' as [T, N] float32)."""
+    import torch
+    x = x_seq.detach().to(torch.float32).contiguous()
+    T = x.shape[0]
+    C, HW = infer_C_HW(tuple(x.shape))
+    thr = kw.get("v_threshold", 1.0)
+    if isinstance(thr, torch.Tensor):
+        thr = thr.detach().to(torch.float32).reshape(-1).numpy()
+    elif isinstance(thr, np.ndarray) and thr.ndim > 0:
+        thr = thr.astype(np.float32).reshape(-1)
+    else:
+        thr = float(thr)
+    common = dict(input_scale=kw.get("input_scale", 1.0),
+                  hard_reset=not kw.get("soft_reset", False), v_reset=kw.get("v_reset", 0.0),
+                  thr=thr, C=C, HW=HW, channel_last=layout == "NHWC", want_vpre=want_vpre)
+    xf = x.reshape(T, -1).numpy()
+    a, b = cuba_eif_params(model, **kw)
+    if model == "cuba":
+        return cuba_lif_multistep(xf, alpha=a, beta=b, **common)
+    return eif_multistep(xf, decay=a, delta_T=kw.get("delta_T", 1.0), v_rh=kw.get("v_rh", 0.5),
+                         **common)

@@ -24,6 +24,12 @@ the CPU) and records, for seeded inputs:
                     calibrate_active), so the fixture is self-contained.
   ssa.npz           the reference test suite's mini Spikingformer block _RefSSA
                     (snn_compiler/tests/test_spike_attention.py:55-80) on spike input.
+  cuba_eif.npz      naive_cuba_lif / naive_eif (snn_compiler/kernels/neurons.py:505-557)
+                    over the matrix of snn_compiler/tests/test_correctness.py:111-155
+                    (soft/hard x v_reset) and the decay overrides of :294-328, plus
+                    per-channel thresholds.
+
+``--only NAME[,NAME]`` regenerates just the named fixtures (file stems).
 
 The fixtures are small; the tests that read them never need the reference.
 """
@@ -244,9 +250,73 @@ def ssa_case(ref_root):
     return rec
 
 
+def cuba_eif_cases(N):
+    """Reference naive_cuba_lif / naive_eif on seeded inputs; kwargs kept as JSON."""
+    import json
+    out = {}
+    idx = 0
+    seed = 900
+
+    def add(model, x, y, kw):
+        nonlocal idx
+        k = f"c{idx:04d}"
+        out[k + "_x"] = x.numpy()
+        out[k + "_y"] = y.numpy().astype(np.uint8)
+        out[k + "_model"] = np.asarray(model)
+        kw = dict(kw)
+        thr = kw.pop("v_threshold")
+        out[k + "_thr"] = thr.numpy() if isinstance(thr, torch.Tensor) else np.float32(thr)
+        out[k + "_kw"] = np.asarray(json.dumps(kw))
+        idx += 1
+
+    shapes = [(4, 2, 8, 4, 4), (8, 3, 16), (6, 2, 3, 5, 7)]
+    for shape in shapes:
+        for soft in (True, False):
+            for v_reset in (0.0, -0.3):
+                if soft and v_reset != 0.0:
+                    continue
+                # thresholds: scalar, per neuron, per channel (the reference's naive
+                # versions take a [C] threshold only for 5-D CubaLIF input)
+                for thr_mode in ("scalar", "per_n", "per_c"):
+                    if thr_mode == "per_c" and len(shape) != 5:
+                        continue
+                    seed += 1
+                    g = _gen(seed)
+                    x = torch.randn(*shape, generator=g)
+                    C = shape[2] if len(shape) == 5 else shape[-1]
+                    if thr_mode == "scalar":
+                        thr = 1.0
+                    elif thr_mode == "per_c":
+                        thr = torch.rand(C, generator=g) * 0.5 + 0.75
+                    else:
+                        thr = (torch.rand(*shape[1:], generator=g) * 0.5 + 0.75).reshape(-1)
+                    kw = dict(tau_syn=2.0, tau_mem=4.0, soft_reset=soft, v_threshold=thr,
+                              v_reset=v_reset)
+                    add("cuba", x, N.naive_cuba_lif(x, **kw), kw)
+                    if thr_mode == "per_c":
+                        continue
+                    kw = dict(tau=2.0, delta_T=1.0, v_rh=0.5, soft_reset=soft,
+                              v_threshold=thr, v_reset=v_reset)
+                    add("eif", x, N.naive_eif(x, **kw), kw)
+    for ds, dm in ((0.0, 0.9), (0.5, 0.5), (0.7, 0.3), (1.0, 0.8)):
+        seed += 1
+        x = torch.randn(4, 4, 16, 8, 8, generator=_gen(seed))
+        kw = dict(tau_syn=2.0, tau_mem=4.0, decay_syn=ds, decay_mem=dm, soft_reset=False,
+                  v_threshold=1.0, v_reset=0.0)
+        add("cuba", x, N.naive_cuba_lif(x, **kw), kw)
+    for d in (0.0, 0.5, 1.0):
+        seed += 1
+        x = torch.randn(4, 4, 16, 8, 8, generator=_gen(seed)) * 0.3
+        kw = dict(tau=2.0, decay=d, delta_T=1.0, v_rh=0.5, soft_reset=False,
+                  v_threshold=1.0, v_reset=0.0)
+        add("eif", x, N.naive_eif(x, **kw), kw)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default="")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -257,11 +327,17 @@ def main():
         naive_if_lif = staticmethod(N.naive_if_lif)
         fold_conv_bn = staticmethod(Fz.fold_conv_bn)
 
-    np.savez_compressed(os.path.join(HERE, "lif_cases.npz"), **lif_cases(_Ref))
-    np.savez_compressed(os.path.join(HERE, "fold_bn.npz"), **fold_case(_Ref))
-    np.savez_compressed(os.path.join(HERE, "bitpack.npz"), **bitpack_case(args.reference))
-    np.savez_compressed(os.path.join(HERE, "ssa.npz"), **ssa_case(args.reference))
-    np.savez_compressed(os.path.join(HERE, "vgg16_active.npz"), **vgg_case(_Ref))
+    makers = {
+        "lif_cases": lambda: lif_cases(_Ref),
+        "fold_bn": lambda: fold_case(_Ref),
+        "bitpack": lambda: bitpack_case(args.reference),
+        "ssa": lambda: ssa_case(args.reference),
+        "vgg16_active": lambda: vgg_case(_Ref),
+        "cuba_eif": lambda: cuba_eif_cases(N),
+    }
+    only = [n for n in args.only.split(",") if n] or list(makers)
+    for name in only:
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **makers[name]())
     print("golden fixtures written to", HERE)
 
 

@@ -73,7 +73,7 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
 
 VARIANTS = [(0, 0, 1), (1, 32, 1), (1, 128, 1), (2, 32, 1), (2, 64, 1), (2, 128, 1), (2, 256, 1),
             (2, 128, 3), (2, 256, 4), (3, 32, 1), (3, 64, 1), (4, 64, 1), (4, 128, 1),
-            (4, 128, 2)]
+            (4, 128, 2), (5, 64, 1), (5, 128, 1), (5, 256, 1), (5, 128, 2), (5, 256, 3)]
 
 
 @pytest.mark.parametrize("vb", VARIANTS)
@@ -85,7 +85,7 @@ def test_conv3x3_lif_against_oracle(geom, vb):
     variant, block_n, splits = vb
     if block_n and Cout % block_n:
         pytest.skip("block_n must divide Cout")
-    if variant in (2, 4) and T not in (2, 4, 8):
+    if variant in (2, 4, 5) and T not in (2, 4, 8):
         pytest.skip("T folding needs T in {2, 4, 8}")
     C = _C()
     if variant == 3 and block_n not in C.band_block_ns(H, Cin, Cout):
@@ -132,7 +132,7 @@ def test_conv3x3_soft_reset_and_if_neuron():
 
 
 @pytest.mark.parametrize("vb", [(0, 0, 1), (1, 64, 1), (2, 32, 1), (2, 128, 1), (2, 128, 2),
-                                (4, 128, 1), (4, 64, 2)])
+                                (4, 128, 1), (4, 64, 2), (5, 128, 1), (5, 64, 2), (5, 256, 1)])
 @pytest.mark.parametrize("TBKN", [(4, 64, 512, 4096), (4, 8, 4096, 256), (2, 130, 128, 96)])
 def test_linear_lif_against_oracle(TBKN, vb):
     T, B, K, N = TBKN

@@ -61,3 +61,39 @@ def test_fused_modules_construct_like_reference():
     assert c.bias is None and c.stride == (2, 2)
     lin = FusedLinearNeuron(32, 64)
     assert lin.weight.shape == (64, 32) and lin.bias.shape == (64,)
+
+
+def test_chunked_driver_passes_state_and_concatenates():
+    """run_chunked / ChunkedForward (reference snn_compiler/nn/chunked.py:33-79): chunks of
+    chunk_t steps, the state of one chunk handed to the next, outputs concatenated."""
+    import torch.nn as nn
+    from snn_compiler.nn import ChunkedForward, run_chunked
+
+    class Acc(nn.Module):                  # y_t = running sum over all steps so far
+        def forward(self, x):
+            return torch.cumsum(x, 0)
+
+        def forward_chunked(self, x, state):
+            s0 = torch.zeros_like(x[0]) if state is None else state["s"]
+            y = torch.cumsum(x, 0) + s0
+            return y, {"s": y[-1]}
+
+    x = torch.randn(11, 3, 5)
+    full = torch.cumsum(x, 0)
+    for chunk in (1, 4, 5, 11, 16):
+        assert torch.allclose(ChunkedForward(Acc(), chunk_t=chunk)(x), full, atol=1e-5)
+    calls = []
+    run_chunked(lambda xc, st: (calls.append(xc.shape[0]) or xc, st), x, chunk_t=4)
+    assert calls == [4, 4, 3]
+    plain = nn.Identity()
+    assert torch.equal(ChunkedForward(plain, chunk_t=2)(x), x)     # no forward_chunked
+
+
+def test_cuba_eif_modules_construct_like_reference():
+    """CubaLIFNode / EIFNode keep the reference's constructor arguments
+    (snn_compiler/nn/modules.py:88-154)."""
+    from snn_compiler.nn import CubaLIFNode, EIFNode
+    c = CubaLIFNode(tau_syn=3.0, decay_mem=0.8, v_threshold=torch.ones(4))
+    assert c.tau_syn == 3.0 and c.decay_mem == 0.8 and c.v_threshold.shape == (4,)
+    e = EIFNode(delta_T=0.5, v_rh=0.2, soft_reset=True)
+    assert e.delta_T == 0.5 and e.v_rh == 0.2 and e.soft_reset and e.v_threshold == 1.0

@@ -190,3 +190,92 @@ def test_bad_arguments_raise_like_reference():
         K.if_lif(x.cpu())
     with pytest.raises(AssertionError):
         K.if_lif(x.transpose(1, 2))
+
+
+# ---- CubaLIF / EIF (snnb_neuron_cuba_eif) ---------------------------------------------------
+from test_oracle_golden import CE, CE_CASES   # noqa: E402
+
+
+def _flip_ok(got, ref, vpre, th, exact):
+    """Spikes equal, or (EIF: CUDA expf vs numpy exp) different only where the charged
+    potential is within 1e-5 of the threshold, in at most 0.1% of the elements."""
+    if exact:
+        assert np.array_equal(got, ref), int((got != ref).sum())
+        return
+    bad = got != ref
+    near = np.abs(vpre - th) <= 1e-5
+    assert not (bad & ~near).any(), int((bad & ~near).sum())
+    assert bad.mean() <= 1e-3
+
+
+@pytest.mark.parametrize("k", CE_CASES)
+def test_cuba_eif_match_reference_golden(k):
+    import json
+    K = _nk()
+    x = torch.from_numpy(CE[k + "_x"])
+    ref = CE[k + "_y"].reshape(x.shape[0], -1)
+    model = CE[k + "_model"].item()
+    kw = json.loads(CE[k + "_kw"].item())
+    thr = CE[k + "_thr"]
+    thr_d = float(thr) if thr.ndim == 0 else torch.from_numpy(thr).to(DEV)
+    fn = K.cuba_lif if model == "cuba" else K.eif
+    out = fn(x.to(DEV), v_threshold=thr_d, **kw)
+    assert out.dtype == torch.float32 and out.shape == x.shape
+    got = out.cpu().numpy().reshape(ref.shape).astype(np.uint8)
+    kw["v_threshold"] = float(thr) if thr.ndim == 0 else thr
+    r = ON.naive_cuba_eif(model, x, want_vpre=True, **kw)
+    T, N = ref.shape
+    th = ON._thr_per_neuron(kw["v_threshold"], T, N, *ON.infer_C_HW(tuple(x.shape)), False)
+    _flip_ok(got, ref, r["vpre"], th[None, :], model == "cuba")
+
+
+@pytest.mark.parametrize("model", ["cuba", "eif"])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("shape,layout,thr_mode", [
+    ((4, 8, 64, 16, 16), "NCHW", "per_c"),
+    ((4, 8, 64, 16, 16), "NHWC", "per_c"),
+    ((6, 3, 5, 7, 9), "NCHW", "per_n"),        # ragged N: scalar path
+    ((16, 2, 40, 8, 8), "NCHW", "scalar"),
+])
+def test_cuba_eif_against_oracle(model, dtype, shape, layout, thr_mode):
+    K = _nk()
+    g = OP.gen(hash((model, dtype, shape, layout, thr_mode)) % 100000)
+    x = (torch.randn(*shape, generator=g) * (0.3 if model == "eif" else 1.0)).to(
+        getattr(torch, dtype))
+    C = shape[2]
+    if thr_mode == "scalar":
+        thr = 0.9
+    elif thr_mode == "per_c":
+        thr = torch.rand(C, generator=g) * 0.5 + 0.6
+    else:
+        thr = (torch.rand(*shape[1:], generator=g) * 0.5 + 0.6).reshape(-1)
+    kw = dict(soft_reset=(thr_mode != "per_c"), v_reset=-0.1 if thr_mode == "per_c" else 0.0)
+    if model == "cuba":
+        kw.update(tau_syn=3.0, tau_mem=5.0)
+    else:
+        kw.update(tau=2.5, delta_T=0.8, v_rh=0.4)
+    thr_d = thr if isinstance(thr, float) else thr.to(DEV)
+    fn = K.cuba_lif if model == "cuba" else K.eif
+    out = fn(x.to(DEV), v_threshold=thr_d, layout=layout, **kw)
+    assert out.dtype == x.dtype
+    r = ON.naive_cuba_eif(model, x.float(), want_vpre=True, layout=layout, v_threshold=thr, **kw)
+    T = shape[0]
+    got = out.float().cpu().numpy().reshape(T, -1).astype(np.uint8)
+    ref = r["spikes"].astype(np.uint8)
+    assert ref.sum() > 0
+    N = got.shape[1]
+    Cc, HW = ON.infer_C_HW(shape)
+    th = ON._thr_per_neuron(thr if isinstance(thr, float) else thr.numpy(), T, N, Cc, HW,
+                            layout == "NHWC")
+    _flip_ok(got, ref, r["vpre"], th[None, :], model == "cuba")
+
+
+def test_cuba_eif_bad_arguments():
+    K = _nk()
+    x = torch.randn(4, 2, 8, device=DEV)
+    with pytest.raises(AssertionError):
+        K.cuba_lif(x.transpose(1, 2))                       # non-contiguous
+    with pytest.raises(ValueError):
+        K.eif(x, v_threshold=torch.ones(5, device=DEV))     # neither C nor NCL
+    with pytest.raises(AssertionError):
+        K.cuba_lif(x.to(torch.int32))

@@ -57,7 +57,22 @@ struct ConvParams {
     float* partial;               // split-K: f32 partial sums [splits][T][B*H*W][Cout]
     int mtiles;                   // pixel tiles per channel block (band kernel)
     int ring, a_bytes, w_bytes;   // band kernel: A ring depth, bytes per A stage, weight bytes
+    const void* wq;               // the layer's weights in global memory, wq_bytes long
+    int64_t wq_bytes;
 };
+
+// Before waiting for the previous kernel: pull this CTA's share of the layer's weights
+// (which no kernel writes) into L2, so the first weight stages of every CTA hit L2 instead
+// of DRAM.  One thread, up to 64 KB per bulk prefetch.
+__device__ __forceinline__ void prefetch_weights_l2(const ConvParams& p) {
+    const int64_t per = ((p.wq_bytes + gridDim.x - 1) / gridDim.x + 15) & ~int64_t(15);
+    const int64_t b0 = per * blockIdx.x;
+    const int64_t b1 = b0 + per < p.wq_bytes ? b0 + per : p.wq_bytes;
+    for (int64_t b = b0; b + 16 <= b1; b += 65536) {
+        const int64_t n = (b1 - b < 65536 ? b1 - b : 65536) & ~int64_t(15);
+        tc::prefetch_l2(static_cast<const uint8_t*>(p.wq) + b, (uint32_t)n);
+    }
+}
 
 struct Tile {
     int w0, h0, img0, n0;
@@ -242,6 +257,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
     pdl_wait();
     pdl_trigger();
 
@@ -384,11 +400,11 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
 // then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
-template <int BN, int STAGES, int TS, int MH>
+template <int BN, int STAGES, int TS, int MH, int CG = 1>
 struct SmemTM {
     static constexpr int P = 128 / TS;
     static constexpr int NCH = BN / 32;
-    static constexpr int B_TILE = BN * 128;
+    static constexpr int B_TILE = BN / CG * 128;       // weight rows this CTA stages
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
     static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 128 x 33 f32
@@ -408,11 +424,19 @@ struct SmemTM {
 // weight stage, so every weight byte brought into shared memory feeds twice the MMAs --
 // these layers are bound by the L2 -> shared-memory stream of ~55 B/cycle per SM).  Each
 // tile has its own pair of TMEM accumulators (slot = (item & 1) * MH + h).
-template <int BN, int STAGES, int TS, bool HARD, int NP, int MH>
+// CG = 2: CTA pairs (clusters of 2) with M = 256 MMAs (cta_group::2).  A work item is two
+// consecutive M-tiles (one per CTA) x BN channels; each CTA stages its own A tile and half
+// of the BN weight rows, so per MMA cycle a CTA streams 2/3 (BN = 128) or 1/2 (BN = 256)
+// of the bytes of the single-CTA form.  The even CTA waits for both CTAs' bytes on its
+// full barrier and issues the MMAs; its commits arrive on both CTAs' barriers (stage free,
+// accumulator ready); both epilogues hand the accumulator back on the even CTA's barrier.
+template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1), 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
-    using S = SmemTM<BN, STAGES, TS, MH>;
+    constexpr bool PAIR = CG == 2;
+    static_assert(!PAIR || MH == 1, "CTA pairs take one M-tile each");
+    using S = SmemTM<BN, STAGES, TS, MH, CG>;
     constexpr int P = S::P, NCH = S::NCH;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -433,15 +457,20 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const int KB = p.taps * p.cin_blocks;
     const int splits = p.splits;
     const int num_items = p.num_tiles * splits;
-    constexpr uint32_t STAGE_TX = MH * A_TILE_BYTES + S::B_TILE;
+    // work items of this CTA (a pair walks its items together)
+    const int item0 = PAIR ? (int)(blockIdx.x / 2) : (int)blockIdx.x;
+    const int item_step = PAIR ? (int)(gridDim.x / 2) : (int)gridDim.x;
+    // bytes that complete a stage: this CTA's tiles, or both CTAs' for a pair
+    constexpr uint32_t STAGE_TX = CG * (MH * A_TILE_BYTES + S::B_TILE);
     constexpr uint32_t TMEM_COLS = 2 * MH * BN < 32 ? 32 : 2 * MH * BN;
     static_assert(2 * MH * BN <= 512, "accumulators exceed TMEM");
+    const uint32_t rank = PAIR ? tc::cluster_rank() : 0u;
     // M-tile h of a work item; false when the item's last tile lies past the layer (odd
     // tile count) -- its box reads zeros and the epilogue stores nothing
     auto half_tile = [&](int item, int h, Tile& tl) {
         const int tile2 = item / splits;
         const int nt = tile2 % p.n_tiles_n;
-        const int mt = (tile2 / p.n_tiles_n) * MH + h;
+        const int mt = (tile2 / p.n_tiles_n) * (MH * CG) + h + (int)rank;
         tl = decode_tile(mt * p.n_tiles_n + nt, p, BN);
         return mt < p.mtiles;
     };
@@ -457,7 +486,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
         for (int a = 0; a < 2 * MH; ++a) {
             tc::mbar_init(accf_bar(a), 1);
-            tc::mbar_init(acce_bar(a), 128);
+            // single CTA: every epilogue thread arrives; pair: one arrival per epilogue
+            // warp of either CTA, on the even CTA's barrier
+            tc::mbar_init(acce_bar(a), PAIR ? 8 : 128);
         }
         tc::mbar_init(done_bar, 1);
         *abort_flag = 0;
@@ -467,13 +498,21 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     }
     for (int i = threadIdx.x; i < TS * NCH * P; i += blockDim.x) smask[i] = 0u;
     if (warp == 1) {
-        tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
-        tc::tmem_relinquish();
+        if constexpr (PAIR) {
+            tc::tmem_alloc_pair(sbase + S::TMEM_OFF, TMEM_COLS);
+            tc::tmem_relinquish_pair();
+        } else {
+            tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
+            tc::tmem_relinquish();
+        }
     }
     tc::tc_fence_before();
     __syncthreads();
+    // a pair: both CTAs' barriers initialised before either signals the other's
+    if constexpr (PAIR) tc::cluster_sync();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
     pdl_wait();
     pdl_trigger();
 
@@ -483,7 +522,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         // whole schedule, as the MMA warp does)
         const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
         uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+        for (int item = item0; item < num_items; item += item_step) {
             Tile tl[MH];
 #pragma unroll
             for (int h = 0; h < MH; ++h) half_tile(item, h, tl[h]);
@@ -499,14 +538,25 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const int cb = kb - tap * p.cin_blocks;
                     const int r = p.taps == 9 ? tap / 3 : 1;
                     const int s = p.taps == 9 ? tap % 3 : 1;
-                    tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
+                    if constexpr (PAIR) {
+                        // both CTAs' bytes complete the even CTA's full barrier
+                        const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
+                        if (rank == 0) tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
+                        tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
+                                             cb * 64, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
+                                             tl[0].img0, 0);
+                        tc::tma_load_3d_pair(sbase + S::B_OFF + stage * S::B_TILE, &tmB, fb,
+                                             cb * 64, tap, tl[0].n0 + (int)rank * (BN / 2));
+                    } else {
+                        tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
 #pragma unroll
-                    for (int h = 0; h < MH; ++h)
-                        tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES, &tmA,
-                                        full_bar(stage), cb * 64, tl[h].w0 + s - 1,
-                                        tl[h].h0 + r - 1, tl[h].img0, 0);
-                    tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
-                                    cb * 64, tap, tl[0].n0);
+                        for (int h = 0; h < MH; ++h)
+                            tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
+                                            &tmA, full_bar(stage), cb * 64, tl[h].w0 + s - 1,
+                                            tl[h].h0 + r - 1, tl[h].img0, 0);
+                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
+                                        full_bar(stage), cb * 64, tap, tl[0].n0);
+                    }
                 }
                 __syncwarp();
                 if (!failed) {
@@ -516,18 +566,31 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
         }
         if (failed) {
-            // wait (bounded) for this producer's copies still in flight
+            // wait (bounded) for this producer's copies still in flight: on the full barrier,
+            // or for the odd CTA of a pair (whose copies complete on the even CTA's barrier)
+            // on the stage's release, which follows the MMAs that read them
             uint32_t gg = last_g;
-            for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP)
-                tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+            for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP) {
+                if (PAIR && rank != 0)
+                    tc::mbar_wait_warp(empty_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+                else
+                    tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+            }
             if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
+        }
+    } else if (warp == 1 && PAIR && rank != 0) {
+        // odd CTA of a pair: the even CTA issues every MMA; its last commit says that this
+        // CTA's TMEM and shared memory are no longer in use by the tensor pipe
+        if (!tc::mbar_wait_warp(done_bar, 0, 0) && lane == 0) {
+            atomicExch(p.status, SNNB_ERR_TIMEOUT);
+            *abort_flag = 1;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128 * CG, BN);
         int stage = 0;
         uint32_t phase = 0, it = 0, failed = 0;
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
+        for (int item = item0; item < num_items; item += item_step, ++it) {
             int k0, k1;
             krange(item % splits, k0, k1);
             const int a0 = (it & 1) * MH;            // this item's first accumulator slot
@@ -554,14 +617,21 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                                               (stage * MH + h) * A_TILE_BYTES);
                         const uint32_t dcol = tmem + (a0 + h) * BN;
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC, (kb > k0) || (k > 0));
+                        for (int k = 0; k < 4; ++k) {
+                            if constexpr (PAIR)
+                                tc::umma_bf16_pair(dcol, da + 2 * k, db + 2 * k, IDESC,
+                                                   (kb > k0) || (k > 0));
+                            else
+                                tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
+                                              (kb > k0) || (k > 0));
+                        }
                     }
                     if (kb + 1 < k1) {
                         failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
                         tc::tc_fence_after();
                     }
-                    tc::umma_commit(empty_bar(stage));
+                    if constexpr (PAIR) tc::umma_commit_pair(empty_bar(stage), 3);
+                    else tc::umma_commit(empty_bar(stage));
                 }
                 __syncwarp();
                 stage = nstage;
@@ -569,14 +639,20 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
             if (tc::elect_one()) {
 #pragma unroll
-                for (int h = 0; h < MH; ++h) tc::umma_commit(accf_bar(a0 + h));
+                for (int h = 0; h < MH; ++h) {
+                    if constexpr (PAIR) tc::umma_commit_pair(accf_bar(a0 + h), 3);
+                    else tc::umma_commit(accf_bar(a0 + h));
+                }
             }
             __syncwarp();
             // lane 0 (the elected lane) owns the failure flag of the stage waits; the warp-wide
             // waits need the same skip value in every lane
             failed = __shfl_sync(0xffffffffu, failed, 0);
         }
-        if (tc::elect_one()) tc::umma_commit(done_bar);
+        if (tc::elect_one()) {
+            if constexpr (PAIR) tc::umma_commit_pair(done_bar, 3);
+            else tc::umma_commit(done_bar);
+        }
         __syncwarp();
         failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
@@ -588,7 +664,17 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         constexpr int NCOL = 32 / TS;
         const int64_t npix_total = (int64_t)p.B * p.H * p.W;
         uint32_t it = 0, failed = 0;
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
+        // hand accumulator a back to the MMA issuer (of the even CTA, for a pair)
+        auto release_acc = [&](int a) {
+            tc::tc_fence_before();
+            if constexpr (PAIR) {
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_cluster(tc::map_to_rank(acce_bar(a), 0));
+            } else {
+                tc::mbar_arrive(acce_bar(a));
+            }
+        };
+        for (int item = item0; item < num_items; item += item_step, ++it) {
           for (int h = 0; h < MH; ++h) {
             Tile tl;
             half_tile(item, h, tl);
@@ -616,8 +702,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             d4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
                     }
                 }
-                tc::tc_fence_before();
-                tc::mbar_arrive(acce_bar(a));
+                release_acc(a);
                 continue;
             }
 #pragma unroll 1
@@ -625,10 +710,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 float r[32];
                 tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32, r);
                 tc::tmem_wait_ld();
-                if (c == NCH - 1) {           // accumulator fully read: hand it back
-                    tc::tc_fence_before();
-                    tc::mbar_arrive(acce_bar(a));
-                }
+                if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
 #pragma unroll
                 for (int j = 0; j < 32; ++j) ybuf[row * 33 + j] = r[j];
                 tc::named_bar_sync(1, 128);
@@ -673,9 +755,13 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     }
     tc::tc_fence_before();
     __syncthreads();
+    // a pair: neither CTA leaves (or frees TMEM) while the other may still signal its
+    // barriers or have its shared memory read by the tensor pipe
+    if constexpr (PAIR) tc::cluster_sync();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, TMEM_COLS);
+        if constexpr (PAIR) tc::tmem_dealloc_pair(tmem, TMEM_COLS);
+        else tc::tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -771,6 +857,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
     pdl_wait();
     pdl_trigger();
 
@@ -1189,6 +1276,33 @@ int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorM
     return launch_k(kernel, dim3(grid), dim3(threads), smem, s, ta, tb, p);
 }
 
+// Persistent launch of a CTA-pair kernel: clusters of 2, as many as can be resident at
+// once (pairs sit on the two SMs of a TPC, so this can be below half the SM count).
+template <typename K>
+int launch_persistent_pair(K kernel, int smem, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const ConvParams& p, cudaStream_t s, int threads) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    const int64_t items = (int64_t)p.num_tiles * (p.splits > 1 ? p.splits : 1);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * (sm_count() / 2)));
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (clusters < 1) return SNNB_ERR_UNSUPPORTED;
+    const int pairs = (int)(items < clusters ? items : clusters);
+    return launch_kc(kernel, dim3(2 * pairs), dim3(threads), smem, s, 2u, ta, tb, p);
+}
+
 // Ring depths fill the ~227 KB of shared memory: at these tile sizes one k-slab of MMAs
 // (0.1-0.4 us) is far shorter than a TMA round trip, so depth is what keeps the tensor
 // pipe fed.
@@ -1204,13 +1318,32 @@ int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParam
     constexpr int dyn = SmemTM<BN, STAGES, TS, MH>::DYN;
     constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
     constexpr int threads = THREADS + 32 * (NP - 1);
-    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH>, dyn, ta, tb, p, s, threads)
-                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH>, dyn, ta, tb, p, s, threads);
+    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH, 1>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH, 1>, dyn, ta, tb, p, s, threads);
+}
+
+// CTA-pair form: each CTA stages A (16 KB) + BN/2 weight rows per k-slab.
+template <int BN, int STAGES, int TS>
+int launch_conv_tm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+                        cudaStream_t s) {
+    constexpr int dyn = SmemTM<BN, STAGES, TS, 1, 2>::DYN;
+    constexpr int NP = BN == 256 ? 2 : 3;
+    constexpr int threads = THREADS + 32 * (NP - 1);
+    return p.hard ? launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 2>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 2>, dyn, ta, tb, p, s, threads);
 }
 
 template <int TS>
 int launch_tm_bn(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
-                 cudaStream_t s, int mh = 1) {
+                 cudaStream_t s, int mh = 1, int cg = 1) {
+    if (cg == 2) {
+        switch (BN) {
+            case 256: return launch_conv_tm_pair<256, 6, TS>(ta, tb, p, s);
+            case 128: return launch_conv_tm_pair<128, 8, TS>(ta, tb, p, s);
+            case 64: return launch_conv_tm_pair<64, 9, TS>(ta, tb, p, s);
+            default: return SNNB_ERR_UNSUPPORTED;
+        }
+    }
     if (mh == 2) {
         switch (BN) {
             case 128: return launch_conv_tm<128, 4, TS, 2>(ta, tb, p, s);
@@ -1378,6 +1511,7 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     p.taps = 9; p.cin_blocks = CB; p.pool = pool;
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
+    p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
     p.splits = 1; p.partial = nullptr;
     p.ring = ring; p.a_bytes = a_bytes; p.w_bytes = w_bytes;
     const int dyn = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes)
@@ -1406,11 +1540,17 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
     if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    if (variant < 0 || variant > 4) return SNNB_ERR_ARG;
+    if (variant < 0 || variant > 5) return SNNB_ERR_ARG;
     // variant 4: T folded into M with two M-tiles per CTA sharing each weight stage
     const int mh = variant == 4 ? 2 : 1;
     if (variant == 4) {
         if (block_n == 256) return SNNB_ERR_UNSUPPORTED;      // 2 x 2 x 256 TMEM columns
+        variant = 2;
+    }
+    // variant 5: T folded into M, CTA pairs with M = 256 MMAs (cta_group::2)
+    const int cg = variant == 5 ? 2 : 1;
+    if (variant == 5) {
+        if (block_n == 32) return SNNB_ERR_UNSUPPORTED;       // 16 weight rows per CTA
         variant = 2;
     }
     if (block_n != 0 && block_n != 32 && block_n != 64 && block_n != 128 && block_n != 256)
@@ -1456,8 +1596,11 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         BN = bn_max;
         // narrower channel blocks until the grid covers the SMs
         if (mh == 2 && BN > 128) BN = 128;
-        while (BN > 32 && ((mtiles + mh - 1) / mh) * (Cout / BN) * splits < 148) BN /= 2;
+        const int bn_min = cg == 2 ? 64 : 32;
+        while (BN > bn_min && ((mtiles + mh * cg - 1) / (mh * cg)) * (Cout / BN) * splits * cg < 148)
+            BN /= 2;
     }
+    if (cg == 2 && BN < 64) return SNNB_ERR_UNSUPPORTED;
     if (splits > 1) {
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
         if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
@@ -1489,7 +1632,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     // weight map: dims (Cin, taps, Cout), box (64, 1, BN): channels past Cin read as zero
     const uint64_t bdims[3] = {(uint64_t)Cin, (uint64_t)taps, (uint64_t)Cout};
     const uint64_t bstr[2] = {(uint64_t)Cin * 2, (uint64_t)taps * Cin * 2};
-    const uint32_t bbox[3] = {64, 1, (uint32_t)BN};
+    const uint32_t bbox[3] = {64, 1, (uint32_t)(BN / cg)};   // a pair: half the rows per CTA
     rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
@@ -1501,17 +1644,18 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.taps = taps; p.cin_blocks = (Cin + 63) / 64; p.pool = pool;
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
+    p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
     p.splits = splits;
     p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
-    const int64_t ntiles = ((mtiles + mh - 1) / mh) * p.n_tiles_n;
+    const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
     p.mtiles = (int)mtiles;
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
     p.num_tiles = (int)ntiles;
     if (variant == 2) {
         switch (T) {
-            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh); break;
-            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh); break;
-            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh); break;
+            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;
+            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh, cg); break;
+            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh, cg); break;
         }
         if (rc != SNNB_OK || splits == 1) return rc;
         return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
@@ -1597,6 +1741,7 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     p.taps = 1; p.cin_blocks = (iK + 63) / 64; p.pool = 0;
     p.df = 0.f; p.sc = 0.f; p.thr = 0.f; p.v_reset = 0.f; p.hard = 1;
     p.bias = bias; p.out = nullptr; p.status = status;
+    p.wq = w; p.wq_bytes = (int64_t)iN * iK * 2;
     p.splits = 1;
     p.partial = out;
     p.mtiles = (int)mtiles;

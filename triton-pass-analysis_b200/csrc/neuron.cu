@@ -274,10 +274,147 @@ int launch_x(const NeuronParams& p, int spikes_dtype, bool vec, cudaStream_t s) 
     }
 }
 
+// ---- CubaLIF / EIF ---------------------------------------------------------------------
+// Same streaming structure as neuron_vec8_kernel (8 neurons per thread, 16-byte loads and
+// stores), with two state registers per neuron for CubaLIF and the exponential term for EIF.
+struct Neuron2Params {
+    const void* x;
+    const float* thr;
+    void* spikes;
+    int64_t T, N, C, HW;
+    float a, b, sc, delta_T, v_rh, v_reset, thr_scalar;
+    int thr_mode, channel_last;
+};
+
+__device__ __forceinline__ int64_t channel_of2(int64_t n, const Neuron2Params& p) {
+    return p.channel_last ? n % p.C : (n / p.HW) % p.C;
+}
+
+// One step of neuron n: returns the spike; i (CubaLIF synaptic current) and v updated.
+template <int MODEL, bool HARD>
+__device__ __forceinline__ bool step2(float& v, float& i, float x, float th, const Neuron2Params& p) {
+    if (MODEL == SNNB_MODEL_CUBA) {
+        i = __fadd_rn(__fmul_rn(p.a, i), __fmul_rn(p.sc, x));
+        v = __fadd_rn(__fmul_rn(p.b, v), i);
+    } else {
+        const float z = fminf(__fdiv_rn(__fsub_rn(v, p.v_rh), p.delta_T), 16.0f);
+        const float e = expf(z);
+        v = __fadd_rn(__fadd_rn(__fmul_rn(p.a, v), __fmul_rn(p.delta_T, e)), __fmul_rn(p.sc, x));
+    }
+    const bool s = v >= th;
+    v = reset_v<HARD>(v, s, th, p.v_reset);
+    return s;
+}
+
+__device__ __forceinline__ float thr_of(int64_t n, const Neuron2Params& p) {
+    if (p.thr_mode == SNNB_THR_SCALAR) return p.thr_scalar;
+    return p.thr_mode == SNNB_THR_PER_CHANNEL ? __ldg(p.thr + channel_of2(n, p)) : __ldg(p.thr + n);
+}
+
+template <typename TX, int MODEL, bool HARD>
+__global__ void __launch_bounds__(THREADS) neuron2_vec8_kernel(Neuron2Params p) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t n0 = ((int64_t)blockIdx.x * THREADS + threadIdx.x) * VEC;
+    if (n0 >= p.N) return;                 // N % VEC == 0: a vector is all in or all out
+    float v[VEC], cur[VEC], th[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        v[k] = 0.0f;
+        cur[k] = 0.0f;
+        th[k] = thr_of(n0 + k, p);
+    }
+    const TX* x = static_cast<const TX*>(p.x);
+    TX* sp = static_cast<TX*>(p.spikes);
+    float xc[VEC], xn[VEC];
+    load8(x + n0, xc);
+    for (int64_t t = 0; t < p.T; ++t) {
+        if (t + 1 < p.T) load8(x + (t + 1) * p.N + n0, xn);   // next step in flight
+        uint32_t bits = 0;
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+            bits |= (step2<MODEL, HARD>(v[k], cur[k], xc[k], th[k], p) ? 1u : 0u) << k;
+        store8(sp + t * p.N + n0, bits);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) xc[k] = xn[k];
+    }
+}
+
+template <typename TX, int MODEL, bool HARD>
+__global__ void __launch_bounds__(THREADS) neuron2_scalar_kernel(Neuron2Params p) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t n = (int64_t)blockIdx.x * THREADS + threadIdx.x;
+    if (n >= p.N) return;
+    const float th = thr_of(n, p);
+    float v = 0.0f, cur = 0.0f;
+    const TX* x = static_cast<const TX*>(p.x);
+    TX* sp = static_cast<TX*>(p.spikes);
+    for (int64_t t = 0; t < p.T; ++t) {
+        const bool s = step2<MODEL, HARD>(v, cur, to_f32(x[t * p.N + n]), th, p);
+        sp[t * p.N + n] = spike_value<TX>(s);
+    }
+}
+
+template <typename TX, int MODEL, bool HARD>
+int launch_neuron2_m(const Neuron2Params& p, bool vec, cudaStream_t s) {
+    if (vec) {
+        const int64_t blocks = ((p.N + VEC - 1) / VEC + THREADS - 1) / THREADS;
+        return launch_k(neuron2_vec8_kernel<TX, MODEL, HARD>, dim3((unsigned)blocks),
+                        dim3(THREADS), 0, s, p);
+    }
+    const int64_t blocks = (p.N + THREADS - 1) / THREADS;
+    return launch_k(neuron2_scalar_kernel<TX, MODEL, HARD>, dim3((unsigned)blocks),
+                    dim3(THREADS), 0, s, p);
+}
+
+template <typename TX>
+int launch_neuron2(const Neuron2Params& p, int model, bool hard, bool vec, cudaStream_t s) {
+    if (model == SNNB_MODEL_CUBA)
+        return hard ? launch_neuron2_m<TX, SNNB_MODEL_CUBA, true>(p, vec, s)
+                    : launch_neuron2_m<TX, SNNB_MODEL_CUBA, false>(p, vec, s);
+    return hard ? launch_neuron2_m<TX, SNNB_MODEL_EIF, true>(p, vec, s)
+                : launch_neuron2_m<TX, SNNB_MODEL_EIF, false>(p, vec, s);
+}
+
 }  // namespace
 }  // namespace snnb
 
 using namespace snnb;
+
+extern "C" int snnb_neuron_cuba_eif(
+    const void* x, int x_dtype, int64_t T, int64_t N, int64_t C, int64_t HW, int channel_last,
+    int model, float a, float b, float input_scale, float delta_T, float v_rh,
+    int hard_reset, float v_reset, int thr_mode, float thr_scalar, const float* thr,
+    void* spikes, snnb_stream_t stream)
+{
+    if (T < 0 || N < 0) return SNNB_ERR_ARG;
+    if (x_dtype != SNNB_F32 && x_dtype != SNNB_F16 && x_dtype != SNNB_BF16) return SNNB_ERR_ARG;
+    if (model != SNNB_MODEL_CUBA && model != SNNB_MODEL_EIF) return SNNB_ERR_ARG;
+    if (thr_mode != SNNB_THR_SCALAR && thr_mode != SNNB_THR_PER_CHANNEL &&
+        thr_mode != SNNB_THR_PER_NEURON) return SNNB_ERR_ARG;
+    if (thr_mode != SNNB_THR_SCALAR && thr == nullptr) return SNNB_ERR_ARG;
+    if (thr_mode == SNNB_THR_PER_CHANNEL && (C <= 0 || (!channel_last && HW <= 0)))
+        return SNNB_ERR_ARG;
+    if (N == 0 || T == 0) return SNNB_OK;
+    if (x == nullptr || spikes == nullptr) return SNNB_ERR_ARG;
+    if (T > (int64_t)1 << 40 || N > (int64_t)1 << 40) return SNNB_ERR_ARG;
+    if ((N + 255) / 256 > 0x7fffffffll) return SNNB_ERR_ARG;
+    Neuron2Params p;
+    p.x = x; p.thr = thr; p.spikes = spikes;
+    p.T = T; p.N = N; p.C = C > 0 ? C : 1; p.HW = HW > 0 ? HW : 1;
+    p.a = a; p.b = b; p.sc = input_scale; p.delta_T = delta_T; p.v_rh = v_rh;
+    p.v_reset = v_reset; p.thr_scalar = thr_scalar;
+    p.thr_mode = thr_mode; p.channel_last = channel_last ? 1 : 0;
+    const bool vec = (N % VEC == 0) && aligned16(x) && aligned16(spikes);
+    const bool hard = hard_reset != 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (x_dtype) {
+        case SNNB_F32: return launch_neuron2<float>(p, model, hard, vec, s);
+        case SNNB_F16: return launch_neuron2<__half>(p, model, hard, vec, s);
+        default: return launch_neuron2<__nv_bfloat16>(p, model, hard, vec, s);
+    }
+}
 
 extern "C" int snnb_neuron_multistep(
     const void* x, int x_dtype, int64_t T, int64_t N,

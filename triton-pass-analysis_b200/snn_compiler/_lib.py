@@ -28,6 +28,8 @@ F = ctypes.c_float
 SIGNATURES = {
     "snnb_neuron_multistep": [P, I32, I64, I64, P, P, I64, I64, I32, F, F, P, I32, F, I32, F, P,
                               P, P, I32, P, P, P, P],
+    "snnb_neuron_cuba_eif": [P, I32, I64, I64, I64, I64, I32, I32, F, F, F, F, F, I32, F, I32, F,
+                             P, P, P],
     "snnb_bitpack": [P, I32, I64, I64, I64, I32, P, P],
     "snnb_bgemm": [P, P, P, I64, I64, I64, I64, I32, I32, P],
     "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32,

@@ -34,8 +34,8 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
                 splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool).
     variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M, 3 row bands with halo reuse
-    and resident weights (band_block_ns), 4 = 2 with two M-tiles per CTA; block_n: 0 or
-    32/64/128/256;
+    and resident weights (band_block_ns), 4 = 2 with two M-tiles per CTA, 5 = 2 on CTA pairs
+    (M = 256 MMAs, half the weight rows staged per CTA); block_n: 0 or 32/64/128/256;
     splits > 1: split-K with float32 partials in `workspace` (allocated here if None)."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1:3] == (3, 3)
@@ -217,6 +217,15 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=()):
             s = 2
             while s <= max_splits and s <= kslabs // 2:
                 out.append((4, bn, s))
+                s *= 2
+    if T in (2, 4, 8):                # T folded, CTA pairs
+        for bn in (64, 128, 256):
+            if cout % bn:
+                continue
+            out.append((5, bn, 1))
+            s = 2
+            while s <= max_splits and s <= kslabs // 2:
+                out.append((5, bn, s))
                 s *= 2
     out.extend((3, bn, 1) for bn in band)
     return out

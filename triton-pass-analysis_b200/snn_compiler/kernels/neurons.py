@@ -4,6 +4,7 @@ Mirrors snn_compiler/kernels/neurons.py of the reference:
   if_lif          neurons.py:311-376   (argument meaning, parameter derivation
                                         :349-356, threshold resolution :267-292,
                                         AssertionError / ValueError behaviour)
+  cuba_lif, eif   neurons.py:379-457   (snnb_neuron_cuba_eif)
   NEURON_* / RESET_* / THR_* codes      neurons.py:58-68
 and adds ``plif`` (SpikingJelly ParametricLIFNode semantics restated in the
 reference's form: k = sigmoid(w), decay = 1 - k, input scale = k).
@@ -198,13 +199,103 @@ def plif(
                             v_reset=v_reset)["spikes"]
 
 
-def _unsupported(name):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(
-            f"{name} (reference neurons.py:379-461) is outside this build's hot path")
-    fn.__name__ = name
-    return fn
+MODEL_CUBA = 0
+MODEL_EIF = 1
 
 
-cuba_lif = _unsupported("cuba_lif")
-eif = _unsupported("eif")
+def _resolve_thr_layout(v_threshold, x_seq: torch.Tensor, layout: str):
+    """(mode, scalar, tensor, channel_last) as neurons.py:265-292 resolves them for
+    cuba_lif / eif: x_seq is contiguous and `layout` alone says whether the per-channel
+    index is n % C (NHWC) or (n // HW) % C; per-neuron thresholds are in memory order."""
+    nhwc = layout == "NHWC"
+    if isinstance(v_threshold, (int, float)):
+        return THR_SCALAR, float(v_threshold), None, nhwc
+    assert isinstance(v_threshold, torch.Tensor), type(v_threshold)
+    assert v_threshold.is_cuda and v_threshold.dtype == torch.float32 and v_threshold.is_contiguous()
+    if x_seq.ndim >= 4:
+        C = x_seq.shape[2]
+    elif x_seq.ndim == 3:
+        C = x_seq.shape[-1]
+    else:
+        C = 1
+    NCL = x_seq[0].numel()
+    if v_threshold.numel() == C:
+        return THR_PER_CHANNEL, 0.0, v_threshold, nhwc
+    if v_threshold.numel() == NCL:
+        return THR_PER_NEURON, 0.0, v_threshold, False
+    raise ValueError(f"v_threshold shape {tuple(v_threshold.shape)} matches neither C={C} "
+                     f"nor NCL={NCL}")
+
+
+def _infer_C_HW(x_seq: torch.Tensor):
+    """C and HW of the [T, B, C, ...] shape (neurons.py:295-308)."""
+    if x_seq.ndim == 5:
+        return x_seq.shape[2], x_seq.shape[3] * x_seq.shape[4]
+    if x_seq.ndim == 4:
+        return x_seq.shape[2], x_seq.shape[3]
+    if x_seq.ndim == 3:
+        return x_seq.shape[-1], 1
+    return 1, 1
+
+
+def _neuron2(x_seq, model, a, b, input_scale, delta_T, v_rh, soft_reset, v_threshold,
+             v_reset, layout):
+    assert x_seq.is_cuda and x_seq.is_contiguous()
+    assert x_seq.dtype in (torch.float32, torch.float16, torch.bfloat16)
+    T = x_seq.shape[0]
+    NCL = x_seq[0].numel()
+    C, HW = _infer_C_HW(x_seq)
+    mode, thr_s, thr_t, cl = _resolve_thr_layout(v_threshold, x_seq, layout)
+    spikes = torch.empty_like(x_seq)
+    st = _lib.lib().snnb_neuron_cuba_eif(
+        _lib.ptr(x_seq), _lib.dtype_code(x_seq.dtype), T, NCL, C, HW, int(cl), model,
+        float(a), float(b), float(input_scale), float(delta_T), float(v_rh),
+        0 if soft_reset else 1, float(v_reset), mode, thr_s, _lib.ptr(thr_t),
+        _lib.ptr(spikes), _lib.stream_of(x_seq))
+    _lib.check(st, "snnb_neuron_cuba_eif")
+    return spikes
+
+
+def cuba_lif(
+    x_seq: torch.Tensor,
+    *,
+    tau_syn: float = 2.0,
+    tau_mem: float = 4.0,
+    dt: float = 1.0,
+    decay_syn: float | None = None,
+    decay_mem: float | None = None,
+    input_scale: float = 1.0,
+    soft_reset: bool = False,
+    v_threshold=1.0,
+    v_reset: float = 0.0,
+    layout: str = "NCHW",
+) -> torch.Tensor:
+    """CubaLIF (reference neurons.py:379-418): synaptic current i and potential v,
+    i = alpha*i + input_scale*x, v = beta*v + i, with alpha = exp(-dt/tau_syn) and
+    beta = exp(-dt/tau_mem) unless decay_syn / decay_mem override them.  Spikes of
+    x_seq's dtype."""
+    alpha = math.exp(-dt / tau_syn) if decay_syn is None else float(decay_syn)
+    beta = math.exp(-dt / tau_mem) if decay_mem is None else float(decay_mem)
+    return _neuron2(x_seq, MODEL_CUBA, alpha, beta, input_scale, 1.0, 0.0, soft_reset,
+                    v_threshold, v_reset, layout)
+
+
+def eif(
+    x_seq: torch.Tensor,
+    *,
+    tau: float = 2.0,
+    decay: float | None = None,
+    delta_T: float = 1.0,
+    v_rh: float = 0.5,
+    input_scale: float = 1.0,
+    soft_reset: bool = False,
+    v_threshold=1.0,
+    v_reset: float = 0.0,
+    layout: str = "NCHW",
+) -> torch.Tensor:
+    """Exponential IF (reference neurons.py:421-457):
+    v = decay*v + delta_T*exp(min((v - v_rh)/delta_T, 16)) + input_scale*x with
+    decay = 1 - 1/tau unless given.  Spikes of x_seq's dtype."""
+    df = (1.0 - 1.0 / tau) if decay is None else float(decay)
+    return _neuron2(x_seq, MODEL_EIF, df, 0.0, input_scale, delta_T, v_rh, soft_reset,
+                    v_threshold, v_reset, layout)

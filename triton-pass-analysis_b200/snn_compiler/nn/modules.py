@@ -1,8 +1,9 @@
 """nn.Module API (SpikingJelly-style multi-step neurons), same as the reference.
 
 Mirrors snn_compiler/nn/modules.py of the reference:
-  IFNode :26-49, LIFNode :52-85, FusedAddNeuron :446-481, RateCodedLIFNode :487-522,
-  RateCodedIFNode :525-547, StatefulLIFNode :553-586
+  IFNode :26-49, LIFNode :52-85, CubaLIFNode :88-121, EIFNode :124-154,
+  FusedAddNeuron :446-481, RateCodedLIFNode :487-522, RateCodedIFNode :525-547,
+  StatefulLIFNode :553-586
 plus PLIFNode (SpikingJelly ParametricLIFNode: learnable w, k = sigmoid(w),
 init_tau = 2 -> w = 0).  Every module takes x_seq [T, B, ...] and returns
 [T, B, ...] spikes of x_seq's dtype; state is not kept between calls.
@@ -17,7 +18,7 @@ import torch.nn as nn
 
 from ..kernels.fused import (fused_bias_if_lif, fused_bias_if_lif_rate,
                              fused_bias_if_lif_stateful)
-from ..kernels.neurons import if_lif, plif
+from ..kernels.neurons import cuba_lif, eif, if_lif, plif
 
 
 def _store_threshold(mod, v_threshold):
@@ -65,6 +66,59 @@ class LIFNode(nn.Module):
                       tau=self.tau, decay=self.decay, decay_input=self.decay_input,
                       soft_reset=self.soft_reset, v_threshold=self.v_threshold,
                       v_reset=self.v_reset, layout=self.layout)
+
+
+class CubaLIFNode(nn.Module):
+    """Current-based LIF (two states): i = alpha*i + input_scale*x, v = beta*v + i, with
+    alpha = exp(-dt/tau_syn), beta = exp(-dt/tau_mem) unless decay_syn / decay_mem
+    override them (decay_syn = 0 gives a one-state LIF, decay_mem = 1 no membrane leak)."""
+
+    def __init__(self, *, tau_syn: float = 2.0, tau_mem: float = 4.0, dt: float = 1.0,
+                 decay_syn: float | None = None, decay_mem: float | None = None,
+                 input_scale: float = 1.0, soft_reset: bool = False,
+                 v_threshold=1.0, v_reset: float = 0.0, layout: str = "NCHW"):
+        super().__init__()
+        self.tau_syn = tau_syn
+        self.tau_mem = tau_mem
+        self.dt = dt
+        self.decay_syn = decay_syn
+        self.decay_mem = decay_mem
+        self.input_scale = input_scale
+        self.soft_reset = soft_reset
+        self.v_reset = v_reset
+        self.layout = layout
+        _store_threshold(self, v_threshold)
+
+    def forward(self, x_seq):
+        return cuba_lif(x_seq.contiguous(), tau_syn=self.tau_syn, tau_mem=self.tau_mem,
+                        dt=self.dt, decay_syn=self.decay_syn, decay_mem=self.decay_mem,
+                        input_scale=self.input_scale, soft_reset=self.soft_reset,
+                        v_threshold=self.v_threshold, v_reset=self.v_reset, layout=self.layout)
+
+
+class EIFNode(nn.Module):
+    """Exponential IF: v = decay*v + delta_T*exp(min((v - v_rh)/delta_T, 16)) + input_scale*x,
+    decay = 1 - 1/tau unless given."""
+
+    def __init__(self, *, tau: float = 2.0, decay: float | None = None,
+                 delta_T: float = 1.0, v_rh: float = 0.5, input_scale: float = 1.0,
+                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                 layout: str = "NCHW"):
+        super().__init__()
+        self.tau = tau
+        self.decay = decay
+        self.delta_T = delta_T
+        self.v_rh = v_rh
+        self.input_scale = input_scale
+        self.soft_reset = soft_reset
+        self.v_reset = v_reset
+        self.layout = layout
+        _store_threshold(self, v_threshold)
+
+    def forward(self, x_seq):
+        return eif(x_seq.contiguous(), tau=self.tau, decay=self.decay, delta_T=self.delta_T,
+                   v_rh=self.v_rh, input_scale=self.input_scale, soft_reset=self.soft_reset,
+                   v_threshold=self.v_threshold, v_reset=self.v_reset, layout=self.layout)
 
 
 class PLIFNode(nn.Module):
