@@ -190,6 +190,24 @@ int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W, 
                      snnb_stream_t stream);
 
 /*
+ * K1 with a residual input (ResNet / SEW-ResNet blocks): as snnb_conv3x3_lif without
+ * pooling, the neuron's input being (conv + bias) + residual.
+ *
+ * Replaces FusedConvBNAddNeuron.forward (snn_compiler/nn/modules.py:415-443: conv + BN, then
+ * fused_bias_if_lif with residual, fused.py:97-108).
+ * residual       : NHWC [T*B, H, W, Cout] (the output's layout) of residual_dtype
+ *                  (SNNB_BF16 or SNNB_F32), 16-byte aligned.
+ * variant        : 0, 1 (block_n <= 64) or 2 (any splits); 3, 4 and 5 return
+ *                  SNNB_ERR_UNSUPPORTED.
+ */
+int snnb_conv3x3_lif_res(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                         int64_t Cin, const void* w, const float* bias, int64_t Cout,
+                         float decay, float input_scale, float v_threshold, float v_reset,
+                         int hard_reset, const void* residual, int residual_dtype, int variant,
+                         int block_n, int splits, void* workspace, int64_t workspace_bytes,
+                         void* out, snnb_stream_t stream);
+
+/*
  * K1, linear variant: spikes [T*B, K] bf16 @ w [N, K] bf16 + bias -> multi-step LIF ->
  * bf16 spikes [T*B, N].  Replaces FusedLinearNeuron.forward
  * (snn_compiler/nn/modules.py:241-255: F.linear + fused_bias_if_lif).  K % 8 == 0,

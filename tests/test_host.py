@@ -97,3 +97,24 @@ def test_cuba_eif_modules_construct_like_reference():
     assert c.tau_syn == 3.0 and c.decay_mem == 0.8 and c.v_threshold.shape == (4,)
     e = EIFNode(delta_T=0.5, v_rh=0.2, soft_reset=True)
     assert e.delta_T == 0.5 and e.v_rh == 0.2 and e.soft_reset and e.v_threshold == 1.0
+
+
+def test_resnet_zoo_builds_and_fuses_on_cpu():
+    """ResNetSNN / SEWResNetSNN keep the reference's structure (zoo/resnet.py:120-213,
+    zoo/sew_resnet.py:134-199): fuse() swaps every block for fused modules -- standard
+    blocks end in FusedConvBNAddNeuron (residual before the neuron), SEW blocks in
+    FusedConvBNNeuron plus the element-wise connection (after the neuron)."""
+    from snn_compiler.nn import FusedConvBNAddNeuron, FusedConvBNNeuron
+    from snn_compiler.zoo import resnet18_snn, resnet34_snn, sew_resnet18_snn
+    m = resnet18_snn(num_classes=10, base_ch=32, fused=True)
+    assert len(m.blocks()) == 8 and isinstance(m.stem_fused, FusedConvBNNeuron)
+    assert all(isinstance(b.block2, FusedConvBNAddNeuron) for b in m.blocks())
+    assert m.layer2[0].downsample is not None and m.layer1[0].downsample is None
+    assert len(resnet34_snn(num_classes=10, base_ch=32).blocks()) == 16
+    s = sew_resnet18_snn(num_classes=10, base_ch=32, connect_f="and", fused=True)
+    blk = s.layer3[0]
+    assert blk.connect_f == "AND" and isinstance(blk.block2, FusedConvBNNeuron)
+    assert isinstance(blk.ds_block, FusedConvBNNeuron) and s.layer1[1].ds_block is None
+    from snn_compiler.zoo.sew_resnet import sew_connect
+    o, i = torch.tensor([0., 1., 1.]), torch.tensor([1., 1., 0.])
+    assert sew_connect(o, i, "IAND").tolist() == [1.0, 0.0, 0.0]

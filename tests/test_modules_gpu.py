@@ -118,6 +118,8 @@ def test_fused_conv_neuron_other_geometry_and_residual_form():
     flip_check(y, s, vpre)
     w, b = OV.fold_conv_bn(conv.weight.detach(), conv.bias.detach(), bn.weight.detach(),
                            bn.bias.detach(), bn.running_mean, bn.running_var, bn.eps)
+    # the residual form of a 3x3 / s1 / p1 conv runs on the tensor cores: bf16 weights
+    w = w.to(torch.bfloat16).float()
     with torch.no_grad():
         za = torch.nn.functional.conv2d(x.reshape(T * B, Cin, H, H), w, None, 1, 1) \
                   .reshape(T, B, Cout, H, H)

@@ -29,6 +29,7 @@
 // Every mbarrier wait is bounded; on timeout the CTA records SNNB_ERR_TIMEOUT, drains
 // its in-flight copies, frees its TMEM and returns.
 #include <mutex>
+#include <type_traits>
 
 #include "tc_common.cuh"
 
@@ -59,7 +60,55 @@ struct ConvParams {
     int ring, a_bytes, w_bytes;   // band kernel: A ring depth, bytes per A stage, weight bytes
     const void* wq;               // the layer's weights in global memory, wq_bytes long
     int64_t wq_bytes;
+    const void* res;              // residual input of the neuron or nullptr (no pooling then)
+    int res_f32;                  // residual dtype: float32 (1) or bf16 (0)
 };
+
+// Residual input of the neuron, added after the bias as the reference's fused kernel does
+// (x = y + b; x = x + residual: fused.py:97-108).  NHWC [T*B, H, W, Cout] of bf16 or
+// float32 -- the unpooled output's layout.  8 consecutive channels from element idx
+// (idx % 8 == 0: 16-byte aligned loads).
+__device__ __forceinline__ void load_res8(const void* res, int res_f32, int64_t idx,
+                                          float (&o)[8]) {
+    if (res_f32) {
+        const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(res) + idx);
+        const float4 a = __ldg(q), b = __ldg(q + 1);
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    } else {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+            static_cast<const __nv_bfloat16*>(res) + idx));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            o[2 * i] = __uint_as_float(w[i] << 16);
+            o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+}
+__device__ __forceinline__ float load_res1(const ConvParams& p, int64_t idx) {
+    return p.res_f32 ? __ldg(static_cast<const float*>(p.res) + idx)
+                     : __bfloat162float(static_cast<const __nv_bfloat16*>(p.res)[idx]);
+}
+__device__ __forceinline__ int64_t res_index(const ConvParams& p, int t, int on, int oh, int ow,
+                                             int ch) {
+    return ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) * p.Cout + ch;
+}
+// r[j] = (r[j] + bias[j]) + residual[j] over one 32-channel slice of one output pixel; the
+// bias is then consumed (set to 0) so the neuron's own "+ bias" adds nothing.
+__device__ __forceinline__ void add_res_slice(const ConvParams& p, int64_t idx, float (&r)[32],
+                                              float (&bias)[32]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        float rr[8];
+        load_res8(p.res, p.res_f32, idx + 8 * u, rr);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            r[8 * u + k] = __fadd_rn(__fadd_rn(r[8 * u + k], bias[8 * u + k]), rr[k]);
+            bias[8 * u + k] = 0.0f;
+        }
+    }
+}
 
 // Before waiting for the previous kernel: pull this CTA's share of the layer's weights
 // (which no kernel writes) into L2, so the first weight stages of every CTA hit L2 instead
@@ -369,6 +418,14 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         bb[4 * j] = b4.x; bb[4 * j + 1] = b4.y; bb[4 * j + 2] = b4.z; bb[4 * j + 3] = b4.w;
                     }
                     tc::tmem_wait_ld();
+                    // residual input: block_n <= 64 only (with v[128] in registers the
+                    // extra operands would spill)
+                    if (BN <= 64 && p.res) {
+                        const int x = m % p.bw, y = (m / p.bw) % p.bh, n = m / (p.bw * p.bh);
+                        const int ow = tl.w0 + x, oh = tl.h0 + y, on = tl.img0 + n;
+                        if (ow < p.W && oh < p.H && on < p.B)
+                            add_res_slice(p, res_index(p, t, on, oh, ow, tl.n0 + c * 32), r, bb);
+                    }
                     mk[c] = lif_slice<HARD>(r, bb, v + c * 32, p);
                 }
                 tc::tc_fence_before();
@@ -430,12 +487,15 @@ struct SmemTM {
 // of the bytes of the single-CTA form.  The even CTA waits for both CTAs' bytes on its
 // full barrier and issues the MMAs; its commits arrive on both CTAs' barriers (stage free,
 // accumulator ready); both epilogues hand the accumulator back on the even CTA's barrier.
-template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG>
+// RES: the neuron input also takes p.res (a separate instantiation: the residual loads in
+// the epilogue cost the plain form ~4% when compiled in behind a run-time test).
+template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1), 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
     constexpr bool PAIR = CG == 2;
     static_assert(!PAIR || MH == 1, "CTA pairs take one M-tile each");
+    static_assert(!RES || (MH == 1 && CG == 1), "residual input: one M-tile, single CTA");
     using S = SmemTM<BN, STAGES, TS, MH, CG>;
     constexpr int P = S::P, NCH = S::NCH;
     extern __shared__ uint8_t smem_raw[];
@@ -679,6 +739,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             Tile tl;
             half_tile(item, h, tl);
             const int a = (int)(it & 1) * MH + h;
+            // this thread's neuron pixel (for the residual input)
+            const int res_ow = RES ? tl.w0 + pp % p.bw : 0;
+            const int res_oh = RES ? tl.h0 + (pp / p.bw) % p.bh : 0;
+            const int res_on = RES ? tl.img0 + pp / (p.bw * p.bh) : 0;
+            const bool res_inside = RES && res_ow < p.W && res_oh < p.H && res_on < p.B;
             failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
             if (p.partial) {
@@ -717,21 +782,31 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 uint32_t bits[TS];
 #pragma unroll
                 for (int t = 0; t < TS; ++t) bits[t] = 0u;
+                // the neuron over this thread's columns; WITH_RES adds the residual input
+                auto lif_cols = [&](auto with_res) {
+                    constexpr bool WITH_RES = decltype(with_res)::value;
 #pragma unroll
-                for (int jj = 0; jj < NCOL; ++jj) {
-                    const int col = g * NCOL + jj;
-                    const float bb = __ldg(p.bias + tl.n0 + c * 32 + col);
-                    float v = 0.0f;
+                    for (int jj = 0; jj < NCOL; ++jj) {
+                        const int col = g * NCOL + jj;
+                        const float bb = __ldg(p.bias + tl.n0 + c * 32 + col);
+                        float v = 0.0f;
 #pragma unroll
-                    for (int t = 0; t < TS; ++t) {
-                        const float in = __fadd_rn(ybuf[(t * P + pp) * 33 + col], bb);
-                        float vv = charge(v, p.df, p.sc, in);
-                        const bool s = vv >= p.thr;
-                        vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                        v = vv;
-                        bits[t] |= (s ? 1u : 0u) << col;
+                        for (int t = 0; t < TS; ++t) {
+                            float in = __fadd_rn(ybuf[(t * P + pp) * 33 + col], bb);
+                            if constexpr (WITH_RES) {
+                                if (res_inside)
+                                    in = __fadd_rn(in, load_res1(p, res_index(p, t, res_on, res_oh, res_ow,
+                                                                              tl.n0 + c * 32 + col)));
+                            }
+                            float vv = charge(v, p.df, p.sc, in);
+                            const bool s = vv >= p.thr;
+                            vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
+                            v = vv;
+                            bits[t] |= (s ? 1u : 0u) << col;
+                        }
                     }
-                }
+                };
+                lif_cols(std::integral_constant<bool, RES>{});
 #pragma unroll
                 for (int t = 0; t < TS; ++t)
                     if (bits[t]) atomicOr(&smask[(t * NCH + c) * P + pp], bits[t]);
@@ -1138,7 +1213,7 @@ template <int S, bool POOL, bool HARD>
 __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     const float* __restrict__ partial, int T, int B, int H, int W, int C,
     const float* __restrict__ bias, float df, float sc, float thr, float v_reset,
-    __nv_bfloat16* __restrict__ out) {
+    const void* __restrict__ res, int res_f32, __nv_bfloat16* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
     constexpr int NP = POOL ? 4 : 1;
@@ -1191,8 +1266,16 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
                 y[6] = __fadd_rn(y[6], in[k][1].z); y[7] = __fadd_rn(y[7], in[k][1].w);
             }
 #pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], bb[j]);
+            if (!POOL && res) {              // residual input after the bias (no pooling then)
+                float rr[8];
+                load_res8(res, res_f32, ((((int64_t)t * B + b) * H + h) * W + w) * C + g * 8, rr);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], rr[j]);
+            }
+#pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float vv = charge(v[j], df, sc, __fadd_rn(y[j], bb[j]));
+                float vv = charge(v[j], df, sc, y[j]);
                 const bool sp = vv >= thr;
                 v[j] = reset_v<HARD>(vv, sp, thr, v_reset);
                 bits |= (sp ? 1u : 0u) << j;
@@ -1212,31 +1295,33 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
 template <int S>
 int launch_splitsum_lif_s(const float* partial, int T, int B, int H, int W, int C,
                           const float* bias, float df, float sc, float thr, float v_reset,
-                          int hard, int pool, __nv_bfloat16* out, cudaStream_t s) {
+                          int hard, int pool, const void* res, int res_f32,
+                          __nv_bfloat16* out, cudaStream_t s) {
     const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
     const int64_t threads = (int64_t)B * Ho * Wo * (C / 8) * (pool ? 4 : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     if (pool) {
-        if (hard) return launch_k(splitsum_lif_kernel<S, true, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
-        else return launch_k(splitsum_lif_kernel<S, true, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        if (hard) return launch_k(splitsum_lif_kernel<S, true, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, res, res_f32, out);
+        else return launch_k(splitsum_lif_kernel<S, true, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, res, res_f32, out);
     } else {
-        if (hard) return launch_k(splitsum_lif_kernel<S, false, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
-        else return launch_k(splitsum_lif_kernel<S, false, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, out);
+        if (hard) return launch_k(splitsum_lif_kernel<S, false, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, res, res_f32, out);
+        else return launch_k(splitsum_lif_kernel<S, false, false>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, res, res_f32, out);
     }
     return launch_status();
 }
 
 int launch_splitsum_lif(const float* partial, int S, int T, int B, int H, int W, int C,
                         const float* bias, float df, float sc, float thr, float v_reset, int hard,
-                        int pool, __nv_bfloat16* out, cudaStream_t s) {
+                        int pool, const void* res, int res_f32, __nv_bfloat16* out,
+                        cudaStream_t s) {
     switch (S) {
-        case 2: return launch_splitsum_lif_s<2>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 3: return launch_splitsum_lif_s<3>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 4: return launch_splitsum_lif_s<4>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 5: return launch_splitsum_lif_s<5>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 6: return launch_splitsum_lif_s<6>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 7: return launch_splitsum_lif_s<7>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
-        case 8: return launch_splitsum_lif_s<8>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, out, s);
+        case 2: return launch_splitsum_lif_s<2>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 3: return launch_splitsum_lif_s<3>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 4: return launch_splitsum_lif_s<4>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 5: return launch_splitsum_lif_s<5>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 6: return launch_splitsum_lif_s<6>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 7: return launch_splitsum_lif_s<7>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
+        case 8: return launch_splitsum_lif_s<8>(partial, T, B, H, W, C, bias, df, sc, thr, v_reset, hard, pool, res, res_f32, out, s);
         default: return SNNB_ERR_UNSUPPORTED;
     }
 }
@@ -1318,8 +1403,12 @@ int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParam
     constexpr int dyn = SmemTM<BN, STAGES, TS, MH>::DYN;
     constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
     constexpr int threads = THREADS + 32 * (NP - 1);
-    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH, 1>, dyn, ta, tb, p, s, threads)
-                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH, 1>, dyn, ta, tb, p, s, threads);
+    if (MH == 1 && p.res)
+        return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH, 1, MH == 1>, dyn, ta, tb, p, s, threads)
+                      : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH, 1, MH == 1>, dyn, ta, tb, p, s, threads);
+    if (p.res) return SNNB_ERR_UNSUPPORTED;
+    return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH, 1, false>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH, 1, false>, dyn, ta, tb, p, s, threads);
 }
 
 // CTA-pair form: each CTA stages A (16 KB) + BN/2 weight rows per k-slab.
@@ -1329,8 +1418,9 @@ int launch_conv_tm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Conv
     constexpr int dyn = SmemTM<BN, STAGES, TS, 1, 2>::DYN;
     constexpr int NP = BN == 256 ? 2 : 3;
     constexpr int threads = THREADS + 32 * (NP - 1);
-    return p.hard ? launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 2>, dyn, ta, tb, p, s, threads)
-                  : launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 2>, dyn, ta, tb, p, s, threads);
+    if (p.res) return SNNB_ERR_UNSUPPORTED;
+    return p.hard ? launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 2, false>, dyn, ta, tb, p, s, threads)
+                  : launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 2, false>, dyn, ta, tb, p, s, threads);
 }
 
 template <int TS>
@@ -1473,7 +1563,8 @@ int band_block_n(int W, int Cin, int Cout, int block_n) {
 
 int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                    const float* bias, int Cout, int BN, float df, float sc, float thr,
-                   float v_reset, int hard, int pool, void* out, int* status, cudaStream_t s) {
+                   float v_reset, int hard, int pool, const void* res, int res_f32, void* out,
+                   int* status, cudaStream_t s) {
     const int bh = 128 / W;
     if (pool && (bh % 2)) return SNNB_ERR_UNSUPPORTED;
     const int CB = (Cin + 63) / 64;
@@ -1512,6 +1603,7 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
+    p.res = res; p.res_f32 = res_f32;
     p.splits = 1; p.partial = nullptr;
     p.ring = ring; p.a_bytes = a_bytes; p.w_bytes = w_bytes;
     const int dyn = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes)
@@ -1533,8 +1625,10 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
 int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                  const float* bias, int Cout, int taps, float df, float sc, float thr,
                  float v_reset, int hard, int pool, int variant, int block_n, int splits,
-                 void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s) {
+                 void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s,
+                 const void* res = nullptr, int res_f32 = 0) {
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
+    if (res && (pool || !aligned16(res))) return res && pool ? SNNB_ERR_UNSUPPORTED : SNNB_ERR_ARG;
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
     if (Cin % 8 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
@@ -1561,13 +1655,13 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     const int KB = taps * ((Cin + 63) / 64);
     if (splits > KB) return SNNB_ERR_ARG;
     if (variant == 3) {
-        if (taps != 9 || splits > 1) return SNNB_ERR_UNSUPPORTED;
+        if (taps != 9 || splits > 1 || res) return SNNB_ERR_UNSUPPORTED;
         const int BN3 = band_block_n(W, Cin, Cout, block_n);
         if (!BN3) return SNNB_ERR_UNSUPPORTED;
         int* st = device_status_ptr();
         if (!st) return SNNB_ERR_CUDA;
         return run_band_layer(x, T, B, H, W, Cin, w, bias, Cout, BN3, df, sc, thr, v_reset, hard,
-                              pool, out, st, s);
+                              pool, res, res_f32, out, st, s);
     }
     const bool tm_ok = (T == 2 || T == 4 || T == 8);
     if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;
@@ -1588,6 +1682,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         }
     }
     if (variant == 1 && block_n == 256) return SNNB_ERR_UNSUPPORTED;   // v[] would not fit
+    if (variant == 1 && res && block_n == 128) return SNNB_ERR_UNSUPPORTED;
     const int P = variant == 2 ? 128 / T : 128;
     if (!choose_block(H, W, P, pool, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
     const int64_t mtiles = (int64_t)((W + bw - 1) / bw) * ((H + bh - 1) / bh) * ((B + bn - 1) / bn);
@@ -1601,6 +1696,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
             BN /= 2;
     }
     if (cg == 2 && BN < 64) return SNNB_ERR_UNSUPPORTED;
+    if (variant == 1 && res && BN > 64) BN = 64;     // residual operands: see conv_lif_kernel
     if (splits > 1) {
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
         if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
@@ -1645,6 +1741,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.df = df; p.sc = sc; p.thr = thr; p.v_reset = v_reset; p.hard = hard ? 1 : 0;
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
+    p.res = res; p.res_f32 = res_f32;
     p.splits = splits;
     p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
     const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
@@ -1659,7 +1756,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         }
         if (rc != SNNB_OK || splits == 1) return rc;
         return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
-                                   p.hard, pool, p.out, s);
+                                   p.hard, pool, res, res_f32, p.out, s);
     }
     switch (BN) {
         case 128: return launch_conv<128, 6>(ta, tb, p, s);
@@ -1685,6 +1782,24 @@ extern "C" int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, 
     return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout, 9, decay,
                         input_scale, v_threshold, v_reset, hard_reset, pool, variant, block_n,
                         splits, workspace, workspace_bytes, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int snnb_conv3x3_lif_res(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                                    int64_t Cin, const void* w, const float* bias, int64_t Cout,
+                                    float decay, float input_scale, float v_threshold,
+                                    float v_reset, int hard_reset, const void* residual,
+                                    int residual_dtype, int variant, int block_n, int splits,
+                                    void* workspace, int64_t workspace_bytes, void* out,
+                                    snnb_stream_t stream) {
+    if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
+        Cin > 0x7fffffff || Cout > 0x7fffffff)
+        return SNNB_ERR_ARG;
+    if (!residual || (residual_dtype != SNNB_BF16 && residual_dtype != SNNB_F32))
+        return SNNB_ERR_ARG;
+    return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout, 9, decay,
+                        input_scale, v_threshold, v_reset, hard_reset, 0, variant, block_n,
+                        splits, workspace, workspace_bytes, out, static_cast<cudaStream_t>(stream),
+                        residual, residual_dtype == SNNB_F32 ? 1 : 0);
 }
 
 extern "C" int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
@@ -1742,6 +1857,7 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     p.df = 0.f; p.sc = 0.f; p.thr = 0.f; p.v_reset = 0.f; p.hard = 1;
     p.bias = bias; p.out = nullptr; p.status = status;
     p.wq = w; p.wq_bytes = (int64_t)iN * iK * 2;
+    p.res = nullptr; p.res_f32 = 0;
     p.splits = 1;
     p.partial = out;
     p.mtiles = (int)mtiles;

@@ -31,8 +31,11 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
                 tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
                 v_threshold=1.0, v_reset: float = 0.0, pool: bool = False,
                 out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
-                splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                splits: int = 1, workspace: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None) -> torch.Tensor:
     """x [T, B, H, W, Cin] bf16 -> spikes [T, B, Ho, Wo, Cout] bf16 (Ho = H/2 when pool).
+    residual: None, or [T, B, H, W, Cout] bf16 / float32 added to conv + bias before the
+    neuron (no pooling; snnb_conv3x3_lif_res).
     variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M, 3 row bands with halo reuse
     and resident weights (band_block_ns), 4 = 2 with two M-tiles per CTA, 5 = 2 on CTA pairs
     (M = 256 MMAs, half the weight rows staged per CTA); block_n: 0 or 32/64/128/256;
@@ -49,6 +52,18 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     if out is None:
         out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
     ws, ws_bytes = _workspace(workspace, splits, T, B, H, W, Cout, x.device)
+    if residual is not None:
+        assert not pool, "residual input with pooling is not supported"
+        assert residual.is_cuda and residual.is_contiguous() and \
+            residual.dtype in (torch.bfloat16, torch.float32) and \
+            tuple(residual.shape) == (T, B, H, W, Cout), tuple(residual.shape)
+        st = _lib.lib().snnb_conv3x3_lif_res(
+            _lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias), Cout, df, sc, thr, vr,
+            hard, _lib.ptr(residual), _lib.dtype_code(residual.dtype), int(variant),
+            int(block_n), int(splits), _lib.ptr(ws), ws_bytes, _lib.ptr(out),
+            _lib.stream_of(x))
+        _lib.check(st, "snnb_conv3x3_lif_res")
+        return out
     st = _lib.lib().snnb_conv3x3_lif(_lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias),
                                      Cout, df, sc, thr, vr, hard, int(bool(pool)), int(variant),
                                      int(block_n), int(splits), _lib.ptr(ws), ws_bytes,

@@ -15,9 +15,11 @@ Routing (every launch is libsnnb200.so):
   - the same geometry on a float32 input with Cin % 8 != 0 (the image-input first layer):
     the float32 CUDA-core conv + neuron kernel;
   - linears with in_features % 8 == 0 and out_features % 32 == 0: the fused linear kernel;
-  - fold_bn=False, the residual form and any other conv geometry keep the reference's own
-    two-step structure: torch's conv (+ eval BN) followed by the fused neuron kernel
-    (snnb_neuron_multistep), exactly as modules.py:324-357 / :415-443 do.
+  - the residual form (FusedConvBNAddNeuron) on the first geometry: the same tcgen05 kernel
+    with the residual added in its epilogue (snnb_conv3x3_lif_res);
+  - fold_bn=False and any other conv geometry keep the reference's own two-step structure:
+    torch's conv (+ eval BN) followed by the fused neuron kernel (snnb_neuron_multistep),
+    exactly as modules.py:324-357 / :415-443 do.
 """
 from __future__ import annotations
 
@@ -62,9 +64,16 @@ def _fused_conv_ok(weight, stride, padding, dilation, groups, v_threshold):
             and isinstance(v_threshold, (int, float)))
 
 
-def _conv_lif(x_seq, weight, bias, layout, kw, cache):
-    """Fused conv + bias + neuron for a 3x3 / s1 / p1 conv.  `cache` holds the kernel-layout
-    weights so they are converted once per module, not per call."""
+def _res_frames(r):
+    """Residual [T, B, C, H, W] -> contiguous [T, B, H, W, C]: bf16 stays bf16 (spikes are
+    exact in it), any other dtype goes to float32 so no value is rounded."""
+    dt = torch.bfloat16 if r.dtype == torch.bfloat16 else torch.float32
+    return r.permute(0, 1, 3, 4, 2).to(dt).contiguous()
+
+
+def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None):
+    """Fused conv + bias (+ residual) + neuron for a 3x3 / s1 / p1 conv.  `cache` holds the
+    kernel-layout weights so they are converted once per module, not per call."""
     T, B, Cin = x_seq.shape[:3]
     Cout = weight.shape[0]
     b = bias.detach().float().contiguous() if bias is not None else \
@@ -74,8 +83,11 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache):
         if cache.get("key") != key:
             cache.clear()
             cache["key"], cache["w"] = key, KC.weight_khwc(weight)
-        y = KC.conv3x3_lif(KC._to_frames(x_seq), cache["w"], b, **kw)
+        res = None if residual is None else _res_frames(residual)
+        y = KC.conv3x3_lif(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
+    if residual is not None:
+        return None
     if x_seq.dtype == torch.float32 and Cout % 8 == 0:
         w = weight.detach().float().contiguous()
         y = KC.first_conv_lif(x_seq.contiguous(), w, b, T=T, **kw)
@@ -228,8 +240,9 @@ class FusedConvBNNeuron(_ConvBNBase):
 
 class FusedConvBNAddNeuron(_ConvBNBase):
     """Conv2d + BN + residual add + IF/LIF (reference modules.py:360-443):
-    spike = neuron(conv_bn(x) + bias + residual), the residual consumed inside the
-    neuron kernel's t loop."""
+    spike = neuron((conv_bn(x) + bias) + residual).  With folded BN on a 3x3 / s1 / p1 conv
+    the residual is read in the tensor-core kernel's epilogue (one launch); otherwise
+    torch's conv + BN runs first and the residual is consumed in the neuron kernel."""
 
     def __init__(self, conv: nn.Conv2d, bn: nn.BatchNorm2d, *, fold_bn: bool = True,
                  neuron: str = "if", tau: float = 2.0, decay: float | None = None,
@@ -239,6 +252,13 @@ class FusedConvBNAddNeuron(_ConvBNBase):
                          v_threshold, v_reset, layout)
 
     def forward(self, x_seq, residual_seq):
+        if self.fold_bn and _fused_conv_ok(self.weight, self.stride, self.padding,
+                                           self.dilation, self.groups, self.v_threshold) \
+                and tuple(residual_seq.shape[:2]) == tuple(x_seq.shape[:2]):
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+                          self._cache, residual=residual_seq)
+            if y is not None:
+                return y
         y, b = self._conv_bn(x_seq)
         return fused_bias_if_lif(y, b, residual=residual_seq, layout=self.layout,
                                  **self._neuron_kw())
