@@ -166,6 +166,21 @@ __device__ __forceinline__ void store_spikes(const ConvParams& p, const Tile& tl
     }
 }
 
+// NPT spikes (bits 0..NPT-1) as bf16 0/1 values at dst (2 * NPT bytes, aligned to them).
+template <int NPT>
+__device__ __forceinline__ void store_bits_bf16(__nv_bfloat16* dst, uint32_t bits) {
+    auto two = [](uint32_t b2) {
+        return ((b2 & 1u) ? 0x3F80u : 0u) | ((b2 & 2u) ? 0x3F800000u : 0u);
+    };
+    if constexpr (NPT == 8) {
+        *reinterpret_cast<uint4*>(dst) = spikes_to_bf16x8(bits);
+    } else if constexpr (NPT == 4) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(two(bits), two(bits >> 2));
+    } else {
+        *reinterpret_cast<uint32_t*>(dst) = two(bits);
+    }
+}
+
 // Producer drain after a failed wait: wait (bounded, whole warp) for the copies still in
 // flight -- the last min(stages, issued) stages before ring position (stage, phase).
 __device__ __forceinline__ void drain_ring_warp(uint32_t bar0, int stages, int stage,
@@ -464,9 +479,10 @@ struct SmemTM {
     static constexpr int B_TILE = BN / CG * 128;       // weight rows this CTA stages
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
-    static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 128 x 33 f32
-    static constexpr int MASK_OFF = Y_OFF + 128 * 33 * 4;               // TS x NCH x P u32
-    static constexpr int BAR_OFF = (MASK_OFF + TS * NCH * P * 4 + 7) & ~7;
+    static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 2 x 128 x 17 f32
+    static constexpr int MASK_OFF = Y_OFF + 2 * 128 * 17 * 4;           // 2 x 128 u32 (pool)
+    static constexpr int SB_OFF = MASK_OFF + 256 * 4;                  // BN f32 (bias)
+    static constexpr int BAR_OFF = (SB_OFF + BN * 4 + 7) & ~7;
     static constexpr int NBARS = 2 * STAGES + 4 * MH + 1;
     static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
     static constexpr int ABORT_OFF = TMEM_OFF + 4;
@@ -489,8 +505,11 @@ struct SmemTM {
 // accumulator ready); both epilogues hand the accumulator back on the even CTA's barrier.
 // RES: the neuron input also takes p.res (a separate instantiation: the residual loads in
 // the epilogue cost the plain form ~4% when compiled in behind a run-time test).
+// Two sets of 4 epilogue warps (warps 2-5 and 5+NP .. 8+NP) split every 32-column slice of
+// the accumulator into halves: the epilogue of a CTA's last work item, which no MMA
+// overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
 template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES>
-__global__ void __launch_bounds__(THREADS + 32 * (NP - 1), 1)
+__global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
     constexpr bool PAIR = CG == 2;
@@ -504,6 +523,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const uint32_t sbase = tc::smem_u32(smem);
     float* ybuf = reinterpret_cast<float*>(smem + S::Y_OFF);
     uint32_t* smask = reinterpret_cast<uint32_t*>(smem + S::MASK_OFF);
+    float* sbias = reinterpret_cast<float*>(smem + S::SB_OFF);
     const uint32_t bar0 = sbase + S::BAR_OFF;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
@@ -546,9 +566,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
         for (int a = 0; a < 2 * MH; ++a) {
             tc::mbar_init(accf_bar(a), 1);
-            // single CTA: every epilogue thread arrives; pair: one arrival per epilogue
-            // warp of either CTA, on the even CTA's barrier
-            tc::mbar_init(acce_bar(a), PAIR ? 8 : 128);
+            // single CTA: every epilogue thread arrives (2 sets of 128); pair: one arrival
+            // per epilogue warp of either CTA, on the even CTA's barrier
+            tc::mbar_init(acce_bar(a), PAIR ? 16 : 256);
         }
         tc::mbar_init(done_bar, 1);
         *abort_flag = 0;
@@ -556,7 +576,6 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         tc::prefetch_tmap(&tmA);
         tc::prefetch_tmap(&tmB);
     }
-    for (int i = threadIdx.x; i < TS * NCH * P; i += blockDim.x) smask[i] = 0u;
     if (warp == 1) {
         if constexpr (PAIR) {
             tc::tmem_alloc_pair(sbase + S::TMEM_OFF, TMEM_COLS);
@@ -576,7 +595,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     pdl_wait();
     pdl_trigger();
 
-    if (warp == 0 || warp >= 6) {
+    constexpr int W1 = 5 + NP;                    // first warp of the second epilogue set
+    if (warp == 0 || (warp >= 6 && warp < W1)) {
         // ------------------------------------------------------------- TMA producers
         // producer pi issues the stages g with g % NP == pi (g counts k-slabs over the
         // whole schedule, as the MMA warp does)
@@ -717,11 +737,16 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
-        const int q = warp & 3;
+        const int set = warp >= W1 ? 1 : 0;             // which half of each slice
+        const int q = warp & 3;                         // TMEM lane quadrant
         const int row = 32 * q + lane;
-        const int et = threadIdx.x - 64;
+        const int et = threadIdx.x - (set ? 32 * W1 : 64);   // 0..127 within the set
+        const int et2 = set * 128 + et;                 // 0..255 over both sets
         const int pp = et % P, g = et / P;              // pixel, column group (TS groups)
-        constexpr int NCOL = 32 / TS;
+        constexpr int HC = 16;                          // columns of a slice per set
+        constexpr int NPT = P / 8;                      // neurons (columns) per thread
+        constexpr int CG = HC / NPT;                    // threads per pixel
+        float* yb = ybuf + set * 128 * 17;
         const int64_t npix_total = (int64_t)p.B * p.H * p.W;
         uint32_t it = 0, failed = 0;
         // hand accumulator a back to the MMA issuer (of the even CTA, for a pair)
@@ -735,6 +760,15 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
         };
         for (int item = item0; item < num_items; item += item_step, ++it) {
+          if (!p.partial) {
+            // the channel block's bias into shared memory before the accumulator is ready
+            // (a global load after each slice's barrier would cost its latency per slice)
+            Tile t0;
+            half_tile(item, 0, t0);
+            tc::named_bar_sync(3, 256);              // both sets done with the last item's bias
+            for (int i = et2; i < BN; i += 256) sbias[i] = __ldg(p.bias + t0.n0 + i);
+            tc::named_bar_sync(3, 256);
+          }
           for (int h = 0; h < MH; ++h) {
             Tile tl;
             half_tile(item, h, tl);
@@ -757,73 +791,92 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 float* dst = p.partial + (((int64_t)split * p.T + t) * npix_total + gpix) * p.Cout + tl.n0;
 #pragma unroll 1
                 for (int c = 0; c < NCH; ++c) {
-                    float r[32];
-                    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32, r);
+                    float r[HC];
+                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
                     tc::tmem_wait_ld();
                     if (valid) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+                        float4* d4 = reinterpret_cast<float4*>(dst + c * 32 + set * HC);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
+                        for (int j = 0; j < HC / 4; ++j)
                             d4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
                     }
                 }
                 release_acc(a);
                 continue;
             }
+            // Neuron and stores: thread = (pixel lx, NPT consecutive columns of this set's
+            // half-slice), so a warp's store of one step covers whole 32-byte sectors
+            // (32 / CG pixels x 16 columns) and spikes go straight from registers to HBM.
+            const int lx = et / CG, cg = et % CG;
+            const int lw = lx % p.bw, lh = (lx / p.bw) % p.bh, ln = lx / (p.bw * p.bh);
+            const int ow = tl.w0 + lw, oh = tl.h0 + lh, on = tl.img0 + ln;
+            const bool inside = ow < p.W && oh < p.H && on < p.B;
+            const int Ho = p.H >> 1, Wo = p.W >> 1;
+            // pooled: the window's top-left thread stores (window inside the layer)
+            const bool pool_store = ((lw | lh) & 1) == 0 && (ow >> 1) < Wo && (oh >> 1) < Ho &&
+                                    on < p.B;
 #pragma unroll 1
             for (int c = 0; c < NCH; ++c) {
-                float r[32];
-                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32, r);
+                float r[HC];
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
                 tc::tmem_wait_ld();
                 if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
 #pragma unroll
-                for (int j = 0; j < 32; ++j) ybuf[row * 33 + j] = r[j];
-                tc::named_bar_sync(1, 128);
-                uint32_t bits[TS];
-#pragma unroll
-                for (int t = 0; t < TS; ++t) bits[t] = 0u;
+                for (int j = 0; j < HC; ++j) yb[row * 17 + j] = r[j];
+                tc::named_bar_sync(1 + set, 128);
+                uint32_t lb = 0;                    // bit t * NPT + jj: step t, column jj
                 // the neuron over this thread's columns; WITH_RES adds the residual input
                 auto lif_cols = [&](auto with_res) {
                     constexpr bool WITH_RES = decltype(with_res)::value;
 #pragma unroll
-                    for (int jj = 0; jj < NCOL; ++jj) {
-                        const int col = g * NCOL + jj;
-                        const float bb = __ldg(p.bias + tl.n0 + c * 32 + col);
+                    for (int jj = 0; jj < NPT; ++jj) {
+                        const int hcol = cg * NPT + jj;             // column within the half
+                        const int col = set * HC + hcol;           // column within the slice
+                        const float bb = sbias[c * 32 + col];
                         float v = 0.0f;
 #pragma unroll
                         for (int t = 0; t < TS; ++t) {
-                            float in = __fadd_rn(ybuf[(t * P + pp) * 33 + col], bb);
+                            float in = __fadd_rn(yb[(t * P + lx) * 17 + hcol], bb);
                             if constexpr (WITH_RES) {
-                                if (res_inside)
-                                    in = __fadd_rn(in, load_res1(p, res_index(p, t, res_on, res_oh, res_ow,
+                                if (inside)
+                                    in = __fadd_rn(in, load_res1(p, res_index(p, t, on, oh, ow,
                                                                               tl.n0 + c * 32 + col)));
                             }
                             float vv = charge(v, p.df, p.sc, in);
                             const bool s = vv >= p.thr;
                             vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
                             v = vv;
-                            bits[t] |= (s ? 1u : 0u) << col;
+                            lb |= (s ? 1u : 0u) << (t * NPT + jj);
                         }
                     }
                 };
                 lif_cols(std::integral_constant<bool, RES>{});
+                const int ch = tl.n0 + c * 32 + set * HC + cg * NPT;
+                if (!p.pool) {
+                    tc::named_bar_sync(1 + set, 128);    // yb free for the next slice
+                    if (inside) {
 #pragma unroll
-                for (int t = 0; t < TS; ++t)
-                    if (bits[t]) atomicOr(&smask[(t * NCH + c) * P + pp], bits[t]);
-                tc::named_bar_sync(1, 128);
+                        for (int t = 0; t < TS; ++t)
+                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
+                                                             p.Cout + ch,
+                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                    }
+                } else {
+                    // 2x2 max-pool = OR: the column neighbour is CG lanes away; the row
+                    // neighbour (bw pixels away, possibly another warp) through shared memory
+                    lb |= __shfl_xor_sync(0xffffffffu, lb, CG);
+                    smask[set * 128 + et] = lb;
+                    tc::named_bar_sync(1 + set, 128);    // yb free, row neighbours' bits visible
+                    lb |= smask[set * 128 + (et ^ (CG * p.bw))];
+                    if (pool_store) {
+#pragma unroll
+                        for (int t = 0; t < TS; ++t)
+                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * Ho + (oh >> 1)) * Wo +
+                                                          (ow >> 1)) * p.Cout + ch,
+                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                    }
+                }
             }
-            // ---- stores
-            const int npix = p.pool ? P / 4 : P;
-            for (int w_item = et; w_item < TS * npix * NCH; w_item += 128) {
-                const int c = w_item % NCH;
-                const int rest = w_item / NCH;
-                const int pix = rest % npix, t = rest / npix;
-                store_spikes(p, tl, t, c, pix,
-                             [&](int mm) { return smask[(t * NCH + c) * P + mm]; });
-            }
-            tc::named_bar_sync(1, 128);
-            for (int i = et; i < TS * NCH * P; i += 128) smask[i] = 0u;
-            tc::named_bar_sync(1, 128);
           }
         }
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
@@ -1402,7 +1455,7 @@ int launch_conv_tm(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParam
                    cudaStream_t s) {
     constexpr int dyn = SmemTM<BN, STAGES, TS, MH>::DYN;
     constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
-    constexpr int threads = THREADS + 32 * (NP - 1);
+    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
     if (MH == 1 && p.res)
         return p.hard ? launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, MH, 1, MH == 1>, dyn, ta, tb, p, s, threads)
                       : launch_persistent(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, MH, 1, MH == 1>, dyn, ta, tb, p, s, threads);
@@ -1417,7 +1470,7 @@ int launch_conv_tm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Conv
                         cudaStream_t s) {
     constexpr int dyn = SmemTM<BN, STAGES, TS, 1, 2>::DYN;
     constexpr int NP = BN == 256 ? 2 : 3;
-    constexpr int threads = THREADS + 32 * (NP - 1);
+    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
     if (p.res) return SNNB_ERR_UNSUPPORTED;
     return p.hard ? launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 2, false>, dyn, ta, tb, p, s, threads)
                   : launch_persistent_pair(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 2, false>, dyn, ta, tb, p, s, threads);
