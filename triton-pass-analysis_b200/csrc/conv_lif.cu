@@ -778,6 +778,17 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             const int res_oh = RES ? tl.h0 + (pp / p.bw) % p.bh : 0;
             const int res_on = RES ? tl.img0 + pp / (p.bw * p.bh) : 0;
             const bool res_inside = RES && res_ow < p.W && res_oh < p.H && res_on < p.B;
+            // (computed before the accumulator is ready) Neuron and stores: thread = (pixel lx, NPT consecutive columns of this set's
+            // half-slice), so a warp's store of one step covers whole 32-byte sectors
+            // (32 / CG pixels x 16 columns) and spikes go straight from registers to HBM.
+            const int lx = et / CG, cg = et % CG;
+            const int lw = lx % p.bw, lh = (lx / p.bw) % p.bh, ln = lx / (p.bw * p.bh);
+            const int ow = tl.w0 + lw, oh = tl.h0 + lh, on = tl.img0 + ln;
+            const bool inside = ow < p.W && oh < p.H && on < p.B;
+            const int Ho = p.H >> 1, Wo = p.W >> 1;
+            // pooled: the window's top-left thread stores (window inside the layer)
+            const bool pool_store = ((lw | lh) & 1) == 0 && (ow >> 1) < Wo && (oh >> 1) < Ho &&
+                                    on < p.B;
             failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
             if (p.partial) {
@@ -804,17 +815,6 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 release_acc(a);
                 continue;
             }
-            // Neuron and stores: thread = (pixel lx, NPT consecutive columns of this set's
-            // half-slice), so a warp's store of one step covers whole 32-byte sectors
-            // (32 / CG pixels x 16 columns) and spikes go straight from registers to HBM.
-            const int lx = et / CG, cg = et % CG;
-            const int lw = lx % p.bw, lh = (lx / p.bw) % p.bh, ln = lx / (p.bw * p.bh);
-            const int ow = tl.w0 + lw, oh = tl.h0 + lh, on = tl.img0 + ln;
-            const bool inside = ow < p.W && oh < p.H && on < p.B;
-            const int Ho = p.H >> 1, Wo = p.W >> 1;
-            // pooled: the window's top-left thread stores (window inside the layer)
-            const bool pool_store = ((lw | lh) & 1) == 0 && (ow >> 1) < Wo && (oh >> 1) < Ho &&
-                                    on < p.B;
 #pragma unroll 1
             for (int c = 0; c < NCH; ++c) {
                 float r[HC];
@@ -826,26 +826,35 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 tc::named_bar_sync(1 + set, 128);
                 uint32_t lb = 0;                    // bit t * NPT + jj: step t, column jj
                 // the neuron over this thread's columns; WITH_RES adds the residual input
+                // (steps outer, columns inner: the NPT recurrences interleave)
                 auto lif_cols = [&](auto with_res) {
                     constexpr bool WITH_RES = decltype(with_res)::value;
+                    float in[TS][NPT], v[NPT];
 #pragma unroll
                     for (int jj = 0; jj < NPT; ++jj) {
-                        const int hcol = cg * NPT + jj;             // column within the half
-                        const int col = set * HC + hcol;           // column within the slice
-                        const float bb = sbias[c * 32 + col];
-                        float v = 0.0f;
+                        const float bb = sbias[c * 32 + set * HC + cg * NPT + jj];
+                        v[jj] = 0.0f;
 #pragma unroll
-                        for (int t = 0; t < TS; ++t) {
-                            float in = __fadd_rn(yb[(t * P + lx) * 17 + hcol], bb);
-                            if constexpr (WITH_RES) {
-                                if (inside)
-                                    in = __fadd_rn(in, load_res1(p, res_index(p, t, on, oh, ow,
-                                                                              tl.n0 + c * 32 + col)));
-                            }
-                            float vv = charge(v, p.df, p.sc, in);
+                        for (int t = 0; t < TS; ++t)
+                            in[t][jj] = __fadd_rn(yb[(t * P + lx) * 17 + cg * NPT + jj], bb);
+                    }
+                    if constexpr (WITH_RES) {
+                        if (inside) {
+#pragma unroll
+                            for (int t = 0; t < TS; ++t)
+#pragma unroll
+                                for (int jj = 0; jj < NPT; ++jj)
+                                    in[t][jj] = __fadd_rn(in[t][jj], load_res1(p, res_index(
+                                        p, t, on, oh, ow, tl.n0 + c * 32 + set * HC + cg * NPT + jj)));
+                        }
+                    }
+#pragma unroll
+                    for (int t = 0; t < TS; ++t) {
+#pragma unroll
+                        for (int jj = 0; jj < NPT; ++jj) {
+                            float vv = charge(v[jj], p.df, p.sc, in[t][jj]);
                             const bool s = vv >= p.thr;
-                            vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                            v = vv;
+                            v[jj] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
                             lb |= (s ? 1u : 0u) << (t * NPT + jj);
                         }
                     }
