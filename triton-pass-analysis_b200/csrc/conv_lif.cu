@@ -1266,11 +1266,25 @@ __global__ void __launch_bounds__(256) splitsum_kernel(float* __restrict__ parti
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// Split-K finish in one pass: thread = (pixel, 8 channels).  Per step it loads the S
-// partial sums of its pixel at once, adds them in the order s = 0..S-1, adds the bias, runs
-// the neuron with v in registers and stores bf16 spikes [T][B][Ho][Wo][C].  With pooling the
-// four pixels of a 2x2 window are four adjacent lanes that OR their spike bits by shuffles;
-// the first of them stores the pooled spikes.
+// Split-K finish in one pass: thread = (pixel, 4 channels).  Per step it adds the S partial
+// sums of its pixel in the order s = 0..S-1 (the loads of step t+1 are in flight while step t
+// is computed), adds the bias (and the residual input), runs the neuron with v in registers
+// and stores bf16 spikes [T][B][Ho][Wo][C].  With pooling the four pixels of a 2x2 window are
+// four adjacent lanes that OR their spike bits by shuffles; the first of them stores the
+// pooled spikes.
+__device__ __forceinline__ void load_res4(const void* res, int res_f32, int64_t idx,
+                                          float (&o)[4]) {
+    if (res_f32) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(res) + idx));
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    } else {
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+            static_cast<const __nv_bfloat16*>(res) + idx));
+        o[0] = __uint_as_float(q.x << 16); o[1] = __uint_as_float(q.x & 0xffff0000u);
+        o[2] = __uint_as_float(q.y << 16); o[3] = __uint_as_float(q.y & 0xffff0000u);
+    }
+}
+
 template <int S, bool POOL, bool HARD>
 __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     const float* __restrict__ partial, int T, int B, int H, int W, int C,
@@ -1280,7 +1294,7 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     pdl_trigger();
     constexpr int NP = POOL ? 4 : 1;
     const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
-    const int groups = C / 8;
+    const int groups = C / 4;
     const int64_t total = (int64_t)B * Ho * Wo * groups * NP;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     // out-of-range lanes stay (no early exit) so the window shuffles see full warps; total
@@ -1297,46 +1311,40 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
     const int h = POOL ? 2 * oh + (q >> 1) : oh;
     const int w = POOL ? 2 * ow + (q & 1) : ow;
     const int64_t npix = (int64_t)B * H * W;
-    const int64_t split_stride = (int64_t)T * npix * C;
-    float bb[8], v[8];
+    const int64_t pix = ((int64_t)b * H + h) * W + w;
+    const int64_t split4 = (int64_t)T * npix * C / 4;        // one split, in float4
+    float bb[4] = {0.f, 0.f, 0.f, 0.f}, v[4] = {0.f, 0.f, 0.f, 0.f};
     if (valid) {
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + g * 8));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + g * 8) + 1);
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + g * 4));
         bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
-        bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
     }
+    auto load_step = [&](int t, float4 (&dst)[S]) {
+        const float4* src = reinterpret_cast<const float4*>(partial + ((int64_t)t * npix + pix) * C) + g;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        for (int k = 0; k < S; ++k) dst[k] = __ldcs(src + k * split4);
+    };
+    float4 cur[S], nxt[S];
+    if (valid) load_step(0, cur);
     for (int t = 0; t < T; ++t) {
+        if (valid && t + 1 < T) load_step(t + 1, nxt);
         uint32_t bits = 0;
         if (valid) {
-            const float4* src = reinterpret_cast<const float4*>(
-                partial + ((int64_t)t * npix + ((int64_t)b * H + h) * W + w) * C + g * 8);
-            float4 in[S][2];
-#pragma unroll
-            for (int k = 0; k < S; ++k) {          // all S loads in flight at once
-                in[k][0] = __ldcs(src + k * (split_stride / 4));
-                in[k][1] = __ldcs(src + k * (split_stride / 4) + 1);
-            }
-            float y[8] = {in[0][0].x, in[0][0].y, in[0][0].z, in[0][0].w,
-                          in[0][1].x, in[0][1].y, in[0][1].z, in[0][1].w};
+            float y[4] = {cur[0].x, cur[0].y, cur[0].z, cur[0].w};
 #pragma unroll
             for (int k = 1; k < S; ++k) {
-                y[0] = __fadd_rn(y[0], in[k][0].x); y[1] = __fadd_rn(y[1], in[k][0].y);
-                y[2] = __fadd_rn(y[2], in[k][0].z); y[3] = __fadd_rn(y[3], in[k][0].w);
-                y[4] = __fadd_rn(y[4], in[k][1].x); y[5] = __fadd_rn(y[5], in[k][1].y);
-                y[6] = __fadd_rn(y[6], in[k][1].z); y[7] = __fadd_rn(y[7], in[k][1].w);
+                y[0] = __fadd_rn(y[0], cur[k].x); y[1] = __fadd_rn(y[1], cur[k].y);
+                y[2] = __fadd_rn(y[2], cur[k].z); y[3] = __fadd_rn(y[3], cur[k].w);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], bb[j]);
+            for (int j = 0; j < 4; ++j) y[j] = __fadd_rn(y[j], bb[j]);
             if (!POOL && res) {              // residual input after the bias (no pooling then)
-                float rr[8];
-                load_res8(res, res_f32, ((((int64_t)t * B + b) * H + h) * W + w) * C + g * 8, rr);
+                float rr[4];
+                load_res4(res, res_f32, (((int64_t)t * B + b) * H * W + (int64_t)h * W + w) * C + g * 4, rr);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], rr[j]);
+                for (int j = 0; j < 4; ++j) y[j] = __fadd_rn(y[j], rr[j]);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 4; ++j) {
                 float vv = charge(v[j], df, sc, y[j]);
                 const bool sp = vv >= thr;
                 v[j] = reset_v<HARD>(vv, sp, thr, v_reset);
@@ -1348,9 +1356,11 @@ __global__ void __launch_bounds__(256) splitsum_lif_kernel(
             bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
         }
         if (valid && q == 0) {
-            const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 8;
-            *reinterpret_cast<uint4*>(out + o) = spikes_to_bf16x8(bits & 0xffu);
+            const int64_t o = ((((int64_t)t * B + b) * Ho + oh) * Wo + ow) * C + g * 4;
+            store_bits_bf16<4>(out + o, bits);
         }
+#pragma unroll
+        for (int k = 0; k < S; ++k) cur[k] = nxt[k];
     }
 }
 
@@ -1360,7 +1370,7 @@ int launch_splitsum_lif_s(const float* partial, int T, int B, int H, int W, int 
                           int hard, int pool, const void* res, int res_f32,
                           __nv_bfloat16* out, cudaStream_t s) {
     const int Ho = pool ? H / 2 : H, Wo = pool ? W / 2 : W;
-    const int64_t threads = (int64_t)B * Ho * Wo * (C / 8) * (pool ? 4 : 1);
+    const int64_t threads = (int64_t)B * Ho * Wo * (C / 4) * (pool ? 4 : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     if (pool) {
         if (hard) return launch_k(splitsum_lif_kernel<S, true, true>, dim3(blocks), dim3(256), 0, s, partial, T, B, H, W, C, bias, df, sc, thr, v_reset, res, res_f32, out);
