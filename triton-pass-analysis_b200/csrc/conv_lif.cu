@@ -136,35 +136,6 @@ __device__ __forceinline__ Tile decode_tile(int tile, const ConvParams& p, int B
     return Tile{tw * p.bw, th * p.bh, tn * p.bn, nt * BN};
 }
 
-// Spike bits of one (step, 32-channel slice) of the pixel block -> bf16 NHWC, pooled
-// (OR of each 2x2 window) or not; 64 bytes per (pixel, slice), 16-byte stores.
-// mask(pix) returns the 32-bit spike word of block pixel pix.
-template <typename MaskFn>
-__device__ __forceinline__ void store_spikes(const ConvParams& p, const Tile& tl, int t, int c,
-                                             int pix_item, MaskFn mask) {
-    if (p.pool) {
-        const int pw = p.bw / 2, ph = p.bh / 2;
-        const int xw = pix_item % pw, xh = (pix_item / pw) % ph, xn = pix_item / (pw * ph);
-        const int m00 = 2 * xw + p.bw * (2 * xh + p.bh * xn);
-        const uint32_t bits = mask(m00) | mask(m00 + 1) | mask(m00 + p.bw) | mask(m00 + p.bw + 1);
-        const int Ho = p.H / 2, Wo = p.W / 2;
-        const int ow = tl.w0 / 2 + xw, oh = tl.h0 / 2 + xh, on = tl.img0 + xn;
-        if (ow >= Wo || oh >= Ho || on >= p.B) return;
-        const int64_t base = ((((int64_t)t * p.B + on) * Ho + oh) * Wo + ow) * p.Cout + tl.n0 + c * 32;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + base);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
-    } else {
-        const int xw = pix_item % p.bw, xh = (pix_item / p.bw) % p.bh, xn = pix_item / (p.bw * p.bh);
-        const int ow = tl.w0 + xw, oh = tl.h0 + xh, on = tl.img0 + xn;
-        if (ow >= p.W || oh >= p.H || on >= p.B) return;
-        const uint32_t bits = mask(pix_item);
-        const int64_t base = ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) * p.Cout + tl.n0 + c * 32;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + base);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = spikes_to_bf16x8((bits >> (8 * k)) & 0xffu);
-    }
-}
 
 // NPT spikes (bits 0..NPT-1) as bf16 0/1 values at dst (2 * NPT bytes, aligned to them).
 template <int NPT>
@@ -463,11 +434,13 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 // 128 accumulator rows of a tile are TS steps x P = 128/TS pixels (row t*P + p), so the
 // grid is TS times larger and each tile runs the K loop once.  One 5-D TMA box per k-slab
 // (channels, w, h, image, step) lands the TS per-step pixel blocks in consecutive rows of
-// the A tile.  The epilogue stages each 32-column slice of the accumulator through shared
-// memory (row stride 33 words, conflict-free) so that a thread owns (pixel, columns) and
-// runs the T recurrence of those neurons itself; spike bits are OR-ed into per-(step,
-// slice, pixel) words, then stored.  Persistent, with two TMEM accumulators alternating
-// between consecutive work items of a CTA.
+// the A tile.  The epilogue (two sets of 4 warps, each taking 16 columns of every 32-column
+// slice) stages the accumulator through shared memory (row stride 17 words) so that a thread
+// owns (pixel, P/8 consecutive columns) and runs the T recurrence of those neurons itself,
+// then stores their spikes directly (a warp's store of one step covers whole 32-byte
+// sectors); 2x2 pooling ORs the column neighbour by a shuffle and the row neighbour through
+// one shared-memory word.  Persistent, with two TMEM accumulators alternating between
+// consecutive work items of a CTA.
 //
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
