@@ -99,9 +99,11 @@ class SpikingVGG:
         self.graphs = None
 
     # ---- per-layer launch plan -----------------------------------------------------------
-    def plan(self, img: torch.Tensor, *, per_step_logits: bool = False):
+    def plan(self, img: torch.Tensor, *, per_step_logits: bool = False,
+             out: torch.Tensor | None = None):
         """List of (name, flops, callable) for one forward over img [Ti, B, 3, H, W] f32.
-        Buffers are allocated once per (B, H, W) and reused."""
+        Buffers are allocated once per (B, H, W) and reused; ``out`` (optional) receives the
+        logits instead of the engine's own buffer."""
         Ti, B, Cin, H, W = img.shape
         T = self.T
         key = (B, H, W, per_step_logits)
@@ -120,7 +122,11 @@ class SpikingVGG:
             out = torch.empty((T, B, self.num_classes) if per_step_logits else (B, self.num_classes),
                               device=self.device, dtype=torch.float32)
             self._bufs[key] = (bufs, fbufs, out)
-        bufs, fbufs, out = self._bufs[key]
+        bufs, fbufs, own_out = self._bufs[key]
+        if out is None:
+            out = own_out
+        else:
+            assert out.shape == own_out.shape and out.dtype == own_out.dtype and out.is_contiguous()
         steps = []
         h, w = H, W
         x_prev = None
@@ -224,7 +230,7 @@ class SpikingVGG:
 
     # ---- CUDA graphs ----------------------------------------------------------------------
     def capture(self, img: torch.Tensor, *, split_at: int | None = None,
-                mark: int | None = None):
+                mark: int | None = None, out: torch.Tensor | None = None):
         """Capture the forward over the static input buffer ``img`` into CUDA graphs.
         With split_at=i the launches are split into three graphs [0, i), [i], (i, end) so
         that the i-th launch can be timed alone between replays.  With mark=i the forward is
@@ -232,7 +238,7 @@ class SpikingVGG:
         read them after a replay has completed).  Returns the output."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
-        steps, out = self.plan(img)
+        steps, out = self.plan(img, out=out)
         for _, _, fn in steps:            # warm up (sets kernel attributes, caches maps)
             fn()
         torch.cuda.synchronize()
