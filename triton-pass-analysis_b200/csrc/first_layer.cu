@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(1024) first_conv_band_kernel(
 constexpr int QUAD_THREADS = 128;
 
 template <bool HARD, bool DIRECT>
-__global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
+__global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_kernel(
     const float* __restrict__ x, int Ti, int T, int B, int Cin, int H, int W, int R,
     const float* __restrict__ w, const float* __restrict__ bias, int Cout,
     float df, float sc, float thr, float v_reset, __nv_bfloat16* __restrict__ out) {
@@ -295,7 +295,35 @@ __global__ void __launch_bounds__(QUAD_THREADS, 3) first_conv_quad_kernel(
             dst[p * (Cout / 8) + 1] = spikes_to_bf16x8(bits >> 8);
         }
     };
-    if (DIRECT) conv(0);                              // one input frame for every step
+    if (DIRECT) {
+        // one input frame for every step: each pixel's 16 neurons run their whole T
+        // recurrence at once (v for 16 neurons live, not 64: the kernel fits 4 CTAs per SM)
+        // and each (pixel, step) leaves as two 16-byte stores
+        conv(0);
+        if (!live) return;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            float2 vp[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vp[j] = make_float2(0.0f, 0.0f);
+            for (int t = 0; t < T; ++t) {
+                uint32_t bits = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float2 vv = __fadd2_rn(__fmul2_rn(df2, vp[j]), u[p][j]);
+                    const bool s0 = vv.x >= thr, s1 = vv.y >= thr;
+                    vp[j] = make_float2(reset_v<HARD>(vv.x, s0, thr, v_reset),
+                                        reset_v<HARD>(vv.y, s1, thr, v_reset));
+                    bits |= ((s0 ? 1u : 0u) | (s1 ? 2u : 0u)) << (2 * j);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(
+                    out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0 + p) * Cout + c0);
+                dst[0] = spikes_to_bf16x8(bits & 0xffu);
+                dst[1] = spikes_to_bf16x8(bits >> 8);
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int p = 0; p < 4; ++p)
 #pragma unroll
