@@ -431,15 +431,14 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
 // ---- variant 2: T folded into M -----------------------------------------------------------
 // For layers whose pixel count is too small to fill the GPU with 128-pixel blocks: the
-// 128 accumulator rows of a tile are TS steps x P = 128/TS pixels (row t*P + p), so the
+// 128 accumulator rows of a tile are P = 128/TS pixels x TS steps (row p*TS + t), so the
 // grid is TS times larger and each tile runs the K loop once.  One 5-D TMA box per k-slab
-// (channels, w, h, image, step) lands the TS per-step pixel blocks in consecutive rows of
-// the A tile.  The epilogue (two sets of 4 warps, each taking 16 columns of every 32-column
-// slice) stages the accumulator through shared memory (row stride 17 words) so that a thread
-// owns (pixel, P/8 consecutive columns) and runs the T recurrence of those neurons itself,
-// then stores their spikes directly (a warp's store of one step covers whole 32-byte
-// sectors); 2x2 pooling ORs the column neighbour by a shuffle and the row neighbour through
-// one shared-memory word.  Persistent, with two TMEM accumulators alternating between
+// (channels, step, w, h, image) lands each pixel's TS steps in consecutive rows of the A
+// tile.  The epilogue (two sets of 4 warps, each taking 16 columns of every 32-column slice)
+// finds a pixel's steps in TS adjacent lanes, transposes them in registers with shuffles so
+// that a lane owns 16/TS columns at every step, runs the T recurrence there and stores the
+// spikes directly (a warp's store of one step covers whole 32-byte sectors); 2x2 pooling ORs
+// the column neighbour by a shuffle and the row neighbour through one shared-memory word.  Persistent, with two TMEM accumulators alternating between
 // consecutive work items of a CTA.
 //
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
@@ -452,8 +451,7 @@ struct SmemTM {
     static constexpr int B_TILE = BN / CG * 128;       // weight rows this CTA stages
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
-    static constexpr int Y_OFF = B_OFF + STAGES * B_TILE;              // 2 x 128 x 17 f32
-    static constexpr int MASK_OFF = Y_OFF + 2 * 128 * 17 * 4;           // 2 x 128 u32 (pool)
+    static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;           // 2 x 128 u32 (pool)
     static constexpr int SB_OFF = MASK_OFF + 256 * 4;                  // BN f32 (bias)
     static constexpr int BAR_OFF = (SB_OFF + BN * 4 + 7) & ~7;
     static constexpr int NBARS = 2 * STAGES + 4 * MH + 1;
@@ -494,7 +492,6 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = tc::smem_u32(smem);
-    float* ybuf = reinterpret_cast<float*>(smem + S::Y_OFF);
     uint32_t* smask = reinterpret_cast<uint32_t*>(smem + S::MASK_OFF);
     float* sbias = reinterpret_cast<float*>(smem + S::SB_OFF);
     const uint32_t bar0 = sbase + S::BAR_OFF;
@@ -596,8 +593,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
                         if (rank == 0) tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
                         tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
-                                             cb * 64, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
-                                             tl[0].img0, 0);
+                                             cb * 64, 0, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
+                                             tl[0].img0);
                         tc::tma_load_3d_pair(sbase + S::B_OFF + stage * S::B_TILE, &tmB, fb,
                                              cb * 64, tap, tl[0].n0 + (int)rank * (BN / 2));
                     } else {
@@ -605,8 +602,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 #pragma unroll
                         for (int h = 0; h < MH; ++h)
                             tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
-                                            &tmA, full_bar(stage), cb * 64, tl[h].w0 + s - 1,
-                                            tl[h].h0 + r - 1, tl[h].img0, 0);
+                                            &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 + s - 1,
+                                            tl[h].h0 + r - 1, tl[h].img0);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
                                         full_bar(stage), cb * 64, tap, tl[0].n0);
                     }
@@ -712,14 +709,15 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     } else {
         const int set = warp >= W1 ? 1 : 0;             // which half of each slice
         const int q = warp & 3;                         // TMEM lane quadrant
-        const int row = 32 * q + lane;
+        const int row = 32 * q + lane;                  // accumulator row = pixel * TS + step
         const int et = threadIdx.x - (set ? 32 * W1 : 64);   // 0..127 within the set
         const int et2 = set * 128 + et;                 // 0..255 over both sets
-        const int pp = et % P, g = et / P;              // pixel, column group (TS groups)
         constexpr int HC = 16;                          // columns of a slice per set
-        constexpr int NPT = P / 8;                      // neurons (columns) per thread
-        constexpr int CG = HC / NPT;                    // threads per pixel
-        float* yb = ybuf + set * 128 * 17;
+        constexpr int NPT = HC / TS;                    // columns per thread after the transpose
+        // After the in-register transpose the TS lanes of a pixel (rows px*TS .. px*TS+TS-1)
+        // hold its TS steps of NPT consecutive columns each: lane k of the group owns columns
+        // k*NPT .. k*NPT+NPT-1 (of this set's 16) at every step.
+        const int lx = row / TS, kq = row % TS;
         const int64_t npix_total = (int64_t)p.B * p.H * p.W;
         uint32_t it = 0, failed = 0;
         // hand accumulator a back to the MMA issuer (of the even CTA, for a pair)
@@ -735,7 +733,6 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         for (int item = item0; item < num_items; item += item_step, ++it) {
           if (!p.partial) {
             // the channel block's bias into shared memory before the accumulator is ready
-            // (a global load after each slice's barrier would cost its latency per slice)
             Tile t0;
             half_tile(item, 0, t0);
             tc::named_bar_sync(3, 256);              // both sets done with the last item's bias
@@ -746,39 +743,27 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             Tile tl;
             half_tile(item, h, tl);
             const int a = (int)(it & 1) * MH + h;
-            // this thread's neuron pixel (for the residual input)
-            const int res_ow = RES ? tl.w0 + pp % p.bw : 0;
-            const int res_oh = RES ? tl.h0 + (pp / p.bw) % p.bh : 0;
-            const int res_on = RES ? tl.img0 + pp / (p.bw * p.bh) : 0;
-            const bool res_inside = RES && res_ow < p.W && res_oh < p.H && res_on < p.B;
-            // (computed before the accumulator is ready) Neuron and stores: thread = (pixel lx, NPT consecutive columns of this set's
-            // half-slice), so a warp's store of one step covers whole 32-byte sectors
-            // (32 / CG pixels x 16 columns) and spikes go straight from registers to HBM.
-            const int lx = et / CG, cg = et % CG;
+            // (before the accumulator is ready) this lane's pixel in the layer
             const int lw = lx % p.bw, lh = (lx / p.bw) % p.bh, ln = lx / (p.bw * p.bh);
             const int ow = tl.w0 + lw, oh = tl.h0 + lh, on = tl.img0 + ln;
             const bool inside = ow < p.W && oh < p.H && on < p.B;
             const int Ho = p.H >> 1, Wo = p.W >> 1;
-            // pooled: the window's top-left thread stores (window inside the layer)
+            // pooled: the window's top-left pixel stores (window inside the layer)
             const bool pool_store = ((lw | lh) & 1) == 0 && (ow >> 1) < Wo && (oh >> 1) < Ho &&
                                     on < p.B;
             failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
             if (p.partial) {
-                // ---- split-K: raw float32 partial sums of this split
+                // ---- split-K: raw float32 partial sums of this split, row = (pixel, step)
                 const int split = item % splits;
-                const int t = row / P, px = row % P;
-                const int xw = px % p.bw, xh = (px / p.bw) % p.bh, xn = px / (p.bw * p.bh);
-                const int ow = tl.w0 + xw, oh = tl.h0 + xh, on = tl.img0 + xn;
-                const bool valid = ow < p.W && oh < p.H && on < p.B;
                 const int64_t gpix = ((int64_t)on * p.H + oh) * p.W + ow;
-                float* dst = p.partial + (((int64_t)split * p.T + t) * npix_total + gpix) * p.Cout + tl.n0;
+                float* dst = p.partial + (((int64_t)split * p.T + kq) * npix_total + gpix) * p.Cout + tl.n0;
 #pragma unroll 1
                 for (int c = 0; c < NCH; ++c) {
                     float r[HC];
                     tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
                     tc::tmem_wait_ld();
-                    if (valid) {
+                    if (inside) {
                         float4* d4 = reinterpret_cast<float4*>(dst + c * 32 + set * HC);
 #pragma unroll
                         for (int j = 0; j < HC / 4; ++j)
@@ -794,48 +779,62 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
                 tc::tmem_wait_ld();
                 if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
+                // transpose across the TS lanes of the pixel: block j (NPT columns) of the
+                // lane with step t moves to the lane with k = j, slot t (butterfly over the
+                // bits of t; each stage swaps half of the blocks with the partner lane)
 #pragma unroll
-                for (int j = 0; j < HC; ++j) yb[row * 17 + j] = r[j];
-                tc::named_bar_sync(1 + set, 128);
-                uint32_t lb = 0;                    // bit t * NPT + jj: step t, column jj
-                // the neuron over this thread's columns; WITH_RES adds the residual input
-                // (steps outer, columns inner: the NPT recurrences interleave)
+                for (int bb = TS / 2; bb >= 1; bb >>= 1) {
+                    const bool hi = (kq & bb) != 0;
+#pragma unroll
+                    for (int j0 = 0; j0 < TS; ++j0) {
+                        if (j0 & bb) continue;
+                        const int j1 = j0 | bb;
+#pragma unroll
+                        for (int e = 0; e < NPT; ++e) {
+                            const float snd = hi ? r[j0 * NPT + e] : r[j1 * NPT + e];
+                            const float rcv = __shfl_xor_sync(0xffffffffu, snd, bb);
+                            if (hi) r[j0 * NPT + e] = rcv;
+                            else r[j1 * NPT + e] = rcv;
+                        }
+                    }
+                }
+                // r[t * NPT + e] = step t of column kq * NPT + e
+                const int ch0 = c * 32 + set * HC + kq * NPT;        // column within the block
+                uint32_t lb = 0;                    // bit t * NPT + e
                 auto lif_cols = [&](auto with_res) {
                     constexpr bool WITH_RES = decltype(with_res)::value;
                     float in[TS][NPT], v[NPT];
 #pragma unroll
-                    for (int jj = 0; jj < NPT; ++jj) {
-                        const float bb = sbias[c * 32 + set * HC + cg * NPT + jj];
-                        v[jj] = 0.0f;
+                    for (int e = 0; e < NPT; ++e) {
+                        const float bb = sbias[ch0 + e];
+                        v[e] = 0.0f;
 #pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            in[t][jj] = __fadd_rn(yb[(t * P + lx) * 17 + cg * NPT + jj], bb);
+                        for (int t = 0; t < TS; ++t) in[t][e] = __fadd_rn(r[t * NPT + e], bb);
                     }
                     if constexpr (WITH_RES) {
                         if (inside) {
 #pragma unroll
                             for (int t = 0; t < TS; ++t)
 #pragma unroll
-                                for (int jj = 0; jj < NPT; ++jj)
-                                    in[t][jj] = __fadd_rn(in[t][jj], load_res1(p, res_index(
-                                        p, t, on, oh, ow, tl.n0 + c * 32 + set * HC + cg * NPT + jj)));
+                                for (int e = 0; e < NPT; ++e)
+                                    in[t][e] = __fadd_rn(in[t][e], load_res1(p, res_index(
+                                        p, t, on, oh, ow, tl.n0 + ch0 + e)));
                         }
                     }
 #pragma unroll
                     for (int t = 0; t < TS; ++t) {
 #pragma unroll
-                        for (int jj = 0; jj < NPT; ++jj) {
-                            float vv = charge(v[jj], p.df, p.sc, in[t][jj]);
+                        for (int e = 0; e < NPT; ++e) {
+                            float vv = charge(v[e], p.df, p.sc, in[t][e]);
                             const bool s = vv >= p.thr;
-                            v[jj] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                            lb |= (s ? 1u : 0u) << (t * NPT + jj);
+                            v[e] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
+                            lb |= (s ? 1u : 0u) << (t * NPT + e);
                         }
                     }
                 };
                 lif_cols(std::integral_constant<bool, RES>{});
-                const int ch = tl.n0 + c * 32 + set * HC + cg * NPT;
+                const int ch = tl.n0 + ch0;
                 if (!p.pool) {
-                    tc::named_bar_sync(1 + set, 128);    // yb free for the next slice
                     if (inside) {
 #pragma unroll
                         for (int t = 0; t < TS; ++t)
@@ -844,12 +843,12 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                                  (lb >> (t * NPT)) & ((1u << NPT) - 1u));
                     }
                 } else {
-                    // 2x2 max-pool = OR: the column neighbour is CG lanes away; the row
-                    // neighbour (bw pixels away, possibly another warp) through shared memory
-                    lb |= __shfl_xor_sync(0xffffffffu, lb, CG);
-                    smask[set * 128 + et] = lb;
-                    tc::named_bar_sync(1 + set, 128);    // yb free, row neighbours' bits visible
-                    lb |= smask[set * 128 + (et ^ (CG * p.bw))];
+                    // 2x2 max-pool = OR: the column neighbour is TS lanes away; the row
+                    // neighbour (bw pixels away, possibly in another warp) through shared memory
+                    lb |= __shfl_xor_sync(0xffffffffu, lb, TS);
+                    smask[set * 128 + row] = lb;
+                    tc::named_bar_sync(1 + set, 128);    // row neighbours' bits visible
+                    lb |= smask[set * 128 + (row ^ (TS * p.bw))];
                     if (pool_store) {
 #pragma unroll
                         for (int t = 0; t < TS; ++t)
@@ -857,6 +856,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                                           (ow >> 1)) * p.Cout + ch,
                                                  (lb >> (t * NPT)) & ((1u << NPT) - 1u));
                     }
+                    tc::named_bar_sync(1 + set, 128);    // smask free for the next slice
                 }
             }
           }
@@ -1751,13 +1751,14 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     CUtensorMap ta, tb;
     int rc;
     if (variant == 2) {
-        // activation map: dims (Cin, W, H, B, T), box (64, bw, bh, bn, T): one box = the
-        // pixel block at every step, rows ordered (t, pixel)
-        const uint64_t adims[5] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B,
-                                   (uint64_t)T};
-        const uint64_t astr[4] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2,
-                                  (uint64_t)H * W * Cin * 2, (uint64_t)B * H * W * Cin * 2};
-        const uint32_t abox[5] = {64, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn, (uint32_t)T};
+        // activation map: dims (Cin, T, W, H, B), box (64, T, bw, bh, bn): one box = the
+        // pixel block at every step, rows ordered (pixel, t) -- a pixel's T steps are
+        // adjacent accumulator rows, i.e. adjacent lanes of one epilogue warp
+        const uint64_t adims[5] = {(uint64_t)Cin, (uint64_t)T, (uint64_t)W, (uint64_t)H,
+                                   (uint64_t)B};
+        const uint64_t astr[4] = {(uint64_t)B * H * W * Cin * 2, (uint64_t)Cin * 2,
+                                  (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
+        const uint32_t abox[5] = {64, (uint32_t)T, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn};
         rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, x, adims, astr, abox,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
@@ -1880,10 +1881,10 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     int BN = (iN % 128 == 0) ? 128 : (iN % 64 == 0 ? 64 : 32);
     while (BN > 32 && mtiles * (iN / BN) < 148) BN /= 2;
     CUtensorMap ta, tb;
-    const uint64_t adims[5] = {(uint64_t)K, 1, 1, (uint64_t)B, (uint64_t)T};
-    const uint64_t astr[4] = {(uint64_t)K * 2, (uint64_t)K * 2, (uint64_t)K * 2,
-                              (uint64_t)B * K * 2};
-    const uint32_t abox[5] = {64, 1, 1, (uint32_t)bn, (uint32_t)T};
+    const uint64_t adims[5] = {(uint64_t)K, (uint64_t)T, 1, 1, (uint64_t)B};
+    const uint64_t astr[4] = {(uint64_t)B * K * 2, (uint64_t)K * 2, (uint64_t)K * 2,
+                              (uint64_t)K * 2};
+    const uint32_t abox[5] = {64, (uint32_t)T, 1, 1, (uint32_t)bn};
     int rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, x, adims, astr, abox,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
