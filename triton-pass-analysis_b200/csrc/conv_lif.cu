@@ -1489,9 +1489,9 @@ int launch_tm_bn(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const Con
     }
     switch (BN) {
         case 256: return launch_conv_tm<256, 4, TS>(ta, tb, p, s);
-        case 128: return launch_conv_tm<128, 6, TS>(ta, tb, p, s);
-        case 64: return launch_conv_tm<64, 8, TS>(ta, tb, p, s);
-        default: return launch_conv_tm<32, 9, TS>(ta, tb, p, s);
+        case 128: return launch_conv_tm<128, 7, TS>(ta, tb, p, s);
+        case 64: return launch_conv_tm<64, 9, TS>(ta, tb, p, s);
+        default: return launch_conv_tm<32, 10, TS>(ta, tb, p, s);
     }
 }
 
