@@ -753,35 +753,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                     on < p.B;
             failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
             tc::tc_fence_after();
-            if (p.partial) {
-                // ---- split-K: raw float32 partial sums of this split, row = (pixel, step)
-                const int split = item % splits;
-                const int64_t gpix = ((int64_t)on * p.H + oh) * p.W + ow;
-                float* dst = p.partial + (((int64_t)split * p.T + kq) * npix_total + gpix) * p.Cout + tl.n0;
-#pragma unroll 1
-                for (int c = 0; c < NCH; ++c) {
-                    float r[HC];
-                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
-                    tc::tmem_wait_ld();
-                    if (inside) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + c * 32 + set * HC);
-#pragma unroll
-                        for (int j = 0; j < HC / 4; ++j)
-                            d4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-                    }
-                }
-                release_acc(a);
-                continue;
-            }
-#pragma unroll 1
-            for (int c = 0; c < NCH; ++c) {
-                float r[HC];
-                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
-                tc::tmem_wait_ld();
-                if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
-                // transpose across the TS lanes of the pixel: block j (NPT columns) of the
-                // lane with step t moves to the lane with k = j, slot t (butterfly over the
-                // bits of t; each stage swaps half of the blocks with the partner lane)
+            // transpose across the TS lanes of the pixel: block j (NPT columns) of the lane
+            // with step t moves to the lane with k = j, slot t (butterfly over the bits of t;
+            // each stage swaps half of the blocks with the partner lane).  Afterwards
+            // r[t * NPT + e] = step t of column kq * NPT + e.
+            auto transpose = [&](float (&r)[HC]) {
 #pragma unroll
                 for (int bb = TS / 2; bb >= 1; bb >>= 1) {
                     const bool hi = (kq & bb) != 0;
@@ -798,7 +774,39 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         }
                     }
                 }
-                // r[t * NPT + e] = step t of column kq * NPT + e
+            };
+            if (p.partial) {
+                // ---- split-K: raw float32 partial sums of this split, transposed like the
+                // neuron path so that a warp's store of one step covers whole sectors
+                const int split = item % splits;
+                const int64_t gpix = ((int64_t)on * p.H + oh) * p.W + ow;
+#pragma unroll 1
+                for (int c = 0; c < NCH; ++c) {
+                    float r[HC];
+                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
+                    tc::tmem_wait_ld();
+                    transpose(r);
+                    if (inside) {
+#pragma unroll
+                        for (int t = 0; t < TS; ++t) {
+                            float* d = p.partial + (((int64_t)split * p.T + t) * npix_total + gpix) * p.Cout +
+                                       tl.n0 + c * 32 + set * HC + kq * NPT;
+#pragma unroll
+                            for (int e = 0; e < NPT; e += 2)
+                                *reinterpret_cast<float2*>(d + e) = make_float2(r[t * NPT + e], r[t * NPT + e + 1]);
+                        }
+                    }
+                }
+                release_acc(a);
+                continue;
+            }
+#pragma unroll 1
+            for (int c = 0; c < NCH; ++c) {
+                float r[HC];
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
+                tc::tmem_wait_ld();
+                if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
+                transpose(r);
                 const int ch0 = c * 32 + set * HC + kq * NPT;        // column within the block
                 uint32_t lb = 0;                    // bit t * NPT + e
                 auto lif_cols = [&](auto with_res) {
