@@ -73,6 +73,19 @@ __device__ __forceinline__ uint32_t row_mask(const __nv_bfloat16* row, int d, bo
     return m;
 }
 
+// x = row `lane` of a 32 x 32 bit matrix (bit c = column c); afterwards x = column `lane`
+// (bit r = row r).  Stage s swaps the off-diagonal s x s blocks of every 2s x 2s block.
+__device__ __forceinline__ void transpose32(uint32_t& x, int lane) {
+    const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+        const int sft = 16 >> k;
+        const uint32_t m = masks[k];
+        const uint32_t y = __shfl_xor_sync(0xffffffffu, x, sft);
+        x = (lane & sft) ? ((x & ~m) | ((y >> sft) & m)) : ((x & m) | ((y & m) << sft));
+    }
+}
+
 constexpr int JG = 4;                    // features per work item in the Q kv stage
 constexpr int MAX_ITEMS = 8;             // work items per thread: N * d / JG <= 2048
 
@@ -116,13 +129,14 @@ __global__ void __launch_bounds__(THREADS) attention_core_kernel(const AttnParam
                 if (p.do_av) qm = row_mask(p.q + row, d, vec);
             }
             if (p.kv_in == nullptr) {
-                for (int i = 0; i < d; ++i) {
-                    const uint32_t kw = __ballot_sync(0xffffffffu, (km >> i) & 1u);
-                    const uint32_t vw = __ballot_sync(0xffffffffu, (vmk >> i) & 1u);
-                    if (lane == i) {
-                        kbits[i][w] = kw;
-                        vbits[i][w] = vw;
-                    }
+                // 32 x 32 bit-matrix transpose across the warp (lane = token, bit = feature
+                // -> lane = feature, bit = token): five shuffle stages swapping off-diagonal
+                // blocks, instead of one ballot per feature
+                transpose32(km, lane);
+                transpose32(vmk, lane);
+                if (lane < d) {
+                    kbits[lane][w] = km;
+                    vbits[lane][w] = vmk;
                 }
             }
             qmask[n] = qm;
