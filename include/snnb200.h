@@ -172,7 +172,12 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *           4 = as 2 with two 128-row tiles per CTA sharing every weight stage (block_n <= 128);
  *           5 = as 2 on CTA pairs (clusters of 2, M = 256 tcgen05 MMAs with cta_group::2):
  *           each CTA stages its own 128-row tile and half of the block_n weight rows
- *           (block_n 64 / 128 / 256).
+ *           (block_n 64 / 128 / 256);
+ *           6 = as 2 with the K range split across a thread-block cluster of `splits`
+ *           CTAs (2 or 4 with block_n 128; 2, 4 or 8 with block_n 256; default block_n
+ *           128, 256 for 8) that add their partial sums through distributed shared
+ *           memory in the order of the two-launch split-K form (bit-identical to it), each
+ *           CTA running the neuron on block_n / splits channels: one launch, no workspace.
  * block_n : output channels per CTA (per CTA pair for variant 5), 0 = choose, or 32 / 64 /
  *           128 (dividing Cout), or 256 with variants 2 and 5; 32 / 64 with variant 3.
  * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32
@@ -197,7 +202,7 @@ int snnb_conv3x3_lif(const void* x, int64_t T, int64_t B, int64_t H, int64_t W, 
  * fused_bias_if_lif with residual, fused.py:97-108).
  * residual       : NHWC [T*B, H, W, Cout] (the output's layout) of residual_dtype
  *                  (SNNB_BF16 or SNNB_F32), 16-byte aligned.
- * variant        : 0, 1 (block_n <= 64) or 2 (any splits); 3, 4 and 5 return
+ * variant        : 0, 1 (block_n <= 64), 2 (any splits) or 6; 3, 4 and 5 return
  *                  SNNB_ERR_UNSUPPORTED.
  */
 int snnb_conv3x3_lif_res(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
@@ -218,6 +223,29 @@ int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* 
                     float v_threshold, float v_reset, int hard_reset, int variant, int block_n,
                     int splits, void* workspace, int64_t workspace_bytes, void* out,
                     snnb_stream_t stream);
+
+/*
+ * K1 on images of at most 2 x 2 pixels (no counterpart in the reference, which runs these
+ * layers through snnb_conv3x3_lif's path: F.conv2d + fused_bias_if_lif,
+ * snn_compiler/nn/modules.py:324-357): there every output pixel's 3x3 window covers the
+ * whole image, so the conv is one dense GEMM per image, K = H*W*Cin -> N = H*W*Cout, and
+ * the zero-padding taps (5 of 9 at 2x2) leave the tensor-core work.  Same neuron and
+ * result as snnb_conv3x3_lif up to float32 summation order.
+ * x      : bf16 spikes NHWC [T*B, H, W, Cin], H and W in {1, 2}
+ * wd     : bf16 [H*W*Cout, H*W*Cin]: row (p, co), column (q, ci) holds
+ *          w[co, qh - ph + 1, qw - pw + 1, ci] (pixels p, q row-major, NHWC columns); with
+ *          pool != 0 the rows are ordered (co, p) instead (pixel fastest)
+ * bias_d : f32 [H*W*Cout], b'[co] for row (p, co) (or (co, p) with pool)
+ * pool   : 2x2 max-pool (H == W == 2): out [T*B, 1, 1, Cout]; else out [T*B, H, W, Cout]
+ * variant / block_n / splits / workspace: as snnb_linear_lif for an N = H*W*Cout layer;
+ * with pool: variants 0, 2, 4, 5 (splits == 1) or 6.
+ */
+int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                           int64_t Cin, const void* wd, const float* bias_d, int64_t Cout,
+                           float decay, float input_scale, float v_threshold, float v_reset,
+                           int hard_reset, int pool, int variant, int block_n, int splits,
+                           void* workspace, int64_t workspace_bytes, void* out,
+                           snnb_stream_t stream);
 
 /* Workspace bytes snnb_conv3x3_lif / snnb_linear_lif (H = W = 1) need for `splits`. */
 int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cout,

@@ -73,7 +73,8 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
 
 VARIANTS = [(0, 0, 1), (1, 32, 1), (1, 128, 1), (2, 32, 1), (2, 64, 1), (2, 128, 1), (2, 256, 1),
             (2, 128, 3), (2, 256, 4), (3, 32, 1), (3, 64, 1), (4, 64, 1), (4, 128, 1),
-            (4, 128, 2), (5, 64, 1), (5, 128, 1), (5, 256, 1), (5, 128, 2), (5, 256, 3)]
+            (4, 128, 2), (5, 64, 1), (5, 128, 1), (5, 256, 1), (5, 128, 2), (5, 256, 3),
+            (6, 128, 2), (6, 128, 4), (6, 256, 2), (6, 256, 8)]
 
 
 @pytest.mark.parametrize("vb", VARIANTS)
@@ -85,7 +86,7 @@ def test_conv3x3_lif_against_oracle(geom, vb):
     variant, block_n, splits = vb
     if block_n and Cout % block_n:
         pytest.skip("block_n must divide Cout")
-    if variant in (2, 4, 5) and T not in (2, 4, 8):
+    if variant in (2, 4, 5, 6) and T not in (2, 4, 8):
         pytest.skip("T folding needs T in {2, 4, 8}")
     C = _C()
     if variant == 3 and block_n not in C.band_block_ns(H, Cin, Cout):
@@ -111,6 +112,78 @@ def test_conv3x3_lif_against_oracle(geom, vb):
         assert torch.equal(yp.float().cpu().permute(0, 1, 4, 2, 3), own)
 
 
+@pytest.mark.parametrize("sk", [(128, 2), (128, 4), (256, 2), (256, 4), (256, 8)])
+@pytest.mark.parametrize("geom", [(4, 32, 512, 512, 2), (4, 8, 256, 512, 4), (2, 16, 128, 256, 4),
+                                  (8, 4, 512, 256, 2), (4, 2, 64, 128, 16)])
+def test_cluster_splitk_bit_identical_to_two_launch_form(geom, sk):
+    """The cluster split-K form (variant 6) adds the partial sums in the order of the
+    two-launch split-K form (variant 2 + splitsum_lif_kernel): spikes identical, pooled and
+    not, and with a residual input."""
+    T, B, Cin, Cout, H = geom
+    block_n, splits = sk
+    if Cout % block_n:
+        pytest.skip("block_n must divide Cout")
+    C = _C()
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.2, sum(geom) * 7 + block_n + splits, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    wd = C.weight_khwc(w).to(DEV)
+    bd = b.to(DEV)
+    g = OP.gen(Cout + splits)
+    rd = (torch.randn(T, B, H, H, Cout, generator=g) * 0.5).to(DEV)
+    for kw in (dict(pool=False), dict(pool=True), dict(residual=rd)):
+        ref = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, variant=2, block_n=block_n,
+                            splits=splits, **kw)
+        got = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, variant=6, block_n=block_n,
+                            splits=splits, **kw)
+        assert C.device_status() == 0
+        assert ref.float().sum() > 0
+        assert torch.equal(got, ref), kw.keys()
+
+
+@pytest.mark.parametrize("vb", [(0, 0, 1), (2, 32, 1), (2, 128, 1), (2, 64, 2), (4, 64, 1),
+                                (5, 128, 1), (6, 128, 2), (6, 256, 4)])
+@pytest.mark.parametrize("case", [(4, 16, 512, 512, 2), (4, 8, 128, 256, 1), (2, 8, 64, 128, 2),
+                                  (8, 4, 256, 128, 2), (4, 6, 64, 64, 2)])
+def test_conv3x3_dense_small_image_against_oracle(case, vb):
+    """Layers on 1x1 / 2x2 images as one dense GEMM per image (snnb_conv3x3_lif_dense), with
+    and without the fused 2x2 pool (OR over 4 consecutive columns), against the oracle's
+    padded conv."""
+    T, B, Cin, Cout, H = case
+    variant, block_n, splits = vb
+    if block_n and (H * H * Cout) % block_n:
+        pytest.skip("block_n must divide H*W*Cout")
+    if splits > (H * H * Cin + 63) // 64:
+        pytest.skip("more splits than 64-channel k-slabs")
+    C = _C()
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.2, sum(case) * 13 + block_n + splits, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    wk = C.weight_khwc(w).to(DEV)
+    bd = b.to(DEV)
+    kw = dict(tau=2.0, v_threshold=THR, variant=variant, block_n=block_n, splits=splits)
+    y = C.conv3x3_lif_dense(xd, C.dense_conv_weight(wk, H, H), C.dense_conv_bias(bd, H, H), **kw)
+    assert C.device_status() == 0
+    s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True)
+    got = y.float().cpu().permute(0, 1, 4, 2, 3)
+    assert got.sum() > 0, "degenerate case: no spikes"
+    flip_check(got, s, vpre)
+    if H != 2:
+        return
+    wp, bp = C.dense_conv_weight(wk, 2, 2, pool=True), C.dense_conv_bias(bd, 2, 2, pool=True)
+    if splits > 1 and variant != 6:
+        with pytest.raises(RuntimeError):
+            C.conv3x3_lif_dense(xd, wp, bp, pool=True, **kw)
+        return
+    yp = C.conv3x3_lif_dense(xd, wp, bp, pool=True, **kw)
+    assert C.device_status() == 0 and tuple(yp.shape) == (T, B, 1, 1, Cout)
+    gp = yp.float().cpu().reshape(T, B, Cout)
+    ref = s.reshape(T, B, Cout, 4).amax(-1)
+    # a window may differ only where one of its neurons came within 1e-4 of the threshold
+    near = ((vpre - THR).abs() < 1e-4).reshape(T, B, Cout, 4).any(-1).any(0, keepdim=True)
+    assert ref.sum() > 0
+    assert not ((gp != ref) & ~near).any()
+    assert (gp != ref).float().mean() <= 1e-3
+
+
 def test_conv3x3_soft_reset_and_if_neuron():
     C = _C()
     T, B, Cin, Cout, H = 4, 2, 64, 64, 8
@@ -132,7 +205,8 @@ def test_conv3x3_soft_reset_and_if_neuron():
 
 
 @pytest.mark.parametrize("vb", [(0, 0, 1), (1, 64, 1), (2, 32, 1), (2, 128, 1), (2, 128, 2),
-                                (4, 128, 1), (4, 64, 2), (5, 128, 1), (5, 64, 2), (5, 256, 1)])
+                                (4, 128, 1), (4, 64, 2), (5, 128, 1), (5, 64, 2), (5, 256, 1),
+                                (6, 128, 2), (6, 256, 4)])
 @pytest.mark.parametrize("TBKN", [(4, 64, 512, 4096), (4, 8, 4096, 256), (2, 130, 128, 96)])
 def test_linear_lif_against_oracle(TBKN, vb):
     T, B, K, N = TBKN

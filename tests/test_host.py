@@ -118,3 +118,21 @@ def test_resnet_zoo_builds_and_fuses_on_cpu():
     from snn_compiler.zoo.sew_resnet import sew_connect
     o, i = torch.tensor([0., 1., 1.]), torch.tensor([1., 1., 0.])
     assert sew_connect(o, i, "IAND").tolist() == [1.0, 0.0, 0.0]
+
+
+def test_dense_conv_weight_equals_padded_conv():
+    """A 3x3 / padding-1 conv on 1x1, 1x2, 2x1 and 2x2 images equals the GEMM with
+    dense_conv_weight (NHWC flattening on both sides), bias repeated per pixel."""
+    import torch.nn.functional as F
+    from snn_compiler.kernels import conv as KC
+    g = torch.Generator().manual_seed(5)
+    for H, W in ((1, 1), (1, 2), (2, 1), (2, 2)):
+        Cin, Cout, N = 8, 12, 3
+        w = torch.randn(Cout, Cin, 3, 3, generator=g, dtype=torch.float64)
+        b = torch.randn(Cout, generator=g, dtype=torch.float64)
+        x = torch.randn(N, Cin, H, W, generator=g, dtype=torch.float64)
+        ref = F.conv2d(x, w, b, padding=1).permute(0, 2, 3, 1).reshape(N, -1)
+        wd = KC.dense_conv_weight(w.permute(0, 2, 3, 1).contiguous(), H, W)
+        assert wd.shape == (H * W * Cout, H * W * Cin)
+        got = x.permute(0, 2, 3, 1).reshape(N, -1) @ wd.t() + KC.dense_conv_bias(b, H, W).double()
+        assert torch.allclose(got, ref, atol=1e-10), (H, W)

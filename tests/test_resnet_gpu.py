@@ -81,10 +81,10 @@ def test_sew_resnet18_fused_modules_match_oracle(connect):
 @pytest.mark.parametrize("res_dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("variant,block_n,splits", [(0, 0, 1), (1, 64, 1), (1, 32, 1),
                                                     (2, 128, 1), (2, 64, 1), (2, 64, 2),
-                                                    (2, 128, 3)])
+                                                    (2, 128, 3), (6, 128, 2), (6, 128, 4)])
 def test_conv3x3_residual_epilogue_against_oracle(variant, block_n, splits, res_dtype):
     """The residual input in every kernel variant that takes one (T-sequential, T-folded,
-    split-K finish) against the oracle."""
+    split-K finish, cluster split-K) against the oracle."""
     from snn_compiler.kernels import conv as C
     T, B, Cin, Cout, H = 4, 8, 64, 128, 8
     g = torch.Generator().manual_seed(variant * 10 + block_n + splits)

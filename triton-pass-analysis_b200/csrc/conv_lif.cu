@@ -31,126 +31,13 @@
 #include <mutex>
 #include <type_traits>
 
-#include "tc_common.cuh"
+#include "conv_tm.cuh"
 
 namespace snnb {
 
 __device__ int g_device_status = 0;
 
 namespace {
-
-constexpr int THREADS = 192;
-constexpr int A_TILE_BYTES = 128 * 128;          // 128 rows x 64 bf16
-
-struct ConvParams {
-    int T, B, H, W, Cin, Cout;
-    int bw, bh, bn;               // pixel block: bn images x bh rows x bw columns
-    int tiles_w, tiles_h, n_tiles_n, num_tiles;
-    int taps;                     // 9 (3x3 conv) or 1 (linear / 1x1)
-    int cin_blocks;               // Cin / 64
-    int pool;
-    float df, sc, thr, v_reset;
-    int hard;
-    const float* bias;
-    __nv_bfloat16* out;
-    int* status;
-    int splits;                   // k-range splits (T-folded kernel); 1 = none
-    float* partial;               // split-K: f32 partial sums [splits][T][B*H*W][Cout]
-    int mtiles;                   // pixel tiles per channel block (band kernel)
-    int ring, a_bytes, w_bytes;   // band kernel: A ring depth, bytes per A stage, weight bytes
-    const void* wq;               // the layer's weights in global memory, wq_bytes long
-    int64_t wq_bytes;
-    const void* res;              // residual input of the neuron or nullptr (no pooling then)
-    int res_f32;                  // residual dtype: float32 (1) or bf16 (0)
-};
-
-// Residual input of the neuron, added after the bias as the reference's fused kernel does
-// (x = y + b; x = x + residual: fused.py:97-108).  NHWC [T*B, H, W, Cout] of bf16 or
-// float32 -- the unpooled output's layout.  8 consecutive channels from element idx
-// (idx % 8 == 0: 16-byte aligned loads).
-__device__ __forceinline__ void load_res8(const void* res, int res_f32, int64_t idx,
-                                          float (&o)[8]) {
-    if (res_f32) {
-        const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(res) + idx);
-        const float4 a = __ldg(q), b = __ldg(q + 1);
-        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
-    } else {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
-            static_cast<const __nv_bfloat16*>(res) + idx));
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            o[2 * i] = __uint_as_float(w[i] << 16);
-            o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        }
-    }
-}
-__device__ __forceinline__ float load_res1(const ConvParams& p, int64_t idx) {
-    return p.res_f32 ? __ldg(static_cast<const float*>(p.res) + idx)
-                     : __bfloat162float(static_cast<const __nv_bfloat16*>(p.res)[idx]);
-}
-__device__ __forceinline__ int64_t res_index(const ConvParams& p, int t, int on, int oh, int ow,
-                                             int ch) {
-    return ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) * p.Cout + ch;
-}
-// r[j] = (r[j] + bias[j]) + residual[j] over one 32-channel slice of one output pixel; the
-// bias is then consumed (set to 0) so the neuron's own "+ bias" adds nothing.
-__device__ __forceinline__ void add_res_slice(const ConvParams& p, int64_t idx, float (&r)[32],
-                                              float (&bias)[32]) {
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        float rr[8];
-        load_res8(p.res, p.res_f32, idx + 8 * u, rr);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            r[8 * u + k] = __fadd_rn(__fadd_rn(r[8 * u + k], bias[8 * u + k]), rr[k]);
-            bias[8 * u + k] = 0.0f;
-        }
-    }
-}
-
-// Before waiting for the previous kernel: pull this CTA's share of the layer's weights
-// (which no kernel writes) into L2, so the first weight stages of every CTA hit L2 instead
-// of DRAM.  One thread, up to 64 KB per bulk prefetch.
-__device__ __forceinline__ void prefetch_weights_l2(const ConvParams& p) {
-    const int64_t per = ((p.wq_bytes + gridDim.x - 1) / gridDim.x + 15) & ~int64_t(15);
-    const int64_t b0 = per * blockIdx.x;
-    const int64_t b1 = b0 + per < p.wq_bytes ? b0 + per : p.wq_bytes;
-    for (int64_t b = b0; b + 16 <= b1; b += 65536) {
-        const int64_t n = (b1 - b < 65536 ? b1 - b : 65536) & ~int64_t(15);
-        tc::prefetch_l2(static_cast<const uint8_t*>(p.wq) + b, (uint32_t)n);
-    }
-}
-
-struct Tile {
-    int w0, h0, img0, n0;
-};
-
-__device__ __forceinline__ Tile decode_tile(int tile, const ConvParams& p, int BN) {
-    const int nt = tile % p.n_tiles_n;
-    const int mt = tile / p.n_tiles_n;
-    const int tw = mt % p.tiles_w;
-    const int th = (mt / p.tiles_w) % p.tiles_h;
-    const int tn = mt / (p.tiles_w * p.tiles_h);
-    return Tile{tw * p.bw, th * p.bh, tn * p.bn, nt * BN};
-}
-
-
-// NPT spikes (bits 0..NPT-1) as bf16 0/1 values at dst (2 * NPT bytes, aligned to them).
-template <int NPT>
-__device__ __forceinline__ void store_bits_bf16(__nv_bfloat16* dst, uint32_t bits) {
-    auto two = [](uint32_t b2) {
-        return ((b2 & 1u) ? 0x3F80u : 0u) | ((b2 & 2u) ? 0x3F800000u : 0u);
-    };
-    if constexpr (NPT == 8) {
-        *reinterpret_cast<uint4*>(dst) = spikes_to_bf16x8(bits);
-    } else if constexpr (NPT == 4) {
-        *reinterpret_cast<uint2*>(dst) = make_uint2(two(bits), two(bits >> 2));
-    } else {
-        *reinterpret_cast<uint32_t*>(dst) = two(bits);
-    }
-}
 
 // Producer drain after a failed wait: wait (bounded, whole warp) for the copies still in
 // flight -- the last min(stages, issued) stages before ring position (stage, phase).
@@ -429,459 +316,6 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
 }
 
-// ---- variant 2: T folded into M -----------------------------------------------------------
-// For layers whose pixel count is too small to fill the GPU with 128-pixel blocks: the
-// 128 accumulator rows of a tile are P = 128/TS pixels x TS steps (row p*TS + t), so the
-// grid is TS times larger and each tile runs the K loop once.  One 5-D TMA box per k-slab
-// (channels, step, w, h, image) lands each pixel's TS steps in consecutive rows of the A
-// tile.  The epilogue (two sets of 4 warps, each taking 16 columns of every 32-column slice)
-// finds a pixel's steps in TS adjacent lanes, transposes them in registers with shuffles so
-// that a lane owns 16/TS columns at every step, runs the T recurrence there and stores the
-// spikes directly (a warp's store of one step covers whole 32-byte sectors); 2x2 pooling ORs
-// the column neighbour by a shuffle and the row neighbour through one shared-memory word.  Persistent, with two TMEM accumulators alternating between
-// consecutive work items of a CTA.
-//
-// Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
-// accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
-// then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
-template <int BN, int STAGES, int TS, int MH, int CG = 1>
-struct SmemTM {
-    static constexpr int P = 128 / TS;
-    static constexpr int NCH = BN / 32;
-    static constexpr int B_TILE = BN / CG * 128;       // weight rows this CTA stages
-    static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
-    static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;           // 2 x 128 u32 (pool)
-    static constexpr int SB_OFF = MASK_OFF + 256 * 4;                  // BN f32 (bias)
-    static constexpr int BAR_OFF = (SB_OFF + BN * 4 + 7) & ~7;
-    static constexpr int NBARS = 2 * STAGES + 4 * MH + 1;
-    static constexpr int TMEM_OFF = BAR_OFF + NBARS * 8;
-    static constexpr int ABORT_OFF = TMEM_OFF + 4;
-    static constexpr int TOTAL = ABORT_OFF + 4;
-    static constexpr int DYN = TOTAL + 1024;
-};
-
-// NP producer warps (warp 0 and warps 6 ..) take the k-slab stages round-robin: each TMA
-// issue occupies its thread for ~250 cycles whatever the box size, so one issuing thread
-// cannot keep up with 4 MMAs per stage.
-// MH M-tiles per work item (MH = 2: two 128-row tiles of the same channel block share each
-// weight stage, so every weight byte brought into shared memory feeds twice the MMAs --
-// these layers are bound by the L2 -> shared-memory stream of ~55 B/cycle per SM).  Each
-// tile has its own pair of TMEM accumulators (slot = (item & 1) * MH + h).
-// CG = 2: CTA pairs (clusters of 2) with M = 256 MMAs (cta_group::2).  A work item is two
-// consecutive M-tiles (one per CTA) x BN channels; each CTA stages its own A tile and half
-// of the BN weight rows, so per MMA cycle a CTA streams 2/3 (BN = 128) or 1/2 (BN = 256)
-// of the bytes of the single-CTA form.  The even CTA waits for both CTAs' bytes on its
-// full barrier and issues the MMAs; its commits arrive on both CTAs' barriers (stage free,
-// accumulator ready); both epilogues hand the accumulator back on the even CTA's barrier.
-// RES: the neuron input also takes p.res (a separate instantiation: the residual loads in
-// the epilogue cost the plain form ~4% when compiled in behind a run-time test).
-// Two sets of 4 epilogue warps (warps 2-5 and 5+NP .. 8+NP) split every 32-column slice of
-// the accumulator into halves: the epilogue of a CTA's last work item, which no MMA
-// overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
-template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES>
-__global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
-conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const ConvParams p) {
-    constexpr bool PAIR = CG == 2;
-    static_assert(!PAIR || MH == 1, "CTA pairs take one M-tile each");
-    static_assert(!RES || (MH == 1 && CG == 1), "residual input: one M-tile, single CTA");
-    using S = SmemTM<BN, STAGES, TS, MH, CG>;
-    constexpr int P = S::P, NCH = S::NCH;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t sbase = tc::smem_u32(smem);
-    uint32_t* smask = reinterpret_cast<uint32_t*>(smem + S::MASK_OFF);
-    float* sbias = reinterpret_cast<float*>(smem + S::SB_OFF);
-    const uint32_t bar0 = sbase + S::BAR_OFF;
-    auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-    auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
-    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 * MH + a); };
-    const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4 * MH);
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::ABORT_OFF);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KB = p.taps * p.cin_blocks;
-    const int splits = p.splits;
-    const int num_items = p.num_tiles * splits;
-    // work items of this CTA (a pair walks its items together)
-    const int item0 = PAIR ? (int)(blockIdx.x / 2) : (int)blockIdx.x;
-    const int item_step = PAIR ? (int)(gridDim.x / 2) : (int)gridDim.x;
-    // bytes that complete a stage: this CTA's tiles, or both CTAs' for a pair
-    constexpr uint32_t STAGE_TX = CG * (MH * A_TILE_BYTES + S::B_TILE);
-    constexpr uint32_t TMEM_COLS = 2 * MH * BN < 32 ? 32 : 2 * MH * BN;
-    static_assert(2 * MH * BN <= 512, "accumulators exceed TMEM");
-    const uint32_t rank = PAIR ? tc::cluster_rank() : 0u;
-    // M-tile h of a work item; false when the item's last tile lies past the layer (odd
-    // tile count) -- its box reads zeros and the epilogue stores nothing
-    auto half_tile = [&](int item, int h, Tile& tl) {
-        const int tile2 = item / splits;
-        const int nt = tile2 % p.n_tiles_n;
-        const int mt = (tile2 / p.n_tiles_n) * (MH * CG) + h + (int)rank;
-        tl = decode_tile(mt * p.n_tiles_n + nt, p, BN);
-        return mt < p.mtiles;
-    };
-    auto krange = [&](int s, int& k0, int& k1) {
-        k0 = (int)((int64_t)KB * s / splits);
-        k1 = (int)((int64_t)KB * (s + 1) / splits);
-    };
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(full_bar(s), 1);
-            tc::mbar_init(empty_bar(s), 1);
-        }
-        for (int a = 0; a < 2 * MH; ++a) {
-            tc::mbar_init(accf_bar(a), 1);
-            // single CTA: every epilogue thread arrives (2 sets of 128); pair: one arrival
-            // per epilogue warp of either CTA, on the even CTA's barrier
-            tc::mbar_init(acce_bar(a), PAIR ? 16 : 256);
-        }
-        tc::mbar_init(done_bar, 1);
-        *abort_flag = 0;
-        tc::fence_mbar_init();
-        tc::prefetch_tmap(&tmA);
-        tc::prefetch_tmap(&tmB);
-    }
-    if (warp == 1) {
-        if constexpr (PAIR) {
-            tc::tmem_alloc_pair(sbase + S::TMEM_OFF, TMEM_COLS);
-            tc::tmem_relinquish_pair();
-        } else {
-            tc::tmem_alloc(sbase + S::TMEM_OFF, TMEM_COLS);
-            tc::tmem_relinquish();
-        }
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    // a pair: both CTAs' barriers initialised before either signals the other's
-    if constexpr (PAIR) tc::cluster_sync();
-    tc::tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
-    pdl_wait();
-    pdl_trigger();
-
-    constexpr int W1 = 5 + NP;                    // first warp of the second epilogue set
-    if (warp == 0 || (warp >= 6 && warp < W1)) {
-        // ------------------------------------------------------------- TMA producers
-        // producer pi issues the stages g with g % NP == pi (g counts k-slabs over the
-        // whole schedule, as the MMA warp does)
-        const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
-        uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
-        for (int item = item0; item < num_items; item += item_step) {
-            Tile tl[MH];
-#pragma unroll
-            for (int h = 0; h < MH; ++h) half_tile(item, h, tl[h]);
-            int k0, k1;
-            krange(item % splits, k0, k1);
-            for (int kb = k0; kb < k1; ++kb, ++g) {
-                if (g % NP != pi) continue;
-                const int stage = (int)(g % STAGES);
-                const uint32_t phase = (g / STAGES) & 1u;
-                failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
-                if (!failed && tc::elect_one()) {
-                    const int tap = kb / p.cin_blocks;
-                    const int cb = kb - tap * p.cin_blocks;
-                    const int r = p.taps == 9 ? tap / 3 : 1;
-                    const int s = p.taps == 9 ? tap % 3 : 1;
-                    if constexpr (PAIR) {
-                        // both CTAs' bytes complete the even CTA's full barrier
-                        const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
-                        if (rank == 0) tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-                        tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
-                                             cb * 64, 0, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
-                                             tl[0].img0);
-                        tc::tma_load_3d_pair(sbase + S::B_OFF + stage * S::B_TILE, &tmB, fb,
-                                             cb * 64, tap, tl[0].n0 + (int)rank * (BN / 2));
-                    } else {
-                        tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-#pragma unroll
-                        for (int h = 0; h < MH; ++h)
-                            tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
-                                            &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 + s - 1,
-                                            tl[h].h0 + r - 1, tl[h].img0);
-                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
-                                        full_bar(stage), cb * 64, tap, tl[0].n0);
-                    }
-                }
-                __syncwarp();
-                if (!failed) {
-                    ++issued;
-                    last_g = g;
-                }
-            }
-        }
-        if (failed) {
-            // wait (bounded) for this producer's copies still in flight: on the full barrier,
-            // or for the odd CTA of a pair (whose copies complete on the even CTA's barrier)
-            // on the stage's release, which follows the MMAs that read them
-            uint32_t gg = last_g;
-            for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP) {
-                if (PAIR && rank != 0)
-                    tc::mbar_wait_warp(empty_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
-                else
-                    tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
-            }
-            if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
-        }
-    } else if (warp == 1 && PAIR && rank != 0) {
-        // odd CTA of a pair: the even CTA issues every MMA; its last commit says that this
-        // CTA's TMEM and shared memory are no longer in use by the tensor pipe
-        if (!tc::mbar_wait_warp(done_bar, 0, 0) && lane == 0) {
-            atomicExch(p.status, SNNB_ERR_TIMEOUT);
-            *abort_flag = 1;
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------- MMA issuer
-        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128 * CG, BN);
-        int stage = 0;
-        uint32_t phase = 0, it = 0, failed = 0;
-        for (int item = item0; item < num_items; item += item_step, ++it) {
-            int k0, k1;
-            krange(item % splits, k0, k1);
-            const int a0 = (it & 1) * MH;            // this item's first accumulator slot
-#pragma unroll
-            for (int h = 0; h < MH; ++h)
-                failed |= 1u - tc::mbar_wait_warp(acce_bar(a0 + h), ((it >> 1) & 1u) ^ 1u, failed);
-            tc::tc_fence_after();
-            for (int kb = k0; kb < k1; ++kb) {
-                int nstage = stage + 1;
-                uint32_t nphase = phase;
-                if (nstage == STAGES) { nstage = 0; nphase ^= 1u; }
-                // only the issuing lane waits for stages (the others meet it at __syncwarp),
-                // and it waits for the next stage before committing this one: a wait queued
-                // behind a commit would not return until the tensor pipe had drained
-                if (tc::elect_one()) {
-                    if (kb == k0) {
-                        failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
-                        tc::tc_fence_after();
-                    }
-                    const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + stage * S::B_TILE);
-#pragma unroll
-                    for (int h = 0; h < MH; ++h) {
-                        const uint64_t da = tc::sdesc_k_sw128(sbase + S::A_OFF +
-                                                              (stage * MH + h) * A_TILE_BYTES);
-                        const uint32_t dcol = tmem + (a0 + h) * BN;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            if constexpr (PAIR)
-                                tc::umma_bf16_pair(dcol, da + 2 * k, db + 2 * k, IDESC,
-                                                   (kb > k0) || (k > 0));
-                            else
-                                tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
-                                              (kb > k0) || (k > 0));
-                        }
-                    }
-                    if (kb + 1 < k1) {
-                        failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
-                        tc::tc_fence_after();
-                    }
-                    if constexpr (PAIR) tc::umma_commit_pair(empty_bar(stage), 3);
-                    else tc::umma_commit(empty_bar(stage));
-                }
-                __syncwarp();
-                stage = nstage;
-                phase = nphase;
-            }
-            if (tc::elect_one()) {
-#pragma unroll
-                for (int h = 0; h < MH; ++h) {
-                    if constexpr (PAIR) tc::umma_commit_pair(accf_bar(a0 + h), 3);
-                    else tc::umma_commit(accf_bar(a0 + h));
-                }
-            }
-            __syncwarp();
-            // lane 0 (the elected lane) owns the failure flag of the stage waits; the warp-wide
-            // waits need the same skip value in every lane
-            failed = __shfl_sync(0xffffffffu, failed, 0);
-        }
-        if (tc::elect_one()) {
-            if constexpr (PAIR) tc::umma_commit_pair(done_bar, 3);
-            else tc::umma_commit(done_bar);
-        }
-        __syncwarp();
-        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
-        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
-    } else {
-        const int set = warp >= W1 ? 1 : 0;             // which half of each slice
-        const int q = warp & 3;                         // TMEM lane quadrant
-        const int row = 32 * q + lane;                  // accumulator row = pixel * TS + step
-        const int et = threadIdx.x - (set ? 32 * W1 : 64);   // 0..127 within the set
-        const int et2 = set * 128 + et;                 // 0..255 over both sets
-        constexpr int HC = 16;                          // columns of a slice per set
-        constexpr int NPT = HC / TS;                    // columns per thread after the transpose
-        // After the in-register transpose the TS lanes of a pixel (rows px*TS .. px*TS+TS-1)
-        // hold its TS steps of NPT consecutive columns each: lane k of the group owns columns
-        // k*NPT .. k*NPT+NPT-1 (of this set's 16) at every step.
-        const int lx = row / TS, kq = row % TS;
-        const int64_t npix_total = (int64_t)p.B * p.H * p.W;
-        uint32_t it = 0, failed = 0;
-        // hand accumulator a back to the MMA issuer (of the even CTA, for a pair)
-        auto release_acc = [&](int a) {
-            tc::tc_fence_before();
-            if constexpr (PAIR) {
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive_cluster(tc::map_to_rank(acce_bar(a), 0));
-            } else {
-                tc::mbar_arrive(acce_bar(a));
-            }
-        };
-        for (int item = item0; item < num_items; item += item_step, ++it) {
-          if (!p.partial) {
-            // the channel block's bias into shared memory before the accumulator is ready
-            Tile t0;
-            half_tile(item, 0, t0);
-            tc::named_bar_sync(3, 256);              // both sets done with the last item's bias
-            for (int i = et2; i < BN; i += 256) sbias[i] = __ldg(p.bias + t0.n0 + i);
-            tc::named_bar_sync(3, 256);
-          }
-          for (int h = 0; h < MH; ++h) {
-            Tile tl;
-            half_tile(item, h, tl);
-            const int a = (int)(it & 1) * MH + h;
-            // (before the accumulator is ready) this lane's pixel in the layer
-            const int lw = lx % p.bw, lh = (lx / p.bw) % p.bh, ln = lx / (p.bw * p.bh);
-            const int ow = tl.w0 + lw, oh = tl.h0 + lh, on = tl.img0 + ln;
-            const bool inside = ow < p.W && oh < p.H && on < p.B;
-            const int Ho = p.H >> 1, Wo = p.W >> 1;
-            // pooled: the window's top-left pixel stores (window inside the layer)
-            const bool pool_store = ((lw | lh) & 1) == 0 && (ow >> 1) < Wo && (oh >> 1) < Ho &&
-                                    on < p.B;
-            failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
-            tc::tc_fence_after();
-            // transpose across the TS lanes of the pixel: block j (NPT columns) of the lane
-            // with step t moves to the lane with k = j, slot t (butterfly over the bits of t;
-            // each stage swaps half of the blocks with the partner lane).  Afterwards
-            // r[t * NPT + e] = step t of column kq * NPT + e.
-            auto transpose = [&](float (&r)[HC]) {
-#pragma unroll
-                for (int bb = TS / 2; bb >= 1; bb >>= 1) {
-                    const bool hi = (kq & bb) != 0;
-#pragma unroll
-                    for (int j0 = 0; j0 < TS; ++j0) {
-                        if (j0 & bb) continue;
-                        const int j1 = j0 | bb;
-#pragma unroll
-                        for (int e = 0; e < NPT; ++e) {
-                            const float snd = hi ? r[j0 * NPT + e] : r[j1 * NPT + e];
-                            const float rcv = __shfl_xor_sync(0xffffffffu, snd, bb);
-                            if (hi) r[j0 * NPT + e] = rcv;
-                            else r[j1 * NPT + e] = rcv;
-                        }
-                    }
-                }
-            };
-            if (p.partial) {
-                // ---- split-K: raw float32 partial sums of this split, transposed like the
-                // neuron path so that a warp's store of one step covers whole sectors
-                const int split = item % splits;
-                const int64_t gpix = ((int64_t)on * p.H + oh) * p.W + ow;
-#pragma unroll 1
-                for (int c = 0; c < NCH; ++c) {
-                    float r[HC];
-                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
-                    tc::tmem_wait_ld();
-                    transpose(r);
-                    if (inside) {
-#pragma unroll
-                        for (int t = 0; t < TS; ++t) {
-                            float* d = p.partial + (((int64_t)split * p.T + t) * npix_total + gpix) * p.Cout +
-                                       tl.n0 + c * 32 + set * HC + kq * NPT;
-#pragma unroll
-                            for (int e = 0; e < NPT; e += 2)
-                                *reinterpret_cast<float2*>(d + e) = make_float2(r[t * NPT + e], r[t * NPT + e + 1]);
-                        }
-                    }
-                }
-                release_acc(a);
-                continue;
-            }
-#pragma unroll 1
-            for (int c = 0; c < NCH; ++c) {
-                float r[HC];
-                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
-                tc::tmem_wait_ld();
-                if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
-                transpose(r);
-                const int ch0 = c * 32 + set * HC + kq * NPT;        // column within the block
-                uint32_t lb = 0;                    // bit t * NPT + e
-                auto lif_cols = [&](auto with_res) {
-                    constexpr bool WITH_RES = decltype(with_res)::value;
-                    float in[TS][NPT], v[NPT];
-#pragma unroll
-                    for (int e = 0; e < NPT; ++e) {
-                        const float bb = sbias[ch0 + e];
-                        v[e] = 0.0f;
-#pragma unroll
-                        for (int t = 0; t < TS; ++t) in[t][e] = __fadd_rn(r[t * NPT + e], bb);
-                    }
-                    if constexpr (WITH_RES) {
-                        if (inside) {
-#pragma unroll
-                            for (int t = 0; t < TS; ++t)
-#pragma unroll
-                                for (int e = 0; e < NPT; ++e)
-                                    in[t][e] = __fadd_rn(in[t][e], load_res1(p, res_index(
-                                        p, t, on, oh, ow, tl.n0 + ch0 + e)));
-                        }
-                    }
-#pragma unroll
-                    for (int t = 0; t < TS; ++t) {
-#pragma unroll
-                        for (int e = 0; e < NPT; ++e) {
-                            float vv = charge(v[e], p.df, p.sc, in[t][e]);
-                            const bool s = vv >= p.thr;
-                            v[e] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                            lb |= (s ? 1u : 0u) << (t * NPT + e);
-                        }
-                    }
-                };
-                lif_cols(std::integral_constant<bool, RES>{});
-                const int ch = tl.n0 + ch0;
-                if (!p.pool) {
-                    if (inside) {
-#pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
-                                                             p.Cout + ch,
-                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
-                    }
-                } else {
-                    // 2x2 max-pool = OR: the column neighbour is TS lanes away; the row
-                    // neighbour (bw pixels away, possibly in another warp) through shared memory
-                    lb |= __shfl_xor_sync(0xffffffffu, lb, TS);
-                    smask[set * 128 + row] = lb;
-                    tc::named_bar_sync(1 + set, 128);    // row neighbours' bits visible
-                    lb |= smask[set * 128 + (row ^ (TS * p.bw))];
-                    if (pool_store) {
-#pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * Ho + (oh >> 1)) * Wo +
-                                                          (ow >> 1)) * p.Cout + ch,
-                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
-                    }
-                    tc::named_bar_sync(1 + set, 128);    // smask free for the next slice
-                }
-            }
-          }
-        }
-        if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    // a pair: neither CTA leaves (or frees TMEM) while the other may still signal its
-    // barriers or have its shared memory read by the tensor pipe
-    if constexpr (PAIR) tc::cluster_sync();
-    if (warp == 1) {
-        tc::tc_fence_after();
-        if constexpr (PAIR) tc::tmem_dealloc_pair(tmem, TMEM_COLS);
-        else tc::tmem_dealloc(tmem, TMEM_COLS);
-    }
-}
 
 // ---- variant 3: row bands, halo reuse, resident weights ------------------------------------
 // For 3x3 layers whose width W divides 128 (W in 8..64): a tile is a band of bh = 128 / W
@@ -1671,10 +1105,13 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
 // Shared host path of the conv / linear entries.
 // variant: 0 = choose, 1 = T sequential inside the CTA (128-pixel blocks),
 //          2 = T folded into M (128/T-pixel blocks, T in {2, 4, 8}),
-//          3 = row bands with halo reuse and resident weights (W in {8, 16, 32, 64}).
+//          3 = row bands with halo reuse and resident weights (W in {8, 16, 32, 64}),
+//          4 = as 2 with two M-tiles per CTA, 5 = as 2 on CTA pairs (cta_group::2),
+//          6 = as 2 with the K range split across a cluster (conv_cluster.cu).
 // block_n: 0 = choose, else 32 / 64 / 128 (/ 256 with variant 2) output channels per CTA.
-// splits : > 1 splits the K range (variant 2 only): partial sums go to `workspace`
-//          ([splits][T][B*H*W][Cout] f32, caller-owned) and splitsum_lif_kernel finishes.
+// splits : > 1 splits the K range (variants 2 and 6): with variant 2 partial sums go to
+//          `workspace` ([splits][T][B*H*W][Cout] f32, caller-owned) and
+//          splitsum_lif_kernel finishes; with variant 6 the cluster reduces them itself.
 int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                  const float* bias, int Cout, int taps, float df, float sc, float thr,
                  float v_reset, int hard, int pool, int variant, int block_n, int splits,
@@ -1682,12 +1119,32 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  const void* res = nullptr, int res_f32 = 0) {
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
     if (res && (pool || !aligned16(res))) return res && pool ? SNNB_ERR_UNSUPPORTED : SNNB_ERR_ARG;
+    // pool == 2: OR over groups of 4 consecutive output columns (the dense form of a pooled
+    // 2x2-image conv, snnb_conv3x3_lif_dense); T-folded epilogues only
+    const bool gpool = pool == 2;
+    if (pool < 0 || pool > 2) return SNNB_ERR_ARG;
+    if (gpool) {
+        if (taps != 1 || H != 1 || W != 1 || Cout % 128 != 0) return SNNB_ERR_UNSUPPORTED;
+        if (variant == 1 || variant == 3) return SNNB_ERR_UNSUPPORTED;
+        if (splits > 1 && variant != 6) return SNNB_ERR_UNSUPPORTED;
+        if (variant == 0) variant = 2;
+    }
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
     if (Cin % 8 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
     if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
-    if (pool && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
+    if (pool == 1 && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    if (variant < 0 || variant > 5) return SNNB_ERR_ARG;
+    if (variant < 0 || variant > 6) return SNNB_ERR_ARG;
+    // variant 6: T folded into M, the K range split across a cluster of `splits` CTAs that
+    // reduce through distributed shared memory (conv_cluster.cu); no workspace
+    const bool ck = variant == 6;
+    if (ck) {
+        if (splits != 2 && splits != 4 && splits != 8) return SNNB_ERR_UNSUPPORTED;
+        if (block_n == 0) block_n = splits == 8 ? 256 : 128;
+        if (block_n != 128 && block_n != 256) return SNNB_ERR_UNSUPPORTED;
+        if (splits == 8 && block_n != 256) return SNNB_ERR_UNSUPPORTED;
+        variant = 2;
+    }
     // variant 4: T folded into M with two M-tiles per CTA sharing each weight stage
     const int mh = variant == 4 ? 2 : 1;
     if (variant == 4) {
@@ -1726,7 +1183,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (variant == 0) {
         // sequential kernel unless its grid leaves SMs idle and folding T is possible
         variant = 1;
-        if (tm_ok && choose_block(H, W, 128, pool, bw, bh, bn)) {
+        if (tm_ok && choose_block(H, W, 128, pool == 1, bw, bh, bn)) {
             const int64_t seq_grid = ((int64_t)((W + bw - 1) / bw) * ((H + bh - 1) / bh) *
                                       ((B + bn - 1) / bn)) * (Cout / (block_n ? block_n : bn_max));
             if (seq_grid < 2 * 148) variant = 2;
@@ -1737,7 +1194,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (variant == 1 && block_n == 256) return SNNB_ERR_UNSUPPORTED;   // v[] would not fit
     if (variant == 1 && res && block_n == 128) return SNNB_ERR_UNSUPPORTED;
     const int P = variant == 2 ? 128 / T : 128;
-    if (!choose_block(H, W, P, pool, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
+    if (!choose_block(H, W, P, pool == 1, bw, bh, bn)) return SNNB_ERR_UNSUPPORTED;
     const int64_t mtiles = (int64_t)((W + bw - 1) / bw) * ((H + bh - 1) / bh) * ((B + bn - 1) / bn);
     int BN = block_n;
     if (!BN) {
@@ -1750,7 +1207,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     }
     if (cg == 2 && BN < 64) return SNNB_ERR_UNSUPPORTED;
     if (variant == 1 && res && BN > 64) BN = 64;     // residual operands: see conv_lif_kernel
-    if (splits > 1) {
+    if (splits > 1 && !ck) {
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
         if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
     }
@@ -1796,12 +1253,13 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
     p.res = res; p.res_f32 = res_f32;
-    p.splits = splits;
-    p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+    p.splits = ck ? 1 : splits;
+    p.partial = splits > 1 && !ck ? static_cast<float*>(workspace) : nullptr;
     const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
     p.mtiles = (int)mtiles;
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
     p.num_tiles = (int)ntiles;
+    if (ck) return launch_tm_cluster(T, BN, splits, ta, tb, p, s);
     if (variant == 2) {
         switch (T) {
             case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;
@@ -1925,6 +1383,22 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     return launch_splitsum(out, 1, (int64_t)T * B, iN, bias, s);
 }
 
+extern "C" int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                                      int64_t Cin, const void* wd, const float* bias_d,
+                                      int64_t Cout, float decay, float input_scale,
+                                      float v_threshold, float v_reset, int hard_reset, int pool,
+                                      int variant, int block_n, int splits, void* workspace,
+                                      int64_t workspace_bytes, void* out, snnb_stream_t stream) {
+    if (H < 1 || H > 2 || W < 1 || W > 2 || Cin <= 0 || Cout <= 0 || T <= 0 || B <= 0 ||
+        T > 0x7fffffff || B > 0x7fffffff || Cin > 0x7fffffff || Cout > 0x7fffffff)
+        return SNNB_ERR_ARG;
+    if (pool && (H != 2 || W != 2)) return SNNB_ERR_UNSUPPORTED;
+    // one image = one "pixel" of a linear layer with K = H*W*Cin inputs and H*W*Cout outputs
+    return run_tc_layer(x, (int)T, (int)B, 1, 1, (int)(H * W * Cin), wd, bias_d,
+                        (int)(H * W * Cout), 1, decay, input_scale, v_threshold, v_reset,
+                        hard_reset, pool ? 2 : 0, variant, block_n, splits, workspace,
+                        workspace_bytes, out, static_cast<cudaStream_t>(stream));
+}
 extern "C" int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W,
                                               int64_t Cout, int splits) {
     if (splits <= 1) return 0;

@@ -303,6 +303,49 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
+// Orders this thread's earlier shared-memory writes (and those its CTA barrier made visible
+// to it) before its later arrivals on other CTAs' barriers.
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+// 16 bytes of another CTA's shared memory (a mapa address).
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr));
+    return v;
+}
+// mbar_wait_warp with cluster-scope acquire: for a barrier other CTAs of the cluster arrive
+// on after writing shared memory this warp then reads.
+__device__ __forceinline__ uint32_t mbar_wait_warp_cluster(uint32_t bar, uint32_t parity,
+                                                           uint32_t skip) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "@q bra CFAIL_%=;\n\t"
+        "mov.u64 t0, %%clock64;\n\t"
+        "CLOOP_%=:\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "vote.sync.all.pred p, p, 0xffffffff;\n\t"
+        "@p bra COK_%=;\n\t"
+        "mov.u64 t1, %%clock64;\n\t"
+        "sub.u64 t1, t1, t0;\n\t"
+        "setp.lt.u64 q, t1, %4;\n\t"
+        "vote.sync.any.pred q, q, 0xffffffff;\n\t"
+        "@q bra CLOOP_%=;\n\t"
+        "CFAIL_%=:\n\t"
+        "mov.u32 %0, 0;\n\t"
+        "bra.uni CEND_%=;\n\t"
+        "COK_%=:\n\t"
+        "mov.u32 %0, 1;\n\t"
+        "CEND_%=:\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "memory");
+    return ok;
+}
 // Tiled loads into this CTA's shared memory whose completion bytes are counted on the
 // mbarrier at `bar` (a shared::cluster address: the pair's even CTA); no multicast.
 __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* tm, uint32_t bar,

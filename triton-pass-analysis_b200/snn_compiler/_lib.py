@@ -37,6 +37,8 @@ SIGNATURES = {
     "snnb_conv3x3_lif_res": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, I32, I32,
                              I32, I32, P, I64, P, P],
     "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32, P, I64, P, P],
+    "snnb_conv3x3_lif_dense": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32,
+                               I32, I32, P, I64, P, P],
     "snnb_linear_mean": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_linear_out": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,

@@ -38,8 +38,11 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     neuron (no pooling; snnb_conv3x3_lif_res).
     variant: 0 choose, 1 T-sequential CTAs, 2 T folded into M, 3 row bands with halo reuse
     and resident weights (band_block_ns), 4 = 2 with two M-tiles per CTA, 5 = 2 on CTA pairs
-    (M = 256 MMAs, half the weight rows staged per CTA); block_n: 0 or 32/64/128/256;
-    splits > 1: split-K with float32 partials in `workspace` (allocated here if None)."""
+    (M = 256 MMAs, half the weight rows staged per CTA), 6 = 2 with the K range split across
+    a thread-block cluster of `splits` CTAs that reduce through distributed shared memory
+    (no workspace); block_n: 0 or 32/64/128/256;
+    splits > 1: split-K with float32 partials in `workspace` (allocated here if None)
+    except with variant 6."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1:3] == (3, 3)
     T, B, H, W, Cin = x.shape
@@ -51,7 +54,8 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     Ho, Wo = (H // 2, W // 2) if pool else (H, W)
     if out is None:
         out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
-    ws, ws_bytes = _workspace(workspace, splits, T, B, H, W, Cout, x.device)
+    ws, ws_bytes = _workspace(workspace, 1 if variant == 6 else splits, T, B, H, W, Cout,
+                              x.device)
     if residual is not None:
         assert not pool, "residual input with pooling is not supported"
         assert residual.is_cuda and residual.is_contiguous() and \
@@ -87,7 +91,8 @@ def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: 
                                       v_reset)
     if out is None:
         out = torch.empty(T, B, N, device=x.device, dtype=torch.bfloat16)
-    ws, ws_bytes = _workspace(workspace, splits, T, B, 1, 1, N, x.device)
+    ws, ws_bytes = _workspace(workspace, 1 if variant == 6 else splits, T, B, 1, 1, N,
+                              x.device)
     st = _lib.lib().snnb_linear_lif(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N, df, sc,
                                     thr, vr, hard, int(variant), int(block_n), int(splits),
                                     _lib.ptr(ws), ws_bytes, _lib.ptr(out), _lib.stream_of(x))
@@ -210,9 +215,15 @@ def band_block_ns(W: int, cin: int, cout: int):
     return tuple(bn for bn in (32, 64) if cout % bn == 0 and 9 * cb * bn <= 864)
 
 
-def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=()):
+def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
+               dense_pool: bool = False):
     """(variant, block_n, splits) configurations a layer admits; `band` lists the
-    block widths of variant 3 the layer qualifies for (band_block_ns)."""
+    block widths of variant 3 the layer qualifies for (band_block_ns); dense_pool: the
+    pooled dense form (snnb_conv3x3_lif_dense), whose epilogue the T-folded kernels alone
+    have (no T-sequential variant, split-K only within a cluster)."""
+    if dense_pool:
+        return [c for c in candidates(cout, T, kslabs, max_splits)
+                if c[0] in (2, 4, 5, 6) and (c[2] == 1 or c[0] == 6)]
     out = []
     for v in ((1, 2) if T in (2, 4, 8) else (1,)):
         for bn in ((32, 64, 128) if v == 1 else (32, 64, 128, 256)):
@@ -242,15 +253,20 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=()):
             while s <= max_splits and s <= kslabs // 2:
                 out.append((5, bn, s))
                 s *= 2
+    if T in (2, 4, 8):                # T folded, K split across a cluster
+        for bn, sk in ((128, 2), (128, 4), (256, 2), (256, 4), (256, 8)):
+            if cout % bn == 0 and sk <= max_splits and sk <= kslabs // 2:
+                out.append((6, bn, sk))
     out.extend((3, bn, 1) for bn in band)
     return out
 
 
-def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=()):
+def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=(),
+                 dense_pool: bool = False):
     """Time launch(variant, block_n, splits) for every configuration the layer admits
     (on its real operands, device time via time_graph) and return the fastest."""
     best, best_ms = (0, 0, 1), float("inf")
-    for cfg in candidates(cout, T, kslabs, band=band):
+    for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool):
         ms = time_graph(lambda: launch(*cfg), reps)
         if ms < best_ms:
             best, best_ms = cfg, ms
@@ -267,6 +283,67 @@ def device_status(stream_tensor: torch.Tensor | None = None) -> int:
 
 
 # ---- reference-API entries ----------------------------------------------------------------
+def dense_conv_weight(w_khwc: torch.Tensor, H: int, W: int, *,
+                      pool: bool = False) -> torch.Tensor:
+    """A 3x3 / stride 1 / padding 1 conv on H x W images (H, W <= 2) as one dense matrix:
+    every output pixel's window covers the whole image, so the conv is a linear map from
+    the image's H*W*Cin inputs (NHWC order) to its H*W*Cout outputs, and
+    W'[(p, co), (q, ci)] = w[co, qh - ph + 1, qw - pw + 1, ci].  The padding taps, whose
+    products are zero (5 of the 9 at 2x2, 8 of 9 at 1x1), drop out of the GEMM.
+    pool: rows ordered (co, p) instead, so that the 2x2 max-pool is an OR over 4
+    consecutive outputs (snnb_conv3x3_lif_dense with pool).
+    w_khwc [Cout, 3, 3, Cin] -> [H*W*Cout, H*W*Cin], same dtype and device."""
+    assert w_khwc.ndim == 4 and tuple(w_khwc.shape[1:3]) == (3, 3)
+    assert 1 <= H <= 2 and 1 <= W <= 2, (H, W)
+    assert not pool or (H, W) == (2, 2)
+    Cout, Cin = w_khwc.shape[0], w_khwc.shape[3]
+    out = w_khwc.new_zeros(H * W, Cout, H * W, Cin)
+    for ph in range(H):
+        for pw in range(W):
+            for qh in range(H):
+                for qw in range(W):
+                    out[ph * W + pw, :, qh * W + qw, :] = w_khwc[:, qh - ph + 1, qw - pw + 1, :]
+    if pool:
+        out = out.transpose(0, 1)
+    return out.reshape(H * W * Cout, H * W * Cin).contiguous()
+
+
+def dense_conv_bias(bias: torch.Tensor, H: int, W: int, *, pool: bool = False) -> torch.Tensor:
+    """The bias of dense_conv_weight's outputs: b'[co] for row (p, co), or (co, p) with
+    pool."""
+    b = bias.float()
+    return (b.repeat_interleave(H * W) if pool else b.repeat(H * W)).contiguous()
+
+
+def conv3x3_lif_dense(x: torch.Tensor, wd: torch.Tensor, bd: torch.Tensor, *,
+                      neuron: str = "lif", tau: float = 2.0, decay=None,
+                      decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
+                      v_reset: float = 0.0, pool: bool = False,
+                      out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
+                      splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """conv3x3_lif for images of at most 2x2 pixels as one dense GEMM per image
+    (snnb_conv3x3_lif_dense): x [T, B, H, W, Cin] bf16, wd / bd from dense_conv_weight /
+    dense_conv_bias (with the same `pool`) -> spikes [T, B, Ho, Wo, Cout] bf16."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
+    T, B, H, W, Cin = x.shape
+    assert wd.dtype == torch.bfloat16 and wd.is_contiguous() and wd.shape[1] == H * W * Cin
+    Cout = wd.shape[0] // (H * W)
+    assert bd.dtype == torch.float32 and bd.is_contiguous() and bd.numel() == H * W * Cout
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    Ho, Wo = (1, 1) if pool else (H, W)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
+    ws, ws_bytes = _workspace(workspace, 1 if variant == 6 else splits, T, B, 1, 1,
+                              H * W * Cout, x.device)
+    st = _lib.lib().snnb_conv3x3_lif_dense(
+        _lib.ptr(x), T, B, H, W, Cin, _lib.ptr(wd), _lib.ptr(bd), Cout, df, sc, thr, vr, hard,
+        int(bool(pool)), int(variant), int(block_n), int(splits), _lib.ptr(ws), ws_bytes,
+        _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_conv3x3_lif_dense")
+    return out
+
+
 def weight_khwc(w: torch.Tensor) -> torch.Tensor:
     """torch conv weight [Cout, Cin, 3, 3] -> the kernels' K-major [Cout, 3, 3, Cin] bf16."""
     return w.detach().permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)

@@ -71,9 +71,13 @@ class SpikingVGG:
 
     def __init__(self, P, *, T: int = 4, tau: float = 2.0, decay_input: bool = True,
                  v_threshold: float = 1.0, v_reset: float = 0.0, soft_reset: bool = False,
-                 neuron: str = "lif", device="cuda", autotune: bool = True):
+                 neuron: str = "lif", device="cuda", autotune: bool = True,
+                 dense_small: bool = True):
         self.T = T
         self.autotune = autotune
+        # unpooled 3x3 layers on images of at most 2x2 pixels run as dense GEMMs
+        self.dense_small = dense_small
+        self._dense_w = {}
         self.choice = {}          # (layer, B, H, W) -> (variant, block_n) picked by timing
         self.lif = dict(neuron=neuron, tau=tau, decay_input=decay_input, soft_reset=soft_reset,
                         v_threshold=v_threshold, v_reset=v_reset)
@@ -135,12 +139,27 @@ class SpikingVGG:
             if i == 0:
                 fn = (lambda L=L, o=bufs[0]: KC.first_conv_lif(img, L["w"], L["b"], T=T,
                                                              pool=L["pool"], out=o, **self.lif))
+            elif h <= 2 and w <= 2 and self.dense_small and (not L["pool"] or h == w == 2):
+                # the whole image is every output pixel's window: a dense GEMM over the
+                # image's pixels x channels (no zero-padding taps), K1's linear form
+                wd, bd = self._dense(i, h, w)
+                K, N = h * w * L["cin"], h * w * L["cout"]
+                fn = self._tuned(("dconv", i, B, h, w), N, K // 64,
+                                 lambda v, bn, sp, L=L, wd=wd, bd=bd, x=x_prev, o=bufs[i],
+                                 NN=N:
+                                 KC.conv3x3_lif_dense(x, wd, bd, pool=L["pool"], out=o,
+                                                      variant=v, block_n=bn, splits=sp,
+                                                      workspace=self._ws(T, B, 1, 1, NN,
+                                                                         1 if v == 6 else sp),
+                                                      **self.lif),
+                                 dense_pool=L["pool"])
             else:
                 fn = self._tuned(("conv", i, B, h, w), L["cout"], 9 * L["cin"] // 64,
                                  lambda v, bn, sp, L=L, x=x_prev, o=bufs[i], hh=h, ww=w:
                                  KC.conv3x3_lif(x, L["w"], L["b"], pool=L["pool"], out=o,
                                                 variant=v, block_n=bn, splits=sp,
-                                                workspace=self._ws(T, B, hh, ww, L["cout"], sp),
+                                                workspace=self._ws(T, B, hh, ww, L["cout"],
+                                                                   1 if v == 6 else sp),
                                                 **self.lif),
                                  band=KC.band_block_ns(w, L["cin"], L["cout"]))
             steps.append((f"conv{i + 1}_{L['cin']}x{L['cout']}@{h}", flops, fn))
@@ -155,7 +174,8 @@ class SpikingVGG:
                                       lambda v, bn, sp, f=f, x=hcur, o=fbufs[j], NN=N:
                                       KC.linear_lif(x, f["w"], f["b"], out=o, variant=v,
                                                     block_n=bn, splits=sp,
-                                                    workspace=self._ws(T, B, 1, 1, NN, sp),
+                                                    workspace=self._ws(T, B, 1, 1, NN,
+                                                                      1 if v == 6 else sp),
                                                     **self.lif))))
             hcur = fbufs[j]
         f = self.fcs[-1]
@@ -164,6 +184,15 @@ class SpikingVGG:
         steps.append((f"fc{len(self.fcs)}_{K}x{N}", 2 * T * B * K * N,
                       (lambda f=f, x=hcur: head(x, f["w"], f["b"], out=out))))
         return steps, out
+
+    def _dense(self, i, h, w):
+        """Dense-GEMM weights of conv layer i on h x w images (dense_conv_weight), cached."""
+        key = (i, h, w)
+        if key not in self._dense_w:
+            L = self.layers[i]
+            self._dense_w[key] = (KC.dense_conv_weight(L["w"], h, w, pool=L["pool"]),
+                                  KC.dense_conv_bias(L["b"], h, w, pool=L["pool"]))
+        return self._dense_w[key]
 
     def _ws(self, T, B, H, W, Cout, splits):
         """Split-K workspace, one buffer shared by every layer of the engine (layers run one
@@ -175,21 +204,24 @@ class SpikingVGG:
             self._workspace = torch.empty(need // 4, device=self.device, dtype=torch.float32)
         return self._workspace
 
-    def _tuned(self, key, cout, kslabs, launch, band=()):
+    def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False):
         """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
         call times every (variant, block_n, splits) the layer admits and keeps the fastest."""
         def run():
             if key not in self.choice:
-                self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs, band=band) \
+                self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs, band=band,
+                                                   dense_pool=dense_pool) \
                     if self.autotune else (0, 0, 1)
             return launch(*self.choice[key])
         return run
 
     def kernel_launches(self, B: int) -> int:
         """Kernel launches of one forward at batch B after its layers were tuned: one per
-        layer, plus the split-K finish (sum + bias + neuron) of every split-K layer."""
+        layer, plus the split-K finish (sum + bias + neuron) of every two-launch split-K
+        layer (the cluster split-K form, variant 6, finishes in its own launch)."""
         n = len(self.layers) + len(self.fcs)
-        return n + sum(1 for k, c in self.choice.items() if k[2] == B and c[2] > 1)
+        return n + sum(1 for k, c in self.choice.items()
+                       if k[2] == B and c[2] > 1 and c[0] != 6)
 
     def forward(self, img: torch.Tensor, *, per_step_logits: bool = False) -> torch.Tensor:
         """img [B, 3, H, W] (direct encoding: the same image at every step) or
