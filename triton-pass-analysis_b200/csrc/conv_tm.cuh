@@ -271,7 +271,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
-    pdl_wait();
+    // Programmatic dependent launch: only the activation loads read what the previous
+    // kernel wrote, so each producer waits for it just before its first activation load --
+    // the tile decode, the first weight loads and every other role's setup overlap the
+    // previous kernel's tail.  Everything this kernel writes follows those loads (through
+    // the full / accumulator barriers).
     pdl_trigger();
 
     constexpr int W1 = 5 + NP;                    // first warp of the second epilogue set
@@ -281,6 +285,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         // whole schedule, as the MMA warp does)
         const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
         uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
+        bool dep_ready = false;                 // griddepcontrol.wait done (this warp)
         for (int item = item0; item < num_items; item += item_step) {
             Tile tl[MH];
 #pragma unroll
@@ -292,29 +297,42 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int stage = (int)(g % STAGES);
                 const uint32_t phase = (g / STAGES) & 1u;
                 failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                const int tap = kb / p.cin_blocks;
+                const int cb = kb - tap * p.cin_blocks;
+                const int r = p.taps == 9 ? tap / 3 : 1;
+                const int s = p.taps == 9 ? tap % 3 : 1;
+                // the stage's weight rows first (no kernel writes them), then, once the
+                // previous kernel has completed, its activation box(es)
                 if (!failed && tc::elect_one()) {
-                    const int tap = kb / p.cin_blocks;
-                    const int cb = kb - tap * p.cin_blocks;
-                    const int r = p.taps == 9 ? tap / 3 : 1;
-                    const int s = p.taps == 9 ? tap % 3 : 1;
                     if constexpr (PAIR) {
                         // both CTAs' bytes complete the even CTA's full barrier
                         const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
                         if (rank == 0) tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-                        tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
-                                             cb * 64, 0, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
-                                             tl[0].img0);
                         tc::tma_load_3d_pair(sbase + S::B_OFF + stage * S::B_TILE, &tmB, fb,
                                              cb * 64, tap, tl[0].n0 + (int)rank * (BN / 2));
                     } else {
                         tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
+                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
+                                        full_bar(stage), cb * 64, tap, tl[0].n0);
+                    }
+                }
+                __syncwarp();
+                if (!dep_ready) {
+                    pdl_wait();
+                    dep_ready = true;
+                }
+                if (!failed && tc::elect_one()) {
+                    if constexpr (PAIR) {
+                        const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
+                        tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
+                                             cb * 64, 0, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
+                                             tl[0].img0);
+                    } else {
 #pragma unroll
                         for (int h = 0; h < MH; ++h)
                             tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
                                             &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 + s - 1,
                                             tl[h].h0 + r - 1, tl[h].img0);
-                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
-                                        full_bar(stage), cb * 64, tap, tl[0].n0);
                     }
                 }
                 __syncwarp();
@@ -540,6 +558,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 release_acc(a);
                 continue;
             }
+            // (not cluster split-K) the next slice's columns are loaded from TMEM while this
+            // slice's neurons run
+            float rn[HC];
+            if constexpr (!CK)
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c_lo * 32 + set * HC, rn);
 #pragma unroll 1
             for (int c = c_lo; c < c_hi; ++c) {
                 float r[HC];
@@ -566,8 +589,13 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         }
                     }
                 } else {
-                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + c * 32 + set * HC, r);
                     tc::tmem_wait_ld();
+                    tc::reg_fence16(rn);                // rn is valid only after the wait
+#pragma unroll
+                    for (int e = 0; e < HC; ++e) r[e] = rn[e];
+                    if (c + 1 < c_hi)
+                        tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * BN + (c + 1) * 32 +
+                                      set * HC, rn);
                     if (c == NCH - 1) release_acc(a);   // accumulator fully read: hand it back
                 }
                 transpose(r);

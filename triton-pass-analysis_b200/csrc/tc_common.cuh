@@ -241,6 +241,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
 }
+// Ties later uses of r to this point of the instruction stream: after tcgen05.wait::ld, so
+// that no use of an asynchronously loaded register is scheduled before the wait.
+__device__ __forceinline__ void reg_fence16(float (&r)[16]) {
+    asm volatile(""
+                 : "+f"(r[0]), "+f"(r[1]), "+f"(r[2]), "+f"(r[3]), "+f"(r[4]), "+f"(r[5]),
+                   "+f"(r[6]), "+f"(r[7]), "+f"(r[8]), "+f"(r[9]), "+f"(r[10]), "+f"(r[11]),
+                   "+f"(r[12]), "+f"(r[13]), "+f"(r[14]), "+f"(r[15])
+                 :
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
     uint32_t u[16];
     asm volatile(
