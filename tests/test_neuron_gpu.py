@@ -1,5 +1,7 @@
 """K2 parity: the sm_100a multi-step neuron vs the CPU oracle and the reference's
 golden vectors (bit-exact spikes, counts and potentials)."""
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -197,15 +199,24 @@ from test_oracle_golden import CE, CE_CASES   # noqa: E402
 
 
 def _flip_ok(got, ref, vpre, th, exact):
-    """Spikes equal, or (EIF: CUDA expf vs numpy exp) different only where the charged
-    potential is within 1e-5 of the threshold, in at most 0.1% of the elements."""
+    """Spikes equal, or (EIF: CUDA expf vs numpy exp) each neuron's first differing step one
+    whose charged potential is within 2e-3 of the threshold (after a flip the two runs'
+    states legitimately part: reset against no reset), in at most 0.1% of the elements.
+    The EIF window is wider than LIF's 1e-4 because the EIF map amplifies differences: its
+    slope dv'/dv = decay + exp((v - v_rh) / delta_T) is ~2.5 near the threshold with these
+    parameters, so a 2-ulp expf difference can grow to ~1e-3 over 16 steps (measured worst
+    case on B200: 6.9e-4 over 180 seeded cases)."""
     if exact:
         assert np.array_equal(got, ref), int((got != ref).sum())
         return
     bad = got != ref
-    near = np.abs(vpre - th) <= 1e-5
-    assert not (bad & ~near).any(), int((bad & ~near).sum())
-    assert bad.mean() <= 1e-3
+    assert bad.mean() <= 1e-3, bad.mean()
+    cols = np.nonzero(bad.any(0))[0]
+    if cols.size:
+        first = bad[:, cols].argmax(0)
+        thr = np.broadcast_to(th, vpre.shape)
+        d = np.abs(vpre[first, cols] - thr[first, cols])
+        assert (d < 2e-3).all(), float(d.max())
 
 
 @pytest.mark.parametrize("k", CE_CASES)
@@ -239,7 +250,7 @@ def test_cuba_eif_match_reference_golden(k):
 ])
 def test_cuba_eif_against_oracle(model, dtype, shape, layout, thr_mode):
     K = _nk()
-    g = OP.gen(hash((model, dtype, shape, layout, thr_mode)) % 100000)
+    g = OP.gen(zlib.crc32(repr((model, dtype, shape, layout, thr_mode)).encode()) % 100000)
     x = (torch.randn(*shape, generator=g) * (0.3 if model == "eif" else 1.0)).to(
         getattr(torch, dtype))
     C = shape[2]

@@ -180,30 +180,38 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
-    pdl_wait();
+    // Programmatic dependent launch: the producer waits for the previous kernel only before
+    // its first activation load (see conv_lif_tm_kernel).
     pdl_trigger();
 
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
         int stage = 0, istage = 0;
         uint32_t phase = 0, iphase = 0, issued = 0, failed = 0;
+        bool dep_ready = false;                 // griddepcontrol.wait done
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_tile(tile, p, BN);
             for (int t = 0; t < p.T; ++t) {
                 const int f0 = t * p.B + tl.img0;
                 for (int kb = 0; kb < KB; ++kb) {
                     failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                    const int tap = kb / p.cin_blocks;
+                    const int cb = kb - tap * p.cin_blocks;
+                    const int r = p.taps == 9 ? tap / 3 : 1;
+                    const int s = p.taps == 9 ? tap % 3 : 1;
                     if (!failed && tc::elect_one()) {
-                        const int tap = kb / p.cin_blocks;
-                        const int cb = kb - tap * p.cin_blocks;
-                        const int r = p.taps == 9 ? tap / 3 : 1;
-                        const int s = p.taps == 9 ? tap % 3 : 1;
                         tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
-                        tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
-                                        full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
                                         cb * 64, tap, tl.n0);
                     }
+                    __syncwarp();
+                    if (!dep_ready) {
+                        pdl_wait();
+                        dep_ready = true;
+                    }
+                    if (!failed && tc::elect_one())
+                        tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
+                                        full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
                     __syncwarp();
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     if (!failed) {
@@ -410,7 +418,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 64 && p.wq) prefetch_weights_l2(p);
-    pdl_wait();
+    // Programmatic dependent launch: the producer waits for the previous kernel only before
+    // its first activation load (the resident weights are loaded before that); everything
+    // this kernel writes follows those loads through the barriers.
     pdl_trigger();
 
     // Failure protocol: every role walks the whole schedule; a bounded wait that gives up
@@ -421,6 +431,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         // ------------------------------------------------------------- TMA producer
         int stage = 0, cur_nb = -1, istage = 0;
         uint32_t phase = 0, wloads = 0, failed = 0, issued = 0, iphase = 0, wissued = 0;
+        bool dep_ready = false;                 // griddepcontrol.wait done
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_band(tile, p, BN);
             const int nb = tile / p.mtiles;
@@ -445,6 +456,10 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 const int f = t * p.B + tl.img0;
                 for (int cb = 0; cb < CB; ++cb) {
                     failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                    if (!dep_ready) {
+                        pdl_wait();
+                        dep_ready = true;
+                    }
                     if (!failed && tc::elect_one()) {
                         tc::mbar_expect_tx(full_bar(stage), st_bytes);
                         const uint32_t dst = sbase + a_off + (uint32_t)stage * st_bytes;
