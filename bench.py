@@ -539,18 +539,23 @@ class ConvLayerWorkload:
     name = "conv"
     flush_l2 = True
 
-    def __init__(self, cin=512, cout=512, H=56, B=64, T=4, p=0.15, fixed=None):
+    def __init__(self, cin=512, cout=512, H=56, B=64, T=4, p=0.15, fixed=None, packed="none"):
         self.cin, self.cout, self.H, self.B, self.T, self.p = cin, cout, H, B, T, p
         self.fixed = fixed
+        # packed spikes between layers: "in" / "out" / "both" run snnb_conv3x3_lif_packed
+        self.pk_in, self.pk_out = packed in ("in", "both"), packed in ("out", "both")
+        self.packed = packed
         self.flops = 2 * T * B * H * H * cout * cin * 9
-        self.metric = f"fused conv3x3+BN+LIF+maxpool TFLOP/s (Cin={cin}, Cout={cout}, H=W={H}, B={B}, T={T})"
+        pk = "" if packed == "none" else f", packed spikes {packed}"
+        self.metric = f"fused conv3x3+BN+LIF+maxpool TFLOP/s (Cin={cin}, Cout={cout}, H=W={H}, B={B}, T={T}{pk})"
         self.unit = "TFLOP/s"
         self.dtype = "bf16"
 
     def config(self):
         return {"workload": f"conv_layer_{self.cin}x{self.cout}@{self.H}", "T": self.T,
                 "B": self.B, "Cin": self.cin, "Cout": self.cout, "H": self.H, "W": self.H,
-                "spike_p": self.p, "pool": "max 2x2", "l2": "256 MB buffer written before every step"}
+                "spike_p": self.p, "pool": "max 2x2", "packed_spikes": self.packed,
+                "l2": "256 MB buffer written before every step"}
 
     def setup(self, rank, world, dist=None):
         from snn_compiler.kernels import conv as KC
@@ -564,6 +569,23 @@ class ConvLayerWorkload:
         self.b = torch.rand(self.cout, device="cuda", generator=g) * 0.9 + 0.3
         self.out = torch.empty(T, B, H // 2, H // 2, self.cout, device="cuda", dtype=torch.bfloat16)
         self.ws = None
+        if self.pk_in or self.pk_out:
+            # packed spikes: the T-folded kernel; the fastest channel block
+            self.xin = KC.pack_spikes(self.x) if self.pk_in else self.x
+            if self.pk_out:
+                self.out = torch.empty(T, B, H // 2, H // 2, self.cout // 32, device="cuda",
+                                       dtype=torch.int32)
+            run = lambda bn: KC.conv3x3_lif_packed(self.xin, self.w, self.b, x_packed=self.pk_in,
+                                                   out_packed=self.pk_out, pool=True,
+                                                   block_n=bn, out=self.out)
+            if self.fixed:
+                self.choice = (2, self.fixed[1], 1)
+            else:
+                bns = [bn for bn in (64, 128, 256) if self.cout % bn == 0]
+                times = [KC.time_graph(lambda bn=bn: run(bn), 10) for bn in bns]
+                self.choice = (2, bns[times.index(min(times))], 1)
+            self.launches_per_step = 1
+            return
         # pick the fastest (variant, block_n) the way the VGG engine does
         run = lambda v, bn, sp: KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out,
                                                variant=v, block_n=bn, splits=sp)
@@ -575,6 +597,11 @@ class ConvLayerWorkload:
 
     def step(self):
         v, bn, sp = self.choice
+        if self.pk_in or self.pk_out:
+            self.KC.conv3x3_lif_packed(self.xin, self.w, self.b, x_packed=self.pk_in,
+                                       out_packed=self.pk_out, pool=True, block_n=bn,
+                                       out=self.out)
+            return
         self.KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out, variant=v, block_n=bn,
                             splits=sp, workspace=self.ws)
 
@@ -585,13 +612,14 @@ class ConvLayerWorkload:
         return self.flops / 1e12
 
     def e2e_setup(self):
-        self.hx = self.x.cpu().pin_memory()
-        self.hout = torch.empty(self.out.shape, dtype=torch.bfloat16).pin_memory()
-        self.h2d = self.hx.numel() * 2
-        self.d2h = self.hout.numel() * 2
+        xin = self.xin if (self.pk_in or self.pk_out) else self.x
+        self.hx = xin.cpu().pin_memory()
+        self.hout = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = self.hx.numel() * self.hx.element_size()
+        self.d2h = self.hout.numel() * self.hout.element_size()
 
     def e2e_step(self):
-        self.x.copy_(self.hx, non_blocking=True)
+        (self.xin if (self.pk_in or self.pk_out) else self.x).copy_(self.hx, non_blocking=True)
         self.step()
         self.hout.copy_(self.out, non_blocking=True)
 
@@ -946,6 +974,8 @@ def main():
     ap.add_argument("--load-choices", default=None,
                     help="vgg16: use a tuned kernel table instead of timing (e.g. under ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--packed", default="none", choices=["none", "in", "out", "both"],
+                    help="conv workload: packed spikes in / out (snnb_conv3x3_lif_packed)")
     ap.add_argument("--eager", action="store_true",
                     help="vgg16: launch the forward kernel by kernel instead of replaying CUDA "
                          "graphs (for kernel-replaying profilers; the same work)")
@@ -957,7 +987,7 @@ def main():
         fixed = tuple(int(v) for v in args.choice.split(",")) if args.choice else None
         if fixed and len(fixed) == 2:
             fixed = fixed + (1,)
-        wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed)
+        wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed, packed=args.packed)
     else:
         if args.workload == "lif":
             lt, ln = (int(v) for v in args.lif_shape.split(","))

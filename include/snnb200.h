@@ -247,6 +247,31 @@ int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64_t H, int64
                            void* workspace, int64_t workspace_bytes, void* out,
                            snnb_stream_t stream);
 
+/*
+ * K1 with packed spikes between layers (no counterpart in the reference, whose layers pass
+ * float / bf16 spike tensors): snnb_conv3x3_lif on the T-folded kernel (T in {2, 4, 8}) with
+ * its input and / or output as packed spikes -- NHWC with 32 channels per uint32 word,
+ * channel c in bit c % 32 of word c / 32 (LSB first, as snnb_bitpack packs rows of C
+ * channels), 1/16 of the bf16 bytes.  With x_packed the kernel stages each tile's packed
+ * input patch (pixels plus 1-pixel halo, every step) in shared memory once and expands every
+ * k-slab's A operand from it into bf16 in shared memory; the spikes are identical to
+ * snnb_conv3x3_lif's.
+ * x        : packed words [T*B, H, W, Cin/32] (x_packed, Cin % 64 == 0, 4-byte aligned),
+ *            or bf16 spikes [T*B, H, W, Cin]
+ * out      : packed words [T*B, Ho, Wo, Cout/32] (out_packed) or bf16 [T*B, Ho, Wo, Cout]
+ * block_n  : 0 = choose, 64 / 128 / 256 (32 also without x_packed)
+ * Returns SNNB_ERR_UNSUPPORTED when a tile's packed patch exceeds the kernel's 32 KB.
+ */
+int snnb_conv3x3_lif_packed(const void* x, int x_packed, int64_t T, int64_t B, int64_t H,
+                            int64_t W, int64_t Cin, const void* w, const float* bias,
+                            int64_t Cout, float decay, float input_scale, float v_threshold,
+                            float v_reset, int hard_reset, int pool, int out_packed, int block_n,
+                            void* out, snnb_stream_t stream);
+
+/* Packed spikes [rows, C/32] uint32 (C % 32 == 0) -> bf16 {0,1} [rows, C] (16-byte aligned). */
+int snnb_unpack_spikes(const void* words, int64_t rows, int64_t C, void* out,
+                       snnb_stream_t stream);
+
 /* Workspace bytes snnb_conv3x3_lif / snnb_linear_lif (H = W = 1) need for `splits`. */
 int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cout,
                                    int splits);

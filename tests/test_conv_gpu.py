@@ -267,3 +267,59 @@ def test_bad_geometry_is_rejected():
     w = torch.zeros(64, 3, 3, 20, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError):
         C.conv3x3_lif(x, w, torch.zeros(64, device=DEV))
+
+
+# ---- packed spikes between layers (snnb_conv3x3_lif_packed / snnb_unpack_spikes) ------------
+PK_GEOMS = [(4, 1, 64, 64, 32), (4, 2, 64, 128, 16), (4, 2, 128, 256, 8), (4, 8, 256, 512, 4),
+            (4, 32, 512, 512, 2), (8, 2, 128, 128, 8), (2, 5, 64, 128, 7), (4, 2, 64, 64, 56)]
+
+
+@pytest.mark.parametrize("block_n", [64, 128, 256])
+@pytest.mark.parametrize("mode", [(True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("geom", PK_GEOMS)
+def test_packed_spikes_identical_to_bf16_path(geom, mode, block_n):
+    """Packed input (patch expanded to the bf16 A operand in shared memory) and packed
+    output (16-channel half-words) give exactly the spikes of the bf16 T-folded kernel with
+    the same channel block, pooled and not."""
+    T, B, Cin, Cout, H = geom
+    x_packed, out_packed = mode
+    if Cout % block_n:
+        pytest.skip("block_n must divide Cout")
+    C = _C()
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.2, sum(geom) * 5 + block_n, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    wd = C.weight_khwc(w).to(DEV)
+    bd = b.to(DEV)
+    xin = C.pack_spikes(xd) if x_packed else xd
+    for pool in ((False, True) if H % 2 == 0 else (False,)):
+        ref = C.conv3x3_lif(xd, wd, bd, tau=2.0, v_threshold=THR, variant=2, block_n=block_n,
+                            pool=pool)
+        got = C.conv3x3_lif_packed(xin, wd, bd, x_packed=x_packed, out_packed=out_packed,
+                                   tau=2.0, v_threshold=THR, pool=pool, block_n=block_n)
+        assert C.device_status() == 0
+        if out_packed:
+            assert got.dtype == torch.int32 and got.shape[-1] == Cout // 32
+            got = C.unpack_spikes(got)
+        assert ref.float().sum() > 0
+        assert torch.equal(got, ref), (pool, (got != ref).float().mean().item())
+
+
+def test_pack_unpack_round_trip_and_packed_limits():
+    C = _C()
+    g = OP.gen(77)
+    x = (torch.rand(3, 5, 7, 96, generator=g) < 0.3).to(torch.bfloat16).to(DEV)
+    words = C.pack_spikes(x)
+    assert words.shape == (3, 5, 7, 3) and words.dtype == torch.int32
+    # bit c % 32 of word c / 32, LSB first
+    ref = (x.cpu().reshape(-1, 3, 32).to(torch.int64) << torch.arange(32)).sum(-1)
+    assert torch.equal(words.cpu().reshape(-1, 3).to(torch.int64) & 0xffffffff, ref)
+    assert torch.equal(C.unpack_spikes(words), x)
+    w = torch.zeros(64, 3, 3, 48, device=DEV, dtype=torch.bfloat16)
+    xp = torch.zeros(4, 2, 8, 8, 2, device=DEV, dtype=torch.int32)    # Cin = 64
+    with pytest.raises(AssertionError):                                # Cin mismatch
+        C.conv3x3_lif_packed(xp, w, torch.zeros(64, device=DEV), x_packed=True, out_packed=False)
+    # Cin = 32 (one word per pixel) is not a multiple of 64: the packed-input kernel refuses it
+    with pytest.raises(RuntimeError):
+        C.conv3x3_lif_packed(torch.zeros(4, 2, 8, 8, 1, dtype=torch.int32, device=DEV),
+                             torch.zeros(64, 3, 3, 32, device=DEV, dtype=torch.bfloat16),
+                             torch.zeros(64, device=DEV), x_packed=True, out_packed=False)

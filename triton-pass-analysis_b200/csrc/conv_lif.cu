@@ -1092,7 +1092,7 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
-    ConvParams p;
+    ConvParams p = {};
     p.T = T; p.B = B; p.H = H; p.W = W; p.Cin = Cin; p.Cout = Cout;
     p.bw = W; p.bh = bh; p.bn = 1;
     p.tiles_w = 1; p.tiles_h = (H + bh - 1) / bh;
@@ -1131,8 +1131,18 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  const float* bias, int Cout, int taps, float df, float sc, float thr,
                  float v_reset, int hard, int pool, int variant, int block_n, int splits,
                  void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s,
-                 const void* res = nullptr, int res_f32 = 0) {
+                 const void* res = nullptr, int res_f32 = 0, int x_packed = 0,
+                 int out_packed = 0) {
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
+    // packed spikes in / out: the T-folded kernel (variant 2), one launch (no split-K), no
+    // residual; packed input for 3x3 convs with Cin % 64 == 0
+    if (x_packed || out_packed) {
+        if (variant == 0) variant = 2;
+        if (variant != 2 || splits > 1 || res || pool == 2) return SNNB_ERR_UNSUPPORTED;
+        if (x_packed && (taps != 9 || Cin % 64 != 0)) return SNNB_ERR_UNSUPPORTED;
+        if (x_packed && block_n == 32) return SNNB_ERR_UNSUPPORTED;
+        if (reinterpret_cast<uintptr_t>(out) & 3u) return SNNB_ERR_ARG;
+    }
     if (res && (pool || !aligned16(res))) return res && pool ? SNNB_ERR_UNSUPPORTED : SNNB_ERR_ARG;
     // pool == 2: OR over groups of 4 consecutive output columns (the dense form of a pooled
     // 2x2-image conv, snnb_conv3x3_lif_dense); T-folded epilogues only
@@ -1146,7 +1156,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     }
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
     if (Cin % 8 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
-    if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return SNNB_ERR_ARG;
+    if (!aligned16(x) || !aligned16(w) || (!out_packed && !aligned16(out))) return SNNB_ERR_ARG;
     if (pool == 1 && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
     if (variant < 0 || variant > 6) return SNNB_ERR_ARG;
@@ -1216,7 +1226,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         BN = bn_max;
         // narrower channel blocks until the grid covers the SMs
         if (mh == 2 && BN > 128) BN = 128;
-        const int bn_min = cg == 2 ? 64 : 32;
+        const int bn_min = (cg == 2 || x_packed) ? 64 : 32;
         while (BN > bn_min && ((mtiles + mh * cg - 1) / (mh * cg)) * (Cout / BN) * splits * cg < 148)
             BN /= 2;
     }
@@ -1226,11 +1236,17 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
         if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
     }
+    if (x_packed) {
+        const int64_t patch = (int64_t)T * bn * (bh + 2) * (bw + 2) * (Cin / 8);
+        if (patch > packed_patch_limit()) return SNNB_ERR_UNSUPPORTED;
+    }
     int* status = device_status_ptr();
     if (!status) return SNNB_ERR_CUDA;
     CUtensorMap ta, tb;
-    int rc;
-    if (variant == 2) {
+    int rc = SNNB_OK;
+    if (x_packed) {
+        // no activation tensor map: the kernel reads the packed patch itself
+    } else if (variant == 2) {
         // activation map: dims (Cin, T, W, H, B), box (64, T, bw, bh, bn): one box = the
         // pixel block at every step, rows ordered (pixel, t) -- a pixel's T steps are
         // adjacent accumulator rows, i.e. adjacent lanes of one epilogue warp
@@ -1258,7 +1274,8 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
-    ConvParams p;
+    if (x_packed) ta = tb;                // unused by the packed-input kernel
+    ConvParams p = {};
     p.T = T; p.B = B; p.H = H; p.W = W; p.Cin = Cin; p.Cout = Cout;
     p.bw = bw; p.bh = bh; p.bn = bn;
     p.tiles_w = (W + bw - 1) / bw; p.tiles_h = (H + bh - 1) / bh;
@@ -1268,6 +1285,8 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.bias = bias; p.out = static_cast<__nv_bfloat16*>(out); p.status = status;
     p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
     p.res = res; p.res_f32 = res_f32;
+    p.xq = x_packed ? static_cast<const uint32_t*>(x) : nullptr;
+    p.out_packed = out_packed ? 1 : 0;
     p.splits = ck ? 1 : splits;
     p.partial = splits > 1 && !ck ? static_cast<float*>(workspace) : nullptr;
     const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
@@ -1275,6 +1294,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
     p.num_tiles = (int)ntiles;
     if (ck) return launch_tm_cluster(T, BN, splits, ta, tb, p, s);
+    if (x_packed) return launch_tm_packed(T, BN, ta, tb, p, s);
     if (variant == 2) {
         switch (T) {
             case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;
@@ -1375,7 +1395,7 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SNNB_OK) return rc;
-    ConvParams p;
+    ConvParams p = {};
     p.T = iT; p.B = iB; p.H = 1; p.W = 1; p.Cin = iK; p.Cout = iN;
     p.bw = bw; p.bh = bh; p.bn = bn;
     p.tiles_w = 1; p.tiles_h = 1;
@@ -1398,6 +1418,22 @@ extern "C" int snnb_linear_f32(const void* x, int64_t T, int64_t B, int64_t K, c
     return launch_splitsum(out, 1, (int64_t)T * B, iN, bias, s);
 }
 
+extern "C" int snnb_conv3x3_lif_packed(const void* x, int x_packed, int64_t T, int64_t B,
+                                       int64_t H, int64_t W, int64_t Cin, const void* w,
+                                       const float* bias, int64_t Cout, float decay,
+                                       float input_scale, float v_threshold, float v_reset,
+                                       int hard_reset, int pool, int out_packed, int block_n,
+                                       void* out, snnb_stream_t stream) {
+    if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0 || T > 0x7fffffff ||
+        B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff || Cin > 0x7fffffff ||
+        Cout > 0x7fffffff)
+        return SNNB_ERR_ARG;
+    if (pool != 0 && pool != 1) return SNNB_ERR_ARG;
+    return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout, 9, decay,
+                        input_scale, v_threshold, v_reset, hard_reset, pool, 2, block_n, 1,
+                        nullptr, 0, out, static_cast<cudaStream_t>(stream), nullptr, 0,
+                        x_packed ? 1 : 0, out_packed ? 1 : 0);
+}
 extern "C" int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
                                       int64_t Cin, const void* wd, const float* bias_d,
                                       int64_t Cout, float decay, float input_scale,

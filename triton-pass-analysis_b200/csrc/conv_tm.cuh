@@ -32,6 +32,8 @@ struct ConvParams {
     int64_t wq_bytes;
     const void* res;              // residual input of the neuron or nullptr (no pooling then)
     int res_f32;                  // residual dtype: float32 (1) or bf16 (0)
+    const uint32_t* xq;           // packed-spike input [T*B][H][W][Cin/32] (T-folded kernel)
+    int out_packed;               // spikes stored packed, [T*B][Ho][Wo][Cout/32] uint32
 };
 
 struct Tile {
@@ -139,14 +141,16 @@ __device__ __forceinline__ void store_bits_bf16(__nv_bfloat16* dst, uint32_t bit
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
 // then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
-template <int BN, int STAGES, int TS, int MH, int CG = 1>
+// PATCH: bytes of the packed-spike input patch (packed-input form; 0 otherwise)
+template <int BN, int STAGES, int TS, int MH, int CG = 1, int PATCH = 0>
 struct SmemTM {
     static constexpr int P = 128 / TS;
     static constexpr int NCH = BN / 32;
     static constexpr int B_TILE = BN / CG * 128;       // weight rows this CTA stages
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = STAGES * MH * A_TILE_BYTES;
-    static constexpr int MASK_OFF = B_OFF + STAGES * B_TILE;           // 2 x 128 u32 (pool)
+    static constexpr int PATCH_OFF = B_OFF + STAGES * B_TILE;
+    static constexpr int MASK_OFF = PATCH_OFF + PATCH;                 // 2 x 128 u32 (pool)
     static constexpr int SB_OFF = MASK_OFF + 256 * 4;                  // BN f32 (bias)
     static constexpr int BAR_OFF = (SB_OFF + BN * 4 + 7) & ~7;
     static constexpr int NBARS = 2 * STAGES + 4 * MH + 1 + 2;         // + cluster split-K
@@ -174,16 +178,20 @@ struct SmemTM {
 // Two sets of 4 epilogue warps (warps 2-5 and 5+NP .. 8+NP) split every 32-column slice of
 // the accumulator into halves: the epilogue of a CTA's last work item, which no MMA
 // overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
-template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES, int SK = 1>
+template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES, int SK = 1,
+          int PATCH = 0>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
     constexpr bool PAIR = CG == 2;
     constexpr bool CK = SK > 1;
+    constexpr bool PKI = PATCH > 0;                 // packed-spike input (see below)
+    static_assert(!PKI || (MH == 1 && CG == 1 && !RES && SK == 1 && NP == 4),
+                  "packed input: single CTA, one M-tile, four producer warps");
     static_assert(!PAIR || MH == 1, "CTA pairs take one M-tile each");
     static_assert(!CK || (MH == 1 && CG == 1), "cluster split-K: one M-tile, single CTA");
     static_assert(!RES || (MH == 1 && CG == 1), "residual input: one M-tile, single CTA");
-    using S = SmemTM<BN, STAGES, TS, MH, CG>;
+    using S = SmemTM<BN, STAGES, TS, MH, CG, PATCH>;
     constexpr int P = S::P, NCH = S::NCH;
     static_assert(!CK || NCH % SK == 0, "cluster split-K: whole 32-column slices per CTA");
     static_assert(!CK || BN * 128 * 4 <= STAGES * (MH * A_TILE_BYTES + S::B_TILE),
@@ -238,7 +246,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(full_bar(s), 1);
+            // packed input: the weight copy's expect_tx plus one arrival per producer warp
+            // (its rows of the A tile written)
+            tc::mbar_init(full_bar(s), PKI ? 1 + NP : 1);
             tc::mbar_init(empty_bar(s), 1);
         }
         for (int a = 0; a < 2 * MH; ++a) {
@@ -279,7 +289,92 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     pdl_trigger();
 
     constexpr int W1 = 5 + NP;                    // first warp of the second epilogue set
-    if (warp == 0 || (warp >= 6 && warp < W1)) {
+    if (PKI && (warp == 0 || (warp >= 6 && warp < W1))) {
+        // ------------------------------------------------ packed-input producers (NP == 4)
+        // Per tile the four warps stage the packed spikes of the tile's pixels and their
+        // 1-pixel halo at every step in shared memory ([t][image][PH][PW][Cin/32] words,
+        // zero outside the layer: the conv padding), then for each k-slab (tap, 64-channel
+        // block) each thread expands its A row -- pixel row / TS at step row % TS, shifted by
+        // the tap -- to 64 bf16 {0, 1} values written in the 128-byte-swizzled layout a TMA
+        // box would have produced.  Warp 0 also copies the slab's weight rows by TMA.
+        if constexpr (PKI) {
+            const int pi = warp == 0 ? 0 : warp - 5;
+            const int prow = pi * 32 + lane;                 // A row this thread writes
+            const int px = prow / TS, pt = prow % TS;
+            const int lw = px % p.bw, lh = (px / p.bw) % p.bh, ln = px / (p.bw * p.bh);
+            const int PW = p.bw + 2, PH = p.bh + 2, CW = p.Cin >> 5;
+            uint32_t* patch = reinterpret_cast<uint32_t*>(smem + S::PATCH_OFF);
+            const int units = TS * p.bn * PH * PW * (CW >> 1);      // 8-byte units
+            uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
+            bool dep_ready = false;
+            for (int item = item0; item < num_items; item += item_step) {
+                Tile tl;
+                half_tile(item, 0, tl);
+                int k0, k1;
+                krange(item, k0, k1);
+                if (!dep_ready) {
+                    pdl_wait();                      // the patch is the previous kernel's output
+                    dep_ready = true;
+                }
+                tc::named_bar_sync(4, NP * 32);      // the last tile's expansions are done
+                for (int u = prow; u < units; u += NP * 32) {
+                    int q = u / (CW >> 1);
+                    const int cu = u - q * (CW >> 1);
+                    const int pw = q % PW; q /= PW;
+                    const int ph = q % PH; q /= PH;
+                    const int pn = q % p.bn;
+                    const int t = q / p.bn;
+                    const int gw = tl.w0 - 1 + pw, gh = tl.h0 - 1 + ph, gn = tl.img0 + pn;
+                    uint2 v = make_uint2(0u, 0u);
+                    if (gw >= 0 && gw < p.W && gh >= 0 && gh < p.H && gn < p.B)
+                        v = __ldg(reinterpret_cast<const uint2*>(
+                            p.xq + ((((int64_t)t * p.B + gn) * p.H + gh) * p.W + gw) * CW) + cu);
+                    reinterpret_cast<uint2*>(patch)[u] = v;
+                }
+                tc::named_bar_sync(4, NP * 32);      // patch complete
+                for (int kb = k0; kb < k1; ++kb, ++g) {
+                    const int stage = (int)(g % STAGES);
+                    const uint32_t phase = (g / STAGES) & 1u;
+                    failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
+                    const int tap = kb / p.cin_blocks;
+                    const int cb = kb - tap * p.cin_blocks;
+                    const int r = tap / 3, s = tap % 3;
+                    if (pi == 0 && !failed && tc::elect_one()) {
+                        tc::mbar_expect_tx(full_bar(stage), (uint32_t)S::B_TILE);
+                        tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
+                                        full_bar(stage), cb * 64, tap, tl.n0);
+                    }
+                    __syncwarp();
+                    if (!failed) {
+                        const uint2 bits = *reinterpret_cast<const uint2*>(
+                            patch + (((pt * p.bn + ln) * PH + (lh + r)) * PW + (lw + s)) * CW +
+                            cb * 2);
+                        uint8_t* rowp = smem + S::A_OFF + stage * A_TILE_BYTES + prow * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t w8 = ((j < 4 ? bits.x : bits.y) >> (8 * (j & 3))) & 0xffu;
+                            *reinterpret_cast<uint4*>(rowp + ((j ^ (prow & 7)) << 4)) =
+                                spikes_to_bf16x8(w8);
+                        }
+                        tc::fence_proxy_async_smem();    // visible to the tensor core's reads
+                    }
+                    __syncwarp();
+                    if (!failed) {
+                        if (lane == 0) tc::mbar_arrive(full_bar(stage));
+                        ++issued;
+                        last_g = g;
+                    }
+                }
+            }
+            if (failed) {
+                // the weight copies of this warp still in flight (warp 0): bounded waits
+                uint32_t gg = last_g;
+                for (uint32_t k = 0; pi == 0 && k < issued && k < (uint32_t)STAGES; ++k, --gg)
+                    tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+                if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
+            }
+        }
+    } else if (warp == 0 || (warp >= 6 && warp < W1)) {
         // ------------------------------------------------------------- TMA producers
         // producer pi issues the stages g with g % NP == pi (g counts k-slabs over the
         // whole schedule, as the MMA warp does)
@@ -634,7 +729,28 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 };
                 lif_cols(std::integral_constant<bool, RES>{});
                 const int ch = tl.n0 + ch0;
-                if (!p.pool) {
+                // packed output: the TS lanes of a pixel gather the set's 16 channels of every
+                // step (bit = channel within the half-word) and lane kq stores step kq
+                auto store_packed = [&](bool ok, int y, int x, int Hs, int Ws) {
+                    uint32_t hw[TS];
+#pragma unroll
+                    for (int t = 0; t < TS; ++t)
+                        hw[t] = ((lb >> (t * NPT)) & ((1u << NPT) - 1u)) << (kq * NPT);
+#pragma unroll
+                    for (int bb = 1; bb < TS; bb <<= 1)
+#pragma unroll
+                        for (int t = 0; t < TS; ++t) hw[t] |= __shfl_xor_sync(0xffffffffu, hw[t], bb);
+                    uint32_t mine = hw[0];
+#pragma unroll
+                    for (int t = 1; t < TS; ++t) mine = kq == t ? hw[t] : mine;
+                    if (ok)
+                        reinterpret_cast<unsigned short*>(p.out)[
+                            ((((int64_t)kq * p.B + on) * Hs + y) * Ws + x) * (p.Cout >> 4) +
+                            ((tl.n0 + c * 32) >> 4) + set] = (unsigned short)mine;
+                };
+                if (!p.pool && p.out_packed) {
+                    store_packed(inside, oh, ow, p.H, p.W);
+                } else if (!p.pool) {
                     if (inside) {
 #pragma unroll
                         for (int t = 0; t < TS; ++t)
@@ -668,7 +784,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     smask[set * 128 + row] = lb;
                     tc::named_bar_sync(1 + set, 128);    // row neighbours' bits visible
                     lb |= smask[set * 128 + (row ^ (TS * p.bw))];
-                    if (pool_store) {
+                    if (p.out_packed) {
+                        store_packed(pool_store, oh >> 1, ow >> 1, Ho, Wo);
+                    } else if (pool_store) {
 #pragma unroll
                         for (int t = 0; t < TS; ++t)
                             store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * Ho + (oh >> 1)) * Wo +
@@ -702,5 +820,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // shared memory, so the neuron runs in the same launch.
 int launch_tm_cluster(int TS, int BN, int SK, const CUtensorMap& ta, const CUtensorMap& tb,
                       const ConvParams& p, cudaStream_t s);
+
+// Packed-spike-input launch of conv_lif_tm_kernel (conv_packed.cu); packed_patch_limit() is
+// the largest input patch (bytes) one CTA stages.
+int launch_tm_packed(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const ConvParams& p, cudaStream_t s);
+int packed_patch_limit();
 
 }  // namespace snnb

@@ -313,6 +313,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
+// Makes this thread's earlier generic-proxy shared-memory writes visible to the async proxy
+// (tcgen05.mma operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Orders this thread's earlier shared-memory writes (and those its CTA barrier made visible
 // to it) before its later arrivals on other CTAs' barriers.
 __device__ __forceinline__ void fence_acq_rel_cluster() {

@@ -37,6 +37,9 @@ SIGNATURES = {
     "snnb_conv3x3_lif_res": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, I32, I32,
                              I32, I32, P, I64, P, P],
     "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32, P, I64, P, P],
+    "snnb_conv3x3_lif_packed": [P, I32, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32,
+                                I32, I32, P, P],
+    "snnb_unpack_spikes": [P, I64, I64, P, P],
     "snnb_conv3x3_lif_dense": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32,
                                I32, I32, P, I64, P, P],
     "snnb_linear_mean": [P, I64, I64, I64, P, P, I64, P, P],

@@ -283,6 +283,57 @@ def device_status(stream_tensor: torch.Tensor | None = None) -> int:
 
 
 # ---- reference-API entries ----------------------------------------------------------------
+def pack_spikes(x: torch.Tensor) -> torch.Tensor:
+    """bf16 {0,1} spikes [..., C] (C % 32 == 0) -> packed int32 words [..., C/32]: channel c
+    in bit c % 32 of word c / 32 (snnb_bitpack's order)."""
+    from .binary import bitpack
+    assert x.shape[-1] % 32 == 0
+    return bitpack(x, ldw=x.shape[-1] // 32)
+
+
+def unpack_spikes(words: torch.Tensor, C: int | None = None) -> torch.Tensor:
+    """Packed int32 words [..., C/32] -> bf16 {0,1} spikes [..., C] (snnb_unpack_spikes)."""
+    assert words.is_cuda and words.is_contiguous() and words.dtype == torch.int32
+    C = words.shape[-1] * 32 if C is None else C
+    assert C == words.shape[-1] * 32
+    rows = words.numel() // words.shape[-1] if words.numel() else 0
+    out = torch.empty(*words.shape[:-1], C, device=words.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_unpack_spikes(_lib.ptr(words), rows, C, _lib.ptr(out),
+                                       _lib.stream_of(words))
+    _lib.check(st, "snnb_unpack_spikes")
+    return out
+
+
+def conv3x3_lif_packed(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *,
+                       x_packed: bool, out_packed: bool, neuron: str = "lif", tau: float = 2.0,
+                       decay=None, decay_input: bool = True, soft_reset: bool = False,
+                       v_threshold=1.0, v_reset: float = 0.0, pool: bool = False,
+                       block_n: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """conv3x3_lif with packed spikes in and / or out (snnb_conv3x3_lif_packed, T-folded
+    kernel): x [T, B, H, W, Cin] bf16, or int32 words [T, B, H, W, Cin/32] with x_packed;
+    the result [T, B, Ho, Wo, Cout] bf16, or words [T, B, Ho, Wo, Cout/32] with out_packed.
+    Same spikes as conv3x3_lif."""
+    assert x.is_cuda and x.is_contiguous() and x.ndim == 5
+    assert x.dtype == (torch.int32 if x_packed else torch.bfloat16)
+    T, B, H, W, cx = x.shape
+    Cin = cx * 32 if x_packed else cx
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and tuple(w.shape[1:]) == (3, 3, Cin)
+    Cout = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == Cout
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    Ho, Wo = (H // 2, W // 2) if pool else (H, W)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout // 32 if out_packed else Cout, device=x.device,
+                          dtype=torch.int32 if out_packed else torch.bfloat16)
+    st = _lib.lib().snnb_conv3x3_lif_packed(
+        _lib.ptr(x), int(bool(x_packed)), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias), Cout, df,
+        sc, thr, vr, hard, int(bool(pool)), int(bool(out_packed)), int(block_n), _lib.ptr(out),
+        _lib.stream_of(x))
+    _lib.check(st, "snnb_conv3x3_lif_packed")
+    return out
+
+
 def dense_conv_weight(w_khwc: torch.Tensor, H: int, W: int, *,
                       pool: bool = False) -> torch.Tensor:
     """A 3x3 / stride 1 / padding 1 conv on H x W images (H, W <= 2) as one dense matrix:
