@@ -350,11 +350,25 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             patch + (((pt * p.bn + ln) * PH + (lh + r)) * PW + (lw + s)) * CW +
                             cb * 2);
                         uint8_t* rowp = smem + S::A_OFF + stage * A_TILE_BYTES + prow * 128;
+                        // channel pairs (2i, 2i+1) of each 8-channel chunk -> one word of two
+                        // bf16: the even and odd bits of the chunk's byte are brought to bytes
+                        // 0 and 2 of v (one byte permute), (v >> 2i) & 0x10001 keeps the pair,
+                        // and the multiply by 0x3F80 (bf16 1.0) writes both halves
+                        const uint32_t ev[2] = {bits.x & 0x55555555u, bits.y & 0x55555555u};
+                        const uint32_t od[2] = {(bits.x >> 1) & 0x55555555u,
+                                                (bits.y >> 1) & 0x55555555u};
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
-                            const uint32_t w8 = ((j < 4 ? bits.x : bits.y) >> (8 * (j & 3))) & 0xffu;
-                            *reinterpret_cast<uint4*>(rowp + ((j ^ (prow & 7)) << 4)) =
-                                spikes_to_bf16x8(w8);
+                            const uint32_t k = (uint32_t)(j & 3);
+                            const uint32_t v = __byte_perm(ev[j >> 2], od[j >> 2],
+                                                           k | (k << 4) | ((k + 4) << 8) |
+                                                               ((k + 4) << 12));
+                            uint4 o;
+                            o.x = (v & 0x10001u) * 0x3F80u;
+                            o.y = ((v >> 2) & 0x10001u) * 0x3F80u;
+                            o.z = ((v >> 4) & 0x10001u) * 0x3F80u;
+                            o.w = ((v >> 6) & 0x10001u) * 0x3F80u;
+                            *reinterpret_cast<uint4*>(rowp + ((j ^ (prow & 7)) << 4)) = o;
                         }
                         tc::fence_proxy_async_smem();    // visible to the tensor core's reads
                     }
