@@ -317,6 +317,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     dep_ready = true;
                 }
                 tc::named_bar_sync(4, NP * 32);      // the last tile's expansions are done
+                // every unit an asynchronous 8-byte copy (zero fill outside the layer), all
+                // in flight at once
                 for (int u = prow; u < units; u += NP * 32) {
                     int q = u / (CW >> 1);
                     const int cu = u - q * (CW >> 1);
@@ -325,12 +327,13 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const int pn = q % p.bn;
                     const int t = q / p.bn;
                     const int gw = tl.w0 - 1 + pw, gh = tl.h0 - 1 + ph, gn = tl.img0 + pn;
-                    uint2 v = make_uint2(0u, 0u);
-                    if (gw >= 0 && gw < p.W && gh >= 0 && gh < p.H && gn < p.B)
-                        v = __ldg(reinterpret_cast<const uint2*>(
-                            p.xq + ((((int64_t)t * p.B + gn) * p.H + gh) * p.W + gw) * CW) + cu);
-                    reinterpret_cast<uint2*>(patch)[u] = v;
+                    const bool in = gw >= 0 && gw < p.W && gh >= 0 && gh < p.H && gn < p.B;
+                    const uint32_t* src = in ? p.xq + ((((int64_t)t * p.B + gn) * p.H + gh) *
+                                                           p.W + gw) * CW + 2 * cu
+                                             : p.xq;
+                    tc::cp_async_8(sbase + S::PATCH_OFF + (uint32_t)u * 8u, src, in ? 8u : 0u);
                 }
+                tc::cp_async_wait_all();
                 tc::named_bar_sync(4, NP * 32);      // patch complete
                 for (int kb = k0; kb < k1; ++kb, ++g) {
                     const int stage = (int)(g % STAGES);

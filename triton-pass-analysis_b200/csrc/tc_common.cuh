@@ -313,6 +313,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
+// 8-byte asynchronous global -> shared copy; src_bytes 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(src_bytes)
+                 : "memory");
+}
+// Waits for this thread's cp.async copies.
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
 // Makes this thread's earlier generic-proxy shared-memory writes visible to the async proxy
 // (tcgen05.mma operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
