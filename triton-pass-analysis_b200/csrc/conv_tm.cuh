@@ -246,9 +246,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            // packed input: the weight copy's expect_tx plus one arrival per producer warp
-            // (its rows of the A tile written)
-            tc::mbar_init(full_bar(s), PKI ? 1 + NP : 1);
+            // packed input: the weight copy's expect_tx plus the arrival of the producer warp
+            // that wrote the stage's A tile
+            tc::mbar_init(full_bar(s), PKI ? 2 : 1);
             tc::mbar_init(empty_bar(s), 1);
         }
         for (int a = 0; a < 2 * MH; ++a) {
@@ -293,16 +293,24 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         // ------------------------------------------------ packed-input producers (NP == 4)
         // Per tile the four warps stage the packed spikes of the tile's pixels and their
         // 1-pixel halo at every step in shared memory ([t][image][PH][PW][Cin/32] words,
-        // zero outside the layer: the conv padding), then for each k-slab (tap, 64-channel
-        // block) each thread expands its A row -- pixel row / TS at step row % TS, shifted by
-        // the tap -- to 64 bf16 {0, 1} values written in the 128-byte-swizzled layout a TMA
-        // box would have produced.  Warp 0 also copies the slab's weight rows by TMA.
+        // zero outside the layer: the conv padding).  They then take the k-slabs (tap,
+        // 64-channel block) round-robin: the slab's warp copies its weight rows by TMA and
+        // expands the 128 A rows (row = pixel * TS + step, the pixel shifted by the tap; lane
+        // l writes rows l, l+32, l+64, l+96) to bf16 {0, 1} in the 128-byte-swizzled layout a
+        // TMA box would have produced.
         if constexpr (PKI) {
             const int pi = warp == 0 ? 0 : warp - 5;
-            const int prow = pi * 32 + lane;                 // A row this thread writes
-            const int px = prow / TS, pt = prow % TS;
-            const int lw = px % p.bw, lh = (px / p.bw) % p.bh, ln = px / (p.bw * p.bh);
+            const int prow = pi * 32 + lane;                 // this thread's patch-copy index
             const int PW = p.bw + 2, PH = p.bh + 2, CW = p.Cin >> 5;
+            // the patch word offset of each of this lane's 4 rows (tap (0, 0))
+            int roff[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = lane + 32 * i;
+                const int px = rr / TS, pt = rr % TS;
+                const int lw = px % p.bw, lh = (px / p.bw) % p.bh, ln = px / (p.bw * p.bh);
+                roff[i] = (((pt * p.bn + ln) * PH + lh) * PW + lw) * CW;
+            }
             uint32_t* patch = reinterpret_cast<uint32_t*>(smem + S::PATCH_OFF);
             const int units = TS * p.bn * PH * PW * (CW >> 1);      // 8-byte units
             uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
@@ -336,22 +344,25 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 tc::cp_async_wait_all();
                 tc::named_bar_sync(4, NP * 32);      // patch complete
                 for (int kb = k0; kb < k1; ++kb, ++g) {
+                    if (g % NP != (uint32_t)pi) continue;
                     const int stage = (int)(g % STAGES);
                     const uint32_t phase = (g / STAGES) & 1u;
                     failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
                     const int tap = kb / p.cin_blocks;
                     const int cb = kb - tap * p.cin_blocks;
                     const int r = tap / 3, s = tap % 3;
-                    if (pi == 0 && !failed && tc::elect_one()) {
+                    if (!failed && tc::elect_one()) {
                         tc::mbar_expect_tx(full_bar(stage), (uint32_t)S::B_TILE);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB,
                                         full_bar(stage), cb * 64, tap, tl.n0);
                     }
                     __syncwarp();
-                    if (!failed) {
-                        const uint2 bits = *reinterpret_cast<const uint2*>(
-                            patch + (((pt * p.bn + ln) * PH + (lh + r)) * PW + (lw + s)) * CW +
-                            cb * 2);
+                    const int shift = (r * PW + s) * CW + cb * 2;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (failed) break;
+                        const int prow = lane + 32 * i;          // A row written
+                        const uint2 bits = *reinterpret_cast<const uint2*>(patch + roff[i] + shift);
                         uint8_t* rowp = smem + S::A_OFF + stage * A_TILE_BYTES + prow * 128;
                         // channel pairs (2i, 2i+1) of each 8-channel chunk -> one word of two
                         // bf16: the even and odd bits of the chunk's byte are brought to bytes
@@ -373,8 +384,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             o.w = ((v >> 6) & 0x10001u) * 0x3F80u;
                             *reinterpret_cast<uint4*>(rowp + ((j ^ (prow & 7)) << 4)) = o;
                         }
-                        tc::fence_proxy_async_smem();    // visible to the tensor core's reads
                     }
+                    if (!failed) tc::fence_proxy_async_smem();   // visible to the tensor core
                     __syncwarp();
                     if (!failed) {
                         if (lane == 0) tc::mbar_arrive(full_bar(stage));
@@ -384,9 +395,9 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 }
             }
             if (failed) {
-                // the weight copies of this warp still in flight (warp 0): bounded waits
+                // this warp's weight copies still in flight: bounded waits
                 uint32_t gg = last_g;
-                for (uint32_t k = 0; pi == 0 && k < issued && k < (uint32_t)STAGES; ++k, --gg)
+                for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP)
                     tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
                 if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
             }
