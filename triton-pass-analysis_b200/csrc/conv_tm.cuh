@@ -188,6 +188,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     constexpr bool PKI = PATCH > 0;                 // packed-spike input (see below)
     static_assert(!PKI || (MH == 1 && CG == 1 && !RES && SK == 1 && NP == 4),
                   "packed input: single CTA, one M-tile, four producer warps");
+    // Producer warps taking the k-slabs round-robin must be no more than the ring's stages:
+    // a warp then never runs two ring rounds ahead of the stage releases, the only case in
+    // which the one-bit phase parity of its empty-slot wait could pass early.
+    constexpr int NRR = PKI ? (NP < STAGES ? NP : STAGES) : NP;
+    static_assert(PKI || NP <= STAGES, "more round-robin producers than ring stages");
     static_assert(!PAIR || MH == 1, "CTA pairs take one M-tile each");
     static_assert(!CK || (MH == 1 && CG == 1), "cluster split-K: one M-tile, single CTA");
     static_assert(!RES || (MH == 1 && CG == 1), "residual input: one M-tile, single CTA");
@@ -294,7 +299,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         // Per tile the four warps stage the packed spikes of the tile's pixels and their
         // 1-pixel halo at every step in shared memory ([t][image][PH][PW][Cin/32] words,
         // zero outside the layer: the conv padding).  They then take the k-slabs (tap,
-        // 64-channel block) round-robin: the slab's warp copies its weight rows by TMA and
+        // 64-channel block) round-robin (over min(4, STAGES) warps, see NRR): the slab's warp
+        // copies its weight rows by TMA and
         // expands the 128 A rows (row = pixel * TS + step, the pixel shifted by the tap; lane
         // l writes rows l, l+32, l+64, l+96) to bf16 {0, 1} in the 128-byte-swizzled layout a
         // TMA box would have produced.
@@ -344,7 +350,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 tc::cp_async_wait_all();
                 tc::named_bar_sync(4, NP * 32);      // patch complete
                 for (int kb = k0; kb < k1; ++kb, ++g) {
-                    if (g % NP != (uint32_t)pi) continue;
+                    if (g % NRR != (uint32_t)pi) continue;     // pi >= NRR: patch copies only
                     const int stage = (int)(g % STAGES);
                     const uint32_t phase = (g / STAGES) & 1u;
                     failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
@@ -397,7 +403,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             if (failed) {
                 // this warp's weight copies still in flight: bounded waits
                 uint32_t gg = last_g;
-                for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP)
+                for (uint32_t k = 0; k < issued && k * NRR < (uint32_t)STAGES; ++k, gg -= NRR)
                     tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
                 if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
             }
