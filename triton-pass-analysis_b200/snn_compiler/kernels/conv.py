@@ -267,7 +267,8 @@ def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=()
     (on its real operands, device time via time_graph) and return the fastest."""
     best, best_ms = (0, 0, 1), float("inf")
     for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool):
-        ms = time_graph(lambda: launch(*cfg), reps)
+        # the lower of two timings: one replay can catch another context's work
+        ms = min(time_graph(lambda: launch(*cfg), reps) for _ in range(2))
         if ms < best_ms:
             best, best_ms = cfg, ms
     return best
