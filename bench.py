@@ -445,14 +445,15 @@ class VggWorkload:
         # copy stream while the previous step computes, and its logits come back on that
         # stream while the next step computes.
         eng = self.eng
-        saved = (eng.graphs, eng.graph_out, eng.mark_events, eng.graph_pool)
         self.slot_in = [torch.empty_like(self.img) for _ in range(2)]
         self.slot_out = [torch.empty_like(self.out) for _ in range(2)]
         self.slot_graphs = []
-        for k in range(2):
-            eng.capture(self.slot_in[k], out=self.slot_out[k])
-            self.slot_graphs.append(eng.graphs)
-        eng.graphs, eng.graph_out, eng.mark_events, eng.graph_pool = saved
+        if not self.eager:          # (--eager: the slots are copied around eager launches)
+            saved = (eng.graphs, eng.graph_out, eng.mark_events, eng.graph_pool)
+            for k in range(2):
+                eng.capture(self.slot_in[k], out=self.slot_out[k])
+                self.slot_graphs.append(eng.graphs)
+            eng.graphs, eng.graph_out, eng.mark_events, eng.graph_pool = saved
         self.copy_stream = torch.cuda.Stream()
         self.copied = [torch.cuda.Event() for _ in range(2)]
         self.fwd_done = [torch.cuda.Event() for _ in range(2)]
