@@ -1294,7 +1294,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
     p.num_tiles = (int)ntiles;
     if (ck) return launch_tm_cluster(T, BN, splits, ta, tb, p, s);
-    if (x_packed) return launch_tm_packed(T, BN, ta, tb, p, s);
+    if (x_packed || out_packed) return launch_tm_packed(T, BN, x_packed, out_packed, ta, tb, p, s);
     if (variant == 2) {
         switch (T) {
             case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;

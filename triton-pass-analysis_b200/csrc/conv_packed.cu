@@ -1,5 +1,6 @@
 // Packed spikes between layers: the T-folded fused conv + LIF kernel reading its input as
-// packed spikes (conv_lif_tm_kernel with PATCH > 0), and the unpacking kernel.
+// packed spikes (conv_lif_tm_kernel with PATCH > 0) and / or writing packed spikes (PKO), and
+// the unpacking kernel.
 //
 // Packed layout: NHWC spikes with 32 channels per uint32 word, channel c of a pixel in bit
 // c % 32 of word c / 32 (LSB first; the order snnb_bitpack writes for rows of C channels):
@@ -16,15 +17,9 @@ namespace {
 
 constexpr int PATCH_BYTES = 32 * 1024;
 
-template <int BN, int STAGES, int TS>
-int launch_pk(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
-              cudaStream_t s) {
-    constexpr int NP = 4;
-    constexpr int dyn = SmemTM<BN, STAGES, TS, 1, 1, PATCH_BYTES>::DYN;
-    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
-    void (*k)(const CUtensorMap, const CUtensorMap, const ConvParams) =
-        p.hard ? conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 1, false, 1, PATCH_BYTES>
-               : conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 1, false, 1, PATCH_BYTES>;
+template <typename K>
+int launch_pk_kernel(K k, int dyn, int threads, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const ConvParams& p, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
     if (e != cudaSuccess) return record_cuda_error(e);
     int occ = 0;
@@ -39,13 +34,53 @@ int launch_pk(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
     return launch_k(k, dim3(grid), dim3(threads), dyn, s, ta, tb, p);
 }
 
+// packed input (four producer warps expanding the staged patch), output packed or bf16
+template <int BN, int STAGES, int TS, bool PKO>
+int launch_pk(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+              cudaStream_t s) {
+    constexpr int NP = 4;
+    constexpr int dyn = SmemTM<BN, STAGES, TS, 1, 1, PATCH_BYTES>::DYN;
+    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
+    return p.hard
+        ? launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 1, false, 1, PATCH_BYTES, PKO>,
+                           dyn, threads, ta, tb, p, s)
+        : launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 1, false, 1, PATCH_BYTES, PKO>,
+                           dyn, threads, ta, tb, p, s);
+}
+
+// bf16 input by TMA (the stage depths and producer warps of the plain T-folded kernel),
+// packed output
+template <int BN, int STAGES, int TS>
+int launch_po(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+              cudaStream_t s) {
+    constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
+    constexpr int dyn = SmemTM<BN, STAGES, TS, 1>::DYN;
+    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
+    return p.hard
+        ? launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 1, false, 1, 0, true>,
+                           dyn, threads, ta, tb, p, s)
+        : launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 1, false, 1, 0, true>,
+                           dyn, threads, ta, tb, p, s);
+}
+
 template <int TS>
-int launch_pk_ts(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
-                 cudaStream_t s) {
+int launch_pk_ts(int BN, int x_packed, int out_packed, const CUtensorMap& ta,
+                 const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
+    if (!x_packed) {
+        switch (BN) {
+            case 256: return launch_po<256, 4, TS>(ta, tb, p, s);
+            case 128: return launch_po<128, 7, TS>(ta, tb, p, s);
+            case 64: return launch_po<64, 9, TS>(ta, tb, p, s);
+            default: return launch_po<32, 10, TS>(ta, tb, p, s);
+        }
+    }
     switch (BN) {
-        case 256: return launch_pk<256, 3, TS>(ta, tb, p, s);
-        case 128: return launch_pk<128, 6, TS>(ta, tb, p, s);
-        case 64: return launch_pk<64, 8, TS>(ta, tb, p, s);
+        case 256: return out_packed ? launch_pk<256, 3, TS, true>(ta, tb, p, s)
+                                    : launch_pk<256, 3, TS, false>(ta, tb, p, s);
+        case 128: return out_packed ? launch_pk<128, 6, TS, true>(ta, tb, p, s)
+                                    : launch_pk<128, 6, TS, false>(ta, tb, p, s);
+        case 64: return out_packed ? launch_pk<64, 8, TS, true>(ta, tb, p, s)
+                                   : launch_pk<64, 8, TS, false>(ta, tb, p, s);
         default: return SNNB_ERR_UNSUPPORTED;
     }
 }
@@ -68,12 +103,12 @@ __global__ void __launch_bounds__(256) unpack_spikes_kernel(const uint32_t* __re
 
 int packed_patch_limit() { return PATCH_BYTES; }
 
-int launch_tm_packed(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const ConvParams& p, cudaStream_t s) {
+int launch_tm_packed(int TS, int BN, int x_packed, int out_packed, const CUtensorMap& ta,
+                     const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
     switch (TS) {
-        case 2: return launch_pk_ts<2>(BN, ta, tb, p, s);
-        case 4: return launch_pk_ts<4>(BN, ta, tb, p, s);
-        case 8: return launch_pk_ts<8>(BN, ta, tb, p, s);
+        case 2: return launch_pk_ts<2>(BN, x_packed, out_packed, ta, tb, p, s);
+        case 4: return launch_pk_ts<4>(BN, x_packed, out_packed, ta, tb, p, s);
+        case 8: return launch_pk_ts<8>(BN, x_packed, out_packed, ta, tb, p, s);
         default: return SNNB_ERR_UNSUPPORTED;
     }
 }

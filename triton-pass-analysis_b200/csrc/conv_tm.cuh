@@ -141,6 +141,25 @@ __device__ __forceinline__ void store_bits_bf16(__nv_bfloat16* dst, uint32_t bit
 // Split-K (p.partial != nullptr): work item = (tile, split); the split's k-slab range is
 // accumulated and written as float32 partial sums [split][t][pixel][channel]; the neuron
 // then runs in splitsum_lif_kernel, which adds the splits in a fixed order.
+// Packed output of one epilogue slice: the TS lanes of a pixel (lane kq holds NPT columns of
+// the set's 16 at every step, bit t * NPT + e of lb) gather the 16-channel half-word of every
+// step, and lane kq stores step kq's at dst (already offset to step kq).
+template <int TS, int NPT>
+__device__ __forceinline__ void store_packed_halfword(unsigned short* dst, uint32_t lb, int kq,
+                                                   bool ok) {
+    uint32_t hw[TS];
+#pragma unroll
+    for (int t = 0; t < TS; ++t) hw[t] = ((lb >> (t * NPT)) & ((1u << NPT) - 1u)) << (kq * NPT);
+#pragma unroll
+    for (int bb = 1; bb < TS; bb <<= 1)
+#pragma unroll
+        for (int t = 0; t < TS; ++t) hw[t] |= __shfl_xor_sync(0xffffffffu, hw[t], bb);
+    uint32_t mine = hw[0];
+#pragma unroll
+    for (int t = 1; t < TS; ++t) mine = kq == t ? hw[t] : mine;
+    if (ok) *dst = (unsigned short)mine;
+}
+
 // PATCH: bytes of the packed-spike input patch (packed-input form; 0 otherwise)
 template <int BN, int STAGES, int TS, int MH, int CG = 1, int PATCH = 0>
 struct SmemTM {
@@ -178,8 +197,10 @@ struct SmemTM {
 // Two sets of 4 epilogue warps (warps 2-5 and 5+NP .. 8+NP) split every 32-column slice of
 // the accumulator into halves: the epilogue of a CTA's last work item, which no MMA
 // overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
+// PKO: spikes stored packed (a compile-time choice: a run-time test in the epilogue's loop
+// cost epilogue-bound launches ~5%).
 template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES, int SK = 1,
-          int PATCH = 0>
+          int PATCH = 0, bool PKO = false>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
@@ -766,23 +787,13 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 // packed output: the TS lanes of a pixel gather the set's 16 channels of every
                 // step (bit = channel within the half-word) and lane kq stores step kq
                 auto store_packed = [&](bool ok, int y, int x, int Hs, int Ws) {
-                    uint32_t hw[TS];
-#pragma unroll
-                    for (int t = 0; t < TS; ++t)
-                        hw[t] = ((lb >> (t * NPT)) & ((1u << NPT) - 1u)) << (kq * NPT);
-#pragma unroll
-                    for (int bb = 1; bb < TS; bb <<= 1)
-#pragma unroll
-                        for (int t = 0; t < TS; ++t) hw[t] |= __shfl_xor_sync(0xffffffffu, hw[t], bb);
-                    uint32_t mine = hw[0];
-#pragma unroll
-                    for (int t = 1; t < TS; ++t) mine = kq == t ? hw[t] : mine;
-                    if (ok)
-                        reinterpret_cast<unsigned short*>(p.out)[
+                    store_packed_halfword<TS, NPT>(
+                        reinterpret_cast<unsigned short*>(p.out) +
                             ((((int64_t)kq * p.B + on) * Hs + y) * Ws + x) * (p.Cout >> 4) +
-                            ((tl.n0 + c * 32) >> 4) + set] = (unsigned short)mine;
+                            ((tl.n0 + c * 32) >> 4) + set,
+                        lb, kq, ok);
                 };
-                if (!p.pool && p.out_packed) {
+                if (PKO && !p.pool) {
                     store_packed(inside, oh, ow, p.H, p.W);
                 } else if (!p.pool) {
                     if (inside) {
@@ -818,7 +829,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     smask[set * 128 + row] = lb;
                     tc::named_bar_sync(1 + set, 128);    // row neighbours' bits visible
                     lb |= smask[set * 128 + (row ^ (TS * p.bw))];
-                    if (p.out_packed) {
+                    if (PKO) {
                         store_packed(pool_store, oh >> 1, ow >> 1, Ho, Wo);
                     } else if (pool_store) {
 #pragma unroll
@@ -855,10 +866,11 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 int launch_tm_cluster(int TS, int BN, int SK, const CUtensorMap& ta, const CUtensorMap& tb,
                       const ConvParams& p, cudaStream_t s);
 
-// Packed-spike-input launch of conv_lif_tm_kernel (conv_packed.cu); packed_patch_limit() is
-// the largest input patch (bytes) one CTA stages.
-int launch_tm_packed(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const ConvParams& p, cudaStream_t s);
+// Packed-spike launches of conv_lif_tm_kernel (conv_packed.cu): packed input (PATCH > 0)
+// and / or packed output (PKO); packed_patch_limit() is the largest input patch (bytes) one
+// CTA stages.
+int launch_tm_packed(int TS, int BN, int x_packed, int out_packed, const CUtensorMap& ta,
+                     const CUtensorMap& tb, const ConvParams& p, cudaStream_t s);
 int packed_patch_limit();
 
 }  // namespace snnb
