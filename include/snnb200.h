@@ -238,7 +238,7 @@ int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* 
  * bias_d : f32 [H*W*Cout], b'[co] for row (p, co) (or (co, p) with pool)
  * pool   : 2x2 max-pool (H == W == 2): out [T*B, 1, 1, Cout]; else out [T*B, H, W, Cout]
  * variant / block_n / splits / workspace: as snnb_linear_lif for an N = H*W*Cout layer;
- * with pool: variants 0, 2, 4, 5 (splits == 1) or 6.
+ * with pool: variant 0 or 2, splits == 1.
  */
 int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
                            int64_t Cin, const void* wd, const float* bias_d, int64_t Cout,

@@ -169,7 +169,7 @@ def test_conv3x3_dense_small_image_against_oracle(case, vb):
     if H != 2:
         return
     wp, bp = C.dense_conv_weight(wk, 2, 2, pool=True), C.dense_conv_bias(bd, 2, 2, pool=True)
-    if splits > 1 and variant != 6:
+    if variant not in (0, 2) or splits > 1:       # the pooled dense form: plain T-folded only
         with pytest.raises(RuntimeError):
             C.conv3x3_lif_dense(xd, wp, bp, pool=True, **kw)
         return

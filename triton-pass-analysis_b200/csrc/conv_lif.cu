@@ -1150,9 +1150,8 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (pool < 0 || pool > 2) return SNNB_ERR_ARG;
     if (gpool) {
         if (taps != 1 || H != 1 || W != 1 || Cout % 128 != 0) return SNNB_ERR_UNSUPPORTED;
-        if (variant == 1 || variant == 3) return SNNB_ERR_UNSUPPORTED;
-        if (splits > 1 && variant != 6) return SNNB_ERR_UNSUPPORTED;
-        if (variant == 0) variant = 2;
+        if ((variant != 0 && variant != 2) || splits > 1) return SNNB_ERR_UNSUPPORTED;
+        variant = 2;
     }
     if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return SNNB_ERR_ARG;
     if (Cin % 8 != 0 || Cout % 32 != 0) return SNNB_ERR_UNSUPPORTED;
@@ -1295,6 +1294,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.num_tiles = (int)ntiles;
     if (ck) return launch_tm_cluster(T, BN, splits, ta, tb, p, s);
     if (x_packed || out_packed) return launch_tm_packed(T, BN, x_packed, out_packed, ta, tb, p, s);
+    if (gpool) return launch_tm_cpool(T, BN, ta, tb, p, s);
     if (variant == 2) {
         switch (T) {
             case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;

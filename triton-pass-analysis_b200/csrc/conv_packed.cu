@@ -1,6 +1,7 @@
 // Packed spikes between layers: the T-folded fused conv + LIF kernel reading its input as
-// packed spikes (conv_lif_tm_kernel with PATCH > 0) and / or writing packed spikes (PKO), and
-// the unpacking kernel.
+// packed spikes (conv_lif_tm_kernel with PATCH > 0) and / or writing packed spikes (PKO), the
+// unpacking kernel, and the column-group-pool instantiations of the dense 2x2 form (CPOOL):
+// the epilogue options that only these launches use are compiled into their own kernels.
 //
 // Packed layout: NHWC spikes with 32 channels per uint32 word, channel c of a pixel in bit
 // c % 32 of word c / 32 (LSB first; the order snnb_bitpack writes for rows of C channels):
@@ -63,6 +64,31 @@ int launch_po(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
                            dyn, threads, ta, tb, p, s);
 }
 
+// the dense form of a pooled 2x2-image layer: bf16 in and out, column-group pool
+template <int BN, int STAGES, int TS>
+int launch_cp(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+              cudaStream_t s) {
+    constexpr int NP = BN == 256 ? 2 : (BN == 64 ? 4 : 3);
+    constexpr int dyn = SmemTM<BN, STAGES, TS, 1>::DYN;
+    constexpr int threads = THREADS + 32 * (NP - 1) + 128;
+    return p.hard
+        ? launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, true, NP, 1, 1, false, 1, 0, false, true>,
+                           dyn, threads, ta, tb, p, s)
+        : launch_pk_kernel(conv_lif_tm_kernel<BN, STAGES, TS, false, NP, 1, 1, false, 1, 0, false, true>,
+                           dyn, threads, ta, tb, p, s);
+}
+
+template <int TS>
+int launch_cp_ts(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p,
+                 cudaStream_t s) {
+    switch (BN) {
+        case 256: return launch_cp<256, 4, TS>(ta, tb, p, s);
+        case 128: return launch_cp<128, 7, TS>(ta, tb, p, s);
+        case 64: return launch_cp<64, 9, TS>(ta, tb, p, s);
+        default: return launch_cp<32, 10, TS>(ta, tb, p, s);
+    }
+}
+
 template <int TS>
 int launch_pk_ts(int BN, int x_packed, int out_packed, const CUtensorMap& ta,
                  const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
@@ -102,6 +128,16 @@ __global__ void __launch_bounds__(256) unpack_spikes_kernel(const uint32_t* __re
 }  // namespace
 
 int packed_patch_limit() { return PATCH_BYTES; }
+
+int launch_tm_cpool(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
+                    const ConvParams& p, cudaStream_t s) {
+    switch (TS) {
+        case 2: return launch_cp_ts<2>(BN, ta, tb, p, s);
+        case 4: return launch_cp_ts<4>(BN, ta, tb, p, s);
+        case 8: return launch_cp_ts<8>(BN, ta, tb, p, s);
+        default: return SNNB_ERR_UNSUPPORTED;
+    }
+}
 
 int launch_tm_packed(int TS, int BN, int x_packed, int out_packed, const CUtensorMap& ta,
                      const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {

@@ -197,10 +197,11 @@ struct SmemTM {
 // Two sets of 4 epilogue warps (warps 2-5 and 5+NP .. 8+NP) split every 32-column slice of
 // the accumulator into halves: the epilogue of a CTA's last work item, which no MMA
 // overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
-// PKO: spikes stored packed (a compile-time choice: a run-time test in the epilogue's loop
-// cost epilogue-bound launches ~5%).
+// PKO: spikes stored packed; CPOOL: the column-group pool of the dense 2x2 form (pool == 2).
+// Both are compile-time choices: a run-time test in the epilogue's loop cost epilogue-bound
+// launches ~5%.
 template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES, int SK = 1,
-          int PATCH = 0, bool PKO = false>
+          int PATCH = 0, bool PKO = false, bool CPOOL = false>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
@@ -793,17 +794,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             ((tl.n0 + c * 32) >> 4) + set,
                         lb, kq, ok);
                 };
-                if (PKO && !p.pool) {
-                    store_packed(inside, oh, ow, p.H, p.W);
-                } else if (!p.pool) {
-                    if (inside) {
-#pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
-                                                             p.Cout + ch,
-                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
-                    }
-                } else if (p.pool == 2) {
+                if constexpr (CPOOL) {
                     // dense form of a pooled 2x2-image layer (taps == 1, H == W == 1): the
                     // columns are ordered (channel, pixel), so the 2x2 max-pool is an OR over
                     // 4 consecutive columns -- NPT / 4 groups per lane, or (NPT == 2) half a
@@ -821,6 +812,16 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             for (int gi = 0; gi < G; ++gi)
                                 o[t * tstride + gi] =
                                     ((lb >> (t * NPT + 4 * gi)) & GM) ? 0x3F80u : 0u;
+                    }
+                } else if (PKO && !p.pool) {
+                    store_packed(inside, oh, ow, p.H, p.W);
+                } else if (!p.pool) {
+                    if (inside) {
+#pragma unroll
+                        for (int t = 0; t < TS; ++t)
+                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
+                                                             p.Cout + ch,
+                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
                     }
                 } else {
                     // 2x2 max-pool = OR: the column neighbour is TS lanes away; the row
@@ -872,5 +873,9 @@ int launch_tm_cluster(int TS, int BN, int SK, const CUtensorMap& ta, const CUten
 int launch_tm_packed(int TS, int BN, int x_packed, int out_packed, const CUtensorMap& ta,
                      const CUtensorMap& tb, const ConvParams& p, cudaStream_t s);
 int packed_patch_limit();
+// The dense form of a pooled 2x2-image layer (CPOOL; conv_packed.cu): plain T-folded kernel
+// whose epilogue ORs groups of 4 consecutive columns.
+int launch_tm_cpool(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
+                    const ConvParams& p, cudaStream_t s);
 
 }  // namespace snnb

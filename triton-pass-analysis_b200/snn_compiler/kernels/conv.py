@@ -219,11 +219,11 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
                dense_pool: bool = False):
     """(variant, block_n, splits) configurations a layer admits; `band` lists the
     block widths of variant 3 the layer qualifies for (band_block_ns); dense_pool: the
-    pooled dense form (snnb_conv3x3_lif_dense), whose epilogue the T-folded kernels alone
-    have (no T-sequential variant, split-K only within a cluster)."""
+    pooled dense form (snnb_conv3x3_lif_dense), whose epilogue the plain T-folded kernel
+    alone has (variant 2, no split)."""
     if dense_pool:
         return [c for c in candidates(cout, T, kslabs, max_splits)
-                if c[0] in (2, 4, 5, 6) and (c[2] == 1 or c[0] == 6)]
+                if c[0] == 2 and c[2] == 1]
     out = []
     for v in ((1, 2) if T in (2, 4, 8) else (1,)):
         for bn in ((32, 64, 128) if v == 1 else (32, 64, 128, 256)):
