@@ -1235,9 +1235,18 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
         if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
     }
+    int pk_px = 0, pk_ps = 0;
     if (x_packed) {
-        const int64_t patch = (int64_t)T * bn * (bh + 2) * (bw + 2) * (Cin / 8);
-        if (patch > packed_patch_limit()) return SNNB_ERR_UNSUPPORTED;
+        // the kernel's patch: T planes of bn*(bh+2)*(bw+2) pixel slots -- of Cin/32 + 2 words
+        // and 8 more words per plane (fewer bank conflicts) when that fits, else unpadded
+        const int64_t npx = (int64_t)bn * (bh + 2) * (bw + 2);
+        pk_px = Cin / 32 + 2;
+        pk_ps = (int)(npx * pk_px + 8);
+        if ((int64_t)T * pk_ps * 4 > packed_patch_limit()) {
+            pk_px = Cin / 32;
+            pk_ps = (int)(npx * pk_px);
+        }
+        if ((int64_t)T * npx * (Cin / 32) * 4 > packed_patch_limit()) return SNNB_ERR_UNSUPPORTED;
     }
     int* status = device_status_ptr();
     if (!status) return SNNB_ERR_CUDA;
@@ -1285,6 +1294,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.wq = w; p.wq_bytes = (int64_t)Cout * p.taps * Cin * 2;
     p.res = res; p.res_f32 = res_f32;
     p.xq = x_packed ? static_cast<const uint32_t*>(x) : nullptr;
+    p.pk_px = pk_px; p.pk_ps = pk_ps;
     p.out_packed = out_packed ? 1 : 0;
     p.splits = ck ? 1 : splits;
     p.partial = splits > 1 && !ck ? static_cast<float*>(workspace) : nullptr;

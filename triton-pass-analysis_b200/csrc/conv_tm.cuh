@@ -34,6 +34,7 @@ struct ConvParams {
     int res_f32;                  // residual dtype: float32 (1) or bf16 (0)
     const uint32_t* xq;           // packed-spike input [T*B][H][W][Cin/32] (T-folded kernel)
     int out_packed;               // spikes stored packed, [T*B][Ho][Wo][Cout/32] uint32
+    int pk_px, pk_ps;             // packed-input patch: words per pixel slot / per step plane
 };
 
 struct Tile {
@@ -320,7 +321,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         // ------------------------------------------------ packed-input producers (NP == 4)
         // Per tile the four warps stage the packed spikes of the tile's pixels and their
         // 1-pixel halo at every step in shared memory ([t][image][PH][PW][Cin/32] words,
-        // zero outside the layer: the conv padding).  They then take the k-slabs (tap,
+        // padded, zero outside the layer: the conv padding).  They then take the k-slabs (tap,
         // 64-channel block) round-robin (over min(4, STAGES) warps, see NRR): the slab's warp
         // copies its weight rows by TMA and
         // expands the 128 A rows (row = pixel * TS + step, the pixel shifted by the tap; lane
@@ -330,6 +331,10 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             const int pi = warp == 0 ? 0 : warp - 5;
             const int prow = pi * 32 + lane;                 // this thread's patch-copy index
             const int PW = p.bw + 2, PH = p.bh + 2, CW = p.Cin >> 5;
+            // patch layout in words (host-chosen): pixel slots of PX >= CW and step planes of
+            // PS >= bn * PH * PW * PX -- padded when it fits, so that the 32 rows a warp reads
+            // spread over the banks
+            const int PX = p.pk_px, PS = p.pk_ps;
             // the patch word offset of each of this lane's 4 rows (tap (0, 0))
             int roff[4];
 #pragma unroll
@@ -337,7 +342,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int rr = lane + 32 * i;
                 const int px = rr / TS, pt = rr % TS;
                 const int lw = px % p.bw, lh = (px / p.bw) % p.bh, ln = px / (p.bw * p.bh);
-                roff[i] = (((pt * p.bn + ln) * PH + lh) * PW + lw) * CW;
+                roff[i] = pt * PS + ((ln * PH + lh) * PW + lw) * PX;
             }
             uint32_t* patch = reinterpret_cast<uint32_t*>(smem + S::PATCH_OFF);
             const int units = TS * p.bn * PH * PW * (CW >> 1);      // 8-byte units
@@ -367,7 +372,8 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const uint32_t* src = in ? p.xq + ((((int64_t)t * p.B + gn) * p.H + gh) *
                                                            p.W + gw) * CW + 2 * cu
                                              : p.xq;
-                    tc::cp_async_8(sbase + S::PATCH_OFF + (uint32_t)u * 8u, src, in ? 8u : 0u);
+                    const int dw = t * PS + ((pn * PH + ph) * PW + pw) * PX + 2 * cu;
+                    tc::cp_async_8(sbase + S::PATCH_OFF + (uint32_t)dw * 4u, src, in ? 8u : 0u);
                 }
                 tc::cp_async_wait_all();
                 tc::named_bar_sync(4, NP * 32);      // patch complete
@@ -385,7 +391,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                         full_bar(stage), cb * 64, tap, tl.n0);
                     }
                     __syncwarp();
-                    const int shift = (r * PW + s) * CW + cb * 2;
+                    const int shift = (r * PW + s) * PX + cb * 2;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         if (failed) break;
