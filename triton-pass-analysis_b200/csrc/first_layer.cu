@@ -218,11 +218,16 @@ __global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_
         sw[i] = __ldg(w + (int64_t)co * K + k);
     }
     for (int i = threadIdx.x; i < Cout; i += QUAD_THREADS) sb[i] = __ldg(bias + i);
+    // thread = (4-pixel quad, channel group g): the Cout/16 groups of a quad are adjacent
+    // lanes, and group g owns channels 8g..8g+7 and Cout/2+8g..Cout/2+8g+7, so that one
+    // 16-byte spike store per lane fills whole 32-byte sectors (the quad's groups write
+    // channels 0..Cout/2-1, then Cout/2..Cout-1, contiguously)
     const int quads = R * (W / 4);
-    const int qd = threadIdx.x % quads, g = threadIdx.x / quads;
+    const int G = Cout / 16;
+    const int g = threadIdx.x % G, qd = threadIdx.x / G;
     const int py = qd / (W / 4), px0 = 4 * (qd % (W / 4));
-    const int c0 = g * 16;
-    const bool live = g * 16 < Cout && h0 + py < H;
+    const int c_lo = 8 * g, c_hi = Cout / 2 + 8 * g;
+    const bool live = qd < quads && h0 + py < H;
     const float2 df2 = make_float2(df, df), sc2 = make_float2(sc, sc);
     float2 u[4][8];                                   // sc * (conv + b), channel pairs
     float2 v[4][8];
@@ -251,11 +256,11 @@ __global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_
                 for (int e = 0; e < 6; ++e) xr[e] = row[e];
 #pragma unroll
                 for (int kw = 0; kw < 3; ++kw) {
-                    const float4* wk =
-                        reinterpret_cast<const float4*>(sw + (ci * 9 + kh * 3 + kw) * Cout + c0);
+                    const float* wrow = sw + (ci * 9 + kh * 3 + kw) * Cout;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const float4 w4 = wk[q];
+                        const float4 w4 = *reinterpret_cast<const float4*>(
+                            wrow + (q < 2 ? c_lo + 4 * q : c_hi + 4 * (q - 2)));
                         const float2 wlo = make_float2(w4.x, w4.y);
                         const float2 whi = make_float2(w4.z, w4.w);
 #pragma unroll
@@ -267,17 +272,18 @@ __global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_
                 }
             }
         }
-        const float2* b2 = reinterpret_cast<const float2*>(sb + c0);
+        const float2* b2lo = reinterpret_cast<const float2*>(sb + c_lo);
+        const float2* b2hi = reinterpret_cast<const float2*>(sb + c_hi);
 #pragma unroll
         for (int p = 0; p < 4; ++p)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) u[p][j] = __fmul2_rn(sc2, __fadd2_rn(u[p][j], b2[j]));
+            for (int j = 0; j < 8; ++j)
+                u[p][j] = __fmul2_rn(sc2, __fadd2_rn(u[p][j], j < 4 ? b2lo[j] : b2hi[j - 4]));
     };
     // one LIF step of this thread's 64 neurons and the spike stores of frame t
     auto lif = [&](int t) {
         if (!live) return;
-        uint4* dst = reinterpret_cast<uint4*>(
-            out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0) * Cout + c0);
+        __nv_bfloat16* dst = out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0) * Cout;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
             uint32_t bits = 0;
@@ -291,8 +297,8 @@ __global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_
                 bits |= (s0 ? 1u : 0u) << (2 * j);
                 bits |= (s1 ? 1u : 0u) << (2 * j + 1);
             }
-            dst[p * (Cout / 8)] = spikes_to_bf16x8(bits & 0xffu);
-            dst[p * (Cout / 8) + 1] = spikes_to_bf16x8(bits >> 8);
+            *reinterpret_cast<uint4*>(dst + p * Cout + c_lo) = spikes_to_bf16x8(bits & 0xffu);
+            *reinterpret_cast<uint4*>(dst + p * Cout + c_hi) = spikes_to_bf16x8(bits >> 8);
         }
     };
     if (DIRECT) {
@@ -316,10 +322,10 @@ __global__ void __launch_bounds__(QUAD_THREADS, DIRECT ? 4 : 3) first_conv_quad_
                                         reset_v<HARD>(vv.y, s1, thr, v_reset));
                     bits |= ((s0 ? 1u : 0u) | (s1 ? 2u : 0u)) << (2 * j);
                 }
-                uint4* dst = reinterpret_cast<uint4*>(
-                    out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0 + p) * Cout + c0);
-                dst[0] = spikes_to_bf16x8(bits & 0xffu);
-                dst[1] = spikes_to_bf16x8(bits >> 8);
+                __nv_bfloat16* dst =
+                    out + ((((int64_t)t * B + b) * H + h0 + py) * W + px0 + p) * Cout;
+                *reinterpret_cast<uint4*>(dst + c_lo) = spikes_to_bf16x8(bits & 0xffu);
+                *reinterpret_cast<uint4*>(dst + c_hi) = spikes_to_bf16x8(bits >> 8);
             }
         }
         return;
