@@ -610,14 +610,25 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 tc::mbar_arrive(acce_bar(a));
                 const int64_t frame = (int64_t)t * p.B + tl.img0;
                 if (!p.pool) {
+                    // the lanes of pixels x and x ^ 1 (same row: W is even) store both pixels,
+                    // chunk 2i by the even lane and 2i + 1 by the odd one, so that every
+                    // 16-byte store instruction fills whole 32-byte sectors
+                    uint32_t ok[NCH];
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c) ok[c] = __shfl_xor_sync(0xffffffffu, mk[c], 1);
                     if (hy < p.H) {
-                        uint4* dst = reinterpret_cast<uint4*>(
-                            p.out + ((frame * Ho + hy) * Wo + x) * p.Cout + tl.n0);
+                        const int par = x & 1;
 #pragma unroll
-                        for (int c = 0; c < NCH; ++c)
+                        for (int pi = 0; pi < 2; ++pi) {
+                            uint4* dst = reinterpret_cast<uint4*>(
+                                p.out + ((frame * Ho + hy) * Wo + ((x & ~1) | pi)) * p.Cout + tl.n0);
 #pragma unroll
-                            for (int k = 0; k < 4; ++k)
-                                dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+                            for (int i = 0; i < NCH * 2; ++i) {
+                                const int j = 2 * i + par;          // 16-byte chunk of the pixel
+                                const uint32_t mm = pi == par ? mk[j >> 2] : ok[j >> 2];
+                                dst[j] = spikes_to_bf16x8((mm >> (8 * (j & 3))) & 0xffu);
+                            }
+                        }
                     }
                 } else {
                     // 2x2 max-pool = OR: column pairs are adjacent lanes; row pairs are lanes
