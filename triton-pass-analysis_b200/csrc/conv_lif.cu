@@ -646,14 +646,17 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
                         for (int c = 0; c < NCH; ++c) mk[c] |= sm[c * 128 + (m ^ W)];
                     }
-                    if (((x | y) & 1) == 0 && hy < p.H) {
+                    if ((y & 1) == 0 && hy < p.H) {
+                        // both column lanes of the window hold its OR: the even one stores
+                        // chunks 2i and the odd one 2i + 1 (whole 32-byte sectors per store)
                         uint4* dst = reinterpret_cast<uint4*>(
                             p.out + ((frame * Ho + hy / 2) * Wo + x / 2) * p.Cout + tl.n0);
+                        const int par = x & 1;
 #pragma unroll
-                        for (int c = 0; c < NCH; ++c)
-#pragma unroll
-                            for (int k = 0; k < 4; ++k)
-                                dst[c * 4 + k] = spikes_to_bf16x8((mk[c] >> (8 * k)) & 0xffu);
+                        for (int i = 0; i < NCH * 2; ++i) {
+                            const int j = 2 * i + par;
+                            dst[j] = spikes_to_bf16x8((mk[j >> 2] >> (8 * (j & 3))) & 0xffu);
+                        }
                     }
                 }
             }
