@@ -9,7 +9,10 @@ Workloads
                      BN folded, LIF tau=2 / v_th=1 / hard reset, 2x2 max-pool,
                      classifier 512-4096-4096-10 with the logits averaged over T.
                      Metric: images/s over all ranks (weak scaling: batch 64 per
-                     GPU; one NCCL all-gather of the [64, 10] logits per step).
+                     GPU; one NCCL all-gather of the [64, 10] logits per step,
+                     through snn_compiler.sharding.ShardedInference).  The line
+                     also carries `lif_kernel`: the standalone LIF kernel's HBM
+                     GB/s at T=32, N=2^27 per GPU (the metric's second half).
   lif             -- multi-step LIF sweep point T=32, N=2^27 float32 with
                      fp32 spikes + packed spikes + final v.  Metric: HBM GB/s
                      (algorithmic bytes 4TN + 4TN + TN/8 + 4N per step).
@@ -325,8 +328,9 @@ class VggWorkload:
                 "lif": "tau=2, v_th=1, hard reset 0, decay_input",
                 "weights": "Kaiming-normal seeded, BN folded, bf16 (layer 1 f32)",
                 "parallelism": f"dp{self.world}",
-                "collective": "NCCL all_gather of [64,10] f32 logits per step" if self.world > 1
-                else "none",
+                "collective": "ShardedInference: NCCL all_gather of the [64,10] f32 logits "
+                              "per step on a side stream, overlapping the next step's forward"
+                              if self.world > 1 else "none",
                 "l2": "256 MB buffer written before every timed step",
                 "launch": "eager launches" if self.eager else
                           "one CUDA graph per forward (timing events around the dominant launch)",
@@ -368,9 +372,25 @@ class VggWorkload:
             # one graph per forward, with a timing-event pair around the dominant launch
             self.out = self.eng.capture(self.img, mark=dom)
         self.dom_graph = 1
-        self.gathered = torch.empty(world * self.B, 10, device="cuda") if world > 1 else None
         self._dom_events = []
         self.flops_img = self.eng.flops_per_image()
+        self.sharded = None
+        if world > 1:
+            # the product API: ShardedInference over the engine's graph-replayed forward; the
+            # engine writes its logits into the send slot and the all-gather runs on a side
+            # stream, issued at the start of the next step (after its L2 flush) so that it
+            # overlaps that step's forward and never the untimed flush
+            import functools
+            from snn_compiler.sharding import ShardedInference
+            self.sharded = ShardedInference(functools.partial(self.eng.forward, graph=True))
+            gg = torch.Generator(device="cuda").manual_seed(1000)
+            self.img_global = torch.rand(1, world * self.B, 3, 32, 32, device="cuda",
+                                         generator=gg)
+            for _ in range(2 * self.sharded.slots):         # captures one graph per slot
+                self.sharded.submit(self.img_global, 1, out_shape=(10,)).wait()
+            torch.cuda.synchronize()
+            self._prev = None
+            self._step_ev = torch.cuda.Event()
 
     def _kernel_label(self, i):
         """Name of the kernel that runs plan step i (the autotuned variant)."""
@@ -410,9 +430,21 @@ class VggWorkload:
         return self.out
 
     def step(self):
-        self._forward(between=self._between)
-        if self.gathered is not None:
-            self.dist.all_gather_into_tensor(self.gathered, self.out)
+        if self.sharded is None:
+            self._forward(between=self._between)
+            return
+        self._step_ev.record()                    # this step starts (after its flush)
+        p = self.sharded.submit(self.img_global, 1, out_shape=(10,), defer=True)
+        if self._prev is not None:
+            self._prev.start(after=self._step_ev)     # the last step's all-gather
+        self._prev = p
+
+    def finish(self):
+        """End of a run of steps: issue the outstanding all-gather and make the current
+        stream wait for it (inside the last step's timing)."""
+        if self.sharded is not None and self._prev is not None:
+            torch.cuda.current_stream().wait_event(self._prev.start().done_event)
+            self._prev = None
 
     def kernel_events(self, steps):
         if self.eager:
@@ -448,7 +480,8 @@ class VggWorkload:
         self.slot_in = [torch.empty_like(self.img) for _ in range(2)]
         self.slot_out = [torch.empty_like(self.out) for _ in range(2)]
         self.slot_graphs = []
-        if not self.eager:          # (--eager: the slots are copied around eager launches)
+        if not self.eager and self.sharded is None:
+            # (--eager: the slots are copied around eager launches; N > 1: ShardedInference)
             saved = (eng.graphs, eng.graph_out, eng.mark_events, eng.graph_pool)
             for k in range(2):
                 eng.capture(self.slot_in[k], out=self.slot_out[k])
@@ -479,7 +512,13 @@ class VggWorkload:
         s = torch.cuda.current_stream()
         s.wait_event(self.copied[k])
         s.wait_event(self.read_back[k])      # slot k's logits of two steps ago are on the host
-        if self.eager:
+        pend = None
+        if self.sharded is not None:
+            # this rank's images through ShardedInference: graph-replayed forward into the
+            # send slot, all-gather on the side stream, logits back on the copy stream
+            pend = self.sharded.submit_local(self.slot_in[k], self.world * self.B, 1,
+                                             out_shape=(10,))
+        elif self.eager:
             self.img.copy_(self.slot_in[k], non_blocking=True)
             self._forward()
             self.slot_out[k].copy_(self.out, non_blocking=True)
@@ -489,9 +528,11 @@ class VggWorkload:
         self.fwd_done[k].record(s)
         self._h2d(1 - k)                     # the next step's image
         self._e2e_pending = True
-        if self.gathered is not None:
-            self.dist.all_gather_into_tensor(self.gathered, self.slot_out[k])
-            self.h_out.copy_(self.gathered.view(-1), non_blocking=True)
+        if pend is not None:
+            with torch.cuda.stream(self.copy_stream):
+                self.copy_stream.wait_event(pend.done_event)
+                self.h_out.copy_(pend.wait().view(-1), non_blocking=True)
+                self.read_back[k].record(self.copy_stream)
         else:
             with torch.cuda.stream(self.copy_stream):
                 self.copy_stream.wait_event(self.fwd_done[k])
@@ -871,6 +912,55 @@ def run_reference(args, workload):
     print(json.dumps(line), flush=True)
 
 
+def lif_kernel_object(dist, rank, world, local, peaks, T=32, N=1 << 27, steps=5, warmup=3):
+    """The second half of the headline metric: the standalone multi-step LIF kernel's HBM
+    bandwidth at T=32, N=2^27 float32 per GPU (config 1's largest point), fp32 spikes +
+    packed spikes + final v, timed after the VGG16 region in the same process.  Byte model
+    per launch: 4TN (x) + 4TN (spikes) + TN/8 (packed) + 4N (v) -- the reference's model
+    (snn_compiler/explore/large_T/bench_baseline.py:45, 8 bytes per neuron-step) plus this
+    build's extra outputs.  Every rank runs its own N (weak scaling); the value is the sum
+    of the ranks' bytes over the slowest rank's time."""
+    wl = LifWorkload(T=T, N=N)
+    wl.setup(rank, world, dist)
+    for _ in range(warmup):
+        wl.step()
+    barrier(dist)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t0 = time.time()
+    for i in range(steps):
+        ev[i][0].record(stream)
+        wl.step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    tot = max_over_ranks(dist, sum(ms))
+    if sampler:
+        sampler.mark(t0, t1)
+    clocks = sampler.stop() if sampler else None
+    slowest_mean = max_over_ranks(dist, statistics.mean(ms))
+    per_gpu = wl.bytes_per_step / (slowest_mean * 1e-3) / 1e9      # the slowest rank's
+    total = world * wl.bytes_per_step * steps / (tot * 1e-3) / 1e9
+    del wl
+    torch.cuda.empty_cache()
+    return {"metric": f"LIF kernel HBM GB/s (T={T}, N=2^{N.bit_length() - 1} float32 per GPU, "
+                      "fp32 spikes + packed spikes + final v)",
+            "value": round(total, 1), "unit": "GB/s", "n_gpus": world,
+            "per_gpu_gbs": round(per_gpu, 1), "peak": peaks["hbm_gbs"],
+            "frac": round(per_gpu / peaks["hbm_gbs"], 4),
+            "peak_source": peaks["source"] + " HBM copy",
+            "kernel": "neuron_vec8_kernel<float,float>",
+            "ms_per_launch": round(tot / steps, 4), "steps": steps, "warmup": warmup,
+            "algorithmic_bytes_per_launch": 4 * T * N + 4 * T * N + T * N // 8 + 4 * N,
+            "byte_model": "4TN x + 4TN spikes + TN/8 packed + 4N final v",
+            "l2": "inputs larger than L2 (16 GiB per tensor)", "clocks": clocks}
+
+
 def run_ours(args, workload):
     rank, world, local, dist = dist_setup(args)
     peaks = load_peaks()
@@ -885,6 +975,8 @@ def run_ours(args, workload):
         workload.step()
         if flush is not None:
             flush.fill_(1)
+    if hasattr(workload, "finish"):
+        workload.finish()
     barrier(dist)
     stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -895,6 +987,8 @@ def run_ours(args, workload):
             flush.fill_(1)
         ev[i][0].record(stream)
         workload.step()
+        if i == args.steps - 1 and hasattr(workload, "finish"):
+            workload.finish()
         ev[i][1].record(stream)
     torch.cuda.synchronize()
     barrier(dist)
@@ -933,6 +1027,10 @@ def run_ours(args, workload):
     e2e = {"value": round(e_units / (e_ms * 1e-3), 3), "unit": workload.unit,
            "h2d_bytes_per_step": int(workload.h2d), "d2h_bytes_per_step": int(workload.d2h)}
 
+    lif = None
+    if workload.name == "vgg16" and not args.no_lif:
+        lif = lif_kernel_object(dist, rank, world, local, peaks)
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
@@ -951,6 +1049,8 @@ def run_ours(args, workload):
                 "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(workload.launches_per_step * args.steps),
                 "clocks": clocks}
+        if lif is not None:
+            line["lif_kernel"] = lif
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -975,6 +1075,8 @@ def main():
     ap.add_argument("--load-choices", default=None,
                     help="vgg16: use a tuned kernel table instead of timing (e.g. under ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-lif", action="store_true",
+                    help="vgg16: skip the LIF-kernel bandwidth object (lif_kernel) of the line")
     ap.add_argument("--packed", default="none", choices=["none", "in", "out", "both"],
                     help="conv workload: packed spikes in / out (snnb_conv3x3_lif_packed)")
     ap.add_argument("--eager", action="store_true",

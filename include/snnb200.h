@@ -5,9 +5,12 @@
  * Every entry point
  *   - takes plain device pointers, element counts and a CUDA stream
  *     (snnb_stream_t is a cudaStream_t; NULL means the legacy default stream),
- *   - launches asynchronously on that stream and never synchronises it,
+ *   - launches asynchronously on that stream and never synchronises it (except
+ *     snnb_read_device_status, which must read the status word back),
  *   - allocates nothing: the caller owns every input, output and workspace,
- *     and passes workspace explicitly where a kernel needs scratch memory,
+ *     and passes workspace explicitly where a kernel needs scratch memory.  The
+ *     one exception is snnb_conv3x3_lif_static_scratch, whose scratch is a fixed
+ *     16 MiB array inside the library (held on every GPU that loads it),
  *   - returns an int status (SNNB_OK or a negative SNNB_ERR_*), never aborts and
  *     never throws across the boundary.
  * Shapes follow the reference's flattening: a multi-step tensor [T, B, ...] is
@@ -272,7 +275,8 @@ int snnb_conv3x3_lif_packed(const void* x, int x_packed, int64_t T, int64_t B, i
 int snnb_unpack_spikes(const void* words, int64_t rows, int64_t C, void* out,
                        snnb_stream_t stream);
 
-/* Workspace bytes snnb_conv3x3_lif / snnb_linear_lif (H = W = 1) need for `splits`. */
+/* Workspace bytes snnb_conv3x3_lif / snnb_linear_lif (H = W = 1) need for `splits`; 0 when
+ * splits <= 1, negative when a size is negative or the byte count overflows int64. */
 int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cout,
                                    int splits);
 
@@ -363,6 +367,35 @@ int snnb_spike_attention_core(const void* q, const void* k, const void* v, int64
  * (SNNB_ERR_TIMEOUT after a wait gave up).  Synchronises `stream`.
  */
 int snnb_read_device_status(snnb_stream_t stream, int* status_out);
+
+/*
+ * Spin limit, in SM clock cycles, of the tensor-core kernels' progress waits (a stage's
+ * copies, an accumulator, a free ring slot) on the current device; 0 restores the default
+ * of 4e9 cycles (~2 s at 1.9 GHz), other values must be >= 1000.  A wait that runs out
+ * sets SNNB_ERR_TIMEOUT in the device status word and the launch stops early, leaving its
+ * output incomplete.  The waits that drain copies or MMAs already issued after such a
+ * failure keep the default, so no CTA exits with copies in flight.  A wait's clock starts
+ * when the wait does, which with programmatic dependent launch can be before the previous
+ * kernel on the stream has finished: keep the limit well above the longest kernel.
+ * No counterpart in the reference (its Triton kernels have no waits); it exists so that a
+ * host can bound how long a failed launch holds the GPU, and so the tests can make a wait
+ * run out.
+ */
+int snnb_set_wait_limit(int64_t cycles);
+
+/*
+ * Test hooks (no counterpart in the reference), for exercising the failure paths without
+ * faulting a GPU:
+ *   snnb_debug_inject_status(status, count): the next `count` entry-point calls (any entry
+ *     that launches work) return `status` (a negative SNNB_ERR_*) without launching.
+ *   snnb_debug_inject_stall(count): in the next `count` launches of the T-sequential conv
+ *     kernel (snnb_conv3x3_lif variant 1), the producer warp of CTA 0 withholds every
+ *     stage; that CTA's MMA warp then waits until the wait limit runs out and the launch
+ *     reports SNNB_ERR_TIMEOUT (CTA 0's output is left unspecified).
+ * Both are process-wide; count 0 cancels.
+ */
+int snnb_debug_inject_status(int status, int count);
+int snnb_debug_inject_stall(int count);
 
 #ifdef __cplusplus
 }

@@ -62,3 +62,20 @@ def test_neuron_rejects_bad_arguments_without_a_device():
     assert call(mode=9) == -1                    # unknown threshold mode
     assert call(x=None) == -1                    # T > 0 with no input
     assert call(N=0) == 0                        # empty input is a no-op
+
+
+def test_split_workspace_size_overflow_is_rejected():
+    """A byte count that overflows int64 comes back negative (not wrapped to a small or
+    negative size that would pass a capacity check), and the no-allocation entry refuses it
+    before touching a device."""
+    from snn_compiler import _lib
+    L = _lib.lib()
+    big = 0x7fffffff
+    assert L.snnb_split_workspace_bytes(4, 64, 32, 32, 64, 1) == 0
+    assert L.snnb_split_workspace_bytes(4, 64, 32, 32, 64, 2) == 2 * 4 * 64 * 32 * 32 * 64 * 4
+    assert L.snnb_split_workspace_bytes(big, big, big, big, big, 8) < 0
+    assert L.snnb_split_workspace_bytes(-4, 1, 1, 1, 64, 2) < 0
+    st = L.snnb_conv3x3_lif_static_scratch(
+        None, big, big, big, big, 64, None, None, big, 0.5, 0.5, 1.0, 0.0, 1, 0, 0, 8, None,
+        None)
+    assert st == -1

@@ -33,14 +33,27 @@ def _worker(rank, world, port, B, q):
         from snn_compiler.sharding import ShardedInference
         g = torch.Generator().manual_seed(0)
         x = torch.rand(B, 3, 4, 4, generator=g)
-        y = ShardedInference(_fake_engine)(x)
+        if B < world:
+            # too few samples for the ranks: every rank refuses before any collective
+            try:
+                ShardedInference(_fake_engine)(x)
+                q.put("no error")
+            except ValueError:
+                if rank == 0:
+                    q.put("rejected")
+            return
+        sh = ShardedInference(_fake_engine)
+        y = sh(x)
+        # a second call reuses the preallocated slots and gives the same result
+        y2 = sh(x)
+        assert torch.equal(y, y2)
         if rank == 0:
             q.put(y)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,B", [(2, 8), (3, 10), (2, 1)])
+@pytest.mark.parametrize("world,B", [(2, 8), (3, 10), (3, 3), (2, 1), (3, 2)])
 def test_sharded_gather_equals_full_batch(world, B):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -52,6 +65,9 @@ def test_sharded_gather_equals_full_batch(world, B):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    if B < world:
+        assert y == "rejected"
+        return
     g = torch.Generator().manual_seed(0)
     x = torch.rand(B, 3, 4, 4, generator=g)
     assert torch.equal(y, _fake_engine(x))

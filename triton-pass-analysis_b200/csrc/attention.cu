@@ -221,6 +221,7 @@ extern "C" int snnb_spike_attention_core(
     const float* kv_in, float* kv_out, void* out, int64_t ot, int64_t ob, int64_t oh, int64_t on,
     int64_t T, int64_t B, int64_t H, int64_t N, int64_t d, float decay, float input_scale,
     float scale, float v_threshold, float v_reset, int hard_reset, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (T <= 0 || B <= 0 || H <= 0 || N <= 0 || d <= 0) return SNNB_ERR_ARG;
     const int64_t work = (d % 4 == 0) ? N * (d / 4) : N * d;
     if (d > MAX_D || N > MAX_W * 32 || work > (int64_t)MAX_ITEMS * THREADS)

@@ -218,6 +218,7 @@ using namespace snnb;
 
 extern "C" int snnb_bitpack(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ldw,
                             int positive, uint32_t* out, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (rows < 0 || K < 0 || ldw < (K + 31) / 32) return SNNB_ERR_ARG;
     if (rows == 0 || ldw == 0) return SNNB_OK;
     if (!out || (K > 0 && !x)) return SNNB_ERR_ARG;
@@ -236,6 +237,7 @@ extern "C" int snnb_bitpack(const void* x, int x_dtype, int64_t rows, int64_t K,
 
 extern "C" int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int64_t N,
                           int64_t K, int64_t ldw, int mode, int splits, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (M < 0 || N < 0 || K < 0 || mode < 0 || mode > 2) return SNNB_ERR_ARG;
     if (M == 0 || N == 0) return SNNB_OK;
     if (!A || !B || !C) return SNNB_ERR_ARG;

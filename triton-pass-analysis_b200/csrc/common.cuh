@@ -13,6 +13,16 @@ namespace snnb {
 // Records the text of a CUDA error for snnb_last_cuda_error() and maps it to a status.
 int record_cuda_error(cudaError_t e);
 
+// Test hooks (snnb_debug_inject_status / snnb_debug_inject_stall): a pending injected status
+// is returned (and consumed) by the next entry call; a pending stall is consumed by the next
+// launch of the T-sequential conv kernel.  0 when nothing is pending.
+int take_injected_status();
+int take_injected_stall();
+
+// Each translation unit with tensor-core waits registers the setter of its copy of the
+// per-device wait limit (tc_common.cuh); snnb_set_wait_limit calls them all.
+int register_wait_limit_setter(cudaError_t (*setter)(unsigned long long));
+
 // Status of the most recent launch on this thread (cudaGetLastError, which also clears it).
 inline int launch_status() {
     cudaError_t e = cudaGetLastError();

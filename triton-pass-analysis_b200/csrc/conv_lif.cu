@@ -45,7 +45,7 @@ __device__ __forceinline__ void drain_ring_warp(uint32_t bar0, int stages, int s
                                                 uint32_t phase, uint32_t issued) {
     for (uint32_t k = 0; k < (uint32_t)stages && k < issued; ++k) {
         if (--stage < 0) { stage = stages - 1; phase ^= 1u; }
-        tc::mbar_wait_warp(bar0 + 8u * stage, phase, 0);
+        tc::mbar_wait_warp<true>(bar0 + 8u * stage, phase, 0);
     }
 }
 
@@ -189,7 +189,11 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         int stage = 0, istage = 0;
         uint32_t phase = 0, iphase = 0, issued = 0, failed = 0;
         bool dep_ready = false;                 // griddepcontrol.wait done
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        // Test hook (snnb_debug_inject_stall): CTA 0's producer -- the CTA's only issuer of
+        // copies -- withholds every stage, so that the MMA warp's wait for the first stage
+        // runs out (SNNB_ERR_TIMEOUT) with nothing in flight in the CTA.
+        const int tile0 = (p.stall && blockIdx.x == 0) ? p.num_tiles : (int)blockIdx.x;
+        for (int tile = tile0; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_tile(tile, p, BN);
             for (int t = 0; t < p.T; ++t) {
                 const int f0 = t * p.B + tl.img0;
@@ -270,7 +274,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
         if (tc::elect_one()) tc::umma_commit(done_bar);
         __syncwarp();
-        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        failed |= 1u - tc::mbar_wait_warp<true>(done_bar, 0, 0);
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         // ------------------------------------------------------------- epilogue
@@ -484,9 +488,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
             uint32_t ph = iphase;
             for (uint32_t k = 0; k < (uint32_t)nst && k < issued; ++k) {
                 if (--st < 0) { st = nst - 1; ph ^= 1u; }
-                tc::mbar_wait_warp(full_bar(st), ph, 0);
+                tc::mbar_wait_warp<true>(full_bar(st), ph, 0);
             }
-            if (wissued > 0) tc::mbar_wait_warp(wfull_bar, (wissued - 1) & 1u, 0);
+            if (wissued > 0) tc::mbar_wait_warp<true>(wfull_bar, (wissued - 1) & 1u, 0);
             if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else if (warp == 1) {
@@ -556,7 +560,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         // every MMA issued must be complete before the CTA frees its TMEM
         if (tc::elect_one()) tc::umma_commit(done_bar);
         __syncwarp();
-        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        failed |= 1u - tc::mbar_wait_warp<true>(done_bar, 0, 0);
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         // ------------------------------------------------------------- epilogue
@@ -1131,6 +1135,19 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
                 : launch_persistent(conv_lif_band_kernel<32, false>, dyn, ta, tb, p, s);
 }
 
+// Bytes of the split-K partial sums, splits * T * B * H * W * Cout float32 values, or -1
+// when a factor is negative or the product overflows int64 (each factor may be as large as
+// 2^31 - 1, so the product of six of them can wrap).
+static int64_t split_partial_bytes(int64_t splits, int64_t T, int64_t B, int64_t H, int64_t W,
+                                   int64_t Cout) {
+    const int64_t f[6] = {splits, T, B, H, W, Cout};
+    int64_t n = 4;
+    for (int i = 0; i < 6; ++i) {
+        if (f[i] < 0 || __builtin_mul_overflow(n, f[i], &n)) return -1;
+    }
+    return n;
+}
+
 // Shared host path of the conv / linear entries.
 // variant: 0 = choose, 1 = T sequential inside the CTA (128-pixel blocks),
 //          2 = T folded into M (128/T-pixel blocks, T in {2, 4, 8}),
@@ -1147,6 +1164,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s,
                  const void* res = nullptr, int res_f32 = 0, int x_packed = 0,
                  int out_packed = 0) {
+    if (const int inj = take_injected_status()) return inj;
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
     // packed spikes in / out: the T-folded kernel (variant 2), one launch (no split-K), no
     // residual; packed input for 3x3 convs with Cin % 64 == 0
@@ -1246,8 +1264,9 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (cg == 2 && BN < 64) return SNNB_ERR_UNSUPPORTED;
     if (variant == 1 && res && BN > 64) BN = 64;     // residual operands: see conv_lif_kernel
     if (splits > 1 && !ck) {
-        const int64_t need = (int64_t)splits * T * B * H * W * Cout * 4;
-        if (!workspace || workspace_bytes < need || !aligned16(workspace)) return SNNB_ERR_ARG;
+        const int64_t need = split_partial_bytes(splits, T, B, H, W, Cout);
+        if (need < 0 || !workspace || workspace_bytes < need || !aligned16(workspace))
+            return SNNB_ERR_ARG;
     }
     int pk_px = 0, pk_ps = 0;
     if (x_packed) {
@@ -1329,6 +1348,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
                                    p.hard, pool, res, res_f32, p.out, s);
     }
+    p.stall = take_injected_stall();
     switch (BN) {
         case 128: return launch_conv<128, 6>(ta, tb, p, s);
         case 64: return launch_conv<64, 8>(ta, tb, p, s);
@@ -1477,7 +1497,7 @@ extern "C" int snnb_conv3x3_lif_dense(const void* x, int64_t T, int64_t B, int64
 extern "C" int64_t snnb_split_workspace_bytes(int64_t T, int64_t B, int64_t H, int64_t W,
                                               int64_t Cout, int splits) {
     if (splits <= 1) return 0;
-    return (int64_t)splits * T * B * H * W * Cout * 4;
+    return split_partial_bytes(splits, T, B, H, W, Cout);
 }
 
 extern "C" int snnb_read_device_status(snnb_stream_t stream, int* status_out) {
@@ -1524,7 +1544,8 @@ extern "C" int snnb_conv3x3_lif_static_scratch(
         Cout <= 0 || splits < 1 || splits > 8)
         return SNNB_ERR_ARG;
     const int64_t need = snnb_split_workspace_bytes(T, B, H, W, Cout, splits);
-    if (need > SNNB_STATIC_SCRATCH_BYTES) return SNNB_ERR_ARG;   // exceeds the fixed scratch
+    // negative: the size overflows int64; above the array: exceeds the fixed scratch
+    if (need < 0 || need > SNNB_STATIC_SCRATCH_BYTES) return SNNB_ERR_ARG;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return record_cuda_error(e);

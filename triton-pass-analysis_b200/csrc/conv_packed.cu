@@ -155,6 +155,7 @@ using namespace snnb;
 
 extern "C" int snnb_unpack_spikes(const void* words, int64_t rows, int64_t C, void* out,
                                   snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (!words || !out || rows < 0 || C <= 0 || C % 32 != 0) return SNNB_ERR_ARG;
     if (!aligned16(out) || (reinterpret_cast<uintptr_t>(words) & 3u)) return SNNB_ERR_ARG;
     const int64_t nwords = rows * (C / 32);

@@ -35,6 +35,8 @@ struct ConvParams {
     const uint32_t* xq;           // packed-spike input [T*B][H][W][Cin/32] (T-folded kernel)
     int out_packed;               // spikes stored packed, [T*B][Ho][Wo][Cout/32] uint32
     int pk_px, pk_ps;             // packed-input patch: words per pixel slot / per step plane
+    int stall;                    // test hook (snnb_debug_inject_stall): CTA 0's producer of
+                                  // the T-sequential kernel withholds every stage
 };
 
 struct Tile {
@@ -432,7 +434,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 // this warp's weight copies still in flight: bounded waits
                 uint32_t gg = last_g;
                 for (uint32_t k = 0; k < issued && k * NRR < (uint32_t)STAGES; ++k, gg -= NRR)
-                    tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+                    tc::mbar_wait_warp<true>(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
                 if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
             }
         }
@@ -506,16 +508,16 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             uint32_t gg = last_g;
             for (uint32_t k = 0; k < issued && k * NP < (uint32_t)STAGES; ++k, gg -= NP) {
                 if (PAIR && rank != 0)
-                    tc::mbar_wait_warp(empty_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+                    tc::mbar_wait_warp<true>(empty_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
                 else
-                    tc::mbar_wait_warp(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
+                    tc::mbar_wait_warp<true>(full_bar((int)(gg % STAGES)), (gg / STAGES) & 1u, 0);
             }
             if (lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else if (warp == 1 && PAIR && rank != 0) {
         // odd CTA of a pair: the even CTA issues every MMA; its last commit says that this
         // CTA's TMEM and shared memory are no longer in use by the tensor pipe
-        if (!tc::mbar_wait_warp(done_bar, 0, 0) && lane == 0) {
+        if (!tc::mbar_wait_warp<true>(done_bar, 0, 0) && lane == 0) {
             atomicExch(p.status, SNNB_ERR_TIMEOUT);
             *abort_flag = 1;
         }
@@ -588,7 +590,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             else tc::umma_commit(done_bar);
         }
         __syncwarp();
-        failed |= 1u - tc::mbar_wait_warp(done_bar, 0, 0);
+        failed |= 1u - tc::mbar_wait_warp<true>(done_bar, 0, 0);
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         const int set = warp >= W1 ? 1 : 0;             // which half of each slice

@@ -353,6 +353,7 @@ extern "C" int snnb_first_conv_lif(const float* x, int64_t Ti, int64_t T, int64_
                                    int64_t Cout, float decay, float input_scale,
                                    float v_threshold, float v_reset, int hard_reset, int pool,
                                    void* out, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (!x || !w || !bias || !out) return SNNB_ERR_ARG;
     if (T <= 0 || B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return SNNB_ERR_ARG;
     if (Ti != 1 && Ti != T) return SNNB_ERR_ARG;

@@ -192,10 +192,12 @@ using namespace snnb;
 
 extern "C" int snnb_linear_mean(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                                 const float* bias, int64_t N, float* out, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     return run_head(x, T, B, K, w, bias, N, out, 0, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int snnb_linear_out(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
                                const float* bias, int64_t N, float* out, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
     return run_head(x, T, B, K, w, bias, N, out, 1, static_cast<cudaStream_t>(stream));
 }

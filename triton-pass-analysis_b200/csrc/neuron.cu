@@ -388,6 +388,7 @@ extern "C" int snnb_neuron_cuba_eif(
     int hard_reset, float v_reset, int thr_mode, float thr_scalar, const float* thr,
     void* spikes, snnb_stream_t stream)
 {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (T < 0 || N < 0) return SNNB_ERR_ARG;
     if (x_dtype != SNNB_F32 && x_dtype != SNNB_F16 && x_dtype != SNNB_BF16) return SNNB_ERR_ARG;
     if (model != SNNB_MODEL_CUBA && model != SNNB_MODEL_EIF) return SNNB_ERR_ARG;
@@ -427,6 +428,7 @@ extern "C" int snnb_neuron_multistep(
     uint32_t* spikes_packed, float* count, float* v_out,
     snnb_stream_t stream)
 {
+    if (const int inj = snnb::take_injected_status()) return inj;
     if (T < 0 || N < 0) return SNNB_ERR_ARG;
     if (x_dtype != SNNB_F32 && x_dtype != SNNB_F16 && x_dtype != SNNB_BF16) return SNNB_ERR_ARG;
     if (spikes && (spikes_dtype < SNNB_F32 || spikes_dtype > SNNB_U8)) return SNNB_ERR_ARG;

@@ -11,8 +11,36 @@
 namespace snnb {
 namespace tc {
 
-// Spin limit for every mbarrier wait: ~2 s at the B200's 1.9 GHz SM clock.
-constexpr long long WAIT_LIMIT_CYCLES = 4000000000ll;
+// Spin limits of the mbarrier waits, in SM clock cycles.
+//  - Progress waits (a stage's copies, an accumulator, a free ring slot) give up after the
+//    per-device limit g_wait_limit: ~2 s at the B200's 1.9 GHz SM clock unless the host set
+//    another with snnb_set_wait_limit.  The value is read only once a wait has to spin.
+//  - Drain waits (after a failure: for copies or MMAs already issued, which complete on
+//    their own; or for the whole kernel's last commit) always use DRAIN_LIMIT_CYCLES, so a
+//    short progress limit can never let a CTA exit with copies still landing in its
+//    shared memory.
+constexpr unsigned long long DEFAULT_WAIT_LIMIT = 4000000000ull;
+constexpr unsigned long long DRAIN_LIMIT_CYCLES = 4000000000ull;
+constexpr long long WAIT_LIMIT_CYCLES = (long long)DEFAULT_WAIT_LIMIT;
+
+// One copy per translation unit that includes this header (no relocatable device code);
+// snnb_set_wait_limit writes every copy on the current device through the setters that
+// each unit registers at load time.
+static __device__ unsigned long long g_wait_limit = DEFAULT_WAIT_LIMIT;
+static cudaError_t set_wait_limit_tu(unsigned long long cycles) {
+    return cudaMemcpyToSymbol(g_wait_limit, &cycles, sizeof(cycles));
+}
+static const int g_wait_limit_setter_registered = register_wait_limit_setter(&set_wait_limit_tu);
+
+// The limit a wait uses: the run-time progress limit, or the fixed drain limit.
+template <bool DRAIN>
+__device__ __forceinline__ const unsigned long long* wait_limit_ptr() {
+    if constexpr (DRAIN) {
+        return nullptr;
+    } else {
+        return &g_wait_limit;
+    }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -55,7 +83,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (mbar_try_wait(bar, parity)) return true;
         if ((++it & 255u) == 0) {
             if (*abort_flag) return false;
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            if ((unsigned long long)(clock64() - t0) > *(volatile unsigned long long*)&g_wait_limit) {
                 atomicExch(status, SNNB_ERR_TIMEOUT);
                 *abort_flag = 1;
                 return false;
@@ -81,15 +109,19 @@ __device__ __forceinline__ bool elect_one() {
 // per-lane value (a branch there costs the MMA issuer its warp-uniform registers: each
 // tcgen05.mma issued after it took ~4x longer).  Returns 1 when the phase completed, 0 after
 // WAIT_LIMIT_CYCLES or at once when skip != 0 (an earlier wait of this warp failed).
+template <bool DRAIN = false>
 __device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity, uint32_t skip) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1, lim;\n\t"
         "setp.ne.u32 q, %3, 0;\n\t"
         "@q bra WFAIL_%=;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "vote.sync.all.pred p, p, 0xffffffff;\n\t"
         "@p bra WOK_%=;\n\t"
+        "mov.u64 lim, %4;\n\t"
+        "setp.eq.u64 q, %5, 0;\n\t"
+        "@!q ld.volatile.u64 lim, [%5];\n\t"
         "mov.u64 t0, %%clock64;\n\t"
         "WLOOP_%=:\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -97,7 +129,7 @@ __device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity
         "@p bra WOK_%=;\n\t"
         "mov.u64 t1, %%clock64;\n\t"
         "sub.u64 t1, t1, t0;\n\t"
-        "setp.lt.u64 q, t1, %4;\n\t"
+        "setp.lt.u64 q, t1, lim;\n\t"
         "vote.sync.any.pred q, q, 0xffffffff;\n\t"
         "@q bra WLOOP_%=;\n\t"
         "WFAIL_%=:\n\t"
@@ -107,7 +139,8 @@ __device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity
         "mov.u32 %0, 1;\n\t"
         "WEND_%=:\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "r"(bar), "r"(parity), "r"(skip), "l"(DRAIN_LIMIT_CYCLES),
+          "l"(wait_limit_ptr<DRAIN>())
         : "memory");
     return ok;
 }
@@ -118,18 +151,19 @@ __device__ __forceinline__ uint32_t mbar_wait_warp(uint32_t bar, uint32_t parity
 __device__ __forceinline__ uint32_t mbar_wait_lane(uint32_t bar, uint32_t parity, uint32_t skip) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1, lim;\n\t"
         "setp.ne.u32 q, %3, 0;\n\t"
         "@q bra LFAIL_%=;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "@p bra LOK_%=;\n\t"
+        "ld.volatile.u64 lim, [%4];\n\t"
         "mov.u64 t0, %%clock64;\n\t"
         "LLOOP_%=:\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "@p bra LOK_%=;\n\t"
         "mov.u64 t1, %%clock64;\n\t"
         "sub.u64 t1, t1, t0;\n\t"
-        "setp.lt.u64 q, t1, %4;\n\t"
+        "setp.lt.u64 q, t1, lim;\n\t"
         "@q bra LLOOP_%=;\n\t"
         "LFAIL_%=:\n\t"
         "mov.u32 %0, 0;\n\t"
@@ -138,7 +172,7 @@ __device__ __forceinline__ uint32_t mbar_wait_lane(uint32_t bar, uint32_t parity
         "mov.u32 %0, 1;\n\t"
         "LEND_%=:\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "r"(bar), "r"(parity), "r"(skip), "l"(&g_wait_limit)
         : "memory");
     return ok;
 }
@@ -347,9 +381,10 @@ __device__ __forceinline__ uint32_t mbar_wait_warp_cluster(uint32_t bar, uint32_
                                                            uint32_t skip) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+        "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1, lim;\n\t"
         "setp.ne.u32 q, %3, 0;\n\t"
         "@q bra CFAIL_%=;\n\t"
+        "ld.volatile.u64 lim, [%4];\n\t"
         "mov.u64 t0, %%clock64;\n\t"
         "CLOOP_%=:\n\t"
         "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
@@ -357,7 +392,7 @@ __device__ __forceinline__ uint32_t mbar_wait_warp_cluster(uint32_t bar, uint32_
         "@p bra COK_%=;\n\t"
         "mov.u64 t1, %%clock64;\n\t"
         "sub.u64 t1, t1, t0;\n\t"
-        "setp.lt.u64 q, t1, %4;\n\t"
+        "setp.lt.u64 q, t1, lim;\n\t"
         "vote.sync.any.pred q, q, 0xffffffff;\n\t"
         "@q bra CLOOP_%=;\n\t"
         "CFAIL_%=:\n\t"
@@ -367,7 +402,7 @@ __device__ __forceinline__ uint32_t mbar_wait_warp_cluster(uint32_t bar, uint32_
         "mov.u32 %0, 1;\n\t"
         "CEND_%=:\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(skip), "l"((unsigned long long)WAIT_LIMIT_CYCLES)
+        : "r"(bar), "r"(parity), "r"(skip), "l"(&g_wait_limit)
         : "memory");
     return ok;
 }

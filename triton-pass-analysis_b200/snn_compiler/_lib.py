@@ -47,6 +47,9 @@ SIGNATURES = {
     "snnb_first_conv_lif": [P, I64, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, P,
                             P],
     "snnb_read_device_status": [P, P],
+    "snnb_set_wait_limit": [I64],
+    "snnb_debug_inject_status": [I32, I32],
+    "snnb_debug_inject_stall": [I32],
     "snnb_linear_f32": [P, I64, I64, I64, P, P, I64, P, P],
     "snnb_spike_attention_core": [P, P, P, I64, I64, I64, I64, P, P, P, I64, I64, I64, I64,
                                   I64, I64, I64, I64, I64, F, F, F, F, F, I32, P],

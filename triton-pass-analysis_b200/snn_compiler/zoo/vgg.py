@@ -72,7 +72,7 @@ class SpikingVGG:
     def __init__(self, P, *, T: int = 4, tau: float = 2.0, decay_input: bool = True,
                  v_threshold: float = 1.0, v_reset: float = 0.0, soft_reset: bool = False,
                  neuron: str = "lif", device="cuda", autotune: bool = True,
-                 dense_small: bool = True):
+                 dense_small: bool = True, check_status: bool = False):
         self.T = T
         self.autotune = autotune
         # unpooled 3x3 layers on images of at most 2x2 pixels run as dense GEMMs
@@ -101,6 +101,9 @@ class SpikingVGG:
         self._bufs = {}
         self._workspace = None
         self.graphs = None
+        self._graph_cache = {}
+        self._fwd_pool = None
+        self.check_status = bool(check_status)
 
     # ---- per-layer launch plan -----------------------------------------------------------
     def plan(self, img: torch.Tensor, *, per_step_logits: bool = False,
@@ -123,9 +126,10 @@ class SpikingVGG:
             assert feat == self.fcs[0]["w"].shape[1], (feat, tuple(self.fcs[0]["w"].shape))
             fbufs = [torch.empty(T, B, f["w"].shape[0], device=self.device, dtype=torch.bfloat16)
                      for f in self.fcs[:-1]]
-            out = torch.empty((T, B, self.num_classes) if per_step_logits else (B, self.num_classes),
-                              device=self.device, dtype=torch.float32)
-            self._bufs[key] = (bufs, fbufs, out)
+            logits = torch.empty((T, B, self.num_classes) if per_step_logits
+                                 else (B, self.num_classes), device=self.device,
+                                 dtype=torch.float32)
+            self._bufs[key] = (bufs, fbufs, logits)
         bufs, fbufs, own_out = self._bufs[key]
         if out is None:
             out = own_out
@@ -223,16 +227,64 @@ class SpikingVGG:
         return n + sum(1 for k, c in self.choice.items()
                        if k[2] == B and c[2] > 1 and c[0] != 6)
 
-    def forward(self, img: torch.Tensor, *, per_step_logits: bool = False) -> torch.Tensor:
+    def forward(self, img: torch.Tensor, *, per_step_logits: bool = False,
+                out: torch.Tensor | None = None, graph: bool = False,
+                check: bool | None = None) -> torch.Tensor:
         """img [B, 3, H, W] (direct encoding: the same image at every step) or
-        [Ti, B, 3, H, W] f32 -> logits averaged over T [B, classes] (or [T, B, classes])."""
+        [Ti, B, 3, H, W] f32 -> logits averaged over T [B, classes] (or [T, B, classes]).
+
+        out   : optional float32 buffer of the logits' shape that receives them.
+        graph : replay the forward as a CUDA graph (captured on the first call for this
+                input shape and ``out``; each call's input is copied into the graph's own
+                input buffer, ``graph_input``) -- one graph launch instead of ~16 launches.
+        check : read the device status word after the forward (a stream synchronisation)
+                and raise SnnbError if a kernel's bounded wait gave up; defaults to the
+                engine's ``check_status``."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
-        img = img.to(self.device, torch.float32).contiguous()
-        steps, out = self.plan(img, per_step_logits=per_step_logits)
-        for _, _, fn in steps:
+        img = img.to(self.device, torch.float32)
+        if not img.is_contiguous():
+            img = img.contiguous()
+        if graph:
+            key = (tuple(img.shape), per_step_logits, None if out is None else out.data_ptr())
+            ent = self._graph_cache.get(key)
+            if ent is None:
+                static_in = torch.empty_like(img)          # the engine's own input buffer
+                static_in.copy_(img)
+                graphs, o = self._capture_graphs(static_in, per_step_logits, out)
+                ent = (static_in, graphs, o)
+                self._graph_cache[key] = ent
+            static_in, graphs, o = ent
+            if img.data_ptr() != static_in.data_ptr():
+                static_in.copy_(img, non_blocking=True)
+            for g in graphs:
+                g.replay()
+        else:
+            steps, o = self.plan(img, per_step_logits=per_step_logits, out=out)
+            for _, _, fn in steps:
+                fn()
+        if self.check_status if check is None else check:
+            KC.raise_on_device_status("SpikingVGG.forward")
+        return o
+
+    def graph_input(self, shape, *, per_step_logits: bool = False, out=None):
+        """The input buffer of the graph forward(graph=True) replays for this input shape
+        and ``out`` (a caller that writes its input there saves the copy), or None."""
+        key = (tuple(shape), per_step_logits, None if out is None else out.data_ptr())
+        ent = self._graph_cache.get(key)
+        return None if ent is None else ent[0]
+
+    def _capture_graphs(self, img, per_step_logits, out):
+        steps, o = self.plan(img, per_step_logits=per_step_logits, out=out)
+        for _, _, fn in steps:            # warm up (tunes the layers, sets kernel attributes)
             fn()
-        return out
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._fwd_pool):
+            for _, _, fn in steps:
+                fn()
+        torch.cuda.synchronize()
+        return [g], o
 
     __call__ = forward
 
