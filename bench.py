@@ -402,7 +402,10 @@ class VggWorkload:
         if key is None:
             return f"linear_head_kernel ({name})"
         v = self.eng.choice[key]
-        kern = {1: "conv_lif_kernel", 2: "conv_lif_tm_kernel", 3: "conv_lif_band_kernel"}.get(
+        kern = {1: "conv_lif_kernel", 2: "conv_lif_tm_kernel", 3: "conv_lif_band_kernel",
+                4: "conv_lif_tm_kernel (two M-tiles)", 5: "conv_lif_tm_kernel (CTA pairs)",
+                6: "conv_lif_tm_kernel (cluster split-K)",
+                7: "conv_lif_band_kernel (column taps in the epilogue)"}.get(
             v[0], "conv_lif (auto)")
         return f"{kern}<block_n={v[1]}, splits={v[2]}> ({name})"
 
@@ -632,7 +635,8 @@ class ConvLayerWorkload:
         run = lambda v, bn, sp: KC.conv3x3_lif(self.x, self.w, self.b, pool=True, out=self.out,
                                                variant=v, block_n=bn, splits=sp)
         self.choice = self.fixed if self.fixed else KC.pick_fastest(
-            run, self.cout, T, 9 * C // 64, band=KC.band_block_ns(H, C, self.cout))
+            run, self.cout, T, 9 * C // 64, band=KC.band_block_ns(H, C, self.cout),
+            band_xs=KC.band_xs_block_ns(H, C, self.cout))
         nws = KC.split_workspace_bytes(T, B, H, H, self.cout, self.choice[2])
         self.ws = torch.empty(nws // 4, device="cuda") if nws else None
         self.launches_per_step = 1

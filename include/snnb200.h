@@ -73,7 +73,8 @@ const char* snnb_last_cuda_error(void);
  * bias          : [C] float32 or NULL.
  * plif_w        : NULL, or a device float32 scalar w; then input_scale = k and
  *                 decay = 1 - k with k = sigmoid(w) (evaluated in double and
- *                 rounded to float32), overriding the two float arguments.
+ *                 rounded to float32), overriding the two float arguments -- PLIF in
+ *                 the reference's charge form; snnb_neuron_plif has SpikingJelly's.
  * thr           : [C] (per channel) or [N] (per neuron) float32 for those modes.
  * v_init        : [N] float32 initial potential, or NULL for zeros.
  * outputs (any subset, NULL = not written):
@@ -94,6 +95,27 @@ int snnb_neuron_multistep(
     void* spikes, int spikes_dtype,
     uint32_t* spikes_packed, float* count, float* v_out,
     snnb_stream_t stream);
+
+/*
+ * K2 -- SpikingJelly ParametricLIFNode (PLIF) over x [T, N] (no snn_compiler counterpart:
+ * PLIF lives in SpikingJelly, which the reference drives through
+ * examples/snn_triton_pipeline/.../_common/sj_compat.py:39-44).  k is a device float32
+ * scalar, SpikingJelly's w.sigmoid() (the caller evaluates it, as SpikingJelly does with
+ * torch on the module's device).  Per element, every operation rounded to float32 in
+ * SpikingJelly's order:
+ *   decay_input:                          v = v + (x - (v - v_reset)) * k
+ *   not decay_input, v_reset 0 or soft:   v = v * (1 - k) + x
+ *   not decay_input, v_reset != 0:        v = v - (v - v_reset) * k + x
+ *   s = v >= v_threshold;  hard: v = s ? v_reset : v;  soft: v = s ? v - v_threshold : v
+ * (soft reset is SpikingJelly's v_reset = None: the charge uses 0 for v_reset).  v starts at
+ * v_init, or 0 when v_init is NULL (SpikingJelly starts a hard-reset neuron at v_reset: pass
+ * v_init filled with it).  Outputs as snnb_neuron_multistep.
+ */
+int snnb_neuron_plif(const void* x, int x_dtype, int64_t T, int64_t N, const float* k,
+                     int decay_input, int hard_reset, float v_reset, float v_threshold,
+                     const float* v_init, void* spikes, int spikes_dtype,
+                     uint32_t* spikes_packed, float* count, float* v_out,
+                     snnb_stream_t stream);
 
 /* two-state / nonlinear neuron models of snnb_neuron_cuba_eif */
 #define SNNB_MODEL_CUBA  0
@@ -361,6 +383,40 @@ int snnb_spike_attention_core(const void* q, const void* k, const void* v, int64
                               int64_t on, int64_t T, int64_t B, int64_t H, int64_t N, int64_t d,
                               float decay, float input_scale, float scale, float v_threshold,
                               float v_reset, int hard_reset, snnb_stream_t stream);
+
+/*
+ * Image (first) layer on the tensor cores: replaces the first FusedConvBNNeuron of VGGSNN
+ * (snn_compiler/zoo/vgg.py:88-94 -> nn/modules.py:347-357, F.conv2d in float32 +
+ * fused_bias_if_lif) for direct encoding -- x [B, Cin, H, W] float32 NCHW, the same image at
+ * every one of the T steps, so the conv runs once per pixel and the neuron T times from it.
+ * The conv is float32-accurate: image and weights as three bf16 terms each, six products
+ * summed by tcgen05 MMAs into float32 (see snnb_split_bf16_terms).  w_split [Cout, KP] bf16
+ * is the folded weight's terms, groups [hi, mid, lo, hi, mid, hi] of 9 * Cin values in
+ * torch's (ci, ky, kx) order, zero-padded to KP = snnb_first_conv_tc_weight_k(Cin).
+ * out [T, B, H, W, Cout] bf16 spikes (no pooling).  Cin 1..4, Cout 32 / 64 / 128.
+ */
+int snnb_first_conv_lif_tc(const float* x, int64_t T, int64_t B, int64_t Cin, int64_t H,
+                           int64_t W, const void* w_split, const float* bias, int64_t Cout,
+                           float decay, float input_scale, float v_threshold, float v_reset,
+                           int hard_reset, void* out, snnb_stream_t stream);
+
+/* KP of snnb_first_conv_lif_tc's w_split for Cin input channels (-1 if Cin is not 1..4). */
+int64_t snnb_first_conv_tc_weight_k(int64_t Cin);
+
+/*
+ * float32 operands for the bf16 tensor-core kernels (no kernel of its own in the reference:
+ * it keeps the reference's float32 F.conv2d / F.linear on real-valued inputs float32-exact,
+ * snn_compiler/nn/modules.py:194-206, 241-255, 324-345).  x [rows, C] float32 -> out
+ * [rows, 6 * Cp] bf16: each value a as three bf16 terms hi = rn(a), mid = rn(a - hi),
+ * lo = rn(a - hi - mid), written as six channel groups [hi, hi, hi, mid, mid, lo] of Cp
+ * channels (channels C .. Cp-1 of each group zero).  Against weights split the same way and
+ * grouped [hi, mid, lo, hi, mid, hi], one bf16 conv / GEMM over the 6 * Cp channels sums the
+ * six larger term products, each exact in float32 (the three dropped ones stay below 2^-23
+ * of the product).  Cp >= C, Cp % 4 == 0 (so 6 * Cp % 8 == 0); x 16-byte aligned when
+ * C % 4 == 0, out 8-byte aligned.
+ */
+int snnb_split_bf16_terms(const float* x, int64_t rows, int64_t C, int64_t Cp, void* out,
+                          snnb_stream_t stream);
 
 /*
  * Reads and clears the device status word that kernels with bounded waits write

@@ -5,8 +5,9 @@ Python side of oracle/lif.c.  Parameter derivation follows the reference:
   LIF: df = 1 - 1/tau (or decay), sc = 1/tau if decay_input else 1.0
                                                       snn_compiler/kernels/neurons.py:352-354, :473-475
   PLIF (SpikingJelly ParametricLIFNode, no snn_compiler counterpart):
-       k = sigmoid(w) evaluated in double and rounded to float32, df = 1 - k
-       (float32 subtraction), sc = k
+       neuron_params("plif"): the reference's charge form with k = sigmoid(w) evaluated in
+       double and rounded to float32, df = 1 - k (float32 subtraction), sc = k;
+       plif_sj_multistep: SpikingJelly's own charge order (what PLIFNode computes)
 All arrays are flat in MEMORY order: x is [T, N] where N = numel of one step.
 """
 from __future__ import annotations
@@ -69,6 +70,45 @@ def neuron_params(neuron="if", *, tau=2.0, decay=None, decay_input=True, plif_w=
         k = np.float32(1.0 / (1.0 + np.exp(-w)))
         return np.float32(np.float32(1.0) - k), np.float32(k)
     raise ValueError(f"unknown neuron: {neuron!r}")
+
+
+def plif_sj_multistep(x, *, k, decay_input=True, hard_reset=True, v_reset=0.0, thr=1.0,
+                      v_init=None):
+    """SpikingJelly ParametricLIFNode over x [T, N] float32 (un-vendored third-party code:
+    spikingjelly.activation_based.neuron.ParametricLIFNode, as the reference's
+    examples/snn_triton_pipeline/*/scripts/_common/sj_compat.py:39-44 instantiates it).
+    Restates its published single-step loop, each operation rounded to float32 in its order:
+      neuronal_charge  decay_input:              v = v + (x - (v - v_reset)) * k
+                       else, v_reset None or 0:  v = v * (1 - k) + x
+                       else:                     v = v - (v - v_reset) * k + x
+      neuronal_fire    s = heaviside(v - v_threshold)  (== v >= v_threshold)
+      neuronal_reset   hard: v = (1 - s) * v + s * v_reset;  soft (v_reset None): v - s * thr
+    with k = w.sigmoid() given as a float32 (the caller's value), v starting at v_reset (hard)
+    or 0 (soft) unless v_init is given.  Returns dict(spikes [T, N] float32, v [N])."""
+    x = np.asarray(x, dtype=np.float32)
+    T, N = x.shape
+    k = np.float32(k)
+    vr = np.float32(v_reset if hard_reset else 0.0)
+    th = np.float32(thr)
+    one = np.float32(1.0)
+    v = np.full(N, vr, np.float32) if v_init is None else np.asarray(v_init, np.float32).copy()
+    out = np.zeros((T, N), np.float32)
+    for t in range(T):
+        xt = x[t]
+        if decay_input:
+            v = v + (xt - (v - vr)) * k
+        elif vr == 0:
+            v = v * (one - k) + xt
+        else:
+            v = v - (v - vr) * k + xt
+        v = v.astype(np.float32)
+        s = v >= th
+        out[t] = s
+        if hard_reset:
+            v = np.where(s, vr, v).astype(np.float32)
+        else:
+            v = np.where(s, v - th, v).astype(np.float32)
+    return {"spikes": out, "v": v}
 
 
 def lif_multistep(x, *, df, sc, hard_reset=True, v_reset=0.0, thr=1.0,

@@ -6,11 +6,12 @@ fused_bias_if_lif, kernels/fused.py:50-114):
 
     y = conv2d(x, W', stride, padding);  in = (y + b') (+ residual);  LIF / IF over T
 
-W' / b' are the module's folded weights (fold_conv_bn, fused.py:585-599).  A conv that the
-build runs on the tensor cores (3x3 / stride 1 / padding 1, Cin % 8 == 0, Cout % 32 == 0)
-uses bf16 operands there, so the oracle rounds W' to bf16 for it -- the reference's bf16
-mode; the products are then exact and only the float32 summation order differs.  The block
-structure follows snn_compiler/zoo/resnet.py:30-117 and zoo/sew_resnet.py:44-131.
+W' / b' are the module's folded weights (fold_conv_bn, fused.py:585-599).  The reference
+convolves in the input's dtype: on a bf16 input a tensor-core conv (3x3 / stride 1 /
+padding 1, Cin % 8 == 0, Cout % 32 == 0) has bf16 operands, so the oracle rounds W' to bf16
+for it (the products are then exact and only the float32 summation order differs); on a
+float32 input the conv is float32 and W' is kept as is.  The block structure follows
+snn_compiler/zoo/resnet.py:30-117 and zoo/sew_resnet.py:44-131.
 """
 from __future__ import annotations
 
@@ -37,7 +38,7 @@ def conv_bn_neuron(x_seq, weight, bias, *, stride, padding, neuron="lif", tau=2.
     """x_seq [T, B, Cin, H, W] float32 (CPU) -> (spikes, vpre), both [T, B, Cout, Ho, Wo]."""
     T, B = x_seq.shape[:2]
     w = weight.detach().float().cpu()
-    if tensor_core_conv(w, stride, padding):
+    if x_seq.dtype == torch.bfloat16 and tensor_core_conv(w, stride, padding):
         w = w.to(torch.bfloat16).float()
     y = F.conv2d(x_seq.reshape(T * B, *x_seq.shape[2:]).float(), w, None, stride=stride,
                  padding=padding)

@@ -64,7 +64,8 @@ def test_config2_layer_at_bench_batch(shape, p):
 
     if shape not in _CHOICE:     # the bench's choice: fastest pooled launch at B = 64
         _CHOICE[shape] = KC.pick_fastest(run, cout, T, 9 * cin // 64,
-                                         band=KC.band_block_ns(H, cin, cout))
+                                         band=KC.band_block_ns(H, cin, cout),
+                                         band_xs=KC.band_xs_block_ns(H, cin, cout))
     v, bn, sp = _CHOICE[shape]
     run(v, bn, sp, pool=True, out=out_p)
     run(v, bn, sp, pool=False, out=out_u)

@@ -74,7 +74,7 @@ GEOMS = [  # (T, B, Cin, Cout, H) -- every pixel-block geometry of VGG16 at 32x3
 VARIANTS = [(0, 0, 1), (1, 32, 1), (1, 128, 1), (2, 32, 1), (2, 64, 1), (2, 128, 1), (2, 256, 1),
             (2, 128, 3), (2, 256, 4), (3, 32, 1), (3, 64, 1), (4, 64, 1), (4, 128, 1),
             (4, 128, 2), (5, 64, 1), (5, 128, 1), (5, 256, 1), (5, 128, 2), (5, 256, 3),
-            (6, 128, 2), (6, 128, 4), (6, 256, 2), (6, 256, 8)]
+            (6, 128, 2), (6, 128, 4), (6, 256, 2), (6, 256, 8), (7, 32, 1), (7, 64, 1)]
 
 
 @pytest.mark.parametrize("vb", VARIANTS)
@@ -89,11 +89,12 @@ def test_conv3x3_lif_against_oracle(geom, vb):
     if variant in (2, 4, 5, 6) and T not in (2, 4, 8):
         pytest.skip("T folding needs T in {2, 4, 8}")
     C = _C()
-    if variant == 3 and block_n not in C.band_block_ns(H, Cin, Cout):
+    band_ok = C.band_block_ns if variant == 3 else C.band_xs_block_ns
+    if variant in (3, 7) and block_n not in band_ok(H, Cin, Cout):
         x = torch.zeros(T, B, H, H, Cin, device=DEV, dtype=torch.bfloat16)
         with pytest.raises(RuntimeError):
             C.conv3x3_lif(x, torch.zeros(Cout, 3, 3, Cin, device=DEV, dtype=torch.bfloat16),
-                          torch.zeros(Cout, device=DEV), variant=3, block_n=block_n)
+                          torch.zeros(Cout, device=DEV), variant=variant, block_n=block_n)
         return
     x, w, b = _layer_case(T, B, Cin, Cout, H, 0.15, sum(geom) * 31 + Cout, False)
     xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
@@ -323,3 +324,27 @@ def test_pack_unpack_round_trip_and_packed_limits():
         C.conv3x3_lif_packed(torch.zeros(4, 2, 8, 8, 1, dtype=torch.int32, device=DEV),
                              torch.zeros(64, 3, 3, 32, device=DEV, dtype=torch.bfloat16),
                              torch.zeros(64, device=DEV), x_packed=True, out_packed=False)
+
+
+@pytest.mark.parametrize("cin,cout,B,H,W,soft", [(3, 64, 3, 32, 32, False), (3, 64, 2, 7, 9, False),
+                                                 (1, 32, 2, 16, 16, True), (4, 128, 2, 12, 20, False),
+                                                 (2, 64, 5, 8, 8, True), (3, 32, 1, 5, 5, False)])
+def test_first_conv_tensor_core_against_oracle(cin, cout, B, H, W, soft):
+    """Image layer on tcgen05 (snnb_first_conv_lif_tc): the float32 conv from split bf16
+    terms against the float32 oracle conv -- flip criterion -- including partial 128-pixel
+    tiles (B*H*W not a multiple of 128) and image borders."""
+    C = _C()
+    T = 4
+    g = OP.gen(31 + cin + cout + H)
+    img = torch.rand(1, B, cin, H, W, generator=g)
+    w = torch.randn(cout, cin, 3, 3, generator=g) * (2.0 / (9 * cin)) ** 0.5 * 1.5
+    b = torch.rand(cout, generator=g) * 0.6 + 0.3
+    ws = C.first_conv_split_weight(w).to(DEV)
+    y = C.first_conv_lif_tc(img.to(DEV), ws, b.to(DEV), T=T, tau=2.0, v_threshold=THR,
+                            soft_reset=soft)
+    assert C.device_status() == 0
+    x = img.expand(T, B, cin, H, W).contiguous()
+    s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True, soft_reset=soft)
+    got = y.float().cpu().permute(0, 1, 4, 2, 3)
+    assert got.sum() > 0
+    flip_check(got, s, vpre)

@@ -136,3 +136,25 @@ def test_dense_conv_weight_equals_padded_conv():
         assert wd.shape == (H * W * Cout, H * W * Cin)
         got = x.permute(0, 2, 3, 1).reshape(N, -1) @ wd.t() + KC.dense_conv_bias(b, H, W).double()
         assert torch.allclose(got, ref, atol=1e-10), (H, W)
+
+
+def test_split_terms_represent_float32_and_six_products_are_float32_accurate():
+    """Host side of the float32-faithful tensor-core path: three bf16 terms reproduce a
+    float32 value to 2^-24, and the six kept products of activation and weight terms give
+    each x * w to within 2^-22 relative (the dropped three are below 2^-23)."""
+    import torch
+    from snn_compiler.kernels import conv as KC
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4096, generator=g) * torch.exp(torch.randn(4096, generator=g) * 5)
+    w = torch.randn(4096, generator=g) * torch.exp(torch.randn(4096, generator=g) * 5)
+    xh, xm, xl = (t.double() for t in KC.split_terms_host(x))
+    wh, wm, wl = (t.double() for t in KC.split_terms_host(w))
+    assert ((xh + xm + xl - x.double()).abs() <= 2.0 ** -24 * x.double().abs()).all()
+    terms = {"hi": (xh, wh), "mid": (xm, wm), "lo": (xl, wl)}
+    prod = sum(terms[a][0] * terms[b][1] for a, b in zip(KC.SPLIT_ACT, KC.SPLIT_WGT))
+    exact = x.double() * w.double()
+    assert ((prod - exact).abs() <= 2.0 ** -22 * exact.abs()).all()
+    # the weight groups line up with the activation groups channel by channel
+    wk = KC.split_weight_khwc(torch.randn(8, 6, 3, 3, generator=g))
+    assert wk.shape == (8, 3, 3, 6 * KC.split_width(6)) and wk.dtype == torch.bfloat16
+    assert (wk[..., 6:8] == 0).all()

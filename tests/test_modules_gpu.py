@@ -58,9 +58,16 @@ def test_fused_conv_bn_neuron_folded_runs_the_fused_kernel(layout):
     assert y.shape == (T, B, Cout, H, H) and y.dtype == torch.float32
     w, b = OV.fold_conv_bn(conv.weight.detach(), conv.bias.detach(), bn.weight.detach(),
                            bn.bias.detach(), bn.running_mean, bn.running_var, bn.eps)
-    s, _, vpre = OV.conv_bn_lif_pool(x, OV.bf16_round(w), b, pool=False, want_vpre=True)
+    # a float32 input convolves in float32 (both operands as three bf16 terms on the
+    # tensor cores): the oracle keeps the float32 folded weights
+    s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True)
     assert y.cpu().sum() > 0
     flip_check(y.cpu(), s, vpre)
+    # a bf16 input runs the bf16 kernel: bf16 weights, as the reference's bf16 mode
+    yb = m(xd.to(torch.bfloat16))
+    assert yb.dtype == torch.bfloat16
+    sb, _, vb = OV.conv_bn_lif_pool(x, OV.bf16_round(w), b, pool=False, want_vpre=True)
+    flip_check(yb.float().cpu(), sb, vb)
 
 
 def test_fused_conv_bn_neuron_unfolded_keeps_conv_and_bn_separate():
@@ -118,8 +125,8 @@ def test_fused_conv_neuron_other_geometry_and_residual_form():
     flip_check(y, s, vpre)
     w, b = OV.fold_conv_bn(conv.weight.detach(), conv.bias.detach(), bn.weight.detach(),
                            bn.bias.detach(), bn.running_mean, bn.running_var, bn.eps)
-    # the residual form of a 3x3 / s1 / p1 conv runs on the tensor cores: bf16 weights
-    w = w.to(torch.bfloat16).float()
+    # the residual form of a 3x3 / s1 / p1 conv runs on the tensor cores; a float32 input
+    # convolves float32-faithfully (split terms), so the oracle keeps float32 weights
     with torch.no_grad():
         za = torch.nn.functional.conv2d(x.reshape(T * B, Cin, H, H), w, None, 1, 1) \
                   .reshape(T, B, Cout, H, H)
@@ -138,8 +145,85 @@ def test_fused_linear_neuron_against_oracle():
     m = m.to(DEV)
     x = (torch.rand(T, B, K, generator=OP.gen(10)) < 0.2).float()
     y = m(x.to(DEV)).cpu()
-    w = OV.bf16_round(m.weight.detach().cpu())
+    w = m.weight.detach().cpu()                    # float32 input: float32 linear
     z = torch.nn.functional.linear(x.reshape(T * B, K), w).reshape(T, B, N)
     s, vpre = OV.lif_seq(z, m.bias.detach().cpu(), want_vpre=True)
     assert y.sum() > 0
     flip_check(y, s, vpre)
+    # bf16 input: the bf16 kernel, against bf16-rounded weights (the reference's bf16 mode)
+    yb = m(x.to(torch.bfloat16).to(DEV)).float().cpu()
+    zb = torch.nn.functional.linear(x.reshape(T * B, K), OV.bf16_round(w)).reshape(T, B, N)
+    sb, vb = OV.lif_seq(zb, m.bias.detach().cpu(), want_vpre=True)
+    flip_check(yb, sb, vb)
+
+
+def test_real_valued_float32_input_is_convolved_in_float32():
+    """A float32 module on a real-valued float32 input (Cin = 64, e.g. a second encoder
+    layer or a membrane-shortcut block) convolves in float32 as the reference's F.conv2d
+    does: the fused tcgen05 kernel carries both operands as three bf16 terms.  Membrane
+    potentials agree with the float32 oracle to float32 summation order (1e-5 here, against
+    ~1e-3 for bf16-rounded operands), and spikes flip only within 1e-4 of the threshold."""
+    from snn_compiler.kernels import conv as KC
+    from snn_compiler.nn import FusedConvBNNeuron, FusedLinearNeuron
+    T, B, Cin, Cout, H = 4, 2, 64, 64, 16
+    conv, bn = _conv_bn(Cin, Cout, 11)
+    m = FusedConvBNNeuron(conv, bn, **LIF).to(DEV)
+    x = torch.randn(T, B, Cin, H, H, generator=OP.gen(12)) * 0.7 + 0.3
+    y = m(x.to(DEV)).cpu()
+    assert "w" in m._cache and m._cache["key"][0] == "split"
+    w, b = OV.fold_conv_bn(conv.weight.detach(), conv.bias.detach(), bn.weight.detach(),
+                           bn.bias.detach(), bn.running_mean, bn.running_var, bn.eps)
+    s, _, vpre = OV.conv_bn_lif_pool(x, w, b, pool=False, want_vpre=True)
+    assert y.sum() > 0
+    flip_check(y, s, vpre)
+    # the pre-activation itself, through the GEMM form with a float32 output: the split
+    # operands' six products summed on the tensor cores against the exact (float64) sum,
+    # beside the bf16-rounded operands' error
+    xl0 = torch.randn(T, 32, 384, generator=OP.gen(15))
+    wl0 = torch.randn(96, 384, generator=OP.gen(16)) * 0.05
+    bl0 = torch.zeros(96)
+    ysplit = KC.linear_f32(KC.split_activations(xl0.to(DEV)), KC.split_weight_rows(wl0).to(DEV),
+                           bl0.to(DEV)).cpu().double()
+    exact = (xl0.double().reshape(-1, 384) @ wl0.double().t()).reshape(T, 32, 96)
+    ybf = (xl0.bfloat16().double().reshape(-1, 384) @ wl0.bfloat16().double().t()).reshape(T, 32, 96)
+    err = (ysplit - exact).abs().max().item()
+    assert err <= 1e-5 * exact.abs().max().item(), err
+    assert err * 20 < (ybf - exact).abs().max().item()
+    # float16 input: exact in float32, same float32-faithful path
+    y16 = m(x.to(torch.float16).to(DEV))
+    assert y16.dtype == torch.float16
+    s16, _, v16 = OV.conv_bn_lif_pool(x.half().float(), w, b, pool=False, want_vpre=True)
+    flip_check(y16.float().cpu(), s16, v16)
+    # linear on a real-valued float32 input
+    K, N = 384, 256
+    torch.manual_seed(2)
+    ml = FusedLinearNeuron(K, N, **LIF)
+    with torch.no_grad():
+        ml.weight.mul_(3.0)
+    ml = ml.to(DEV)
+    xl = torch.randn(T, 8, K, generator=OP.gen(13))
+    yl = ml(xl.to(DEV)).cpu()
+    zl = torch.nn.functional.linear(xl.reshape(T * 8, K), ml.weight.detach().cpu()).reshape(T, 8, N)
+    sl, vl = OV.lif_seq(zl, ml.bias.detach().cpu(), want_vpre=True)
+    assert yl.sum() > 0
+    flip_check(yl, sl, vl)
+
+
+def test_split_terms_device_matches_host_and_sums_to_the_value():
+    from snn_compiler.kernels import conv as KC
+    g = OP.gen(14)
+    x = torch.randn(1000, 20, generator=g) * torch.exp(torch.randn(1000, 20, generator=g) * 8)
+    x[0, :5] = torch.tensor([0.0, -0.0, 1e-40, 3.4e38, -1.5])
+    d = KC.split_activations(x.to(DEV)).cpu()
+    Cp = KC.split_width(20)
+    h, mi, lo = KC.split_terms_host(x)
+    for gi, name in enumerate(KC.SPLIT_ACT):
+        ref = {"hi": h, "mid": mi, "lo": lo}[name]
+        assert torch.equal(d[:, gi * Cp: gi * Cp + 20].view(torch.int16), ref.view(torch.int16))
+        assert (d[:, gi * Cp + 20: (gi + 1) * Cp] == 0).all()
+    # within 2^-24 of the value, or of the bf16 subnormal spacing 2^-133 for values so small
+    # that the terms fall below bf16's normal range
+    tot = h.double() + mi.double() + lo.double()
+    fin = torch.isfinite(x)
+    assert ((tot - x.double()).abs()[fin] <=
+            2.0 ** -24 * x.double().abs()[fin] + 2.0 ** -133).all()

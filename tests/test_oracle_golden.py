@@ -79,6 +79,23 @@ def test_plif_identity_with_lif_tau2():
     assert np.array_equal(a["spikes"], b["spikes"]) and np.array_equal(a["v"], b["v"])
 
 
+def test_plif_spikingjelly_order_tracks_lif_tau2_at_k_half():
+    """SpikingJelly's PLIF charge at k = 0.5 (init_tau 2), v + (x - v) * 0.5, against the
+    reference LIF tau=2, 0.5 v + 0.5 x: the same spikes except where v sits at the threshold
+    (the two round differently in the last bit), and the three charge forms of the restated
+    ParametricLIFNode agree at v_reset = 0 where they must."""
+    x = OP.lif_input(3, T=8, N=1 << 16).numpy()
+    sj = ON.plif_sj_multistep(x, k=np.float32(0.5))
+    ref = ON.lif_multistep(x, df=np.float32(0.5), sc=np.float32(0.5), want_vpre=True)
+    mism = sj["spikes"] != ref["spikes"]
+    assert mism.mean() < 1e-4
+    assert (np.abs(ref["vpre"][mism] - 1.0) < 1e-5).all()
+    # not decay_input with v_reset 0: the (1 - k) form; with v_reset != 0 the general form
+    a = ON.plif_sj_multistep(x, k=np.float32(0.25), decay_input=False, v_reset=0.0)
+    b = ON.plif_sj_multistep(x, k=np.float32(0.25), decay_input=False, v_reset=-0.5)
+    assert a["spikes"].sum() > 0 and b["spikes"].sum() > 0
+
+
 def test_stateful_chunks_compose():
     """v_out of one chunk as v_init of the next equals one full run
     (snn_compiler/tests/test_largeT_and_rate.py:106-132)."""

@@ -98,7 +98,8 @@ def test_conv3x3_residual_epilogue_against_oracle(variant, block_n, splits, res_
     y = C.conv3x3_lif(xd, C.weight_khwc(w).to(DEV), b.to(DEV), tau=2.0, v_threshold=1.0,
                       variant=variant, block_n=block_n, splits=splits, residual=rd)
     assert C.device_status() == 0
-    ref, vpre = OR.conv_bn_neuron(x, w, b, stride=1, padding=1, residual=res)
+    # the kernel ran on bf16 spikes: the oracle's bf16 mode (bf16-rounded weights)
+    ref, vpre = OR.conv_bn_neuron(x.to(torch.bfloat16), w, b, stride=1, padding=1, residual=res)
     got = y.float().cpu().permute(0, 1, 4, 2, 3)
     assert ref.sum() > 0
     bad = got != ref

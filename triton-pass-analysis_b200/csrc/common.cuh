@@ -114,6 +114,25 @@ __device__ __forceinline__ float reset_v(float v, bool s, float thr, float v_res
     return s ? __fsub_rn(v, thr) : v;
 }
 
+// float32 a as three bf16 terms hi = rn(a), mid = rn(a - hi), lo = rn(a - hi - mid) (each
+// subtraction exact in float32; non-finite values keep only hi).  A finite value
+// above bf16's largest (rounding would give infinity) takes hi = +-0x7F7F, the largest bf16.
+__device__ __forceinline__ void split_bf16x3(float a, __nv_bfloat16& h, __nv_bfloat16& m,
+                                       __nv_bfloat16& l) {
+    h = __float2bfloat16_rn(a);
+    if (isinf(__bfloat162float(h)) && isfinite(a))
+        h = __ushort_as_bfloat16(a > 0.0f ? (unsigned short)0x7F7F : (unsigned short)0xFF7F);
+    const float fh = __bfloat162float(h);
+    if (!isfinite(fh)) {
+        m = l = __float2bfloat16_rn(0.0f);
+        return;
+    }
+    const float r1 = __fsub_rn(a, fh);
+    m = __float2bfloat16_rn(r1);
+    const float r2 = __fsub_rn(r1, __bfloat162float(m));
+    l = __float2bfloat16_rn(r2);
+}
+
 // 8 spike bits -> 8 bf16 values (0.0 / 1.0) packed in 16 bytes, bit i -> element i.
 __device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
     uint32_t w[4];

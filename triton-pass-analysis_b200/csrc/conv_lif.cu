@@ -349,8 +349,8 @@ struct SmemBand {
     static constexpr int NBARS = 2 * BAND_MAX_STAGES + 7;
     // layout (runtime sizes): weights [w_bytes] | A ring [ring x a_bytes] | masks | barriers |
     // TMEM slot | abort flag
-    static int dyn_bytes(int w_bytes, int ring, int a_bytes) {
-        return w_bytes + ring * 3 * a_bytes + MASK_BYTES + NBARS * 8 + 8 + 1024;
+    static int dyn_bytes(int w_bytes, int ring, int a_bytes, int copies = 3) {
+        return w_bytes + ring * copies * a_bytes + MASK_BYTES + NBARS * 8 + 8 + 1024;
     }
 };
 
@@ -362,22 +362,34 @@ __device__ __forceinline__ Tile decode_band(int tile, const ConvParams& p, int B
     return Tile{0, band * p.bh, img, nb * BN};
 }
 
-template <int BN, bool HARD>
+// XS (variant 7, W <= 32): the column taps are shifted on the OUTPUT side instead.  A stage
+// holds ONE copy of the band (columns 0..W-1, no column halo), and tap (dy, dx) multiplies
+// rows dy*W .. dy*W + 127 of it into accumulator dx of the tile: D_dx[m] is then the dx tap's
+// share of output pixel m + 1 - dx (same image row).  The epilogue adds the three,
+// out[m] = D_1[m] + D_0[m - 1] + D_2[m + 1], with one-lane shuffles inside each row's W
+// lanes; a row's first (last) column takes no D_0 (D_2) term -- it would come from the
+// zero padding.  Stages are a third of the size, so the ring is three times deeper and the
+// operand copies' round trips hide behind the MMAs; TMEM holds 2 x 3 accumulators.
+template <int BN, bool HARD, bool XS>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const ConvParams p) {
     using S = SmemBand<BN>;
     constexpr int NCH = BN / 32;
     constexpr uint32_t TAP_BYTES = BN * 128;
-    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    constexpr int NACC = XS ? 3 : 1;                     // accumulators per (tile, step)
+    constexpr uint32_t ACC_COLS = NACC * BN;             // TMEM columns of one buffer
+    constexpr uint32_t TMEM_COLS = 2 * ACC_COLS <= 32 ? 32 : (2 * ACC_COLS <= 64 ? 64
+                                 : (2 * ACC_COLS <= 128 ? 128 : (2 * ACC_COLS <= 256 ? 256 : 512)));
+    static_assert(2 * ACC_COLS <= 512, "accumulators exceed TMEM");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = tc::smem_u32(smem);
     const int nst = p.ring;
     const uint32_t a_off = (uint32_t)p.w_bytes;
-    const uint32_t a_bytes = (uint32_t)p.a_bytes;        // one column-shifted copy
-    const uint32_t st_bytes = 3 * a_bytes;               // a stage: the three copies of a slab
+    const uint32_t a_bytes = (uint32_t)p.a_bytes;        // one (column-shifted) copy
+    const uint32_t st_bytes = (XS ? 1u : 3u) * a_bytes;  // a stage: the copies of a slab
     const uint32_t mask_off = a_off + (uint32_t)nst * st_bytes;
     uint32_t* smask = reinterpret_cast<uint32_t*>(smem + mask_off);
     const uint32_t bar_off = mask_off + S::MASK_BYTES;
@@ -467,9 +479,13 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (!failed && tc::elect_one()) {
                         tc::mbar_expect_tx(full_bar(stage), st_bytes);
                         const uint32_t dst = sbase + a_off + (uint32_t)stage * st_bytes;
-                        for (int dx = 0; dx < 3; ++dx)
-                            tc::tma_load_4d(dst + dx * a_bytes, &tmA, full_bar(stage), cb * 64,
-                                            dx - 1, tl.h0 - 1, f);
+                        if constexpr (XS) {
+                            tc::tma_load_4d(dst, &tmA, full_bar(stage), cb * 64, 0, tl.h0 - 1, f);
+                        } else {
+                            for (int dx = 0; dx < 3; ++dx)
+                                tc::tma_load_4d(dst + dx * a_bytes, &tmA, full_bar(stage),
+                                                cb * 64, dx - 1, tl.h0 - 1, f);
+                        }
                     }
                     __syncwarp();
                     if (++stage == nst) { stage = 0; phase ^= 1u; }
@@ -516,7 +532,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 const int a = it & 1;
                 failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
                 tc::tc_fence_after();
-                const uint32_t dcol = tmem + a * BN;
+                const uint32_t dcol = tmem + a * ACC_COLS;
                 for (int cb = 0; cb < CB; ++cb) {
                     int nstage = stage + 1;
                     uint32_t nphase = phase;
@@ -530,16 +546,18 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                         }
 #pragma unroll
                         for (int dx = 0; dx < 3; ++dx) {
-                            const uint32_t abase = sb + dx * a_bytes;
+                            const uint32_t abase = XS ? sb : sb + dx * a_bytes;
                             const uint32_t wbase = sbase + (uint32_t)((cb * 3 + dx) * 3) * TAP_BYTES;
+                            const uint32_t dst = XS ? dcol + dx * BN : dcol;
 #pragma unroll
                             for (int dy = 0; dy < 3; ++dy) {
                                 const uint64_t da = tc::sdesc_k_sw128(abase + dy * row_step);
                                 const uint64_t db = tc::sdesc_k_sw128(wbase + dy * TAP_BYTES);
 #pragma unroll
                                 for (int k = 0; k < 4; ++k)
-                                    tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
-                                                  (cb | dx | dy | k) != 0);
+                                    tc::umma_bf16(dst, da + 2 * k, db + 2 * k, IDESC,
+                                                  XS ? ((cb | dy | k) != 0)
+                                                     : ((cb | dx | dy | k) != 0));
                             }
                         }
                         if (cb + 1 < CB) {
@@ -591,13 +609,32 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 const int a = it & 1;
                 failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
                 tc::tc_fence_after();
-                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * BN;
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * ACC_COLS;
                 uint32_t mk[NCH];
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
                     float r[32];
-                    tc::tmem_ld32(tbase + c * 32, r);
+                    tc::tmem_ld32(tbase + (XS ? BN : 0) + c * 32, r);
                     tc::tmem_wait_ld();
+                    if constexpr (XS) {
+                        // out[m] = D_1[m] + D_0[m - 1] + D_2[m + 1] within the image row
+                        // (W lanes; W <= 32 divides the warp)
+                        float e[32];
+                        tc::tmem_ld32(tbase + c * 32, e);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float u = __shfl_up_sync(0xffffffffu, e[j], 1, W);
+                            r[j] = __fadd_rn(r[j], x > 0 ? u : 0.0f);
+                        }
+                        tc::tmem_ld32(tbase + 2 * BN + c * 32, e);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float d = __shfl_down_sync(0xffffffffu, e[j], 1, W);
+                            r[j] = __fadd_rn(r[j], x < W - 1 ? d : 0.0f);
+                        }
+                    }
                     uint32_t mask = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -1084,15 +1121,17 @@ int band_block_n(int W, int Cin, int Cout, int block_n) {
 int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const void* w,
                    const float* bias, int Cout, int BN, float df, float sc, float thr,
                    float v_reset, int hard, int pool, const void* res, int res_f32, void* out,
-                   int* status, cudaStream_t s) {
+                   int* status, cudaStream_t s, bool xs = false) {
     const int bh = 128 / W;
     if (pool && (bh % 2)) return SNNB_ERR_UNSUPPORTED;
+    if (xs && W > 32) return SNNB_ERR_UNSUPPORTED;       // a row's lanes must share a warp
     const int CB = (Cin + 63) / 64;
     const int a_bytes = (bh + 2) * W * 128;
     const int w_bytes = 9 * CB * BN * 128;
-    const int fixed = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, 0, a_bytes)
-                               : SmemBand<32>::dyn_bytes(w_bytes, 0, a_bytes);
-    int ring = (smem_optin() - fixed) / (3 * a_bytes);
+    const int copies = xs ? 1 : 3;
+    const int fixed = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, 0, a_bytes, copies)
+                               : SmemBand<32>::dyn_bytes(w_bytes, 0, a_bytes, copies);
+    int ring = (smem_optin() - fixed) / (copies * a_bytes);
     if (ring > BAND_MAX_STAGES) ring = BAND_MAX_STAGES;
     if (ring < 2) return SNNB_ERR_UNSUPPORTED;
     // activation map: dims (Cin, W, H, T*B), box (64, W, bh + 2, 1): the band and its halo
@@ -1126,13 +1165,20 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
     p.res = res; p.res_f32 = res_f32;
     p.splits = 1; p.partial = nullptr;
     p.ring = ring; p.a_bytes = a_bytes; p.w_bytes = w_bytes;
-    const int dyn = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes)
-                             : SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes);
+    const int dyn = BN == 64 ? SmemBand<64>::dyn_bytes(w_bytes, ring, a_bytes, copies)
+                             : SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes, copies);
+    if (xs) {
+        if (BN == 64)
+            return hard ? launch_persistent(conv_lif_band_kernel<64, true, true>, dyn, ta, tb, p, s)
+                        : launch_persistent(conv_lif_band_kernel<64, false, true>, dyn, ta, tb, p, s);
+        return hard ? launch_persistent(conv_lif_band_kernel<32, true, true>, dyn, ta, tb, p, s)
+                    : launch_persistent(conv_lif_band_kernel<32, false, true>, dyn, ta, tb, p, s);
+    }
     if (BN == 64)
-        return hard ? launch_persistent(conv_lif_band_kernel<64, true>, dyn, ta, tb, p, s)
-                    : launch_persistent(conv_lif_band_kernel<64, false>, dyn, ta, tb, p, s);
-    return hard ? launch_persistent(conv_lif_band_kernel<32, true>, dyn, ta, tb, p, s)
-                : launch_persistent(conv_lif_band_kernel<32, false>, dyn, ta, tb, p, s);
+        return hard ? launch_persistent(conv_lif_band_kernel<64, true, false>, dyn, ta, tb, p, s)
+                    : launch_persistent(conv_lif_band_kernel<64, false, false>, dyn, ta, tb, p, s);
+    return hard ? launch_persistent(conv_lif_band_kernel<32, true, false>, dyn, ta, tb, p, s)
+                : launch_persistent(conv_lif_band_kernel<32, false, false>, dyn, ta, tb, p, s);
 }
 
 // Bytes of the split-K partial sums, splits * T * B * H * W * Cout float32 values, or -1
@@ -1190,7 +1236,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (!aligned16(x) || !aligned16(w) || (!out_packed && !aligned16(out))) return SNNB_ERR_ARG;
     if (pool == 1 && ((H % 2) || (W % 2))) return SNNB_ERR_UNSUPPORTED;
     if ((int64_t)T * B > 0x7fffffff / 2) return SNNB_ERR_ARG;
-    if (variant < 0 || variant > 6) return SNNB_ERR_ARG;
+    if (variant < 0 || variant > 7) return SNNB_ERR_ARG;
     // variant 6: T folded into M, the K range split across a cluster of `splits` CTAs that
     // reduce through distributed shared memory (conv_cluster.cu); no workspace
     const bool ck = variant == 6;
@@ -1220,14 +1266,14 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (splits > 8) return SNNB_ERR_UNSUPPORTED;
     const int KB = taps * ((Cin + 63) / 64);
     if (splits > KB) return SNNB_ERR_ARG;
-    if (variant == 3) {
+    if (variant == 3 || variant == 7) {
         if (taps != 9 || splits > 1 || res) return SNNB_ERR_UNSUPPORTED;
         const int BN3 = band_block_n(W, Cin, Cout, block_n);
         if (!BN3) return SNNB_ERR_UNSUPPORTED;
         int* st = device_status_ptr();
         if (!st) return SNNB_ERR_CUDA;
         return run_band_layer(x, T, B, H, W, Cin, w, bias, Cout, BN3, df, sc, thr, v_reset, hard,
-                              pool, res, res_f32, out, st, s);
+                              pool, res, res_f32, out, st, s, variant == 7);
     }
     const bool tm_ok = (T == 2 || T == 4 || T == 8);
     if (variant == 2 && !tm_ok) return SNNB_ERR_UNSUPPORTED;

@@ -25,6 +25,7 @@ struct NeuronParams {
     const float* thr;
     const float* v_init;
     const float* plif_w;
+    const float* plif_k;       // charge modes 1-3: device scalar k (SpikingJelly's w.sigmoid())
     void* spikes;
     uint32_t* packed;
     float* count;
@@ -32,6 +33,7 @@ struct NeuronParams {
     int64_t T, N, C, HW, words;
     float df, sc, v_reset, thr_scalar;
     int hard, thr_mode, channel_last;
+    int charge_mode;
 };
 
 __device__ __forceinline__ int64_t channel_of(int64_t n, const NeuronParams& p) {
@@ -41,6 +43,27 @@ __device__ __forceinline__ int64_t channel_of(int64_t n, const NeuronParams& p) 
                               : (int64_t)((u / (uint32_t)p.HW) % (uint32_t)p.C);
     }
     return p.channel_last ? n % p.C : (n / p.HW) % p.C;
+}
+
+// Charge modes.  0: the reference's v = decay*v + input_scale*in (neurons.py:129-132,
+// fused.py:106-110).  1-3: SpikingJelly ParametricLIFNode.neuronal_charge, term by term in
+// its order, with k = sigmoid(w) computed by the caller:
+//   1  decay_input:                     v = v + (in - (v - v_reset)) * k
+//   2  not decay_input, v_reset 0/None: v = v * (1 - k) + in
+//   3  not decay_input, v_reset != 0:   v = v - (v - v_reset) * k + in
+// (for v_reset == 0, mode 1 is SpikingJelly's v + (in - v) * k exactly: v - 0 == v).
+template <int CM>
+__device__ __forceinline__ float charge_cm(float v, float df, float sc, float in, float k,
+                                           float om, float vr) {
+    if constexpr (CM == 0) {
+        return charge(v, df, sc, in);
+    } else if constexpr (CM == 1) {
+        return __fadd_rn(v, __fmul_rn(__fsub_rn(in, __fsub_rn(v, vr)), k));
+    } else if constexpr (CM == 2) {
+        return __fadd_rn(__fmul_rn(v, om), in);
+    } else {
+        return __fadd_rn(__fsub_rn(v, __fmul_rn(__fsub_rn(v, vr), k)), in);
+    }
 }
 
 __device__ __forceinline__ void neuron_coeffs(const NeuronParams& p, float& df, float& sc) {
@@ -118,7 +141,7 @@ constexpr int VEC = 8;     // neurons per thread
 constexpr int TU = 4;      // time steps whose loads are in flight together
 constexpr int THREADS = 256;
 
-template <typename TX, typename TS>
+template <typename TX, typename TS, int CM>
 __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
     pdl_wait();
     pdl_trigger();
@@ -128,6 +151,8 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
     const int lane = threadIdx.x & 31;
     float df, sc;
     neuron_coeffs(p, df, sc);
+    const float pk = CM ? __ldg(p.plif_k) : 0.0f;
+    const float om = CM == 2 ? __fsub_rn(1.0f, pk) : 0.0f;
 
     float v[VEC], th[VEC], bb[VEC], cnt[VEC];
     const bool need_c = (p.bias != nullptr) || (p.thr_mode == SNNB_THR_PER_CHANNEL);
@@ -176,7 +201,7 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
                 float in = xr[u][k];
                 if (has_bias) in = __fadd_rn(in, bb[k]);
                 if (res) in = __fadd_rn(in, rr[u][k]);
-                float vv = charge(v[k], df, sc, in);
+                float vv = charge_cm<CM>(v[k], df, sc, in, pk, om, p.v_reset);
                 const bool s = vv >= th[k];
                 if (p.hard) {
                     vv = s ? p.v_reset : vv;
@@ -208,7 +233,7 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
 
 // Scalar path for ragged N or unaligned pointers: one neuron per thread; a warp
 // covers 32 consecutive neurons, so one ballot is one packed word.
-template <typename TX, typename TS>
+template <typename TX, typename TS, int CM>
 __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) {
     pdl_wait();
     pdl_trigger();
@@ -217,6 +242,8 @@ __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) 
     const int lane = threadIdx.x & 31;
     float df, sc;
     neuron_coeffs(p, df, sc);
+    const float pk = CM ? __ldg(p.plif_k) : 0.0f;
+    const float om = CM == 2 ? __fsub_rn(1.0f, pk) : 0.0f;
     const bool need_c = (p.bias != nullptr) || (p.thr_mode == SNNB_THR_PER_CHANNEL);
     const int64_t c = (active && need_c) ? channel_of(n, p) : 0;
     float v = (active && p.v_init) ? p.v_init[n] : 0.0f;
@@ -233,7 +260,7 @@ __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) 
             float in = to_f32(x[t * p.N + n]);
             if (p.bias) in = __fadd_rn(in, bb);
             if (res) in = __fadd_rn(in, to_f32(res[t * p.N + n]));
-            float vv = charge(v, df, sc, in);
+            float vv = charge_cm<CM>(v, df, sc, in, pk, om, p.v_reset);
             s = vv >= th;
             if (p.hard) vv = s ? p.v_reset : vv;
             else vv = s ? __fsub_rn(vv, th) : vv;
@@ -252,15 +279,27 @@ __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) 
     }
 }
 
-template <typename TX, typename TS>
-int launch_typed(const NeuronParams& p, bool vec, cudaStream_t s) {
+template <typename TX, typename TS, int CM>
+int launch_cm(const NeuronParams& p, bool vec, cudaStream_t s) {
     if (vec) {
         const int64_t threads = (p.N + VEC - 1) / VEC;
         const int64_t blocks = (threads + THREADS - 1) / THREADS;
-        return launch_k(neuron_vec8_kernel<TX, TS>, dim3((unsigned)blocks), dim3(THREADS), 0, s, p);
+        return launch_k(neuron_vec8_kernel<TX, TS, CM>, dim3((unsigned)blocks), dim3(THREADS), 0,
+                        s, p);
     }
     const int64_t blocks = (p.N + THREADS - 1) / THREADS;
-    return launch_k(neuron_scalar_kernel<TX, TS>, dim3((unsigned)blocks), dim3(THREADS), 0, s, p);
+    return launch_k(neuron_scalar_kernel<TX, TS, CM>, dim3((unsigned)blocks), dim3(THREADS), 0,
+                    s, p);
+}
+
+template <typename TX, typename TS>
+int launch_typed(const NeuronParams& p, bool vec, cudaStream_t s) {
+    switch (p.charge_mode) {
+        case 1: return launch_cm<TX, TS, 1>(p, vec, s);
+        case 2: return launch_cm<TX, TS, 2>(p, vec, s);
+        case 3: return launch_cm<TX, TS, 3>(p, vec, s);
+        default: return launch_cm<TX, TS, 0>(p, vec, s);
+    }
 }
 
 template <typename TX>
@@ -442,7 +481,7 @@ extern "C" int snnb_neuron_multistep(
     if (T > (int64_t)1 << 40 || N > (int64_t)1 << 40) return SNNB_ERR_ARG;
     if ((N + 255) / 256 > 0x7fffffffll) return SNNB_ERR_ARG;
 
-    NeuronParams p;
+    NeuronParams p = {};
     p.x = x; p.residual = residual; p.bias = bias; p.thr = thr; p.v_init = v_init;
     p.plif_w = plif_w; p.spikes = spikes; p.packed = spikes_packed; p.count = count;
     p.v_out = v_out;
@@ -452,6 +491,39 @@ extern "C" int snnb_neuron_multistep(
 
     const bool vec = (N % VEC == 0) && aligned16(x) && (!residual || aligned16(residual)) &&
                      (!spikes || aligned16(spikes));
+    const int sd = spikes ? spikes_dtype : SNNB_U8;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (x_dtype) {
+        case SNNB_F32: return launch_x<float>(p, sd, vec, s);
+        case SNNB_F16: return launch_x<__half>(p, sd, vec, s);
+        default: return launch_x<__nv_bfloat16>(p, sd, vec, s);
+    }
+}
+
+extern "C" int snnb_neuron_plif(
+    const void* x, int x_dtype, int64_t T, int64_t N, const float* k, int decay_input,
+    int hard_reset, float v_reset, float v_threshold, const float* v_init,
+    void* spikes, int spikes_dtype, uint32_t* spikes_packed, float* count, float* v_out,
+    snnb_stream_t stream)
+{
+    if (const int inj = snnb::take_injected_status()) return inj;
+    if (T < 0 || N < 0 || !k) return SNNB_ERR_ARG;
+    if (x_dtype != SNNB_F32 && x_dtype != SNNB_F16 && x_dtype != SNNB_BF16) return SNNB_ERR_ARG;
+    if (spikes && (spikes_dtype < SNNB_F32 || spikes_dtype > SNNB_U8)) return SNNB_ERR_ARG;
+    if (N == 0) return SNNB_OK;
+    if (T > 0 && x == nullptr) return SNNB_ERR_ARG;
+    if (T > (int64_t)1 << 40 || N > (int64_t)1 << 40) return SNNB_ERR_ARG;
+    if ((N + 255) / 256 > 0x7fffffffll) return SNNB_ERR_ARG;
+    NeuronParams p = {};
+    p.x = x; p.v_init = v_init; p.plif_k = k;
+    p.spikes = spikes; p.packed = spikes_packed; p.count = count; p.v_out = v_out;
+    p.T = T; p.N = N; p.C = 1; p.HW = 1; p.words = (N + 31) / 32;
+    // SpikingJelly's soft reset (v_reset None) charges as v_reset == 0
+    const float vr = hard_reset ? v_reset : 0.0f;
+    p.v_reset = vr; p.thr_scalar = v_threshold;
+    p.hard = hard_reset ? 1 : 0; p.thr_mode = SNNB_THR_SCALAR;
+    p.charge_mode = decay_input ? 1 : (vr == 0.0f ? 2 : 3);
+    const bool vec = (N % VEC == 0) && aligned16(x) && (!spikes || aligned16(spikes));
     const int sd = spikes ? spikes_dtype : SNNB_U8;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (x_dtype) {

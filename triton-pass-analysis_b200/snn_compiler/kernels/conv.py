@@ -40,7 +40,8 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     and resident weights (band_block_ns), 4 = 2 with two M-tiles per CTA, 5 = 2 on CTA pairs
     (M = 256 MMAs, half the weight rows staged per CTA), 6 = 2 with the K range split across
     a thread-block cluster of `splits` CTAs that reduce through distributed shared memory
-    (no workspace); block_n: 0 or 32/64/128/256;
+    (no workspace), 7 = 3 with the column taps shifted in the epilogue (one operand copy
+    per stage, W <= 32, band_xs_block_ns); block_n: 0 or 32/64/128/256;
     splits > 1: split-K with float32 partials in `workspace` (allocated here if None)
     except with variant 6."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
@@ -101,7 +102,10 @@ def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: 
 
 
 def split_workspace_bytes(T, B, H, W, Cout, splits) -> int:
-    return int(_lib.lib().snnb_split_workspace_bytes(T, B, H, W, Cout, int(splits)))
+    n = int(_lib.lib().snnb_split_workspace_bytes(T, B, H, W, Cout, int(splits)))
+    if n < 0:
+        raise ValueError(f"split-K workspace size overflows: {(splits, T, B, H, W, Cout)}")
+    return n
 
 
 def _workspace(ws, splits, T, B, H, W, Cout, device):
@@ -184,6 +188,48 @@ def first_conv_lif(img: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, T:
     return out
 
 
+def first_conv_split_weight(w: torch.Tensor) -> torch.Tensor:
+    """Image-layer conv weight [Cout, Cin, 3, 3] (float32, BN folded) -> the tensor-core
+    image kernel's operand [Cout, KP] bf16: six groups of K0 = 9 * Cin terms in torch's
+    (ci, ky, kx) order, [hi, mid, lo, hi, mid, hi] (SPLIT_WGT), zero-padded to KP."""
+    Cout, Cin = w.shape[:2]
+    K0 = 9 * Cin
+    KP = int(_lib.lib().snnb_first_conv_tc_weight_k(Cin))
+    if KP < 0:
+        raise ValueError(f"tensor-core image layer takes Cin <= 4, got {Cin}")
+    h, m, l = split_terms_host(w.detach().float().reshape(Cout, K0))
+    terms = {"hi": h, "mid": m, "lo": l}
+    out = torch.zeros(Cout, KP, dtype=torch.bfloat16, device=w.device)
+    for g, name in enumerate(SPLIT_WGT):
+        out[:, g * K0:(g + 1) * K0] = terms[name]
+    return out.contiguous()
+
+
+def first_conv_lif_tc(img: torch.Tensor, w_split: torch.Tensor, bias: torch.Tensor, *, T: int,
+                      neuron: str = "lif", tau: float = 2.0, decay=None, decay_input: bool = True,
+                      soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Image layer on the tensor cores (snnb_first_conv_lif_tc): img [1, B, Cin, H, W] float32
+    (direct encoding: the same image at every step), w_split from first_conv_split_weight ->
+    spikes [T, B, H, W, Cout] bf16.  float32-accurate conv (split operands), computed once
+    per pixel; no pooling."""
+    assert img.is_cuda and img.dtype == torch.float32 and img.is_contiguous() and img.ndim == 5
+    assert img.shape[0] == 1, "direct encoding: one image per sample"
+    _, B, Cin, H, W = img.shape
+    Cout = w_split.shape[0]
+    assert w_split.dtype == torch.bfloat16 and w_split.is_contiguous()
+    assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == Cout
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    if out is None:
+        out = torch.empty(T, B, H, W, Cout, device=img.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_first_conv_lif_tc(_lib.ptr(img), T, B, Cin, H, W, _lib.ptr(w_split),
+                                           _lib.ptr(bias), Cout, df, sc, thr, vr, hard,
+                                           _lib.ptr(out), _lib.stream_of(img))
+    _lib.check(st, "snnb_first_conv_lif_tc")
+    return out
+
+
 def time_graph(fn, reps: int = 10) -> float:
     """Device milliseconds per call of fn (a launcher on the current stream): reps calls
     are captured into one CUDA graph and the replay is timed with events, so host-side
@@ -215,12 +261,18 @@ def band_block_ns(W: int, cin: int, cout: int):
     return tuple(bn for bn in (32, 64) if cout % bn == 0 and 9 * cb * bn <= 864)
 
 
+def band_xs_block_ns(W: int, cin: int, cout: int):
+    """Channel-block widths of variant 7 (band kernel with the column taps shifted in the
+    epilogue): those of variant 3 when an image row fits one warp (W <= 32)."""
+    return band_block_ns(W, cin, cout) if W <= 32 else ()
+
+
 def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
-               dense_pool: bool = False):
-    """(variant, block_n, splits) configurations a layer admits; `band` lists the
-    block widths of variant 3 the layer qualifies for (band_block_ns); dense_pool: the
-    pooled dense form (snnb_conv3x3_lif_dense), whose epilogue the plain T-folded kernel
-    alone has (variant 2, no split)."""
+               dense_pool: bool = False, band_xs=()):
+    """(variant, block_n, splits) configurations a layer admits; `band` / `band_xs` list the
+    block widths of variants 3 / 7 the layer qualifies for (band_block_ns,
+    band_xs_block_ns); dense_pool: the pooled dense form (snnb_conv3x3_lif_dense), whose
+    epilogue the plain T-folded kernel alone has (variant 2, no split)."""
     if dense_pool:
         return [c for c in candidates(cout, T, kslabs, max_splits)
                 if c[0] == 2 and c[2] == 1]
@@ -258,15 +310,16 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
             if cout % bn == 0 and sk <= max_splits and sk <= kslabs // 2:
                 out.append((6, bn, sk))
     out.extend((3, bn, 1) for bn in band)
+    out.extend((7, bn, 1) for bn in band_xs)
     return out
 
 
 def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=(),
-                 dense_pool: bool = False):
+                 dense_pool: bool = False, band_xs=()):
     """Time launch(variant, block_n, splits) for every configuration the layer admits
     (on its real operands, device time via time_graph) and return the fastest."""
     best, best_ms = (0, 0, 1), float("inf")
-    for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool):
+    for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool, band_xs=band_xs):
         # the lower of two timings: one replay can catch another context's work
         ms = min(time_graph(lambda: launch(*cfg), reps) for _ in range(2))
         if ms < best_ms:
@@ -281,6 +334,16 @@ def device_status(stream_tensor: torch.Tensor | None = None) -> int:
     v = ctypes.c_int(0)
     _lib.check(_lib.lib().snnb_read_device_status(s, ctypes.byref(v)), "snnb_read_device_status")
     return v.value
+
+
+def raise_on_device_status(what: str) -> None:
+    """Read (and clear) the device status word on the current stream -- a stream
+    synchronisation -- and raise SnnbError if a kernel reported a failure since the last
+    read (SNNB_ERR_TIMEOUT: a bounded wait gave up and the launch left its output
+    incomplete)."""
+    st = device_status()
+    if st != 0:
+        _lib.check(st, what + " (device status)")
 
 
 # ---- reference-API entries ----------------------------------------------------------------
@@ -396,6 +459,82 @@ def conv3x3_lif_dense(x: torch.Tensor, wd: torch.Tensor, bd: torch.Tensor, *,
     return out
 
 
+# ---- float32 operands on the bf16 tensor cores (csrc/split.cu) ----------------------------
+# A float32 value is carried as three bf16 terms (hi, mid, lo); activations are laid out as
+# six channel groups [hi, hi, hi, mid, mid, lo] against weights [hi, mid, lo, hi, mid, hi], so
+# one bf16 conv / GEMM over 6 * Cp channels sums the six larger products of the terms, each
+# exact in float32 (the dropped three are below 2^-23 of the product).  Cp = Cin rounded up
+# to a multiple of 4 (zero channels), so that 6 * Cp is a multiple of 8.
+SPLIT_ACT = ("hi", "hi", "hi", "mid", "mid", "lo")
+SPLIT_WGT = ("hi", "mid", "lo", "hi", "mid", "hi")
+
+
+def split_width(C: int) -> int:
+    return (C + 3) // 4 * 4
+
+
+def split_terms_host(t: torch.Tensor):
+    """float32 tensor -> (hi, mid, lo) bf16 tensors, hi + mid + lo == t to within 2^-24 |t|
+    (the same rounding as the device split: each residual is exact in float32)."""
+    t = t.detach().float()
+    h = t.to(torch.bfloat16)
+    over = torch.isinf(h.float()) & torch.isfinite(t)     # above bf16's largest finite value
+    if bool(over.any()):
+        big = torch.full_like(h, torch.finfo(torch.bfloat16).max)
+        h = torch.where(over, torch.where(t > 0, big, -big), h)
+    r1 = t - h.float()
+    m = r1.to(torch.bfloat16)
+    l = (r1 - m.float()).to(torch.bfloat16)
+    bad = ~torch.isfinite(h.float())
+    if bool(bad.any()):
+        m = m.masked_fill(bad, 0)
+        l = l.masked_fill(bad, 0)
+    return h, m, l
+
+
+def _split_groups(t_last: torch.Tensor, order) -> torch.Tensor:
+    """[..., C] float32 -> [..., 6 * Cp] bf16, group g = term order[g] of t (zero padded)."""
+    C = t_last.shape[-1]
+    Cp = split_width(C)
+    h, m, l = split_terms_host(t_last)
+    terms = {"hi": h, "mid": m, "lo": l}
+    out = torch.zeros(*t_last.shape[:-1], 6 * Cp, dtype=torch.bfloat16, device=t_last.device)
+    for g, name in enumerate(order):
+        out[..., g * Cp: g * Cp + C] = terms[name]
+    return out.contiguous()
+
+
+def split_weight_khwc(w: torch.Tensor) -> torch.Tensor:
+    """torch conv weight [Cout, Cin, 3, 3] (float32) -> [Cout, 3, 3, 6 * Cp] bf16 weight
+    groups for a float32-faithful conv3x3_lif on split_activations' output."""
+    return _split_groups(w.detach().float().permute(0, 2, 3, 1), SPLIT_WGT)
+
+
+def split_weight_rows(w: torch.Tensor) -> torch.Tensor:
+    """linear weight [N, K] (float32) -> [N, 6 * Kp] bf16 weight groups."""
+    return _split_groups(w.detach().float(), SPLIT_WGT)
+
+
+def split_activations(x: torch.Tensor) -> torch.Tensor:
+    """x [..., C] float32 (contiguous) -> [..., 6 * Cp] bf16 activation groups on the device
+    (snnb_split_bf16_terms)."""
+    assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+    C = x.shape[-1]
+    Cp = split_width(C)
+    rows = x.numel() // C if C else 0
+    out = torch.empty(*x.shape[:-1], 6 * Cp, device=x.device, dtype=torch.bfloat16)
+    st = _lib.lib().snnb_split_bf16_terms(_lib.ptr(x), rows, C, Cp, _lib.ptr(out),
+                                          _lib.stream_of(x))
+    _lib.check(st, "snnb_split_bf16_terms")
+    return out
+
+
+def _frames_f32(x_seq: torch.Tensor) -> torch.Tensor:
+    """[T, B, C, H, W] (NCHW or channels-last view) float32 / float16 -> contiguous
+    [T, B, H, W, C] float32 (float16 values are exact in float32)."""
+    return x_seq.permute(0, 1, 3, 4, 2).to(torch.float32).contiguous()
+
+
 def weight_khwc(w: torch.Tensor) -> torch.Tensor:
     """torch conv weight [Cout, Cin, 3, 3] -> the kernels' K-major [Cout, 3, 3, Cin] bf16."""
     return w.detach().permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)
@@ -419,10 +558,12 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
                 layout: str = "NCHW"):
     """conv + bias + neuron (reference fused.py:513-551) for x_seq [T, B, Cin, H, W].
-    3x3 / stride 1 / padding 1 convs with a scalar threshold run one fused launch: the
-    tcgen05 kernel when Cin % 8 == 0 and Cout % 32 == 0 (bf16 operands), the float32
-    CUDA-core kernel for a float32 input with Cin % 8 != 0 (the image layer).  Any other
-    geometry keeps the reference's two steps: torch's conv, then the fused neuron kernel."""
+    3x3 / stride 1 / padding 1 convs with a scalar threshold run fused on the tcgen05 kernel
+    when Cout % 32 == 0: bf16 operands for a bf16 input (Cin % 8 == 0); for a float32 /
+    float16 input (Cin % 4 == 0) float32-faithful, each operand as three bf16 terms (a
+    split-terms launch, then the conv over six channel groups); a float32 input with other
+    Cin (the image layer) takes the float32 CUDA-core kernel.  Any other geometry keeps the
+    reference's two steps: torch's conv in the input's dtype, then the fused neuron kernel."""
     from .fused import fused_bias_if_lif
     Cin, Cout = weight.shape[1], weight.shape[0]
     kw = dict(neuron=neuron, tau=tau, decay=decay, decay_input=decay_input,
@@ -432,8 +573,13 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
     if tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1) and \
             _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1 and \
             isinstance(v_threshold, (int, float)):
-        if Cin % 8 == 0 and Cout % 32 == 0:
+        if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0 and Cout % 32 == 0:
             y = conv3x3_lif(_to_frames(x_seq), weight_khwc(weight), b, **kw)
+            return _from_frames(y, x_seq.dtype, layout)
+        if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0 and Cout % 32 == 0:
+            # float32-faithful: three bf16 terms per operand, six products on the tensor cores
+            y = conv3x3_lif(split_activations(_frames_f32(x_seq)), split_weight_khwc(weight),
+                            b, **kw)
             return _from_frames(y, x_seq.dtype, layout)
         if x_seq.dtype == torch.float32 and Cout % 8 == 0:
             y = first_conv_lif(x_seq.contiguous(), weight.detach().float().contiguous(), b,
@@ -453,16 +599,22 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
 def linear_neuron(x_seq, weight, bias, *, neuron: str = "if", tau: float = 2.0, decay=None,
                   decay_input: bool = True, soft_reset: bool = False, v_threshold=1.0,
                   v_reset: float = 0.0):
-    """linear + bias + neuron (reference fused.py:554-579); one fused launch (bf16
-    operands, float32 accumulation); in_features % 8 == 0, out_features % 32 == 0."""
+    """linear + bias + neuron (reference fused.py:554-579); one fused tcgen05 launch with
+    float32 accumulation, out_features % 32 == 0: bf16 operands for a bf16 input
+    (in_features % 8 == 0); for a float32 / float16 input float32-faithful, each operand as
+    three bf16 terms (in_features % 4 == 0)."""
     T, B = x_seq.shape[:2]
-    x = x_seq.reshape(T, B, -1).to(torch.bfloat16).contiguous()
     N = weight.shape[0]
     b = bias.detach().float().contiguous() if bias is not None else \
-        torch.zeros(N, device=x.device)
-    y = linear_lif(x, weight.detach().to(torch.bfloat16).contiguous(), b, neuron=neuron,
-                   tau=tau, decay=decay, decay_input=decay_input, soft_reset=soft_reset,
-                   v_threshold=v_threshold, v_reset=v_reset)
+        torch.zeros(N, device=x_seq.device)
+    kw = dict(neuron=neuron, tau=tau, decay=decay, decay_input=decay_input,
+              soft_reset=soft_reset, v_threshold=v_threshold, v_reset=v_reset)
+    if x_seq.dtype == torch.bfloat16:
+        x = x_seq.reshape(T, B, -1).contiguous()
+        y = linear_lif(x, weight.detach().to(torch.bfloat16).contiguous(), b, **kw)
+    else:
+        x = split_activations(x_seq.reshape(T, B, -1).to(torch.float32).contiguous())
+        y = linear_lif(x, split_weight_rows(weight), b, **kw)
     return y.to(x_seq.dtype)
 
 

@@ -186,17 +186,61 @@ def plif(
     x_seq: torch.Tensor,
     w: torch.Tensor,
     *,
+    decay_input: bool = True,
     soft_reset: bool = False,
     v_threshold=1.0,
     v_reset: float = 0.0,
     layout: str = "NCHW",
-) -> torch.Tensor:
-    """Parametric LIF: k = sigmoid(w) (w a 1-element float32 CUDA tensor, read on the
-    device), v = (1-k) v + k x.  With w = 0 (init tau 2) it equals LIF tau=2."""
+    v_init: torch.Tensor | None = None,
+    packed: bool = False,
+    count: bool = False,
+    v_out: bool = False,
+):
+    """SpikingJelly ParametricLIFNode, multi-step (snnb_neuron_plif): k = w.sigmoid() on
+    w's device (as SpikingJelly evaluates it), then per step, in SpikingJelly's order,
+    v = v + (x - (v - v_reset)) * k (decay_input) or v * (1 - k) + x / v - (v - v_reset) * k
+    + x (not), fire at v >= v_threshold, hard or soft reset.  A hard-reset neuron starts at
+    v_reset (SpikingJelly's initial state), a soft one at 0, unless v_init is given.
+    Returns the spikes (x_seq's dtype and layout), or a dict with 'spikes' and the requested
+    'packed' / 'count' / 'v' when any of those is asked for."""
     assert x_seq.is_cuda
-    return neuron_multistep(x_seq, decay_factor=0.0, input_scale=0.0, plif_w=w.reshape(1),
-                            soft_reset=soft_reset, v_threshold=v_threshold,
-                            v_reset=v_reset)["spikes"]
+    assert x_seq.dtype in (torch.float32, torch.float16, torch.bfloat16)
+    assert isinstance(v_threshold, (int, float)), "PLIF takes a scalar threshold"
+    if not x_seq.is_contiguous():
+        assert layout == "NHWC", f"non-contiguous x_seq requires layout='NHWC', got {layout}"
+    T = x_seq.shape[0]
+    NCL = math.prod(x_seq.shape[1:])
+    k = torch.sigmoid(w.detach().reshape(1).to(device=x_seq.device, dtype=torch.float32))
+    hard = not soft_reset
+    if v_init is None and hard and float(v_reset) != 0.0:
+        v_init = torch.full((NCL,), float(v_reset), device=x_seq.device, dtype=torch.float32)
+    elif v_init is not None:
+        assert v_init.is_cuda and v_init.dtype == torch.float32 and v_init.numel() == NCL
+        v_init = v_init.contiguous()
+    sp = torch.empty_like(x_seq)
+    pk = torch.empty((T, (NCL + 31) // 32), device=x_seq.device, dtype=torch.int32) \
+        if packed else None
+    cnt = torch.empty(x_seq.shape[1:], device=x_seq.device, dtype=torch.float32) \
+        if count else None
+    vo = torch.empty(x_seq.shape[1:], device=x_seq.device, dtype=torch.float32) \
+        if v_out else None
+    # elementwise: the memory order of x (NCHW or channels-last storage) is kept as is
+    st = _lib.lib().snnb_neuron_plif(
+        _lib.ptr(x_seq), _lib.dtype_code(x_seq.dtype), T, NCL, _lib.ptr(k), int(decay_input),
+        int(hard), float(v_reset), float(v_threshold), _lib.ptr(v_init), _lib.ptr(sp),
+        _lib.dtype_code(sp.dtype), _lib.ptr(pk), _lib.ptr(cnt), _lib.ptr(vo),
+        _lib.stream_of(x_seq))
+    _lib.check(st, "snnb_neuron_plif")
+    if not (packed or count or v_out):
+        return sp
+    out = {"spikes": sp}
+    if packed:
+        out["packed"] = pk
+    if count:
+        out["count"] = cnt
+    if v_out:
+        out["v"] = vo
+    return out
 
 
 MODEL_CUBA = 0

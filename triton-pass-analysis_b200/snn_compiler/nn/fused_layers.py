@@ -8,13 +8,18 @@ Mirrors snn_compiler/nn/modules.py of the reference:
 x_seq is [T, B, C, H, W] (logical NCHW; channels-last storage when layout="NHWC") or
 [T, B, features]; the result has the same layout.
 
-Routing (every launch is libsnnb200.so):
-  - 3x3 / stride 1 / padding 1 convs on spike-like input (Cin % 8 == 0, Cout % 32 == 0):
+Routing (every launch is libsnnb200.so).  The reference convolves in the input's dtype, so
+the route depends on it:
+  - 3x3 / stride 1 / padding 1 convs with Cout % 32 == 0 on a bf16 input (Cin % 8 == 0):
     one launch of the fused tcgen05 conv + bias + neuron kernel (bf16 operands, float32
     accumulation -- the reference's bf16 mode);
-  - the same geometry on a float32 input with Cin % 8 != 0 (the image-input first layer):
-    the float32 CUDA-core conv + neuron kernel;
-  - linears with in_features % 8 == 0 and out_features % 32 == 0: the fused linear kernel;
+  - the same geometry on a float32 / float16 input (Cin % 4 == 0): float32-faithful on the
+    same kernel -- input and weights each carried as three bf16 terms (snnb_split_bf16_terms,
+    weights split once per module), six products per pair summed in float32;
+  - a float32 input with other Cin (the image-input first layer): the float32 CUDA-core
+    conv + neuron kernel;
+  - linears with out_features % 32 == 0 (in_features % 8 == 0 for bf16, % 4 == 0 for
+    float32 / float16, split as above): the fused linear kernel;
   - the residual form (FusedConvBNAddNeuron) on the first geometry: the same tcgen05 kernel
     with the residual added in its epilogue (snnb_conv3x3_lif_res);
   - fold_bn=False and any other conv geometry keep the reference's own two-step structure:
@@ -78,13 +83,22 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None):
     Cout = weight.shape[0]
     b = bias.detach().float().contiguous() if bias is not None else \
         torch.zeros(Cout, device=x_seq.device)
-    if Cin % 8 == 0 and Cout % 32 == 0:
+    res = None if residual is None else _res_frames(residual)
+    if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0 and Cout % 32 == 0:
         key = ("khwc", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
             cache["key"], cache["w"] = key, KC.weight_khwc(weight)
-        res = None if residual is None else _res_frames(residual)
         y = KC.conv3x3_lif(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
+        return KC._from_frames(y, x_seq.dtype, layout)
+    if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0 and Cout % 32 == 0:
+        # float32-faithful on the tensor cores: both operands as three bf16 terms
+        key = ("split", weight.data_ptr(), weight._version)
+        if cache.get("key") != key:
+            cache.clear()
+            cache["key"], cache["w"] = key, KC.split_weight_khwc(weight)
+        y = KC.conv3x3_lif(KC.split_activations(KC._frames_f32(x_seq)), cache["w"], b,
+                           residual=res, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
     if residual is not None:
         return None
@@ -159,7 +173,9 @@ class FusedLinearNeuron(nn.Module, _NeuronArgs):
 
     def forward(self, x_seq):
         K, N = self.weight.shape[1], self.weight.shape[0]
-        if K % 8 == 0 and N % 32 == 0 and isinstance(self.v_threshold, (int, float)):
+        kmod = 8 if x_seq.dtype == torch.bfloat16 else 4
+        if x_seq.dtype in (torch.bfloat16, torch.float32, torch.float16) and K % kmod == 0 \
+                and N % 32 == 0 and isinstance(self.v_threshold, (int, float)):
             return KC.linear_neuron(x_seq, self.weight, self.bias, **self._neuron_kw())
         T, B = x_seq.shape[:2]
         y = F.linear(x_seq.reshape(T * B, -1), self.weight.to(x_seq.dtype)).view(T, B, N)

@@ -4,8 +4,8 @@ Mirrors snn_compiler/nn/modules.py of the reference:
   IFNode :26-49, LIFNode :52-85, CubaLIFNode :88-121, EIFNode :124-154,
   FusedAddNeuron :446-481, RateCodedLIFNode :487-522, RateCodedIFNode :525-547,
   StatefulLIFNode :553-586
-plus PLIFNode (SpikingJelly ParametricLIFNode: learnable w, k = sigmoid(w),
-init_tau = 2 -> w = 0).  Every module takes x_seq [T, B, ...] and returns
+plus PLIFNode (SpikingJelly ParametricLIFNode, in SpikingJelly's arithmetic: learnable w,
+k = sigmoid(w), init_tau = 2 -> w = 0).  Every module takes x_seq [T, B, ...] and returns
 [T, B, ...] spikes of x_seq's dtype; state is not kept between calls.
 The conv / linear fused modules live in snn_compiler.nn.fused_layers.
 """
@@ -122,13 +122,18 @@ class EIFNode(nn.Module):
 
 
 class PLIFNode(nn.Module):
-    """Parametric LIF (SpikingJelly ParametricLIFNode): w is learnable, k = sigmoid(w),
-    v = (1-k) v + k x; init_tau = 2 gives w = 0 and k = 0.5."""
+    """Parametric LIF (SpikingJelly ParametricLIFNode, multi-step): learnable w with
+    init_tau = 1 + exp(-w) (w = -log(init_tau - 1)), k = w.sigmoid(), and SpikingJelly's
+    charge v = v + (x - (v - v_reset)) * k (decay_input; see kernels.neurons.plif for the
+    other form), fire at v >= v_threshold, hard reset to v_reset (the neuron starts there)
+    or soft reset (SpikingJelly's v_reset=None).  init_tau = 2 gives w = 0 and k = 0.5."""
 
-    def __init__(self, *, init_tau: float = 2.0, soft_reset: bool = False,
-                 v_threshold=1.0, v_reset: float = 0.0, layout: str = "NCHW"):
+    def __init__(self, *, init_tau: float = 2.0, decay_input: bool = True,
+                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                 layout: str = "NCHW"):
         super().__init__()
         self.w = nn.Parameter(torch.tensor([-math.log(init_tau - 1.0)], dtype=torch.float32))
+        self.decay_input = decay_input
         self.soft_reset = soft_reset
         self.v_reset = v_reset
         self.layout = layout
@@ -136,8 +141,8 @@ class PLIFNode(nn.Module):
 
     def forward(self, x_seq):
         return plif(x_seq if _dense(x_seq) else x_seq.contiguous(), self.w.detach(),
-                    soft_reset=self.soft_reset, v_threshold=self.v_threshold,
-                    v_reset=self.v_reset, layout=self.layout)
+                    decay_input=self.decay_input, soft_reset=self.soft_reset,
+                    v_threshold=self.v_threshold, v_reset=self.v_reset, layout=self.layout)
 
 
 class FusedAddNeuron(nn.Module):

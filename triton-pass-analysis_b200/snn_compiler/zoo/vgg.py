@@ -141,8 +141,7 @@ class SpikingVGG:
         for i, L in enumerate(self.layers):
             flops = 2 * T * B * h * w * L["cout"] * L["cin"] * 9
             if i == 0:
-                fn = (lambda L=L, o=bufs[0]: KC.first_conv_lif(img, L["w"], L["b"], T=T,
-                                                             pool=L["pool"], out=o, **self.lif))
+                fn = self._first_layer(img, L, bufs[0])
             elif h <= 2 and w <= 2 and self.dense_small and (not L["pool"] or h == w == 2):
                 # the whole image is every output pixel's window: a dense GEMM over the
                 # image's pixels x channels (no zero-padding taps), K1's linear form
@@ -165,7 +164,8 @@ class SpikingVGG:
                                                 workspace=self._ws(T, B, hh, ww, L["cout"],
                                                                    1 if v == 6 else sp),
                                                 **self.lif),
-                                 band=KC.band_block_ns(w, L["cin"], L["cout"]))
+                                 band=KC.band_block_ns(w, L["cin"], L["cout"]),
+                                 band_xs=KC.band_xs_block_ns(w, L["cin"], L["cout"]))
             steps.append((f"conv{i + 1}_{L['cin']}x{L['cout']}@{h}", flops, fn))
             x_prev = bufs[i]
             if L["pool"]:
@@ -189,6 +189,32 @@ class SpikingVGG:
                       (lambda f=f, x=hcur: head(x, f["w"], f["b"], out=out))))
         return steps, out
 
+    def _first_layer(self, img, L, o):
+        """Launcher of the image layer: the float32 CUDA-core kernel, or (direct encoding,
+        Cin <= 4, no pooling) the tensor-core kernel with split operands -- whichever the
+        autotuner times faster for this input shape."""
+        T = self.T
+        cuda_core = (lambda: KC.first_conv_lif(img, L["w"], L["b"], T=T, pool=L["pool"], out=o,
+                                               **self.lif))
+        if not (img.shape[0] == 1 and L["cin"] <= 4 and L["cout"] in (32, 64, 128)
+                and not L["pool"]):
+            return cuda_core
+        if "wsplit" not in L:
+            L["wsplit"] = KC.first_conv_split_weight(L["w"])
+        tensor_core = (lambda: KC.first_conv_lif_tc(img, L["wsplit"], L["b"], T=T, out=o,
+                                                    **self.lif))
+        key = ("first", 0) + tuple(img.shape)
+
+        def run():
+            if key not in self.choice:
+                if self.autotune:
+                    ms = [min(KC.time_graph(f) for _ in range(2)) for f in (cuda_core, tensor_core)]
+                    self.choice[key] = (1 if ms[1] < ms[0] else 0, 0, 1)
+                else:
+                    self.choice[key] = (1, 0, 1)
+            return (tensor_core if self.choice[key][0] == 1 else cuda_core)()
+        return run
+
     def _dense(self, i, h, w):
         """Dense-GEMM weights of conv layer i on h x w images (dense_conv_weight), cached."""
         key = (i, h, w)
@@ -208,13 +234,13 @@ class SpikingVGG:
             self._workspace = torch.empty(need // 4, device=self.device, dtype=torch.float32)
         return self._workspace
 
-    def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False):
+    def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False, band_xs=()):
         """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
         call times every (variant, block_n, splits) the layer admits and keeps the fastest."""
         def run():
             if key not in self.choice:
                 self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs, band=band,
-                                                   dense_pool=dense_pool) \
+                                                   dense_pool=dense_pool, band_xs=band_xs) \
                     if self.autotune else (0, 0, 1)
             return launch(*self.choice[key])
         return run
