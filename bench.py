@@ -397,7 +397,8 @@ class VggWorkload:
         name = self.layer_names[i]
         if i == 0:
             return f"first_conv_lif ({name})"
-        keys = [k for k in self.eng.choice if k[2] == self.B]
+        bs = self.eng.chain_batch(self.B)
+        keys = [k for k in self.eng.choice if k[0] != "first" and k[2] == bs]
         key = sorted(keys, key=lambda k: (k[0] != "conv", k[1]))[i - 1] if i - 1 < len(keys) else None
         if key is None:
             return f"linear_head_kernel ({name})"

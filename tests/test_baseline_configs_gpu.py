@@ -140,7 +140,7 @@ def test_vgg16_bench_network_at_batch64():
     eng.replay()
     torch.cuda.synchronize()
     logits = out.cpu()
-    bufs = eng._bufs[(B, 32, 32, False)][0]
+    bufs = eng.layer_outputs(B)
     ref, trace = OV.vgg16_forward(img.expand(T, B, 3, 32, 32).contiguous(), Po, collect=True)
     for i, buf in enumerate(bufs):
         gl = buf.float().cpu().permute(0, 1, 4, 2, 3)

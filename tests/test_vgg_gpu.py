@@ -78,3 +78,20 @@ def test_vgg16_graph_replay_equals_eager():
     eng.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+
+
+def test_vgg16_concurrent_chains_equal_one_chain():
+    """SpikingVGG(chains=2): the captured forward runs two sub-batch chains on concurrent
+    streams (separate buffers and workspaces); the logits equal the one-chain forward."""
+    from snn_compiler.zoo.vgg import SpikingVGG
+    P = OP.vgg16_params(1)
+    img = torch.rand(1, 32, 3, 32, 32, generator=OP.gen(4)).to(DEV)
+    one = SpikingVGG(P, T=4, device=DEV).forward(img, graph=True).clone()
+    eng2 = SpikingVGG(P, T=4, device=DEV, chains=2)
+    two = eng2.forward(img, graph=True)
+    torch.cuda.synchronize()
+    assert eng2.kernel_launches(32) >= 2 * 16
+    # each chain's kernels are tuned for its sub-batch (the schedules, hence the float32
+    # summation order, may differ): equal up to that
+    assert torch.allclose(one, two, rtol=1e-5, atol=1e-5)
+    assert torch.equal(one.argmax(-1), two.argmax(-1))

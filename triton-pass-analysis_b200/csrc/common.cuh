@@ -31,6 +31,20 @@ inline int launch_status() {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Debug build (-DSNNB_CHECK_BOUNDS, `make check` -> libsnnb200_check.so): index checks on the
+// kernels' global accesses that record SNNB_ERR_DEVICE in the device status word and skip the
+// access.  The release build compiles them to `true`.
+#ifdef SNNB_CHECK_BOUNDS
+__device__ __forceinline__ bool check_index(int64_t i, int64_t n, int* status) {
+    if (i >= 0 && i < n) return true;
+    if (status) atomicExch(status, SNNB_ERR_DEVICE);
+    return false;
+}
+#define SNNB_IN_BOUNDS(i, n, status) (::snnb::check_index((int64_t)(i), (int64_t)(n), (status)))
+#else
+#define SNNB_IN_BOUNDS(i, n, status) (true)
+#endif
+
 // Programmatic dependent launch.  Every kernel of this library is launched with programmatic
 // stream serialization allowed (launch_k), so its CTAs may be scheduled while the previous
 // kernel on the stream is still finishing.  Each kernel runs pdl_wait() before it touches

@@ -370,8 +370,10 @@ __device__ __forceinline__ Tile decode_band(int tile, const ConvParams& p, int B
 // lanes; a row's first (last) column takes no D_0 (D_2) term -- it would come from the
 // zero padding.  Stages are a third of the size, so the ring is three times deeper and the
 // operand copies' round trips hide behind the MMAs; TMEM holds 2 x 3 accumulators.
+constexpr int BAND_THREADS = 320;   // producer, MMA issuer, 2 x 4 epilogue warps
+
 template <int BN, bool HARD, bool XS>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(BAND_THREADS, 1)
 conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const ConvParams p) {
     using S = SmemBand<BN>;
@@ -415,7 +417,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         for (int a = 0; a < 2; ++a) {
             tc::mbar_init(accf_bar(a), 1);
-            tc::mbar_init(acce_bar(a), 128);
+            tc::mbar_init(acce_bar(a), 256);             // every thread of both epilogue sets
         }
         tc::mbar_init(wfull_bar, 1);
         tc::mbar_init(wempty_bar, 1);
@@ -511,11 +513,16 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        // The whole warp walks the schedule and waits; one elected lane issues.
+        // The whole warp walks the schedule; one elected lane waits and issues.  A wait that
+        // the issuing thread places behind a tcgen05.commit returns only once the tensor pipe
+        // has drained, so the waits for the next step -- its accumulator and its first stage
+        // -- are made before this step's commits (unless the next step belongs to another
+        // channel block, whose weights are loaded only after this block's last MMAs): with
+        // Cin = 64 a step is one stage of 36 MMAs, and a drain per step cost ~40% of them.
         constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
         const uint32_t row_step = (uint32_t)p.W * 128u;         // one image row of the band copy
         int stage = 0, cur_nb = -1;
-        uint32_t phase = 0, it = 0, wl = 0, failed = 0;
+        uint32_t phase = 0, it = 0, wl = 0, failed = 0, ready = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const int nb = tile / p.mtiles;
             if (nb != cur_nb) {
@@ -528,19 +535,21 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 ++wl;
                 cur_nb = nb;
             }
+            const int ntile = tile + (int)gridDim.x;
+            const bool next_same_block = ntile < p.num_tiles && ntile / p.mtiles == nb;
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
-                failed |= 1u - tc::mbar_wait_warp(acce_bar(a), ((it >> 1) & 1u) ^ 1u, failed);
-                tc::tc_fence_after();
+                const bool has_next = (t + 1 < p.T) || next_same_block;
                 const uint32_t dcol = tmem + a * ACC_COLS;
                 for (int cb = 0; cb < CB; ++cb) {
                     int nstage = stage + 1;
                     uint32_t nphase = phase;
                     if (nstage == nst) { nstage = 0; nphase ^= 1u; }
                     const uint32_t sb = sbase + a_off + (uint32_t)stage * st_bytes;
-                    // the issuing lane alone waits, for the next slab before committing this one
                     if (tc::elect_one()) {
-                        if (cb == 0) {
+                        if (cb == 0 && !ready) {
+                            failed |= 1u - tc::mbar_wait_lane(acce_bar(a), ((it >> 1) & 1u) ^ 1u,
+                                                              failed);
                             failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
                             tc::tc_fence_after();
                         }
@@ -563,15 +572,21 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                         if (cb + 1 < CB) {
                             failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
                             tc::tc_fence_after();
+                        } else if (has_next) {
+                            const uint32_t na = (it + 1) & 1u;
+                            failed |= 1u - tc::mbar_wait_lane(acce_bar((int)na),
+                                                              (((it + 1) >> 1) & 1u) ^ 1u, failed);
+                            failed |= 1u - tc::mbar_wait_lane(full_bar(nstage), nphase, failed);
+                            tc::tc_fence_after();
                         }
                         tc::umma_commit(empty_bar(stage));
+                        if (cb + 1 == CB) tc::umma_commit(accf_bar(a));
                     }
                     __syncwarp();
                     stage = nstage;
                     phase = nphase;
                 }
-                if (tc::elect_one()) tc::umma_commit(accf_bar(a));
-                __syncwarp();
+                ready = has_next ? 1u : 0u;
                 failed = __shfl_sync(0xffffffffu, failed, 0);
             }
         }
@@ -582,11 +597,15 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         if (failed && lane == 0) { atomicExch(p.status, SNNB_ERR_TIMEOUT); *abort_flag = 1; }
     } else {
         // ------------------------------------------------------------- epilogue
-        // Thread = TMEM lane = band pixel m (row y = m / W, column x = m % W).  The bias of
-        // the channel block stays in registers for the tile, v across t; shared memory is
-        // touched only to pool across warps (W >= 32), because while the tensor pipe streams
-        // operands every shared-memory / L1 round trip of the epilogue waits ~1000 cycles.
+        // Two sets of 4 warps (warps 2-5 and 6-9): thread = TMEM lane = band pixel m (row
+        // y = m / W, column x = m % W), set s taking the 32-channel slices c = s, s + 2, ...
+        // (one warp per SM sub-partition was too few: a step's neurons, loads and stores of
+        // a single warp outlasted the step's MMAs).  The bias of the slices stays in
+        // registers for the tile, v across t; shared memory is touched only to pool across
+        // warps (W >= 32).
         const int q = warp & 3;
+        const int set = (warp - 2) >> 2;
+        constexpr int NCS = (NCH + 1) / 2;                  // slices per set
         const int m = 32 * q + lane;
         const int W = p.W;
         const int x = m % W, y = m / W;
@@ -594,25 +613,33 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         uint32_t it = 0, failed = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_band(tile, p, BN);
-            float bias[BN];
-            const float4* bias4 = reinterpret_cast<const float4*>(p.bias + tl.n0);
+            float bias[32 * NCS];
 #pragma unroll
-            for (int j = 0; j < BN / 4; ++j) {
-                const float4 b4 = __ldg(bias4 + j);
-                bias[4 * j] = b4.x; bias[4 * j + 1] = b4.y; bias[4 * j + 2] = b4.z; bias[4 * j + 3] = b4.w;
+            for (int cs = 0; cs < NCS; ++cs) {
+                const int c = set + 2 * cs;
+                const float4* bias4 = reinterpret_cast<const float4*>(p.bias + tl.n0 + 32 * c);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 b4 = c < NCH ? __ldg(bias4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    bias[32 * cs + 4 * j] = b4.x; bias[32 * cs + 4 * j + 1] = b4.y;
+                    bias[32 * cs + 4 * j + 2] = b4.z; bias[32 * cs + 4 * j + 3] = b4.w;
+                }
             }
-            float v[BN];
+            float v[32 * NCS];
 #pragma unroll
-            for (int j = 0; j < BN; ++j) v[j] = 0.0f;
+            for (int j = 0; j < 32 * NCS; ++j) v[j] = 0.0f;
             const int hy = tl.h0 + y;                         // image row of this pixel
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
                 failed |= 1u - tc::mbar_wait_warp(accf_bar(a), (it >> 1) & 1u, failed);
                 tc::tc_fence_after();
                 const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * ACC_COLS;
-                uint32_t mk[NCH];
+                uint32_t mk[NCS];
 #pragma unroll
-                for (int c = 0; c < NCH; ++c) {
+                for (int cs = 0; cs < NCS; ++cs) {
+                    const int c = set + 2 * cs;
+                    mk[cs] = 0;
+                    if (c >= NCH) continue;
                     float r[32];
                     tc::tmem_ld32(tbase + (XS ? BN : 0) + c * 32, r);
                     tc::tmem_wait_ld();
@@ -638,65 +665,81 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t mask = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const float in = __fadd_rn(r[j], bias[c * 32 + j]);
-                        float vv = charge(v[c * 32 + j], p.df, p.sc, in);
+                        const float in = __fadd_rn(r[j], bias[32 * cs + j]);
+                        float vv = charge(v[32 * cs + j], p.df, p.sc, in);
                         const bool s = vv >= p.thr;
                         vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                        v[c * 32 + j] = vv;
+                        v[32 * cs + j] = vv;
                         mask |= (s ? 1u : 0u) << j;
                     }
-                    mk[c] = mask;
+                    mk[cs] = mask;
                 }
                 tc::tc_fence_before();
                 tc::mbar_arrive(acce_bar(a));
+                if (set >= NCH) continue;                     // no slice for this set (BN 32)
                 const int64_t frame = (int64_t)t * p.B + tl.img0;
                 if (!p.pool) {
                     // the lanes of pixels x and x ^ 1 (same row: W is even) store both pixels,
-                    // chunk 2i by the even lane and 2i + 1 by the odd one, so that every
-                    // 16-byte store instruction fills whole 32-byte sectors
-                    uint32_t ok[NCH];
+                    // 16-byte chunk 2i of a slice by the even lane and 2i + 1 by the odd one,
+                    // so that every store instruction fills whole 32-byte sectors
+                    uint32_t ok[NCS];
 #pragma unroll
-                    for (int c = 0; c < NCH; ++c) ok[c] = __shfl_xor_sync(0xffffffffu, mk[c], 1);
+                    for (int cs = 0; cs < NCS; ++cs) ok[cs] = __shfl_xor_sync(0xffffffffu, mk[cs], 1);
                     if (hy < p.H) {
                         const int par = x & 1;
 #pragma unroll
                         for (int pi = 0; pi < 2; ++pi) {
-                            uint4* dst = reinterpret_cast<uint4*>(
-                                p.out + ((frame * Ho + hy) * Wo + ((x & ~1) | pi)) * p.Cout + tl.n0);
+                            const int64_t e0 = ((frame * Ho + hy) * Wo + ((x & ~1) | pi)) * p.Cout + tl.n0;
+                            uint4* dst = reinterpret_cast<uint4*>(p.out + e0);
 #pragma unroll
-                            for (int i = 0; i < NCH * 2; ++i) {
-                                const int j = 2 * i + par;          // 16-byte chunk of the pixel
-                                const uint32_t mm = pi == par ? mk[j >> 2] : ok[j >> 2];
-                                dst[j] = spikes_to_bf16x8((mm >> (8 * (j & 3))) & 0xffu);
+                            for (int cs = 0; cs < NCS; ++cs) {
+                                const int c = set + 2 * cs;
+                                if (c >= NCH) continue;
+                                if (!SNNB_IN_BOUNDS(e0 + 32 * c + 31, out_elems(p), p.status)) continue;
+                                const uint32_t mm = pi == par ? mk[cs] : ok[cs];
+#pragma unroll
+                                for (int i = 0; i < 2; ++i) {
+                                    const int j = 2 * i + par;      // 16-byte chunk of the slice
+                                    dst[4 * c + j] = spikes_to_bf16x8((mm >> (8 * j)) & 0xffu);
+                                }
                             }
                         }
                     }
                 } else {
                     // 2x2 max-pool = OR: column pairs are adjacent lanes; row pairs are lanes
-                    // W apart (W < 32) or the same lane of another warp (W >= 32)
+                    // W apart (W < 32) or the same lane of another warp of the set (W >= 32)
 #pragma unroll
-                    for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], 1);
+                    for (int cs = 0; cs < NCS; ++cs) mk[cs] |= __shfl_xor_sync(0xffffffffu, mk[cs], 1);
                     if (W < 32) {
 #pragma unroll
-                        for (int c = 0; c < NCH; ++c) mk[c] |= __shfl_xor_sync(0xffffffffu, mk[c], W);
+                        for (int cs = 0; cs < NCS; ++cs)
+                            mk[cs] |= __shfl_xor_sync(0xffffffffu, mk[cs], W);
                     } else {
                         uint32_t* sm = smask + (it & 1) * (NCH * 128);
 #pragma unroll
-                        for (int c = 0; c < NCH; ++c) sm[c * 128 + m] = mk[c];
-                        tc::named_bar_sync(1, 128);
+                        for (int cs = 0; cs < NCS; ++cs)
+                            if (set + 2 * cs < NCH) sm[(set + 2 * cs) * 128 + m] = mk[cs];
+                        tc::named_bar_sync(1 + set, 128);
 #pragma unroll
-                        for (int c = 0; c < NCH; ++c) mk[c] |= sm[c * 128 + (m ^ W)];
+                        for (int cs = 0; cs < NCS; ++cs)
+                            if (set + 2 * cs < NCH) mk[cs] |= sm[(set + 2 * cs) * 128 + (m ^ W)];
                     }
                     if ((y & 1) == 0 && hy < p.H) {
                         // both column lanes of the window hold its OR: the even one stores
                         // chunks 2i and the odd one 2i + 1 (whole 32-byte sectors per store)
-                        uint4* dst = reinterpret_cast<uint4*>(
-                            p.out + ((frame * Ho + hy / 2) * Wo + x / 2) * p.Cout + tl.n0);
+                        const int64_t e0 = ((frame * Ho + hy / 2) * Wo + x / 2) * p.Cout + tl.n0;
+                        uint4* dst = reinterpret_cast<uint4*>(p.out + e0);
                         const int par = x & 1;
 #pragma unroll
-                        for (int i = 0; i < NCH * 2; ++i) {
-                            const int j = 2 * i + par;
-                            dst[j] = spikes_to_bf16x8((mk[j >> 2] >> (8 * (j & 3))) & 0xffu);
+                        for (int cs = 0; cs < NCS; ++cs) {
+                            const int c = set + 2 * cs;
+                            if (c >= NCH) continue;
+                            if (!SNNB_IN_BOUNDS(e0 + 32 * c + 31, out_elems(p), p.status)) continue;
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                const int j = 2 * i + par;
+                                dst[4 * c + j] = spikes_to_bf16x8((mk[cs] >> (8 * j)) & 0xffu);
+                            }
                         }
                     }
                 }
@@ -1169,16 +1212,16 @@ int run_band_layer(const void* x, int T, int B, int H, int W, int Cin, const voi
                              : SmemBand<32>::dyn_bytes(w_bytes, ring, a_bytes, copies);
     if (xs) {
         if (BN == 64)
-            return hard ? launch_persistent(conv_lif_band_kernel<64, true, true>, dyn, ta, tb, p, s)
-                        : launch_persistent(conv_lif_band_kernel<64, false, true>, dyn, ta, tb, p, s);
-        return hard ? launch_persistent(conv_lif_band_kernel<32, true, true>, dyn, ta, tb, p, s)
-                    : launch_persistent(conv_lif_band_kernel<32, false, true>, dyn, ta, tb, p, s);
+            return hard ? launch_persistent(conv_lif_band_kernel<64, true, true>, dyn, ta, tb, p, s, BAND_THREADS)
+                        : launch_persistent(conv_lif_band_kernel<64, false, true>, dyn, ta, tb, p, s, BAND_THREADS);
+        return hard ? launch_persistent(conv_lif_band_kernel<32, true, true>, dyn, ta, tb, p, s, BAND_THREADS)
+                    : launch_persistent(conv_lif_band_kernel<32, false, true>, dyn, ta, tb, p, s, BAND_THREADS);
     }
     if (BN == 64)
-        return hard ? launch_persistent(conv_lif_band_kernel<64, true, false>, dyn, ta, tb, p, s)
-                    : launch_persistent(conv_lif_band_kernel<64, false, false>, dyn, ta, tb, p, s);
-    return hard ? launch_persistent(conv_lif_band_kernel<32, true, false>, dyn, ta, tb, p, s)
-                : launch_persistent(conv_lif_band_kernel<32, false, false>, dyn, ta, tb, p, s);
+        return hard ? launch_persistent(conv_lif_band_kernel<64, true, false>, dyn, ta, tb, p, s, BAND_THREADS)
+                    : launch_persistent(conv_lif_band_kernel<64, false, false>, dyn, ta, tb, p, s, BAND_THREADS);
+    return hard ? launch_persistent(conv_lif_band_kernel<32, true, false>, dyn, ta, tb, p, s, BAND_THREADS)
+                : launch_persistent(conv_lif_band_kernel<32, false, false>, dyn, ta, tb, p, s, BAND_THREADS);
 }
 
 // Bytes of the split-K partial sums, splits * T * B * H * W * Cout float32 values, or -1

@@ -104,6 +104,13 @@ __device__ __forceinline__ void prefetch_weights_l2(const ConvParams& p) {
 }
 
 
+// bf16 elements of the spike output [T, B, Ho, Wo, Cout] (pool 0 / 1) -- the debug build's
+// bound for the epilogue stores.
+__device__ __forceinline__ int64_t out_elems(const ConvParams& p) {
+    const int64_t hw = p.pool == 1 ? (int64_t)(p.H / 2) * (p.W / 2) : (int64_t)p.H * p.W;
+    return (int64_t)p.T * p.B * hw * p.Cout;
+}
+
 __device__ __forceinline__ Tile decode_tile(int tile, const ConvParams& p, int BN) {
     const int nt = tile % p.n_tiles_n;
     const int mt = tile / p.n_tiles_n;
@@ -826,10 +833,12 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 } else if (!p.pool) {
                     if (inside) {
 #pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
-                                                             p.Cout + ch,
-                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                        for (int t = 0; t < TS; ++t) {
+                            const int64_t e = ((((int64_t)t * p.B + on) * p.H + oh) * p.W + ow) *
+                                                  p.Cout + ch;
+                            if (SNNB_IN_BOUNDS(e + NPT - 1, out_elems(p), p.status))
+                                store_bits_bf16<NPT>(p.out + e, (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                        }
                     }
                 } else {
                     // 2x2 max-pool = OR: the column neighbour is TS lanes away; the row
@@ -842,10 +851,12 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         store_packed(pool_store, oh >> 1, ow >> 1, Ho, Wo);
                     } else if (pool_store) {
 #pragma unroll
-                        for (int t = 0; t < TS; ++t)
-                            store_bits_bf16<NPT>(p.out + ((((int64_t)t * p.B + on) * Ho + (oh >> 1)) * Wo +
-                                                          (ow >> 1)) * p.Cout + ch,
-                                                 (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                        for (int t = 0; t < TS; ++t) {
+                            const int64_t e = ((((int64_t)t * p.B + on) * Ho + (oh >> 1)) * Wo +
+                                               (ow >> 1)) * p.Cout + ch;
+                            if (SNNB_IN_BOUNDS(e + NPT - 1, out_elems(p), p.status))
+                                store_bits_bf16<NPT>(p.out + e, (lb >> (t * NPT)) & ((1u << NPT) - 1u));
+                        }
                     }
                     tc::named_bar_sync(1 + set, 128);    // smask free for the next slice
                 }

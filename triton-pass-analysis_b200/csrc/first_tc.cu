@@ -20,8 +20,9 @@
 //      swizzled K-major layout the MMA descriptor reads (one 1024-byte atom per 8 rows);
 //   2. one thread issues KP / 16 MMAs (M = 128, N = Cout, K = 16) and commits to an
 //      mbarrier;
-//   3. thread = TMEM lane = pixel: per 32-channel slice, bias + T steps of the neuron, each
-//      step's 32 spikes stored as bf16 (64 bytes).
+//   3. thread = TMEM lane = pixel: per 32-channel slice, bias + T steps of the neuron; each
+//      step's 32 spikes leave as bf16 (64 bytes per pixel), a pixel pair's lanes splitting
+//      the stores so that each instruction writes whole 32-byte sectors.
 // Several CTAs share an SM (about 72 KB of shared memory each), so one CTA's MMA and
 // stores overlap another's A build.
 #include "tc_common.cuh"
@@ -29,7 +30,7 @@
 namespace snnb {
 namespace {
 
-constexpr int FT_THREADS = 128;
+constexpr int FT_THREADS = 256;     // warps 0-3 build A, 4-7 copy the weights; all 8 run the epilogue
 
 template <int CIN, int KP, int COUT>
 struct FirstTcSmem {
@@ -78,20 +79,22 @@ first_conv_tc_kernel(const float* __restrict__ x, int T, int B, int H, int W,
         tc::tmem_alloc(sbase + S::TMEM_OFF, S::TMEM_COLS);
         tc::tmem_relinquish();
     }
-    // weights: [COUT][KP] bf16 rows -> swizzled B slabs (no kernel writes them: before the
-    // dependency wait)
-    constexpr int BCH = COUT * (KP / 8);                  // 16-byte chunks
-    for (int i = tid; i < BCH; i += FT_THREADS) {
-        const int r = i / (KP / 8), c = i - r * (KP / 8);
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(wsplit) + i);
-        *reinterpret_cast<uint4*>(smem + S::B_OFF + sw128_chunk(r, c, S::B_SLAB)) = v;
+    const int64_t npix = (int64_t)B * H * W;
+    if (tid >= 128) {
+        // weights: [COUT][KP] bf16 rows -> swizzled B slabs (no kernel writes them: before
+        // the dependency wait)
+        constexpr int BCH = COUT * (KP / 8);              // 16-byte chunks
+        for (int i = tid - 128; i < BCH; i += 128) {
+            const int r = i / (KP / 8), c = i - r * (KP / 8);
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(wsplit) + i);
+            *reinterpret_cast<uint4*>(smem + S::B_OFF + sw128_chunk(r, c, S::B_SLAB)) = v;
+        }
     }
     pdl_wait();                                           // the image is the stream's input
     pdl_trigger();
-
+    if (tid < 128) {
     // A tile: this thread's pixel, its 3x3 window over CIN channels in torch order
     // (ci, ky, kx), each value split into three bf16 terms
-    const int64_t npix = (int64_t)B * H * W;
     const int64_t pix = (int64_t)blockIdx.x * 128 + tid;
     const bool inside = pix < npix;
     uint16_t th[K0], tm[K0], tl[K0];
@@ -136,6 +139,7 @@ first_conv_tc_kernel(const float* __restrict__ x, int T, int B, int H, int W,
         v.w = elem(8 * c + 6) | (elem(8 * c + 7) << 16);
         *reinterpret_cast<uint4*>(smem + S::A_OFF + sw128_chunk(tid, c, S::A_SLAB)) = v;
     }
+    }
     tc::fence_proxy_async_smem();                          // generic writes -> tensor core
     tc::tc_fence_before();
     __syncthreads();
@@ -161,34 +165,66 @@ first_conv_tc_kernel(const float* __restrict__ x, int T, int B, int H, int W,
     if (!ok) {
         if (lane == 0) atomicExch(status, SNNB_ERR_TIMEOUT);
     } else {
-        // epilogue: TMEM lane = pixel row of this warp's quadrant
-        const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
+        // epilogue: TMEM lane = pixel row of the warp's quadrant (warp & 3); the two warp sets
+        // (warp >> 2) take alternate 32-channel slices
+        const int q = warp & 3;
+        const int64_t pix = (int64_t)blockIdx.x * 128 + 32 * q + lane;
+        const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
         const int64_t step_stride = npix * COUT;
 #pragma unroll 1
-        for (int c = 0; c < COUT / 32; ++c) {
+        for (int c = warp >> 2; c < COUT / 32; c += 2) {
             float r[32];
             tc::tmem_ld32(tbase + c * 32, r);
+            float bb[32];
+            const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 f = __ldg(b4 + j);
+                bb[4 * j] = f.x; bb[4 * j + 1] = f.y; bb[4 * j + 2] = f.z; bb[4 * j + 3] = f.w;
+            }
             tc::tmem_wait_ld();
-            float in[32], v[32];
+            // direct encoding: the input current, and its scaled form, is the same at every
+            // step (sc * in rounded once, as the charge rounds it every step)
+            float sin_[32], v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                in[j] = __fadd_rn(r[j], __ldg(bias + c * 32 + j));
+                sin_[j] = __fmul_rn(sc, __fadd_rn(r[j], bb[j]));
                 v[j] = 0.0f;
             }
-            __nv_bfloat16* dst = out + pix * COUT + c * 32;
+            // the lanes of pixels 2i and 2i + 1 store both pixels' 64 bytes: the even lane the
+            // 16-byte chunks 0 and 2, the odd one 1 and 3, so that every store instruction
+            // fills whole 32-byte sectors (a lane storing its own pixel alone wrote half
+            // sectors)
+            const int par = lane & 1;
+            const int64_t pbase = pix & ~(int64_t)1;
+            const bool pair_in = pbase < npix;
+            __nv_bfloat16* dst = out + pbase * COUT + c * 32;
             for (int t = 0; t < T; ++t) {
                 uint32_t mask = 0;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    float vv = charge(v[j], df, sc, in[j]);
+                    float vv = __fadd_rn(__fmul_rn(df, v[j]), sin_[j]);   // charge()
                     const bool s = vv >= thr;
                     v[j] = reset_v<HARD>(vv, s, thr, v_reset);
                     mask |= (s ? 1u : 0u) << j;
                 }
-                if (inside) {
-                    uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)t * step_stride);
+                const uint32_t other = __shfl_xor_sync(0xffffffffu, mask, 1);
+                if (pair_in) {
+                    __nv_bfloat16* d0 = dst + (int64_t)t * step_stride;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) d[q] = spikes_to_bf16x8((mask >> (8 * q)) & 0xffu);
+                    for (int pi = 0; pi < 2; ++pi) {
+                        if (pbase + pi >= npix) continue;
+                        if (!SNNB_IN_BOUNDS((int64_t)t * step_stride + (pbase + pi) * COUT + c * 32 + 31,
+                                            (int64_t)T * step_stride, status))
+                            continue;
+                        const uint32_t mm = pi == par ? mask : other;
+                        uint4* d = reinterpret_cast<uint4*>(d0 + pi * COUT);
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const int q = 2 * i + par;
+                            d[q] = spikes_to_bf16x8((mm >> (8 * q)) & 0xffu);
+                        }
+                    }
                 }
             }
         }

@@ -16,6 +16,9 @@
 #include "common.cuh"
 
 namespace snnb {
+
+int* device_status_ptr();
+
 namespace {
 
 struct NeuronParams {
@@ -34,6 +37,7 @@ struct NeuronParams {
     float df, sc, v_reset, thr_scalar;
     int hard, thr_mode, channel_last;
     int charge_mode;
+    int* status;               // debug build: where a failed index check is recorded
 };
 
 __device__ __forceinline__ int64_t channel_of(int64_t n, const NeuronParams& p) {
@@ -177,7 +181,8 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
         float rr[TU][VEC];
 #pragma unroll
         for (int u = 0; u < TU; ++u) {
-            const bool ok = active && (t0 + u < p.T);
+            const bool ok = active && (t0 + u < p.T) &&
+                            SNNB_IN_BOUNDS((t0 + u) * p.N + n0 + VEC - 1, p.T * p.N, p.status);
             if (ok) {
                 load8(x + (t0 + u) * p.N + n0, xr[u]);
             } else {
@@ -213,16 +218,19 @@ __global__ void __launch_bounds__(THREADS) neuron_vec8_kernel(NeuronParams p) {
                 bits |= (s ? 1u : 0u) << k;
             }
             if (!active) bits = 0;
-            if (sp && active) store8(sp + t * p.N + n0, bits);
+            if (sp && active && SNNB_IN_BOUNDS(t * p.N + n0 + VEC - 1, p.T * p.N, p.status))
+                store8(sp + t * p.N + n0, bits);
             if (p.packed) {
                 uint32_t w = bits << (8 * (lane & 3));
                 w |= __shfl_xor_sync(0xffffffffu, w, 1);
                 w |= __shfl_xor_sync(0xffffffffu, w, 2);
-                if ((lane & 3) == 0 && active) __stcs(p.packed + t * p.words + (n0 >> 5), w);
+                if ((lane & 3) == 0 && active &&
+                    SNNB_IN_BOUNDS(t * p.words + (n0 >> 5), p.T * p.words, p.status))
+                    __stcs(p.packed + t * p.words + (n0 >> 5), w);
             }
         }
     }
-    if (active) {
+    if (active && SNNB_IN_BOUNDS(n0 + VEC - 1, p.N, p.status)) {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
             if (p.count) p.count[n0 + k] = cnt[k];
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) 
     TS* sp = static_cast<TS*>(p.spikes);
     for (int64_t t = 0; t < p.T; ++t) {
         bool s = false;
-        if (active) {
+        if (active && SNNB_IN_BOUNDS(t * p.N + n, p.T * p.N, p.status)) {
             float in = to_f32(x[t * p.N + n]);
             if (p.bias) in = __fadd_rn(in, bb);
             if (res) in = __fadd_rn(in, to_f32(res[t * p.N + n]));
@@ -270,7 +278,9 @@ __global__ void __launch_bounds__(THREADS) neuron_scalar_kernel(NeuronParams p) 
         }
         if (p.packed) {
             const uint32_t w = __ballot_sync(0xffffffffu, s);
-            if (lane == 0 && active) p.packed[t * p.words + (n >> 5)] = w;
+            if (lane == 0 && active &&
+                SNNB_IN_BOUNDS(t * p.words + (n >> 5), p.T * p.words, p.status))
+                p.packed[t * p.words + (n >> 5)] = w;
         }
     }
     if (active) {
@@ -488,6 +498,9 @@ extern "C" int snnb_neuron_multistep(
     p.T = T; p.N = N; p.C = C > 0 ? C : 1; p.HW = HW > 0 ? HW : 1; p.words = (N + 31) / 32;
     p.df = decay; p.sc = input_scale; p.v_reset = v_reset; p.thr_scalar = thr_scalar;
     p.hard = hard_reset ? 1 : 0; p.thr_mode = thr_mode; p.channel_last = channel_last ? 1 : 0;
+#ifdef SNNB_CHECK_BOUNDS
+    p.status = device_status_ptr();
+#endif
 
     const bool vec = (N % VEC == 0) && aligned16(x) && (!residual || aligned16(residual)) &&
                      (!spikes || aligned16(spikes));
@@ -523,6 +536,9 @@ extern "C" int snnb_neuron_plif(
     p.v_reset = vr; p.thr_scalar = v_threshold;
     p.hard = hard_reset ? 1 : 0; p.thr_mode = SNNB_THR_SCALAR;
     p.charge_mode = decay_input ? 1 : (vr == 0.0f ? 2 : 3);
+#ifdef SNNB_CHECK_BOUNDS
+    p.status = device_status_ptr();
+#endif
     const bool vec = (N % VEC == 0) && aligned16(x) && (!spikes || aligned16(spikes));
     const int sd = spikes ? spikes_dtype : SNNB_U8;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -10,7 +10,9 @@ import ctypes
 import os
 
 _PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(_PKG_DIR, "libsnnb200.so")
+# SNNB_LIBRARY selects another build of the same ABI, e.g. the bounds-checking debug build
+# libsnnb200_check.so (`make -C triton-pass-analysis_b200 check`).
+LIB_PATH = os.environ.get("SNNB_LIBRARY") or os.path.join(_PKG_DIR, "libsnnb200.so")
 
 SNNB_OK = 0
 STATUS = {-1: "invalid argument", -2: "unsupported combination", -3: "CUDA error",
@@ -72,7 +74,7 @@ def lib():
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise ImportError(f"libsnnb200.so not built (expected at {LIB_PATH}); "
+            raise ImportError(f"libsnnb200 not built (expected at {LIB_PATH}); "
                               "run `make -C triton-pass-analysis_b200`")
         L = ctypes.CDLL(LIB_PATH)
         L.snnb_abi_version.restype = ctypes.c_int

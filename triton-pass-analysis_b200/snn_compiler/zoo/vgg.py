@@ -72,8 +72,14 @@ class SpikingVGG:
     def __init__(self, P, *, T: int = 4, tau: float = 2.0, decay_input: bool = True,
                  v_threshold: float = 1.0, v_reset: float = 0.0, soft_reset: bool = False,
                  neuron: str = "lif", device="cuda", autotune: bool = True,
-                 dense_small: bool = True, check_status: bool = False):
+                 dense_small: bool = True, check_status: bool = False, chains: int = 1):
         self.T = T
+        # chains > 1: captured forwards run the batch as `chains` sub-batches on concurrent
+        # streams, so that one chain's layer tails and launch gaps overlap the other's layers.
+        # At VGG16 B = 64 per GPU two chains of 32 measured 0.3125 ms per step against 0.2688
+        # for one chain of 64 (each B = 32 kernel is too much less efficient), so the
+        # default is one chain.
+        self.chains = max(1, int(chains))
         self.autotune = autotune
         # unpooled 3x3 layers on images of at most 2x2 pixels run as dense GEMMs
         self.dense_small = dense_small
@@ -99,21 +105,23 @@ class SpikingVGG:
                      "b": f["b"].float().contiguous().to(dev)} for f in P["fcs"]]
         self.num_classes = P["fcs"][-1]["w"].shape[0]
         self._bufs = {}
-        self._workspace = None
+        self._workspace = {}          # chain -> split-K workspace
         self.graphs = None
         self._graph_cache = {}
         self._fwd_pool = None
+        self._side_streams = []
         self.check_status = bool(check_status)
 
     # ---- per-layer launch plan -----------------------------------------------------------
     def plan(self, img: torch.Tensor, *, per_step_logits: bool = False,
-             out: torch.Tensor | None = None):
+             out: torch.Tensor | None = None, chain: int = 0):
         """List of (name, flops, callable) for one forward over img [Ti, B, 3, H, W] f32.
-        Buffers are allocated once per (B, H, W) and reused; ``out`` (optional) receives the
-        logits instead of the engine's own buffer."""
+        Buffers are allocated once per (B, H, W, chain) and reused; ``out`` (optional)
+        receives the logits instead of the engine's own buffer.  Plans of different chains
+        share no buffer or workspace, so they may run concurrently."""
         Ti, B, Cin, H, W = img.shape
         T = self.T
-        key = (B, H, W, per_step_logits)
+        key = (B, H, W, per_step_logits) if chain == 0 else (B, H, W, per_step_logits, chain)
         if key not in self._bufs:
             bufs = []
             h, w = H, W
@@ -153,7 +161,8 @@ class SpikingVGG:
                                  KC.conv3x3_lif_dense(x, wd, bd, pool=L["pool"], out=o,
                                                       variant=v, block_n=bn, splits=sp,
                                                       workspace=self._ws(T, B, 1, 1, NN,
-                                                                         1 if v == 6 else sp),
+                                                                         1 if v == 6 else sp,
+                                                                         chain),
                                                       **self.lif),
                                  dense_pool=L["pool"])
             else:
@@ -162,7 +171,7 @@ class SpikingVGG:
                                  KC.conv3x3_lif(x, L["w"], L["b"], pool=L["pool"], out=o,
                                                 variant=v, block_n=bn, splits=sp,
                                                 workspace=self._ws(T, B, hh, ww, L["cout"],
-                                                                   1 if v == 6 else sp),
+                                                                   1 if v == 6 else sp, chain),
                                                 **self.lif),
                                  band=KC.band_block_ns(w, L["cin"], L["cout"]),
                                  band_xs=KC.band_xs_block_ns(w, L["cin"], L["cout"]))
@@ -179,7 +188,8 @@ class SpikingVGG:
                                       KC.linear_lif(x, f["w"], f["b"], out=o, variant=v,
                                                     block_n=bn, splits=sp,
                                                     workspace=self._ws(T, B, 1, 1, NN,
-                                                                      1 if v == 6 else sp),
+                                                                      1 if v == 6 else sp,
+                                                                      chain),
                                                     **self.lif))))
             hcur = fbufs[j]
         f = self.fcs[-1]
@@ -224,15 +234,17 @@ class SpikingVGG:
                                   KC.dense_conv_bias(L["b"], h, w, pool=L["pool"]))
         return self._dense_w[key]
 
-    def _ws(self, T, B, H, W, Cout, splits):
-        """Split-K workspace, one buffer shared by every layer of the engine (layers run one
+    def _ws(self, T, B, H, W, Cout, splits, chain=0):
+        """Split-K workspace, one buffer per chain shared by the chain's layers (they run one
         after another on one stream), grown to the largest request."""
         need = KC.split_workspace_bytes(T, B, H, W, Cout, splits)
         if need == 0:
             return None
-        if self._workspace is None or self._workspace.numel() * 4 < need:
-            self._workspace = torch.empty(need // 4, device=self.device, dtype=torch.float32)
-        return self._workspace
+        ws = self._workspace.get(chain)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.empty(need // 4, device=self.device, dtype=torch.float32)
+            self._workspace[chain] = ws
+        return ws
 
     def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False, band_xs=()):
         """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
@@ -246,12 +258,81 @@ class SpikingVGG:
         return run
 
     def kernel_launches(self, B: int) -> int:
-        """Kernel launches of one forward at batch B after its layers were tuned: one per
-        layer, plus the split-K finish (sum + bias + neuron) of every two-launch split-K
-        layer (the cluster split-K form, variant 6, finishes in its own launch)."""
+        """Kernel launches of one captured forward at batch B after its layers were tuned: per
+        chain one per layer, plus the split-K finish (sum + bias + neuron) of every two-launch
+        split-K layer (the cluster split-K form, variant 6, finishes in its own launch)."""
+        nc = self._chain_count(B, 1)
+        bs = B // nc
         n = len(self.layers) + len(self.fcs)
-        return n + sum(1 for k, c in self.choice.items()
-                       if k[2] == B and c[2] > 1 and c[0] != 6)
+        return nc * (n + sum(1 for k, c in self.choice.items()
+                             if k[0] != "first" and k[2] == bs and c[2] > 1 and c[0] != 6))
+
+    # ---- concurrent chains ------------------------------------------------------------------
+    def _chain_count(self, B: int, Ti: int = 1, per_step_logits: bool = False) -> int:
+        """Chains a captured forward of batch B uses: self.chains when B splits evenly into
+        sub-batches of at least 8 images (direct encoding, T-averaged logits), else 1."""
+        n = self.chains
+        if n <= 1 or per_step_logits or Ti != 1 or B % n or B // n < 8:
+            return 1
+        return n
+
+    def chain_batch(self, B: int) -> int:
+        """Sub-batch of each chain of a captured forward of batch B (its tuned kernels)."""
+        return B // self._chain_count(B, 1)
+
+    def _chain_plans(self, img, out=None, per_step_logits=False):
+        """[(steps, img part, out part)] per chain: chain c takes samples [c*b, (c+1)*b) of
+        img [1, B, ...] and writes their logits to rows [c*b, (c+1)*b) of out [B, classes]."""
+        B = img.shape[1]
+        nc = self._chain_count(B, img.shape[0], per_step_logits)
+        if nc == 1:
+            steps, o = self.plan(img, per_step_logits=per_step_logits, out=out)
+            return [(steps, img, o)], o
+        if out is None:
+            key = ("chain_out", B)
+            if key not in self._bufs:
+                self._bufs[key] = torch.empty(B, self.num_classes, device=self.device,
+                                              dtype=torch.float32)
+            out = self._bufs[key]
+        bs = B // nc
+        parts = []
+        for c in range(nc):
+            im = img.narrow(1, c * bs, bs)
+            oc = out.narrow(0, c * bs, bs)
+            steps, _ = self.plan(im, out=oc, chain=c)
+            parts.append((steps, im, oc))
+        return parts, out
+
+    def layer_outputs(self, B: int, H: int = 32, W: int = 32):
+        """Each conv layer's spikes [T, B, Ho, Wo, C] of the last captured forward of batch B
+        (the chains' sub-batch buffers joined along the batch), for checks and debugging."""
+        nc = self._chain_count(B, 1)
+        bs = B // nc
+        per = [self._bufs[(bs, H, W, False) if c == 0 else (bs, H, W, False, c)][0]
+               for c in range(nc)]
+        return [torch.cat([p[i] for p in per], dim=1) for i in range(len(per[0]))]
+
+    def _record_chains(self, parts, mark=None):
+        """Issue every chain's launches inside a stream capture: chain 0 on the current stream,
+        chain c > 0 on side stream c, forked from and joined back to the current stream;
+        timing events around chain 0's launch `mark`."""
+        s0 = torch.cuda.current_stream()
+        while len(self._side_streams) < len(parts) - 1:
+            self._side_streams.append(torch.cuda.Stream(device=self.device))
+        side = self._side_streams[:len(parts) - 1]
+        for st in side:
+            st.wait_stream(s0)
+        for c, (steps, _, _) in enumerate(parts):
+            stream = s0 if c == 0 else side[c - 1]
+            with torch.cuda.stream(stream):
+                for k, (_, _, fn) in enumerate(steps):
+                    if c == 0 and k == mark:
+                        self.mark_events[0].record()
+                    fn()
+                    if c == 0 and k == mark:
+                        self.mark_events[1].record()
+        for st in side:
+            s0.wait_stream(st)
 
     def forward(self, img: torch.Tensor, *, per_step_logits: bool = False,
                 out: torch.Tensor | None = None, graph: bool = False,
@@ -301,25 +382,27 @@ class SpikingVGG:
         return None if ent is None else ent[0]
 
     def _capture_graphs(self, img, per_step_logits, out):
-        steps, o = self.plan(img, per_step_logits=per_step_logits, out=out)
-        for _, _, fn in steps:            # warm up (tunes the layers, sets kernel attributes)
-            fn()
+        parts, o = self._chain_plans(img, out, per_step_logits)
+        for steps, _, _ in parts:         # warm up (tunes the layers, sets kernel attributes)
+            for _, _, fn in steps:
+                fn()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=self._fwd_pool):
-            for _, _, fn in steps:
-                fn()
+            self._record_chains(parts)
         torch.cuda.synchronize()
         return [g], o
 
     __call__ = forward
 
     def profile_layers(self, img: torch.Tensor, reps: int = 10):
-        """[(name, flops, device ms per launch)] for one forward plan, each launch timed
-        alone from a CUDA graph of `reps` repetitions (no host overhead in the figure)."""
+        """[(name, flops, device ms per launch)] for the launches of chain 0 of a captured
+        forward (its sub-batch), each launch timed alone from a CUDA graph of `reps`
+        repetitions (no host overhead in the figure)."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
-        steps, _ = self.plan(img)
+        parts, _ = self._chain_plans(img)
+        steps = parts[0][0]                 # chain 0's launches (its sub-batch)
         for _, _, fn in steps:
             fn()
         return [(name, flops, KC.time_graph(fn, reps)) for name, flops, fn in steps]
@@ -343,11 +426,33 @@ class SpikingVGG:
                 mark: int | None = None, out: torch.Tensor | None = None):
         """Capture the forward over the static input buffer ``img`` into CUDA graphs.
         With split_at=i the launches are split into three graphs [0, i), [i], (i, end) so
-        that the i-th launch can be timed alone between replays.  With mark=i the forward is
-        one graph holding a pair of timing events around launch i (``self.mark_events``;
-        read them after a replay has completed).  Returns the output."""
+        that the i-th launch can be timed alone between replays (one chain).  Otherwise the
+        forward is one graph of ``chains`` concurrent sub-batch chains (when the batch
+        splits evenly); with mark=i it holds a pair of timing events around launch i of
+        chain 0 (``self.mark_events``; read them after a replay has completed).  Returns the
+        output."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        self.mark_events = None
+        if mark is not None:
+            self.mark_events = (torch.cuda.Event(enable_timing=True, external=True),
+                                torch.cuda.Event(enable_timing=True, external=True))
+        if split_at is None and self._chain_count(img.shape[1], img.shape[0]) > 1:
+            # concurrent chains in one graph (mark: a launch of chain 0)
+            parts, out = self._chain_plans(img, out)
+            for steps, _, _ in parts:
+                for _, _, fn in steps:
+                    fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.graph_pool):
+                self._record_chains(parts, mark=mark)
+            self.graphs = [g]
+            torch.cuda.synchronize()
+            self.graph_out = out
+            self._graph_parts = parts          # keeps the sub-batch views alive
+            return out
         steps, out = self.plan(img, out=out)
         for _, _, fn in steps:            # warm up (sets kernel attributes, caches maps)
             fn()
@@ -355,11 +460,6 @@ class SpikingVGG:
         groups = [list(range(len(steps)))] if split_at is None else \
             [list(range(split_at)), [split_at], list(range(split_at + 1, len(steps)))]
         self.graphs = []
-        self.graph_pool = torch.cuda.graph_pool_handle()
-        self.mark_events = None
-        if mark is not None:
-            self.mark_events = (torch.cuda.Event(enable_timing=True, external=True),
-                                torch.cuda.Event(enable_timing=True, external=True))
         for grp in groups:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=self.graph_pool):
