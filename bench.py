@@ -563,6 +563,12 @@ class VggWorkload:
                 "kernel_ms": round(kernel_ms, 5),
                 "per_layer_device_ms": {n: round(t, 4) for n, t in
                                         zip(self.layer_names, self.layer_ms)},
+                "per_layer_device_ms_note": "each launch alone, 10 back-to-back in a graph, "
+                                            "warm L2",
+                "per_layer_in_step_ms": {n: round(t, 4) for n, t in
+                                         self.eng.layer_times_in_step(self.img)},
+                "per_layer_in_step_ms_note": "inside one forward graph, events around every "
+                                             "launch, L2 flushed before each replay, median of 10",
                 "choices": {str(k): v for k, v in self.eng.choice.items()},
                 "model_tflops_per_s": None}
 

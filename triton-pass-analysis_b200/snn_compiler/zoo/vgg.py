@@ -407,6 +407,40 @@ class SpikingVGG:
             fn()
         return [(name, flops, KC.time_graph(fn, reps)) for name, flops, fn in steps]
 
+    def layer_times_in_step(self, img: torch.Tensor, reps: int = 10, flush_bytes: int = 256 << 20):
+        """[(name, device ms)] of every launch inside one captured forward (one chain), with
+        a pair of timing events around each launch, median over `reps` replays each after
+        writing `flush_bytes` to flush L2 -- the layers as the step runs them (an event
+        between two launches also stops the next one's programmatic early start, so the sum
+        is a little above the step)."""
+        if img.ndim == 4:
+            img = img.unsqueeze(0)
+        steps, _ = self.plan(img)
+        for _, _, fn in steps:
+            fn()
+        ev = [(torch.cuda.Event(enable_timing=True, external=True),
+               torch.cuda.Event(enable_timing=True, external=True)) for _ in steps]
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for (a, b), (_, _, fn) in zip(ev, steps):
+                a.record()
+                fn()
+                b.record()
+        flush = torch.empty(flush_bytes, dtype=torch.uint8, device=self.device)
+        samples = []
+        for _ in range(reps):
+            flush.fill_(1)
+            g.replay()
+            torch.cuda.synchronize()
+            samples.append([a.elapsed_time(b) for a, b in ev])
+        del g, flush
+        out = []
+        for i, (name, _, _) in enumerate(steps):
+            col = sorted(s[i] for s in samples)
+            out.append((name, col[len(col) // 2]))
+        return out
+
     def flops_per_image(self, H: int = 32, W: int = 32) -> int:
         """Dense algorithmic FLOPs of one image (every conv at every step)."""
         img = torch.empty(1, 1, 3, H, W)
