@@ -385,6 +385,26 @@ int snnb_spike_attention_core(const void* q, const void* k, const void* v, int64
                               float v_reset, int hard_reset, snnb_stream_t stream);
 
 /*
+ * Linear + bias + multi-step LIF in the transposed form, for layers with few rows (the
+ * classifier FusedLinearNeuron, modules.py:241-255, and the dense form of 3x3 layers on 2x2
+ * images; reference: F.linear + fused_bias_if_lif).  x [T, B, K] bf16, w [N, K] bf16
+ * (N % 128 == 0, K % 8 == 0), bias [N] f32 -> spikes [T, B, N] bf16, or with pool4 the OR
+ * of 4 consecutive features [T, B, N / 4].  D^T = W X^T on tcgen05: 128 features x the
+ * T * (256 / T) rows of a column tile per CTA; splits in {1, 2, 4, 8} split K over a
+ * cluster whose float32 partial sums go to `workspace`
+ * (>= snnb_linear_t_workspace_bytes, 16-byte aligned) and are added in split order.
+ * T in {1, 2, 4, 8}.
+ */
+int snnb_linear_lif_t(const void* x, int64_t T, int64_t B, int64_t K, const void* w,
+                      const float* bias, int64_t N, float decay, float input_scale,
+                      float v_threshold, float v_reset, int hard_reset, int pool4, int splits,
+                      void* workspace, int64_t workspace_bytes, void* out,
+                      snnb_stream_t stream);
+
+/* Workspace bytes of snnb_linear_lif_t (0 when splits <= 1, negative when invalid). */
+int64_t snnb_linear_t_workspace_bytes(int64_t T, int64_t B, int64_t N, int splits);
+
+/*
  * Image (first) layer on the tensor cores: replaces the first FusedConvBNNeuron of VGGSNN
  * (snn_compiler/zoo/vgg.py:88-94 -> nn/modules.py:347-357, F.conv2d in float32 +
  * fused_bias_if_lif) for direct encoding -- x [B, Cin, H, W] float32 NCHW, the same image at

@@ -30,7 +30,8 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_every_declared_entry_has_a_python_signature():
     from snn_compiler import _lib
     helpers = {"snnb_abi_version", "snnb_status_string", "snnb_last_cuda_error",
-               "snnb_split_workspace_bytes", "snnb_first_conv_tc_weight_k"}
+               "snnb_split_workspace_bytes", "snnb_first_conv_tc_weight_k",
+               "snnb_linear_t_workspace_bytes"}
     for n in declared_functions():
         if n not in helpers:
             assert n in _lib.SIGNATURES, n

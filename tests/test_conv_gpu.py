@@ -348,3 +348,58 @@ def test_first_conv_tensor_core_against_oracle(cin, cout, B, H, W, soft):
     got = y.float().cpu().permute(0, 1, 4, 2, 3)
     assert got.sum() > 0
     flip_check(got, s, vpre)
+
+
+@pytest.mark.parametrize("T,B,K,N,splits,pool4", [(4, 64, 512, 4096, 1, False),
+                                                  (4, 64, 4096, 4096, 2, False),
+                                                  (4, 64, 2048, 2048, 8, False),
+                                                  (4, 64, 2048, 2048, 4, True),
+                                                  (2, 50, 384, 256, 2, False),
+                                                  (8, 70, 1000, 384, 4, True),
+                                                  (1, 300, 256, 128, 1, False)])
+def test_linear_transposed_against_oracle(T, B, K, N, splits, pool4):
+    """snnb_linear_lif_t (D^T = W X^T, split-K over a cluster, partial sums in split order)
+    against the oracle: linear of the same bf16 values in float32 + LIF, flip criterion;
+    with pool4 the OR of 4 consecutive features of the kernel's own unpooled spikes, exactly;
+    partial column tiles (B not a multiple of 256 / T) included."""
+    C = _C()
+    g = OP.gen(T * 1000 + B + K + splits)
+    x = (torch.rand(T, B, K, generator=g) < 0.2).float()
+    w = (torch.randn(N, K, generator=g) * (3.0 / K) ** 0.5).to(torch.bfloat16).float()
+    b = torch.rand(N, generator=g) * 0.5 + 0.2
+    xd, wd, bd = x.to(torch.bfloat16).to(DEV), w.to(torch.bfloat16).to(DEV), b.to(DEV)
+    y = C.linear_lif_t(xd, wd, bd, tau=2.0, v_threshold=THR, splits=splits)
+    assert C.device_status() == 0
+    z = F.linear(x.reshape(T * B, K), w).reshape(T, B, N)
+    s, vpre = OV.lif_seq(z, b, want_vpre=True)
+    got = y.float().cpu()
+    assert got.sum() > 0
+    flip_check(got, s, vpre)
+    if pool4:
+        yp = C.linear_lif_t(xd, wd, bd, tau=2.0, v_threshold=THR, splits=splits, pool4=True)
+        own = got.reshape(T, B, N // 4, 4).amax(-1)
+        assert torch.equal(yp.float().cpu(), own)
+
+
+def test_dense_conv_transposed_form_equals_row_form():
+    """The dense form of a 2x2 layer through the transposed kernel (variant 8) against the
+    row-major T-folded form (variant 2): flip criterion between them via the oracle."""
+    C = _C()
+    T, B, Cin, Cout, H = 4, 64, 512, 512, 2
+    x, w, b = _layer_case(T, B, Cin, Cout, H, 0.2, 77, False)
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    wk = C.weight_khwc(w).to(DEV)
+    for pool in (False, True):
+        wd = C.dense_conv_weight(wk, H, H, pool=pool)
+        bd = C.dense_conv_bias(b.to(DEV), H, H, pool=pool)
+        y8 = C.conv3x3_lif_dense(xd, wd, bd, pool=pool, variant=8, splits=4, tau=2.0,
+                                 v_threshold=THR)
+        y2 = C.conv3x3_lif_dense(xd, wd, bd, pool=pool, variant=2, block_n=32, tau=2.0,
+                                 v_threshold=THR)
+        assert C.device_status() == 0
+        s, p, vpre = OV.conv_bn_lif_pool(x, w, b, pool=pool, want_vpre=True)
+        got = y8.float().cpu().permute(0, 1, 4, 2, 3)
+        if not pool:
+            flip_check(got, s, vpre)
+        else:
+            assert (got != y2.float().cpu().permute(0, 1, 4, 2, 3)).float().mean() <= 1e-3

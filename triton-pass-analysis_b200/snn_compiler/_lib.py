@@ -50,6 +50,7 @@ SIGNATURES = {
                             P],
     "snnb_read_device_status": [P, P],
     "snnb_set_wait_limit": [I64],
+    "snnb_linear_lif_t": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, P, I64, P, P],
     "snnb_first_conv_lif_tc": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, P],
     "snnb_neuron_plif": [P, I32, I64, I64, P, I32, I32, F, F, P, P, I32, P, P, P, P],
     "snnb_split_bf16_terms": [P, I64, I64, I64, P, P],
@@ -83,6 +84,8 @@ def lib():
         L.snnb_last_cuda_error.restype = ctypes.c_char_p
         L.snnb_split_workspace_bytes.restype = ctypes.c_int64
         L.snnb_split_workspace_bytes.argtypes = [I64, I64, I64, I64, I64, I32]
+        L.snnb_linear_t_workspace_bytes.restype = ctypes.c_int64
+        L.snnb_linear_t_workspace_bytes.argtypes = [I64, I64, I64, I32]
         L.snnb_first_conv_tc_weight_k.restype = ctypes.c_int64
         L.snnb_first_conv_tc_weight_k.argtypes = [I64]
         for name, args in SIGNATURES.items():

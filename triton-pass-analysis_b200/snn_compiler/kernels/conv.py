@@ -82,12 +82,19 @@ def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: 
                v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,
                variant: int = 0, block_n: int = 0, splits: int = 1,
                workspace: torch.Tensor | None = None):
-    """x [T, B, K] bf16 @ w[N, K]^T + bias -> LIF -> spikes [T, B, N] bf16."""
+    """x [T, B, K] bf16 @ w[N, K]^T + bias -> LIF -> spikes [T, B, N] bf16.
+    variant 8: the transposed form (features x rows, split-K over `splits` CTAs of a
+    cluster; snnb_linear_lif_t) for layers with few rows."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
     T, B, K = x.shape
     N = w.shape[0]
     assert bias.dtype == torch.float32 and bias.numel() == N
+    if variant == 8:
+        return linear_lif_t(x, w, bias, neuron=neuron, tau=tau, decay=decay,
+                            decay_input=decay_input, soft_reset=soft_reset,
+                            v_threshold=v_threshold, v_reset=v_reset, out=out, splits=splits,
+                            workspace=workspace)
     df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
                                       v_reset)
     if out is None:
@@ -98,6 +105,45 @@ def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: 
                                     thr, vr, hard, int(variant), int(block_n), int(splits),
                                     _lib.ptr(ws), ws_bytes, _lib.ptr(out), _lib.stream_of(x))
     _lib.check(st, "snnb_linear_lif")
+    return out
+
+
+def linear_t_workspace_bytes(T, B, N, splits) -> int:
+    n = int(_lib.lib().snnb_linear_t_workspace_bytes(T, B, N, int(splits)))
+    if n < 0:
+        raise ValueError(f"transposed-linear workspace size invalid: {(T, B, N, splits)}")
+    return n
+
+
+def linear_lif_t(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
+                 tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
+                 v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,
+                 splits: int = 1, workspace: torch.Tensor | None = None, pool4: bool = False):
+    """The transposed linear + LIF (snnb_linear_lif_t): x [T, B, K] bf16, w [N, K] bf16
+    (N % 128 == 0), bias [N] f32 -> spikes [T, B, N] bf16 ([T, B, N / 4] with pool4, the OR
+    of 4 consecutive features).  splits in {1, 2, 4, 8}: the K range over a cluster, partial
+    sums in `workspace` (linear_t_workspace_bytes; allocated here if None)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 3
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[2]
+    T, B, K = x.shape
+    N = w.shape[0]
+    assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == N
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    No = N // 4 if pool4 else N
+    if out is None:
+        out = torch.empty(T, B, No, device=x.device, dtype=torch.bfloat16)
+    assert out.is_contiguous() and out.numel() == T * B * No and out.dtype == torch.bfloat16
+    need = linear_t_workspace_bytes(T, B, N, splits)
+    if need and workspace is None:
+        workspace = torch.empty(need // 4, device=x.device, dtype=torch.float32)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    assert ws_bytes >= need
+    st = _lib.lib().snnb_linear_lif_t(_lib.ptr(x), T, B, K, _lib.ptr(w), _lib.ptr(bias), N, df,
+                                      sc, thr, vr, hard, int(bool(pool4)), int(splits),
+                                      _lib.ptr(workspace), ws_bytes, _lib.ptr(out),
+                                      _lib.stream_of(x))
+    _lib.check(st, "snnb_linear_lif_t")
     return out
 
 
@@ -268,15 +314,17 @@ def band_xs_block_ns(W: int, cin: int, cout: int):
 
 
 def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
-               dense_pool: bool = False, band_xs=()):
+               dense_pool: bool = False, band_xs=(), linear_t: bool = False):
     """(variant, block_n, splits) configurations a layer admits; `band` / `band_xs` list the
     block widths of variants 3 / 7 the layer qualifies for (band_block_ns,
     band_xs_block_ns); dense_pool: the pooled dense form (snnb_conv3x3_lif_dense), whose
     epilogue the plain T-folded kernel alone has (variant 2, no split)."""
+    lt = [(8, 128, sp) for sp in (1, 2, 4, 8)
+          if linear_t and cout % 128 == 0 and T in (1, 2, 4, 8) and sp <= max(1, kslabs)]
     if dense_pool:
         return [c for c in candidates(cout, T, kslabs, max_splits)
-                if c[0] == 2 and c[2] == 1]
-    out = []
+                if c[0] == 2 and c[2] == 1] + lt
+    out = lt
     for v in ((1, 2) if T in (2, 4, 8) else (1,)):
         for bn in ((32, 64, 128) if v == 1 else (32, 64, 128, 256)):
             if cout % bn:
@@ -315,11 +363,12 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
 
 
 def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=(),
-                 dense_pool: bool = False, band_xs=()):
+                 dense_pool: bool = False, band_xs=(), linear_t: bool = False):
     """Time launch(variant, block_n, splits) for every configuration the layer admits
     (on its real operands, device time via time_graph) and return the fastest."""
     best, best_ms = (0, 0, 1), float("inf")
-    for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool, band_xs=band_xs):
+    for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool, band_xs=band_xs,
+                          linear_t=linear_t):
         # the lower of two timings: one replay can catch another context's work
         ms = min(time_graph(lambda: launch(*cfg), reps) for _ in range(2))
         if ms < best_ms:
@@ -449,6 +498,13 @@ def conv3x3_lif_dense(x: torch.Tensor, wd: torch.Tensor, bd: torch.Tensor, *,
     Ho, Wo = (1, 1) if pool else (H, W)
     if out is None:
         out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
+    if variant == 8:
+        # the transposed form: features (p, co) -- or (co, p) with pool -- as M
+        linear_lif_t(x.view(T, B, H * W * Cin), wd, bd, neuron=neuron, tau=tau, decay=decay,
+                     decay_input=decay_input, soft_reset=soft_reset, v_threshold=v_threshold,
+                     v_reset=v_reset, out=out.view(T, B, -1), splits=splits,
+                     workspace=workspace, pool4=pool)
+        return out
     ws, ws_bytes = _workspace(workspace, 1 if variant == 6 else splits, T, B, 1, 1,
                               H * W * Cout, x.device)
     st = _lib.lib().snnb_conv3x3_lif_dense(

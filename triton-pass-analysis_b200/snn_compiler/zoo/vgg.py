@@ -162,9 +162,9 @@ class SpikingVGG:
                                                       variant=v, block_n=bn, splits=sp,
                                                       workspace=self._ws(T, B, 1, 1, NN,
                                                                          1 if v == 6 else sp,
-                                                                         chain),
+                                                                         chain, v),
                                                       **self.lif),
-                                 dense_pool=L["pool"])
+                                 dense_pool=L["pool"], linear_t=True)
             else:
                 fn = self._tuned(("conv", i, B, h, w), L["cout"], 9 * L["cin"] // 64,
                                  lambda v, bn, sp, L=L, x=x_prev, o=bufs[i], hh=h, ww=w:
@@ -189,8 +189,9 @@ class SpikingVGG:
                                                     block_n=bn, splits=sp,
                                                     workspace=self._ws(T, B, 1, 1, NN,
                                                                       1 if v == 6 else sp,
-                                                                      chain),
-                                                    **self.lif))))
+                                                                      chain, v),
+                                                    **self.lif),
+                                      linear_t=True)))
             hcur = fbufs[j]
         f = self.fcs[-1]
         K, N = f["w"].shape[1], f["w"].shape[0]
@@ -234,10 +235,12 @@ class SpikingVGG:
                                   KC.dense_conv_bias(L["b"], h, w, pool=L["pool"]))
         return self._dense_w[key]
 
-    def _ws(self, T, B, H, W, Cout, splits, chain=0):
+    def _ws(self, T, B, H, W, Cout, splits, chain=0, variant=0):
         """Split-K workspace, one buffer per chain shared by the chain's layers (they run one
-        after another on one stream), grown to the largest request."""
-        need = KC.split_workspace_bytes(T, B, H, W, Cout, splits)
+        after another on one stream), grown to the largest request (variant 8: the
+        transposed linear's partial sums)."""
+        need = KC.linear_t_workspace_bytes(T, B, Cout, splits) if variant == 8 else \
+            KC.split_workspace_bytes(T, B, H, W, Cout, splits)
         if need == 0:
             return None
         ws = self._workspace.get(chain)
@@ -246,13 +249,15 @@ class SpikingVGG:
             self._workspace[chain] = ws
         return ws
 
-    def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False, band_xs=()):
+    def _tuned(self, key, cout, kslabs, launch, band=(), dense_pool=False, band_xs=(),
+               linear_t=False):
         """A zero-argument launcher for one tensor-core layer.  With autotune on, the first
         call times every (variant, block_n, splits) the layer admits and keeps the fastest."""
         def run():
             if key not in self.choice:
                 self.choice[key] = KC.pick_fastest(launch, cout, self.T, kslabs, band=band,
-                                                   dense_pool=dense_pool, band_xs=band_xs) \
+                                                   dense_pool=dense_pool, band_xs=band_xs,
+                                                   linear_t=linear_t) \
                     if self.autotune else (0, 0, 1)
             return launch(*self.choice[key])
         return run
