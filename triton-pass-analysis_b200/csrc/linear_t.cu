@@ -18,7 +18,7 @@
 //   warps 2-5  epilogue, thread = TMEM lane = output feature
 // S == 1: each thread adds the bias and runs the neuron over the T steps of each sample from
 // its accumulator row, and stores the spikes.  S > 1: each CTA stores its float32 partial
-// sums [feature][256 columns] to the workspace, the cluster synchronises (release /
+// sums [256 columns][feature] to the workspace (coalesced: a warp's 32 features per column), the cluster synchronises (release /
 // acquire at cluster scope), and CTA r finishes columns [r * 256 / S, (r + 1) * 256 / S):
 // it adds the S partial sums in split order, the bias, runs the neuron and stores.
 // pool4: OR over 4 consecutive features (the dense form of a pooled 2x2 layer, rows ordered
@@ -44,7 +44,7 @@ struct LtParams {
     float df, sc, thr, v_reset;
     const float* bias;
     __nv_bfloat16* out;
-    float* partial;                          // [splits][nbt][N][256] float32 when splits > 1
+    float* partial;                          // [splits][nbt][256][N] float32 when splits > 1
     int* status;
 };
 
@@ -226,18 +226,17 @@ linear_t_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__
                     }
                 }
             } else {
-                // this split's partial sums, [feature][256 columns] float32
-                float* dst = p.partial + (((int64_t)split * p.nbt + bt) * p.N + feature) * LT_COLS;
+                // this split's partial sums, [256 columns][feature] float32: for each column
+                // a warp writes 32 consecutive features (128 bytes)
+                float* dst = p.partial + ((int64_t)split * p.nbt + bt) * LT_COLS * p.N + feature;
 #pragma unroll 1
                 for (int c = 0; c < LT_COLS / 32; ++c) {
                     float r[32];
                     tc::tmem_ld32(tbase + c * 32, r);
                     tc::tmem_wait_ld();
                     if (feature < p.N) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            d4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                        for (int j = 0; j < 32; ++j) dst[(int64_t)(c * 32 + j) * p.N] = r[j];
                     }
                 }
             }
@@ -253,19 +252,32 @@ linear_t_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__
             const int wc = LT_COLS / p.splits;                // columns this CTA finishes
             const int c0 = split * wc;
             const float bias = feature < p.N ? __ldg(p.bias + feature) : 0.0f;
-            const float* src = p.partial + ((int64_t)bt * p.N + feature) * LT_COLS + c0;
-            const int64_t sstride = (int64_t)p.nbt * p.N * LT_COLS;
+            const float* src = p.partial + ((int64_t)bt * LT_COLS + c0) * p.N + feature;
+            const int64_t sstride = (int64_t)p.nbt * LT_COLS * p.N;
             for (int cc = 0; cc < wc; cc += 8) {
                 float y[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) y[e] = 0.0f;
                 if (feature < p.N) {
-                    for (int s = 0; s < p.splits; ++s) {
-                        const float4* s4 = reinterpret_cast<const float4*>(src + s * sstride + cc);
-                        const float4 u = s4[0], w = s4[1];
-                        const float in[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+                    // every split's 8 values in flight at once (one L2 round trip per 8
+                    // columns, not one per split), then added in split order
+                    float in[8][8];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) y[e] = s == 0 ? in[e] : __fadd_rn(y[e], in[e]);
+                    for (int s = 0; s < 8; ++s) {
+                        if (s < p.splits) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                in[s][e] = __ldcg(src + s * sstride + (int64_t)(cc + e) * p.N);
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = in[0][e];
+#pragma unroll
+                    for (int s = 1; s < 8; ++s) {
+                        if (s < p.splits) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(y[e], in[s][e]);
+                        }
                     }
                 }
 #pragma unroll
