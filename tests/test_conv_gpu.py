@@ -328,11 +328,15 @@ def test_pack_unpack_round_trip_and_packed_limits():
 
 @pytest.mark.parametrize("cin,cout,B,H,W,soft", [(3, 64, 3, 32, 32, False), (3, 64, 2, 7, 9, False),
                                                  (1, 32, 2, 16, 16, True), (4, 128, 2, 12, 20, False),
-                                                 (2, 64, 5, 8, 8, True), (3, 32, 1, 5, 5, False)])
+                                                 (2, 64, 5, 8, 8, True), (3, 32, 1, 5, 5, False),
+                                                 (3, 64, 20, 32, 32, False),
+                                                 (2, 128, 37, 23, 23, True),
+                                                 (1, 32, 300, 16, 16, False)])
 def test_first_conv_tensor_core_against_oracle(cin, cout, B, H, W, soft):
     """Image layer on tcgen05 (snnb_first_conv_lif_tc): the float32 conv from split bf16
     terms against the float32 oracle conv -- flip criterion -- including partial 128-pixel
-    tiles (B*H*W not a multiple of 128) and image borders."""
+    tiles (B*H*W not a multiple of 128), image borders, and more tiles than SMs (the
+    persistent CTAs then cycle through both stages several times)."""
     C = _C()
     T = 4
     g = OP.gen(31 + cin + cout + H)

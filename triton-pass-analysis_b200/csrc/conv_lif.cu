@@ -340,7 +340,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 // instead of 9 loads of 128 rows.  The weights of the CTA's channel block (9 taps x Cin x
 // BN, <= 108 KB) stay in shared memory; tiles are ordered channel-block-major so a CTA
 // reloads them only when its next tile belongs to another block.  Weight slab (cb, dx)
-// holds taps dy = 0..2 as [dy][BN rows][64 channels].
+// holds taps dy = 0..2 as [dy][BN rows][64 channels] (XS below: slab (cb, dy) holds
+// dx = 0..2).
 constexpr int BAND_MAX_STAGES = 8;
 
 template <int BN>
@@ -369,7 +370,11 @@ __device__ __forceinline__ Tile decode_band(int tile, const ConvParams& p, int B
 // out[m] = D_1[m] + D_0[m - 1] + D_2[m + 1], with one-lane shuffles inside each row's W
 // lanes; a row's first (last) column takes no D_0 (D_2) term -- it would come from the
 // zero padding.  Stages are a third of the size, so the ring is three times deeper and the
-// operand copies' round trips hide behind the MMAs; TMEM holds 2 x 3 accumulators.
+// operand copies' round trips hide behind the MMAs; TMEM holds 2 x 3 accumulators.  The
+// three column taps of a tap row run as ONE MMA of N = 3 x BN (their weights adjacent in
+// shared memory, their accumulators adjacent in TMEM): per (step, slab) 12 MMAs reading
+// 120 KB of operands instead of 36 reading 216 KB, and one band copy (a third of the TMA
+// bytes) -- shared-memory bandwidth, not the tensor pipe, bounds the N = 64 MMAs.
 constexpr int BAND_THREADS = 320;   // producer, MMA issuer, 2 x 4 epilogue warps
 
 template <int BN, bool HARD, bool XS>
@@ -409,6 +414,12 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int CB = p.cin_blocks;
+    // weight slot of tap (dy, dx) of slab cb: [cb][dx][dy] (the A copy dx serves taps
+    // dy = 0..2), or with XS [cb][dy][dx], so that a tap row's three column taps are one
+    // B operand of 3 x BN rows
+    auto wslot = [](int cb, int dx, int dy) -> uint32_t {
+        return (uint32_t)(XS ? (cb * 3 + dy) * 3 + dx : (cb * 3 + dx) * 3 + dy);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < nst; ++s) {
@@ -461,9 +472,8 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     for (int cb = 0; cb < CB; ++cb)
                         for (int dx = 0; dx < 3; ++dx)
                             for (int dy = 0; dy < 3; ++dy)
-                                tc::tma_load_3d(
-                                    sbase + (uint32_t)((cb * 3 + dx) * 3 + dy) * TAP_BYTES, &tmB,
-                                    wfull_bar, cb * 64, dy * 3 + dx, tl.n0);
+                                tc::tma_load_3d(sbase + wslot(cb, dx, dy) * TAP_BYTES, &tmB,
+                                                wfull_bar, cb * 64, dy * 3 + dx, tl.n0);
                 }
                 __syncwarp();
                 wissued += failed ? 0u : 1u;
@@ -520,6 +530,8 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         // channel block, whose weights are loaded only after this block's last MMAs): with
         // Cin = 64 a step is one stage of 36 MMAs, and a drain per step cost ~40% of them.
         constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+        constexpr uint32_t IDESC3 = tc::idesc_bf16_f32(128, XS ? 3 * BN : BN);
+        static_assert(!XS || (3 * BN <= 256 && (3 * BN) % 16 == 0), "MMA N of the XS form");
         const uint32_t row_step = (uint32_t)p.W * 128u;         // one image row of the band copy
         int stage = 0, cur_nb = -1;
         uint32_t phase = 0, it = 0, wl = 0, failed = 0, ready = 0;
@@ -553,20 +565,35 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                             failed |= 1u - tc::mbar_wait_lane(full_bar(stage), phase, failed);
                             tc::tc_fence_after();
                         }
-#pragma unroll
-                        for (int dx = 0; dx < 3; ++dx) {
-                            const uint32_t abase = XS ? sb : sb + dx * a_bytes;
-                            const uint32_t wbase = sbase + (uint32_t)((cb * 3 + dx) * 3) * TAP_BYTES;
-                            const uint32_t dst = XS ? dcol + dx * BN : dcol;
+                        if constexpr (XS) {
+                            // one MMA per (dy, k) with N = 3 x BN: the three column taps'
+                            // weights are adjacent rows of the B operand and their sums land
+                            // in the adjacent accumulators D_0 | D_1 | D_2, so each A row is
+                            // read from shared memory once for all three
 #pragma unroll
                             for (int dy = 0; dy < 3; ++dy) {
-                                const uint64_t da = tc::sdesc_k_sw128(abase + dy * row_step);
-                                const uint64_t db = tc::sdesc_k_sw128(wbase + dy * TAP_BYTES);
+                                const uint64_t da = tc::sdesc_k_sw128(sb + dy * row_step);
+                                const uint64_t db =
+                                    tc::sdesc_k_sw128(sbase + wslot(cb, 0, dy) * TAP_BYTES);
 #pragma unroll
                                 for (int k = 0; k < 4; ++k)
-                                    tc::umma_bf16(dst, da + 2 * k, db + 2 * k, IDESC,
-                                                  XS ? ((cb | dy | k) != 0)
-                                                     : ((cb | dx | dy | k) != 0));
+                                    tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC3,
+                                                  (cb | dy | k) != 0);
+                            }
+                        } else {
+#pragma unroll
+                            for (int dx = 0; dx < 3; ++dx) {
+                                const uint32_t abase = sb + dx * a_bytes;
+#pragma unroll
+                                for (int dy = 0; dy < 3; ++dy) {
+                                    const uint64_t da = tc::sdesc_k_sw128(abase + dy * row_step);
+                                    const uint64_t db =
+                                        tc::sdesc_k_sw128(sbase + wslot(cb, dx, dy) * TAP_BYTES);
+#pragma unroll
+                                    for (int k = 0; k < 4; ++k)
+                                        tc::umma_bf16(dcol, da + 2 * k, db + 2 * k, IDESC,
+                                                      (cb | dx | dy | k) != 0);
+                                }
                             }
                         }
                         if (cb + 1 < CB) {
@@ -933,6 +960,9 @@ int launch_splitsum(float* partial, int S, int64_t rows, int C, const float* bia
     return launch_k(splitsum_kernel<1>, dim3(blocks), dim3(256), 0, s, partial, rows, C, bias);
 }
 
+}  // namespace
+
+// SM count of the current device (cached per device); also used by first_tc.cu.
 int sm_count() {
     static int n[64] = {0};
     int dev = 0;
@@ -945,6 +975,8 @@ int sm_count() {
     }
     return n[dev];
 }
+
+namespace {
 
 template <typename K>
 int launch_persistent(K kernel, int smem, const CUtensorMap& ta, const CUtensorMap& tb,
