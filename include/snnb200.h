@@ -411,9 +411,11 @@ int64_t snnb_linear_t_workspace_bytes(int64_t T, int64_t B, int64_t N, int split
  * every one of the T steps, so the conv runs once per pixel and the neuron T times from it.
  * The conv is float32-accurate: image and weights as three bf16 terms each, six products
  * summed by tcgen05 MMAs into float32 (see snnb_split_bf16_terms).  w_split [Cout, KP] bf16
- * is the folded weight's terms, groups [hi, mid, lo, hi, mid, hi] of 9 * Cin values in
- * torch's (ci, ky, kx) order, zero-padded to KP = snnb_first_conv_tc_weight_k(Cin).
- * out [T, B, H, W, Cout] bf16 spikes (no pooling).  Cin 1..4, Cout 32 / 64 / 128.
+ * is the folded weight's terms, groups [hi, mid, lo, hi, mid, hi] of the 9 * Cin values in
+ * torch's (ci, ky, kx) order, each group G = 9 * Cin + (Cin & 1) entries wide (one zero after
+ * the values when 9 * Cin is odd), zero-padded to KP = snnb_first_conv_tc_weight_k(Cin).
+ * out [T, B, H, W, Cout] bf16 spikes (no pooling), 32-byte aligned.  Cin 1..4,
+ * Cout 32 / 64 / 128.
  */
 int snnb_first_conv_lif_tc(const float* x, int64_t T, int64_t B, int64_t Cin, int64_t H,
                            int64_t W, const void* w_split, const float* bias, int64_t Cout,

@@ -147,6 +147,55 @@ __device__ __forceinline__ void split_bf16x3(float a, __nv_bfloat16& h, __nv_bfl
     l = __float2bfloat16_rn(r2);
 }
 
+// split_bf16x3 of two values with |a| <= SPLIT2_FAST_MAX (finite, and their bf16 rounding
+// cannot overflow), as bf16x2 words (a0 in the low half): the same roundings and exact
+// residuals, with paired conversions.
+constexpr float SPLIT2_FAST_MAX = 3.0e38f;
+__device__ __forceinline__ void split2_bf16x3_finite(float a0, float a1, uint32_t& h,
+                                                     uint32_t& m, uint32_t& l) {
+    auto bits = [](__nv_bfloat162 v) -> uint32_t {
+        return (uint32_t)__bfloat16_as_ushort(v.x) | ((uint32_t)__bfloat16_as_ushort(v.y) << 16);
+    };
+    const __nv_bfloat162 h2 = __float22bfloat162_rn(make_float2(a0, a1));
+    const float2 fh = __bfloat1622float2(h2);
+    const float2 r1 = make_float2(__fsub_rn(a0, fh.x), __fsub_rn(a1, fh.y));
+    const __nv_bfloat162 m2 = __float22bfloat162_rn(r1);
+    const float2 fm = __bfloat1622float2(m2);
+    const __nv_bfloat162 l2 =
+        __float22bfloat162_rn(make_float2(__fsub_rn(r1.x, fm.x), __fsub_rn(r1.y, fm.y)));
+    h = bits(h2);
+    m = bits(m2);
+    l = bits(l2);
+}
+
+// The same for any two values: those whose bf16 rounding could overflow, and non-finite
+// ones, take the scalar path.
+__device__ __forceinline__ void split2_bf16x3(float a0, float a1, uint32_t& h, uint32_t& m,
+                                              uint32_t& l) {
+    auto bits = [](__nv_bfloat162 v) -> uint32_t {
+        return (uint32_t)__bfloat16_as_ushort(v.x) | ((uint32_t)__bfloat16_as_ushort(v.y) << 16);
+    };
+    if (fabsf(a0) <= SPLIT2_FAST_MAX && fabsf(a1) <= SPLIT2_FAST_MAX) {
+        split2_bf16x3_finite(a0, a1, h, m, l);
+    } else {
+        __nv_bfloat16 h0, m0, l0, h1, m1, l1;
+        split_bf16x3(a0, h0, m0, l0);
+        split_bf16x3(a1, h1, m1, l1);
+        h = bits(__halves2bfloat162(h0, h1));
+        m = bits(__halves2bfloat162(m0, m1));
+        l = bits(__halves2bfloat162(l0, l1));
+    }
+}
+
+// One 32-byte store (sm_100's 256-bit vector store): whole sectors from one lane.  The
+// address must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[16], int o) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p),
+                 "r"(w[o]), "r"(w[o + 1]), "r"(w[o + 2]), "r"(w[o + 3]), "r"(w[o + 4]),
+                 "r"(w[o + 5]), "r"(w[o + 6]), "r"(w[o + 7])
+                 : "memory");
+}
+
 // 8 spike bits -> 8 bf16 values (0.0 / 1.0) packed in 16 bytes, bit i -> element i.
 __device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
     uint32_t w[4];

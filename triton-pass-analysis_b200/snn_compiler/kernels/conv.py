@@ -236,10 +236,13 @@ def first_conv_lif(img: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, T:
 
 def first_conv_split_weight(w: torch.Tensor) -> torch.Tensor:
     """Image-layer conv weight [Cout, Cin, 3, 3] (float32, BN folded) -> the tensor-core
-    image kernel's operand [Cout, KP] bf16: six groups of K0 = 9 * Cin terms in torch's
-    (ci, ky, kx) order, [hi, mid, lo, hi, mid, hi] (SPLIT_WGT), zero-padded to KP."""
+    image kernel's operand [Cout, KP] bf16: six groups [hi, mid, lo, hi, mid, hi]
+    (SPLIT_WGT) of the K0 = 9 * Cin terms in torch's (ci, ky, kx) order, each group G = K0
+    rounded up to even entries wide (a zero after the values when K0 is odd), zero-padded to
+    KP."""
     Cout, Cin = w.shape[:2]
     K0 = 9 * Cin
+    G = K0 + (K0 & 1)
     KP = int(_lib.lib().snnb_first_conv_tc_weight_k(Cin))
     if KP < 0:
         raise ValueError(f"tensor-core image layer takes Cin <= 4, got {Cin}")
@@ -247,7 +250,7 @@ def first_conv_split_weight(w: torch.Tensor) -> torch.Tensor:
     terms = {"hi": h, "mid": m, "lo": l}
     out = torch.zeros(Cout, KP, dtype=torch.bfloat16, device=w.device)
     for g, name in enumerate(SPLIT_WGT):
-        out[:, g * K0:(g + 1) * K0] = terms[name]
+        out[:, g * G:g * G + K0] = terms[name]
     return out.contiguous()
 
 
