@@ -1167,7 +1167,8 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 namespace {
 
 // ---- variant 3 host path -----------------------------------------------------------------
-constexpr int BAND_W_MAX = 108 * 1024;          // resident weights per CTA
+constexpr int BAND_W_MAX = 108 * 1024;          // resident weights per CTA (3 band copies)
+constexpr int BAND_XS_W_MAX = 160 * 1024;       // the XS form: one copy per stage
 
 int smem_optin() {
     static int v[64] = {0};
@@ -1183,11 +1184,15 @@ int smem_optin() {
     return v[dev];
 }
 
-// Channel-block width for the band kernel, or 0 if the layer does not qualify.
-int band_block_n(int W, int Cin, int Cout, int block_n) {
+// Channel-block width for the band kernel, or 0 if the layer does not qualify.  The XS
+// form's stages hold one band copy instead of three, which leaves room for larger resident
+// weights (its ring still gets >= 2 stages: run_band_layer checks).
+int band_block_n(int W, int Cin, int Cout, int block_n, bool xs) {
     if (!(W == 8 || W == 16 || W == 32 || W == 64)) return 0;
+    if (xs && W > 32) return 0;
     const int CB = (Cin + 63) / 64;
-    auto fits = [&](int bn) { return Cout % bn == 0 && 9 * CB * bn * 128 <= BAND_W_MAX; };
+    const int wmax = xs ? BAND_XS_W_MAX : BAND_W_MAX;
+    auto fits = [&](int bn) { return Cout % bn == 0 && 9 * CB * bn * 128 <= wmax; };
     if (block_n) return (block_n == 32 || block_n == 64) && fits(block_n) ? block_n : 0;
     if (fits(64)) return 64;
     return fits(32) ? 32 : 0;
@@ -1343,7 +1348,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (splits > KB) return SNNB_ERR_ARG;
     if (variant == 3 || variant == 7) {
         if (taps != 9 || splits > 1 || res) return SNNB_ERR_UNSUPPORTED;
-        const int BN3 = band_block_n(W, Cin, Cout, block_n);
+        const int BN3 = band_block_n(W, Cin, Cout, block_n, variant == 7);
         if (!BN3) return SNNB_ERR_UNSUPPORTED;
         int* st = device_status_ptr();
         if (!st) return SNNB_ERR_CUDA;

@@ -312,8 +312,12 @@ def band_block_ns(W: int, cin: int, cout: int):
 
 def band_xs_block_ns(W: int, cin: int, cout: int):
     """Channel-block widths of variant 7 (band kernel with the column taps shifted in the
-    epilogue): those of variant 3 when an image row fits one warp (W <= 32)."""
-    return band_block_ns(W, cin, cout) if W <= 32 else ()
+    epilogue): W in {8, 16, 32} (an image row fits one warp) and the block's weights within
+    160 KB of shared memory (its stages hold one band copy, not three)."""
+    if W not in (8, 16, 32):
+        return ()
+    cb = (cin + 63) // 64
+    return tuple(bn for bn in (32, 64) if cout % bn == 0 and 9 * cb * bn <= 1280)
 
 
 def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
