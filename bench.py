@@ -702,6 +702,102 @@ class ConvLayerWorkload:
         return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
 
 
+class FirstLayerWorkload:
+    """The image (first) layer of VGG16-SNN on its own: float32 image [1, B, 3, 32, 32]
+    (direct encoding) -> conv3x3 3->64 + folded BN + LIF over T steps -> spikes
+    [T, B, 32, 32, 64] bf16.  The tensor-core kernel (split operands) or the CUDA-core one,
+    whichever is faster (or `--choice 1` / `0`)."""
+    name = "first"
+    flush_l2 = True
+
+    def __init__(self, B=64, T=4, cin=3, cout=64, H=32, fixed=None):
+        self.B, self.T, self.cin, self.cout, self.H = B, T, cin, cout, H
+        self.fixed = fixed
+        self.flops = 2 * T * B * H * H * cout * cin * 9
+        # algorithmic bytes: the image read once, the spikes written once
+        self.bytes = 4 * B * cin * H * H + 2 * T * B * H * H * cout
+        self.metric = (f"image layer conv3x3 {cin}->{cout} (float32 image, split-operand tensor "
+                       f"cores) + LIF TFLOP/s (H=W={H}, B={B}, T={T})")
+        self.unit = "TFLOP/s"
+        self.dtype = "f32 (as 3 bf16 terms)"
+
+    def config(self):
+        return {"workload": f"image_layer_{self.cin}x{self.cout}@{self.H}", "T": self.T,
+                "B": self.B, "Cin": self.cin, "Cout": self.cout, "H": self.H, "W": self.H,
+                "input": "U(0,1) float32 image, direct encoding",
+                "l2": "256 MB buffer written before every step"}
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.kernels import conv as KC
+        self.KC = KC
+        g = torch.Generator(device="cuda").manual_seed(11 + rank)
+        B, C, H = self.B, self.cin, self.H
+        self.img = torch.rand(1, B, C, H, H, device="cuda", generator=g)
+        self.w = torch.randn(self.cout, C, 3, 3, device="cuda", generator=g) * (2.0 / (9 * C)) ** 0.5
+        self.b = torch.rand(self.cout, device="cuda", generator=g) * 0.5 + 0.2
+        self.ws = KC.first_conv_split_weight(self.w)
+        self.out = torch.empty(self.T, B, H, H, self.cout, device="cuda", dtype=torch.bfloat16)
+        runs = [lambda: KC.first_conv_lif(self.img, self.w, self.b, T=self.T, out=self.out),
+                lambda: KC.first_conv_lif_tc(self.img, self.ws, self.b, T=self.T, out=self.out)]
+        if self.fixed is not None:
+            self.choice = self.fixed
+        else:
+            times = [KC.time_graph(r, 10) for r in runs]
+            self.choice = times.index(min(times))
+        self.run = runs[self.choice]
+        self.launches_per_step = 1
+
+    def step(self):
+        self.run()
+
+    def kernel_events(self, steps):
+        return None
+
+    def units_per_step(self):
+        return self.flops / 1e12
+
+    def e2e_setup(self):
+        self.hx = self.img.cpu().pin_memory()
+        self.hout = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = self.hx.numel() * self.hx.element_size()
+        self.d2h = self.hout.numel() * self.hout.element_size()
+
+    def e2e_step(self):
+        self.img.copy_(self.hx, non_blocking=True)
+        self.step()
+        self.hout.copy_(self.out, non_blocking=True)
+
+    def e2e_units(self):
+        return self.flops / 1e12
+
+    def roofline(self, kernel_ms, peaks):
+        # the layer's tensor work is small (0.9 GFLOP standard count); its one large stream
+        # is the spikes it writes, so it is reported against HBM bandwidth
+        gbs = self.bytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"] + " HBM copy",
+                "kernel": ["first_conv_quad_kernel (CUDA cores)",
+                           "first_conv_tc_kernel (tcgen05, split operands)"][self.choice],
+                "algorithmic_bytes_per_launch": self.bytes,
+                "tflops": round(self.flops / (kernel_ms * 1e-3) / 1e12, 2), "traffic": None}
+
+    def cpu_sample(self):
+        from oracle import params as OP
+        B, H, C = 2, self.H, self.cin
+        img = torch.rand(1, B, C, H, H, generator=OP.gen(3))
+        w = torch.randn(self.cout, C, 3, 3, generator=OP.gen(1)) * (2.0 / (9 * C)) ** 0.5
+        b = torch.rand(self.cout, generator=OP.gen(2)) * 0.5 + 0.2
+        return {"B": B, "x": img.expand(self.T, B, C, H, H).contiguous(), "w": w, "b": b,
+                "what": "oracle conv+LIF, torch-CPU f32"}
+
+    def cpu_run(self, s, threads):
+        from oracle import vgg as OV
+        torch.set_num_threads(threads)
+        OV.conv_bn_lif_pool(s["x"], s["w"], s["b"], pool=False)
+        return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
+
+
 class AttnWorkload:
     """Spiking self-attention block (config 3): x [T=4, B=32, N=196, D=384] spikes, 12 heads."""
     name = "attention"
@@ -1075,7 +1171,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="vgg16",
-                    choices=["vgg16", "lif", "conv", "attention", "bgemm"])
+                    choices=["vgg16", "lif", "conv", "first", "attention", "bgemm"])
     ap.add_argument("--lif-shape", default="32,134217728", help="lif workload: T,N")
     ap.add_argument("--gemm-shape", default="16384,8192,8192", help="bgemm workload: M,K,N")
     ap.add_argument("--layer", default="512,512,56", help="conv workload: Cin,Cout,H")
@@ -1102,6 +1198,9 @@ def main():
         if fixed and len(fixed) == 2:
             fixed = fixed + (1,)
         wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed, packed=args.packed)
+    elif args.workload == "first":
+        wl = FirstLayerWorkload(B=args.batch,
+                                fixed=int(args.choice) if args.choice is not None else None)
     else:
         if args.workload == "lif":
             lt, ln = (int(v) for v in args.lif_shape.split(","))
