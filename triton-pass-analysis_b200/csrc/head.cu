@@ -129,9 +129,6 @@ __global__ void __launch_bounds__(HEAD2_THREADS) linear_head_nb_kernel(
         float acc[TC];
 #pragma unroll
         for (int i = 0; i < TC; ++i) acc[i] = 0.0f;
-        // unrolled so that the slices' loads of several iterations are in flight together
-        // (the sums still run in k order: the same results)
-#pragma unroll 4
         for (int k8 = threadIdx.x; k8 < K8; k8 += HEAD2_THREADS) {
             float wv[8];
             bf16x8_to_f32(__ldg(wrow + k8), wv);
