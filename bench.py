@@ -406,7 +406,8 @@ class VggWorkload:
         kern = {1: "conv_lif_kernel", 2: "conv_lif_tm_kernel", 3: "conv_lif_band_kernel",
                 4: "conv_lif_tm_kernel (two M-tiles)", 5: "conv_lif_tm_kernel (CTA pairs)",
                 6: "conv_lif_tm_kernel (cluster split-K)",
-                7: "conv_lif_band_kernel (column taps in the epilogue)"}.get(
+                7: "conv_lif_band_kernel (column taps in the epilogue)",
+                8: "linear_t_kernel (transposed, split-K)"}.get(
             v[0], "conv_lif (auto)")
         return f"{kern}<block_n={v[1]}, splits={v[2]}> ({name})"
 

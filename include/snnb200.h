@@ -202,9 +202,13 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
  *           CTAs (2 or 4 with block_n 128; 2, 4 or 8 with block_n 256; default block_n
  *           128, 256 for 8) that add their partial sums through distributed shared
  *           memory in the order of the two-launch split-K form (bit-identical to it), each
- *           CTA running the neuron on block_n / splits channels: one launch, no workspace.
+ *           CTA running the neuron on block_n / splits channels: one launch, no workspace;
+ *           7 = as 3 with ONE band copy per stage (W in {8, 16, 32}): each tap row's three
+ *           column taps run as one MMA of N = 3 * block_n into three accumulators that the
+ *           epilogue adds shifted by one column (9 * ceil(Cin/64) * block_n <= 1280).
  * block_n : output channels per CTA (per CTA pair for variant 5), 0 = choose, or 32 / 64 /
- *           128 (dividing Cout), or 256 with variants 2 and 5; 32 / 64 with variant 3.
+ *           128 (dividing Cout), or 256 with variants 2 and 5; 32 / 64 with variants 3
+ *           and 7.
  * splits  : 1, or 2..8 k-range splits for small layers (variant 2): each split's float32
  *           partial sums go to `workspace` (caller-owned, >= snnb_split_workspace_bytes,
  *           16-byte aligned) and a second kernel adds them in a fixed order, adds the bias
