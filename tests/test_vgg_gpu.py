@@ -95,3 +95,19 @@ def test_vgg16_concurrent_chains_equal_one_chain():
     # summation order, may differ): equal up to that
     assert torch.allclose(one, two, rtol=1e-5, atol=1e-5)
     assert torch.equal(one.argmax(-1), two.argmax(-1))
+
+
+def test_vgg16_split_graph_forward_equals_one_graph():
+    """forward(graph=True, mid_event=e): the forward captured as two graphs split before
+    launch mid_at, the event recorded between them; the logits equal the one-graph forward
+    (the same launches) and the event completes."""
+    P = OP.vgg16_params(1)
+    eng = _engine(P)
+    img = torch.rand(1, 64, 3, 32, 32, generator=OP.gen(5)).to(DEV)
+    one = eng.forward(img, graph=True).clone()
+    ev = torch.cuda.Event()
+    two = eng.forward(img, graph=True, mid_event=ev, mid_at=4).clone()
+    torch.cuda.synchronize()
+    assert ev.query()
+    assert torch.equal(one, two)
+    assert eng.graph_input(tuple(img.shape), mid_at=4) is not None

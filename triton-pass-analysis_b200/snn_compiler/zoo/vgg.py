@@ -341,7 +341,8 @@ class SpikingVGG:
 
     def forward(self, img: torch.Tensor, *, per_step_logits: bool = False,
                 out: torch.Tensor | None = None, graph: bool = False,
-                check: bool | None = None) -> torch.Tensor:
+                check: bool | None = None, mid_event: torch.cuda.Event | None = None,
+                mid_at: int = 4) -> torch.Tensor:
         """img [B, 3, H, W] (direct encoding: the same image at every step) or
         [Ti, B, 3, H, W] f32 -> logits averaged over T [B, classes] (or [T, B, classes]).
 
@@ -351,26 +352,37 @@ class SpikingVGG:
                 input buffer, ``graph_input``) -- one graph launch instead of ~16 launches.
         check : read the device status word after the forward (a stream synchronisation)
                 and raise SnnbError if a kernel's bounded wait gave up; defaults to the
-                engine's ``check_status``."""
+                engine's ``check_status``.
+        mid_event : (graph=True, one chain) the forward is captured as two graphs split
+                before launch ``mid_at`` and this event is recorded between their replays,
+                so that other work (a collective) can start once the first ``mid_at``
+                launches -- VGG16's full-grid image and band layers -- are done and run beside
+                the later layers, whose grids leave SMs free."""
         if img.ndim == 4:
             img = img.unsqueeze(0)
         img = img.to(self.device, torch.float32)
         if not img.is_contiguous():
             img = img.contiguous()
         if graph:
-            key = (tuple(img.shape), per_step_logits, None if out is None else out.data_ptr())
+            split = mid_at if mid_event is not None else None
+            key = (tuple(img.shape), per_step_logits, None if out is None else out.data_ptr(),
+                   split)
             ent = self._graph_cache.get(key)
             if ent is None:
                 static_in = torch.empty_like(img)          # the engine's own input buffer
                 static_in.copy_(img)
-                graphs, o = self._capture_graphs(static_in, per_step_logits, out)
+                graphs, o = self._capture_graphs(static_in, per_step_logits, out, split)
                 ent = (static_in, graphs, o)
                 self._graph_cache[key] = ent
             static_in, graphs, o = ent
             if img.data_ptr() != static_in.data_ptr():
                 static_in.copy_(img, non_blocking=True)
-            for g in graphs:
+            for gi, g in enumerate(graphs):
+                if gi == 1 and mid_event is not None:
+                    mid_event.record()
                 g.replay()
+            if len(graphs) == 1 and mid_event is not None:
+                mid_event.record()
         else:
             steps, o = self.plan(img, per_step_logits=per_step_logits, out=out)
             for _, _, fn in steps:
@@ -379,19 +391,32 @@ class SpikingVGG:
             KC.raise_on_device_status("SpikingVGG.forward")
         return o
 
-    def graph_input(self, shape, *, per_step_logits: bool = False, out=None):
+    def graph_input(self, shape, *, per_step_logits: bool = False, out=None,
+                    mid_at: int | None = None):
         """The input buffer of the graph forward(graph=True) replays for this input shape
-        and ``out`` (a caller that writes its input there saves the copy), or None."""
-        key = (tuple(shape), per_step_logits, None if out is None else out.data_ptr())
+        and ``out`` (and ``mid_at`` when it was called with a mid_event) -- a caller that
+        writes its input there saves the copy -- or None."""
+        key = (tuple(shape), per_step_logits, None if out is None else out.data_ptr(), mid_at)
         ent = self._graph_cache.get(key)
         return None if ent is None else ent[0]
 
-    def _capture_graphs(self, img, per_step_logits, out):
+    def _capture_graphs(self, img, per_step_logits, out, split=None):
         parts, o = self._chain_plans(img, out, per_step_logits)
         for steps, _, _ in parts:         # warm up (tunes the layers, sets kernel attributes)
             for _, _, fn in steps:
                 fn()
         torch.cuda.synchronize()
+        if split is not None and len(parts) == 1 and 0 < split < len(parts[0][0]):
+            steps = parts[0][0]
+            graphs = []
+            for grp in (steps[:split], steps[split:]):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=self._fwd_pool):
+                    for _, _, fn in grp:
+                        fn()
+                graphs.append(g)
+            torch.cuda.synchronize()
+            return graphs, o
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=self._fwd_pool):
             self._record_chains(parts)
