@@ -640,7 +640,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
         uint32_t it = 0, failed = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_band(tile, p, BN);
-            float bias[32 * NCS];
+            // channel pairs: the neuron runs on packed f32x2 operations (each component
+            // rounded as the scalar operation: the same values, half the instructions)
+            float2 bias2[16 * NCS];
 #pragma unroll
             for (int cs = 0; cs < NCS; ++cs) {
                 const int c = set + 2 * cs;
@@ -648,13 +650,14 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float4 b4 = c < NCH ? __ldg(bias4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    bias[32 * cs + 4 * j] = b4.x; bias[32 * cs + 4 * j + 1] = b4.y;
-                    bias[32 * cs + 4 * j + 2] = b4.z; bias[32 * cs + 4 * j + 3] = b4.w;
+                    bias2[16 * cs + 2 * j] = make_float2(b4.x, b4.y);
+                    bias2[16 * cs + 2 * j + 1] = make_float2(b4.z, b4.w);
                 }
             }
-            float v[32 * NCS];
+            float2 v2[16 * NCS];
 #pragma unroll
-            for (int j = 0; j < 32 * NCS; ++j) v[j] = 0.0f;
+            for (int j = 0; j < 16 * NCS; ++j) v2[j] = make_float2(0.0f, 0.0f);
+            const float2 df2 = make_float2(p.df, p.df), sc2 = make_float2(p.sc, p.sc);
             const int hy = tl.h0 + y;                         // image row of this pixel
             for (int t = 0; t < p.T; ++t, ++it) {
                 const int a = it & 1;
@@ -670,6 +673,9 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     float r[32];
                     tc::tmem_ld32(tbase + (XS ? BN : 0) + c * 32, r);
                     tc::tmem_wait_ld();
+                    float2 r2[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) r2[j] = make_float2(r[2 * j], r[2 * j + 1]);
                     if constexpr (XS) {
                         // out[m] = D_1[m] + D_0[m - 1] + D_2[m + 1] within the image row
                         // (W lanes; W <= 32 divides the warp)
@@ -677,27 +683,34 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                         tc::tmem_ld32(tbase + c * 32, e);
                         tc::tmem_wait_ld();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float u = __shfl_up_sync(0xffffffffu, e[j], 1, W);
-                            r[j] = __fadd_rn(r[j], x > 0 ? u : 0.0f);
+                        for (int j = 0; j < 16; ++j) {
+                            const float u0 = __shfl_up_sync(0xffffffffu, e[2 * j], 1, W);
+                            const float u1 = __shfl_up_sync(0xffffffffu, e[2 * j + 1], 1, W);
+                            r2[j] = __fadd2_rn(r2[j], x > 0 ? make_float2(u0, u1)
+                                                            : make_float2(0.0f, 0.0f));
                         }
                         tc::tmem_ld32(tbase + 2 * BN + c * 32, e);
                         tc::tmem_wait_ld();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float d = __shfl_down_sync(0xffffffffu, e[j], 1, W);
-                            r[j] = __fadd_rn(r[j], x < W - 1 ? d : 0.0f);
+                        for (int j = 0; j < 16; ++j) {
+                            const float d0 = __shfl_down_sync(0xffffffffu, e[2 * j], 1, W);
+                            const float d1 = __shfl_down_sync(0xffffffffu, e[2 * j + 1], 1, W);
+                            r2[j] = __fadd2_rn(r2[j], x < W - 1 ? make_float2(d0, d1)
+                                                                : make_float2(0.0f, 0.0f));
                         }
                     }
                     uint32_t mask = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float in = __fadd_rn(r[j], bias[32 * cs + j]);
-                        float vv = charge(v[32 * cs + j], p.df, p.sc, in);
-                        const bool s = vv >= p.thr;
-                        vv = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                        v[32 * cs + j] = vv;
-                        mask |= (s ? 1u : 0u) << j;
+                    for (int j = 0; j < 16; ++j) {
+                        // charge(): decay * v + input_scale * (acc + bias), each rounded
+                        const float2 in2 = __fadd2_rn(r2[j], bias2[16 * cs + j]);
+                        const float2 vv = __fadd2_rn(__fmul2_rn(df2, v2[16 * cs + j]),
+                                                     __fmul2_rn(sc2, in2));
+                        const bool s0 = vv.x >= p.thr, s1 = vv.y >= p.thr;
+                        v2[16 * cs + j] = make_float2(reset_v<HARD>(vv.x, s0, p.thr, p.v_reset),
+                                                      reset_v<HARD>(vv.y, s1, p.thr, p.v_reset));
+                        mask |= (s0 ? 1u : 0u) << (2 * j);
+                        mask |= (s1 ? 1u : 0u) << (2 * j + 1);
                     }
                     mk[cs] = mask;
                 }
