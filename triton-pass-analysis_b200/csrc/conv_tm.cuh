@@ -767,34 +767,48 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 transpose(r);
                 const int ch0 = c * 32 + set * HC + kq * NPT;        // column within the block
                 uint32_t lb = 0;                    // bit t * NPT + e
+                // column pairs on packed f32x2 operations (each component rounded as the
+                // scalar operation: the same values, half the instructions)
                 auto lif_cols = [&](auto with_res) {
                     constexpr bool WITH_RES = decltype(with_res)::value;
-                    float in[TS][NPT], v[NPT];
+                    constexpr int NP2 = NPT / 2;
+                    static_assert(NPT % 2 == 0, "column pairs");
+                    const float2 df2 = make_float2(p.df, p.df), sc2 = make_float2(p.sc, p.sc);
+                    float2 in[TS][NP2], v[NP2];
 #pragma unroll
-                    for (int e = 0; e < NPT; ++e) {
-                        const float bb = sbias[ch0 + e];
-                        v[e] = 0.0f;
+                    for (int e = 0; e < NP2; ++e) {
+                        const float2 bb = *reinterpret_cast<const float2*>(sbias + ch0 + 2 * e);
+                        v[e] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                        for (int t = 0; t < TS; ++t) in[t][e] = __fadd_rn(r[t * NPT + e], bb);
+                        for (int t = 0; t < TS; ++t)
+                            in[t][e] = __fadd2_rn(make_float2(r[t * NPT + 2 * e],
+                                                              r[t * NPT + 2 * e + 1]), bb);
                     }
                     if constexpr (WITH_RES) {
                         if (inside) {
 #pragma unroll
                             for (int t = 0; t < TS; ++t)
 #pragma unroll
-                                for (int e = 0; e < NPT; ++e)
-                                    in[t][e] = __fadd_rn(in[t][e], load_res1(p, res_index(
-                                        p, t, on, oh, ow, tl.n0 + ch0 + e)));
+                                for (int e = 0; e < NP2; ++e) {
+                                    in[t][e].x = __fadd_rn(in[t][e].x, load_res1(p, res_index(
+                                        p, t, on, oh, ow, tl.n0 + ch0 + 2 * e)));
+                                    in[t][e].y = __fadd_rn(in[t][e].y, load_res1(p, res_index(
+                                        p, t, on, oh, ow, tl.n0 + ch0 + 2 * e + 1)));
+                                }
                         }
                     }
 #pragma unroll
                     for (int t = 0; t < TS; ++t) {
 #pragma unroll
-                        for (int e = 0; e < NPT; ++e) {
-                            float vv = charge(v[e], p.df, p.sc, in[t][e]);
-                            const bool s = vv >= p.thr;
-                            v[e] = reset_v<HARD>(vv, s, p.thr, p.v_reset);
-                            lb |= (s ? 1u : 0u) << (t * NPT + e);
+                        for (int e = 0; e < NP2; ++e) {
+                            // charge(): decay * v + input_scale * in, each product rounded
+                            const float2 vv = __fadd2_rn(__fmul2_rn(df2, v[e]),
+                                                         __fmul2_rn(sc2, in[t][e]));
+                            const bool s0 = vv.x >= p.thr, s1 = vv.y >= p.thr;
+                            v[e] = make_float2(reset_v<HARD>(vv.x, s0, p.thr, p.v_reset),
+                                               reset_v<HARD>(vv.y, s1, p.thr, p.v_reset));
+                            lb |= (s0 ? 1u : 0u) << (t * NPT + 2 * e);
+                            lb |= (s1 ? 1u : 0u) << (t * NPT + 2 * e + 1);
                         }
                     }
                 };
