@@ -665,6 +665,14 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                 tc::tc_fence_after();
                 const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + a * ACC_COLS;
                 uint32_t mk[NCS];
+                // the accumulator goes back to the MMA warp as soon as its last columns are in
+                // registers: the MMAs of step t + 2 then overlap this step's neurons
+                bool released = false;
+                auto release = [&]() {
+                    tc::tc_fence_before();
+                    tc::mbar_arrive(acce_bar(a));
+                    released = true;
+                };
 #pragma unroll
                 for (int cs = 0; cs < NCS; ++cs) {
                     const int c = set + 2 * cs;
@@ -673,6 +681,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     float r[32];
                     tc::tmem_ld32(tbase + (XS ? BN : 0) + c * 32, r);
                     tc::tmem_wait_ld();
+                    if (!XS && cs == NCS - 1) release();
                     float2 r2[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) r2[j] = make_float2(r[2 * j], r[2 * j + 1]);
@@ -691,6 +700,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                         }
                         tc::tmem_ld32(tbase + 2 * BN + c * 32, e);
                         tc::tmem_wait_ld();
+                        if (cs == NCS - 1) release();
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const float d0 = __shfl_down_sync(0xffffffffu, e[2 * j], 1, W);
@@ -714,8 +724,7 @@ conv_lif_band_kernel(const __grid_constant__ CUtensorMap tmA,
                     }
                     mk[cs] = mask;
                 }
-                tc::tc_fence_before();
-                tc::mbar_arrive(acce_bar(a));
+                if (!released) release();                     // (a set without a last slice)
                 if (set >= NCH) continue;                     // no slice for this set (BN 32)
                 const int64_t frame = (int64_t)t * p.B + tl.img0;
                 if (!p.pool) {
