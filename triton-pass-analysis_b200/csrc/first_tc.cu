@@ -22,9 +22,10 @@
 //   - warps 0-3 build the A tile of their next tile -- thread = pixel: the K0 input values of
 //     its 3x3 window (zeros outside the image; the loads are issued before the wait for a
 //     free stage), split into terms two values at a time (bf16x2 conversions) and written as
-//     16-byte chunks in the 128-byte-swizzled K-major layout the MMA descriptor reads -- and
-//     warp 0's elected lane issues the MMAs (M = 128, N = Cout, K = 16) into the stage's
-//     accumulator and commits them to the stage's full barrier;
+//     16-byte chunks in the 128-byte-swizzled K-major layout the MMA descriptor reads;
+//   - warp 12's elected lane, once a stage's A tile is written and its accumulator free,
+//     issues the MMAs (M = 128, N = Cout, K = 16) into it and commits them to the stage's
+//     full barrier (a warp of its own: the builders go on to their next tile at once);
 //   - warps 4-11 (TMEM lane quadrant = warp % 4, two sets taking the two 32-channel
 //     halves of each 64-channel panel) read the accumulator, free the stage on its empty
 //     barrier and run bias + the T steps of the neuron; each compare yields its spike's
@@ -44,7 +45,7 @@ int sm_count();
 
 namespace {
 
-constexpr int FT_THREADS = 384;     // warps 0-3 build A / issue MMAs, 4-11 run the neuron
+constexpr int FT_THREADS = 416;     // warps 0-3 build A, 4-11 run the neuron, 12 issues MMAs
 constexpr int FT_STAGES = 2;
 
 template <int CIN, int KP, int COUT>
@@ -61,8 +62,9 @@ struct FirstTcSmem {
     static constexpr int STG_OFF = B_OFF + SLABS * B_SLAB;
     // staging buffers per neuron warp: 4 where they fit, else 2
     static constexpr int NSTG = STG_OFF + 8 * 4 * STG_BYTES + 64 + 1024 <= 227 * 1024 ? 4 : 2;
-    static constexpr int BAR_OFF = STG_OFF + 8 * NSTG * STG_BYTES;  // full[], empty[], weights
-    static constexpr int TMEM_OFF = BAR_OFF + 16 * FT_STAGES + 8;
+    // barriers: full[FT_STAGES], empty[FT_STAGES], weights, afull[FT_STAGES]
+    static constexpr int BAR_OFF = STG_OFF + 8 * NSTG * STG_BYTES;
+    static constexpr int TMEM_OFF = BAR_OFF + 24 * FT_STAGES + 8;
     static constexpr int TOTAL = TMEM_OFF + 8;
     static constexpr int DYN = TOTAL + 1024;              // slack for 1024-byte alignment
     static constexpr uint32_t ACC_COLS = COUT < 32 ? 32 : COUT;
@@ -121,6 +123,7 @@ first_conv_tc_kernel(const __grid_constant__ CUtensorMap tmO, const __grid_const
     const uint32_t full0 = sbase + S::BAR_OFF;             // + 8 * stage
     const uint32_t empty0 = full0 + 8 * FT_STAGES;
     const uint32_t wbar = full0 + 16 * FT_STAGES;          // the weights' TMA loads
+    const uint32_t afull0 = wbar + 8;                       // + 8 * stage: A tile written
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S::TMEM_OFF);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -129,6 +132,7 @@ first_conv_tc_kernel(const __grid_constant__ CUtensorMap tmO, const __grid_const
         for (int s = 0; s < FT_STAGES; ++s) {
             tc::mbar_init(full0 + 8 * s, 1);
             tc::mbar_init(empty0 + 8 * s, 8);             // one arrival per neuron warp
+            tc::mbar_init(afull0 + 8 * s, 1);             // the builders, after their barrier
         }
         tc::mbar_init(wbar, 1);
         tc::fence_mbar_init();
@@ -157,8 +161,8 @@ first_conv_tc_kernel(const __grid_constant__ CUtensorMap tmO, const __grid_const
     const bool narrow = npix < 0x7fffffffll;
 
     if (warp < 4) {
-        // ---- A builders; warp 0's elected lane issues the MMAs ----
-        uint32_t failed = 0, committed = 0, last_bar = 0, last_par = 0, wready = 0;
+        // ---- A builders ----
+        uint32_t failed = 0;
         auto load = [&](int64_t t, float (&v)[G]) {
             if (narrow) load_window<CIN, uint32_t>(x, t * 128 + tid, npix, H, W, v);
             else load_window<CIN, int64_t>(x, t * 128 + tid, npix, H, W, v);
@@ -214,43 +218,49 @@ first_conv_tc_kernel(const __grid_constant__ CUtensorMap tmO, const __grid_const
                 failed = 1;
                 break;
             }
-            if (warp == 0) {
-                // the weights, before the first MMAs
-                if (!wready) {
-                    if (!tc::mbar_wait_warp(wbar, 0, 0)) failed = 1;
-                    wready = 1;
-                }
-                // stage s's accumulator is free once the neuron warps have read local tile
-                // i - FT_STAGES
-                if (failed || (i >= FT_STAGES && !tc::mbar_wait_warp(empty0 + 8 * s, (u - 1) & 1, 0))) {
-                    failed = 1;                           // the builders abort at the next tile
-                } else {
-                    tc::tc_fence_after();
-                    if (lane == 0) {
-                        constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, COUT);
-                        constexpr int KSTEPS = (6 * G + 15) / 16;    // past 6 * G: all zero
-                        const uint32_t acc = tmem + (uint32_t)s * S::ACC_COLS;
-                        const uint32_t abase = sbase + S::A_OFF + s * S::A_STAGE;
+            // A tile i is written (every builder passed the barrier): the MMA warp may read it
+            if (tid == 0) tc::mbar_arrive(afull0 + 8 * s);
+        }
+        if (failed && lane == 0) atomicExch(status, SNNB_ERR_TIMEOUT);
+    } else if (warp == 12) {
+        // ---- MMA issuer: per local tile, once its A tile is written and its accumulator
+        //      stage is free, KP / 16 MMAs from the elected lane, committed to full[s] ----
+        uint32_t failed = 0, committed = 0, last_bar = 0, last_par = 0;
+        if (!tc::mbar_wait_warp(wbar, 0, 0)) failed = 1;   // the weights
+        int i = 0;
+        for (int64_t tile = blockIdx.x; tile < ntiles && !failed; tile += gridDim.x, ++i) {
+            const int s = i % FT_STAGES;
+            const uint32_t u = (uint32_t)(i / FT_STAGES);
+            if (!tc::mbar_wait_warp(afull0 + 8 * s, u & 1, failed)) failed = 1;
+            // the accumulator stage is free once the neuron warps have read local tile
+            // i - FT_STAGES
+            if (i >= FT_STAGES && !tc::mbar_wait_warp(empty0 + 8 * s, (u - 1) & 1, failed))
+                failed = 1;
+            if (failed) break;
+            tc::tc_fence_after();
+            if (lane == 0) {
+                constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, COUT);
+                constexpr int KSTEPS = (6 * G + 15) / 16;    // past 6 * G: all zero
+                const uint32_t acc = tmem + (uint32_t)s * S::ACC_COLS;
+                const uint32_t abase = sbase + S::A_OFF + s * S::A_STAGE;
 #pragma unroll
-                        for (int ks = 0; ks < KSTEPS; ++ks) {
-                            const int slab = ks >> 2, k = ks & 3;
-                            const uint64_t da = tc::sdesc_k_sw128(abase + slab * S::A_SLAB);
-                            const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + slab * S::B_SLAB);
-                            tc::umma_bf16(acc, da + 2 * k, db + 2 * k, IDESC, ks != 0);
-                        }
-                        tc::umma_commit(full0 + 8 * s);
-                    }
-                    __syncwarp();
-                    committed = 1;
-                    last_bar = full0 + 8 * s;
-                    last_par = u & 1;
+                for (int ks = 0; ks < KSTEPS; ++ks) {
+                    const int slab = ks >> 2, k = ks & 3;
+                    const uint64_t da = tc::sdesc_k_sw128(abase + slab * S::A_SLAB);
+                    const uint64_t db = tc::sdesc_k_sw128(sbase + S::B_OFF + slab * S::B_SLAB);
+                    tc::umma_bf16(acc, da + 2 * k, db + 2 * k, IDESC, ks != 0);
                 }
+                tc::umma_commit(full0 + 8 * s);
             }
+            __syncwarp();
+            committed = 1;
+            last_bar = full0 + 8 * s;
+            last_par = u & 1;
         }
         // the MMAs still in flight (only after an abort) finish before TMEM is freed, and the
         // weight copies before the CTA exits
-        if (warp == 0 && committed) tc::mbar_wait_warp<true>(last_bar, last_par, 0);
-        if (warp == 0) tc::mbar_wait_warp<true>(wbar, 0, 0);
+        if (committed) tc::mbar_wait_warp<true>(last_bar, last_par, 0);
+        tc::mbar_wait_warp<true>(wbar, 0, 0);
         if (failed && lane == 0) atomicExch(status, SNNB_ERR_TIMEOUT);
     } else {
         // ---- neuron warps: TMEM lane quadrant warp % 4, 32-channel slices set, set + 2, ...
