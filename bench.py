@@ -794,7 +794,7 @@ class FirstLayerWorkload:
 
     def cpu_sample(self):
         from oracle import params as OP
-        B, H, C = 2, self.H, self.cin
+        B, H, C = 32, self.H, self.cin
         img = torch.rand(1, B, C, H, H, generator=OP.gen(3))
         w = torch.randn(self.cout, C, 3, 3, generator=OP.gen(1)) * (2.0 / (9 * C)) ** 0.5
         b = torch.rand(self.cout, generator=OP.gen(2)) * 0.5 + 0.2
