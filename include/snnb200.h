@@ -174,6 +174,15 @@ int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int64_t M, int6
                int64_t K, int64_t ldw, int mode, int splits, snnb_stream_t stream);
 
 /*
+ * Measurement helper (no reference counterpart): the binary GEMM's inner operation at this
+ * GPU's peak -- `blocks` CTAs of 256 threads, each thread `iters` rounds of 64 independent
+ * word-ops acc += popc(a & b) on registers, i.e. blocks * 256 * iters * 64 word-ops per
+ * launch; time it to get the roofline denominator of snnb_bgemm.  sink: >= 1 KB of device
+ * memory (written only in a case that does not occur).
+ */
+int snnb_popc_peak(int64_t blocks, int iters, void* sink, snnb_stream_t stream);
+
+/*
  * K1 -- fused conv3x3 (stride 1, pad 1) + folded-BN bias + multi-step LIF (+ 2x2 max-pool)
  * on the tcgen05 tensor cores (bf16 x bf16 -> f32 in TMEM, operands fed by TMA).
  *

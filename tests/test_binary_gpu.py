@@ -76,3 +76,15 @@ def test_bgemm_baseline_shapes_checksums(MKN):
     ni = torch.randint(0, N, (4096,), generator=g)
     ref = (A[mi].long() * Bpm[:, ni].t()).sum(1)
     assert torch.equal(C[mi.to(DEV), ni.to(DEV)].cpu().long(), ref)
+
+
+def test_popc_peak_helper_runs_and_leaves_sink():
+    """snnb_popc_peak (the binary GEMM's roofline denominator) launches, reports success and
+    never writes its sink (the sum it guards against does not occur)."""
+    from snn_compiler import _lib
+    sink = torch.full((256,), 7, dtype=torch.int32, device=DEV)
+    L = _lib.lib()
+    _lib.check(L.snnb_popc_peak(8, 16, _lib.ptr(sink), _lib.stream_of(sink)), "snnb_popc_peak")
+    torch.cuda.synchronize()
+    assert torch.all(sink == 7)
+    assert L.snnb_popc_peak(0, 16, _lib.ptr(sink), _lib.stream_of(sink)) == -1

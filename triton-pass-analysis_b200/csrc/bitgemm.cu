@@ -211,6 +211,41 @@ __global__ void __launch_bounds__(256) bitpack_kernel(const T* __restrict__ x, i
     out[gid] = word;
 }
 
+// Peak of the binary GEMM's inner operation on this GPU, for its roofline: every thread
+// runs `iters` rounds of 64 independent word-ops -- acc += popc(a & b), the AND, POPC and
+// add of bgemm_kernel's inner product -- on register operands.  The AND and the popcount
+// are volatile asm, so the compiler can neither hoist the loop-invariant products out of
+// the loop nor drop them.  The sum is written only if it equals a value it never takes.
+constexpr int POPC_PEAK_THREADS = 256;
+
+__global__ void __launch_bounds__(POPC_PEAK_THREADS) popc_peak_kernel(int iters, uint32_t* sink) {
+    uint32_t a[8], b[8], acc[8][8];
+    const uint32_t s = blockIdx.x * 7919u + threadIdx.x * 104729u + 12345u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        a[i] = s * (2u * i + 1u) + 0x9E3779B9u * i;
+        b[i] = (~s) * (2u * i + 3u) ^ (0x85EBCA6Bu * i);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0u;
+    }
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t t;
+                asm volatile("and.b32 %0, %1, %2;\n\tpopc.b32 %0, %0;" : "=r"(t) : "r"(a[i]), "r"(b[j]));
+                acc[i][j] += t;
+            }
+    }
+    uint32_t r = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r += acc[i][j] * (uint32_t)(i * 8 + j + 1);
+    if (r == 0x9E3779B9u) sink[threadIdx.x] = r;
+}
+
 }  // namespace
 }  // namespace snnb
 
@@ -274,4 +309,12 @@ extern "C" int snnb_bgemm(const uint32_t* A, const uint32_t* B, int32_t* C, int6
             return launch_k(bgemm_kernel<2>, grid, dim3(THREADS), SMEM_BYTES, s, A, B, C, M, N, ldw, K, wps, atomic);
     }
     return launch_status();
+}
+
+extern "C" int snnb_popc_peak(int64_t blocks, int iters, void* sink, snnb_stream_t stream) {
+    if (const int inj = snnb::take_injected_status()) return inj;
+    if (blocks <= 0 || blocks > 0x7fffffff || iters <= 0 || !sink) return SNNB_ERR_ARG;
+    return snnb::launch_k(snnb::popc_peak_kernel, dim3((unsigned)blocks),
+                          dim3(snnb::POPC_PEAK_THREADS), 0, static_cast<cudaStream_t>(stream),
+                          iters, static_cast<uint32_t*>(sink));
 }

@@ -187,15 +187,6 @@ __device__ __forceinline__ void split2_bf16x3(float a0, float a1, uint32_t& h, u
     }
 }
 
-// One 32-byte store (sm_100's 256-bit vector store): whole sectors from one lane.  The
-// address must be 32-byte aligned.
-__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[16], int o) {
-    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p),
-                 "r"(w[o]), "r"(w[o + 1]), "r"(w[o + 2]), "r"(w[o + 3]), "r"(w[o + 4]),
-                 "r"(w[o + 5]), "r"(w[o + 6]), "r"(w[o + 7])
-                 : "memory");
-}
-
 // 8 spike bits -> 8 bf16 values (0.0 / 1.0) packed in 16 bytes, bit i -> element i.
 __device__ __forceinline__ uint4 spikes_to_bf16x8(uint32_t bits8) {
     uint32_t w[4];

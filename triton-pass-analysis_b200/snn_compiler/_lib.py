@@ -34,6 +34,7 @@ SIGNATURES = {
                              P, P, P],
     "snnb_bitpack": [P, I32, I64, I64, I64, I32, P, P],
     "snnb_bgemm": [P, P, P, I64, I64, I64, I64, I32, I32, P],
+    "snnb_popc_peak": [I64, I32, P, P],
     "snnb_conv3x3_lif": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32,
                          I32, P, I64, P, P],
     "snnb_conv3x3_lif_res": [P, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, P, I32, I32,
