@@ -7,8 +7,9 @@ fused_bias_if_lif, kernels/fused.py:50-114):
     y = conv2d(x, W', stride, padding);  in = (y + b') (+ residual);  LIF / IF over T
 
 W' / b' are the module's folded weights (fold_conv_bn, fused.py:585-599).  The reference
-convolves in the input's dtype: on a bf16 input a tensor-core conv (3x3 / stride 1 /
-padding 1, Cin % 8 == 0, Cout % 32 == 0) has bf16 operands, so the oracle rounds W' to bf16
+convolves in the input's dtype: on a bf16 input a tensor-core conv (3x3 / padding 1 or
+1x1 / padding 0, stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0) has bf16 operands, so the
+oracle rounds W' to bf16
 for it (the products are then exact and only the float32 summation order differs); on a
 float32 input the conv is float32 and W' is kept as is.  The block structure follows
 snn_compiler/zoo/resnet.py:30-117 and zoo/sew_resnet.py:44-131.
@@ -26,10 +27,13 @@ def _pair(v):
 
 
 def tensor_core_conv(weight, stride, padding, dilation=1, groups=1) -> bool:
+    """The geometries the library runs on its tensor-core conv kernels: 3x3 / padding 1 or
+    1x1 / padding 0, stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0."""
     cout, cin = weight.shape[0], weight.shape[1]
-    return (tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1)
-            and _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1
-            and cin % 8 == 0 and cout % 32 == 0)
+    ks = tuple(weight.shape[2:])
+    return (ks in ((3, 3), (1, 1)) and _pair(stride) in ((1, 1), (2, 2))
+            and _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1)
+            and groups == 1 and cin % 8 == 0 and cout % 32 == 0)
 
 
 def conv_bn_neuron(x_seq, weight, bias, *, stride, padding, neuron="lif", tau=2.0, decay=None,
@@ -53,6 +57,19 @@ def conv_bn_neuron(x_seq, weight, bias, *, stride, padding, neuron="lif", tau=2.
     shape = y.shape
     return (torch.from_numpy(r["spikes"]).reshape(shape),
             torch.from_numpy(r["vpre"]).reshape(shape))
+
+
+def conv_bias(x_seq, weight, bias, *, stride, padding):
+    """Conv + folded-BN bias with no neuron (a ResNet block's downsample branch,
+    snn_compiler/zoo/resnet.py:139-142) in float32: x_seq [T, B, Cin, H, W] (CPU) ->
+    [T, B, Cout, Ho, Wo]; bf16-rounded weights on a bf16 input, as conv_bn_neuron."""
+    T, B = x_seq.shape[:2]
+    w = weight.detach().float().cpu()
+    if x_seq.dtype == torch.bfloat16 and tensor_core_conv(w, stride, padding):
+        w = w.to(torch.bfloat16).float()
+    y = F.conv2d(x_seq.reshape(T * B, *x_seq.shape[2:]).float(), w,
+                 bias.detach().float().cpu(), stride=stride, padding=padding)
+    return y.reshape(T, B, *y.shape[1:])
 
 
 def fused_module_oracle(mod, x_seq, residual=None):

@@ -80,3 +80,31 @@ def test_split_workspace_size_overflow_is_rejected():
         None, big, big, big, big, 64, None, None, big, 0.5, 0.5, 1.0, 0.0, 1, 0, 0, 8, None,
         None)
     assert st == -1
+
+
+def test_strided_conv_entries_reject_bad_geometry_without_a_device():
+    """Kernel sizes other than 1 / 3, strides other than 1 / 2, a missing input and
+    oversized dimensions come back SNNB_ERR_ARG before any device work."""
+    from snn_compiler import _lib
+    L = _lib.lib()
+
+    def strided(**kw):
+        a = dict(x=None, T=4, B=2, H=8, W=8, Cin=64, w=None, b=None, Cout=64, k=3, s=2,
+                 df=0.5, sc=0.5, thr=1.0, vr=0.0, hard=1, res=None, rdt=0, v=0, bn=0, sp=1,
+                 ws=None, wsb=0, out=None, st=None)
+        a.update(kw)
+        return L.snnb_conv_lif_strided(*a.values())
+
+    def f32(**kw):
+        a = dict(x=None, T=4, B=2, H=8, W=8, Cin=64, w=None, b=None, Cout=64, k=1, s=2,
+                 out=None, st=None)
+        a.update(kw)
+        return L.snnb_conv_f32(*a.values())
+    for call in (strided, f32):
+        assert call(k=5) == -1
+        assert call(k=2) == -1
+        assert call(s=3) == -1
+        assert call(s=0) == -1
+        assert call() == -1                       # no input / weight / output pointers
+        assert call(T=1 << 40) == -1
+    assert strided(res=ctypes.c_void_p(16), rdt=7) == -1     # unknown residual dtype

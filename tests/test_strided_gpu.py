@@ -1,0 +1,160 @@
+"""Strided and 1x1 convs on the tensor-core kernels (snnb_conv_lif_strided, snnb_conv_f32):
+the convs of a spiking ResNet that are not 3x3 / stride 1 -- the first conv of a
+downsampling BasicBlock (3x3 / stride 2), pointwise convs and the downsample branch
+(1x1 / stride 2 + folded BN, float32 result) -- against the CPU oracle
+(oracle/resnet.py, restating snn_compiler/nn/modules.py:258-443 and
+snn_compiler/zoo/resnet.py:30-142)."""
+import pytest
+import torch
+
+from oracle import resnet as OR
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+THR = 1.0
+
+
+def _spikes(shape, p, g):
+    return (torch.rand(*shape, generator=g) < p).float()
+
+
+def _weights(cout, cin, k, g, gain=1.0):
+    return torch.randn(cout, cin, k, k, generator=g) * gain * (2.0 / (k * k * cin)) ** 0.5
+
+
+def _flip_ok(got, ref, vpre):
+    """BASELINE's criterion: every disagreement at a neuron within 1e-4 of the threshold,
+    and at most 0.1% of the elements."""
+    bad = got != ref
+    near = (vpre - THR).abs() < 1e-4
+    return not (bad & ~near).any() and bad.float().mean().item() <= 1e-3
+
+
+GEOMS = [  # (k, stride, H, W, Cin, Cout)
+    (3, 2, 16, 16, 64, 128),
+    (3, 2, 15, 13, 64, 64),       # odd sizes: the last output row / column reads padding
+    (3, 2, 8, 8, 128, 256),
+    (1, 2, 16, 16, 64, 128),
+    (1, 2, 7, 9, 64, 64),
+    (1, 1, 8, 8, 128, 64),
+    (3, 1, 8, 8, 64, 64),         # the stride-1 3x3 conv through the same entry
+]
+SCHEDS = [(0, 0, 1), (1, 64, 1), (1, 32, 1), (2, 128, 1), (2, 64, 2), (4, 64, 1), (5, 128, 1),
+          (6, 128, 2)]
+
+
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("sched", SCHEDS)
+@pytest.mark.parametrize("geom", GEOMS)
+def test_strided_conv_lif_against_oracle(geom, sched, residual):
+    from snn_compiler.kernels import conv as C
+    k, stride, H, W, Cin, Cout = geom
+    variant, block_n, splits = sched
+    kslabs = k * k * ((Cin + 63) // 64)
+    if block_n and Cout % block_n or splits > kslabs // 2 and splits > 1:
+        pytest.skip("schedule does not apply to this geometry")
+    if residual and variant in (4, 5):
+        pytest.skip("no residual input in this variant")
+    T, B = 4, 4
+    g = torch.Generator().manual_seed(hash(geom) % 1000 + 7 * variant + block_n + splits)
+    x = _spikes((T, B, Cin, H, W), 0.2, g)
+    w = _weights(Cout, Cin, k, g, gain=1.5)
+    b = torch.rand(Cout, generator=g) * 0.4
+    Ho, Wo = (H - 1) // stride + 1, (W - 1) // stride + 1
+    res = torch.randn(T, B, Cout, Ho, Wo, generator=g) * 0.5 if residual else None
+    xd = x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV)
+    rd = None if res is None else res.permute(0, 1, 3, 4, 2).contiguous().to(DEV)
+    y = C.conv_lif_strided(xd, C.weight_khwc(w).to(DEV), b.to(DEV), stride=stride, tau=2.0,
+                           v_threshold=THR, variant=variant, block_n=block_n, splits=splits,
+                           residual=rd)
+    assert C.device_status() == 0
+    assert tuple(y.shape) == (T, B, Ho, Wo, Cout)
+    ref, vpre = OR.conv_bn_neuron(x.to(torch.bfloat16), w, b, stride=stride, padding=k // 2,
+                                  residual=res)
+    got = y.float().cpu().permute(0, 1, 4, 2, 3)
+    assert ref.sum() > 0 and ref.mean() < 0.9, "degenerate case"
+    assert _flip_ok(got, ref, vpre)
+
+
+@pytest.mark.parametrize("geom", [(1, 2, 16, 16, 64, 128), (1, 2, 7, 9, 64, 64),
+                                  (3, 2, 8, 8, 64, 128), (1, 1, 8, 8, 128, 64)])
+@pytest.mark.parametrize("T", [2, 4])
+def test_conv_f32_against_oracle(geom, T):
+    """The float32 conv + bias (no neuron) against the oracle's float32 conv: the products of
+    spikes and bf16 weights are exact, so only the summation order differs."""
+    from snn_compiler.kernels import conv as C
+    k, stride, H, W, Cin, Cout = geom
+    B = 3
+    g = torch.Generator().manual_seed(sum(geom) + T)
+    x = _spikes((T, B, Cin, H, W), 0.3, g)
+    w = _weights(Cout, Cin, k, g)
+    b = torch.randn(Cout, generator=g) * 0.1
+    y = C.conv_f32(x.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16).to(DEV),
+                   C.weight_khwc(w).to(DEV), b.to(DEV), stride=stride)
+    ref = OR.conv_bias(x.to(torch.bfloat16), w, b, stride=stride, padding=k // 2)
+    got = y.cpu().permute(0, 1, 4, 2, 3)
+    assert got.shape == ref.shape
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_strided_entry_rejects_band_variants_and_bad_strides():
+    from snn_compiler.kernels import conv as C
+    x = torch.zeros(4, 2, 16, 16, 64, device=DEV, dtype=torch.bfloat16)
+    w = torch.zeros(64, 3, 3, 64, device=DEV, dtype=torch.bfloat16)
+    b = torch.zeros(64, device=DEV)
+    for variant in (3, 7):          # the band kernels take stride-1 3x3 convs only
+        with pytest.raises(RuntimeError):
+            C.conv_lif_strided(x, w, b, stride=2, variant=variant, block_n=64)
+    with pytest.raises(AssertionError):
+        C.conv_lif_strided(x, w, b, stride=3)
+
+
+def test_resnet_block_with_downsample_bf16_on_the_kernels():
+    """A downsampling BasicBlock (3x3 / stride 2 conv, 1x1 / stride 2 downsample + BN, 3x3
+    conv + residual) fused and run in bf16: each fused module against the oracle on its own
+    inputs, every one of them on this library's kernels."""
+    from snn_compiler.nn import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron
+    from snn_compiler.zoo.resnet import BasicBlockSNN
+    torch.manual_seed(11)
+    down = torch.nn.Sequential(torch.nn.Conv2d(64, 128, 1, stride=2, bias=False),
+                               torch.nn.BatchNorm2d(128))
+    blk = BasicBlockSNN(64, 128, stride=2, downsample=down, neuron="lif")
+    with torch.no_grad():
+        for mod in blk.modules():
+            if isinstance(mod, torch.nn.Conv2d):
+                mod.weight.mul_(3.0)
+            if isinstance(mod, torch.nn.BatchNorm2d):
+                mod.bias.add_(0.5)
+                mod.running_mean.normal_(0, 0.1)
+                mod.running_var.uniform_(0.5, 1.5)
+    blk = blk.eval().fuse().to(DEV).to(torch.bfloat16)
+    assert isinstance(blk.downsample, FusedConvBN)
+    rec = []
+    hooks = [m.register_forward_hook(
+        lambda m, inp, out: rec.append((m, [i.detach().cpu() for i in inp], out.detach().cpu())))
+        for m in blk.modules() if isinstance(m, (FusedConvBN, FusedConvBNNeuron,
+                                                  FusedConvBNAddNeuron))]
+    g = torch.Generator().manual_seed(5)
+    x = _spikes((4, 2, 64, 16, 16), 0.25, g).to(torch.bfloat16).to(DEV)
+    try:
+        with torch.no_grad():
+            y = blk(x)
+    finally:
+        for h in hooks:
+            h.remove()
+    assert y.shape == (4, 2, 128, 8, 8)
+    kinds = set()
+    for mod, inp, out in rec:
+        assert "w" in mod._cache, type(mod).__name__       # ran on the tensor-core kernels
+        kinds.add(type(mod).__name__)
+        if isinstance(mod, FusedConvBN):
+            assert out.dtype == torch.float32
+            ref = OR.conv_bias(inp[0], mod.weight, mod.bias, stride=mod.stride,
+                               padding=mod.padding)
+            torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+            continue
+        res = inp[1] if len(inp) > 1 else None
+        ref, vpre = OR.fused_module_oracle(mod, inp[0], residual=res)
+        assert ref.sum() > 0, type(mod).__name__
+        assert _flip_ok(out.float(), ref, vpre), type(mod).__name__
+    assert kinds == {"FusedConvBN", "FusedConvBNNeuron", "FusedConvBNAddNeuron"}

@@ -203,6 +203,7 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     const int cb = kb - tap * p.cin_blocks;
                     const int r = p.taps == 9 ? tap / 3 : 1;
                     const int s = p.taps == 9 ? tap % 3 : 1;
+                    const int cst = p.stride > 1 ? p.stride : 1;   // the box's traversal stride
                     if (!failed && tc::elect_one()) {
                         tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
@@ -215,7 +216,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     }
                     if (!failed && tc::elect_one())
                         tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
-                                        full_bar(stage), cb * 64, tl.w0 + s - 1, tl.h0 + r - 1, f0);
+                                        full_bar(stage), cb * 64, tl.w0 * cst + s - 1,
+                                        tl.h0 * cst + r - 1, f0);
                     __syncwarp();
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     if (!failed) {
@@ -1160,7 +1162,7 @@ int* device_status_ptr() {
 
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                CUtensorMapSwizzle swizzle) {
+                CUtensorMapSwizzle swizzle, const uint32_t* elem_strides) {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
         cudaDriverEntryPointQueryResult q;
@@ -1177,7 +1179,9 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
     for (int i = 0; i < rank; ++i) {
         d[i] = dims[i];
         b[i] = box[i];
-        es[i] = 1;
+        // traversal stride: a box of box[i] elements along dimension i loads every
+        // es[i]-th of them (ceil(box[i] / es[i]) elements)
+        es[i] = elem_strides ? elem_strides[i] : 1;
         if (i < rank - 1) st[i] = strides_bytes[i];
     }
     CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, es,
@@ -1311,9 +1315,28 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  float v_reset, int hard, int pool, int variant, int block_n, int splits,
                  void* workspace, int64_t workspace_bytes, void* out, cudaStream_t s,
                  const void* res = nullptr, int res_f32 = 0, int x_packed = 0,
-                 int out_packed = 0) {
+                 int out_packed = 0, int stride = 1, int f32_out = 0) {
     if (const int inj = take_injected_status()) return inj;
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
+    // stride 2 (3x3 / padding 1 or 1x1 / padding 0): H, W are the input's sizes here and the
+    // output's from the shape checks on, (H - 1) / 2 + 1 x (W - 1) / 2 + 1; the activation
+    // boxes traverse the input with stride 2.  T-sequential and T-folded kernels only.
+    if (stride != 1 && stride != 2) return SNNB_ERR_ARG;
+    if (stride == 2 && (x_packed || out_packed || pool == 2 || variant == 3 || variant == 7))
+        return SNNB_ERR_UNSUPPORTED;
+    // f32_out: no neuron -- out is float32 [T*B, H, W, Cout] = conv + bias (the T-folded
+    // kernel's raw sums, then the bias added in place), e.g. a downsample branch
+    if (f32_out) {
+        if (pool || res || x_packed || out_packed || splits > 1) return SNNB_ERR_UNSUPPORTED;
+        if (variant != 0 && variant != 2) return SNNB_ERR_UNSUPPORTED;
+        variant = 2;
+    }
+    if (H <= 0 || W <= 0) return SNNB_ERR_ARG;
+    const int Hin = H, Win = W;
+    if (stride == 2) {
+        H = (H - 1) / 2 + 1;
+        W = (W - 1) / 2 + 1;
+    }
     // packed spikes in / out: the T-folded kernel (variant 2), one launch (no split-K), no
     // residual; packed input for 3x3 convs with Cin % 64 == 0
     if (x_packed || out_packed) {
@@ -1436,24 +1459,30 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (x_packed) {
         // no activation tensor map: the kernel reads the packed patch itself
     } else if (variant == 2) {
-        // activation map: dims (Cin, T, W, H, B), box (64, T, bw, bh, bn): one box = the
-        // pixel block at every step, rows ordered (pixel, t) -- a pixel's T steps are
-        // adjacent accumulator rows, i.e. adjacent lanes of one epilogue warp
-        const uint64_t adims[5] = {(uint64_t)Cin, (uint64_t)T, (uint64_t)W, (uint64_t)H,
+        // activation map: dims (Cin, T, W, H, B) of the input, box (64, T, bw, bh, bn) of
+        // loaded elements: one box = the pixel block at every step, rows ordered (pixel, t)
+        // -- a pixel's T steps are adjacent accumulator rows, i.e. adjacent lanes of one
+        // epilogue warp.  Stride 2: the box spans 2 bw x 2 bh input pixels, every second one
+        // loaded (traversal stride 2).
+        const uint64_t adims[5] = {(uint64_t)Cin, (uint64_t)T, (uint64_t)Win, (uint64_t)Hin,
                                    (uint64_t)B};
-        const uint64_t astr[4] = {(uint64_t)B * H * W * Cin * 2, (uint64_t)Cin * 2,
-                                  (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
-        const uint32_t abox[5] = {64, (uint32_t)T, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn};
+        const uint64_t astr[4] = {(uint64_t)B * Hin * Win * Cin * 2, (uint64_t)Cin * 2,
+                                  (uint64_t)Win * Cin * 2, (uint64_t)Hin * Win * Cin * 2};
+        const uint32_t abox[5] = {64, (uint32_t)T, (uint32_t)(bw * stride), (uint32_t)(bh * stride),
+                                  (uint32_t)bn};
+        const uint32_t aes[5] = {1, 1, (uint32_t)stride, (uint32_t)stride, 1};
         rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, x, adims, astr, abox,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+                         CU_TENSOR_MAP_SWIZZLE_128B, aes);
     } else {
-        // activation map: dims (Cin, W, H, T*B), box (64, bw, bh, bn)
-        const uint64_t adims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)T * B};
-        const uint64_t astr[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2,
-                                  (uint64_t)H * W * Cin * 2};
-        const uint32_t abox[4] = {64, (uint32_t)bw, (uint32_t)bh, (uint32_t)bn};
+        // activation map: dims (Cin, W, H, T*B) of the input, box (64, bw, bh, bn) of loaded
+        // elements (traversal stride as above)
+        const uint64_t adims[4] = {(uint64_t)Cin, (uint64_t)Win, (uint64_t)Hin, (uint64_t)T * B};
+        const uint64_t astr[3] = {(uint64_t)Cin * 2, (uint64_t)Win * Cin * 2,
+                                  (uint64_t)Hin * Win * Cin * 2};
+        const uint32_t abox[4] = {64, (uint32_t)(bw * stride), (uint32_t)(bh * stride), (uint32_t)bn};
+        const uint32_t aes[4] = {1, (uint32_t)stride, (uint32_t)stride, 1};
         rc = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, adims, astr, abox,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+                         CU_TENSOR_MAP_SWIZZLE_128B, aes);
     }
     if (rc != SNNB_OK) return rc;
     // weight map: dims (Cin, taps, Cout), box (64, 1, BN): channels past Cin read as zero
@@ -1479,6 +1508,11 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     p.out_packed = out_packed ? 1 : 0;
     p.splits = ck ? 1 : splits;
     p.partial = splits > 1 && !ck ? static_cast<float*>(workspace) : nullptr;
+    if (f32_out) {
+        p.out = nullptr;
+        p.partial = static_cast<float*>(out);     // one split: the raw sums are the result
+    }
+    p.stride = stride;
     const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
     p.mtiles = (int)mtiles;
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
@@ -1492,7 +1526,10 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
             case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh, cg); break;
             default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh, cg); break;
         }
-        if (rc != SNNB_OK || splits == 1) return rc;
+        if (rc != SNNB_OK) return rc;
+        if (f32_out)
+            return launch_splitsum(p.partial, 1, (int64_t)T * B * H * W, Cout, bias, s);
+        if (splits == 1) return rc;
         return launch_splitsum_lif(p.partial, splits, T, B, H, W, Cout, bias, df, sc, thr, v_reset,
                                    p.hard, pool, res, res_f32, p.out, s);
     }
@@ -1539,6 +1576,37 @@ extern "C" int snnb_conv3x3_lif_res(const void* x, int64_t T, int64_t B, int64_t
                         input_scale, v_threshold, v_reset, hard_reset, 0, variant, block_n,
                         splits, workspace, workspace_bytes, out, static_cast<cudaStream_t>(stream),
                         residual, residual_dtype == SNNB_F32 ? 1 : 0);
+}
+
+extern "C" int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                                     int64_t Cin, const void* w, const float* bias, int64_t Cout,
+                                     int ksize, int stride, float decay, float input_scale,
+                                     float v_threshold, float v_reset, int hard_reset,
+                                     const void* residual, int residual_dtype, int variant,
+                                     int block_n, int splits, void* workspace,
+                                     int64_t workspace_bytes, void* out, snnb_stream_t stream) {
+    if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
+        Cin > 0x7fffffff || Cout > 0x7fffffff)
+        return SNNB_ERR_ARG;
+    if ((ksize != 1 && ksize != 3) || (stride != 1 && stride != 2)) return SNNB_ERR_ARG;
+    if (residual && residual_dtype != SNNB_BF16 && residual_dtype != SNNB_F32) return SNNB_ERR_ARG;
+    return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout,
+                        ksize * ksize, decay, input_scale, v_threshold, v_reset, hard_reset, 0,
+                        variant, block_n, splits, workspace, workspace_bytes, out,
+                        static_cast<cudaStream_t>(stream), residual,
+                        residual && residual_dtype == SNNB_F32 ? 1 : 0, 0, 0, stride, 0);
+}
+
+extern "C" int snnb_conv_f32(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
+                             int64_t Cin, const void* w, const float* bias, int64_t Cout,
+                             int ksize, int stride, float* out, snnb_stream_t stream) {
+    if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
+        Cin > 0x7fffffff || Cout > 0x7fffffff)
+        return SNNB_ERR_ARG;
+    if ((ksize != 1 && ksize != 3) || (stride != 1 && stride != 2)) return SNNB_ERR_ARG;
+    return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout,
+                        ksize * ksize, 0.0f, 0.0f, 0.0f, 0.0f, 1, 0, 2, 0, 1, nullptr, 0, out,
+                        static_cast<cudaStream_t>(stream), nullptr, 0, 0, 0, stride, 1);
 }
 
 extern "C" int snnb_linear_lif(const void* x, int64_t T, int64_t B, int64_t K, const void* w,

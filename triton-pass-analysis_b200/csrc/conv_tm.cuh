@@ -37,6 +37,10 @@ struct ConvParams {
     int pk_px, pk_ps;             // packed-input patch: words per pixel slot / per step plane
     int stall;                    // test hook (snnb_debug_inject_stall): CTA 0's producer of
                                   // the T-sequential kernel withholds every stage
+    int stride;                   // conv stride (T-sequential and T-folded kernels): output
+                                  // pixel (h, w) reads input (stride*h + dy - 1, stride*w +
+                                  // dx - 1) for 3x3 taps, (stride*h, stride*w) for one tap;
+                                  // H, W above are the OUTPUT sizes.  0 reads as 1.
 };
 
 struct Tile {
@@ -467,6 +471,7 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int cb = kb - tap * p.cin_blocks;
                 const int r = p.taps == 9 ? tap / 3 : 1;
                 const int s = p.taps == 9 ? tap % 3 : 1;
+                const int cst = p.stride > 1 ? p.stride : 1;   // the box's traversal stride
                 // the stage's weight rows first (no kernel writes them), then, once the
                 // previous kernel has completed, its activation box(es)
                 if (!failed && tc::elect_one()) {
@@ -491,14 +496,14 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     if constexpr (PAIR) {
                         const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
                         tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
-                                             cb * 64, 0, tl[0].w0 + s - 1, tl[0].h0 + r - 1,
-                                             tl[0].img0);
+                                             cb * 64, 0, tl[0].w0 * cst + s - 1,
+                                             tl[0].h0 * cst + r - 1, tl[0].img0);
                     } else {
 #pragma unroll
                         for (int h = 0; h < MH; ++h)
                             tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
-                                            &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 + s - 1,
-                                            tl[h].h0 + r - 1, tl[h].img0);
+                                            &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 * cst + s - 1,
+                                            tl[h].h0 * cst + r - 1, tl[h].img0);
                     }
                 }
                 __syncwarp();

@@ -27,9 +27,6 @@
 
 namespace snnb {
 
-int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
-                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                CUtensorMapSwizzle swizzle);
 int* device_status_ptr();
 
 namespace {

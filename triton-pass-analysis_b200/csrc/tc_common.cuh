@@ -510,9 +510,10 @@ __device__ __forceinline__ bool named_bar_any(int id, int threads, bool pred) {
 int* device_status_ptr();
 
 // Host: encode a tiled TMA descriptor (bf16 or f32 elements, 128-byte swizzle,
-// zero fill out of bounds).  Returns SNNB_OK or an error status.
+// zero fill out of bounds; elem_strides: per-dimension traversal strides, nullptr = all 1).
+// Returns SNNB_OK or an error status.
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                CUtensorMapSwizzle swizzle);
+                CUtensorMapSwizzle swizzle, const uint32_t* elem_strides = nullptr);
 
 }  // namespace snnb

@@ -77,6 +77,72 @@ def conv3x3_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron:
     return out
 
 
+def conv_out_size(n: int, stride: int) -> int:
+    """Output size of a 3x3 / padding 1 or 1x1 / padding 0 conv with this stride."""
+    return (n - 1) // stride + 1
+
+
+def conv_lif_strided(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, stride: int = 1,
+                     neuron: str = "lif", tau: float = 2.0, decay=None, decay_input: bool = True,
+                     soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
+                     out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
+                     splits: int = 1, workspace: torch.Tensor | None = None,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k = 3, padding 1, or k = 1,
+    padding 0), stride 1 or 2 -> spikes [T, B, Ho, Wo, Cout] bf16, Ho = (H - 1) // stride + 1
+    (snnb_conv_lif_strided: the strided and 1x1 convs of a spiking ResNet).  residual: None
+    or [T, B, Ho, Wo, Cout] bf16 / float32; variant / block_n / splits as conv3x3_lif
+    (variants 0, 1, 2, 4, 5, 6)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.ndim == 4
+    k = w.shape[1]
+    assert k in (1, 3) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
+    T, B, H, W, Cin = x.shape
+    Cout = w.shape[0]
+    assert w.shape[3] == Cin, (tuple(w.shape), Cin)
+    assert bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == Cout
+    df, sc, thr, vr, hard = _lif_args(neuron, tau, decay, decay_input, soft_reset, v_threshold,
+                                      v_reset)
+    Ho, Wo = conv_out_size(H, stride), conv_out_size(W, stride)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.bfloat16)
+    ws, ws_bytes = _workspace(workspace, 1 if variant == 6 else splits, T, B, Ho, Wo, Cout,
+                              x.device)
+    if residual is not None:
+        assert residual.is_cuda and residual.is_contiguous() and \
+            residual.dtype in (torch.bfloat16, torch.float32) and \
+            tuple(residual.shape) == (T, B, Ho, Wo, Cout), tuple(residual.shape)
+    st = _lib.lib().snnb_conv_lif_strided(
+        _lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w), _lib.ptr(bias), Cout, k, stride, df, sc, thr,
+        vr, hard, _lib.ptr(residual), _lib.dtype_code(residual.dtype) if residual is not None
+        else 0, int(variant), int(block_n), int(splits), _lib.ptr(ws), ws_bytes, _lib.ptr(out),
+        _lib.stream_of(x))
+    _lib.check(st, "snnb_conv_lif_strided")
+    return out
+
+
+def conv_f32(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, stride: int = 1,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k = 1 or 3) -> float32
+    [T, B, Ho, Wo, Cout] = conv + bias, no neuron (snnb_conv_f32: the downsample branch of a
+    spiking ResNet block, BN folded into w and bias); T in {2, 4, 8}."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
+    assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.ndim == 4
+    k = w.shape[1]
+    assert k in (1, 3) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
+    T, B, H, W, Cin = x.shape
+    Cout = w.shape[0]
+    assert w.shape[3] == Cin and bias.dtype == torch.float32 and bias.numel() == Cout
+    Ho, Wo = conv_out_size(H, stride), conv_out_size(W, stride)
+    if out is None:
+        out = torch.empty(T, B, Ho, Wo, Cout, device=x.device, dtype=torch.float32)
+    st = _lib.lib().snnb_conv_f32(_lib.ptr(x), T, B, H, W, Cin, _lib.ptr(w),
+                                  _lib.ptr(bias.contiguous()), Cout, k, stride, _lib.ptr(out),
+                                  _lib.stream_of(x))
+    _lib.check(st, "snnb_conv_f32")
+    return out
+
+
 def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
                tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
                v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,
@@ -621,11 +687,11 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
                 layout: str = "NCHW"):
     """conv + bias + neuron (reference fused.py:513-551) for x_seq [T, B, Cin, H, W].
-    3x3 / stride 1 / padding 1 convs with a scalar threshold run fused on the tcgen05 kernel
-    when Cout % 32 == 0: bf16 operands for a bf16 input (Cin % 8 == 0); for a float32 /
+    3x3 / padding 1 and 1x1 / padding 0 convs of stride 1 or 2 with a scalar threshold run
+    fused on the tcgen05 kernels when Cout % 32 == 0: bf16 operands for a bf16 input (Cin % 8 == 0); for a float32 /
     float16 input (Cin % 4 == 0) float32-faithful, each operand as three bf16 terms (a
     split-terms launch, then the conv over six channel groups); a float32 input with other
-    Cin (the image layer) takes the float32 CUDA-core kernel.  Any other geometry keeps the
+    Cin (the 3x3 / stride 1 image layer) takes the float32 CUDA-core kernel.  Any other geometry keeps the
     reference's two steps: torch's conv in the input's dtype, then the fused neuron kernel."""
     from .fused import fused_bias_if_lif
     Cin, Cout = weight.shape[1], weight.shape[0]
@@ -633,6 +699,19 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
               soft_reset=soft_reset, v_threshold=v_threshold, v_reset=v_reset)
     b = bias.detach().float().contiguous() if bias is not None else \
         torch.zeros(Cout, device=x_seq.device)
+    ks, st = tuple(weight.shape[2:]), _pair(stride)
+    if ks in ((1, 1), (3, 3)) and st in ((1, 1), (2, 2)) and (ks, st) != ((3, 3), (1, 1)) and \
+            _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1) and \
+            groups == 1 and isinstance(v_threshold, (int, float)) and Cout % 32 == 0:
+        # strided 3x3 and 1x1 convs: the same kernels, activation boxes traversing the input
+        # with the stride (snnb_conv_lif_strided)
+        if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0:
+            y = conv_lif_strided(_to_frames(x_seq), weight_khwc(weight), b, stride=st[0], **kw)
+            return _from_frames(y, x_seq.dtype, layout)
+        if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0:
+            y = conv_lif_strided(split_activations(_frames_f32(x_seq)),
+                                 split_weight_khwc(weight), b, stride=st[0], **kw)
+            return _from_frames(y, x_seq.dtype, layout)
     if tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1) and \
             _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1 and \
             isinstance(v_threshold, (int, float)):

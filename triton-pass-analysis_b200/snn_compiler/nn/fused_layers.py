@@ -20,8 +20,13 @@ the route depends on it:
     conv + neuron kernel;
   - linears with out_features % 32 == 0 (in_features % 8 == 0 for bf16, % 4 == 0 for
     float32 / float16, split as above): the fused linear kernel;
-  - the residual form (FusedConvBNAddNeuron) on the first geometry: the same tcgen05 kernel
-    with the residual added in its epilogue (snnb_conv3x3_lif_res);
+  - 3x3 / padding 1 convs of stride 2 and 1x1 / padding 0 convs of stride 1 or 2 (a
+    ResNet's strided and pointwise convs) on the same kernels, the activation boxes
+    traversing the input with the stride (snnb_conv_lif_strided), bf16 or split as above;
+  - the residual form (FusedConvBNAddNeuron) on these geometries: the same tcgen05 kernels
+    with the residual added in the epilogue (snnb_conv3x3_lif_res, snnb_conv_lif_strided);
+  - FusedConvBN (conv + folded BN, no neuron: a ResNet block's downsample branch) on a bf16
+    input: the T-folded kernel with a float32 result (snnb_conv_f32);
   - fold_bn=False and any other conv geometry keep the reference's own two-step structure:
     torch's conv (+ eval BN) followed by the fused neuron kernel (snnb_neuron_multistep),
     exactly as modules.py:324-357 / :415-443 do.
@@ -64,9 +69,11 @@ class _NeuronArgs:
 
 
 def _fused_conv_ok(weight, stride, padding, dilation, groups, v_threshold):
-    return (tuple(weight.shape[2:]) == (3, 3) and _pair(stride) == (1, 1)
-            and _pair(padding) == (1, 1) and _pair(dilation) == (1, 1) and groups == 1
-            and isinstance(v_threshold, (int, float)))
+    """3x3 / padding 1 or 1x1 / padding 0, stride 1 or 2 (the convs of VGG and ResNet)."""
+    ks = tuple(weight.shape[2:])
+    return (ks in ((3, 3), (1, 1)) and _pair(stride) in ((1, 1), (2, 2))
+            and _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1)
+            and groups == 1 and isinstance(v_threshold, (int, float)))
 
 
 def _res_frames(r):
@@ -76,20 +83,24 @@ def _res_frames(r):
     return r.permute(0, 1, 3, 4, 2).to(dt).contiguous()
 
 
-def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None):
-    """Fused conv + bias (+ residual) + neuron for a 3x3 / s1 / p1 conv.  `cache` holds the
-    kernel-layout weights so they are converted once per module, not per call."""
+def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None, stride=1):
+    """Fused conv + bias (+ residual) + neuron for a conv _fused_conv_ok accepts.  `cache`
+    holds the kernel-layout weights so they are converted once per module, not per call."""
     T, B, Cin = x_seq.shape[:3]
     Cout = weight.shape[0]
     b = bias.detach().float().contiguous() if bias is not None else \
         torch.zeros(Cout, device=x_seq.device)
     res = None if residual is None else _res_frames(residual)
+    st = _pair(stride)[0]
+    plain = tuple(weight.shape[2:]) == (3, 3) and st == 1       # the 3x3 / stride 1 entry
+    conv = KC.conv3x3_lif if plain else \
+        (lambda x, w, b, **k: KC.conv_lif_strided(x, w, b, stride=st, **k))
     if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0 and Cout % 32 == 0:
         key = ("khwc", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
             cache["key"], cache["w"] = key, KC.weight_khwc(weight)
-        y = KC.conv3x3_lif(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
+        y = conv(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
     if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0 and Cout % 32 == 0:
         # float32-faithful on the tensor cores: both operands as three bf16 terms
@@ -97,10 +108,10 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None):
         if cache.get("key") != key:
             cache.clear()
             cache["key"], cache["w"] = key, KC.split_weight_khwc(weight)
-        y = KC.conv3x3_lif(KC.split_activations(KC._frames_f32(x_seq)), cache["w"], b,
-                           residual=res, **kw)
+        y = conv(KC.split_activations(KC._frames_f32(x_seq)), cache["w"], b, residual=res,
+                 **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
-    if residual is not None:
+    if residual is not None or not plain:
         return None
     if x_seq.dtype == torch.float32 and Cout % 8 == 0:
         w = weight.detach().float().contiguous()
@@ -150,7 +161,7 @@ class FusedConvNeuron(nn.Module, _NeuronArgs):
         if _fused_conv_ok(self.weight, self.stride, self.padding, self.dilation, self.groups,
                           self.v_threshold):
             y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
-                          self._cache)
+                          self._cache, stride=self.stride)
             if y is not None:
                 return y
         y = _torch_conv(x_seq, self.weight, None, self.stride, self.padding, self.dilation,
@@ -247,7 +258,7 @@ class FusedConvBNNeuron(_ConvBNBase):
         if self.fold_bn and _fused_conv_ok(self.weight, self.stride, self.padding,
                                            self.dilation, self.groups, self.v_threshold):
             y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
-                          self._cache)
+                          self._cache, stride=self.stride)
             if y is not None:
                 return y
         y, b = self._conv_bn(x_seq)
@@ -272,9 +283,52 @@ class FusedConvBNAddNeuron(_ConvBNBase):
                                            self.dilation, self.groups, self.v_threshold) \
                 and tuple(residual_seq.shape[:2]) == tuple(x_seq.shape[:2]):
             y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
-                          self._cache, residual=residual_seq)
+                          self._cache, residual=residual_seq, stride=self.stride)
             if y is not None:
                 return y
         y, b = self._conv_bn(x_seq)
         return fused_bias_if_lif(y, b, residual=residual_seq, layout=self.layout,
                                  **self._neuron_kw())
+
+
+class FusedConvBN(nn.Module):
+    """Conv2d + BN with no neuron, BN folded into the conv: the downsample branch of a
+    spiking ResNet block, nn.Sequential(Conv2d 1x1 / stride 2, BatchNorm2d) in the
+    reference (zoo/resnet.py:139-142).  The reference keeps it as torch ops; its result is
+    the float32 residual of the block's second fused module.  On a bf16 input (spikes)
+    with Cin % 8 == 0, Cout % 32 == 0, T in {2, 4, 8} and a 1x1 / padding 0 or 3x3 /
+    padding 1 conv of stride 1 or 2 it is one launch of the T-folded kernel with a float32
+    result (snnb_conv_f32); otherwise torch's conv in the input's dtype plus the folded
+    bias.  Input [T, B, Cin, H, W] (layout as the other modules), output float32
+    [T, B, Cout, Ho, Wo] for a bf16 input, else the input's dtype."""
+
+    def __init__(self, conv: nn.Conv2d, bn: nn.BatchNorm2d, *, layout: str = "NCHW"):
+        super().__init__()
+        assert bn.running_mean is not None
+        new_w, new_b = fold_conv_bn(conv.weight.detach(),
+                                    conv.bias.detach() if conv.bias is not None else None,
+                                    bn.weight.detach(), bn.bias.detach(),
+                                    bn.running_mean.detach(), bn.running_var.detach(), bn.eps)
+        self.weight = nn.Parameter(new_w)
+        self.bias = nn.Parameter(new_b)
+        self.stride, self.padding = conv.stride, conv.padding
+        self.dilation, self.groups = conv.dilation, conv.groups
+        self.layout = layout
+        self._cache = {}
+
+    def forward(self, x_seq):
+        T, B, Cin = x_seq.shape[:3]
+        Cout = self.weight.shape[0]
+        if x_seq.dtype == torch.bfloat16 and T in (2, 4, 8) and Cin % 8 == 0 and \
+                Cout % 32 == 0 and _fused_conv_ok(self.weight, self.stride, self.padding,
+                                                  self.dilation, self.groups, 1.0):
+            key = ("khwc", self.weight.data_ptr(), self.weight._version)
+            if self._cache.get("key") != key:
+                self._cache.clear()
+                self._cache["key"], self._cache["w"] = key, KC.weight_khwc(self.weight)
+            y = KC.conv_f32(KC._to_frames(x_seq), self._cache["w"],
+                            self.bias.detach().float().contiguous(), stride=_pair(self.stride)[0])
+            return KC._from_frames(y, torch.float32, self.layout)
+        y = _torch_conv(x_seq, self.weight, None, self.stride, self.padding, self.dilation,
+                        self.groups, self.layout)
+        return y + self.bias.detach().to(y.dtype).view(1, 1, -1, 1, 1)

@@ -8,10 +8,12 @@ ResNetSNN :120-213, resnet18_snn / resnet34_snn :216-229).  A block computes
     out      = neuron2(bn2(conv2(out)) + identity)        residual added BEFORE the neuron
 
 ``fuse()`` swaps each block's three steps for two fused modules: conv1 -> FusedConvBNNeuron,
-conv2 + residual -> FusedConvBNAddNeuron.  With BN folded, every 3x3 / stride-1 conv on
-spike input (Cin % 8 == 0, Cout % 32 == 0) is one launch of the tcgen05 conv + neuron
-kernel, the second one reading the residual in its epilogue; strided convs, the 7x7 stem
-and the downsample branch run torch's conv followed by the fused neuron kernel.
+conv2 + residual -> FusedConvBNAddNeuron, and the downsample (1x1 / stride 2 conv + BN) for
+FusedConvBN.  With BN folded, every 3x3 conv (stride 1 or 2) and 1x1 conv on spike input
+(Cin % 8 == 0, Cout % 32 == 0) is one launch of the tcgen05 conv + neuron kernels, the
+second one reading the residual in its epilogue, and the downsample one launch of the
+T-folded kernel with a float32 result; only the 7x7 stem (real-valued image, stride 2) runs
+torch's conv followed by the fused neuron kernel.
 Unfused (``fused=False``) the network runs torch conv + BN and the K2 neuron modules.
 """
 from __future__ import annotations
@@ -19,7 +21,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from ..nn.fused_layers import FusedConvBNAddNeuron, FusedConvBNNeuron
+from ..nn.fused_layers import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron
 from ..nn.modules import IFNode, LIFNode
 
 
@@ -83,6 +85,11 @@ class BasicBlockSNN(nn.Module):
         self.block2 = FusedConvBNAddNeuron(self.conv2.eval(), self.bn2.eval(), fold_bn=fold_bn,
                                            layout=self.layout, **node_kwargs(self.neuron2)
                                            ).to(device=dev, dtype=dt)
+        if self.downsample is not None and fold_bn:
+            conv = next(m for m in self.downsample.modules() if isinstance(m, nn.Conv2d))
+            bn = next(m for m in self.downsample.modules() if isinstance(m, nn.BatchNorm2d))
+            self.downsample = FusedConvBN(conv.eval(), bn.eval(), layout=self.layout
+                                          ).to(device=dev, dtype=dt)
         self.conv1 = self.bn1 = self.neuron1 = nn.Identity()
         self.conv2 = self.bn2 = self.neuron2 = nn.Identity()
         self._fused = True
@@ -91,6 +98,8 @@ class BasicBlockSNN(nn.Module):
     def identity(self, x_seq):
         if self.downsample is None:
             return x_seq
+        if isinstance(self.downsample, FusedConvBN):
+            return self.downsample(x_seq)
         return frames_op(self.downsample, x_seq, self.layout)
 
     def forward(self, x_seq):
