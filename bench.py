@@ -597,23 +597,40 @@ class VggWorkload:
 
 
 class ConvLayerWorkload:
-    """One fused conv3x3 + BN(folded) + LIF + 2x2 max-pool layer (config 2)."""
+    """One fused conv3x3 + BN(folded) + LIF + 2x2 max-pool layer (config 2); with k / stride
+    other than 3 / 1 a ResNet conv instead (3x3 / stride 2 or 1x1, no pool:
+    snnb_conv_lif_strided)."""
     name = "conv"
     flush_l2 = True
 
-    def __init__(self, cin=512, cout=512, H=56, B=64, T=4, p=0.15, fixed=None, packed="none"):
+    def __init__(self, cin=512, cout=512, H=56, B=64, T=4, p=0.15, fixed=None, packed="none",
+                 k=3, stride=1):
         self.cin, self.cout, self.H, self.B, self.T, self.p = cin, cout, H, B, T, p
         self.fixed = fixed
+        self.k, self.stride = k, stride
+        self.strided = (k, stride) != (3, 1)
+        assert not (self.strided and packed != "none"), "packed spikes: 3x3 / stride 1 only"
+        self.Ho = (H - 1) // stride + 1 if self.strided else H // 2
         # packed spikes between layers: "in" / "out" / "both" run snnb_conv3x3_lif_packed
         self.pk_in, self.pk_out = packed in ("in", "both"), packed in ("out", "both")
         self.packed = packed
-        self.flops = 2 * T * B * H * H * cout * cin * 9
-        pk = "" if packed == "none" else f", packed spikes {packed}"
-        self.metric = f"fused conv3x3+BN+LIF+maxpool TFLOP/s (Cin={cin}, Cout={cout}, H=W={H}, B={B}, T={T}{pk})"
+        if self.strided:
+            self.flops = 2 * T * B * self.Ho * self.Ho * cout * cin * k * k
+            self.metric = (f"fused conv{k}x{k}/stride {stride}+BN+LIF TFLOP/s (ResNet conv; Cin={cin}, "
+                           f"Cout={cout}, H=W={H}, B={B}, T={T})")
+        else:
+            self.flops = 2 * T * B * H * H * cout * cin * 9
+            pk = "" if packed == "none" else f", packed spikes {packed}"
+            self.metric = f"fused conv3x3+BN+LIF+maxpool TFLOP/s (Cin={cin}, Cout={cout}, H=W={H}, B={B}, T={T}{pk})"
         self.unit = "TFLOP/s"
         self.dtype = "bf16"
 
     def config(self):
+        if self.strided:
+            return {"workload": f"resnet_conv{self.k}x{self.k}s{self.stride}_{self.cin}x{self.cout}@{self.H}",
+                    "T": self.T, "B": self.B, "Cin": self.cin, "Cout": self.cout, "H": self.H,
+                    "W": self.H, "kernel": self.k, "stride": self.stride, "spike_p": self.p,
+                    "pool": "none", "l2": "256 MB buffer written before every step"}
         return {"workload": f"conv_layer_{self.cin}x{self.cout}@{self.H}", "T": self.T,
                 "B": self.B, "Cin": self.cin, "Cout": self.cout, "H": self.H, "W": self.H,
                 "spike_p": self.p, "pool": "max 2x2", "packed_spikes": self.packed,
@@ -626,11 +643,23 @@ class ConvLayerWorkload:
         g = torch.Generator(device="cuda").manual_seed(7 + rank)
         T, B, H, C = self.T, self.B, self.H, self.cin
         self.x = (torch.rand(T, B, H, H, C, device="cuda", generator=g) < self.p).to(torch.bfloat16)
-        w = torch.randn(self.cout, 3, 3, C, device="cuda", generator=g) * (2.0 / (9 * C)) ** 0.5
+        k = self.k
+        w = torch.randn(self.cout, k, k, C, device="cuda", generator=g) * (2.0 / (k * k * C)) ** 0.5
         self.w = w.to(torch.bfloat16).contiguous()
         self.b = torch.rand(self.cout, device="cuda", generator=g) * 0.9 + 0.3
-        self.out = torch.empty(T, B, H // 2, H // 2, self.cout, device="cuda", dtype=torch.bfloat16)
+        self.out = torch.empty(T, B, self.Ho, self.Ho, self.cout, device="cuda",
+                               dtype=torch.bfloat16)
         self.ws = None
+        if self.strided:
+            run = lambda v, bn, sp: KC.conv_lif_strided(self.x, self.w, self.b, stride=self.stride,
+                                                        out=self.out, variant=v, block_n=bn,
+                                                        splits=sp)
+            self.choice = self.fixed if self.fixed else KC.pick_fastest(
+                run, self.cout, T, k * k * ((C + 63) // 64), variants=(1, 2))
+            nws = KC.split_workspace_bytes(T, B, self.Ho, self.Ho, self.cout, self.choice[2])
+            self.ws = torch.empty(nws // 4, device="cuda") if nws else None
+            self.launches_per_step = 1
+            return
         if self.pk_in or self.pk_out:
             # packed spikes: the T-folded kernel; the fastest channel block
             self.xin = KC.pack_spikes(self.x) if self.pk_in else self.x
@@ -660,6 +689,10 @@ class ConvLayerWorkload:
 
     def step(self):
         v, bn, sp = self.choice
+        if self.strided:
+            self.KC.conv_lif_strided(self.x, self.w, self.b, stride=self.stride, out=self.out,
+                                     variant=v, block_n=bn, splits=sp, workspace=self.ws)
+            return
         if self.pk_in or self.pk_out:
             self.KC.conv3x3_lif_packed(self.xin, self.w, self.b, x_packed=self.pk_in,
                                        out_packed=self.pk_out, pool=True, block_n=bn,
@@ -694,20 +727,27 @@ class ConvLayerWorkload:
         return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
-                "kernel": f"conv_lif (variant, block_n, splits = {self.choice})",
+                "kernel": (f"conv_lif{' strided' if self.strided else ''} "
+                           f"(variant, block_n, splits = {self.choice})"),
                 "algorithmic_flops_per_launch": self.flops, "traffic": None}
 
     def cpu_sample(self):
         from oracle import params as OP
-        B, H, C = 1, self.H, self.cin
+        B, H, C, k = 1, self.H, self.cin, self.k
         x = OP.spikes(0, (self.T, B, C, H, H), self.p)
-        w = torch.randn(self.cout, C, 3, 3, generator=OP.gen(1)) * (2.0 / (9 * C)) ** 0.5
+        w = torch.randn(self.cout, C, k, k, generator=OP.gen(1)) * (2.0 / (k * k * C)) ** 0.5
         b = torch.rand(self.cout, generator=OP.gen(2)) * 0.9 + 0.3
-        return {"B": B, "x": x, "w": w, "b": b, "what": "oracle conv+LIF+pool, torch-CPU f32"}
+        what = "oracle conv+LIF, torch-CPU f32" if self.strided else \
+            "oracle conv+LIF+pool, torch-CPU f32"
+        return {"B": B, "x": x, "w": w, "b": b, "what": what}
 
     def cpu_run(self, s, threads):
-        from oracle import vgg as OV
         torch.set_num_threads(threads)
+        if self.strided:
+            from oracle import resnet as OR
+            OR.conv_bn_neuron(s["x"], s["w"], s["b"], stride=self.stride, padding=self.k // 2)
+            return 2 * self.T * s["B"] * self.Ho * self.Ho * self.cout * self.cin * self.k ** 2 / 1e12
+        from oracle import vgg as OV
         OV.conv_bn_lif_pool(s["x"], s["w"], s["b"], pool=True)
         return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
 
@@ -1214,7 +1254,9 @@ def main():
                     choices=["vgg16", "lif", "conv", "first", "attention", "bgemm"])
     ap.add_argument("--lif-shape", default="32,134217728", help="lif workload: T,N")
     ap.add_argument("--gemm-shape", default="16384,8192,8192", help="bgemm workload: M,K,N")
-    ap.add_argument("--layer", default="512,512,56", help="conv workload: Cin,Cout,H")
+    ap.add_argument("--layer", default="512,512,56",
+                    help="conv workload: Cin,Cout,H (3x3 + pool) or Cin,Cout,H,k,stride (ResNet "
+                         "conv, k in {1, 3}, stride in {1, 2}, no pool)")
     ap.add_argument("--batch", type=int, default=64, help="conv workload batch")
     ap.add_argument("--choice", default=None,
                     help="conv workload: fixed 'variant,block_n' instead of timing the candidates")
@@ -1233,11 +1275,14 @@ def main():
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.workload == "conv":
-        cin, cout, hh = (int(v) for v in args.layer.split(","))
+        lay = [int(v) for v in args.layer.split(",")]
+        cin, cout, hh = lay[:3]
+        k, stride = (lay[3], lay[4]) if len(lay) == 5 else (3, 1)
         fixed = tuple(int(v) for v in args.choice.split(",")) if args.choice else None
         if fixed and len(fixed) == 2:
             fixed = fixed + (1,)
-        wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed, packed=args.packed)
+        wl = ConvLayerWorkload(cin, cout, hh, B=args.batch, fixed=fixed, packed=args.packed,
+                               k=k, stride=stride)
     elif args.workload == "first":
         wl = FirstLayerWorkload(B=args.batch,
                                 fixed=int(args.choice) if args.choice is not None else None)

@@ -251,20 +251,23 @@ int snnb_conv3x3_lif_res(const void* x, int64_t T, int64_t B, int64_t H, int64_t
                          void* out, snnb_stream_t stream);
 
 /*
- * K1 for the other convs of a spiking ResNet: 3x3 / padding 1 or 1x1 / padding 0, stride 1
- * or 2, on spike (or any bf16) input, + bias -> multi-step neuron, optionally with the
+ * K1 for the other convs of a spiking ResNet: k x k / padding k / 2 with k in {1, 3, 5, 7}
+ * (3x3, pointwise and the 7x7 stem), stride 1 or 2, on spike (or any bf16) input, + bias ->
+ * multi-step neuron, optionally with the
  * residual input of snnb_conv3x3_lif_res.  Replaces FusedConvBNNeuron.forward and
  * FusedConvBNAddNeuron.forward for these geometries (snn_compiler/nn/modules.py:324-357,
  * :415-443: F.conv2d with stride, then fused_bias_if_lif), i.e. the strided first conv of a
- * downsampling BasicBlock (snn_compiler/zoo/resnet.py:30-117) and 1x1 convs.  The activation
+ * downsampling BasicBlock (snn_compiler/zoo/resnet.py:30-117), 1x1 convs and the stem
+ * (zoo/resnet.py:120-131; its float32 image as split bf16 terms).  The activation
  * boxes traverse the input with the conv's stride (TMA traversal stride), so the strided
  * conv is the same implicit GEMM as the stride-1 one with no gather.
  * x        : bf16 NHWC [T*B, H, W, Cin] (H, W: the INPUT's sizes), Cin % 8 == 0
  * w        : bf16 [Cout, ksize, ksize, Cin], Cout % 32 == 0
  * out      : bf16 spikes NHWC [T*B, Ho, Wo, Cout], Ho = (H - 1) / stride + 1 (same for W)
  * residual : nullptr, or NHWC [T*B, Ho, Wo, Cout] of residual_dtype (SNNB_BF16 / SNNB_F32)
- * variant / block_n / splits / workspace: as snnb_conv3x3_lif_res (the band variants 3 and 7
- * take stride 1 3x3 convs only); snnb_split_workspace_bytes takes the OUTPUT sizes.
+ * variant / block_n / splits / workspace: as snnb_conv3x3_lif_res; with stride 2 or k > 3
+ * (general tap coordinates) variants 0, 1 and 2 only -- 3 to 7 return SNNB_ERR_UNSUPPORTED;
+ * snnb_split_workspace_bytes takes the OUTPUT sizes.
  */
 int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_t H, int64_t W,
                           int64_t Cin, const void* w, const float* bias, int64_t Cout, int ksize,
@@ -274,8 +277,8 @@ int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_t H, int64_
                           int64_t workspace_bytes, void* out, snnb_stream_t stream);
 
 /*
- * A conv with a float32 result and no neuron: out = conv(x, w) + bias, 3x3 / padding 1 or
- * 1x1 / padding 0, stride 1 or 2.  Replaces the downsample branch of a spiking ResNet block,
+ * A conv with a float32 result and no neuron: out = conv(x, w) + bias, k x k / padding
+ * k / 2 (k in {1, 3, 5, 7}), stride 1 or 2.  Replaces the downsample branch of a spiking ResNet block,
  * nn.Sequential(Conv2d 1x1 stride 2, BatchNorm2d) with BN folded into w and bias
  * (snn_compiler/zoo/resnet.py:139-142, applied in BasicBlockSNN.forward :96-117), whose
  * result is the float32 residual input of the block's second conv (snnb_conv3x3_lif_res).

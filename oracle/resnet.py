@@ -7,8 +7,8 @@ fused_bias_if_lif, kernels/fused.py:50-114):
     y = conv2d(x, W', stride, padding);  in = (y + b') (+ residual);  LIF / IF over T
 
 W' / b' are the module's folded weights (fold_conv_bn, fused.py:585-599).  The reference
-convolves in the input's dtype: on a bf16 input a tensor-core conv (3x3 / padding 1 or
-1x1 / padding 0, stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0) has bf16 operands, so the
+convolves in the input's dtype: on a bf16 input a tensor-core conv (k x k / padding k // 2
+for k in {1, 3, 5, 7}, stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0) has bf16 operands, so the
 oracle rounds W' to bf16
 for it (the products are then exact and only the float32 summation order differs); on a
 float32 input the conv is float32 and W' is kept as is.  The block structure follows
@@ -27,11 +27,11 @@ def _pair(v):
 
 
 def tensor_core_conv(weight, stride, padding, dilation=1, groups=1) -> bool:
-    """The geometries the library runs on its tensor-core conv kernels: 3x3 / padding 1 or
-    1x1 / padding 0, stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0."""
+    """The geometries the library runs on its tensor-core conv kernels with bf16 operands:
+    k x k / padding k // 2 (k in {1, 3, 5, 7}), stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0."""
     cout, cin = weight.shape[0], weight.shape[1]
     ks = tuple(weight.shape[2:])
-    return (ks in ((3, 3), (1, 1)) and _pair(stride) in ((1, 1), (2, 2))
+    return (ks in ((3, 3), (1, 1), (5, 5), (7, 7)) and _pair(stride) in ((1, 1), (2, 2))
             and _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1)
             and groups == 1 and cin % 8 == 0 and cout % 32 == 0)
 

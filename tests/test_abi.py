@@ -83,7 +83,7 @@ def test_split_workspace_size_overflow_is_rejected():
 
 
 def test_strided_conv_entries_reject_bad_geometry_without_a_device():
-    """Kernel sizes other than 1 / 3, strides other than 1 / 2, a missing input and
+    """Kernel sizes other than 1 / 3 / 5 / 7, strides other than 1 / 2, a missing input and
     oversized dimensions come back SNNB_ERR_ARG before any device work."""
     from snn_compiler import _lib
     L = _lib.lib()
@@ -101,7 +101,8 @@ def test_strided_conv_entries_reject_bad_geometry_without_a_device():
         a.update(kw)
         return L.snnb_conv_f32(*a.values())
     for call in (strided, f32):
-        assert call(k=5) == -1
+        assert call(k=4) == -1
+        assert call(k=9) == -1
         assert call(k=2) == -1
         assert call(s=3) == -1
         assert call(s=0) == -1

@@ -1,7 +1,8 @@
-"""Strided and 1x1 convs on the tensor-core kernels (snnb_conv_lif_strided, snnb_conv_f32):
-the convs of a spiking ResNet that are not 3x3 / stride 1 -- the first conv of a
-downsampling BasicBlock (3x3 / stride 2), pointwise convs and the downsample branch
-(1x1 / stride 2 + folded BN, float32 result) -- against the CPU oracle
+"""Strided, 1x1 and 7x7 convs on the tensor-core kernels (snnb_conv_lif_strided,
+snnb_conv_f32): the convs of a spiking ResNet that are not 3x3 / stride 1 -- the first conv
+of a downsampling BasicBlock (3x3 / stride 2), pointwise convs, the downsample branch
+(1x1 / stride 2 + folded BN, float32 result) and the 7x7 / stride 2 stem on the float32
+image -- against the CPU oracle
 (oracle/resnet.py, restating snn_compiler/nn/modules.py:258-443 and
 snn_compiler/zoo/resnet.py:30-142)."""
 import pytest
@@ -23,11 +24,19 @@ def _weights(cout, cin, k, g, gain=1.0):
 
 
 def _flip_ok(got, ref, vpre):
-    """BASELINE's criterion: every disagreement at a neuron within 1e-4 of the threshold,
-    and at most 0.1% of the elements."""
-    bad = got != ref
-    near = (vpre - THR).abs() < 1e-4
-    return not (bad & ~near).any() and bad.float().mean().item() <= 1e-3
+    """BASELINE's criterion: at most 0.1% of the elements disagree, and each neuron's FIRST
+    disagreement sits within 1e-4 of the threshold (after a flip the two membranes follow
+    different resets, so a neuron's later steps may differ anywhere)."""
+    T = got.shape[0]
+    bad = (got != ref).reshape(T, -1)
+    if bad.float().mean().item() > 1e-3:
+        return False
+    if not bad.any():
+        return True
+    cols = bad.any(0).nonzero().squeeze(1)
+    first = torch.argmax(bad.int(), dim=0)[cols]
+    v = vpre.reshape(T, -1)[first, cols]
+    return bool(((v - THR).abs() < 1e-4).all())
 
 
 GEOMS = [  # (k, stride, H, W, Cin, Cout)
@@ -38,6 +47,8 @@ GEOMS = [  # (k, stride, H, W, Cin, Cout)
     (1, 2, 7, 9, 64, 64),
     (1, 1, 8, 8, 128, 64),
     (3, 1, 8, 8, 64, 64),         # the stride-1 3x3 conv through the same entry
+    (7, 2, 16, 16, 64, 64),       # a 7x7 / stride 2 conv (the ResNet stem's geometry)
+    (5, 1, 9, 9, 64, 64),
 ]
 SCHEDS = [(0, 0, 1), (1, 64, 1), (1, 32, 1), (2, 128, 1), (2, 64, 2), (4, 64, 1), (5, 128, 1),
           (6, 128, 2)]
@@ -56,6 +67,14 @@ def test_strided_conv_lif_against_oracle(geom, sched, residual):
     if residual and variant in (4, 5):
         pytest.skip("no residual input in this variant")
     T, B = 4, 4
+    if (stride != 1 or k > 3) and variant in (4, 5, 6):
+        # general tap coordinates: the T-sequential and single-CTA T-folded kernels only
+        x = torch.zeros(T, B, H, W, Cin, device=DEV, dtype=torch.bfloat16)
+        with pytest.raises(RuntimeError):
+            C.conv_lif_strided(x, torch.zeros(Cout, k, k, Cin, device=DEV, dtype=torch.bfloat16),
+                               torch.zeros(Cout, device=DEV), stride=stride, variant=variant,
+                               block_n=block_n, splits=splits)
+        return
     g = torch.Generator().manual_seed(hash(geom) % 1000 + 7 * variant + block_n + splits)
     x = _spikes((T, B, Cin, H, W), 0.2, g)
     w = _weights(Cout, Cin, k, g, gain=1.5)
@@ -158,3 +177,28 @@ def test_resnet_block_with_downsample_bf16_on_the_kernels():
         assert ref.sum() > 0, type(mod).__name__
         assert _flip_ok(out.float(), ref, vpre), type(mod).__name__
     assert kinds == {"FusedConvBN", "FusedConvBNNeuron", "FusedConvBNAddNeuron"}
+
+
+def test_resnet_stem_on_the_float32_image():
+    """The 7x7 / stride 2 / padding 3 stem conv + BN + LIF of ResNetSNN on a float32 image
+    (Cin = 3): float32-faithful on the tensor cores (image and weights as three bf16 terms,
+    zero padded to 4 channels), against the float32 oracle."""
+    from snn_compiler.nn import FusedConvBNNeuron
+    torch.manual_seed(3)
+    conv = torch.nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False)
+    bn = torch.nn.BatchNorm2d(64)
+    with torch.no_grad():
+        conv.weight.mul_(2.0)
+        bn.bias.add_(0.3)
+        bn.running_mean.normal_(0, 0.1)
+        bn.running_var.uniform_(0.5, 1.5)
+    mod = FusedConvBNNeuron(conv.eval(), bn.eval(), neuron="lif", tau=2.0).to(DEV)
+    g = torch.Generator().manual_seed(9)
+    img = torch.rand(1, 4, 3, 32, 32, generator=g).expand(4, 4, 3, 32, 32).contiguous()
+    with torch.no_grad():
+        y = mod(img.to(DEV))
+    assert "w" in mod._cache                    # ran on the tensor-core kernel
+    assert y.shape == (4, 4, 64, 16, 16) and y.dtype == torch.float32
+    ref, vpre = OR.fused_module_oracle(mod, img)
+    assert ref.sum() > 0 and ref.mean() < 0.9
+    assert _flip_ok(y.cpu(), ref, vpre)

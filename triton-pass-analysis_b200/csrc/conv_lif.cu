@@ -131,7 +131,10 @@ struct Smem {
     static constexpr int DYN = TOTAL + 1024;     // slack for 1024-byte alignment
 };
 
-template <int BN, int STAGES, bool HARD>
+// GEN: general tap coordinates (conv stride p.stride, k x k kernel p.ksize) for the strided
+// and 5x5 / 7x7 convs; without it the stride-1 3x3 / 1x1 coordinates only (as the T-folded
+// kernel's GEN).
+template <int BN, int STAGES, bool HARD, bool GEN = false>
 __global__ void __launch_bounds__(THREADS, 1)
 conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const ConvParams p) {
@@ -193,6 +196,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         // copies -- withholds every stage, so that the MMA warp's wait for the first stage
         // runs out (SNNB_ERR_TIMEOUT) with nothing in flight in the CTA.
         const int tile0 = (p.stall && blockIdx.x == 0) ? p.num_tiles : (int)blockIdx.x;
+        const int cst = GEN ? p.stride : 1;             // the boxes' traversal stride
+        const int kk = GEN ? p.ksize : 3;
         for (int tile = tile0; tile < p.num_tiles; tile += gridDim.x) {
             const Tile tl = decode_tile(tile, p, BN);
             for (int t = 0; t < p.T; ++t) {
@@ -201,9 +206,15 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
                     const int tap = kb / p.cin_blocks;
                     const int cb = kb - tap * p.cin_blocks;
-                    const int r = p.taps == 9 ? tap / 3 : 1;
-                    const int s = p.taps == 9 ? tap % 3 : 1;
-                    const int cst = p.stride > 1 ? p.stride : 1;   // the box's traversal stride
+                    int r, s;                   // input offset of the tap from the pixel
+                    if constexpr (GEN) {
+                        r = tap / kk;
+                        s = tap - r * kk - (kk >> 1);
+                        r -= kk >> 1;
+                    } else {
+                        r = p.taps == 9 ? tap / 3 - 1 : 0;
+                        s = p.taps == 9 ? tap % 3 - 1 : 0;
+                    }
                     if (!failed && tc::elect_one()) {
                         tc::mbar_expect_tx(full_bar(stage), STAGE_TX);
                         tc::tma_load_3d(sbase + S::B_OFF + stage * S::B_TILE, &tmB, full_bar(stage),
@@ -216,8 +227,8 @@ conv_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     }
                     if (!failed && tc::elect_one())
                         tc::tma_load_4d(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA,
-                                        full_bar(stage), cb * 64, tl.w0 * cst + s - 1,
-                                        tl.h0 * cst + r - 1, f0);
+                                        full_bar(stage), cb * 64, tl.w0 * cst + s,
+                                        tl.h0 * cst + r, f0);
                     __syncwarp();
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     if (!failed) {
@@ -1047,10 +1058,10 @@ int launch_persistent_pair(K kernel, int smem, const CUtensorMap& ta, const CUte
 // Ring depths fill the ~227 KB of shared memory: at these tile sizes one k-slab of MMAs
 // (0.1-0.4 us) is far shorter than a TMA round trip, so depth is what keeps the tensor
 // pipe fed.
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool GEN = false>
 int launch_conv(const CUtensorMap& ta, const CUtensorMap& tb, const ConvParams& p, cudaStream_t s) {
-    return p.hard ? launch_persistent(conv_lif_kernel<BN, STAGES, true>, Smem<BN, STAGES>::DYN, ta, tb, p, s)
-                  : launch_persistent(conv_lif_kernel<BN, STAGES, false>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
+    return p.hard ? launch_persistent(conv_lif_kernel<BN, STAGES, true, GEN>, Smem<BN, STAGES>::DYN, ta, tb, p, s)
+                  : launch_persistent(conv_lif_kernel<BN, STAGES, false, GEN>, Smem<BN, STAGES>::DYN, ta, tb, p, s);
 }
 
 template <int BN, int STAGES, int TS, int MH = 1>
@@ -1318,11 +1329,18 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                  int out_packed = 0, int stride = 1, int f32_out = 0) {
     if (const int inj = take_injected_status()) return inj;
     if (!x || !w || !out || !bias) return SNNB_ERR_ARG;
-    // stride 2 (3x3 / padding 1 or 1x1 / padding 0): H, W are the input's sizes here and the
+    // stride 2 (k x k / padding k / 2, k odd): H, W are the input's sizes here and the
     // output's from the shape checks on, (H - 1) / 2 + 1 x (W - 1) / 2 + 1; the activation
     // boxes traverse the input with stride 2.  T-sequential and T-folded kernels only.
     if (stride != 1 && stride != 2) return SNNB_ERR_ARG;
-    if (stride == 2 && (x_packed || out_packed || pool == 2 || variant == 3 || variant == 7))
+    // k x k kernels, padding k / 2: 1, 3 (taps 1 / 9) and 5, 7 (T-sequential / T-folded)
+    const int ksize = taps == 1 ? 1 : taps == 9 ? 3 : taps == 25 ? 5 : taps == 49 ? 7 : 0;
+    if (!ksize) return SNNB_ERR_ARG;
+    // general tap coordinates (stride 2 or a 5x5 / 7x7 kernel): the T-sequential kernel and
+    // the single-CTA T-folded kernel (any splits) -- not the band, two-tile, CTA-pair,
+    // cluster split-K, packed or dense forms
+    const bool gen = stride != 1 || ksize > 3;
+    if (gen && (x_packed || out_packed || pool == 2 || variant >= 3))
         return SNNB_ERR_UNSUPPORTED;
     // f32_out: no neuron -- out is float32 [T*B, H, W, Cout] = conv + bias (the T-folded
     // kernel's raw sums, then the bias added in place), e.g. a downsample branch
@@ -1513,6 +1531,7 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
         p.partial = static_cast<float*>(out);     // one split: the raw sums are the result
     }
     p.stride = stride;
+    p.ksize = ksize;
     const int64_t ntiles = ((mtiles + mh * cg - 1) / (mh * cg)) * p.n_tiles_n;
     p.mtiles = (int)mtiles;
     if (ntiles * splits > 0x7fffffff) return SNNB_ERR_ARG;
@@ -1521,10 +1540,14 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
     if (x_packed || out_packed) return launch_tm_packed(T, BN, x_packed, out_packed, ta, tb, p, s);
     if (gpool) return launch_tm_cpool(T, BN, ta, tb, p, s);
     if (variant == 2) {
-        switch (T) {
-            case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;
-            case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh, cg); break;
-            default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh, cg); break;
+        if (gen) {
+            rc = launch_tm_general(T, BN, ta, tb, p, s);
+        } else {
+            switch (T) {
+                case 2: rc = launch_tm_bn<2>(BN, ta, tb, p, s, mh, cg); break;
+                case 4: rc = launch_tm_bn<4>(BN, ta, tb, p, s, mh, cg); break;
+                default: rc = launch_tm_bn<8>(BN, ta, tb, p, s, mh, cg); break;
+            }
         }
         if (rc != SNNB_OK) return rc;
         if (f32_out)
@@ -1534,6 +1557,13 @@ int run_tc_layer(const void* x, int T, int B, int H, int W, int Cin, const void*
                                    p.hard, pool, res, res_f32, p.out, s);
     }
     p.stall = take_injected_stall();
+    if (gen) {
+        switch (BN) {
+            case 128: return launch_conv<128, 6, true>(ta, tb, p, s);
+            case 64: return launch_conv<64, 8, true>(ta, tb, p, s);
+            default: return launch_conv<32, 10, true>(ta, tb, p, s);
+        }
+    }
     switch (BN) {
         case 128: return launch_conv<128, 6>(ta, tb, p, s);
         case 64: return launch_conv<64, 8>(ta, tb, p, s);
@@ -1588,7 +1618,8 @@ extern "C" int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_
     if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
         Cin > 0x7fffffff || Cout > 0x7fffffff)
         return SNNB_ERR_ARG;
-    if ((ksize != 1 && ksize != 3) || (stride != 1 && stride != 2)) return SNNB_ERR_ARG;
+    if ((ksize != 1 && ksize != 3 && ksize != 5 && ksize != 7) || (stride != 1 && stride != 2))
+        return SNNB_ERR_ARG;
     if (residual && residual_dtype != SNNB_BF16 && residual_dtype != SNNB_F32) return SNNB_ERR_ARG;
     return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout,
                         ksize * ksize, decay, input_scale, v_threshold, v_reset, hard_reset, 0,
@@ -1603,7 +1634,8 @@ extern "C" int snnb_conv_f32(const void* x, int64_t T, int64_t B, int64_t H, int
     if (T > 0x7fffffff || B > 0x7fffffff || H > 0x7fffffff || W > 0x7fffffff ||
         Cin > 0x7fffffff || Cout > 0x7fffffff)
         return SNNB_ERR_ARG;
-    if ((ksize != 1 && ksize != 3) || (stride != 1 && stride != 2)) return SNNB_ERR_ARG;
+    if ((ksize != 1 && ksize != 3 && ksize != 5 && ksize != 7) || (stride != 1 && stride != 2))
+        return SNNB_ERR_ARG;
     return run_tc_layer(x, (int)T, (int)B, (int)H, (int)W, (int)Cin, w, bias, (int)Cout,
                         ksize * ksize, 0.0f, 0.0f, 0.0f, 0.0f, 1, 0, 2, 0, 1, nullptr, 0, out,
                         static_cast<cudaStream_t>(stream), nullptr, 0, 0, 0, stride, 1);

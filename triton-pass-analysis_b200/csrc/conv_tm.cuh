@@ -38,9 +38,10 @@ struct ConvParams {
     int stall;                    // test hook (snnb_debug_inject_stall): CTA 0's producer of
                                   // the T-sequential kernel withholds every stage
     int stride;                   // conv stride (T-sequential and T-folded kernels): output
-                                  // pixel (h, w) reads input (stride*h + dy - 1, stride*w +
-                                  // dx - 1) for 3x3 taps, (stride*h, stride*w) for one tap;
-                                  // H, W above are the OUTPUT sizes.  0 reads as 1.
+                                  // pixel (h, w) reads input (stride*h + dy - k/2, stride*w +
+                                  // dx - k/2) for tap (dy, dx) of a k x k kernel; H, W above
+                                  // are the OUTPUT sizes.  0 reads as 1.
+    int ksize;                    // k of the k x k kernel (taps = k * k)
 };
 
 struct Tile {
@@ -213,9 +214,12 @@ struct SmemTM {
 // overlaps, takes half as long (measured: 4.3 us of a conv9 launch's 21.5 us with one set).
 // PKO: spikes stored packed; CPOOL: the column-group pool of the dense 2x2 form (pool == 2).
 // Both are compile-time choices: a run-time test in the epilogue's loop cost epilogue-bound
-// launches ~5%.
+// launches ~5%.  GEN: general tap coordinates -- conv stride p.stride and k x k kernels
+// (p.ksize) -- for the strided / 5x5 / 7x7 convs (conv_strided.cu); without it the producers
+// compute the stride-1 3x3 / 1x1 coordinates only (the general arithmetic in the same loop
+// cost the VGG16 layers ~1%, measured A/B on one box).
 template <int BN, int STAGES, int TS, bool HARD, int NP, int MH, int CG, bool RES, int SK = 1,
-          int PATCH = 0, bool PKO = false, bool CPOOL = false>
+          int PATCH = 0, bool PKO = false, bool CPOOL = false, bool GEN = false>
 __global__ void __launch_bounds__(THREADS + 32 * (NP - 1) + 128, 1)
 conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p) {
@@ -456,6 +460,10 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const uint32_t pi = warp == 0 ? 0u : (uint32_t)(warp - 5);
         uint32_t g = 0, issued = 0, last_g = 0, failed = 0;
         bool dep_ready = false;                 // griddepcontrol.wait done (this warp)
+        // GEN: the boxes traverse the input with the conv's stride; tap (r, s) of a k x k
+        // kernel reads input (stride * h0 + r - k/2, stride * w0 + s - k/2)
+        const int cst = GEN ? p.stride : 1;
+        const int kk = GEN ? p.ksize : 3;
         for (int item = item0; item < num_items; item += item_step) {
             Tile tl[MH];
 #pragma unroll
@@ -469,9 +477,15 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 failed |= 1u - tc::mbar_wait_warp(empty_bar(stage), phase ^ 1u, failed);
                 const int tap = kb / p.cin_blocks;
                 const int cb = kb - tap * p.cin_blocks;
-                const int r = p.taps == 9 ? tap / 3 : 1;
-                const int s = p.taps == 9 ? tap % 3 : 1;
-                const int cst = p.stride > 1 ? p.stride : 1;   // the box's traversal stride
+                int r, s;                       // input offset of the tap from the pixel
+                if constexpr (GEN) {
+                    r = tap / kk;
+                    s = tap - r * kk - (kk >> 1);
+                    r -= kk >> 1;
+                } else {
+                    r = p.taps == 9 ? tap / 3 - 1 : 0;
+                    s = p.taps == 9 ? tap % 3 - 1 : 0;
+                }
                 // the stage's weight rows first (no kernel writes them), then, once the
                 // previous kernel has completed, its activation box(es)
                 if (!failed && tc::elect_one()) {
@@ -496,14 +510,15 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     if constexpr (PAIR) {
                         const uint32_t fb = tc::map_to_rank(full_bar(stage), 0);
                         tc::tma_load_5d_pair(sbase + S::A_OFF + stage * A_TILE_BYTES, &tmA, fb,
-                                             cb * 64, 0, tl[0].w0 * cst + s - 1,
-                                             tl[0].h0 * cst + r - 1, tl[0].img0);
+                                             cb * 64, 0, tl[0].w0 * cst + s,
+                                             tl[0].h0 * cst + r, tl[0].img0);
                     } else {
 #pragma unroll
                         for (int h = 0; h < MH; ++h)
                             tc::tma_load_5d(sbase + S::A_OFF + (stage * MH + h) * A_TILE_BYTES,
-                                            &tmA, full_bar(stage), cb * 64, 0, tl[h].w0 * cst + s - 1,
-                                            tl[h].h0 * cst + r - 1, tl[h].img0);
+                                            &tmA, full_bar(stage), cb * 64, 0,
+                                            tl[h].w0 * cst + s, tl[h].h0 * cst + r,
+                                            tl[h].img0);
                     }
                 }
                 __syncwarp();
@@ -903,6 +918,12 @@ conv_lif_tm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // a tile run as one thread-block cluster and reduce their partial sums through distributed
 // shared memory, so the neuron runs in the same launch.
 int launch_tm_cluster(int TS, int BN, int SK, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const ConvParams& p, cudaStream_t s);
+
+// Strided and k x k (k in {1, 3, 5, 7}) convs on conv_lif_tm_kernel with general tap
+// coordinates (GEN; conv_strided.cu): single-CTA T-folded form, any split count, residual
+// or not.
+int launch_tm_general(int TS, int BN, const CUtensorMap& ta, const CUtensorMap& tb,
                       const ConvParams& p, cudaStream_t s);
 
 // Packed-spike launches of conv_lif_tm_kernel (conv_packed.cu): packed input (PATCH > 0)

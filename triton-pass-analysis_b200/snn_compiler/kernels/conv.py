@@ -88,15 +88,16 @@ def conv_lif_strided(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, st
                      out: torch.Tensor | None = None, variant: int = 0, block_n: int = 0,
                      splits: int = 1, workspace: torch.Tensor | None = None,
                      residual: torch.Tensor | None = None) -> torch.Tensor:
-    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k = 3, padding 1, or k = 1,
-    padding 0), stride 1 or 2 -> spikes [T, B, Ho, Wo, Cout] bf16, Ho = (H - 1) // stride + 1
-    (snnb_conv_lif_strided: the strided and 1x1 convs of a spiking ResNet).  residual: None
-    or [T, B, Ho, Wo, Cout] bf16 / float32; variant / block_n / splits as conv3x3_lif
-    (variants 0, 1, 2, 4, 5, 6)."""
+    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k in {1, 3, 5, 7}, padding k // 2),
+    stride 1 or 2 -> spikes [T, B, Ho, Wo, Cout] bf16, Ho = (H - 1) // stride + 1
+    (snnb_conv_lif_strided: the strided, 1x1 and 7x7 stem convs of a spiking ResNet).
+    residual: None
+    or [T, B, Ho, Wo, Cout] bf16 / float32; variant / block_n / splits as conv3x3_lif:
+    variants 0, 1 and 2 (any splits), and for 3x3 / 1x1 convs of stride 1 also 4, 5, 6."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.ndim == 4
     k = w.shape[1]
-    assert k in (1, 3) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
+    assert k in (1, 3, 5, 7) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
     T, B, H, W, Cin = x.shape
     Cout = w.shape[0]
     assert w.shape[3] == Cin, (tuple(w.shape), Cin)
@@ -123,13 +124,13 @@ def conv_lif_strided(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, st
 
 def conv_f32(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, stride: int = 1,
              out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k = 1 or 3) -> float32
+    """x [T, B, H, W, Cin] bf16, w [Cout, k, k, Cin] bf16 (k in {1, 3, 5, 7}) -> float32
     [T, B, Ho, Wo, Cout] = conv + bias, no neuron (snnb_conv_f32: the downsample branch of a
     spiking ResNet block, BN folded into w and bias); T in {2, 4, 8}."""
     assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim == 5
     assert w.dtype == torch.bfloat16 and w.is_contiguous() and w.ndim == 4
     k = w.shape[1]
-    assert k in (1, 3) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
+    assert k in (1, 3, 5, 7) and w.shape[2] == k and stride in (1, 2), (tuple(w.shape), stride)
     T, B, H, W, Cin = x.shape
     Cout = w.shape[0]
     assert w.shape[3] == Cin and bias.dtype == torch.float32 and bias.numel() == Cout
@@ -436,12 +437,15 @@ def candidates(cout: int, T: int, kslabs: int, max_splits: int = 8, band=(),
 
 
 def pick_fastest(launch, cout: int, T: int, kslabs: int, reps: int = 10, band=(),
-                 dense_pool: bool = False, band_xs=(), linear_t: bool = False):
+                 dense_pool: bool = False, band_xs=(), linear_t: bool = False, variants=None):
     """Time launch(variant, block_n, splits) for every configuration the layer admits
-    (on its real operands, device time via time_graph) and return the fastest."""
+    (on its real operands, device time via time_graph) and return the fastest.
+    variants: only these kernel variants (e.g. (1, 2) for strided convs)."""
     best, best_ms = (0, 0, 1), float("inf")
     for cfg in candidates(cout, T, kslabs, band=band, dense_pool=dense_pool, band_xs=band_xs,
                           linear_t=linear_t):
+        if variants is not None and cfg[0] not in variants:
+            continue
         # the lower of two timings: one replay can catch another context's work
         ms = min(time_graph(lambda: launch(*cfg), reps) for _ in range(2))
         if ms < best_ms:
@@ -687,8 +691,8 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
                 soft_reset: bool = False, v_threshold=1.0, v_reset: float = 0.0,
                 layout: str = "NCHW"):
     """conv + bias + neuron (reference fused.py:513-551) for x_seq [T, B, Cin, H, W].
-    3x3 / padding 1 and 1x1 / padding 0 convs of stride 1 or 2 with a scalar threshold run
-    fused on the tcgen05 kernels when Cout % 32 == 0: bf16 operands for a bf16 input (Cin % 8 == 0); for a float32 /
+    k x k / padding k // 2 convs (k in {1, 3, 5, 7}) of stride 1 or 2 with a scalar threshold
+    run fused on the tcgen05 kernels when Cout % 32 == 0: bf16 operands for a bf16 input (Cin % 8 == 0); for a float32 /
     float16 input (Cin % 4 == 0) float32-faithful, each operand as three bf16 terms (a
     split-terms launch, then the conv over six channel groups); a float32 input with other
     Cin (the 3x3 / stride 1 image layer) takes the float32 CUDA-core kernel.  Any other geometry keeps the
@@ -700,15 +704,17 @@ def conv_neuron(x_seq, weight, bias, *, stride=1, padding=0, dilation=1, groups=
     b = bias.detach().float().contiguous() if bias is not None else \
         torch.zeros(Cout, device=x_seq.device)
     ks, st = tuple(weight.shape[2:]), _pair(stride)
-    if ks in ((1, 1), (3, 3)) and st in ((1, 1), (2, 2)) and (ks, st) != ((3, 3), (1, 1)) and \
-            _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1) and \
-            groups == 1 and isinstance(v_threshold, (int, float)) and Cout % 32 == 0:
-        # strided 3x3 and 1x1 convs: the same kernels, activation boxes traversing the input
-        # with the stride (snnb_conv_lif_strided)
+    if ks in ((1, 1), (3, 3), (5, 5), (7, 7)) and st in ((1, 1), (2, 2)) and \
+            (ks, st) != ((3, 3), (1, 1)) and _pair(padding) == (ks[0] // 2,) * 2 and \
+            _pair(dilation) == (1, 1) and groups == 1 and \
+            isinstance(v_threshold, (int, float)) and Cout % 32 == 0:
+        # strided, 1x1 and 5x5 / 7x7 convs: the same kernels, activation boxes traversing the
+        # input with the stride (snnb_conv_lif_strided); a float32 input of any Cin (the
+        # 7x7 stem on the image) as split terms, zero padded to a multiple of 4 channels
         if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0:
             y = conv_lif_strided(_to_frames(x_seq), weight_khwc(weight), b, stride=st[0], **kw)
             return _from_frames(y, x_seq.dtype, layout)
-        if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0:
+        if x_seq.dtype in (torch.float32, torch.float16):
             y = conv_lif_strided(split_activations(_frames_f32(x_seq)),
                                  split_weight_khwc(weight), b, stride=st[0], **kw)
             return _from_frames(y, x_seq.dtype, layout)

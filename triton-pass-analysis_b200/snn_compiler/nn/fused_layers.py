@@ -20,9 +20,10 @@ the route depends on it:
     conv + neuron kernel;
   - linears with out_features % 32 == 0 (in_features % 8 == 0 for bf16, % 4 == 0 for
     float32 / float16, split as above): the fused linear kernel;
-  - 3x3 / padding 1 convs of stride 2 and 1x1 / padding 0 convs of stride 1 or 2 (a
-    ResNet's strided and pointwise convs) on the same kernels, the activation boxes
-    traversing the input with the stride (snnb_conv_lif_strided), bf16 or split as above;
+  - 3x3 / padding 1 convs of stride 2, 1x1 / padding 0 convs and 5x5 / 7x7 convs (padding
+    k // 2) of stride 1 or 2 (a ResNet's strided, pointwise and stem convs) on the same
+    kernels, the activation boxes traversing the input with the stride
+    (snnb_conv_lif_strided), bf16 or split as above (a float32 input of any Cin);
   - the residual form (FusedConvBNAddNeuron) on these geometries: the same tcgen05 kernels
     with the residual added in the epilogue (snnb_conv3x3_lif_res, snnb_conv_lif_strided);
   - FusedConvBN (conv + folded BN, no neuron: a ResNet block's downsample branch) on a bf16
@@ -69,9 +70,10 @@ class _NeuronArgs:
 
 
 def _fused_conv_ok(weight, stride, padding, dilation, groups, v_threshold):
-    """3x3 / padding 1 or 1x1 / padding 0, stride 1 or 2 (the convs of VGG and ResNet)."""
+    """k x k / padding k // 2 with k in {1, 3, 5, 7}, stride 1 or 2 (the convs of VGG and
+    ResNet, its 7x7 stem included)."""
     ks = tuple(weight.shape[2:])
-    return (ks in ((3, 3), (1, 1)) and _pair(stride) in ((1, 1), (2, 2))
+    return (ks in ((3, 3), (1, 1), (5, 5), (7, 7)) and _pair(stride) in ((1, 1), (2, 2))
             and _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1)
             and groups == 1 and isinstance(v_threshold, (int, float)))
 
@@ -102,8 +104,10 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None, stride=1):
             cache["key"], cache["w"] = key, KC.weight_khwc(weight)
         y = conv(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
-    if x_seq.dtype in (torch.float32, torch.float16) and Cin % 4 == 0 and Cout % 32 == 0:
-        # float32-faithful on the tensor cores: both operands as three bf16 terms
+    if x_seq.dtype in (torch.float32, torch.float16) and (Cin % 4 == 0 or not plain) and \
+            Cout % 32 == 0:
+        # float32-faithful on the tensor cores: both operands as three bf16 terms (a 3x3 /
+        # stride 1 image layer with Cin % 4 != 0 takes the CUDA-core kernel below instead)
         key = ("split", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
