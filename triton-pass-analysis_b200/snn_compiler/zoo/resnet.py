@@ -12,8 +12,8 @@ conv2 + residual -> FusedConvBNAddNeuron, and the downsample (1x1 / stride 2 con
 FusedConvBN.  With BN folded, every 3x3 conv (stride 1 or 2) and 1x1 conv on spike input
 (Cin % 8 == 0, Cout % 32 == 0) is one launch of the tcgen05 conv + neuron kernels, the
 second one reading the residual in its epilogue, and the downsample one launch of the
-T-folded kernel with a float32 result; only the 7x7 stem (real-valued image, stride 2) runs
-torch's conv followed by the fused neuron kernel.
+T-folded kernel with a float32 result; the 7x7 / stride 2 stem on the real-valued image
+runs on the same kernels with both operands as split bf16 terms (float32-faithful).
 Unfused (``fused=False``) the network runs torch conv + BN and the K2 neuron modules.
 """
 from __future__ import annotations
