@@ -752,6 +752,147 @@ class ConvLayerWorkload:
         return 2 * self.T * s["B"] * self.H * self.H * self.cout * self.cin * 9 / 1e12
 
 
+class ResNetWorkload:
+    """Spiking ResNet-18 (the reference zoo's ResNetSNN: 7x7 / stride 2 stem + BN + LIF,
+    3x3 / stride 2 max-pool, four BasicBlock stages with 1x1 / stride 2 downsample branches,
+    global average pool, linear head) at T = 4 on 224x224 images, batch 64, bf16, fused
+    (BN folded): every conv on this library's kernels, the forward captured as one CUDA
+    graph.  The image is the same at every step (direct encoding)."""
+    name = "resnet18"
+    flush_l2 = True
+
+    def __init__(self, B=64, T=4, H=224, classes=10):
+        self.B, self.T, self.H, self.classes = B, T, H, classes
+        self.metric = (f"ResNet-18-SNN T={T} inference images/s (batch {B} per GPU, "
+                       f"{H}x{H}x3, {classes} classes)")
+        self.unit = "images/s"
+        self.dtype = "bf16"
+
+    def config(self):
+        return {"workload": f"resnet18_snn_T{self.T}_b{self.B}_{self.H}px", "model": "ResNet-18-SNN",
+                "T": self.T, "batch_per_gpu": self.B, "input": f"{self.H}x{self.H}x3 U(0,1), direct encoding",
+                "classes": self.classes, "lif": "tau=2, v_th=1, hard reset 0, decay_input",
+                "weights": "Kaiming-uniform (torch default) seeded, BN stats randomised and folded, bf16",
+                "layout": "NHWC (channels-last storage)",
+                "launch": "one CUDA graph per forward; torch ops for the max-pool, channel pad of the "
+                          "image, average pool and head",
+                "l2": "256 MB buffer written before every timed step"}
+
+    def _model(self):
+        from snn_compiler.zoo import resnet18_snn
+        torch.manual_seed(0)
+        m = resnet18_snn(num_classes=self.classes, layout="NHWC")
+        with torch.no_grad():       # a lively network: every layer spikes
+            for mod in m.modules():
+                if isinstance(mod, torch.nn.Conv2d):
+                    mod.weight.mul_(3.0)
+                if isinstance(mod, torch.nn.BatchNorm2d):
+                    mod.bias.add_(0.3)
+        return m.eval().fuse()
+
+    def setup(self, rank, world, dist=None):
+        from snn_compiler.nn import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron
+        self.world = world
+        self.m = self._model().to("cuda").to(torch.bfloat16)
+        g = torch.Generator(device="cuda").manual_seed(5 + rank)
+        img = torch.rand(1, self.B, 3, self.H, self.H, device="cuda", generator=g)
+        self.x = self._nhwc(img.expand(self.T, -1, -1, -1, -1).to(torch.bfloat16))
+        # FLOPs of every conv (dense, padding zeros counted) from one forward's shapes
+        self.flops = 0
+        kinds = (FusedConvBN, FusedConvBNNeuron, FusedConvBNAddNeuron)
+
+        def hook(mod, inp, out):
+            k = mod.weight.shape[2] * mod.weight.shape[3]
+            self.flops += 2 * out.numel() * mod.weight.shape[1] * k
+        hs = [mod.register_forward_hook(hook) for mod in self.m.modules() if isinstance(mod, kinds)]
+        with torch.no_grad():
+            self.m(self.x)
+        for h in hs:
+            h.remove()
+        self.n_convs = sum(1 for mod in self.m.modules() if isinstance(mod, kinds))
+        self.flops_img = self.flops / self.B
+        # capture the forward (warm the modules' weight caches first)
+        with torch.no_grad():
+            for _ in range(2):
+                self.m(self.x)
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.out = self.m(self.x)
+        torch.cuda.synchronize()
+        # this library's launches per forward: one per conv, plus the bias-add launch of each
+        # float32 downsample conv
+        self.launches_per_step = self.n_convs + sum(
+            1 for mod in self.m.modules() if isinstance(mod, FusedConvBN))
+
+    @staticmethod
+    def _nhwc(t):
+        T, B = t.shape[:2]
+        return t.reshape(T * B, *t.shape[2:]).contiguous(memory_format=torch.channels_last) \
+            .view(T, B, *t.shape[2:])
+
+    def step(self):
+        self.graph.replay()
+
+    def kernel_events(self, steps):
+        return None
+
+    def units_per_step(self):
+        return self.B
+
+    def roofline(self, kernel_ms, peaks):
+        achieved = self.flops / (kernel_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
+                "kernel": "whole forward (one CUDA graph; every conv on the tcgen05 kernels)",
+                "algorithmic_flops_per_launch": self.flops, "traffic": None}
+
+    def e2e_setup(self):
+        self.hx = self.x.cpu().pin_memory()
+        self.hout = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = self.hx.numel() * self.hx.element_size()
+        self.d2h = self.hout.numel() * self.hout.element_size()
+
+    def e2e_step(self):
+        self.x.copy_(self.hx, non_blocking=True)
+        self.graph.replay()
+        self.hout.copy_(self.out, non_blocking=True)
+
+    def e2e_units(self):
+        return self.B
+
+    def cpu_sample(self):
+        """One image through the reference's CPU path, restated by the oracle per fused
+        module (torch-CPU float32 conv, C LIF), with the same folded weights."""
+        m = self._model()                   # float32 weights on the CPU
+        g = torch.Generator().manual_seed(5)
+        img = torch.rand(1, 1, 3, self.H, self.H, generator=g).expand(self.T, 1, 3, self.H, self.H)
+        return {"B": 1, "m": m, "x": img.contiguous(), "what": "oracle ResNet-18-SNN forward, torch-CPU f32 conv + C LIF"}
+
+    def cpu_run(self, s, threads):
+        import torch.nn.functional as F
+        from oracle import resnet as OR
+        torch.set_num_threads(threads)
+        m, x = s["m"], s["x"]
+        T, B = x.shape[:2]
+
+        def frames(t, fn):
+            y = fn(t.reshape(T * B, *t.shape[2:]))
+            return y.reshape(T, B, *y.shape[1:])
+        x = OR.fused_module_oracle(m.stem_fused, x)[0]
+        x = frames(x, lambda z: F.max_pool2d(z, 3, 2, 1))
+        for b in m.blocks():
+            out = OR.fused_module_oracle(b.block1, x)[0]
+            idn = x if b.downsample is None else OR.conv_bias(
+                x, b.downsample.weight, b.downsample.bias, stride=b.downsample.stride,
+                padding=b.downsample.padding)
+            x = OR.fused_module_oracle(b.block2, out, residual=idn)[0]
+        f = x.mean(dim=(3, 4)).reshape(T * B, -1)
+        m.fc(f).view(T, B, -1)
+        return s["B"]
+
+
 class FirstLayerWorkload:
     """The image (first) layer of VGG16-SNN on its own: float32 image [1, B, 3, 32, 32]
     (direct encoding) -> conv3x3 3->64 + folded BN + LIF over T steps -> spikes
@@ -1251,7 +1392,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="vgg16",
-                    choices=["vgg16", "lif", "conv", "first", "attention", "bgemm"])
+                    choices=["vgg16", "lif", "conv", "first", "attention", "bgemm", "resnet18"])
     ap.add_argument("--lif-shape", default="32,134217728", help="lif workload: T,N")
     ap.add_argument("--gemm-shape", default="16384,8192,8192", help="bgemm workload: M,K,N")
     ap.add_argument("--layer", default="512,512,56",
@@ -1294,7 +1435,8 @@ def main():
             gm, gk, gn = (int(v) for v in args.gemm_shape.split(","))
             wl = BgemmWorkload(gm, gk, gn)
         else:
-            wl = {"vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
+            wl = {"vgg16": VggWorkload, "attention": AttnWorkload,
+                  "resnet18": ResNetWorkload}[args.workload]()
         if args.workload == "vgg16":
             wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
             wl.eager = args.eager

@@ -277,6 +277,16 @@ int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_t H, int64_
                           int64_t workspace_bytes, void* out, snnb_stream_t stream);
 
 /*
+ * k x k max-pool (stride, padding; each window clipped to the image, as torch's -inf padding
+ * gives) on bf16 NHWC frames [frames, H, W, C] -> [frames, Ho, Wo, C], Ho = (H + 2 pad - k) /
+ * stride + 1 (W likewise).  Replaces the spiking ResNet stem's nn.MaxPool2d(3, stride=2,
+ * padding=1) (snn_compiler/zoo/resnet.py:131) applied per frame; on {0, 1} spikes it is the
+ * OR of the window.  C % 8 == 0; x and out 16-byte aligned; 1 <= k, stride <= 8; 0 <= pad < k.
+ */
+int snnb_maxpool_nhwc(const void* x, int64_t frames, int64_t H, int64_t W, int64_t C, int k,
+                      int stride, int pad, void* out, snnb_stream_t stream);
+
+/*
  * A conv with a float32 result and no neuron: out = conv(x, w) + bias, k x k / padding
  * k / 2 (k in {1, 3, 5, 7}), stride 1 or 2.  Replaces the downsample branch of a spiking ResNet block,
  * nn.Sequential(Conv2d 1x1 stride 2, BatchNorm2d) with BN folded into w and bias

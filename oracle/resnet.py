@@ -28,12 +28,14 @@ def _pair(v):
 
 def tensor_core_conv(weight, stride, padding, dilation=1, groups=1) -> bool:
     """The geometries the library runs on its tensor-core conv kernels with bf16 operands:
-    k x k / padding k // 2 (k in {1, 3, 5, 7}), stride 1 or 2, Cin % 8 == 0, Cout % 32 == 0."""
+    k x k / padding k // 2 (k in {1, 3, 5, 7}), stride 1 or 2, Cout % 32 == 0, Cin % 8 == 0
+    (any Cin, zero padded, off the 3x3 / stride 1 form)."""
     cout, cin = weight.shape[0], weight.shape[1]
     ks = tuple(weight.shape[2:])
+    general = ks != (3, 3) or _pair(stride) != (1, 1)     # channels zero padded to 8 there
     return (ks in ((3, 3), (1, 1), (5, 5), (7, 7)) and _pair(stride) in ((1, 1), (2, 2))
             and _pair(padding) == (ks[0] // 2,) * 2 and _pair(dilation) == (1, 1)
-            and groups == 1 and cin % 8 == 0 and cout % 32 == 0)
+            and groups == 1 and (cin % 8 == 0 or general) and cout % 32 == 0)
 
 
 def conv_bn_neuron(x_seq, weight, bias, *, stride, padding, neuron="lif", tau=2.0, decay=None,

@@ -181,8 +181,8 @@ def test_resnet_block_with_downsample_bf16_on_the_kernels():
 
 def test_resnet_stem_on_the_float32_image():
     """The 7x7 / stride 2 / padding 3 stem conv + BN + LIF of ResNetSNN on a float32 image
-    (Cin = 3): float32-faithful on the tensor cores (image and weights as three bf16 terms,
-    zero padded to 4 channels), against the float32 oracle."""
+    (Cin = 3): the 7x7 x 3 window gathered into K = 147 channels, then float32-faithful on
+    the tensor cores (image and weights as three bf16 terms), against the float32 oracle."""
     from snn_compiler.nn import FusedConvBNNeuron
     torch.manual_seed(3)
     conv = torch.nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False)
@@ -202,3 +202,43 @@ def test_resnet_stem_on_the_float32_image():
     ref, vpre = OR.fused_module_oracle(mod, img)
     assert ref.sum() > 0 and ref.mean() < 0.9
     assert _flip_ok(y.cpu(), ref, vpre)
+
+
+def test_resnet_stem_on_a_bf16_image_channel_padded():
+    """The same stem module in bf16 (the reference's bf16 mode): the 7x7 x 3 window gathered
+    into K = 147 channels (zero padded to 152) and run as a 1x1 conv on the bf16 kernel,
+    against the oracle with bf16 weights."""
+    from snn_compiler.nn import FusedConvBNNeuron
+    torch.manual_seed(4)
+    conv = torch.nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False)
+    bn = torch.nn.BatchNorm2d(64)
+    with torch.no_grad():
+        conv.weight.mul_(2.0)
+        bn.bias.add_(0.3)
+    mod = FusedConvBNNeuron(conv.eval(), bn.eval(), neuron="lif", tau=2.0, layout="NHWC")
+    mod = mod.to(DEV).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(10)
+    img = torch.rand(1, 2, 3, 40, 40, generator=g).expand(4, 2, 3, 40, 40).to(torch.bfloat16)
+    xd = img.reshape(8, 3, 40, 40).contiguous(memory_format=torch.channels_last).view(4, 2, 3, 40, 40)
+    with torch.no_grad():
+        y = mod(xd.to(DEV))
+    assert "w" in mod._cache and tuple(mod._cache["w"].shape) == (64, 1, 1, 152)
+    assert y.shape == (4, 2, 64, 20, 20) and y.dtype == torch.bfloat16
+    ref, vpre = OR.fused_module_oracle(mod, img)
+    assert ref.sum() > 0 and ref.mean() < 0.9
+    assert _flip_ok(y.float().cpu(), ref, vpre)
+
+
+@pytest.mark.parametrize("shape", [(8, 112, 112, 64), (3, 15, 13, 32), (2, 7, 9, 8)])
+@pytest.mark.parametrize("kind", ["spikes", "values"])
+def test_maxpool_nhwc_equals_torch(shape, kind):
+    """snnb_maxpool_nhwc (3x3 / stride 2 / padding 1, the ResNet stem's pool) against torch's
+    max_pool2d on the same bf16 frames: identical (a max picks one of its inputs)."""
+    from snn_compiler.kernels import conv as C
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.rand(*shape, generator=g) < 0.3).float() if kind == "spikes" \
+        else torch.randn(*shape, generator=g)
+    xd = x.to(torch.bfloat16).to(DEV)
+    y = C.maxpool_nhwc(xd, 3, 2, 1)
+    ref = torch.nn.functional.max_pool2d(xd.permute(0, 3, 1, 2).float(), 3, 2, 1)
+    assert torch.equal(y.float().permute(0, 3, 1, 2), ref)

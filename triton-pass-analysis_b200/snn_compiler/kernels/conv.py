@@ -144,6 +144,23 @@ def conv_f32(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, stride: in
     return out
 
 
+def maxpool_nhwc(x: torch.Tensor, k: int = 3, stride: int = 2, pad: int = 1,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [..., H, W, C] bf16 NHWC frames (C % 8 == 0) -> k x k max-pool with stride and
+    padding [..., Ho, Wo, C], Ho = (H + 2 pad - k) // stride + 1 (snnb_maxpool_nhwc: the
+    ResNet stem's 3x3 / stride 2 pool, reference zoo/resnet.py:131)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim >= 3
+    H, W, C = x.shape[-3:]
+    frames = x.numel() // (H * W * C) if x.numel() else 0
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    if out is None:
+        out = torch.empty(*x.shape[:-3], Ho, Wo, C, device=x.device, dtype=x.dtype)
+    st = _lib.lib().snnb_maxpool_nhwc(_lib.ptr(x), frames, H, W, C, int(k), int(stride),
+                                      int(pad), _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_maxpool_nhwc")
+    return out
+
+
 def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
                tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
                v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,

@@ -23,7 +23,8 @@ the route depends on it:
   - 3x3 / padding 1 convs of stride 2, 1x1 / padding 0 convs and 5x5 / 7x7 convs (padding
     k // 2) of stride 1 or 2 (a ResNet's strided, pointwise and stem convs) on the same
     kernels, the activation boxes traversing the input with the stride
-    (snnb_conv_lif_strided), bf16 or split as above (a float32 input of any Cin);
+    (snnb_conv_lif_strided), bf16 (channels zero padded to a multiple of 8) or split as
+    above (a float32 input of any Cin);
   - the residual form (FusedConvBNAddNeuron) on these geometries: the same tcgen05 kernels
     with the residual added in the epilogue (snnb_conv3x3_lif_res, snnb_conv_lif_strided);
   - FusedConvBN (conv + folded BN, no neuron: a ResNet block's downsample branch) on a bf16
@@ -95,14 +96,24 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None, stride=1):
     res = None if residual is None else _res_frames(residual)
     st = _pair(stride)[0]
     plain = tuple(weight.shape[2:]) == (3, 3) and st == 1       # the 3x3 / stride 1 entry
+    k = weight.shape[2]
+    if not plain and k > 1 and Cin < 8 and Cout % 32 == 0 and \
+            x_seq.dtype in (torch.bfloat16, torch.float32, torch.float16):
+        return _stem_conv_lif(x_seq, weight, b, layout, kw, cache, res, st)
     conv = KC.conv3x3_lif if plain else \
         (lambda x, w, b, **k: KC.conv_lif_strided(x, w, b, stride=st, **k))
-    if x_seq.dtype == torch.bfloat16 and Cin % 8 == 0 and Cout % 32 == 0:
+    if x_seq.dtype == torch.bfloat16 and (Cin % 8 == 0 or not plain) and Cout % 32 == 0:
+        # (a bf16 image with Cin % 8 != 0, e.g. a ResNet stem: channels zero padded to a
+        # multiple of 8 in the frames and the weights -- the padded products are zero)
+        cp = (Cin + 7) // 8 * 8
         key = ("khwc", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
-            cache["key"], cache["w"] = key, KC.weight_khwc(weight)
-        y = conv(KC._to_frames(x_seq), cache["w"], b, residual=res, **kw)
+            cache["key"], cache["w"] = key, F.pad(KC.weight_khwc(weight), (0, cp - Cin))
+        xf = KC._to_frames(x_seq)
+        if cp != Cin:
+            xf = F.pad(xf, (0, cp - Cin))
+        y = conv(xf, cache["w"], b, residual=res, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
     if x_seq.dtype in (torch.float32, torch.float16) and (Cin % 4 == 0 or not plain) and \
             Cout % 32 == 0:
@@ -122,6 +133,39 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None, stride=1):
         y = KC.first_conv_lif(x_seq.contiguous(), w, b, T=T, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
     return None
+
+
+def _stem_conv_lif(x_seq, weight, b, layout, kw, cache, res, st):
+    """A k x k conv on an image of few channels (a ResNet's 7x7 / stride 2 stem, Cin = 3):
+    with Cin channels per tap a tap's 64-wide k-slab would be mostly zero padding (49 taps
+    for 147 products per pixel), so the window is gathered into the channel dimension first
+    -- column (c, dy, dx) = x[c, stride*h + dy - k/2, stride*w + dx - k/2] (zero outside),
+    F.unfold's order -- and the conv runs as a 1x1 conv with K = k*k*Cin on the same kernel
+    (the same products, summed in another order).  bf16: K zero padded to a multiple of 8;
+    float32 / float16: split terms as the other float32 convs."""
+    T, B, Cin, H, W = x_seq.shape
+    Cout, k = weight.shape[0], weight.shape[2]
+    Ho, Wo = KC.conv_out_size(H, st), KC.conv_out_size(W, st)
+    K = Cin * k * k
+    cols = F.unfold(x_seq.reshape(T * B, Cin, H, W), k, padding=k // 2, stride=st)
+    cols = cols.transpose(1, 2).reshape(T, B, Ho, Wo, K)      # [T, B, Ho, Wo, K]
+    if x_seq.dtype == torch.bfloat16:
+        kp = (K + 7) // 8 * 8
+        key = ("stem", weight.data_ptr(), weight._version)
+        if cache.get("key") != key:
+            cache.clear()
+            w1 = weight.detach().reshape(Cout, 1, 1, K).to(torch.bfloat16)
+            cache["key"], cache["w"] = key, F.pad(w1, (0, kp - K)).contiguous()
+        xf = F.pad(cols, (0, kp - K)).contiguous()
+    else:
+        key = ("stem-split", weight.data_ptr(), weight._version)
+        if cache.get("key") != key:
+            cache.clear()
+            cache["key"], cache["w"] = key, KC.split_weight_khwc(
+                weight.detach().reshape(Cout, K, 1, 1))
+        xf = KC.split_activations(cols.to(torch.float32).contiguous())
+    y = KC.conv_lif_strided(xf, cache["w"], b, stride=1, residual=res, **kw)
+    return KC._from_frames(y, x_seq.dtype, layout)
 
 
 def _torch_conv(x_seq, weight, bias, stride, padding, dilation, groups, layout):

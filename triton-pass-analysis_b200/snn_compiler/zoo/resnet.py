@@ -21,6 +21,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
+from ..kernels import conv as KC
 from ..nn.fused_layers import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron
 from ..nn.modules import IFNode, LIFNode
 
@@ -173,6 +174,13 @@ class ResNetSNN(nn.Module):
     def stem(self, x_seq):
         if self._fused:
             x = self.stem_fused(x_seq)
+            xf = x.permute(0, 1, 3, 4, 2)
+            if x.is_cuda and x.dtype == torch.bfloat16 and xf.is_contiguous() and \
+                    x.shape[2] % 8 == 0:
+                # NHWC bf16 spikes: the pool (an OR of each window) on snnb_maxpool_nhwc
+                p = self.stem_pool
+                y = KC.maxpool_nhwc(xf, p.kernel_size, p.stride, p.padding)
+                return y.permute(0, 1, 4, 2, 3)
         else:
             x = self.stem_neuron(frames_op(lambda z: self.stem_bn(self.stem_conv(z)), x_seq,
                                            self.layout))
