@@ -277,6 +277,19 @@ int snnb_conv_lif_strided(const void* x, int64_t T, int64_t B, int64_t H, int64_
                           int64_t workspace_bytes, void* out, snnb_stream_t stream);
 
 /*
+ * Window gather for a k x k conv on an image of few channels (no kernel of its own in the
+ * reference, whose stem runs F.conv2d: snn_compiler/zoo/resnet.py:128-130 -> nn/modules.py:
+ * 324-357): x bf16 NHWC [frames, H, W, C] -> out bf16 [frames, Ho, Wo, Kp], column
+ * (dy * k + dx) * C + c = x[stride * ho + dy - pad, stride * wo + dx - pad, c] (zero outside
+ * the image), columns k*k*C .. Kp-1 zero; Ho = (H + 2 pad - k) / stride + 1.  The conv is then
+ * a 1x1 conv (snnb_conv_lif_strided with ksize 1) against w [Cout, k, k, C] viewed as
+ * [Cout, 1, 1, k*k*C] (zero padded to Kp).  Kp % 8 == 0, out 16-byte aligned, C <= 4096.
+ */
+int snnb_window_gather_nhwc(const void* x, int64_t frames, int64_t H, int64_t W, int64_t C,
+                            int k, int stride, int pad, int64_t Kp, void* out,
+                            snnb_stream_t stream);
+
+/*
  * k x k max-pool (stride, padding; each window clipped to the image, as torch's -inf padding
  * gives) on bf16 NHWC frames [frames, H, W, C] -> [frames, Ho, Wo, C], Ho = (H + 2 pad - k) /
  * stride + 1 (W likewise).  Replaces the spiking ResNet stem's nn.MaxPool2d(3, stride=2,

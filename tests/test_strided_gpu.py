@@ -242,3 +242,23 @@ def test_maxpool_nhwc_equals_torch(shape, kind):
     y = C.maxpool_nhwc(xd, 3, 2, 1)
     ref = torch.nn.functional.max_pool2d(xd.permute(0, 3, 1, 2).float(), 3, 2, 1)
     assert torch.equal(y.float().permute(0, 3, 1, 2), ref)
+
+
+@pytest.mark.parametrize("shape,k,stride", [((3, 20, 17, 3), 7, 2), ((2, 9, 9, 4), 3, 1),
+                                            ((2, 224, 224, 3), 7, 2)])
+def test_window_gather_equals_unfold(shape, k, stride):
+    """snnb_window_gather_nhwc against F.unfold on the same bf16 frames: the same values, in
+    columns (dy, dx, c), zero padded to a multiple of 8 (a copy: exact)."""
+    from snn_compiler.kernels import conv as C
+    g = torch.Generator().manual_seed(sum(shape) + k)
+    x = torch.randn(*shape, generator=g).to(torch.bfloat16)
+    N, H, W, Cin = shape
+    y = C.window_gather_nhwc(x.to(DEV), k, stride, k // 2).cpu()
+    Ho, Wo = (H - 1) // stride + 1, (W - 1) // stride + 1
+    K = k * k * Cin
+    assert tuple(y.shape) == (N, Ho, Wo, (K + 7) // 8 * 8)
+    cols = torch.nn.functional.unfold(x.permute(0, 3, 1, 2).float(), k, padding=k // 2,
+                                      stride=stride)                 # [N, (c, dy, dx), L]
+    ref = cols.reshape(N, Cin, k, k, Ho * Wo).permute(0, 4, 2, 3, 1).reshape(N, Ho, Wo, K)
+    assert torch.equal(y[..., :K].float(), ref)
+    assert not y[..., K:].float().any()

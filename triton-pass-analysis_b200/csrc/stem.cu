@@ -1,0 +1,149 @@
+// Data movement around a spiking ResNet's stem (snn_compiler/zoo/resnet.py:128-131: 7x7 /
+// stride 2 conv + BN + neuron on the image, then nn.MaxPool2d(3, stride=2, padding=1)).
+//
+// Window gather (snnb_window_gather_nhwc): with 3 image channels a 7x7 conv would give each
+// tap's 64-wide k-slab 3 useful channels, so the window is gathered into the channel
+// dimension first and the conv runs as a 1x1 conv with K = 147 on the tensor-core kernel.
+// One thread per output pixel writes its K columns, ordered (dy, dx, c) and zero padded to
+// Kp, as 16-byte stores; the reads are 2-byte loads of the (L2-resident) image.
+//
+// Max-pool (snnb_maxpool_nhwc): k x k with stride and padding on NHWC bf16 frames, applied
+// per frame.  Memory-bound: one thread per (output pixel, 8 channels) reads the window's
+// 16-byte chunks and writes one; padding positions are skipped (max over the in-image
+// window, as torch's -inf padding gives).  On {0, 1} spikes the max is the OR of the window.
+#include "common.cuh"
+
+namespace snnb {
+namespace {
+
+__global__ void __launch_bounds__(256) window_gather_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t frames, int H, int W, int C, int k, int stride,
+    int pad, int Ho, int Wo, int Kp, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t total = frames * Ho * Wo;
+    const int K = k * k * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int wo = (int)(i % Wo);
+        const int64_t r = i / Wo;
+        const int ho = (int)(r % Ho);
+        const int64_t f = r / Ho;
+        const __nv_bfloat16* src = x + f * H * W * C;
+        uint4* dst = reinterpret_cast<uint4*>(out + i * Kp);
+        const int h0 = ho * stride - pad, w0 = wo * stride - pad;
+        // column j = (dy * k + dx) * C + c, eight columns per 16-byte store
+        uint16_t buf[8];
+        int nb = 0, dy = 0, dx = 0, c = 0;
+        for (int j = 0; j < Kp; ++j) {
+            uint16_t v = 0;
+            if (j < K) {
+                const int h = h0 + dy, w = w0 + dx;
+                if (h >= 0 && h < H && w >= 0 && w < W)
+                    v = __bfloat16_as_ushort(src[((int64_t)h * W + w) * C + c]);
+                if (++c == C) {
+                    c = 0;
+                    if (++dx == k) { dx = 0; ++dy; }
+                }
+            }
+            buf[nb++] = v;
+            if (nb == 8) {
+                uint4 q;
+                q.x = buf[0] | ((uint32_t)buf[1] << 16);
+                q.y = buf[2] | ((uint32_t)buf[3] << 16);
+                q.z = buf[4] | ((uint32_t)buf[5] << 16);
+                q.w = buf[6] | ((uint32_t)buf[7] << 16);
+                dst[j >> 3] = q;
+                nb = 0;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) maxpool_nhwc_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t frames, int H, int W, int C, int k, int stride,
+    int pad, int Ho, int Wo, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    const int C8 = C / 8;
+    const int64_t total = frames * Ho * Wo * C8;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int c8 = (int)(i % C8);
+        int64_t r = i / C8;
+        const int wo = (int)(r % Wo);
+        r /= Wo;
+        const int ho = (int)(r % Ho);
+        const int64_t f = r / Ho;
+        const int h0 = ho * stride - pad, w0 = wo * stride - pad;
+        __nv_bfloat162 m[4];
+        bool first = true;
+        for (int dy = 0; dy < k; ++dy) {
+            const int h = h0 + dy;
+            if (h < 0 || h >= H) continue;
+            for (int dx = 0; dx < k; ++dx) {
+                const int w = w0 + dx;
+                if (w < 0 || w >= W) continue;
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+                    x + ((f * H + h) * W + w) * C) + c8);
+                const __nv_bfloat162* v = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) m[j] = first ? v[j] : __hmax2(m[j], v[j]);
+                first = false;
+            }
+        }
+        uint4 o;
+        __nv_bfloat162* ov = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ov[j] = m[j];
+        reinterpret_cast<uint4*>(out + ((f * Ho + ho) * Wo + wo) * C)[c8] = o;
+    }
+}
+
+}  // namespace
+}  // namespace snnb
+
+using namespace snnb;
+
+extern "C" int snnb_maxpool_nhwc(const void* x, int64_t frames, int64_t H, int64_t W, int64_t C,
+                                 int k, int stride, int pad, void* out, snnb_stream_t stream) {
+    if (const int inj = take_injected_status()) return inj;
+    if (!x || !out || frames < 0 || H <= 0 || W <= 0 || C <= 0 || C % 8) return SNNB_ERR_ARG;
+    // (pad < k: every window touches the image)
+    if (k < 1 || k > 8 || stride < 1 || stride > 8 || pad < 0 || pad >= k) return SNNB_ERR_ARG;
+    if (H > 0x7fffffff || W > 0x7fffffff || C > 0x7fffffff || !aligned16(x) || !aligned16(out))
+        return SNNB_ERR_ARG;
+    if (H + 2 * pad < k || W + 2 * pad < k) return SNNB_ERR_ARG;
+    const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+    if (frames > ((int64_t)1 << 40) / (Ho * Wo * C)) return SNNB_ERR_ARG;
+    const int64_t total = frames * Ho * Wo * (C / 8);
+    if (total == 0) return SNNB_OK;
+    const int64_t blocks = (total + 255) / 256;
+    const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
+    return launch_k(maxpool_nhwc_kernel, dim3(grid), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                    frames, (int)H, (int)W, (int)C, k, stride, pad, (int)Ho, (int)Wo,
+                    static_cast<__nv_bfloat16*>(out));
+}
+
+extern "C" int snnb_window_gather_nhwc(const void* x, int64_t frames, int64_t H, int64_t W,
+                                       int64_t C, int k, int stride, int pad, int64_t Kp,
+                                       void* out, snnb_stream_t stream) {
+    if (const int inj = take_injected_status()) return inj;
+    if (!x || !out || frames < 0 || H <= 0 || W <= 0 || C <= 0) return SNNB_ERR_ARG;
+    if (k < 1 || k > 11 || stride < 1 || stride > 8 || pad < 0 || pad >= k) return SNNB_ERR_ARG;
+    if (H > 0x7fffffff || W > 0x7fffffff || C > 4096 || Kp % 8 || Kp < (int64_t)k * k * C ||
+        Kp > 0x7fffffff || !aligned16(out))
+        return SNNB_ERR_ARG;
+    if (H + 2 * pad < k || W + 2 * pad < k) return SNNB_ERR_ARG;
+    const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+    if (frames > ((int64_t)1 << 40) / (Ho * Wo * Kp)) return SNNB_ERR_ARG;
+    const int64_t total = frames * Ho * Wo;
+    if (total == 0) return SNNB_OK;
+    const int64_t blocks = (total + 255) / 256;
+    const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
+    return launch_k(window_gather_kernel, dim3(grid), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                    frames, (int)H, (int)W, (int)C, k, stride, pad, (int)Ho, (int)Wo, (int)Kp,
+                    static_cast<__nv_bfloat16*>(out));
+}

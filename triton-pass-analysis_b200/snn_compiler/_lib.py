@@ -43,6 +43,7 @@ SIGNATURES = {
                               I32, I32, I32, I32, P, I64, P, P],
     "snnb_conv_f32": [P, I64, I64, I64, I64, I64, P, P, I64, I32, I32, P, P],
     "snnb_maxpool_nhwc": [P, I64, I64, I64, I64, I32, I32, I32, P, P],
+    "snnb_window_gather_nhwc": [P, I64, I64, I64, I64, I32, I32, I32, I64, P, P],
     "snnb_linear_lif": [P, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32, I32, I32, P, I64, P, P],
     "snnb_conv3x3_lif_packed": [P, I32, I64, I64, I64, I64, I64, P, P, I64, F, F, F, F, I32, I32,
                                 I32, I32, P, P],

@@ -161,6 +161,23 @@ def maxpool_nhwc(x: torch.Tensor, k: int = 3, stride: int = 2, pad: int = 1,
     return out
 
 
+def window_gather_nhwc(x: torch.Tensor, k: int, stride: int, pad: int,
+                       Kp: int | None = None) -> torch.Tensor:
+    """x [..., H, W, C] bf16 NHWC frames -> [..., Ho, Wo, Kp] bf16: each output pixel's
+    k x k window in columns (dy * k + dx) * C + c, zero outside the image and past k*k*C
+    (snnb_window_gather_nhwc; Kp defaults to k*k*C rounded up to a multiple of 8)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.ndim >= 3
+    H, W, C = x.shape[-3:]
+    Kp = (k * k * C + 7) // 8 * 8 if Kp is None else Kp
+    frames = x.numel() // (H * W * C) if x.numel() else 0
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    out = torch.empty(*x.shape[:-3], Ho, Wo, Kp, device=x.device, dtype=x.dtype)
+    st = _lib.lib().snnb_window_gather_nhwc(_lib.ptr(x), frames, H, W, C, int(k), int(stride),
+                                            int(pad), int(Kp), _lib.ptr(out), _lib.stream_of(x))
+    _lib.check(st, "snnb_window_gather_nhwc")
+    return out
+
+
 def linear_lif(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, *, neuron: str = "lif",
                tau: float = 2.0, decay=None, decay_input: bool = True, soft_reset: bool = False,
                v_threshold=1.0, v_reset: float = 0.0, out: torch.Tensor | None = None,

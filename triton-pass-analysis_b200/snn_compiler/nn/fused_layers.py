@@ -139,25 +139,29 @@ def _stem_conv_lif(x_seq, weight, b, layout, kw, cache, res, st):
     """A k x k conv on an image of few channels (a ResNet's 7x7 / stride 2 stem, Cin = 3):
     with Cin channels per tap a tap's 64-wide k-slab would be mostly zero padding (49 taps
     for 147 products per pixel), so the window is gathered into the channel dimension first
-    -- column (c, dy, dx) = x[c, stride*h + dy - k/2, stride*w + dx - k/2] (zero outside),
-    F.unfold's order -- and the conv runs as a 1x1 conv with K = k*k*Cin on the same kernel
-    (the same products, summed in another order).  bf16: K zero padded to a multiple of 8;
-    float32 / float16: split terms as the other float32 convs."""
+    -- each column one (dy, dx, c) of x[c, stride*h + dy - k/2, stride*w + dx - k/2] (zero
+    outside) -- and the conv runs as a 1x1 conv with K = k*k*Cin on the same kernel (the
+    same products, summed in another order).  bf16: snnb_window_gather_nhwc, K zero padded to
+    a multiple of 8; float32 / float16: F.unfold, then split terms as the other float32
+    convs."""
     T, B, Cin, H, W = x_seq.shape
     Cout, k = weight.shape[0], weight.shape[2]
     Ho, Wo = KC.conv_out_size(H, st), KC.conv_out_size(W, st)
     K = Cin * k * k
-    cols = F.unfold(x_seq.reshape(T * B, Cin, H, W), k, padding=k // 2, stride=st)
-    cols = cols.transpose(1, 2).reshape(T, B, Ho, Wo, K)      # [T, B, Ho, Wo, K]
     if x_seq.dtype == torch.bfloat16:
+        # the window gathered by snnb_window_gather_nhwc, columns (dy, dx, c)
         kp = (K + 7) // 8 * 8
         key = ("stem", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
-            w1 = weight.detach().reshape(Cout, 1, 1, K).to(torch.bfloat16)
+            w1 = KC.weight_khwc(weight).reshape(Cout, 1, 1, K)
             cache["key"], cache["w"] = key, F.pad(w1, (0, kp - K)).contiguous()
-        xf = F.pad(cols, (0, kp - K)).contiguous()
+        xf = KC.window_gather_nhwc(KC._to_frames(x_seq), k, st, k // 2, kp)
     else:
+        # float32 / float16: F.unfold's columns (c, dy, dx), then the split terms
+        cols = F.unfold(x_seq.reshape(T * B, Cin, H, W).to(torch.float32), k, padding=k // 2,
+                        stride=st)
+        cols = cols.transpose(1, 2).reshape(T, B, Ho, Wo, K)      # [T, B, Ho, Wo, K]
         key = ("stem-split", weight.data_ptr(), weight._version)
         if cache.get("key") != key:
             cache.clear()
