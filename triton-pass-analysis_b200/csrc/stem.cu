@@ -4,8 +4,9 @@
 // Window gather (snnb_window_gather_nhwc): with 3 image channels a 7x7 conv would give each
 // tap's 64-wide k-slab 3 useful channels, so the window is gathered into the channel
 // dimension first and the conv runs as a 1x1 conv with K = 147 on the tensor-core kernel.
-// One thread per output pixel writes its K columns, ordered (dy, dx, c) and zero padded to
-// Kp, as 16-byte stores; the reads are 2-byte loads of the (L2-resident) image.
+// One thread per (output pixel, 8 columns) writes one 16-byte chunk of the pixel's K
+// columns, ordered (dy, dx, c) and zero padded to Kp; the reads are 2-byte loads of the
+// (L2-resident) image.
 //
 // Max-pool (snnb_maxpool_nhwc): k x k with stride and padding on NHWC bf16 frames, applied
 // per frame.  Memory-bound: one thread per (output pixel, 8 channels) reads the window's
@@ -21,42 +22,44 @@ __global__ void __launch_bounds__(256) window_gather_kernel(
     int pad, int Ho, int Wo, int Kp, __nv_bfloat16* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
-    const int64_t total = frames * Ho * Wo;
+    // thread = (output pixel, group of 8 columns): adjacent threads store adjacent 16 bytes
+    const int KG = Kp / 8;
+    const int64_t total = frames * Ho * Wo * KG;
     const int K = k * k * C;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int wo = (int)(i % Wo);
-        const int64_t r = i / Wo;
+        const int grp = (int)(i % KG);
+        const int64_t pix = i / KG;
+        const int wo = (int)(pix % Wo);
+        const int64_t r = pix / Wo;
         const int ho = (int)(r % Ho);
         const int64_t f = r / Ho;
         const __nv_bfloat16* src = x + f * H * W * C;
-        uint4* dst = reinterpret_cast<uint4*>(out + i * Kp);
         const int h0 = ho * stride - pad, w0 = wo * stride - pad;
-        // column j = (dy * k + dx) * C + c, eight columns per 16-byte store
-        uint16_t buf[8];
-        int nb = 0, dy = 0, dx = 0, c = 0;
-        for (int j = 0; j < Kp; ++j) {
-            uint16_t v = 0;
+        // column j = (dy * k + dx) * C + c
+        int j = grp * 8;
+        int c = j % C, t = j / C;
+        int dx = t % k, dy = t / k;
+        uint32_t v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e, ++j) {
+            v[e] = 0;
             if (j < K) {
                 const int h = h0 + dy, w = w0 + dx;
                 if (h >= 0 && h < H && w >= 0 && w < W)
-                    v = __bfloat16_as_ushort(src[((int64_t)h * W + w) * C + c]);
+                    v[e] = __bfloat16_as_ushort(src[((int64_t)h * W + w) * C + c]);
                 if (++c == C) {
                     c = 0;
                     if (++dx == k) { dx = 0; ++dy; }
                 }
             }
-            buf[nb++] = v;
-            if (nb == 8) {
-                uint4 q;
-                q.x = buf[0] | ((uint32_t)buf[1] << 16);
-                q.y = buf[2] | ((uint32_t)buf[3] << 16);
-                q.z = buf[4] | ((uint32_t)buf[5] << 16);
-                q.w = buf[6] | ((uint32_t)buf[7] << 16);
-                dst[j >> 3] = q;
-                nb = 0;
-            }
         }
+        uint4 q;
+        q.x = v[0] | (v[1] << 16);
+        q.y = v[2] | (v[3] << 16);
+        q.z = v[4] | (v[5] << 16);
+        q.w = v[6] | (v[7] << 16);
+        reinterpret_cast<uint4*>(out)[i] = q;
     }
 }
 
@@ -138,7 +141,7 @@ extern "C" int snnb_window_gather_nhwc(const void* x, int64_t frames, int64_t H,
     if (H + 2 * pad < k || W + 2 * pad < k) return SNNB_ERR_ARG;
     const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
     if (frames > ((int64_t)1 << 40) / (Ho * Wo * Kp)) return SNNB_ERR_ARG;
-    const int64_t total = frames * Ho * Wo;
+    const int64_t total = frames * Ho * Wo * (Kp / 8);
     if (total == 0) return SNNB_OK;
     const int64_t blocks = (total + 255) / 256;
     const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
