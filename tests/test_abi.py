@@ -109,3 +109,35 @@ def test_strided_conv_entries_reject_bad_geometry_without_a_device():
         assert call() == -1                       # no input / weight / output pointers
         assert call(T=1 << 40) == -1
     assert strided(res=ctypes.c_void_p(16), rdt=7) == -1     # unknown residual dtype
+
+
+def test_stem_data_movement_entries_reject_bad_arguments_without_a_device():
+    """snnb_maxpool_nhwc and snnb_window_gather_nhwc: missing pointers, channel counts the
+    16-byte layout cannot hold, windows that could lie wholly in the padding, and a padded
+    width below the window all come back SNNB_ERR_ARG before any device work."""
+    from snn_compiler import _lib
+    L = _lib.lib()
+    p16 = ctypes.c_void_p(1 << 20)          # aligned stand-ins: rejected before any access
+
+    def pool(**kw):
+        a = dict(x=p16, F=2, H=8, W=8, C=64, k=3, s=2, pad=1, out=p16, st=None)
+        a.update(kw)
+        return L.snnb_maxpool_nhwc(*a.values())
+
+    def gather(**kw):
+        a = dict(x=p16, F=2, H=8, W=8, C=3, k=7, s=2, pad=3, Kp=152, out=p16, st=None)
+        a.update(kw)
+        return L.snnb_window_gather_nhwc(*a.values())
+    for call in (pool, gather):
+        assert call(x=None) == -1
+        assert call(out=None) == -1
+        assert call(k=0) == -1
+        assert call(s=0) == -1
+        assert call(pad=-1) == -1
+        assert call(H=0) == -1
+        assert call(F=0) == 0                       # nothing to do
+    assert pool(C=60) == -1                         # not a multiple of 8 channels
+    assert pool(k=3, pad=3) == -1                   # pad >= k: a window in the padding
+    assert pool(out=ctypes.c_void_p((1 << 20) + 8)) == -1     # misaligned output
+    assert gather(Kp=144) == -1                     # below k*k*C = 147
+    assert gather(Kp=150) == -1                     # not a multiple of 8
