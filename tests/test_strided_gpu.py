@@ -245,10 +245,13 @@ def test_maxpool_nhwc_equals_torch(shape, kind):
 
 
 @pytest.mark.parametrize("shape,k,stride", [((3, 20, 17, 3), 7, 2), ((2, 9, 9, 4), 3, 1),
-                                            ((2, 224, 224, 3), 7, 2)])
+                                            ((2, 224, 224, 3), 7, 2), ((2, 70, 45, 3), 5, 1),
+                                            ((1, 12, 10, 64), 7, 2)])   # (last: global form)
 def test_window_gather_equals_unfold(shape, k, stride):
     """snnb_window_gather_nhwc against F.unfold on the same bf16 frames: the same values, in
-    columns (dy, dx, c), zero padded to a multiple of 8 (a copy: exact)."""
+    columns (dy, dx, c), zero padded to a multiple of 8 (a copy: exact) -- through the
+    shared-memory staged kernel, and through the global-memory one where the staged window
+    would not fit (64 channels x 7 x 69 columns)."""
     from snn_compiler.kernels import conv as C
     g = torch.Generator().manual_seed(sum(shape) + k)
     x = torch.randn(*shape, generator=g).to(torch.bfloat16)

@@ -4,9 +4,9 @@
 // Window gather (snnb_window_gather_nhwc): with 3 image channels a 7x7 conv would give each
 // tap's 64-wide k-slab 3 useful channels, so the window is gathered into the channel
 // dimension first and the conv runs as a 1x1 conv with K = 147 on the tensor-core kernel.
-// One thread per (output pixel, 8 columns) writes one 16-byte chunk of the pixel's K
-// columns, ordered (dy, dx, c) and zero padded to Kp; the reads are 2-byte loads of the
-// (L2-resident) image.
+// The pixel's K columns are ordered (dy, dx, c) and zero padded to Kp.  The staged kernel
+// below takes the windows from shared memory; where its window does not fit, one thread per
+// (output pixel, 8 columns) gathers from global memory with 2-byte loads.
 //
 // Max-pool (snnb_maxpool_nhwc): k x k with stride and padding on NHWC bf16 frames, applied
 // per frame.  Memory-bound: one thread per (output pixel, 8 channels) reads the window's
@@ -60,6 +60,78 @@ __global__ void __launch_bounds__(256) window_gather_kernel(
         q.z = v[4] | (v[5] << 16);
         q.w = v[6] | (v[7] << 16);
         reinterpret_cast<uint4*>(out)[i] = q;
+    }
+}
+
+// Staged form: CTA = (frame, output row, 64 output columns).  The k input rows x the
+// (63 * stride + k) input columns the 64 windows span are loaded once into shared memory
+// (coalesced: consecutive threads, consecutive values of a row; zeros outside the image),
+// then the threads build the pixels' 16-byte column groups from shared memory and the CTA
+// stores its 64 pixels' Kp columns as one contiguous run.  Run-time divisions stay out of
+// the loops (an earlier form with four per staged value was issue-bound at ~1 ms for the
+// ResNet stem at batch 64).
+constexpr int GATHER_WB = 64;                 // output columns per CTA
+constexpr int GATHER_SMEM = 16 * 1024;        // largest staged window (bytes)
+
+__global__ void __launch_bounds__(128) window_gather_staged_kernel(
+    const __nv_bfloat16* __restrict__ x, int H, int W, int C, int k, int stride, int pad,
+    int Ho, int Wo, int Kp, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ uint16_t win[GATHER_SMEM / 2];
+    const int nwb = (Wo + GATHER_WB - 1) / GATHER_WB;
+    const int wb = (int)(blockIdx.x % nwb);
+    const int ho = (int)((blockIdx.x / nwb) % Ho);
+    const int64_t f = (int64_t)blockIdx.x / nwb / Ho;
+    const int wo0 = wb * GATHER_WB;
+    const int cols = (GATHER_WB - 1) * stride + k;          // input columns of the 32 windows
+    const int rowv = cols * C;                                // values per staged row
+    const int h0 = ho * stride - pad, w0 = wo0 * stride - pad;
+    const __nv_bfloat16* src = x + f * H * W * C;
+    // a staged row is one contiguous run of the image row (columns w0 .. w0 + cols - 1);
+    // the columns outside the image are the values q < qlo or q >= qhi (no division)
+    const int qlo = w0 < 0 ? -w0 * C : 0, qhi = (W - w0) * C;
+    for (int r = 0; r < k; ++r) {
+        const int h = h0 + r;
+        const bool hin = h >= 0 && h < H;
+        const int64_t rb = ((int64_t)(hin ? h : 0) * W + w0) * C;   // value q at rb + q
+        for (int q = threadIdx.x; q < rowv; q += blockDim.x)
+            win[r * rowv + q] = (hin && q >= qlo && q < qhi) ? __bfloat16_as_ushort(src[rb + q])
+                                                              : (uint16_t)0;
+    }
+    // thread = one column group g (8 columns) for pixels lane, lane + lanes, ...: the 8
+    // columns' offsets in the staged window are computed once (the run-time divisions by C
+    // and k stay out of the pixel loop); consecutive threads store consecutive 16 bytes
+    const int KG = Kp / 8, K = k * k * C;
+    const int lanes = blockDim.x / KG;                        // >= 1 (host: KG <= blockDim)
+    const int g = threadIdx.x % KG, lane = threadIdx.x / KG;
+    int off[8];
+    {
+        int j = g * 8, c = j % C, t = j / C, dx = t % k, dy = t / k;   // one division set
+#pragma unroll
+        for (int e = 0; e < 8; ++e, ++j) {
+            off[e] = j < K ? dy * rowv + dx * C + c : -1;
+            if (++c == C) {
+                c = 0;
+                if (++dx == k) { dx = 0; ++dy; }
+            }
+        }
+    }
+    __syncthreads();
+    const int npix = Wo - wo0 < GATHER_WB ? Wo - wo0 : GATHER_WB;
+    uint4* dst = reinterpret_cast<uint4*>(out + (((f * Ho + ho) * Wo) + wo0) * Kp);
+    if (lane >= lanes) return;
+    for (int p = lane; p < npix; p += lanes) {
+        const int base = p * stride * C;
+        uint32_t v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = off[e] >= 0 ? win[base + off[e]] : 0u;
+        uint4 q;
+        q.x = v[0] | (v[1] << 16);
+        q.y = v[2] | (v[3] << 16);
+        q.z = v[4] | (v[5] << 16);
+        q.w = v[6] | (v[7] << 16);
+        dst[p * KG + g] = q;
     }
 }
 
@@ -143,6 +215,13 @@ extern "C" int snnb_window_gather_nhwc(const void* x, int64_t frames, int64_t H,
     if (frames > ((int64_t)1 << 40) / (Ho * Wo * Kp)) return SNNB_ERR_ARG;
     const int64_t total = frames * Ho * Wo * (Kp / 8);
     if (total == 0) return SNNB_OK;
+    const int64_t staged = (int64_t)k * ((GATHER_WB - 1) * stride + k) * C * 2;
+    const int64_t ctas = frames * Ho * ((Wo + GATHER_WB - 1) / GATHER_WB);
+    if (staged <= GATHER_SMEM && Kp / 8 <= 128 && ctas <= 0x7fffffff)
+        return launch_k(window_gather_staged_kernel, dim3((unsigned)ctas), dim3(128), 0,
+                        static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                        (int)H, (int)W, (int)C, k, stride, pad, (int)Ho, (int)Wo, (int)Kp,
+                        static_cast<__nv_bfloat16*>(out));
     const int64_t blocks = (total + 255) / 256;
     const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
     return launch_k(window_gather_kernel, dim3(grid), dim3(256), 0,
