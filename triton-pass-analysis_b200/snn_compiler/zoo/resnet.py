@@ -175,12 +175,11 @@ class ResNetSNN(nn.Module):
         if self._fused:
             x = self.stem_fused(x_seq)
             xf = x.permute(0, 1, 3, 4, 2)
-            if x.is_cuda and x.dtype == torch.bfloat16 and xf.is_contiguous() and \
-                    x.shape[2] % 8 == 0:
+            pk = _square_pool(self.stem_pool)
+            if pk is not None and x.is_cuda and x.dtype == torch.bfloat16 and \
+                    xf.is_contiguous() and x.shape[2] % 8 == 0:
                 # NHWC bf16 spikes: the pool (an OR of each window) on snnb_maxpool_nhwc
-                p = self.stem_pool
-                y = KC.maxpool_nhwc(xf, p.kernel_size, p.stride, p.padding)
-                return y.permute(0, 1, 4, 2, 3)
+                return KC.maxpool_nhwc(xf, *pk).permute(0, 1, 4, 2, 3)
         else:
             x = self.stem_neuron(frames_op(lambda z: self.stem_bn(self.stem_conv(z)), x_seq,
                                            self.layout))
@@ -196,6 +195,17 @@ class ResNetSNN(nn.Module):
         for b in self.blocks():
             x = b(x)
         return self.head(x)
+
+
+def _square_pool(p: nn.MaxPool2d):
+    """(k, stride, padding) of a square, undilated, floor-mode max-pool, else None."""
+    def one(v):
+        v = tuple(v) if isinstance(v, (tuple, list)) else (v, v)
+        return v[0] if v[0] == v[1] else None
+    k, st, pad, dil = one(p.kernel_size), one(p.stride), one(p.padding), one(p.dilation)
+    if None in (k, st, pad) or dil != 1 or p.ceil_mode or pad >= k:
+        return None
+    return k, st, pad
 
 
 def init_bn(model: nn.Module):
