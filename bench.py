@@ -1398,7 +1398,7 @@ def main():
     ap.add_argument("--layer", default="512,512,56",
                     help="conv workload: Cin,Cout,H (3x3 + pool) or Cin,Cout,H,k,stride (ResNet "
                          "conv, k in {1, 3}, stride in {1, 2}, no pool)")
-    ap.add_argument("--batch", type=int, default=64, help="conv workload batch")
+    ap.add_argument("--batch", type=int, default=64, help="conv / resnet18 workload batch")
     ap.add_argument("--choice", default=None,
                     help="conv workload: fixed 'variant,block_n' instead of timing the candidates")
     ap.add_argument("--save-choices", default=None, help="vgg16: write the tuned kernel table")
@@ -1435,8 +1435,8 @@ def main():
             gm, gk, gn = (int(v) for v in args.gemm_shape.split(","))
             wl = BgemmWorkload(gm, gk, gn)
         else:
-            wl = {"vgg16": VggWorkload, "attention": AttnWorkload,
-                  "resnet18": ResNetWorkload}[args.workload]()
+            wl = ResNetWorkload(B=args.batch) if args.workload == "resnet18" else \
+                {"vgg16": VggWorkload, "attention": AttnWorkload}[args.workload]()
         if args.workload == "vgg16":
             wl.load_choices, wl.save_choices = args.load_choices, args.save_choices
             wl.eager = args.eager
