@@ -774,8 +774,8 @@ class ResNetWorkload:
                 "classes": self.classes, "lif": "tau=2, v_th=1, hard reset 0, decay_input",
                 "weights": "Kaiming-uniform (torch default) seeded, BN stats randomised and folded, bf16",
                 "layout": "NHWC (channels-last storage)",
-                "launch": "one CUDA graph per forward; torch ops for the max-pool, channel pad of the "
-                          "image, average pool and head",
+                "launch": "one CUDA graph per forward; per-layer kernel schedules from "
+                          "snn_compiler.nn.tune_convs; torch ops for the average pool and head",
                 "l2": "256 MB buffer written before every timed step"}
 
     def _model(self):
@@ -811,6 +811,9 @@ class ResNetWorkload:
             h.remove()
         self.n_convs = sum(1 for mod in self.m.modules() if isinstance(mod, kinds))
         self.flops_img = self.flops / self.B
+        # per-layer kernel schedules, timed on each conv's real input (snn_compiler.nn.tune_convs)
+        from snn_compiler.nn import tune_convs
+        self.choices = tune_convs(self.m, self.x)
         # capture the forward (warm the modules' weight caches first)
         with torch.no_grad():
             for _ in range(2):
@@ -820,10 +823,10 @@ class ResNetWorkload:
             with torch.cuda.graph(self.graph):
                 self.out = self.m(self.x)
         torch.cuda.synchronize()
-        # this library's launches per forward: one per conv, plus the bias-add launch of each
-        # float32 downsample conv
+        # this library's launches per forward: one per conv, the bias-add launch of each
+        # float32 downsample conv, the stem's window gather and its max-pool
         self.launches_per_step = self.n_convs + sum(
-            1 for mod in self.m.modules() if isinstance(mod, FusedConvBN))
+            1 for mod in self.m.modules() if isinstance(mod, FusedConvBN)) + 2
 
     @staticmethod
     def _nhwc(t):
@@ -846,7 +849,8 @@ class ResNetWorkload:
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": peaks["source"] + " bf16 burst (cuBLAS)",
                 "kernel": "whole forward (one CUDA graph; every conv on the tcgen05 kernels)",
-                "algorithmic_flops_per_launch": self.flops, "traffic": None}
+                "algorithmic_flops_per_launch": self.flops, "traffic": None,
+                "choices": {k: list(v) for k, v in self.choices.items()}}
 
     def e2e_setup(self):
         self.hx = self.x.cpu().pin_memory()

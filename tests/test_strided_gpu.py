@@ -128,11 +128,13 @@ def test_strided_entry_rejects_band_variants_and_bad_strides():
         C.conv_lif_strided(x, w, b, stride=3)
 
 
-def test_resnet_block_with_downsample_bf16_on_the_kernels():
+@pytest.mark.parametrize("tune", [False, True])
+def test_resnet_block_with_downsample_bf16_on_the_kernels(tune):
     """A downsampling BasicBlock (3x3 / stride 2 conv, 1x1 / stride 2 downsample + BN, 3x3
     conv + residual) fused and run in bf16: each fused module against the oracle on its own
-    inputs, every one of them on this library's kernels."""
-    from snn_compiler.nn import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron
+    inputs, every one of them on this library's kernels -- with the default schedules, and
+    with the per-layer schedules tune_convs picks."""
+    from snn_compiler.nn import FusedConvBN, FusedConvBNAddNeuron, FusedConvBNNeuron, tune_convs
     from snn_compiler.zoo.resnet import BasicBlockSNN
     torch.manual_seed(11)
     down = torch.nn.Sequential(torch.nn.Conv2d(64, 128, 1, stride=2, bias=False),
@@ -148,13 +150,17 @@ def test_resnet_block_with_downsample_bf16_on_the_kernels():
                 mod.running_var.uniform_(0.5, 1.5)
     blk = blk.eval().fuse().to(DEV).to(torch.bfloat16)
     assert isinstance(blk.downsample, FusedConvBN)
+    g = torch.Generator().manual_seed(5)
+    x = _spikes((4, 2, 64, 16, 16), 0.25, g).to(torch.bfloat16).to(DEV)
+    if tune:                        # (before the recording hooks: tuning captures graphs)
+        chosen = tune_convs(blk, x, reps=2)
+        assert set(chosen) == {"block1", "block2"}, chosen
+        assert all(v[0] in (1, 2, 4, 5) for v in chosen.values())
     rec = []
     hooks = [m.register_forward_hook(
         lambda m, inp, out: rec.append((m, [i.detach().cpu() for i in inp], out.detach().cpu())))
         for m in blk.modules() if isinstance(m, (FusedConvBN, FusedConvBNNeuron,
                                                   FusedConvBNAddNeuron))]
-    g = torch.Generator().manual_seed(5)
-    x = _spikes((4, 2, 64, 16, 16), 0.25, g).to(torch.bfloat16).to(DEV)
     try:
         with torch.no_grad():
             y = blk(x)

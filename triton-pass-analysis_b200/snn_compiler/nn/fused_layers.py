@@ -69,6 +69,14 @@ class _NeuronArgs:
                     decay_input=self.decay_input, soft_reset=self.soft_reset,
                     v_threshold=self.v_threshold, v_reset=self.v_reset)
 
+    def _conv_kw(self):
+        """The neuron arguments plus the kernel schedule tune_convs chose (if any)."""
+        kw = self._neuron_kw()
+        sched = getattr(self, "_sched", None)
+        if sched is not None:
+            kw.update(variant=sched[0], block_n=sched[1])
+        return kw
+
 
 def _fused_conv_ok(weight, stride, padding, dilation, groups, v_threshold):
     """k x k / padding k // 2 with k in {1, 3, 5, 7}, stride 1 or 2 (the convs of VGG and
@@ -130,6 +138,7 @@ def _conv_lif(x_seq, weight, bias, layout, kw, cache, residual=None, stride=1):
         return None
     if x_seq.dtype == torch.float32 and Cout % 8 == 0:
         w = weight.detach().float().contiguous()
+        kw = {k_: v for k_, v in kw.items() if k_ not in ("variant", "block_n")}
         y = KC.first_conv_lif(x_seq.contiguous(), w, b, T=T, **kw)
         return KC._from_frames(y, x_seq.dtype, layout)
     return None
@@ -212,7 +221,7 @@ class FusedConvNeuron(nn.Module, _NeuronArgs):
     def forward(self, x_seq):
         if _fused_conv_ok(self.weight, self.stride, self.padding, self.dilation, self.groups,
                           self.v_threshold):
-            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._conv_kw(),
                           self._cache, stride=self.stride)
             if y is not None:
                 return y
@@ -309,7 +318,7 @@ class FusedConvBNNeuron(_ConvBNBase):
     def forward(self, x_seq):
         if self.fold_bn and _fused_conv_ok(self.weight, self.stride, self.padding,
                                            self.dilation, self.groups, self.v_threshold):
-            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._conv_kw(),
                           self._cache, stride=self.stride)
             if y is not None:
                 return y
@@ -334,7 +343,7 @@ class FusedConvBNAddNeuron(_ConvBNBase):
         if self.fold_bn and _fused_conv_ok(self.weight, self.stride, self.padding,
                                            self.dilation, self.groups, self.v_threshold) \
                 and tuple(residual_seq.shape[:2]) == tuple(x_seq.shape[:2]):
-            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._neuron_kw(),
+            y = _conv_lif(x_seq, self.weight, self.bias, self.layout, self._conv_kw(),
                           self._cache, residual=residual_seq, stride=self.stride)
             if y is not None:
                 return y
@@ -384,3 +393,63 @@ class FusedConvBN(nn.Module):
         y = _torch_conv(x_seq, self.weight, None, self.stride, self.padding, self.dilation,
                         self.groups, self.layout)
         return y + self.bias.detach().to(y.dtype).view(1, 1, -1, 1, 1)
+
+
+def tune_convs(model: nn.Module, *inputs, reps: int = 5) -> dict:
+    """Opt-in per-layer schedule choice for the fused conv modules of `model` (the module
+    path otherwise runs the library's default: T-sequential or T-folded by grid size).  One
+    forward of `inputs` records every fused conv module's input; for each, the kernel
+    schedules its geometry admits without a split-K workspace -- T-sequential / T-folded
+    with each channel block width, and for 3x3 / 1x1 stride-1 convs the two-tile and
+    CTA-pair forms -- are timed on that input (device time of graph-replayed calls, the
+    lower of two) and the fastest is kept on the module (`module._sched`).  Returns
+    {module name: (variant, block_n)}.  Call it before capturing the model in a graph."""
+    kinds = (FusedConvNeuron, FusedConvBNNeuron, FusedConvBNAddNeuron)
+    seen = {}
+    hooks = [m.register_forward_pre_hook(lambda mod, inp: seen.setdefault(mod, inp))
+             for m in model.modules() if isinstance(m, kinds)]
+    try:
+        with torch.no_grad():
+            model(*inputs)
+    finally:
+        for h in hooks:
+            h.remove()
+    names = {m: n for n, m in model.named_modules()}
+    chosen = {}
+    for mod, inp in seen.items():
+        if getattr(mod, "fold_bn", True) is False or not _fused_conv_ok(
+                mod.weight, mod.stride, mod.padding, mod.dilation, mod.groups, mod.v_threshold):
+            continue
+        T = inp[0].shape[0]
+        Cout, Cin, k = mod.weight.shape[0], mod.weight.shape[1], mod.weight.shape[2]
+        st = _pair(mod.stride)[0]
+        res = len(inp) > 1
+        stem = not (k == 3 and st == 1) and k > 1 and Cin < 8      # runs as a 1x1 conv
+        general = (st != 1 or k > 3) and not stem
+        tfold = T in (2, 4, 8)
+        cands = []
+        for bn in (32, 64, 128, 256):
+            if Cout % bn:
+                continue
+            if bn <= (64 if res else 128):
+                cands.append((1, bn))
+            if tfold:
+                cands.append((2, bn))
+                if not general and not res and bn != 256:
+                    cands.append((4, bn))
+                if not general and not res and bn >= 64:
+                    cands.append((5, bn))
+        best, best_ms = None, float("inf")
+        with torch.no_grad():
+            for c in cands:
+                mod._sched = c
+                try:
+                    ms = min(KC.time_graph(lambda: mod(*inp), reps) for _ in range(2))
+                except (RuntimeError, AssertionError):
+                    continue
+                if ms < best_ms:
+                    best, best_ms = c, ms
+        mod._sched = best
+        if best is not None:
+            chosen[names.get(mod, type(mod).__name__)] = best
+    return chosen
